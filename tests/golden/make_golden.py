@@ -1,0 +1,322 @@
+#!/usr/bin/env python3
+"""Generate the committed golden vectors under tests/golden/ (run in the build
+container, where the reference checkout is mounted; the GPU box has no
+reference, so everything the tests need is written here).
+
+1. ``hw_<kernel>.npz`` — the reference's register-level known-answer fixtures
+   (``hw/test_data/<kernel>_test_data/manifest.txt`` + ``test_NN_*.hex``,
+   produced by its HLS C++ models and ``kernels/rowops_rtl/scripts/
+   gen_fixtures.py``), converted verbatim to int16 / uint8 arrays.
+2. ``sim_*.npz`` — outputs of the reference's own Python simulator
+   (``inference-scheduler/src``: ``_SimulateMixin._forward_pass``,
+   ``vectorop_act.kernel_table``, ``vectorop_smx.softmax_raw``,
+   ``rowops_spec``) on seeded inputs, imported through the inert ``onnx``
+   stand-in in ``_onnx_stub``.
+
+    python tests/golden/make_golden.py [--ref /root/reference] [--only hw|sim]
+"""
+from __future__ import annotations
+
+import argparse
+import os
+import sys
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+
+
+def read_words(path):
+    """int16 words, one hex word per line (vecop / matmul / conv / pool)."""
+    with open(path) as f:
+        v = [int(x, 16) for x in f.read().split()]
+    return np.array(v, np.uint16).view(np.int16)
+
+
+def read_bytes(path):
+    """16-byte words as 32 hex digits per line, byte 0 first (rowops)."""
+    with open(path) as f:
+        s = "".join(f.read().split())
+    return np.frombuffer(bytes.fromhex(s), np.uint8).copy()
+
+
+def manifest(path):
+    rows = []
+    with open(path) as f:
+        for line in f:
+            line = line.strip()
+            if not line or line.startswith("#"):
+                continue
+            rows.append(line.split())
+    return rows
+
+
+def convert_hw(ref, out):
+    base = os.path.join(ref, "hw", "test_data")
+    specs = {
+        "vecop": ("vecop_test_data", ["a", "b", "c"], read_words, 11),
+        "matmul": ("matmul_test_data", ["a", "b", "c"], read_words, 9),
+        "conv": ("conv_test_data", ["x", "w", "b", "y"], read_words, 21),
+        "pool": ("pool_test_data", ["x", "y"], read_words, 18),
+        "rowops": ("rowops_test_data", ["a", "b", "p", "c"], read_bytes, 16),
+    }
+    for name, (d, parts, reader, nint) in specs.items():
+        rows = manifest(os.path.join(base, d, "manifest.txt"))
+        arrays, params, labels = {}, [], []
+        for r in rows:
+            idx = int(r[0])
+            params.append([int(v) for v in r[:nint]])
+            labels.append(r[nint] if len(r) > nint else "")
+            for p in parts:
+                fn = os.path.join(base, d, f"test_{idx:02d}_{p}.hex")
+                arrays[f"c{idx}_{p}"] = reader(fn) if os.path.exists(fn) else np.zeros(0, np.int16)
+        arrays["params"] = np.array(params, np.int64)
+        arrays["labels"] = np.array(labels)
+        if name == "rowops":
+            arrays["tables"] = read_bytes(os.path.join(base, d, "tables.hex"))
+            chains = manifest(os.path.join(base, d, "chains", "manifest.txt"))
+            arrays["chain_params"] = np.array([[int(v) for v in c[:21]] for c in chains], np.int64)
+            for ci in sorted({int(c[0]) for c in chains}):
+                for p in ("mem", "out"):
+                    arrays[f"chain{ci}_{p}"] = read_bytes(os.path.join(base, d, "chains", f"chain_{ci:02d}_{p}.hex"))
+        np.savez_compressed(os.path.join(out, f"hw_{name}.npz"), **arrays)
+        print(f"hw_{name}.npz: {len(rows)} cases")
+
+
+# --------------------------------------------------------------------------- simulator goldens
+def _import_reference(ref):
+    sys.path[:0] = [os.path.join(HERE, "_onnx_stub"), os.path.join(ref, "inference-scheduler")]
+    import src.codegen._simulate as sim  # noqa: F401
+    return sim
+
+
+class _Graph:
+    def __init__(self, nodes, weights, inputs, outputs):
+        self.nodes, self.weight_tensors = nodes, weights
+        self.input_tensors, self.output_tensors = inputs, outputs
+        self.state_tensors = []
+
+
+def _shim(sim, dtype, graph):
+    """A minimal object carrying what ``_SimulateMixin._forward_pass`` reads."""
+    class Shim(sim._SimulateMixin):
+        pass
+    s = Shim()
+    s._dtype, s._graph = dtype, graph
+    s.initial_states = lambda: {}
+    return s
+
+
+def q88(rng, shape, lo, hi):
+    """raw Q8.8 of uniform values in [lo, hi), rounded half to even."""
+    return np.clip(np.round(rng.uniform(lo, hi, size=shape) * 256.0), -32768, 32767).astype(np.int64)
+
+
+def make_mnist(sim, seed):
+    """Config 1: Conv 1->16 +bias, Relu, MaxPool, Conv 16->32 +bias, Relu,
+    MaxPool, flatten, MatMul 1568x10, Add bias, Softmax (row, Q8.8)."""
+    from src.dtype import AP_FIXED_16_8 as D
+    from src.tensor import TensorInfo as T
+    from src import nodes as N
+    import onnx
+    rng = np.random.default_rng(seed)
+    x = q88(rng, (1, 1, 28, 28), -1, 1)
+    w1, b1 = q88(rng, (16, 1, 3, 3), -0.25, 0.25), q88(rng, (16,), -0.25, 0.25)
+    w2, b2 = q88(rng, (32, 16, 3, 3), -0.25, 0.25), q88(rng, (32,), -0.25, 0.25)
+    wf, bf = q88(rng, (1568, 10), -0.25, 0.25), q88(rng, (1, 10), -0.25, 0.25)
+    t = {}
+
+    def ten(name, shape, data=None):
+        t[name] = T(onnx_name=name, shape=list(shape), dtype="float32", data=None if data is None else data / 256.0)
+        return t[name]
+    X = ten("x", x.shape)
+    W1, B1, W2, B2 = ten("w1", w1.shape, w1), ten("b1", b1.shape, b1), ten("w2", w2.shape, w2), ten("b2", b2.shape, b2)
+    WF, BF = ten("wf", wf.shape, wf), ten("bf", bf.shape, bf)
+    c1, r1, p1 = ten("c1", (1, 16, 28, 28)), ten("r1", (1, 16, 28, 28)), ten("p1", (1, 16, 14, 14))
+    c2, r2, p2 = ten("c2", (1, 32, 14, 14)), ten("r2", (1, 32, 14, 14)), ten("p2", (1, 32, 7, 7))
+    fl, mm, ad = ten("flat", (1, 1568)), ten("mm", (1, 10)), ten("logits", (1, 10))
+    nd = onnx.NodeProto()
+    nodes = [
+        N.ConvNode(onnx_node=nd, inputs=[X, W1, B1], output=c1, batch=1, in_ch=1, in_h=28, in_w=28, out_ch=16,
+                   out_h=28, out_w=28, kh=3, kw=3, pad_top=1, pad_left=1, has_bias=True),
+        N.ScheduledNode(onnx_node=nd, op_code=N.OP_RELU, arity=1, inputs=[c1], output=r1),
+        N.PoolNode(onnx_node=nd, inputs=[r1], output=p1, batch=1, channels=16, in_h=28, in_w=28, out_h=14,
+                   out_w=14, pool_h=2, pool_w=2, stride_h=2, stride_w=2, pool_type=N.POOL_MAX),
+        N.ConvNode(onnx_node=nd, inputs=[p1, W2, B2], output=c2, batch=1, in_ch=16, in_h=14, in_w=14, out_ch=32,
+                   out_h=14, out_w=14, kh=3, kw=3, pad_top=1, pad_left=1, has_bias=True),
+        N.ScheduledNode(onnx_node=nd, op_code=N.OP_RELU, arity=1, inputs=[c2], output=r2),
+        N.PoolNode(onnx_node=nd, inputs=[r2], output=p2, batch=1, channels=32, in_h=14, in_w=14, out_h=7,
+                   out_w=7, pool_h=2, pool_w=2, stride_h=2, stride_w=2, pool_type=N.POOL_MAX),
+        N.ReshapeNode(onnx_node=nd, inputs=[p2], output=fl),
+        N.MatmulNode(onnx_node=nd, inputs=[fl, WF], output=mm, n=1, k=1568, m=10, batch=1),
+        N.ScheduledNode(onnx_node=nd, op_code=N.OP_ADD, arity=2, inputs=[mm, BF], output=ad),
+    ]
+    g = _Graph(nodes, [W1, B1, W2, B2, WF, BF], [X], [ad])
+    arrays = _shim(sim, D, g)._forward_pass({"x": x / 256.0})
+    from src import vectorop_smx as VS
+    cm, cs = VS.scale_regs(8, 1.0)
+    logits = np.round(arrays["logits"] * 256).astype(np.int64)
+    prob = VS.softmax_raw(logits, 10, cm, cs, 8)
+    out = dict(x=x, w1=w1, b1=b1, w2=w2, b2=b2, wf=wf, bf=bf, prob=prob)
+    for k in ("c1", "r1", "p1", "c2", "r2", "p2", "mm", "logits"):
+        out[k] = np.round(arrays[k] * 256).astype(np.int64)
+    return out
+
+
+def make_sim(ref, out):
+    sim = _import_reference(ref)
+    from src import vectorop_act as VA, vectorop_smx as VS, rowops_spec as RS
+    from src.nodes import ACT_SILU, ACT_GELU, ACT_GELU_TANH, ACT_LEAKY_RELU
+    # activation tables over every Q8.8 input
+    tabs = {f"act{a}": np.round(VA.kernel_table(a) * 256).astype(np.int16)
+            for a in (ACT_SILU, ACT_GELU, ACT_GELU_TANH)}
+    from src.dtype import AP_FIXED_16_8 as D
+    xs = np.arange(-32768, 32768, dtype=np.float64) / 256.0
+    for alpha in (0, 655, 6554, 16384, 32768, 65535):
+        tabs[f"leaky{alpha}"] = np.round(VA.apply(ACT_LEAKY_RELU, xs, D, alpha) * 256).astype(np.int16)
+    np.savez_compressed(os.path.join(out, "sim_act.npz"), **tabs)
+    # softmax spec on seeded scores, row and column mode, causal masks
+    rng = np.random.default_rng(7)
+    cm, cs = VS.scale_regs(8, 1.0)
+    smx = {"cm": np.array(cm), "cs": np.array(cs)}
+    for n in (1, 13, 128, 384, 1024):
+        x = rng.integers(-2048, 2048, size=(8, n))
+        smx[f"row{n}_x"] = x
+        smx[f"row{n}_p"] = VS.softmax_raw(x, n, cm, cs, 8)
+        v = VS.causal_valid(8, max(1, n // 3), 4, n)
+        smx[f"row{n}_pc"] = VS.softmax_raw(x, v, cm, cs, 12)
+        smx[f"row{n}_vc"] = v
+        s = rng.integers(-4096, 4096, size=(n, 16))
+        smx[f"col{n}_s"] = s
+        smx[f"col{n}_p"] = VS.softmax_cols(s, n, cm, cs, 8)
+    for fs, sg in ((8, 1.0), (10, 0.125), (6, 0.5), (12, 1.0 / 8.0)):
+        smx[f"regs_{fs}_{sg}"] = np.array(VS.scale_regs(fs, sg))
+    np.savez_compressed(os.path.join(out, "sim_smx.npz"), **smx)
+    # row-ops spec functions
+    rng = np.random.default_rng(11)
+    ro = {}
+    h = rng.integers(-(1 << 20), 1 << 20, size=(6, 960))
+    gam = rng.normal(1.0, 0.1, size=960)
+    ro["rms_h"], ro["rms_g"] = h, gam
+    ro["rms_y"] = RS.rms_norm(h, 15, gam, 1e-5, 10)
+    x = rng.integers(-4096, 4096, size=(6, 768))
+    bet = rng.normal(0.0, 0.2, size=768)
+    ro["ln_x"], ro["ln_g"], ro["ln_b"] = x, gam[:768], bet
+    ro["ln_y"] = RS.layer_norm(x, 8, gam[:768], bet, 1e-12, 9)
+    g = rng.integers(-8000, 8000, size=(5, 256))
+    u = rng.integers(-8000, 8000, size=(5, 256))
+    ro["silu_g"], ro["silu_u"], ro["silu_y"] = g, u, RS.silu_mul(g, 10, u, 10, 11)
+    xr = rng.integers(-6000, 6000, size=(4, 3, 64))
+    ang = np.arange(4)[:, None] * (100000.0 ** (-np.arange(32) / 32.0))[None, :]
+    cos = np.concatenate([np.cos(ang), np.cos(ang)], axis=1).astype(np.float32)
+    sin = np.concatenate([np.sin(ang), np.sin(ang)], axis=1).astype(np.float32)
+    cr, sr = RS.rope_tables_raw(cos, sin)
+    ro["rope_x"], ro["rope_c"], ro["rope_s"] = xr, cr, sr
+    ro["rope_y"] = RS.rope(xr, 11, cr, sr, 11)
+    ro["sig_table"], ro["rsqrt_table"] = RS.sigmoid_table(), RS.rsqrt_table()
+    ro["table_image"] = np.frombuffer(RS.table_image(), np.uint8)
+    D_ = rng.integers(1, 1 << 62, size=64, dtype=np.int64)
+    ro["rsqrt_D"] = D_
+    ro["rsqrt_R"] = np.array([RS.rsqrt_bf(int(d)) for d in D_], np.int64)
+    np.savez_compressed(os.path.join(out, "sim_rowops.npz"), **ro)
+    # the simulator's forward pass: MNIST config, two seeds
+    for seed in (1, 2):
+        np.savez_compressed(os.path.join(out, f"sim_mnist_s{seed}.npz"), **make_mnist(sim, seed))
+    # the simulator's pool / conv / matmul / vectorop branches on small seeded cases
+    np.savez_compressed(os.path.join(out, "sim_ops.npz"), **make_ops(sim))
+    print("sim goldens written")
+
+
+def make_ops(sim):
+    """Single-node graphs through ``_forward_pass`` (Q8.8 and exponent paths)."""
+    from src.dtype import AP_FIXED_16_8 as D
+    from src.tensor import TensorInfo as T
+    from src import nodes as N
+    import onnx
+    nd = onnx.NodeProto()
+    rng = np.random.default_rng(5)
+    out = {}
+
+    def run(nodes, weights, inputs, feeds):
+        g = _Graph(nodes, weights, inputs, [nodes[-1].output])
+        return _shim(sim, D, g)._forward_pass({k: v / 256.0 for k, v in feeds.items()})
+
+    # pools: every type on one input
+    x = q88(rng, (2, 5, 9, 11), -4, 4)
+    out["pool_x"] = x
+    cases = [(0, 0, 0, 2, 2, 2, 2, 0, 0, 1, 1), (1, 0, 0, 3, 3, 2, 2, 1, 1, 1, 1), (1, 0, 1, 3, 3, 2, 2, 1, 1, 1, 1),
+             (2, 1, 0, 2, 3, 1, 2, 0, 1, 1, 1), (2, 2, 0, 3, 3, 2, 2, 1, 1, 1, 1), (2, 2, 0, 2, 2, 1, 1, 0, 0, 2, 2),
+             (1, 0, 0, 9, 11, 1, 1, 0, 0, 1, 1), (2, 2, 0, 9, 11, 1, 1, 0, 0, 1, 1), (0, 0, 0, 3, 3, 3, 3, 2, 2, 1, 1)]
+    for ci, (pt, lp, cip, ph, pw, sh, sw, pt_, pl, dh, dw) in enumerate(cases):
+        oh = (9 + 2 * pt_ - (dh * (ph - 1) + 1)) // sh + 1
+        ow = (11 + 2 * pl - (dw * (pw - 1) + 1)) // sw + 1
+        X, Y = T(onnx_name="x", shape=[2, 5, 9, 11], dtype="float32"), T(onnx_name="y", shape=[2, 5, oh, ow], dtype="float32")
+        n = N.PoolNode(onnx_node=nd, inputs=[X], output=Y, batch=2, channels=5, in_h=9, in_w=11, out_h=oh, out_w=ow,
+                       pool_h=ph, pool_w=pw, stride_h=sh, stride_w=sw, pad_top=pt_, pad_left=pl, dil_h=dh, dil_w=dw,
+                       pool_type=pt, lp_order=lp, count_include_pad=cip)
+        out[f"pool{ci}_params"] = np.array([pt, lp, cip, ph, pw, sh, sw, pt_, pl, dh, dw, oh, ow])
+        out[f"pool{ci}_y"] = np.round(run([n], [], [X], {"x": x})["y"] * 256).astype(np.int64)
+    # conv Q8.8: standard and depthwise, stride / dilation / padding
+    x = q88(rng, (2, 6, 10, 9), -1, 1)
+    out["conv_x"] = x
+    ccases = [(8, 3, 3, 1, 1, 1, 1, 1, 1, False, True), (4, 3, 3, 2, 2, 1, 1, 1, 1, False, False),
+              (6, 3, 3, 1, 2, 1, 1, 2, 1, True, True), (6, 5, 5, 2, 1, 2, 2, 1, 1, True, False),
+              (5, 1, 1, 1, 1, 0, 0, 1, 1, False, True), (3, 7, 7, 2, 2, 3, 3, 1, 1, False, True)]
+    for ci, (M, kh, kw, sh, sw, pt_, pl, dh, dw, dwise, hb) in enumerate(ccases):
+        oh = (10 + 2 * pt_ - (dh * (kh - 1) + 1)) // sh + 1
+        ow = (9 + 2 * pl - (dw * (kw - 1) + 1)) // sw + 1
+        w = q88(rng, (M, 1 if dwise else 6, kh, kw), -0.5, 0.5)
+        b = q88(rng, (M,), -1, 1)
+        X = T(onnx_name="x", shape=[2, 6, 10, 9], dtype="float32")
+        W = T(onnx_name="w", shape=list(w.shape), dtype="float32", data=w / 256.0)
+        B = T(onnx_name="b", shape=[M], dtype="float32", data=b / 256.0)
+        Y = T(onnx_name="y", shape=[2, M, oh, ow], dtype="float32")
+        n = N.ConvNode(onnx_node=nd, inputs=[X, W, B] if hb else [X, W], output=Y, batch=2, in_ch=6, in_h=10, in_w=9,
+                       out_ch=M, out_h=oh, out_w=ow, kh=kh, kw=kw, stride_h=sh, stride_w=sw, dilation_h=dh,
+                       dilation_w=dw, pad_top=pt_, pad_left=pl, has_bias=hb, is_depthwise=dwise)
+        out[f"conv{ci}_params"] = np.array([M, kh, kw, sh, sw, pt_, pl, dh, dw, int(dwise), int(hb), oh, ow])
+        out[f"conv{ci}_w"], out[f"conv{ci}_b"] = w, b
+        out[f"conv{ci}_y"] = np.round(run([n], [W, B] if hb else [W], [X], {"x": x})["y"] * 256).astype(np.int64)
+    # matmul Q8.8, with saturation, and a batched case
+    for ci, (bt, n_, k_, m_, lo, hi) in enumerate([(1, 7, 33, 5, -1, 1), (1, 16, 64, 24, -8, 8), (3, 5, 40, 9, -2, 2),
+                                                    (1, 1, 1568, 10, -1, 1)]):
+        a = q88(rng, (bt, n_, k_), lo, hi)
+        bb = q88(rng, (bt, k_, m_), lo, hi)
+        A, B, C = T(onnx_name="a", shape=[bt, n_, k_], dtype="float32"), T(onnx_name="b", shape=[bt, k_, m_], dtype="float32"), T(onnx_name="c", shape=[bt, n_, m_], dtype="float32")
+        node = N.MatmulNode(onnx_node=nd, inputs=[A, B], output=C, n=n_, k=k_, m=m_, batch=bt)
+        out[f"mm{ci}_a"], out[f"mm{ci}_b"] = a, bb
+        out[f"mm{ci}_c"] = np.round(run([node], [], [A, B], {"a": a, "b": bb})["c"] * 256).astype(np.int64)
+    # vectorop: every op with every act, broadcast b
+    a = q88(rng, (4, 3, 40), -3, 3)
+    b = q88(rng, (40,), -3, 3)
+    b = np.where(b == 0, 1, b)
+    out["vop_a"], out["vop_b"] = a, b
+    for op in range(10):
+        for act in range(7):
+            if op >= 6 and act:
+                continue
+            A = T(onnx_name="a", shape=[4, 3, 40], dtype="float32")
+            Bt = T(onnx_name="b", shape=[40], dtype="float32")
+            C = T(onnx_name="c", shape=[4, 3, 40], dtype="float32")
+            arity = 2 if op <= 3 else 1
+            node = N.ScheduledNode(onnx_node=nd, op_code=op, arity=arity, inputs=[A, Bt] if arity == 2 else [A], output=C)
+            node.act, node.alpha = act, 6554 if (act == 3 or op == 6) else 0
+            feeds = {"a": a, "b": b} if arity == 2 else {"a": a}
+            out[f"vop{op}_{act}"] = np.round(run([node], [], [A, Bt] if arity == 2 else [A], feeds)["c"] * 256).astype(np.int64)
+    return out
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--ref", default="/root/reference")
+    ap.add_argument("--only", choices=["hw", "sim"])
+    ap.add_argument("--out", default=HERE)
+    args = ap.parse_args()
+    if args.only in (None, "hw"):
+        convert_hw(args.ref, args.out)
+    if args.only in (None, "sim"):
+        make_sim(args.ref, args.out)
+
+
+if __name__ == "__main__":
+    main()
