@@ -1,0 +1,104 @@
+"""ctypes binding of libcorm_b200.so (include/cormorant_b200.h).
+
+The structures mirror the C descriptors field for field; ``check`` turns a
+negative status into ``CormError`` with the library's message.  Nothing here
+computes: without the built library (or without a GPU, for the job entry
+points) calls fail loudly — there is no CPU fallback.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+
+LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "libcorm_b200.so")
+
+CORM_OK, CORM_EINVAL, CORM_ELIMIT, CORM_ECUDA, CORM_ENOMEM, CORM_EDEVICE = 0, -1, -2, -3, -4, -5
+F_WRAP32, F_WEIGHT_LOGICAL, F_ACT_RELU, F_ACT_RELU6 = 0x1, 0x2, 0x4, 0x8
+
+# every symbol include/cormorant_b200.h declares
+EXPORTS = ("corm_vectorop", "corm_matmul_workspace_size", "corm_matmul", "corm_conv_workspace_size", "corm_conv",
+           "corm_pool", "corm_rowops", "corm_act_table", "corm_smx_table", "corm_rowops_table_image",
+           "corm_bind_device", "corm_device_status", "corm_version", "corm_last_error")
+
+
+class CormError(RuntimeError):
+    def __init__(self, code: int, msg: str):
+        super().__init__(f"libcorm_b200 error {code}: {msg}")
+        self.code = code
+
+
+def _u32_fields(names):
+    return [(n, C.c_uint32) for n in names]
+
+
+class VectorOpDesc(C.Structure):
+    _fields_ = [("a", C.c_void_p), ("b", C.c_void_p), ("c", C.c_void_p)] + _u32_fields(
+        ["size", "op", "outer", "a_inc", "b_inc", "act", "alpha", "smx_cm", "smx_cfg", "smx_mask"])
+
+
+class MatmulDesc(C.Structure):
+    _fields_ = [("a", C.c_void_p), ("b", C.c_void_p), ("c", C.c_void_p)] + _u32_fields(
+        ["n", "k", "m", "batch", "a_batch_stride", "b_batch_stride", "c_batch_stride", "b_packed", "gemv_kw",
+         "flags"]) + [("workspace", C.c_void_p), ("workspace_bytes", C.c_size_t)]
+
+
+class ConvDesc(C.Structure):
+    _fields_ = [("x", C.c_void_p), ("weight", C.c_void_p), ("bias", C.c_void_p), ("y", C.c_void_p)] + _u32_fields(
+        ["batch", "in_ch", "in_h", "in_w", "out_ch", "out_h", "out_w", "kh", "kw", "stride_h", "stride_w",
+         "dilation_h", "dilation_w", "pad_top", "pad_left", "has_bias", "is_depthwise", "y_cs", "y_cn", "y_gs",
+         "flags"]) + [("workspace", C.c_void_p), ("workspace_bytes", C.c_size_t)]
+
+
+class PoolDesc(C.Structure):
+    _fields_ = [("x", C.c_void_p), ("y", C.c_void_p)] + _u32_fields(
+        ["batch", "channels", "in_h", "in_w", "out_h", "out_w", "pool_h", "pool_w", "stride_h", "stride_w",
+         "pad_top", "pad_left", "dil_h", "dil_w", "pool_type", "lp_order", "count_include_pad"])
+
+
+class RowOpsDesc(C.Structure):
+    _fields_ = _u32_fields(["op", "n", "rows", "blocks"]) + [
+        ("a", C.c_void_p), ("a_s1", C.c_uint32), ("a_s2", C.c_uint32),
+        ("b", C.c_void_p), ("b_s1", C.c_uint32), ("b_s2", C.c_uint32),
+        ("c", C.c_void_p), ("c_s1", C.c_uint32), ("c_s2", C.c_uint32),
+        ("p", C.c_void_p), ("eps", C.c_uint64)] + _u32_fields(["aux", "bq_sh", "win_lo", "win_hi"])
+
+
+_lib = None
+
+
+def lib() -> C.CDLL:
+    """The loaded library (built on first use when nvcc is available)."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not os.path.exists(LIB_PATH):
+        try:
+            from . import build as _build
+            _build.build()
+        except Exception as e:  # pragma: no cover - surfaced to the caller
+            raise CormError(CORM_ECUDA, f"libcorm_b200.so is not built and the build failed: {e}") from e
+    L = C.CDLL(LIB_PATH)
+    for name, argt in (("corm_vectorop", [C.POINTER(VectorOpDesc), C.c_void_p]),
+                       ("corm_matmul", [C.POINTER(MatmulDesc), C.c_void_p]),
+                       ("corm_matmul_workspace_size", [C.POINTER(MatmulDesc), C.POINTER(C.c_size_t)]),
+                       ("corm_conv", [C.POINTER(ConvDesc), C.c_void_p]),
+                       ("corm_conv_workspace_size", [C.POINTER(ConvDesc), C.POINTER(C.c_size_t)]),
+                       ("corm_pool", [C.POINTER(PoolDesc), C.c_void_p]),
+                       ("corm_rowops", [C.POINTER(RowOpsDesc), C.c_void_p]),
+                       ("corm_act_table", [C.c_uint32, C.c_uint32, C.c_void_p]),
+                       ("corm_smx_table", [C.c_void_p]),
+                       ("corm_rowops_table_image", [C.c_void_p]),
+                       ("corm_bind_device", [C.c_int]),
+                       ("corm_device_status", [C.POINTER(C.c_int)])):
+        f = getattr(L, name)
+        f.argtypes = argt
+        f.restype = C.c_int
+    L.corm_version.restype = C.c_char_p
+    L.corm_last_error.restype = C.c_char_p
+    _lib = L
+    return L
+
+
+def check(rc: int) -> None:
+    if rc != CORM_OK:
+        raise CormError(rc, lib().corm_last_error().decode(errors="replace"))

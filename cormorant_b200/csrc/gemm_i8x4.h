@@ -1,0 +1,51 @@
+// Exact int16 x int16 GEMM on the int8 tensor cores (tcgen05 kind::i8): the
+// shared engine of MatmulKernel and ConvKernel jobs.
+//
+// Each int16 operand arrives split into planes hi = v >> 8 (signed byte) and
+// lo = v & 255 (unsigned byte), K-major [batch][rows][Kp] (Kp a multiple of
+// 16, zero padded).  Per 128 x 128 output tile three int32 TMEM accumulators
+// collect HH = sum a_hi b_hi, MID = sum a_hi b_lo + a_lo b_hi and LL = sum a_lo
+// b_lo — exact for K <= 32768 — and the epilogue forms the exact sum
+// 2^16 HH + 2^8 MID + LL (+ bias << 8) in int64, applies the job's rule
+// (optional int32 wrap, floor >> 8, saturation, optional ReLU / Clip(0,6))
+// and stores int16.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace corm {
+
+struct GemmJob {
+  const int8_t* a_hi;
+  const uint8_t* a_lo;
+  const int8_t* b_hi;
+  const uint8_t* b_lo;
+  uint32_t rows, cols, Kp, batch;
+  uint32_t a_planes, b_planes;  // 1 (broadcast) or batch
+  // epilogue addressing
+  int mode;                 // 0: out[b*obs + r*ldc + c]; 1: conv NCHW y[n][pattern(c)][p], r = n*P + p
+  int16_t* out;
+  uint64_t out_batch_stride;
+  uint32_t ldc;
+  uint32_t P, y_cn, y_cs, y_gs;
+  uint64_t img_stride;      // mode 1: elements per image (out_ch * P)
+  const int16_t* bias;      // mode 1 bias per column (raw), or nullptr
+  uint32_t flags;           // CORM_F_WRAP32 | CORM_F_ACT_RELU | CORM_F_ACT_RELU6
+};
+
+constexpr uint32_t kGemmMaxK = 32768;
+
+// Launch the tcgen05 GEMM (error code, 0 on success).
+int gemm_i8x4(const GemmJob& job, cudaStream_t stream);
+
+// Split an int16 matrix into the hi / lo planes, rows K-major:
+//   dst row (b, r) element kk <- src[b*src_bs + r*ld + kk*ks]   (kk < K, zero to Kp)
+// with a generic element stride ks (1: rows contiguous; m: a transposed read).
+int split_planes(const int16_t* src, uint64_t src_bs, uint32_t planes, uint32_t rows, uint64_t ld, uint32_t K,
+                 uint32_t Kp, int8_t* hi, uint8_t* lo, cudaStream_t stream);
+
+// Per-device word the kernels' bounded waits write on a timeout.
+int* device_error_word();
+
+}  // namespace corm

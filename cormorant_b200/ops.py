@@ -1,0 +1,154 @@
+"""Per-op host API over the C ABI: one function per kernel, taking torch CUDA
+tensors (the buffers) and the register values, launched on the current torch
+stream.  These are the calls the reference's generated ``run_op`` /
+``run_matmul`` / ``run_conv`` / ``run_pool`` / ``run_softmax`` /
+``run_rowops`` make (phoenix367/cormorant inference-scheduler/src/codegen/
+_source.py:1112-1580), with device tensors in place of DMA buffers.
+
+Errors: a descriptor the kernel's contract rejects raises ``CormError``
+(nothing launched), as the reference raises ``SchedulerError`` /
+``ValueError`` before emitting a call.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import threading
+
+import torch
+
+from . import _lib
+from ._lib import CormError, check, lib  # noqa: F401
+
+_tls = threading.local()
+
+
+def _ptr(t) -> int:
+    if t is None:
+        return 0
+    if isinstance(t, int):
+        return t
+    if not t.is_cuda:
+        raise CormError(_lib.CORM_EINVAL, "operand is not a CUDA tensor (the library has no CPU path)")
+    return t.data_ptr()
+
+
+def _ready() -> int:
+    """Bind the library's runtime to torch's current device (once per thread
+    and device) and return the current stream handle."""
+    dev = torch.cuda.current_device()
+    if getattr(_tls, "dev", None) != dev:
+        check(lib().corm_bind_device(dev))
+        _tls.dev = dev
+    return torch.cuda.current_stream().cuda_stream
+
+
+def _i16(t, name):
+    if t is not None and t.dtype != torch.int16:
+        raise CormError(_lib.CORM_EINVAL, f"{name} must be int16, got {t.dtype}")
+
+
+def vectorop(a, b, c, *, size, op, outer=1, a_inc=0, b_inc=0, act=0, alpha=0, smx_cm=0, smx_cfg=0, smx_mask=0):
+    """One VectorOPKernel job (host_emu.py:244-293): element offsets from the
+    tensors' data pointers."""
+    for t, n in ((a, "a"), (b, "b"), (c, "c")):
+        _i16(t, n)
+    st = _ready()
+    d = _lib.VectorOpDesc(_ptr(a), _ptr(b), _ptr(c), size, op, outer, a_inc, b_inc, act, alpha & 0xFFFFFFFF,
+                          smx_cm, smx_cfg, smx_mask)
+    check(lib().corm_vectorop(C.byref(d), st))
+
+
+def matmul(a, b, c, *, n, k, m, batch=1, a_batch_stride=0, b_batch_stride=0, c_batch_stride=0, b_packed=0,
+           gemv_kw=0, flags=0, workspace=None):
+    """One MatmulKernel job (host_emu.py:338-362).  ``workspace``: a uint8
+    CUDA tensor, or None to take one from torch's allocator."""
+    for t, nm in ((a, "a"), (b, "b"), (c, "c")):
+        _i16(t, nm)
+    st = _ready()
+    d = _lib.MatmulDesc(_ptr(a), _ptr(b), _ptr(c), n, k, m, batch, a_batch_stride, b_batch_stride, c_batch_stride,
+                        b_packed, gemv_kw, flags, None, 0)
+    need = C.c_size_t(0)
+    check(lib().corm_matmul_workspace_size(C.byref(d), C.byref(need)))
+    if need.value:
+        if workspace is None:
+            workspace = torch.empty(need.value, dtype=torch.uint8, device=a.device)
+        d.workspace, d.workspace_bytes = _ptr(workspace), workspace.numel() * workspace.element_size()
+    check(lib().corm_matmul(C.byref(d), st))
+    return workspace
+
+
+def conv(x, weight, bias, y, *, batch, in_ch, in_h, in_w, out_ch, out_h, out_w, kh, kw, stride_h=1, stride_w=1,
+         dilation_h=1, dilation_w=1, pad_top=0, pad_left=0, has_bias=0, is_depthwise=0, y_cs=0, y_cn=0, y_gs=0,
+         flags=0, workspace=None):
+    """One ConvKernel job (host_emu.py:393-455); CORM_F_WEIGHT_LOGICAL in
+    ``flags`` for [M][C][kh][kw] weights instead of the board image."""
+    for t, nm in ((x, "x"), (weight, "weight"), (bias, "bias"), (y, "y")):
+        _i16(t, nm)
+    st = _ready()
+    d = _lib.ConvDesc(_ptr(x), _ptr(weight), _ptr(bias), _ptr(y), batch, in_ch, in_h, in_w, out_ch, out_h, out_w,
+                      kh, kw, stride_h, stride_w, dilation_h, dilation_w, pad_top, pad_left, int(bool(has_bias)),
+                      int(bool(is_depthwise)), y_cs, y_cn, y_gs, flags, None, 0)
+    need = C.c_size_t(0)
+    check(lib().corm_conv_workspace_size(C.byref(d), C.byref(need)))
+    if need.value:
+        if workspace is None:
+            workspace = torch.empty(need.value, dtype=torch.uint8, device=x.device)
+        d.workspace, d.workspace_bytes = _ptr(workspace), workspace.numel() * workspace.element_size()
+    check(lib().corm_conv(C.byref(d), st))
+    return workspace
+
+
+def pool(x, y, *, batch, channels, in_h, in_w, out_h, out_w, pool_h, pool_w, stride_h=1, stride_w=1, pad_top=0,
+         pad_left=0, dil_h=1, dil_w=1, pool_type=0, lp_order=0, count_include_pad=0):
+    """One PoolingKernel job (_simulate.py:275-358 semantics)."""
+    _i16(x, "x")
+    _i16(y, "y")
+    st = _ready()
+    d = _lib.PoolDesc(_ptr(x), _ptr(y), batch, channels, in_h, in_w, out_h, out_w, pool_h, pool_w, stride_h,
+                      stride_w, pad_top, pad_left, dil_h, dil_w, pool_type, lp_order, count_include_pad)
+    check(lib().corm_pool(C.byref(d), st))
+
+
+def rowops(a, b, c, p, *, op, n, rows=1, blocks=1, a_s1=0, a_s2=0, b_s1=0, b_s2=0, c_s1=0, c_s2=0, eps=0, aux=0,
+           bq_sh=0, win_lo=0, win_hi=0xFFFFFFFF, a_off=0, b_off=0, c_off=0, p_off=0):
+    """One RowOpsKernel job (rowops_ref.h:259-427): byte strides; a / b / c /
+    p are tensors (any dtype) or raw device addresses, plus byte offsets."""
+    st = _ready()
+
+    def addr(t, off):
+        return (_ptr(t) + off) if t is not None else 0
+    d = _lib.RowOpsDesc(op, n, rows, blocks, addr(a, a_off), a_s1 & 0xFFFFFFFF, a_s2 & 0xFFFFFFFF, addr(b, b_off),
+                        b_s1 & 0xFFFFFFFF, b_s2 & 0xFFFFFFFF, addr(c, c_off), c_s1 & 0xFFFFFFFF, c_s2 & 0xFFFFFFFF,
+                        addr(p, p_off), eps & 0xFFFFFFFFFFFFFFFF, aux, bq_sh, win_lo & 0xFFFFFFFF,
+                        win_hi & 0xFFFFFFFF)
+    check(lib().corm_rowops(C.byref(d), st))
+
+
+def device_status() -> int:
+    """Synchronise and return (and clear) the kernels' timeout status word."""
+    _ready()
+    code = C.c_int(0)
+    check(lib().corm_device_status(C.byref(code)))
+    return code.value
+
+
+# ---------------------------------------------------------------- host-side tables (no GPU needed)
+def act_table(act: int, alpha: int = 0):
+    import numpy as np
+    out = np.zeros(65536, np.int16)
+    check(lib().corm_act_table(act, alpha & 0xFFFFFFFF, out.ctypes.data))
+    return out
+
+
+def smx_table():
+    import numpy as np
+    out = np.zeros(4096, np.int32)
+    check(lib().corm_smx_table(out.ctypes.data))
+    return out
+
+
+def rowops_table_image():
+    import numpy as np
+    out = np.zeros(65536, np.uint8)
+    check(lib().corm_rowops_table_image(out.ctypes.data))
+    return out

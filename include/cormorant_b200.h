@@ -1,0 +1,182 @@
+/*
+ * cormorant_b200.h — C ABI of the B200 (sm_100a) implementation of the
+ * Cormorant fixed-point kernels: VectorOPKernel (with its activation and
+ * softmax units), MatmulKernel, ConvKernel, PoolingKernel and RowOpsKernel.
+ *
+ * Each entry point takes one job descriptor whose fields are the kernel's
+ * register block — the same names, units and meaning as the reference's
+ * emulated Xilinx drivers (phoenix367/cormorant
+ * inference-scheduler/test/host_emu.py) — with DEVICE pointers in place of
+ * the physical addresses, plus a CUDA stream.  Calls are stream-ordered and
+ * non-blocking (the reference's run_* + kernel_wait pair becomes a launch
+ * and a stream synchronise).  Buffers are caller-owned; a job only reads its
+ * inputs and writes its output region.
+ *
+ * Return value: CORM_OK (0), or a negative CORM_E* code for a descriptor the
+ * kernel's contract rejects (nothing is launched then) or a CUDA error.
+ * corm_last_error() describes the last failure of the calling thread.
+ *
+ * Element types: int16 storage integers (Q8.8 = ap_fixed<16,8>, or a tensor
+ * at a power-of-two exponent); row-ops rows are int16 / int32 / float32 as
+ * the op word's kind fields say.
+ */
+#ifndef CORMORANT_B200_H
+#define CORMORANT_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st* corm_stream_t; /* a cudaStream_t; NULL = legacy default stream */
+
+enum {
+  CORM_OK = 0,
+  CORM_EINVAL = -1,  /* a field outside the kernel's contract */
+  CORM_ELIMIT = -2,  /* a size beyond this implementation's limit */
+  CORM_ECUDA = -3,   /* a CUDA runtime error (launch, copy, device) */
+  CORM_ENOMEM = -4,  /* workspace too small or allocation failed */
+  CORM_EDEVICE = -5  /* the current device is not sm_100 */
+};
+
+/* Flags shared by MatMul and Conv. */
+#define CORM_F_WRAP32 0x1u          /* wrap the exact sum to int32 before the shift (the hardware
+                                       accumulator; the simulator's exponent path) */
+#define CORM_F_WEIGHT_LOGICAL 0x2u  /* Conv: weight is [out_ch][in_ch | 1][kh][kw], bias [out_ch]
+                                       (the simulator's view) instead of the board images */
+#define CORM_F_ACT_RELU 0x4u        /* fuse max(y, 0) after the saturation (Conv/MatMul + Relu) */
+#define CORM_F_ACT_RELU6 0x8u       /* fuse min(max(y, 0), 6.0) (Clip(0,6)) */
+
+/* ---------------------------------------------------------------- VectorOP
+ * Replaces XVectoropkernel_Set_* / XVectoropkernel_Start
+ * (inference-scheduler/test/host_emu.py:176-293; kernels/vectorop_rtl/model/
+ * include/VectorOP.h:279-333).  c[o*(a_inc+b_inc)+i] = act(op(a[o*a_inc+i],
+ * b[o*b_inc+i])) for o < outer, i < size; the last 8-lane word of every
+ * output row is written whole with zero tail lanes.  op 0..5 ADD SUB MUL DIV
+ * RELU RELU6, 6..9 LEAKY_RELU SILU GELU GELU_TANH, 10/11 softmax row /
+ * keys-major column mode (rows at b_inc; smx_cm, smx_cfg = Cs | f_p << 8,
+ * smx_mask = valid0 | period << 16).  act 0..6 NONE RELU RELU6 LEAKY_RELU
+ * SILU GELU GELU_TANH; LeakyReLU slope alpha[15:0] / 2^16. */
+typedef struct {
+  const int16_t* a;
+  const int16_t* b;  /* unused (may be NULL) for ops 4..11 */
+  int16_t* c;
+  uint32_t size, op, outer, a_inc, b_inc, act, alpha, smx_cm, smx_cfg, smx_mask;
+} corm_vectorop_desc;
+
+int corm_vectorop(const corm_vectorop_desc* d, corm_stream_t stream);
+
+/* ---------------------------------------------------------------- MatMul
+ * Replaces XMatmulkernel_Set_* / XMatmulkernel_Start (host_emu.py:312-362;
+ * kernels/matmul_rtl/model/include/MatmulKernel.h:195-242).  Per batch slice
+ * C[r][j] = sat16(floor(sum_kk A[r][kk] B[kk][j] / 2^8)), A [n][k] and C
+ * [n][m] row-major, B row-major [k][m], packed tile-major [ceil(m/32)][k][32]
+ * (b_packed) or the GEMV image of width gemv_kw; batch strides in elements,
+ * 0 = broadcast.  k <= 4096 (platforms/kv260.json kernels.matmul.max_k).
+ * The sum is exact (int64) unless CORM_F_WRAP32.  workspace: device scratch
+ * of corm_matmul_workspace_size() bytes (256-byte aligned), or NULL to let the
+ * library use its own per-device scratch (grown on demand with cudaMalloc). */
+typedef struct {
+  const int16_t* a;
+  const int16_t* b;
+  int16_t* c;
+  uint32_t n, k, m, batch, a_batch_stride, b_batch_stride, c_batch_stride, b_packed, gemv_kw;
+  uint32_t flags;
+  void* workspace;
+  size_t workspace_bytes;
+} corm_matmul_desc;
+
+int corm_matmul_workspace_size(const corm_matmul_desc* d, size_t* bytes);
+int corm_matmul(const corm_matmul_desc* d, corm_stream_t stream);
+
+/* ---------------------------------------------------------------- Conv
+ * Replaces XConvkernel_Set_* / XConvkernel_Start (host_emu.py:372-455;
+ * kernels/conv_rtl/model/include/ConvKernel.h:229).  y[n][m][oh][ow] =
+ * sat16(floor((bias[m] << 8 + sum x w) / 2^8)), x NCHW with zero padding,
+ * group 1 or depthwise; weight/bias as the board images (packed tile-major
+ * [M][ceil(C/16)][kh][kw][lanes], depthwise [M][roundup(kh*kw,8)], bias
+ * word-padded) or logical with CORM_F_WEIGHT_LOGICAL.  Output channel m at
+ * (m mod y_cn)*y_cs + (m div y_cn)*y_gs elements (dense when y_cn = y_cs = 0).
+ * kh, kw <= 7 and in_ch*kh*kw <= 32768 for group 1 (int32 accumulators stay exact). */
+typedef struct {
+  const int16_t* x;
+  const int16_t* weight;
+  const int16_t* bias; /* may be NULL when has_bias == 0 */
+  int16_t* y;
+  uint32_t batch, in_ch, in_h, in_w, out_ch, out_h, out_w, kh, kw, stride_h, stride_w, dilation_h,
+      dilation_w, pad_top, pad_left, has_bias, is_depthwise, y_cs, y_cn, y_gs;
+  uint32_t flags;
+  void* workspace;
+  size_t workspace_bytes;
+} corm_conv_desc;
+
+int corm_conv_workspace_size(const corm_conv_desc* d, size_t* bytes);
+int corm_conv(const corm_conv_desc* d, corm_stream_t stream);
+
+/* ---------------------------------------------------------------- Pool
+ * Replaces run_pool / XPoolingkernel (inference-scheduler/src/codegen/
+ * _source.py:1548-1580; semantics inference-scheduler/src/codegen/
+ * _simulate.py:230-358).  NCHW int16; pool_type 0 MAX, 1 AVG, 2 LP
+ * (lp_order 1 or 2); window <= 7x7 except a global window (out 1x1, pool =
+ * in). */
+typedef struct {
+  const int16_t* x;
+  int16_t* y;
+  uint32_t batch, channels, in_h, in_w, out_h, out_w, pool_h, pool_w, stride_h, stride_w, pad_top,
+      pad_left, dil_h, dil_w, pool_type, lp_order, count_include_pad;
+} corm_pool_desc;
+
+int corm_pool(const corm_pool_desc* d, corm_stream_t stream);
+
+/* ---------------------------------------------------------------- RowOps
+ * Replaces XRowopskernel_Set_* / XRowopskernel_Start (host_emu.py:464-750;
+ * kernels/rowops_rtl/tb/verilator/rowops_ref.h:259-427).  op word: [3:0] op
+ * (1 COPY, 2 ADDX, 3 DEQUANT, 4 MULACT, 5 NORM, 6 ROPE, 7 XPOSE, 8 TLOAD,
+ * 9 FOLD, 10 GATE), [5:4] [7:6] [9:8] A/B/C kinds (0 int16, 1 int32, 2 f32),
+ * bit 12 B_EN, 13 P_BCAST, 14 P_KEEP, 15 RELU, 16 NORM_LN, 17 SCALE.  Strides
+ * in BYTES; row (i2, i1) of A at a + i2*a_s2 + i1*a_s1.  p: the parameter
+ * block, 16 bytes per column.  TLOAD reads the 64 KiB table image from a.
+ * n <= 4096. */
+typedef struct {
+  uint32_t op, n, rows, blocks;
+  const void* a;
+  uint32_t a_s1, a_s2;
+  const void* b;
+  uint32_t b_s1, b_s2;
+  void* c;
+  uint32_t c_s1, c_s2;
+  const void* p;
+  uint64_t eps;
+  uint32_t aux, bq_sh, win_lo, win_hi;
+} corm_rowops_desc;
+
+int corm_rowops(const corm_rowops_desc* d, corm_stream_t stream);
+
+/* ---------------------------------------------------------------- host-side helpers (no GPU) */
+/* The activation unit's output for every Q8.8 input (raw -32768 .. 32767 at
+ * out[raw + 32768]) — vectorop_act.kernel_table (vectorop_act.py:92-95). */
+int corm_act_table(uint32_t act, uint32_t alpha, int16_t* out65536);
+/* The softmax unit's TAB[k] = round(2^16 2^(-k/4096)), k < 4096 (vectorop_smx.py:29). */
+int corm_smx_table(int32_t* out4096);
+/* The 64 KiB OP_TLOAD table image (rowops_spec.table_image, rowops_spec.py:603-616). */
+int corm_rowops_table_image(uint8_t* out65536);
+
+/* ---------------------------------------------------------------- device plumbing */
+/* Make `device` current for this library's runtime on the calling thread (the
+ * library links the CUDA runtime statically; a host that selects devices with
+ * its own runtime calls this once per thread). */
+int corm_bind_device(int device);
+/* Synchronise the current device, then read and clear the status word that the
+ * kernels' bounded waits set when a wait times out (0 = none).  Replaces the
+ * reference's kernel_wait timeout accounting (runtime/inference_irq.c:259-264). */
+int corm_device_status(int* code);
+/* Library version string and the last error message of the calling thread. */
+const char* corm_version(void);
+const char* corm_last_error(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* CORMORANT_B200_H */

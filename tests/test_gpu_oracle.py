@@ -1,0 +1,269 @@
+"""GPU parity against the CPU oracle (oracle/spec.py) on seeded inputs: the
+tensor-core GEMM path of MatMul and Conv, saturation and int32 wrap, the
+softmax unit in both modes with causal masks, the activation unit, pooling
+and row-ops — bit-exact."""
+import numpy as np
+import pytest
+
+torch = pytest.importorskip("torch")
+
+from oracle import spec  # noqa: E402
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def ops():
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    from cormorant_b200 import ops as o
+    return o
+
+
+def dev(a):
+    return torch.from_numpy(np.ascontiguousarray(a)).cuda()
+
+
+def rnd16(rng, shape, lo=-32768, hi=32768):
+    return rng.integers(lo, hi, size=shape).astype(np.int16)
+
+
+MM_CASES = [  # n, k, m, batch, a_bs0, b_bs0, lo, hi
+    (17, 33, 5, 1, False, False, -256, 256),
+    (128, 64, 32, 1, False, False, -256, 256),
+    (129, 129, 129, 1, False, False, -32768, 32768),
+    (200, 300, 130, 3, False, False, -300, 300),
+    (64, 512, 256, 4, True, False, -256, 256),
+    (96, 1000, 40, 3, False, True, -256, 256),
+    (300, 4096, 300, 1, False, False, -256, 256),
+    (256, 256, 256, 2, False, False, -32768, 32768),
+    (1, 4096, 1000, 1, False, False, -256, 256),
+    (8, 1024, 4096, 2, False, False, -256, 256),
+    (16, 4096, 32, 16, False, False, -256, 256),
+    (3, 7, 5, 2, True, False, -32768, 32768),
+]
+
+
+@pytest.mark.parametrize("case", MM_CASES)
+@pytest.mark.parametrize("wrap", [False, True])
+def test_matmul_vs_oracle(ops, case, wrap):
+    n, k, m, batch, a_bc, b_bc, lo, hi = case
+    rng = np.random.default_rng(n * 7 + k * 13 + m + batch)
+    A = rnd16(rng, (1 if a_bc else batch, n, k), lo, hi)
+    B = rnd16(rng, (1 if b_bc else batch, k, m), lo, hi)
+    c = torch.full((batch * n * m,), -8531, dtype=torch.int16, device="cuda")
+    ops.matmul(dev(A.reshape(-1)), dev(B.reshape(-1)), c, n=n, k=k, m=m, batch=batch,
+               a_batch_stride=0 if a_bc else n * k, b_batch_stride=0 if b_bc else k * m, c_batch_stride=n * m,
+               flags=1 if wrap else 0)
+    exp = spec.matmul_raw(np.broadcast_to(A, (batch, n, k)), np.broadcast_to(B, (batch, k, m)), wrap=wrap)
+    assert np.array_equal(c.cpu().numpy().reshape(batch, n, m), exp)
+
+
+@pytest.mark.parametrize("packed,kw", [(1, 0), (0, 2), (0, 4), (0, 8)])
+def test_matmul_layouts_tensor_path(ops, packed, kw):
+    """Packed-B and GEMV images on the split / tensor-core path (n > 16)."""
+    rng = np.random.default_rng(3 + kw)
+    n, k, m = 40, 256, 72
+    A = rnd16(rng, (n, k), -300, 300)
+    Bl = rnd16(rng, (k, m), -300, 300)
+    idx = spec.b_index(k, m, packed, kw)
+    img = np.zeros(int(idx.max()) + 1 + 64, np.int16)
+    img[idx] = Bl
+    c = torch.zeros(n * m, dtype=torch.int16, device="cuda")
+    ops.matmul(dev(A.reshape(-1)), dev(img), c, n=n, k=k, m=m, batch=1, b_packed=packed, gemv_kw=kw)
+    assert np.array_equal(c.cpu().numpy().reshape(n, m), spec.matmul_raw(A, Bl))
+
+
+CONV_CASES = [  # N, C, H, W, M, kh, kw, sh, sw, pt, pl, dh, dw, depthwise, bias
+    (1, 1, 28, 28, 16, 3, 3, 1, 1, 1, 1, 1, 1, False, True),
+    (1, 16, 14, 14, 32, 3, 3, 1, 1, 1, 1, 1, 1, False, True),
+    (2, 3, 33, 31, 32, 3, 3, 2, 2, 1, 1, 1, 1, False, True),
+    (1, 24, 20, 20, 144, 1, 1, 1, 1, 0, 0, 1, 1, False, False),
+    (2, 144, 10, 10, 144, 3, 3, 2, 2, 1, 1, 1, 1, True, True),
+    (1, 32, 9, 9, 32, 3, 3, 1, 1, 2, 2, 2, 2, True, False),
+    (3, 40, 7, 9, 70, 5, 3, 1, 2, 2, 1, 1, 1, False, True),
+    (1, 160, 7, 7, 960, 1, 1, 1, 1, 0, 0, 1, 1, False, True),
+]
+
+
+@pytest.mark.parametrize("case", CONV_CASES)
+@pytest.mark.parametrize("act", [0, 4, 8])
+def test_conv_vs_oracle(ops, case, act):
+    N, C, H, W, M, kh, kw, sh, sw, pt, pl, dh, dw, dwise, hb = case
+    rng = np.random.default_rng(N + C * 3 + M * 5 + kh)
+    oh = (H + 2 * pt - (dh * (kh - 1) + 1)) // sh + 1
+    ow = (W + 2 * pl - (dw * (kw - 1) + 1)) // sw + 1
+    x = rnd16(rng, (N, C, H, W), -256, 256)
+    w = rnd16(rng, (M, 1 if dwise else C, kh, kw), -128, 128)
+    b = rnd16(rng, (M,), -256, 256)
+    y = torch.full((N * M * oh * ow,), -8531, dtype=torch.int16, device="cuda")
+    ops.conv(dev(x.reshape(-1)), dev(w.reshape(-1)), dev(b) if hb else None, y, batch=N, in_ch=C, in_h=H, in_w=W,
+             out_ch=M, out_h=oh, out_w=ow, kh=kh, kw=kw, stride_h=sh, stride_w=sw, dilation_h=dh, dilation_w=dw,
+             pad_top=pt, pad_left=pl, has_bias=hb, is_depthwise=dwise, flags=2 | act)
+    exp = spec.conv_raw(x, w, b if hb else None, sh, sw, pt, pl, dh, dw, oh, ow, dwise)
+    if act == 4:
+        exp = np.maximum(exp, 0)
+    elif act == 8:
+        exp = np.clip(exp, 0, 1536)
+    assert np.array_equal(y.cpu().numpy().reshape(N, M, oh, ow), exp)
+
+
+def test_conv_wrap(ops):
+    """Large operands: the exact sum leaves int32; CORM_F_WRAP32 wraps it."""
+    rng = np.random.default_rng(9)
+    x = rnd16(rng, (1, 64, 6, 6), 20000, 32767)
+    w = rnd16(rng, (8, 64, 3, 3), 20000, 32767)
+    for wrap in (0, 1):
+        y = torch.zeros(8 * 16, dtype=torch.int16, device="cuda")
+        ops.conv(dev(x.reshape(-1)), dev(w.reshape(-1)), None, y, batch=1, in_ch=64, in_h=6, in_w=6, out_ch=8,
+                 out_h=4, out_w=4, kh=3, kw=3, flags=2 | wrap)
+        exp = spec.conv_raw(x, w, None, 1, 1, 0, 0, 1, 1, 4, 4, False, wrap=bool(wrap))
+        assert np.array_equal(y.cpu().numpy().reshape(1, 8, 4, 4), exp)
+
+
+@pytest.mark.parametrize("op", [0, 1, 2, 3, 4, 5, 6, 7, 8, 9])
+@pytest.mark.parametrize("act", [0, 1, 2, 3, 4, 5, 6])
+def test_vectorop_vs_oracle(ops, op, act):
+    rng = np.random.default_rng(op * 10 + act)
+    size, outer = 1000, 37
+    a = rnd16(rng, (outer * 1000 + 64,))
+    b = rnd16(rng, (1000 + 64,))
+    c_len = (outer - 1) * 1000 + 1000
+    c = torch.full((c_len + 8,), -8531, dtype=torch.int16, device="cuda")
+    regs = dict(size=size, op=op, outer=outer, a_inc=1000, b_inc=0, act=act, alpha=0x12345678)
+    ops.vectorop(dev(a), dev(b), c, **regs)
+    exp = np.full(c_len + 8, -8531, np.int16)
+    spec.vectorop_job(a, b, exp, **regs)
+    assert np.array_equal(c.cpu().numpy(), exp)
+
+
+@pytest.mark.parametrize("n", [1, 7, 128, 255, 1000, 1024, 2048, 4096, 10000])
+@pytest.mark.parametrize("mask", [0, "full", "causal"])
+def test_softmax_rows(ops, n, mask):
+    rng = np.random.default_rng(n)
+    rows = 24
+    W = (n + 7) // 8 * 8
+    x = rng.integers(-2048, 2048, size=(rows, W)).astype(np.int16)
+    cm, cs = spec.smx_scale_regs(8, 1.0)
+    m = {0: 0, "full": n, "causal": max(1, n // 4) | (5 << 16)}[mask]
+    regs = dict(size=n, op=10, outer=rows, a_inc=W, b_inc=W, smx_cm=cm, smx_cfg=cs | (8 << 8), smx_mask=m)
+    c = torch.full((rows * W,), -8531, dtype=torch.int16, device="cuda")
+    ops.vectorop(dev(x.reshape(-1)), None, c, **regs)
+    exp = np.full(rows * W, -8531, np.int16)
+    spec.vectorop_job(x.reshape(-1), None, exp, **regs)
+    assert np.array_equal(c.cpu().numpy(), exp)
+
+
+@pytest.mark.parametrize("keys", [1, 37, 128, 384, 1024, 4096])
+@pytest.mark.parametrize("queries", [16, 50, 96])
+def test_softmax_cols(ops, keys, queries):
+    rng = np.random.default_rng(keys + queries)
+    a_inc = (queries + 7) // 8 * 8
+    W = (keys + 7) // 8 * 8
+    s = rng.integers(-4096, 4096, size=(keys, a_inc)).astype(np.int16)
+    cm, cs = spec.smx_scale_regs(10, 0.125)
+    regs = dict(size=keys, op=11, outer=queries, a_inc=a_inc, b_inc=W, smx_cm=cm, smx_cfg=cs | (12 << 8),
+                smx_mask=max(1, keys // 3) | (3 << 16))
+    rows = queries & ~15
+    c = torch.full((max(rows, 1) * W + 8,), -8531, dtype=torch.int16, device="cuda")
+    ops.vectorop(dev(s.reshape(-1)), None, c, **regs)
+    exp = np.full(max(rows, 1) * W + 8, -8531, np.int16)
+    spec.vectorop_job(s.reshape(-1), None, exp, **regs)
+    assert np.array_equal(c.cpu().numpy(), exp)
+
+
+POOL_CASES = [  # N, C, H, W, ph, pw, sh, sw, pt, pl, dh, dw, type, lp, cip
+    (2, 16, 28, 28, 2, 2, 2, 2, 0, 0, 1, 1, 0, 0, 0),
+    (1, 5, 13, 11, 3, 3, 2, 2, 1, 1, 1, 1, 1, 0, 0),
+    (1, 5, 13, 11, 3, 3, 2, 2, 1, 1, 1, 1, 1, 0, 1),
+    (2, 3, 9, 9, 3, 2, 1, 2, 1, 0, 2, 1, 2, 1, 0),
+    (2, 3, 9, 9, 3, 3, 2, 2, 1, 1, 1, 1, 2, 2, 0),
+    (4, 1280, 7, 7, 7, 7, 1, 1, 0, 0, 1, 1, 1, 0, 0),
+    (2, 64, 7, 7, 7, 7, 1, 1, 0, 0, 1, 1, 0, 0, 0),
+    (2, 64, 8, 8, 8, 8, 1, 1, 0, 0, 1, 1, 2, 2, 0),
+    (1, 3, 4, 4, 3, 3, 3, 3, 2, 2, 1, 1, 0, 0, 0),
+]
+
+
+@pytest.mark.parametrize("case", POOL_CASES)
+def test_pool_vs_oracle(ops, case):
+    N, C, H, W, ph, pw, sh, sw, pt, pl, dh, dw, typ, lp, cip = case
+    rng = np.random.default_rng(C + H)
+    oh = (H + 2 * pt - (dh * (ph - 1) + 1)) // sh + 1
+    ow = (W + 2 * pl - (dw * (pw - 1) + 1)) // sw + 1
+    x = rnd16(rng, (N, C, H, W))
+    y = torch.full((N * C * oh * ow,), -8531, dtype=torch.int16, device="cuda")
+    ops.pool(dev(x.reshape(-1)), y, batch=N, channels=C, in_h=H, in_w=W, out_h=oh, out_w=ow, pool_h=ph, pool_w=pw,
+             stride_h=sh, stride_w=sw, pad_top=pt, pad_left=pl, dil_h=dh, dil_w=dw, pool_type=typ, lp_order=lp,
+             count_include_pad=cip)
+    exp = spec.pool_raw(x, ph, pw, sh, sw, pt, pl, dh, dw, oh, ow, typ, lp, cip)
+    assert np.array_equal(y.cpu().numpy().reshape(N, C, oh, ow), exp)
+
+
+def _param_block(rng, n, sa_max=8, sc_lo=8, sc_hi=30):
+    pb = np.zeros((n, 16), np.uint8)
+    g = rng.integers(1, 1 << 24, size=n).astype(np.int64)
+    bq = rng.integers(-(1 << 21), 1 << 21, size=n).astype(np.int64)
+    pb[:, 0:4] = (g & 0xFFFFFFFF).astype("<u4").view(np.uint8).reshape(n, 4)
+    pb[:, 4:8] = (bq & 0xFFFFFFFF).astype("<u4").view(np.uint8).reshape(n, 4)
+    pb[:, 8] = rng.integers(0, sa_max, size=n)
+    pb[:, 9] = rng.integers(0, sa_max, size=n)
+    pb[:, 10] = rng.integers(sc_lo, sc_hi, size=n)
+    return pb.reshape(-1)
+
+
+ROWOPS_JOBS = [  # op word, n, rows, blocks, kind bytes of a / c
+    ("copy", 1 | spec.F_B_EN, 96, 5, 2),
+    ("addx_i32", 2 | (1 << 4) | (0 << 6) | (1 << 8) | spec.F_B_EN | spec.F_RELU, 40, 3, 1),
+    ("scale", 1 | spec.F_SCALE, 64, 4, 1),
+    ("mulact", 4 | spec.F_B_EN, 256, 4, 1),
+    ("gate", 10 | spec.F_B_EN, 100, 3, 1),
+    ("dequant", 3 | (1 << 4) | (2 << 8), 48, 3, 1),
+    ("rms", 5 | (1 << 4), 960, 3, 1),
+    ("ln", 5 | spec.F_NORM_LN, 768, 3, 1),
+    ("ln_bcast", 5 | spec.F_NORM_LN | spec.F_P_BCAST, 64, 6, 1),
+    ("rope", 6, 192, 4, 1),
+]
+
+
+@pytest.mark.parametrize("job", ROWOPS_JOBS, ids=[j[0] for j in ROWOPS_JOBS])
+def test_rowops_vs_oracle(ops, job):
+    name, op, n, rows, _ = job
+    rng = np.random.default_rng(len(name) * 31 + n)
+    ak, ck = (op >> 4) & 3, (op >> 8) & 3
+    nba = 2 if ak == 0 else 4
+    row_b = (n * 4 + 15) // 16 * 16
+    a = np.zeros(rows * row_b, np.uint8)
+    for r in range(rows):
+        vals = rng.integers(-30000, 30000, size=n) if nba == 2 else rng.integers(-(1 << 28), 1 << 28, size=n)
+        a[r * row_b:r * row_b + n * nba] = vals.astype("<i2" if nba == 2 else "<i4").view(np.uint8)
+    if name == "rope":
+        HD = 64
+        ang = rng.uniform(-3, 3, size=HD)
+        tab = np.concatenate([np.rint(np.cos(ang) * 2 ** 23), np.rint(np.sin(ang) * 2 ** 23)]).astype("<i4")
+        b = np.zeros(rows * row_b, np.uint8)
+        b[:tab.nbytes] = tab.view(np.uint8)
+        b_s1, aux = 0, HD
+    else:
+        b = rng.integers(0, 256, size=rows * row_b).astype(np.uint8)
+        b_s1, aux = row_b, 0
+    p = _param_block(rng, n, sa_max=4 if name in ("mulact", "gate") else 8,
+                     sc_lo=20 if name in ("rms", "ln", "ln_bcast") else 8, sc_hi=40)
+    eps = 12345 if name in ("rms", "ln", "ln_bcast") else 0
+    c_len = rows * row_b
+    mem = np.zeros(len(a) + len(b) + len(p) + c_len + 1024, np.uint8)
+    oa, ob, op_, oc = 0, (len(a) + 255) // 256 * 256, 0, 0
+    op_ = ob + (len(b) + 255) // 256 * 256
+    oc = op_ + (len(p) + 255) // 256 * 256
+    mem = np.zeros(oc + c_len + 256, np.uint8)
+    mem[oa:oa + len(a)] = a
+    mem[ob:ob + len(b)] = b
+    mem[op_:op_ + len(p)] = p
+    mem[oc:oc + c_len] = 0xDE
+    regs = dict(op=op, n=n, rows=rows, blocks=1, a_s1=row_b, a_s2=0, b_s1=b_s1, b_s2=0, c_s1=row_b, c_s2=0, eps=eps,
+                aux=aux, bq_sh=3)
+    buf = dev(mem)
+    ops.rowops(buf, buf, buf, buf, a_off=oa, b_off=ob, c_off=oc, p_off=op_, **regs)
+    m = spec.RowOpsMem(mem.copy())
+    spec.rowops_job(m, op, n, rows, 1, oa, row_b, 0, ob, b_s1, 0, oc, row_b, 0, op_, eps, aux, 3)
+    assert np.array_equal(buf.cpu().numpy(), m.buf)
