@@ -1,0 +1,509 @@
+#!/usr/bin/env python3
+"""Benchmark of the B200 fixed-point simulator kernels (
+the op-level sweep) — one JSON line on rank 0.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+A step is one pass of the MatMul sweep: M in {1, 8, 128, 2048} x K in {64, 512,
+1024, 4096} x N in {32, 256, 1024, 4096} x batch in {1, 16} (A and B both
+batched), int16 Q8.8 inputs uniform in [-1, 1), every product bit-exact
+(sat16(floor(sum / 2^8))).  ``value`` = sum of the sweep's int16 MACs / device
+time (GMAC/s, whole job over all ranks; each rank runs its own instance of the
+sweep: weak scaling).  The VectorOP (Add / Mul / Div with broadcast, fused SiLU /
+GELU-erf / GELU-tanh, 4M elements) and Softmax (rows 128 / 1024 / 4096, row and
+column mode) sweeps of the same config are measured after it and reported under
+``sweeps``.
+
+Timing: inputs resident in HBM, the sweep replayed as one CUDA graph, CUDA
+events on the launching stream, L2 flushed (256 MB write) between steps, max
+over ranks.  ``e2e`` repeats the sweep through the public per-op API with
+pinned host buffers (H2D of A and B, D2H of C inside the timed region).
+``roofline``: the tcgen05 GEMM kernel's int8 tensor ops (8 per int16 MAC: four
+int8 products, 2 ops each) over its event-timed duration, against int8 dense
+peak measured live with cuBLASLt (torch._int_mm).  ``cpu_baseline``: the CPU
+oracle (numpy float64 BLAS + floor / saturate, the reference simulator's own
+method, _simulate.py:631) on the batch-1 half of the sweep, all host threads.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+MS = (1, 8, 128, 2048)
+KS = (64, 512, 1024, 4096)
+NS = (32, 256, 1024, 4096)
+BATCHES = (1, 16)
+
+
+def sweep_problems(batches=BATCHES):
+    return [(b, m, k, n) for b in batches for m in MS for k in KS for n in NS]
+
+
+def macs_of(problems):
+    return sum(b * m * k * n for b, m, k, n in problems)
+
+
+# ---------------------------------------------------------------- clocks
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms while running."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device_index: int):
+        self.dev = device_index
+        self.proc = None
+        self.lines = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.dev}", f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except OSError:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        sm, mx, reasons = [], None, set()
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        for ln in self.lines:
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for nm, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(nm)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ---------------------------------------------------------------- CPU side (oracle)
+def cpu_matmul_rate(problems, min_seconds=10.0, seed=0):
+    """GMAC/s of the CPU oracle (numpy float64 matmul + floor + saturate) over
+    ``problems`` repeated until ``min_seconds`` elapsed."""
+    import numpy as np
+
+    from oracle import spec
+    rng = np.random.default_rng(seed)
+    data = [(rng.integers(-256, 256, size=(b, m, k)).astype(np.int16),
+             rng.integers(-256, 256, size=(b, k, n)).astype(np.int16)) for b, m, k, n in problems]
+    macs, t0 = 0, time.perf_counter()
+    while True:
+        for (A, B), (b, m, k, n) in zip(data, problems):
+            spec.matmul_raw(A, B)
+            macs += b * m * k * n
+        el = time.perf_counter() - t0
+        if el >= min_seconds:
+            return macs / el / 1e9, el, macs
+
+
+def run_reference(args):
+    """--impl reference: the reference's CPU algorithm (the oracle port; the
+    reference is Python and does not travel to the GPU box) on rank 0."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    cores = os.cpu_count() or 1
+    os.environ.setdefault("OMP_NUM_THREADS", str(cores))
+    os.environ.setdefault("OPENBLAS_NUM_THREADS", str(cores))
+    sample = sweep_problems(batches=(1,))
+    for _ in range(args.warmup):
+        cpu_matmul_rate(sample, min_seconds=0.0)
+    rates, secs = [], []
+    for _ in range(args.steps):
+        r, el, _ = cpu_matmul_rate(sample, min_seconds=0.0)
+        rates.append(r)
+        secs.append(el)
+    value = macs_of(sample) * args.steps / sum(secs) / 1e9
+    line = {"metric": "bit-exact fixed-point sim GMAC/s (op-level MatMul sweep)", "value": round(value, 3),
+            "unit": "GMAC/s", "impl": "reference", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(1e3 * sum(secs) / args.steps, 3), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "int16 (exact int64 sums)", "data": "synthetic, seeded",
+            "config": {"workload": "configs[1] op-level MatMul sweep", "step_sample": "batch-1 half (64 problems)"},
+            "cpu_baseline": {"value": round(value, 3), "unit": "GMAC/s", "cores": cores, "kind": "port",
+                             "sample": "batch-1 half of the MatMul sweep (64 problems, %.1f GMAC) per step"
+                                       % (macs_of(sample) / 1e9)},
+            "e2e": {"value": round(value, 3), "unit": "GMAC/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ---------------------------------------------------------------- GPU side
+def measure_int8_peak(torch, device):
+    """Dense int8 tensor throughput (TOPS) of cuBLASLt via torch._int_mm, burst."""
+    try:
+        a = torch.randint(-128, 127, (8192, 8192), dtype=torch.int8, device=device)
+        b = torch.randint(-128, 127, (8192, 8192), dtype=torch.int8, device=device)
+        for _ in range(3):
+            torch._int_mm(a, b)
+        torch.cuda.synchronize()
+        best = 1e9
+        for _ in range(10):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            torch._int_mm(a, b)
+            e1.record()
+            e1.synchronize()
+            best = min(best, e0.elapsed_time(e1))
+        return 2 * 8192 ** 3 / (best * 1e-3) / 1e12, "measured live: torch._int_mm int8 8192^3 (cuBLASLt), best of 10"
+    except Exception as e:  # pragma: no cover
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            pk = json.load(f)
+        return 2 * pk["bf16_tflops"], f"2 x measured bf16 ({e.__class__.__name__} from torch._int_mm)"
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--case", choices=["gemm", "gemm_small", "vectorop", "softmax", "conv"],
+                    help="run one job a few times (a small case for ncu captures) and exit")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+    if args.impl == "reference":
+        return run_reference(args)
+    if args.case:
+        return run_case(args)
+
+    import torch
+
+    from cormorant_b200 import ops
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    pg = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+        pg = dist
+
+    stream = torch.cuda.Stream(device=dev)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(1234 + rank)
+    problems = sweep_problems()
+    bufs = []
+    with torch.cuda.stream(stream):
+        for b, m, k, n in problems:
+            A = torch.randint(-256, 256, (b * m * k,), dtype=torch.int16, device=dev, generator=gen)
+            B = torch.randint(-256, 256, (b * k * n,), dtype=torch.int16, device=dev, generator=gen)
+            Cc = torch.empty(b * m * n, dtype=torch.int16, device=dev)
+            bufs.append((A, B, Cc))
+        ws_bytes = 0
+        import ctypes as Ct
+
+        from cormorant_b200 import _lib
+        for (b, m, k, n) in problems:
+            d = _lib.MatmulDesc(0, 0, 0, m, k, n, b, m * k, k * n, m * n, 0, 0, 0, None, 0)
+            need = Ct.c_size_t(0)
+            _lib.check(_lib.lib().corm_matmul_workspace_size(Ct.byref(d), Ct.byref(need)))
+            ws_bytes = max(ws_bytes, need.value)
+        ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
+        flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+
+    def run_sweep():
+        for (b, m, k, n), (A, B, Cc) in zip(problems, bufs):
+            ops.matmul(A, B, Cc, n=m, k=k, m=n, batch=b, a_batch_stride=m * k, b_batch_stride=k * n,
+                       c_batch_stride=m * n, workspace=ws)
+
+    # eager warm-up (tensor maps, kernel attributes), count launches per step
+    with torch.cuda.stream(stream):
+        l0 = ops.launch_count()
+        run_sweep()
+        launches_per_step = ops.launch_count() - l0
+    stream.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        run_sweep()
+    torch.cuda.synchronize()
+
+    def timed_steps(nsteps, fn):
+        times = []
+        for _ in range(nsteps):
+            with torch.cuda.stream(stream):
+                flush.zero_()
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record(stream)
+                fn()
+                e1.record(stream)
+            e1.synchronize()
+            times.append(e0.elapsed_time(e1))
+        return times
+
+    timed_steps(args.warmup, graph.replay)
+    if pg:
+        pg.barrier()
+    torch.cuda.synchronize()
+    clocks = ClockSampler(local)
+    clocks.start()
+    time.sleep(0.5)
+    times = timed_steps(args.steps, graph.replay)
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    total_ms = sum(times)
+    if pg:
+        t = torch.tensor([total_ms], dtype=torch.float64, device=dev)
+        pg.all_reduce(t, op=pg.ReduceOp.MAX)
+        total_ms = float(t.item())
+    ms_per_step = total_ms / args.steps
+    macs_step = macs_of(problems)
+    value = world * macs_step * args.steps / (total_ms * 1e-3) / 1e9
+
+    # per-kernel times of one eager step (events around every launch)
+    with torch.cuda.stream(stream):
+        flush.zero_()
+        ops.profile_read()
+        ops.profile_enable(True)
+        run_sweep()
+        ops.profile_enable(False)
+    prof = ops.profile_read()
+    tensor_macs = sum(b * m * k * n for b, m, k, n in problems if m > 16)
+    g_launches, g_ms, _ = prof.get("gemm_i8x4_kernel", (0, 0.0, 0.0))
+    peak, peak_src = measure_int8_peak(torch, dev)
+    achieved = 8 * tensor_macs / (g_ms * 1e-3) / 1e12 if g_ms else None
+    step_kernel_ms = sum(v[1] for v in prof.values())
+
+    # VectorOP and Softmax sweeps of the same config
+    sweeps = vector_sweeps(torch, ops, dev, stream, flush, args)
+
+    # verification gather (the only collective): per-rank checksum of the outputs
+    chk = torch.zeros(1, dtype=torch.int64, device=dev)
+    for _, _, Cc in bufs:
+        chk += Cc.to(torch.int64).sum()
+    if pg:
+        allc = [torch.zeros_like(chk) for _ in range(world)]
+        pg.all_gather(allc, chk)
+
+    e2e = None
+    if not args.no_e2e:
+        e2e = run_e2e(torch, ops, dev, stream, problems, bufs, ws, args, pg, world)
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        sample = sweep_problems(batches=(1,))
+        r, el, macs = cpu_matmul_rate(sample, min_seconds=10.0)
+        cpu = {"value": round(r, 3), "unit": "GMAC/s", "cores": os.cpu_count(), "kind": "port",
+               "sample": "batch-1 half of the MatMul sweep (64 problems), repeated %.1f s" % el}
+
+    if rank == 0:
+        line = {
+            "metric": "bit-exact fixed-point sim GMAC/s (op-level MatMul sweep)",
+            "value": round(value, 1), "unit": "GMAC/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "int16 (int8 x4 tensor split, int64 recombine)",
+            "data": "synthetic int16 Q8.8 uniform [-1,1), seeded per rank",
+            "config": {"workload": "configs[1] op-level MatMul sweep: M{1,8,128,2048} x K{64,512,1024,4096} x "
+                                   "N{32,256,1024,4096} x batch{1,16}", "problems": len(problems),
+                       "gmac_per_step_per_gpu": round(macs_step / 1e9, 3), "parallelism": f"dp{world} (replicas)",
+                       "l2": "256 MB flush between steps; 7.6 GB of distinct operands per step",
+                       "launch": "CUDA graph replay of the sweep"},
+            "gpu_launches": int(launches_per_step * args.steps),
+            "roofline": {"bound": "tensor", "kernel": "gemm_i8x4_kernel", "achieved": round(achieved, 1) if achieved else None,
+                         "peak": round(peak, 1), "unit": "TFLOP/s", "frac": round(achieved / peak, 4) if achieved else None,
+                         "traffic": None, "peak_source": peak_src,
+                         "work": "8 int8 tensor ops per int16 MAC (4 int8 products); tensor-path problems only (M > 16)",
+                         "gemm_launches_per_step": g_launches, "gemm_ms_per_step": round(g_ms, 4),
+                         "all_kernels_ms_per_step": round(step_kernel_ms, 4),
+                         "kernels": {k: {"launches": v[0], "ms": round(v[1], 4)} for k, v in sorted(prof.items())}},
+            "clocks": clk,
+            "sweeps": sweeps,
+        }
+        if cpu:
+            line["cpu_baseline"] = cpu
+        if e2e:
+            line["e2e"] = e2e
+        print(json.dumps(line), flush=True)
+    if pg:
+        pg.barrier()
+        pg.destroy_process_group()
+    return 0
+
+
+def vector_sweeps(torch, ops, dev, stream, flush, args):
+    """VectorOP 4M-element broadcast ops with fused activations, and softmax
+    rows / columns: GB/s over the algorithmic bytes."""
+    from cormorant_b200 import _lib  # noqa: F401
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(99)
+    N = 1 << 22
+    size, outer = 1024, N // 1024
+    out = {}
+    with torch.cuda.stream(stream):
+        a = torch.randint(-256, 256, (N,), dtype=torch.int16, device=dev, generator=gen)
+        b = torch.randint(-256, 256, (size,), dtype=torch.int16, device=dev, generator=gen)
+        b = torch.where(b == 0, torch.ones_like(b), b)
+        c = torch.empty(N, dtype=torch.int16, device=dev)
+    jobs = [(op, act) for op in (0, 2, 3) for act in (4, 5, 6)]
+
+    def vop_all():
+        for op, act in jobs:
+            ops.vectorop(a, b, c, size=size, op=op, outer=outer, a_inc=size, b_inc=0, act=act)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(stream):
+        vop_all()
+    torch.cuda.synchronize()
+    with torch.cuda.graph(g, stream=stream):
+        vop_all()
+    t = _time_graph(torch, stream, flush, g, args)
+    vbytes = len(jobs) * (4 * N + 2 * size)
+    out["vectorop"] = {"jobs": "ADD/MUL/DIV x SiLU/GELU/GELU-tanh, 4M elem, b broadcast (outer 4096 x size 1024)",
+                       "ms": round(t, 4), "GB/s": round(vbytes / (t * 1e-3) / 1e9, 1),
+                       "bytes_per_elem": 4, "G_elem/s": round(len(jobs) * N / (t * 1e-3) / 1e9, 2)}
+    from cormorant_b200 import ops as o  # noqa: F401
+    cm, cs = 12102203, 19
+    smx = {}
+    for n in (128, 1024, 4096):
+        rows = N // n
+        with torch.cuda.stream(stream):
+            x = torch.randint(-2048, 2048, (N,), dtype=torch.int16, device=dev, generator=gen)
+            p = torch.empty(N, dtype=torch.int16, device=dev)
+        for mode in ("row", "col"):
+            if mode == "row":
+                fn = lambda: ops.vectorop(x, None, p, size=n, op=10, outer=rows, a_inc=n, b_inc=n, smx_cm=cm,  # noqa
+                                          smx_cfg=cs | (8 << 8), smx_mask=n)
+            else:  # keys-major: n keys x rows queries
+                fn = lambda: ops.vectorop(x, None, p, size=n, op=11, outer=rows, a_inc=rows, b_inc=n,  # noqa
+                                          smx_cm=cm, smx_cfg=cs | (8 << 8), smx_mask=n)
+            with torch.cuda.stream(stream):
+                fn()
+            torch.cuda.synchronize()
+            g2 = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g2, stream=stream):
+                fn()
+            t2 = _time_graph(torch, stream, flush, g2, args)
+            smx[f"{mode}{n}"] = {"ms": round(t2, 4), "GB/s": round(4 * N / (t2 * 1e-3) / 1e9, 1)}
+    out["softmax"] = smx
+    return out
+
+
+def _time_graph(torch, stream, flush, g, args):
+    for _ in range(3):
+        g.replay()
+    torch.cuda.synchronize()
+    ts = []
+    for _ in range(max(3, args.steps)):
+        with torch.cuda.stream(stream):
+            flush.zero_()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            g.replay()
+            e1.record(stream)
+        e1.synchronize()
+        ts.append(e0.elapsed_time(e1))
+    return statistics.median(ts)
+
+
+def run_e2e(torch, ops, dev, stream, problems, bufs, ws, args, pg, world):
+    """The sweep through the public per-op API with host buffers: H2D of A
+    and B from pinned memory, the job, D2H of C, every step."""
+    host = []
+    for A, B, Cc in bufs:
+        host.append((A.cpu().pin_memory(), B.cpu().pin_memory(), torch.empty(Cc.numel(), dtype=torch.int16).pin_memory()))
+    h2d = sum((a.numel() + b.numel()) * 2 for a, b, _ in host)
+    d2h = sum(c.numel() * 2 for _, _, c in host)
+    nsteps = max(1, min(args.steps, 3))
+
+    def step():
+        for (b, m, k, n), (A, B, Cc), (hA, hB, hC) in zip(problems, bufs, host):
+            A.copy_(hA, non_blocking=True)
+            B.copy_(hB, non_blocking=True)
+            ops.matmul(A, B, Cc, n=m, k=k, m=n, batch=b, a_batch_stride=m * k, b_batch_stride=k * n,
+                       c_batch_stride=m * n, workspace=ws)
+            hC.copy_(Cc, non_blocking=True)
+    with torch.cuda.stream(stream):
+        step()
+    torch.cuda.synchronize()
+    ts = []
+    for _ in range(nsteps):
+        with torch.cuda.stream(stream):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            step()
+            e1.record(stream)
+        e1.synchronize()
+        ts.append(e0.elapsed_time(e1))
+    total = sum(ts)
+    if pg:
+        t = torch.tensor([total], dtype=torch.float64, device=dev)
+        pg.all_reduce(t, op=pg.ReduceOp.MAX)
+        total = float(t.item())
+    return {"value": round(world * macs_of(problems) * nsteps / (total * 1e-3) / 1e9, 1), "unit": "GMAC/s",
+            "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "steps": nsteps,
+            "ms_per_step": round(total / nsteps, 3), "path": "cormorant_b200.ops.matmul (C ABI) per problem"}
+
+
+def run_case(args):
+    """One job, warmup + steps launches, for profiler captures of a single
+    kernel on a small case (inputs above L2, a few hundred MB on the device)."""
+    import torch
+
+    from cormorant_b200 import ops
+    torch.cuda.set_device(0)
+    g = torch.Generator(device="cuda")
+    g.manual_seed(5)
+    ri = lambda n, lo=-256, hi=256: torch.randint(lo, hi, (n,), dtype=torch.int16, device="cuda", generator=g)  # noqa
+    if args.case in ("gemm", "gemm_small"):
+        b, m, k, n = (4, 2048, 4096, 4096) if args.case == "gemm" else (16, 8, 4096, 4096)
+        A, B, C = ri(b * m * k), ri(b * k * n), torch.empty(b * m * n, dtype=torch.int16, device="cuda")
+        fn = lambda: ops.matmul(A, B, C, n=m, k=k, m=n, batch=b, a_batch_stride=m * k, b_batch_stride=k * n,  # noqa
+                                c_batch_stride=m * n)
+    elif args.case == "vectorop":
+        N = 1 << 26
+        a, bb, c = ri(N), ri(1024), torch.empty(N, dtype=torch.int16, device="cuda")
+        fn = lambda: ops.vectorop(a, bb, c, size=1024, op=2, outer=N // 1024, a_inc=1024, b_inc=0, act=5)  # noqa
+    elif args.case == "softmax":
+        N = 1 << 26
+        x, p = ri(N, -2048, 2048), torch.empty(N, dtype=torch.int16, device="cuda")
+        fn = lambda: ops.vectorop(x, None, p, size=1024, op=10, outer=N // 1024, a_inc=1024, b_inc=1024,  # noqa
+                                  smx_cm=12102203, smx_cfg=19 | (8 << 8), smx_mask=1024)
+    else:
+        x = ri(64 * 144 * 56 * 56)
+        w = ri(24 * 144, -64, 64)
+        y = torch.empty(64 * 24 * 56 * 56, dtype=torch.int16, device="cuda")
+        fn = lambda: ops.conv(x, w, None, y, batch=64, in_ch=144, in_h=56, in_w=56, out_ch=24, out_h=56,  # noqa
+                              out_w=56, kh=1, kw=1, flags=2)
+    for _ in range(args.warmup + args.steps):
+        fn()
+    torch.cuda.synchronize()
+    assert ops.device_status() == 0
+    print(f"case {args.case}: {args.warmup + args.steps} launches done")
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

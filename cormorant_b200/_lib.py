@@ -18,7 +18,8 @@ F_WRAP32, F_WEIGHT_LOGICAL, F_ACT_RELU, F_ACT_RELU6 = 0x1, 0x2, 0x4, 0x8
 # every symbol include/cormorant_b200.h declares
 EXPORTS = ("corm_vectorop", "corm_matmul_workspace_size", "corm_matmul", "corm_conv_workspace_size", "corm_conv",
            "corm_pool", "corm_rowops", "corm_act_table", "corm_smx_table", "corm_rowops_table_image",
-           "corm_bind_device", "corm_device_status", "corm_version", "corm_last_error")
+           "corm_bind_device", "corm_device_status", "corm_launch_count", "corm_profile_enable",
+           "corm_profile_read", "corm_version", "corm_last_error")
 
 
 class CormError(RuntimeError):
@@ -63,6 +64,10 @@ class RowOpsDesc(C.Structure):
         ("p", C.c_void_p), ("eps", C.c_uint64)] + _u32_fields(["aux", "bq_sh", "win_lo", "win_hi"])
 
 
+class ProfileEntry(C.Structure):
+    _fields_ = [("name", C.c_char * 48), ("launches", C.c_uint64), ("total_ms", C.c_double), ("max_ms", C.c_double)]
+
+
 _lib = None
 
 
@@ -89,10 +94,14 @@ def lib() -> C.CDLL:
                        ("corm_smx_table", [C.c_void_p]),
                        ("corm_rowops_table_image", [C.c_void_p]),
                        ("corm_bind_device", [C.c_int]),
-                       ("corm_device_status", [C.POINTER(C.c_int)])):
+                       ("corm_device_status", [C.POINTER(C.c_int)]),
+                       ("corm_profile_enable", [C.c_int]),
+                       ("corm_profile_read", [C.POINTER(ProfileEntry), C.c_int, C.POINTER(C.c_int)])):
         f = getattr(L, name)
         f.argtypes = argt
         f.restype = C.c_int
+    L.corm_launch_count.restype = C.c_uint64
+    L.corm_launch_count.argtypes = []
     L.corm_version.restype = C.c_char_p
     L.corm_last_error.restype = C.c_char_p
     _lib = L

@@ -1,5 +1,6 @@
 // Library plumbing: errors, the device check, the per-device scratch and the
 // per-device unit tables, and the host-side helper entry points.
+#include <atomic>
 #include <cstdarg>
 #include <cstdlib>
 #include <cstring>
@@ -123,9 +124,74 @@ const DeviceTables* tables() {
   return &g_tables[dev];
 }
 
+// ---------------------------------------------------------------- tracing
+static std::atomic<uint64_t> g_launches{0};
+static std::atomic<int> g_prof_on{0};
+struct ProfRec {
+  const char* name;
+  cudaEvent_t a, b;
+};
+static std::mutex g_prof_mu;
+static std::vector<ProfRec> g_prof;
+
+ProfScope::ProfScope(const char* n, cudaStream_t s) : name(n), stream(s), slot(-1) {
+  g_launches.fetch_add(1, std::memory_order_relaxed);
+  if (!g_prof_on.load(std::memory_order_relaxed)) return;
+  ProfRec r{n, nullptr, nullptr};
+  if (cudaEventCreate(&r.a) != cudaSuccess || cudaEventCreate(&r.b) != cudaSuccess) return;
+  cudaEventRecord(r.a, s);
+  std::lock_guard<std::mutex> lk(g_prof_mu);
+  slot = (int)g_prof.size();
+  g_prof.push_back(r);
+}
+
+ProfScope::~ProfScope() {
+  if (slot < 0) return;
+  std::lock_guard<std::mutex> lk(g_prof_mu);
+  cudaEventRecord(g_prof[slot].b, stream);
+}
+
 }  // namespace corm
 
 extern "C" {
+
+uint64_t corm_launch_count(void) { return corm::g_launches.load(); }
+
+int corm_profile_enable(int on) {
+  corm::g_prof_on.store(on ? 1 : 0);
+  return CORM_OK;
+}
+
+int corm_profile_read(corm_profile_entry* out, int max_entries, int* n_out) {
+  std::vector<corm::ProfRec> recs;
+  {
+    std::lock_guard<std::mutex> lk(corm::g_prof_mu);
+    recs.swap(corm::g_prof);
+  }
+  int n = 0;
+  for (auto& r : recs) {
+    float ms = 0.f;
+    cudaEventSynchronize(r.b);
+    cudaEventElapsedTime(&ms, r.a, r.b);
+    int i = 0;
+    while (i < n && std::strncmp(out[i].name, r.name, sizeof out[i].name) != 0) i++;
+    if (i == n && n < max_entries) {
+      std::memset(&out[n], 0, sizeof out[n]);
+      std::strncpy(out[n].name, r.name, sizeof out[n].name - 1);
+      n++;
+    }
+    if (i < n) {
+      out[i].launches++;
+      out[i].total_ms += ms;
+      if (ms > out[i].max_ms) out[i].max_ms = ms;
+    }
+    cudaEventDestroy(r.a);
+    cudaEventDestroy(r.b);
+  }
+  if (n_out) *n_out = n;
+  return corm::cuda_status("corm_profile_read");
+}
+
 
 int corm_act_table(uint32_t act, uint32_t alpha, int16_t* out65536) {
   if (!out65536 || act > 6) return corm::fail(CORM_EINVAL, "corm_act_table: bad argument");

@@ -218,7 +218,10 @@ extern "C" int corm_conv(const corm_conv_desc* d, corm_stream_t stream) {
   a.y_gs = d->y_gs;
   if (d->is_depthwise) {
     const uint64_t total = (uint64_t)d->batch * d->out_ch * P;
-    conv_depthwise<<<corm_blocks(total, 256, 148u * 16u), 256, 0, st>>>(a);
+    {
+      corm::ProfScope prof_("conv_depthwise", st);
+      conv_depthwise<<<corm_blocks(total, 256, 148u * 16u), 256, 0, st>>>(a);
+    }
     return corm::cuda_status("conv depthwise");
   }
   const ConvPlan pl = plan_of(d);
@@ -232,9 +235,15 @@ extern "C" int corm_conv(const corm_conv_desc* d, corm_stream_t stream) {
   int8_t* b_hi = (int8_t*)(w8 + 2 * pl.a_bytes);
   uint8_t* b_lo = w8 + 2 * pl.a_bytes + pl.b_bytes;
   dim3 gi((pl.Ptot + 63) / 64, (pl.Kp + 63) / 64);
-  im2col_split<<<gi, 256, 0, st>>>(a, pl.Ptot, pl.K, pl.Kp, a_hi, a_lo);
+  {
+    corm::ProfScope prof_("im2col_split", st);
+    im2col_split<<<gi, 256, 0, st>>>(a, pl.Ptot, pl.K, pl.Kp, a_hi, a_lo);
+  }
   if (int rc = corm::cuda_status("conv im2col")) return rc;
-  weight_split<<<corm_blocks((uint64_t)d->out_ch * (pl.Kp / 8), 256), 256, 0, st>>>(a, pl.K, pl.Kp, b_hi, b_lo);
+  {
+    corm::ProfScope prof_("weight_split", st);
+    weight_split<<<corm_blocks((uint64_t)d->out_ch * (pl.Kp / 8), 256), 256, 0, st>>>(a, pl.K, pl.Kp, b_hi, b_lo);
+  }
   if (int rc = corm::cuda_status("conv weight split")) return rc;
   corm::GemmJob j{};
   j.a_hi = a_hi;

@@ -31,6 +31,17 @@ struct DeviceTables {
 };
 const DeviceTables* tables();  // nullptr on failure (error set)
 
+// Kernel-level tracing: every launch site holds a ProfScope, which counts the
+// launch and, while profiling is enabled (corm_profile_enable), brackets it
+// with CUDA events on the launching stream.
+struct ProfScope {
+  ProfScope(const char* name, cudaStream_t stream);
+  ~ProfScope();
+  const char* name;
+  cudaStream_t stream;
+  int slot;
+};
+
 // Host table builders (tables.cpp): bit-exact restatements of the reference's
 // vectorop_act.kernel_table, vectorop_smx.TAB and rowops_spec tables.
 void build_act_table(int act, uint32_t alpha, int16_t* out);

@@ -267,8 +267,11 @@ int split_planes(const int16_t* src, uint64_t src_bs, uint32_t planes, uint32_t 
                  uint32_t Kp, int8_t* hi, uint8_t* lo, cudaStream_t stream) {
   const uint64_t total8 = (uint64_t)planes * rows * (Kp / 8);
   if (total8 == 0) return CORM_OK;
-  split_rows_kernel<<<corm_blocks(total8, 256, 148u * 16u), 256, 0, stream>>>(src, src_bs, rows, ld, K, Kp, total8, hi,
+  {
+    corm::ProfScope prof_("split_rows_kernel", stream);
+    split_rows_kernel<<<corm_blocks(total8, 256, 148u * 16u), 256, 0, stream>>>(src, src_bs, rows, ld, K, Kp, total8, hi,
                                                                               lo);
+  }
   return cuda_status("split_planes");
 }
 
@@ -308,7 +311,10 @@ int gemm_i8x4(const GemmJob& j, cudaStream_t stream) {
   }
   dim3 grid((j.rows + BM - 1) / BM, (j.cols + BN - 1) / BN, j.batch);
   if (grid.y > 65535 || grid.z > 65535) return fail(CORM_ELIMIT, "gemm: grid %u x %u x %u", grid.x, grid.y, grid.z);
-  gemm_i8x4_kernel<<<grid, THREADS, SMEM_BYTES, stream>>>(m_ahi, m_alo, m_bhi, m_blo, ep);
+  {
+    corm::ProfScope prof_("gemm_i8x4_kernel", stream);
+    gemm_i8x4_kernel<<<grid, THREADS, SMEM_BYTES, stream>>>(m_ahi, m_alo, m_bhi, m_blo, ep);
+  }
   return cuda_status("gemm_i8x4");
 }
 

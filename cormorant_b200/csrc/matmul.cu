@@ -210,16 +210,31 @@ extern "C" int corm_matmul(const corm_matmul_desc* d, corm_stream_t stream) {
     if (partial && cudaMemsetAsync(partial, 0, pl.bytes, st) != cudaSuccess) return corm::cuda_status("memset");
     dim3 grid((d->m + 255) / 256, d->batch, pl.ksplit);
     if (d->n <= 1)
-      mm_small_kernel<1><<<grid, 128, 0, st>>>(p, pl.kchunk, partial);
+      {
+        corm::ProfScope prof_("mm_small_kernel<1>", st);
+        mm_small_kernel<1><<<grid, 128, 0, st>>>(p, pl.kchunk, partial);
+      }
     else if (d->n <= 4)
-      mm_small_kernel<4><<<grid, 128, 0, st>>>(p, pl.kchunk, partial);
+      {
+        corm::ProfScope prof_("mm_small_kernel<4>", st);
+        mm_small_kernel<4><<<grid, 128, 0, st>>>(p, pl.kchunk, partial);
+      }
     else if (d->n <= 8)
-      mm_small_kernel<8><<<grid, 128, 0, st>>>(p, pl.kchunk, partial);
+      {
+        corm::ProfScope prof_("mm_small_kernel<8>", st);
+        mm_small_kernel<8><<<grid, 128, 0, st>>>(p, pl.kchunk, partial);
+      }
     else
-      mm_small_kernel<16><<<grid, 128, 0, st>>>(p, pl.kchunk, partial);
+      {
+        corm::ProfScope prof_("mm_small_kernel<16>", st);
+        mm_small_kernel<16><<<grid, 128, 0, st>>>(p, pl.kchunk, partial);
+      }
     if (int rc = corm::cuda_status("matmul small")) return rc;
     if (partial) {
-      mm_small_finish<<<corm_blocks((uint64_t)d->batch * d->n * d->m, 256), 256, 0, st>>>(p, partial);
+      {
+        corm::ProfScope prof_("mm_small_finish", st);
+        mm_small_finish<<<corm_blocks((uint64_t)d->batch * d->n * d->m, 256), 256, 0, st>>>(p, partial);
+      }
       return corm::cuda_status("matmul small finish");
     }
     return CORM_OK;
@@ -232,7 +247,10 @@ extern "C" int corm_matmul(const corm_matmul_desc* d, corm_stream_t stream) {
   if (int rc = corm::split_planes(d->a, d->a_batch_stride, pl.a_planes, d->n, d->k, d->k, pl.Kp, a_hi, a_lo, st))
     return rc;
   dim3 gb((d->m + 63) / 64, (pl.Kp + 63) / 64, pl.b_planes);
-  split_b_kernel<<<gb, 256, 0, st>>>(p, pl.b_planes, pl.Kp, b_hi, b_lo);
+  {
+    corm::ProfScope prof_("split_b_kernel", st);
+    split_b_kernel<<<gb, 256, 0, st>>>(p, pl.b_planes, pl.Kp, b_hi, b_lo);
+  }
   if (int rc = corm::cuda_status("matmul split_b")) return rc;
   corm::GemmJob j{};
   j.a_hi = a_hi;

@@ -124,9 +124,15 @@ extern "C" int corm_pool(const corm_pool_desc* d, corm_stream_t stream) {
   cudaStream_t st = (cudaStream_t)stream;
   if (global && d->in_h * d->in_w >= 32) {
     const uint64_t planes = (uint64_t)d->batch * d->channels;
-    pool_global<<<corm_blocks(planes * 32, 256, 148u * 16u), 256, 0, st>>>(p);
+    {
+      corm::ProfScope prof_("pool_global", st);
+      pool_global<<<corm_blocks(planes * 32, 256, 148u * 16u), 256, 0, st>>>(p);
+    }
   } else {
-    pool_window<<<corm_blocks(total, 256, 148u * 16u), 256, 0, st>>>(p);
+    {
+      corm::ProfScope prof_("pool_window", st);
+      pool_window<<<corm_blocks(total, 256, 148u * 16u), 256, 0, st>>>(p);
+    }
   }
   return corm::cuda_status("pool");
 }

@@ -324,7 +324,10 @@ extern "C" int corm_rowops(const corm_rowops_desc* d, corm_stream_t stream) {
   cudaStream_t st = (cudaStream_t)stream;
   if (op == 8) {
     if (d->n == 0 || d->rows == 0 || d->blocks == 0) return CORM_OK;
-    ro_tload<<<1, 256, 0, st>>>(q, tb->ro_sig, tb->ro_rsq);
+    {
+      corm::ProfScope prof_("ro_tload", st);
+      ro_tload<<<1, 256, 0, st>>>(q, tb->ro_sig, tb->ro_rsq);
+    }
     return corm::cuda_status("rowops tload");
   }
   if (op == 9) {
@@ -333,7 +336,10 @@ extern "C" int corm_rowops(const corm_rowops_desc* d, corm_stream_t stream) {
     if (((uintptr_t)d->a & 1u) || (d->a_s2 & 1u) || ((uintptr_t)d->c & 15u))
       return corm::fail(CORM_EINVAL, "corm_rowops: unaligned FOLD");
     const uint64_t total = (uint64_t)d->n * d->rows * d->blocks;
-    ro_fold<<<corm_blocks((total + 7) & ~7ull, 256, 148u * 8u), 256, 0, st>>>(q);
+    {
+      corm::ProfScope prof_("ro_fold", st);
+      ro_fold<<<corm_blocks((total + 7) & ~7ull, 256, 148u * 8u), 256, 0, st>>>(q);
+    }
     return corm::cuda_status("rowops fold");
   }
   if (d->n == 0 || d->rows == 0 || d->blocks == 0) return CORM_OK;
@@ -355,6 +361,9 @@ extern "C" int corm_rowops(const corm_rowops_desc* d, corm_stream_t stream) {
   }
   if (op == 7 && ((d->aux & 15u) == 0 || (d->aux & 15u) > 8u)) return CORM_OK;
   const uint64_t rows = (uint64_t)d->rows * d->blocks;
-  ro_rows<<<(unsigned)(rows < 148u * 64u ? rows : 148u * 64u), RO_THREADS, 0, st>>>(q);
+  {
+    corm::ProfScope prof_("ro_rows", st);
+    ro_rows<<<(unsigned)(rows < 148u * 64u ? rows : 148u * 64u), RO_THREADS, 0, st>>>(q);
+  }
   return corm::cuda_status("rowops");
 }

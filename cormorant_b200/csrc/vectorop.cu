@@ -253,17 +253,32 @@ int launch_softmax(const corm_vectorop_desc* d, cudaStream_t st, const corm::Dev
     const size_t smem = (size_t)d->size * 16 * sizeof(int16_t);
     if (smem > 200 * 1024) return corm::fail(CORM_ELIMIT, "softmax column mode: %u keys beyond 6400", d->size);
     cudaFuncSetAttribute(smx_cols, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    smx_cols<<<p.rows / 16, 256, smem, st>>>(p);
+    {
+      corm::ProfScope prof_("smx_cols", st);
+      smx_cols<<<p.rows / 16, 256, smem, st>>>(p);
+    }
     return corm::cuda_status("softmax_cols");
   }
   if (d->size <= 256) {
-    smx_rows<32, 8><<<(p.rows + 7) / 8, 256, 0, st>>>(p);
+    {
+      corm::ProfScope prof_("smx_rows<32,8>", st);
+      smx_rows<32, 8><<<(p.rows + 7) / 8, 256, 0, st>>>(p);
+    }
   } else if (d->size <= 1024) {
-    smx_rows<32, 32><<<(p.rows + 7) / 8, 256, 0, st>>>(p);
+    {
+      corm::ProfScope prof_("smx_rows<32,32>", st);
+      smx_rows<32, 32><<<(p.rows + 7) / 8, 256, 0, st>>>(p);
+    }
   } else if (d->size <= 4096) {
-    smx_rows<256, 16><<<p.rows, 256, 0, st>>>(p);
+    {
+      corm::ProfScope prof_("smx_rows<256,16>", st);
+      smx_rows<256, 16><<<p.rows, 256, 0, st>>>(p);
+    }
   } else if (d->size <= 16384) {
-    smx_rows<1024, 16><<<p.rows, 1024, 0, st>>>(p);
+    {
+      corm::ProfScope prof_("smx_rows<1024,16>", st);
+      smx_rows<1024, 16><<<p.rows, 1024, 0, st>>>(p);
+    }
   } else {
     return corm::fail(CORM_ELIMIT, "softmax row mode: size %u beyond 16384", d->size);
   }
@@ -303,8 +318,14 @@ extern "C" int corm_vectorop(const corm_vectorop_desc* d, corm_stream_t stream) 
   const uint64_t words = (uint64_t)p.outer * p.nw;
   const unsigned blocks = corm_blocks(words, 256, 148u * 16u);
   if (d->op <= 3)
-    vop_elementwise<true><<<blocks, 256, 0, st>>>(p);
+    {
+      corm::ProfScope prof_("vop_elementwise<true>", st);
+      vop_elementwise<true><<<blocks, 256, 0, st>>>(p);
+    }
   else
-    vop_elementwise<false><<<blocks, 256, 0, st>>>(p);
+    {
+      corm::ProfScope prof_("vop_elementwise<false>", st);
+      vop_elementwise<false><<<blocks, 256, 0, st>>>(p);
+    }
   return corm::cuda_status("vectorop");
 }

@@ -132,6 +132,25 @@ def device_status() -> int:
     return code.value
 
 
+def launch_count() -> int:
+    """Kernel launches the library has made in this process."""
+    return int(lib().corm_launch_count())
+
+
+def profile_enable(on: bool = True) -> None:
+    check(lib().corm_profile_enable(1 if on else 0))
+
+
+def profile_read() -> dict:
+    """{kernel: (launches, total_ms, max_ms)} of the launches recorded since the
+    last read (synchronises)."""
+    buf = (_lib.ProfileEntry * 64)()
+    n = C.c_int(0)
+    check(lib().corm_profile_read(buf, 64, C.byref(n)))
+    return {buf[i].name.decode(): (int(buf[i].launches), float(buf[i].total_ms), float(buf[i].max_ms))
+            for i in range(n.value)}
+
+
 # ---------------------------------------------------------------- host-side tables (no GPU needed)
 def act_table(act: int, alpha: int = 0):
     import numpy as np

@@ -173,6 +173,21 @@ int corm_bind_device(int device);
  * reference's kernel_wait timeout accounting (runtime/inference_irq.c:259-264). */
 int corm_device_status(int* code);
 /* Library version string and the last error message of the calling thread. */
+/* Tracing (the analogue of the reference's per-layer profiling aggregates,
+ * runtime/inference_prof.h): corm_launch_count() counts every kernel launch of
+ * the library; while corm_profile_enable(1) is on, each launch is bracketed by
+ * CUDA events on its stream, and corm_profile_read() synchronises, sums them
+ * per kernel and clears the record. */
+typedef struct {
+  char name[48];
+  uint64_t launches;
+  double total_ms;
+  double max_ms;
+} corm_profile_entry;
+uint64_t corm_launch_count(void);
+int corm_profile_enable(int on);
+int corm_profile_read(corm_profile_entry* out, int max_entries, int* n_out);
+
 const char* corm_version(void);
 const char* corm_last_error(void);
 

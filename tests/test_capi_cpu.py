@@ -16,7 +16,7 @@ HEADER = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))
 
 def test_exports_match_header():
     text = open(HEADER).read()
-    declared = set(re.findall(r"^(?:int|const char\*)\s+(corm_\w+)\(", text, re.M))
+    declared = set(re.findall(r"^(?:int|uint64_t|const char\*)\s+(corm_\w+)\(", text, re.M))
     assert declared == set(_lib.EXPORTS)
     L = _lib.lib()
     for name in declared:
