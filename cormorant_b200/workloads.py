@@ -1,0 +1,191 @@
+"""Graph builders for the benchmark configurations:
+the MNIST-shaped CNN (config 1) and MobileNetV2-1.0 (config 3), as node
+graphs the simulator runs, with seeded synthetic Q8.8 weights and inputs.
+
+The builders go through a ``NodeFactory`` so the same architecture can be
+instantiated with this package's descriptors (``NodeFactory``) or with the
+reference's own node classes (the golden-vector generator subclasses it), and
+the GPU result compared with the reference simulator's on identical weights.
+"""
+from __future__ import annotations
+
+from typing import Dict, List, Tuple
+
+import numpy as np
+
+from . import nodes as N
+
+
+def q88_uniform(rng, shape, lo, hi) -> np.ndarray:
+    """Q8.8 values of uniform reals in [lo, hi), rounded half to even."""
+    return np.clip(np.round(rng.uniform(lo, hi, size=shape) * 256.0), -32768, 32767) / 256.0
+
+
+def he_normal_q88(rng, shape, fan_in) -> np.ndarray:
+    """He-normal weights (sigma = sqrt(2 / fan_in)) quantised to Q8.8 with
+    saturation."""
+    return np.clip(np.round(rng.normal(0.0, np.sqrt(2.0 / fan_in), size=shape) * 256.0), -32768, 32767) / 256.0
+
+
+class NodeFactory:
+    """Builds graph pieces with cormorant_b200.nodes descriptors."""
+
+    def __init__(self):
+        self.tensors: Dict[str, N.TensorInfo] = {}
+        self.nodes: list = []
+        self.weights: List[N.TensorInfo] = []
+
+    def tensor(self, name, shape, data=None):
+        t = N.TensorInfo(onnx_name=name, shape=list(shape), data=data)
+        self.tensors[name] = t
+        if data is not None:
+            self.weights.append(t)
+        return t
+
+    def conv(self, x, w, b, y, **geo):
+        self.nodes.append(N.ConvNode(inputs=[x, w] + ([b] if b is not None else []), output=y,
+                                     has_bias=b is not None, **geo))
+
+    def vop(self, op, ins, y, act=0):
+        self.nodes.append(N.ScheduledNode(op_code=op, inputs=ins, output=y, act=act))
+
+    def pool(self, x, y, **geo):
+        self.nodes.append(N.PoolNode(inputs=[x], output=y, **geo))
+
+    def reshape(self, x, y):
+        self.nodes.append(N.ReshapeNode(inputs=[x], output=y))
+
+    def matmul(self, a, b, y, n, k, m):
+        self.nodes.append(N.MatmulNode(inputs=[a, b], output=y, n=n, k=k, m=m, batch=1))
+
+    def softmax(self, x, y, rows, n, cm, cfg):
+        self.nodes.append(N.SoftmaxVopNode(inputs=[x], output=y, rows=rows, n=n, cm=cm, cfg=cfg))
+
+    def graph(self, inputs, outputs):
+        return N.Graph(nodes=self.nodes, weight_tensors=self.weights, input_tensors=inputs, output_tensors=outputs)
+
+
+# ---------------------------------------------------------------- config 1: MNIST CNN
+def mnist(seed: int = 1, batch: int = 1, factory: NodeFactory = None):
+    """Conv3x3 1->16 +bias, Relu, MaxPool 2x2, Conv3x3 16->32 +bias, Relu,
+    MaxPool 2x2, flatten 1568, MatMul 1568x10, Add bias, Softmax (row, Q8.8).
+    Returns (graph, {input: values}, macs_per_image)."""
+    f = factory or NodeFactory()
+    rng = np.random.default_rng(seed)
+    x = q88_uniform(rng, (batch, 1, 28, 28), -1, 1)
+    w1, b1 = q88_uniform(rng, (16, 1, 3, 3), -0.25, 0.25), q88_uniform(rng, (16,), -0.25, 0.25)
+    w2, b2 = q88_uniform(rng, (32, 16, 3, 3), -0.25, 0.25), q88_uniform(rng, (32,), -0.25, 0.25)
+    wf, bf = q88_uniform(rng, (1568, 10), -0.25, 0.25), q88_uniform(rng, (1, 10), -0.25, 0.25)
+    X = f.tensor("x", x.shape)
+    W1, B1, W2, B2 = f.tensor("w1", w1.shape, w1), f.tensor("b1", b1.shape, b1), f.tensor("w2", w2.shape, w2), \
+        f.tensor("b2", b2.shape, b2)
+    WF, BF = f.tensor("wf", wf.shape, wf), f.tensor("bf", bf.shape, bf)
+    c1, r1, p1 = f.tensor("c1", (batch, 16, 28, 28)), f.tensor("r1", (batch, 16, 28, 28)), f.tensor("p1", (batch, 16, 14, 14))
+    c2, r2, p2 = f.tensor("c2", (batch, 32, 14, 14)), f.tensor("r2", (batch, 32, 14, 14)), f.tensor("p2", (batch, 32, 7, 7))
+    fl, mm, lg, pr = f.tensor("flat", (batch, 1568)), f.tensor("mm", (batch, 10)), f.tensor("logits", (batch, 10)), \
+        f.tensor("prob", (batch, 10))
+    g3 = dict(kh=3, kw=3, pad_top=1, pad_left=1)
+    f.conv(X, W1, B1, c1, batch=batch, in_ch=1, in_h=28, in_w=28, out_ch=16, out_h=28, out_w=28, **g3)
+    f.vop(N.OP_RELU, [c1], r1)
+    f.pool(r1, p1, batch=batch, channels=16, in_h=28, in_w=28, out_h=14, out_w=14, pool_h=2, pool_w=2, stride_h=2,
+           stride_w=2, pool_type=N.POOL_MAX)
+    f.conv(p1, W2, B2, c2, batch=batch, in_ch=16, in_h=14, in_w=14, out_ch=32, out_h=14, out_w=14, **g3)
+    f.vop(N.OP_RELU, [c2], r2)
+    f.pool(r2, p2, batch=batch, channels=32, in_h=14, in_w=14, out_h=7, out_w=7, pool_h=2, pool_w=2, stride_h=2,
+           stride_w=2, pool_type=N.POOL_MAX)
+    f.reshape(p2, fl)
+    f.matmul(fl, WF, mm, batch, 1568, 10)
+    f.vop(N.OP_ADD, [mm, BF], lg)
+    f.softmax(lg, pr, batch, 10, 12102203, 19 | (8 << 8))
+    macs = 16 * 9 * 784 + 32 * 16 * 9 * 196 + 1568 * 10
+    return f.graph([X], [pr]), {"x": x}, macs
+
+
+# ---------------------------------------------------------------- config 3: MobileNetV2-1.0
+MBV2_BLOCKS = [(1, 16, 1, 1), (6, 24, 2, 2), (6, 32, 3, 2), (6, 64, 4, 2), (6, 96, 3, 1), (6, 160, 3, 2),
+               (6, 320, 1, 1)]  # (expansion t, channels c, repeats n, first stride s)
+
+
+def mobilenet_v2(seed: int = 3, batch: int = 1, res: int = 224, classes: int = 1000, factory: NodeFactory = None):
+    """MobileNetV2-1.0: stem Conv3x3 s2 3->32 + Clip(0,6); inverted residuals
+    (1x1 expand x t + Clip, depthwise 3x3 + Clip, 1x1 project, residual Add
+    when shapes match); Conv1x1 320->1280 + Clip; GlobalAveragePool; MatMul
+    1280 x classes + Add bias.  Batch-norm folded into the conv biases (small
+    seeded values).  Returns (graph, {input: values}, macs_per_image)."""
+    f = factory or NodeFactory()
+    rng = np.random.default_rng(seed)
+    x = q88_uniform(rng, (batch, 3, res, res), -1, 1)
+    X = f.tensor("x", x.shape)
+    macs = 0
+    counter = [0]
+
+    def name(p):
+        counter[0] += 1
+        return f"{p}{counter[0]}"
+
+    def conv(t, cin, h, w, cout, k, s, dw=False, act=True):
+        nonlocal macs
+        pad = k // 2
+        oh, ow = (h + 2 * pad - k) // s + 1, (w + 2 * pad - k) // s + 1
+        fan = k * k * (1 if dw else cin)
+        wv = he_normal_q88(rng, (cout, 1 if dw else cin, k, k), fan)
+        bv = q88_uniform(rng, (cout,), -0.0625, 0.0625)
+        W, B = f.tensor(name("w"), wv.shape, wv), f.tensor(name("b"), bv.shape, bv)
+        y = f.tensor(name("conv"), (batch, cout, oh, ow))
+        f.conv(t, W, B, y, batch=batch, in_ch=cin, in_h=h, in_w=w, out_ch=cout, out_h=oh, out_w=ow, kh=k, kw=k,
+               stride_h=s, stride_w=s, pad_top=pad, pad_left=pad, is_depthwise=dw)
+        macs += cout * oh * ow * fan
+        if act:
+            z = f.tensor(name("clip"), (batch, cout, oh, ow))
+            f.vop(N.OP_RELU6, [y], z)
+            y = z
+        return y, oh, ow
+
+    t, h, w = conv(X, 3, res, res, 32, 3, 2)
+    cin = 32
+    for tt, c, n, s in MBV2_BLOCKS:
+        for r in range(n):
+            stride = s if r == 0 else 1
+            inp = t
+            hid = cin * tt
+            u, hh, ww = (conv(t, cin, h, w, hid, 1, 1) if tt != 1 else (t, h, w))
+            u, hh, ww = conv(u, hid, hh, ww, hid, 3, stride, dw=True)
+            u, hh, ww = conv(u, hid, hh, ww, c, 1, 1, act=False)
+            if stride == 1 and cin == c:
+                z = f.tensor(name("add"), (batch, c, hh, ww))
+                f.vop(N.OP_ADD, [inp, u], z)
+                u = z
+            t, h, w, cin = u, hh, ww, c
+    t, h, w = conv(t, cin, h, w, 1280, 1, 1)
+    gp = f.tensor(name("gap"), (batch, 1280, 1, 1))
+    f.pool(t, gp, batch=batch, channels=1280, in_h=h, in_w=w, out_h=1, out_w=1, pool_h=h, pool_w=w,
+           pool_type=N.POOL_AVG)
+    fl = f.tensor(name("flat"), (batch, 1280))
+    f.reshape(gp, fl)
+    wf = he_normal_q88(rng, (1280, classes), 1280)
+    bf = q88_uniform(rng, (1, classes), -0.0625, 0.0625)
+    WF, BF = f.tensor("wfc", wf.shape, wf), f.tensor("bfc", bf.shape, bf)
+    mm = f.tensor(name("fc"), (batch, classes))
+    f.matmul(fl, WF, mm, batch, 1280, classes)
+    lg = f.tensor("logits", (batch, classes))
+    f.vop(N.OP_ADD, [mm, BF], lg)
+    macs += 1280 * classes
+    return f.graph([X], [lg]), {"x": x}, macs
+
+
+def graph_macs(graph) -> int:
+    """Int16 MACs of one pass: sum over Conv (N M oH oW (C/groups) kh kw) and
+    MatMul (batch n k m) nodes."""
+    total = 0
+    for sn in graph.nodes:
+        k = type(sn).__name__
+        if k == "ConvNode":
+            total += sn.batch * sn.out_ch * sn.out_h * sn.out_w * (1 if sn.is_depthwise else sn.in_ch) * sn.kh * sn.kw
+        elif k in ("MatmulNode", "MatmulConvNode"):
+            a = sn.inputs[0].shape
+            total += int(np.prod(a[:-1])) * a[-1] * sn.inputs[1].shape[-1]
+    return total
+
+
+def shapes_summary(graph) -> List[Tuple[str, list]]:
+    return [(type(sn).__name__, list(sn.output.shape)) for sn in graph.nodes]

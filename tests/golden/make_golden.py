@@ -306,16 +306,77 @@ def make_ops(sim):
     return out
 
 
+def make_graph_goldens(ref, out):
+    """The benchmark architectures (cormorant_b200.workloads) instantiated with
+    the reference's own node classes and run through its _forward_pass."""
+    sim = _import_reference(ref)
+    sys.path.insert(0, os.path.dirname(os.path.dirname(HERE)))
+    from cormorant_b200 import workloads as WL
+    from src.dtype import AP_FIXED_16_8 as D
+    from src.tensor import TensorInfo as T
+    from src import nodes as RN, smx_nodes as SN
+    import onnx
+
+    class RefFactory(WL.NodeFactory):
+        def tensor(self, name, shape, data=None):
+            t = T(onnx_name=name, shape=list(shape), dtype="float32", data=data)
+            self.tensors[name] = t
+            if data is not None:
+                self.weights.append(t)
+            return t
+
+        def conv(self, x, w, b, y, **geo):
+            self.nodes.append(RN.ConvNode(onnx_node=onnx.NodeProto(), inputs=[x, w] + ([b] if b is not None else []),
+                                          output=y, has_bias=b is not None, **geo))
+
+        def vop(self, op, ins, y, act=0):
+            n = RN.ScheduledNode(onnx_node=onnx.NodeProto(), op_code=op, arity=len(ins), inputs=ins, output=y)
+            n.act = act
+            self.nodes.append(n)
+
+        def pool(self, x, y, **geo):
+            self.nodes.append(RN.PoolNode(onnx_node=onnx.NodeProto(), inputs=[x], output=y, **geo))
+
+        def reshape(self, x, y):
+            self.nodes.append(RN.ReshapeNode(onnx_node=onnx.NodeProto(), inputs=[x], output=y))
+
+        def matmul(self, a, b, y, n, k, m):
+            self.nodes.append(RN.MatmulNode(onnx_node=onnx.NodeProto(), inputs=[a, b], output=y, n=n, k=k, m=m,
+                                            batch=1))
+
+        def softmax(self, x, y, rows, n, cm, cfg):
+            self.nodes.append(SN.SoftmaxVopNode(onnx_node=onnx.NodeProto(), inputs=[x], output=y, rows=rows, n=n,
+                                                cm=cm, cfg=cfg))
+
+        def graph(self, inputs, outputs):
+            return _Graph(self.nodes, self.weights, inputs, outputs)
+
+    for name, build in (("mnist_b2", lambda f: WL.mnist(seed=11, batch=2, factory=f)),
+                        ("mbv2_r32_b2", lambda f: WL.mobilenet_v2(seed=13, batch=2, res=32, factory=f))):
+        g, feeds, _ = build(RefFactory())
+        arrays = _shim(sim, D, g)._forward_pass(feeds)
+        outs = {}
+        for t in g.output_tensors:
+            outs["out_" + t.onnx_name] = np.round(arrays[t.onnx_name] * 256).astype(np.int64)
+        # every intermediate too (the fused ones are compared where materialised)
+        for sn in g.nodes:
+            outs["t_" + sn.output.onnx_name] = np.round(arrays[sn.output.onnx_name] * 256).astype(np.int64)
+        np.savez_compressed(os.path.join(out, f"sim_graph_{name}.npz"), **outs)
+        print(f"sim_graph_{name}.npz: {len(g.nodes)} nodes")
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--ref", default="/root/reference")
-    ap.add_argument("--only", choices=["hw", "sim"])
+    ap.add_argument("--only", choices=["hw", "sim", "graph"])
     ap.add_argument("--out", default=HERE)
     args = ap.parse_args()
     if args.only in (None, "hw"):
         convert_hw(args.ref, args.out)
     if args.only in (None, "sim"):
         make_sim(args.ref, args.out)
+    if args.only in (None, "graph"):
+        make_graph_goldens(args.ref, args.out)
 
 
 if __name__ == "__main__":

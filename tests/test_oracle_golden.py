@@ -174,3 +174,21 @@ def test_mnist_sim(golden, seed):
     assert np.array_equal(logits, z["logits"])
     cm, cs = spec.smx_scale_regs(8, 1.0)
     assert np.array_equal(spec.softmax_rows(logits, 10, cm, cs, 8), z["prob"])
+
+
+@pytest.mark.parametrize("name,build", [
+    ("mnist_b2", lambda: __import__("cormorant_b200.workloads", fromlist=["x"]).mnist(seed=11, batch=2)),
+    ("mbv2_r32_b2", lambda: __import__("cormorant_b200.workloads", fromlist=["x"]).mobilenet_v2(seed=13, batch=2,
+                                                                                                 res=32)),
+])
+def test_graph_oracle_vs_reference(golden, name, build):
+    """The oracle's forward pass over this package's workload graphs equals the
+    reference simulator's _forward_pass over the same architecture built with
+    its own node classes (tests/golden/sim_graph_*.npz), node by node."""
+    from oracle import graph as og
+    z = golden(f"sim_graph_{name}.npz")
+    g, feeds, _ = build()
+    arr = og.forward(g, feeds)
+    for sn in g.nodes:
+        key = "t_" + sn.output.onnx_name
+        assert np.array_equal(arr[sn.output.onnx_name].reshape(z[key].shape), z[key]), key
