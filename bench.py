@@ -188,6 +188,7 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--detail", help="write per-problem kernel times of one profiled step to this JSON file")
     ap.add_argument("--case", choices=["gemm", "gemm_small", "vectorop", "softmax", "conv"],
                     help="run one job a few times (a small case for ncu captures) and exit")
     args = ap.parse_args()
@@ -292,6 +293,20 @@ def main():
         run_sweep()
         ops.profile_enable(False)
     prof = ops.profile_read()
+    if args.detail and rank == 0:
+        per = []
+        with torch.cuda.stream(stream):
+            ops.profile_enable(True)
+            for (b, m, k, n), (A, B, Cc) in zip(problems, bufs):
+                ops.matmul(A, B, Cc, n=m, k=k, m=n, batch=b, a_batch_stride=m * k, b_batch_stride=k * n,
+                           c_batch_stride=m * n, workspace=ws)
+                torch.cuda.synchronize()
+                pr = ops.profile_read()
+                per.append({"b": b, "m": m, "k": k, "n": n, "gmac": b * m * k * n / 1e9,
+                            "kernels": {kk: round(v[1], 4) for kk, v in pr.items()}})
+            ops.profile_enable(False)
+        with open(args.detail, "w") as fh:
+            json.dump(per, fh, indent=1)
     tensor_macs = sum(b * m * k * n for b, m, k, n in problems if m > 16)
     g_launches, g_ms, _ = prof.get("gemm_i8x4_kernel", (0, 0.0, 0.0))
     peak, peak_src = measure_int8_peak(torch, dev)

@@ -75,59 +75,114 @@ __global__ void __launch_bounds__(256) split_b_kernel(MmArgs p, uint32_t planes,
   }
 }
 
-// Small-n path: thread = 2 adjacent columns x NR rows, K range [k_lo, k_hi).
-template <int NR>
-__global__ void __launch_bounds__(128) mm_small_kernel(MmArgs p, uint32_t kchunk, unsigned long long* partial) {
-  __shared__ int16_t As[NR][512];
+// Row-major B (m % 8 == 0): a 64 (j) x 128 (kk) tile per CTA, 16-byte loads
+// along j, a shared-memory transpose, 16-byte stores of 16 consecutive kk of
+// one j into each plane.
+__global__ void __launch_bounds__(256) split_b_vec_kernel(MmArgs p, uint32_t Kp, int8_t* hi, uint8_t* lo) {
+  __shared__ int16_t tile[64][136];  // [j][kk], rows padded against bank conflicts
+  const uint32_t j0 = blockIdx.x * 64, k0 = blockIdx.y * 128, pl = blockIdx.z;
+  const int16_t* B = p.b + (uint64_t)pl * p.b_bs;
+#pragma unroll
+  for (int it = 0; it < 4; it++) {
+    const int t = threadIdx.x + it * 256;  // 1024 vectors: 128 kk rows x 8 vectors of 8 j
+    const uint32_t kr = t >> 3, jv = (t & 7) * 8;
+    const uint32_t kk = k0 + kr, j = j0 + jv;
+    int4 v = make_int4(0, 0, 0, 0);
+    if (kk < p.k && j < p.m) v = __ldg((const int4*)(B + (uint64_t)kk * p.m + j));
+    const int16_t* e = (const int16_t*)&v;
+#pragma unroll
+    for (int q = 0; q < 8; q++) tile[jv + q][kr] = e[q];
+  }
+  __syncthreads();
+#pragma unroll
+  for (int it = 0; it < 2; it++) {
+    const int t = threadIdx.x + it * 256;  // 512 = 64 j rows x 8 groups of 16 kk
+    const uint32_t jr = t >> 3, kq = (t & 7) * 16;
+    const uint32_t j = j0 + jr, kk = k0 + kq;
+    if (j >= p.m || kk >= Kp) continue;
+    uint32_t h[4], l[4];
+#pragma unroll
+    for (int w = 0; w < 4; w++) {
+      h[w] = l[w] = 0;
+#pragma unroll
+      for (int e = 0; e < 4; e++) {
+        const int16_t v = tile[jr][kq + 4 * w + e];
+        h[w] |= (uint32_t)(uint8_t)(v >> 8) << (8 * e);
+        l[w] |= (uint32_t)(uint8_t)(v & 0xFF) << (8 * e);
+      }
+    }
+    const uint64_t off = ((uint64_t)pl * p.m + j) * Kp + kk;
+    *(int4*)(hi + off) = make_int4((int)h[0], (int)h[1], (int)h[2], (int)h[3]);
+    *(int4*)(lo + off) = make_int4((int)l[0], (int)l[1], (int)l[2], (int)l[3]);
+  }
+}
+
+// Small-n path (GEMV-like, HBM-bound on B): a CTA covers 64 columns; lane =
+// 2 adjacent columns of a B row (a warp reads 128 contiguous bytes per row);
+// the KW warps split K (interleaved rows), sum in shared memory, and the CTA
+// writes the result or (K split across CTAs) adds it to int64 partials with
+// exact integer atomics.  NR rows x 2 columns of int64 sums per thread.
+template <int NR, int KW>
+__global__ void __launch_bounds__(32 * KW) mm_small_kernel(MmArgs p, uint32_t kchunk, unsigned long long* partial) {
+  __shared__ int16_t As[NR][256];
+  __shared__ long long red[KW][NR][64];
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
   const uint32_t bt = blockIdx.y;
-  const uint32_t j = (blockIdx.x * 128 + threadIdx.x) * 2;
+  const uint32_t j = blockIdx.x * 64 + lane * 2;
   const uint32_t k_lo = blockIdx.z * kchunk, k_hi = min(p.k, k_lo + kchunk);
   const int16_t* A = p.a + (uint64_t)bt * p.a_bs;
   const int16_t* B = p.b + (uint64_t)bt * p.b_bs;
   int64_t acc[NR][2];
 #pragma unroll
   for (int r = 0; r < NR; r++) acc[r][0] = acc[r][1] = 0;
-  const bool rm = p.kw <= 1 && !p.packed;
-  for (uint32_t kb = k_lo; kb < k_hi; kb += 512) {
-    const uint32_t kn = min(512u, k_hi - kb);
+  const bool vec = p.kw <= 1 && !p.packed && (p.m % 2 == 0) && (((uintptr_t)B & 3) == 0);
+  const bool live = j < p.m;
+  for (uint32_t kb = k_lo; kb < k_hi; kb += 256) {
+    const uint32_t kn = min(256u, k_hi - kb);
     __syncthreads();
-    for (uint32_t t = threadIdx.x; t < NR * 512; t += 128) {
-      const uint32_t r = t / 512, kk = t % 512;
+    for (uint32_t t = threadIdx.x; t < NR * 256; t += 32 * KW) {
+      const uint32_t r = t / 256, kk = t % 256;
       As[r][kk] = (r < p.n && kk < kn) ? __ldg(A + (uint64_t)r * p.k + kb + kk) : (int16_t)0;
     }
     __syncthreads();
-    if (j < p.m) {
-      for (uint32_t kk = 0; kk < kn; kk++) {
-        int32_t b0, b1;
-        if (rm) {
-          const int16_t* row = B + (uint64_t)(kb + kk) * p.m + j;
-          b0 = __ldg(row);
-          b1 = (j + 1 < p.m) ? __ldg(row + 1) : 0;
-        } else {
-          b0 = __ldg(B + b_offset(kb + kk, j, p.k, p.m, p.packed, p.kw));
-          b1 = (j + 1 < p.m) ? __ldg(B + b_offset(kb + kk, j + 1, p.k, p.m, p.packed, p.kw)) : 0;
-        }
+    if (!live) continue;
+#pragma unroll 4
+    for (uint32_t kk = w; kk < kn; kk += KW) {
+      int32_t b0, b1;
+      if (vec) {
+        const uint32_t v = __ldg((const uint32_t*)(B + (uint64_t)(kb + kk) * p.m + j));
+        b0 = (int16_t)(v & 0xFFFF);
+        b1 = (j + 1 < p.m) ? (int16_t)(v >> 16) : 0;
+      } else {
+        b0 = __ldg(B + b_offset(kb + kk, j, p.k, p.m, p.packed, p.kw));
+        b1 = (j + 1 < p.m) ? __ldg(B + b_offset(kb + kk, j + 1, p.k, p.m, p.packed, p.kw)) : 0;
+      }
 #pragma unroll
-        for (int r = 0; r < NR; r++) {
-          const int32_t a = As[r][kk];
-          acc[r][0] += (int64_t)(a * b0);  // |a b| <= 2^30
-          acc[r][1] += (int64_t)(a * b1);
-        }
+      for (int r = 0; r < NR; r++) {
+        const int32_t a = As[r][kk];
+        acc[r][0] += (int64_t)(a * b0);  // |a b| <= 2^30
+        acc[r][1] += (int64_t)(a * b1);
       }
     }
   }
-  if (j >= p.m) return;
 #pragma unroll
-  for (int r = 0; r < NR; r++)
+  for (int r = 0; r < NR; r++) {
+    red[w][r][lane * 2] = acc[r][0];
+    red[w][r][lane * 2 + 1] = acc[r][1];
+  }
+  __syncthreads();
+  for (uint32_t t = threadIdx.x; t < NR * 64; t += 32 * KW) {
+    const uint32_t r = t / 64, c = t % 64, jj = blockIdx.x * 64 + c;
+    if (r >= p.n || jj >= p.m) continue;
+    long long s = 0;
 #pragma unroll
-    for (int e = 0; e < 2; e++) {
-      if (r >= (int)p.n || j + e >= p.m) continue;
-      const uint64_t o = (uint64_t)bt * p.n * p.m + (uint64_t)r * p.m + j + e;
-      if (partial)
-        atomicAdd(partial + o, (unsigned long long)acc[r][e]);
-      else
-        p.c[(uint64_t)bt * p.c_bs + (uint64_t)r * p.m + j + e] = mm_finish(acc[r][e], p.flags);
-    }
+    for (int q = 0; q < KW; q++) s += red[q][r][c];
+    const uint64_t o = (uint64_t)bt * p.n * p.m + (uint64_t)r * p.m + jj;
+    if (partial)
+      atomicAdd(partial + o, (unsigned long long)s);
+    else
+      p.c[(uint64_t)bt * p.c_bs + (uint64_t)r * p.m + jj] = mm_finish(s, p.flags);
+  }
 }
 
 __global__ void mm_small_finish(MmArgs p, const unsigned long long* partial) {
@@ -148,11 +203,13 @@ Plan plan_of(const corm_matmul_desc* d) {
   Plan pl{};
   pl.small = d->n <= kSmallRows;
   if (pl.small) {
-    const uint64_t blocks = (uint64_t)((d->m + 255) / 256) * d->batch;
+    const uint64_t blocks = (uint64_t)((d->m + 63) / 64) * d->batch;
     uint32_t ks = 1;
-    while (blocks * ks < 296 && d->k / (ks * 2) >= 256) ks *= 2;
+    while (blocks * ks < 4 * 148 && d->k / (ks * 2) >= 256) ks *= 2;
     pl.ksplit = ks;
-    pl.kchunk = (d->k + ks - 1) / ks;
+    pl.kchunk = ((d->k + ks - 1) / ks + 255) / 256 * 256;
+    pl.ksplit = (d->k + pl.kchunk - 1) / pl.kchunk;
+    ks = pl.ksplit;
     pl.bytes = ks > 1 ? (size_t)d->batch * d->n * d->m * 8 : 0;
     return pl;
   }
@@ -208,27 +265,20 @@ extern "C" int corm_matmul(const corm_matmul_desc* d, corm_stream_t stream) {
   if (pl.small) {
     unsigned long long* partial = pl.ksplit > 1 ? (unsigned long long*)ws : nullptr;
     if (partial && cudaMemsetAsync(partial, 0, pl.bytes, st) != cudaSuccess) return corm::cuda_status("memset");
-    dim3 grid((d->m + 255) / 256, d->batch, pl.ksplit);
-    if (d->n <= 1)
-      {
-        corm::ProfScope prof_("mm_small_kernel<1>", st);
-        mm_small_kernel<1><<<grid, 128, 0, st>>>(p, pl.kchunk, partial);
-      }
-    else if (d->n <= 4)
-      {
-        corm::ProfScope prof_("mm_small_kernel<4>", st);
-        mm_small_kernel<4><<<grid, 128, 0, st>>>(p, pl.kchunk, partial);
-      }
-    else if (d->n <= 8)
-      {
-        corm::ProfScope prof_("mm_small_kernel<8>", st);
-        mm_small_kernel<8><<<grid, 128, 0, st>>>(p, pl.kchunk, partial);
-      }
-    else
-      {
-        corm::ProfScope prof_("mm_small_kernel<16>", st);
-        mm_small_kernel<16><<<grid, 128, 0, st>>>(p, pl.kchunk, partial);
-      }
+    dim3 grid((d->m + 63) / 64, d->batch, pl.ksplit);
+    if (d->n <= 1) {
+      corm::ProfScope prof_("mm_small_kernel<1>", st);
+      mm_small_kernel<1, 8><<<grid, 256, 0, st>>>(p, pl.kchunk, partial);
+    } else if (d->n <= 4) {
+      corm::ProfScope prof_("mm_small_kernel<4>", st);
+      mm_small_kernel<4, 8><<<grid, 256, 0, st>>>(p, pl.kchunk, partial);
+    } else if (d->n <= 8) {
+      corm::ProfScope prof_("mm_small_kernel<8>", st);
+      mm_small_kernel<8, 8><<<grid, 256, 0, st>>>(p, pl.kchunk, partial);
+    } else {
+      corm::ProfScope prof_("mm_small_kernel<16>", st);
+      mm_small_kernel<16, 4><<<grid, 128, 0, st>>>(p, pl.kchunk, partial);
+    }
     if (int rc = corm::cuda_status("matmul small")) return rc;
     if (partial) {
       {
@@ -246,8 +296,13 @@ extern "C" int corm_matmul(const corm_matmul_desc* d, corm_stream_t stream) {
   uint8_t* b_lo = w + 2 * pl.a_plane_bytes + pl.b_plane_bytes;
   if (int rc = corm::split_planes(d->a, d->a_batch_stride, pl.a_planes, d->n, d->k, d->k, pl.Kp, a_hi, a_lo, st))
     return rc;
-  dim3 gb((d->m + 63) / 64, (pl.Kp + 63) / 64, pl.b_planes);
-  {
+  if (!d->b_packed && d->gemv_kw <= 1 && d->m % 8 == 0 && ((uintptr_t)d->b & 15) == 0 &&
+      (d->b_batch_stride % 8 == 0 || pl.b_planes == 1)) {
+    dim3 gb((d->m + 63) / 64, (pl.Kp + 127) / 128, pl.b_planes);
+    corm::ProfScope prof_("split_b_vec_kernel", st);
+    split_b_vec_kernel<<<gb, 256, 0, st>>>(p, pl.Kp, b_hi, b_lo);
+  } else {
+    dim3 gb((d->m + 63) / 64, (pl.Kp + 63) / 64, pl.b_planes);
     corm::ProfScope prof_("split_b_kernel", st);
     split_b_kernel<<<gb, 256, 0, st>>>(p, pl.b_planes, pl.Kp, b_hi, b_lo);
   }
