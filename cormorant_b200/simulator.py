@@ -324,12 +324,7 @@ class GpuSimulator:
         size = nb if nb != N else na
         outer = N // size
         a_inc, b_inc = (size, 0) if nb != N else (0, size)
-        if size % 8 == 0 or outer == 1:
-            ops.vectorop(a, b, y, size=size, op=op, outer=outer, a_inc=a_inc, b_inc=b_inc, act=act, alpha=alpha)
-        else:
-            # rows not on 8-lane words: one job per row, in order (each row's
-            # zero tail is overwritten by the next row, as a sequential write does)
-            for o in range(outer):
-                ops.vectorop(a[o * a_inc:], b[o * b_inc:], y[o * size:], size=size, op=op, outer=1, act=act,
-                             alpha=alpha)
+        # rows need not be on 8-lane words: the kernel writes a row's tail lanes
+        # only where the next row's data does not land (the hardware's order)
+        ops.vectorop(a, b, y, size=size, op=op, outer=outer, a_inc=a_inc, b_inc=b_inc, act=act, alpha=alpha)
         return y
