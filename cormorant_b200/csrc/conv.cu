@@ -143,7 +143,7 @@ __global__ void __launch_bounds__(256) conv_depthwise(ConvArgs a) {
 
 struct ConvPlan {
   uint32_t K, Kp, Ptot;
-  size_t a_bytes, b_bytes, bytes;
+  size_t a_bytes, b_bytes, partial_bytes, bytes;
 };
 
 ConvPlan plan_of(const corm_conv_desc* d) {
@@ -154,7 +154,8 @@ ConvPlan plan_of(const corm_conv_desc* d) {
   p.Ptot = d->batch * d->out_h * d->out_w;
   p.a_bytes = ((size_t)p.Ptot * p.Kp + 255) & ~(size_t)255;
   p.b_bytes = ((size_t)d->out_ch * p.Kp + 255) & ~(size_t)255;
-  p.bytes = 2 * p.a_bytes + 2 * p.b_bytes;
+  p.partial_bytes = corm::gemm_partial_bytes(p.Ptot, d->out_ch, p.Kp, 1);
+  p.bytes = 2 * p.a_bytes + 2 * p.b_bytes + p.partial_bytes;
   return p;
 }
 
@@ -256,6 +257,9 @@ extern "C" int corm_conv(const corm_conv_desc* d, corm_stream_t stream) {
   j.batch = 1;
   j.a_planes = 1;
   j.b_planes = 1;
+  j.b_mn = 0;
+  j.K = pl.K;
+  j.partial = pl.partial_bytes ? (void*)(w8 + 2 * pl.a_bytes + 2 * pl.b_bytes) : nullptr;
   j.mode = 1;
   j.out = d->y;
   j.P = P;

@@ -111,6 +111,19 @@ __device__ __forceinline__ uint64_t sdesc_sw128(uint32_t smem_addr) {
   return d;
 }
 
+// Shared-memory matrix descriptor: MN-major operand, 128-byte swizzle: rows of
+// 128 bytes hold 128 consecutive MN elements of one k, 8-row swizzle atoms of
+// 1024 bytes stacked along K (SBO); one atom along MN (LBO unused at 128).
+__device__ __forceinline__ uint64_t sdesc_sw128_mn(uint32_t smem_addr) {
+  uint64_t d = 0;
+  d |= (uint64_t)((smem_addr & 0x3FFFF) >> 4);  // start address
+  d |= (uint64_t)(8192 >> 4) << 16;             // LBO: stride between 128-byte MN atoms
+  d |= (uint64_t)(1024 >> 4) << 32;             // SBO: stride between 8-row K groups
+  d |= (uint64_t)1 << 46;                       // descriptor version (sm_100)
+  d |= (uint64_t)2 << 61;                       // SWIZZLE_128B
+  return d;
+}
+
 // 32 lanes x 32 columns of 32-bit TMEM -> 32 registers per thread
 __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
   asm volatile(

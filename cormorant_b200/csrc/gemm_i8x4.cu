@@ -1,14 +1,20 @@
 // tcgen05 kind::i8 GEMM with the four-way int16 split (see gemm_i8x4.h).
 //
-// CTA = 6 warps, one 128 x 128 output tile, warp-specialised:
-//   warp 0      TMA producer: per 128-byte K block, 4 tiles (A hi/lo, B hi/lo,
-//               128 rows x 128 bytes each, 128-byte swizzle) into a STAGES-deep ring
+// Persistent: one CTA per SM (6 warps) walks work units = (batch, 128-row
+// tile, 128-column tile, K split), warp-specialised:
+//   warp 0      TMA producer: per 128-byte K block, 4 tiles (A hi/lo K-major,
+//               B hi/lo K-major or MN-major, 128 x 128 bytes, 128-byte swizzle,
+//               no multicast) into a STAGES-deep ring that runs across units
 //   warp 1      TMEM owner (512 columns) and MMA issuer: 16 tcgen05.mma
-//               (128x128x32) per K block into HH / MID / LL, commit frees the slot
-//   warps 2..5  epilogue: tcgen05.ld of the three accumulators, int64 recombine,
-//               the job's rounding rule, int16 stores
+//               (128x128x32) per K block into HH / MID / LL; waits for the
+//               epilogue to drain TMEM before the next unit (tmem_empty)
+//   warps 2..5  epilogue: tcgen05.ld of the three accumulators, int64
+//               recombine, the job's rounding rule and int16 stores — or, for a
+//               K-split unit, exact int64 atomics into a partial-sum buffer that
+//               gemm_finish_kernel rounds afterwards
 // Every mbarrier wait is bounded (sm100::mbar_wait); a timeout leaves an error
-// code in the per-device error word and the CTA unwinds (TMEM freed).
+// code in the per-device error word and the CTA unwinds (in-flight TMA loads
+// and MMAs waited for, TMEM freed).
 #include <cudaTypedefs.h>
 
 #include <mutex>
@@ -27,6 +33,7 @@ constexpr int STAGE_BYTES = 4 * TILE_BYTES;
 constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
 constexpr uint32_t TMEM_COLS = 512;
 constexpr int THREADS = 192;
+constexpr int NUM_SMS = 148;
 
 struct EpiArgs {
   int mode;
@@ -37,7 +44,9 @@ struct EpiArgs {
   uint64_t img_stride;
   const int16_t* bias;
   uint32_t flags;
-  uint32_t num_kb, a_planes, b_planes;
+  uint32_t num_kb, a_planes, b_planes, b_mn;
+  uint32_t tiles_m, tiles_n, batch, splits, kb_per_split;
+  unsigned long long* partial;
   int* err;
 };
 
@@ -49,6 +58,33 @@ __device__ __forceinline__ int16_t finish(int64_t acc, uint32_t flags) {
   return (int16_t)y;
 }
 
+// element (bz, r, c) of the output: its address offset (mode 0: row-major with
+// batch stride; mode 1: NCHW with the y channel pattern, r = n * P + p)
+__device__ __forceinline__ uint64_t out_offset(const EpiArgs& ep, uint32_t bz, uint32_t r, uint32_t c) {
+  if (ep.mode == 0) return (uint64_t)bz * ep.out_batch_stride + (uint64_t)r * ep.ldc + c;
+  const uint32_t n = r / ep.P, p = r - n * ep.P;
+  const uint64_t coff = ep.y_cn ? (uint64_t)(c % ep.y_cn) * ep.y_cs + (uint64_t)(c / ep.y_cn) * ep.y_gs
+                                : (uint64_t)c * ep.y_cs;
+  return (uint64_t)n * ep.img_stride + coff + p;
+}
+
+struct Unit {
+  uint32_t bz, tile_r, tile_c, kb0, kb1;
+};
+
+__device__ __forceinline__ Unit unit_of(const EpiArgs& ep, uint32_t u) {
+  Unit w;
+  const uint32_t s = u % ep.splits, t = u / ep.splits;
+  const uint32_t per_batch = ep.tiles_m * ep.tiles_n;
+  w.bz = t / per_batch;
+  const uint32_t rem = t - w.bz * per_batch;
+  w.tile_c = (rem / ep.tiles_m) * BN;  // row tiles fastest: consecutive CTAs share the B tile
+  w.tile_r = (rem % ep.tiles_m) * BM;
+  w.kb0 = s * ep.kb_per_split;
+  w.kb1 = min(ep.num_kb, w.kb0 + ep.kb_per_split);
+  return w;
+}
+
 __global__ void __launch_bounds__(THREADS, 1)
     gemm_i8x4_kernel(const __grid_constant__ CUtensorMap map_ahi, const __grid_constant__ CUtensorMap map_alo,
                      const __grid_constant__ CUtensorMap map_bhi, const __grid_constant__ CUtensorMap map_blo,
@@ -58,11 +94,12 @@ __global__ void __launch_bounds__(THREADS, 1)
   uint64_t* full = (uint64_t*)(smem + STAGES * STAGE_BYTES);
   uint64_t* empty = full + STAGES;
   uint64_t* tmem_full = empty + STAGES;
-  uint32_t* tmem_slot = (uint32_t*)(tmem_full + 1);
+  uint64_t* tmem_empty = tmem_full + 1;
+  uint64_t* mma_done = tmem_empty + 1;
+  uint32_t* tmem_slot = (uint32_t*)(mma_done + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const uint32_t tile_r = blockIdx.x * BM, tile_c = blockIdx.y * BN, bz = blockIdx.z;
-  const int a_z = ep.a_planes == 1 ? 0 : (int)bz, b_z = ep.b_planes == 1 ? 0 : (int)bz;
+  const uint32_t units = ep.batch * ep.tiles_m * ep.tiles_n * ep.splits;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; s++) {
@@ -70,6 +107,8 @@ __global__ void __launch_bounds__(THREADS, 1)
       sm100::mbar_init(&empty[s], 1);
     }
     sm100::mbar_init(tmem_full, 1);
+    sm100::mbar_init(tmem_empty, 4);
+    sm100::mbar_init(mma_done, 1);
     sm100::fence_mbar_init();
   }
   if (warp == 1) sm100::tmem_alloc<TMEM_COLS>(tmem_slot);
@@ -79,110 +118,142 @@ __global__ void __launch_bounds__(THREADS, 1)
   const uint32_t tmem = *tmem_slot;
 
   if (warp == 0 && lane == 0) {
-    // ---------------- TMA producer
+    // ---------------- TMA producer (ring counter g runs across units)
     sm100::prefetch_tmap(&map_ahi);
     sm100::prefetch_tmap(&map_alo);
     sm100::prefetch_tmap(&map_bhi);
     sm100::prefetch_tmap(&map_blo);
-    uint32_t issued = 0;
+    uint32_t g = 0;
     bool ok = true;
-    for (uint32_t kb = 0; kb < ep.num_kb; kb++) {
-      const int s = kb % STAGES;
-      if (kb >= (uint32_t)STAGES && !sm100::mbar_wait(&empty[s], ((kb / STAGES) - 1) & 1, ep.err, 101)) {
-        ok = false;
-        break;
+    for (uint32_t u = blockIdx.x; u < units && ok; u += gridDim.x) {
+      const Unit w = unit_of(ep, u);
+      const int a_z = ep.a_planes == 1 ? 0 : (int)w.bz, b_z = ep.b_planes == 1 ? 0 : (int)w.bz;
+      for (uint32_t kb = w.kb0; kb < w.kb1; kb++, g++) {
+        const int s = g % STAGES;
+        if (g >= (uint32_t)STAGES && !sm100::mbar_wait(&empty[s], ((g / STAGES) - 1) & 1, ep.err, 101)) {
+          ok = false;
+          break;
+        }
+        uint8_t* st = smem + s * STAGE_BYTES;
+        sm100::mbar_expect_tx(&full[s], STAGE_BYTES);
+        const int x = (int)(kb * BK);
+        sm100::tma_load_3d(st, &map_ahi, &full[s], x, (int)w.tile_r, a_z);
+        sm100::tma_load_3d(st + TILE_BYTES, &map_alo, &full[s], x, (int)w.tile_r, a_z);
+        if (ep.b_mn) {  // B planes [plane][K][cols]: box = 128 columns x 128 K rows
+          sm100::tma_load_3d(st + 2 * TILE_BYTES, &map_bhi, &full[s], (int)w.tile_c, x, b_z);
+          sm100::tma_load_3d(st + 3 * TILE_BYTES, &map_blo, &full[s], (int)w.tile_c, x, b_z);
+        } else {
+          sm100::tma_load_3d(st + 2 * TILE_BYTES, &map_bhi, &full[s], x, (int)w.tile_c, b_z);
+          sm100::tma_load_3d(st + 3 * TILE_BYTES, &map_blo, &full[s], x, (int)w.tile_c, b_z);
+        }
       }
-      uint8_t* st = smem + s * STAGE_BYTES;
-      sm100::mbar_expect_tx(&full[s], STAGE_BYTES);
-      const int x = (int)(kb * BK);
-      sm100::tma_load_3d(st, &map_ahi, &full[s], x, (int)tile_r, a_z);
-      sm100::tma_load_3d(st + TILE_BYTES, &map_alo, &full[s], x, (int)tile_r, a_z);
-      sm100::tma_load_3d(st + 2 * TILE_BYTES, &map_bhi, &full[s], x, (int)tile_c, b_z);
-      sm100::tma_load_3d(st + 3 * TILE_BYTES, &map_blo, &full[s], x, (int)tile_c, b_z);
-      issued++;
     }
     if (!ok) {
       // let the loads already issued land before the CTA's shared memory goes away
-      const uint32_t first = issued > (uint32_t)STAGES ? issued - STAGES : 0;
-      for (uint32_t kb = first; kb < issued; kb++) {
-        sm100::mbar_wait(&full[kb % STAGES], (kb / STAGES) & 1, nullptr, 0, 200000000ll);
-      }
+      for (uint32_t q = g > (uint32_t)STAGES ? g - STAGES : 0; q < g; q++)
+        sm100::mbar_wait(&full[q % STAGES], (q / STAGES) & 1, nullptr, 0, 200000000ll);
     }
   } else if (warp == 1 && lane == 0) {
     // ---------------- MMA issuer
-    constexpr uint32_t ID_SS = sm100::idesc_i8(BM, BN, 1, 1);
-    constexpr uint32_t ID_SU = sm100::idesc_i8(BM, BN, 1, 0);
-    constexpr uint32_t ID_US = sm100::idesc_i8(BM, BN, 0, 1);
-    constexpr uint32_t ID_UU = sm100::idesc_i8(BM, BN, 0, 0);
+    const uint32_t bmaj = ep.b_mn ? (1u << 16) : 0u;
+    const uint32_t ID_SS = sm100::idesc_i8(BM, BN, 1, 1) | bmaj;
+    const uint32_t ID_SU = sm100::idesc_i8(BM, BN, 1, 0) | bmaj;
+    const uint32_t ID_US = sm100::idesc_i8(BM, BN, 0, 1) | bmaj;
+    const uint32_t ID_UU = sm100::idesc_i8(BM, BN, 0, 0) | bmaj;
     const uint32_t acc_hh = tmem, acc_mid = tmem + BN, acc_ll = tmem + 2 * BN;
-    for (uint32_t kb = 0; kb < ep.num_kb; kb++) {
-      const int s = kb % STAGES;
-      if (!sm100::mbar_wait(&full[s], (kb / STAGES) & 1, ep.err, 102)) break;
+    uint32_t g = 0, i = 0;
+    bool ok = true;
+    for (uint32_t u = blockIdx.x; u < units && ok; u += gridDim.x, i++) {
+      const Unit w = unit_of(ep, u);
+      if (i > 0 && !sm100::mbar_wait(tmem_empty, (i - 1) & 1, ep.err, 104)) break;
       sm100::tc_fence_after();
-      const uint32_t base = sm100::smem_u32(smem + s * STAGE_BYTES);
-      const uint64_t d_ahi = sm100::sdesc_sw128(base), d_alo = sm100::sdesc_sw128(base + TILE_BYTES);
-      const uint64_t d_bhi = sm100::sdesc_sw128(base + 2 * TILE_BYTES), d_blo = sm100::sdesc_sw128(base + 3 * TILE_BYTES);
+      for (uint32_t kb = w.kb0; kb < w.kb1; kb++, g++) {
+        const int s = g % STAGES;
+        if (!sm100::mbar_wait(&full[s], (g / STAGES) & 1, ep.err, 102)) {
+          ok = false;
+          break;
+        }
+        sm100::tc_fence_after();
+        const uint32_t base = sm100::smem_u32(smem + s * STAGE_BYTES);
+        const uint64_t d_ahi = sm100::sdesc_sw128(base), d_alo = sm100::sdesc_sw128(base + TILE_BYTES);
+        const uint64_t d_bhi = ep.b_mn ? sm100::sdesc_sw128_mn(base + 2 * TILE_BYTES) : sm100::sdesc_sw128(base + 2 * TILE_BYTES);
+        const uint64_t d_blo = ep.b_mn ? sm100::sdesc_sw128_mn(base + 3 * TILE_BYTES) : sm100::sdesc_sw128(base + 3 * TILE_BYTES);
+        // K step of 32 int8: 32 bytes inside a K-major swizzled row, or 32 rows
+        // (4 swizzle atoms of 1024 bytes) of an MN-major tile
+        const uint64_t b_step = ep.b_mn ? (uint64_t)(4096 >> 4) : (uint64_t)(32 >> 4);
 #pragma unroll
-      for (int ks = 0; ks < BK / 32; ks++) {
-        const uint64_t adv = (uint64_t)((ks * 32) >> 4);  // 32-byte K step inside the swizzled row
-        const uint32_t acc = (kb | ks) ? 1u : 0u;
-        sm100::mma_i8(acc_hh, d_ahi + adv, d_bhi + adv, ID_SS, acc);
-        sm100::mma_i8(acc_mid, d_ahi + adv, d_blo + adv, ID_SU, acc);
-        sm100::mma_i8(acc_mid, d_alo + adv, d_bhi + adv, ID_US, 1u);
-        sm100::mma_i8(acc_ll, d_alo + adv, d_blo + adv, ID_UU, acc);
+        for (int ks = 0; ks < BK / 32; ks++) {
+          const uint64_t adv = (uint64_t)((ks * 32) >> 4), bdv = b_step * ks;
+          const uint32_t acc = (kb != w.kb0 || ks) ? 1u : 0u;
+          sm100::mma_i8(acc_hh, d_ahi + adv, d_bhi + bdv, ID_SS, acc);
+          sm100::mma_i8(acc_mid, d_ahi + adv, d_blo + bdv, ID_SU, acc);
+          sm100::mma_i8(acc_mid, d_alo + adv, d_bhi + bdv, ID_US, 1u);
+          sm100::mma_i8(acc_ll, d_alo + adv, d_blo + bdv, ID_UU, acc);
+        }
+        sm100::mma_commit(&empty[s]);
       }
-      sm100::mma_commit(&empty[s]);
+      if (ok) sm100::mma_commit(tmem_full);
     }
-    sm100::mma_commit(tmem_full);  // also on failure: completes once every issued MMA has
+    // every MMA issued has completed before TMEM is freed
+    sm100::mma_commit(mma_done);
+    sm100::mbar_wait(mma_done, 0, nullptr, 0, 200000000ll);
   } else if (warp >= 2) {
     // ---------------- epilogue
     const int q = warp & 3;  // TMEM lane quarter this warp may access
-    const bool ok = sm100::mbar_wait(tmem_full, 0, ep.err, 103) && *(volatile int*)ep.err == 0;
-    sm100::tc_fence_after();
-    const uint32_t r = tile_r + q * 32 + lane;
-    // row addressing
-    uint64_t row_off = 0;
-    if (ep.mode == 0) {
-      row_off = (uint64_t)bz * ep.out_batch_stride + (uint64_t)r * ep.ldc;
-    } else if (r < ep.rows) {
-      const uint32_t n = r / ep.P, p = r - n * ep.P;
-      row_off = (uint64_t)n * ep.img_stride + p;
-    }
     const uint32_t lane_addr = (uint32_t)(q * 32) << 16;
-    for (int cc = 0; cc < BN; cc += 32) {
-      uint32_t hh[32], mid[32], ll[32];
-      sm100::tmem_ld32(tmem + lane_addr + cc, hh);
-      sm100::tmem_ld32(tmem + lane_addr + BN + cc, mid);
-      sm100::tmem_ld32(tmem + lane_addr + 2 * BN + cc, ll);
-      sm100::tmem_ld_wait();
-      if (!ok || r >= ep.rows) continue;
-      const uint32_t c0 = tile_c + cc;
-      if (ep.mode == 0) {
-        int16_t* dst = ep.out + row_off + c0;
-        alignas(16) int16_t v[32];
-#pragma unroll
-        for (int j = 0; j < 32; j++) {
-          const int64_t acc = ((int64_t)(int32_t)hh[j] << 16) + ((int64_t)(int32_t)mid[j] << 8) + (int64_t)(int32_t)ll[j];
-          v[j] = finish(acc, ep.flags);
+    uint32_t i = 0;
+    for (uint32_t u = blockIdx.x; u < units; u += gridDim.x, i++) {
+      const Unit w = unit_of(ep, u);
+      if (!sm100::mbar_wait(tmem_full, i & 1, ep.err, 103)) break;
+      sm100::tc_fence_after();
+      const uint32_t r = w.tile_r + q * 32 + lane;
+      const bool row_ok = r < ep.rows;
+      for (int cc = 0; cc < BN; cc += 32) {
+        uint32_t hh[32], mid[32], ll[32];
+        sm100::tmem_ld32(tmem + lane_addr + cc, hh);
+        sm100::tmem_ld32(tmem + lane_addr + BN + cc, mid);
+        sm100::tmem_ld32(tmem + lane_addr + 2 * BN + cc, ll);
+        sm100::tmem_ld_wait();
+        if (cc + 32 >= BN) {  // TMEM drained: the next unit's MMAs may start
+          sm100::tc_fence_before();
+          __syncwarp();
+          if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(sm100::smem_u32(tmem_empty)) : "memory");
         }
-        if (c0 + 32 <= ep.cols && ((uintptr_t)dst & 15) == 0) {
+        if (!row_ok) continue;
+        const uint32_t c0 = w.tile_c + cc;
+        if (ep.partial) {
+          unsigned long long* dst = ep.partial + ((uint64_t)w.bz * ep.rows + r) * ep.cols + c0;
 #pragma unroll
-          for (int j = 0; j < 4; j++) ((int4*)dst)[j] = ((const int4*)v)[j];
+          for (int j = 0; j < 32; j++) {
+            if (c0 + j >= ep.cols) continue;
+            const int64_t acc = ((int64_t)(int32_t)hh[j] << 16) + ((int64_t)(int32_t)mid[j] << 8) + (int64_t)(int32_t)ll[j];
+            atomicAdd(dst + j, (unsigned long long)acc);
+          }
+        } else if (ep.mode == 0) {
+          int16_t* dst = ep.out + out_offset(ep, w.bz, r, c0);
+          alignas(16) int16_t v[32];
+#pragma unroll
+          for (int j = 0; j < 32; j++) {
+            const int64_t acc = ((int64_t)(int32_t)hh[j] << 16) + ((int64_t)(int32_t)mid[j] << 8) + (int64_t)(int32_t)ll[j];
+            v[j] = finish(acc, ep.flags);
+          }
+          if (c0 + 32 <= ep.cols && ((uintptr_t)dst & 15) == 0) {
+#pragma unroll
+            for (int j = 0; j < 4; j++) ((int4*)dst)[j] = ((const int4*)v)[j];
+          } else {
+#pragma unroll
+            for (int j = 0; j < 32; j++)
+              if (c0 + j < ep.cols) dst[j] = v[j];
+          }
         } else {
 #pragma unroll
-          for (int j = 0; j < 32; j++)
-            if (c0 + j < ep.cols) dst[j] = v[j];
-        }
-      } else {
-#pragma unroll
-        for (int j = 0; j < 32; j++) {
-          const uint32_t c = c0 + j;
-          if (c >= ep.cols) continue;
-          int64_t acc = ((int64_t)(int32_t)hh[j] << 16) + ((int64_t)(int32_t)mid[j] << 8) + (int64_t)(int32_t)ll[j];
-          if (ep.bias) acc += (int64_t)ep.bias[c] << 8;
-          const uint64_t coff = ep.y_cn ? (uint64_t)(c % ep.y_cn) * ep.y_cs + (uint64_t)(c / ep.y_cn) * ep.y_gs
-                                        : (uint64_t)c * ep.y_cs;
-          ep.out[row_off + coff] = finish(acc, ep.flags);
+          for (int j = 0; j < 32; j++) {
+            const uint32_t c = c0 + j;
+            if (c >= ep.cols) continue;
+            int64_t acc = ((int64_t)(int32_t)hh[j] << 16) + ((int64_t)(int32_t)mid[j] << 8) + (int64_t)(int32_t)ll[j];
+            if (ep.bias) acc += (int64_t)ep.bias[c] << 8;
+            ep.out[out_offset(ep, 0, r, c)] = finish(acc, ep.flags);
+          }
         }
       }
     }
@@ -192,6 +263,19 @@ __global__ void __launch_bounds__(THREADS, 1)
   if (warp == 1) {
     sm100::tc_fence_after();
     sm100::tmem_dealloc<TMEM_COLS>(tmem);
+  }
+}
+
+// K-split units summed exactly in int64; this applies the bias and the rule.
+__global__ void __launch_bounds__(256) gemm_finish_kernel(const EpiArgs ep) {
+  const uint64_t total = (uint64_t)ep.batch * ep.rows * ep.cols;
+  for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (uint64_t)gridDim.x * blockDim.x) {
+    const uint32_t c = (uint32_t)(i % ep.cols);
+    const uint64_t br = i / ep.cols;
+    const uint32_t r = (uint32_t)(br % ep.rows), bz = (uint32_t)(br / ep.rows);
+    int64_t acc = (int64_t)ep.partial[i];
+    if (ep.mode == 1 && ep.bias) acc += (int64_t)ep.bias[c] << 8;
+    ep.out[out_offset(ep, ep.mode == 0 ? bz : 0, r, c)] = finish(acc, ep.flags);
   }
 }
 
@@ -243,18 +327,38 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   return fn;
 }
 
-// [planes][rows][Kp] bytes, box 128 (K) x 128 (rows) x 1, 128-byte swizzle
-bool make_map(CUtensorMap* map, const void* base, uint32_t Kp, uint32_t rows, uint32_t planes) {
+// [planes][outer][inner] bytes, box 128 x 128 x 1, 128-byte swizzle
+bool make_map(CUtensorMap* map, const void* base, uint32_t inner, uint32_t outer, uint32_t planes) {
   auto fn = encode_fn();
   if (!fn) return false;
-  cuuint64_t dims[3] = {Kp, rows, planes};
-  cuuint64_t strides[2] = {Kp, (cuuint64_t)Kp * rows};
-  cuuint32_t box[3] = {BK, BM, 1};
+  cuuint64_t dims[3] = {inner, outer, planes};
+  cuuint64_t strides[2] = {inner, (cuuint64_t)inner * outer};
+  cuuint32_t box[3] = {128, 128, 1};
   cuuint32_t estr[3] = {1, 1, 1};
   CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void*>(base), dims, strides, box, estr,
                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS;
+}
+
+struct Split {
+  uint32_t tiles, num_kb, splits, kps;
+};
+
+Split split_of(uint32_t rows, uint32_t cols, uint32_t Kp, uint32_t batch) {
+  Split s;
+  s.tiles = batch * ((rows + BM - 1) / BM) * ((cols + BN - 1) / BN);
+  s.num_kb = (Kp + BK - 1) / BK;
+  s.splits = 1;
+  // fewer tiles than SMs: split K (at least 4 K blocks per split) to fill the GPU
+  if (s.tiles < (uint32_t)NUM_SMS && s.num_kb >= 8) {
+    uint32_t want = (2 * NUM_SMS + s.tiles - 1) / s.tiles;
+    s.splits = want < s.num_kb / 4 ? want : s.num_kb / 4;
+    if (s.splits < 1) s.splits = 1;
+  }
+  s.kps = (s.num_kb + s.splits - 1) / s.splits;
+  s.splits = (s.num_kb + s.kps - 1) / s.kps;
+  return s;
 }
 
 int* g_err_word[64];
@@ -287,15 +391,24 @@ int split_planes(const int16_t* src, uint64_t src_bs, uint32_t planes, uint32_t 
   return cuda_status("split_planes");
 }
 
+size_t gemm_partial_bytes(uint32_t rows, uint32_t cols, uint32_t Kp, uint32_t batch) {
+  const Split sp = split_of(rows, cols, Kp, batch);
+  return sp.splits > 1 ? (((size_t)batch * rows * cols * 8 + 255) & ~(size_t)255) : 0;
+}
+
 int gemm_i8x4(const GemmJob& j, cudaStream_t stream) {
   if (j.Kp % 16 || j.Kp == 0 || j.Kp > kGemmMaxK + 128)
     return fail(CORM_ELIMIT, "gemm: K %u outside 1..%u", j.Kp, kGemmMaxK);
   int* err = device_error_word();
   if (!err) return fail(CORM_ECUDA, "gemm: error word allocation failed");
   CUtensorMap m_ahi, m_alo, m_bhi, m_blo;
-  if (!make_map(&m_ahi, j.a_hi, j.Kp, j.rows, j.a_planes) || !make_map(&m_alo, j.a_lo, j.Kp, j.rows, j.a_planes) ||
-      !make_map(&m_bhi, j.b_hi, j.Kp, j.cols, j.b_planes) || !make_map(&m_blo, j.b_lo, j.Kp, j.cols, j.b_planes))
-    return fail(CORM_ECUDA, "gemm: cuTensorMapEncodeTiled failed");
+  bool ok = make_map(&m_ahi, j.a_hi, j.Kp, j.rows, j.a_planes) && make_map(&m_alo, j.a_lo, j.Kp, j.rows, j.a_planes);
+  if (j.b_mn)
+    ok = ok && make_map(&m_bhi, j.b_hi, j.cols_p, j.K, j.b_planes) && make_map(&m_blo, j.b_lo, j.cols_p, j.K, j.b_planes);
+  else
+    ok = ok && make_map(&m_bhi, j.b_hi, j.Kp, j.cols, j.b_planes) && make_map(&m_blo, j.b_lo, j.Kp, j.cols, j.b_planes);
+  if (!ok) return fail(CORM_ECUDA, "gemm: cuTensorMapEncodeTiled failed");
+  const Split sp = split_of(j.rows, j.cols, j.Kp, j.batch);
   EpiArgs ep{};
   ep.mode = j.mode;
   ep.out = j.out;
@@ -310,10 +423,23 @@ int gemm_i8x4(const GemmJob& j, cudaStream_t stream) {
   ep.img_stride = j.img_stride;
   ep.bias = j.bias;
   ep.flags = j.flags;
-  ep.num_kb = (j.Kp + BK - 1) / BK;
+  ep.num_kb = sp.num_kb;
   ep.a_planes = j.a_planes;
   ep.b_planes = j.b_planes;
+  ep.b_mn = j.b_mn;
+  ep.tiles_m = (j.rows + BM - 1) / BM;
+  ep.tiles_n = (j.cols + BN - 1) / BN;
+  ep.batch = j.batch;
+  ep.splits = sp.splits;
+  ep.kb_per_split = sp.kps;
+  ep.partial = nullptr;
   ep.err = err;
+  if (sp.splits > 1) {
+    if (!j.partial) return fail(CORM_ENOMEM, "gemm: K-split job without a partial-sum buffer");
+    ep.partial = (unsigned long long*)j.partial;
+    if (cudaMemsetAsync(j.partial, 0, (size_t)j.batch * j.rows * j.cols * 8, stream) != cudaSuccess)
+      return cuda_status("gemm partial memset");
+  }
   static bool attr_set[64];
   int dev = 0;
   cudaGetDevice(&dev);
@@ -321,13 +447,22 @@ int gemm_i8x4(const GemmJob& j, cudaStream_t stream) {
     cudaFuncSetAttribute(gemm_i8x4_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
     attr_set[dev] = true;
   }
-  dim3 grid((j.rows + BM - 1) / BM, (j.cols + BN - 1) / BN, j.batch);
-  if (grid.y > 65535 || grid.z > 65535) return fail(CORM_ELIMIT, "gemm: grid %u x %u x %u", grid.x, grid.y, grid.z);
+  const uint64_t units = (uint64_t)sp.tiles * sp.splits;
+  if (units >= (1ull << 31)) return fail(CORM_ELIMIT, "gemm: %llu work units", (unsigned long long)units);
+  const unsigned grid = (unsigned)(units < (uint64_t)NUM_SMS ? units : NUM_SMS);
   {
-    corm::ProfScope prof_("gemm_i8x4_kernel", stream);
+    ProfScope prof_("gemm_i8x4_kernel", stream);
     gemm_i8x4_kernel<<<grid, THREADS, SMEM_BYTES, stream>>>(m_ahi, m_alo, m_bhi, m_blo, ep);
   }
-  return cuda_status("gemm_i8x4");
+  if (int rc = cuda_status("gemm_i8x4")) return rc;
+  if (sp.splits > 1) {
+    {
+      ProfScope prof_("gemm_finish_kernel", stream);
+      gemm_finish_kernel<<<corm_blocks((uint64_t)j.batch * j.rows * j.cols, 256), 256, 0, stream>>>(ep);
+    }
+    return cuda_status("gemm_finish");
+  }
+  return CORM_OK;
 }
 
 }  // namespace corm

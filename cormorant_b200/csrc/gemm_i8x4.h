@@ -23,6 +23,11 @@ struct GemmJob {
   const uint8_t* b_lo;
   uint32_t rows, cols, Kp, batch;
   uint32_t a_planes, b_planes;  // 1 (broadcast) or batch
+  // B planes: K-major [planes][cols][Kp] (b_mn = 0), or MN-major [planes][K][cols_p]
+  // with cols_p = cols rounded up to 16 (b_mn = 1)
+  uint32_t b_mn, K, cols_p;
+  // K-split partial sums (int64 [batch][rows][cols]), gemm_partial_bytes() bytes, or nullptr
+  void* partial;
   // epilogue addressing
   int mode;                 // 0: out[b*obs + r*ldc + c]; 1: conv NCHW y[n][pattern(c)][p], r = n*P + p
   int16_t* out;
@@ -39,9 +44,11 @@ constexpr uint32_t kGemmMaxK = 32768;
 // Launch the tcgen05 GEMM (error code, 0 on success).
 int gemm_i8x4(const GemmJob& job, cudaStream_t stream);
 
-// Split an int16 matrix into the hi / lo planes, rows K-major:
-//   dst row (b, r) element kk <- src[b*src_bs + r*ld + kk*ks]   (kk < K, zero to Kp)
-// with a generic element stride ks (1: rows contiguous; m: a transposed read).
+// Bytes of the K-split partial-sum buffer the job needs (0: no split).
+size_t gemm_partial_bytes(uint32_t rows, uint32_t cols, uint32_t Kp, uint32_t batch);
+
+// Split an int16 matrix into the hi / lo planes row by row:
+//   dst (b, r, kk) <- src[b*src_bs + r*ld + kk]   (kk < K, zero up to Kp)
 int split_planes(const int16_t* src, uint64_t src_bs, uint32_t planes, uint32_t rows, uint64_t ld, uint32_t K,
                  uint32_t Kp, int8_t* hi, uint8_t* lo, cudaStream_t stream);
 

@@ -47,73 +47,30 @@ __device__ __forceinline__ int16_t mm_finish(int64_t acc, uint32_t flags) {
   return (int16_t)y;
 }
 
-// B (k x m, any layout) of one batch plane -> K-major hi / lo planes [m][Kp].
-__global__ void __launch_bounds__(256) split_b_kernel(MmArgs p, uint32_t planes, uint32_t Kp, int8_t* hi, uint8_t* lo) {
-  __shared__ int16_t tile[64][65];  // [j][kk]
-  const uint32_t j0 = blockIdx.x * 64, k0 = blockIdx.y * 64, pl = blockIdx.z;
-  const int16_t* B = p.b + (uint64_t)pl * p.b_bs;
-  for (int t = threadIdx.x; t < 64 * 64; t += 256) {
-    const uint32_t kk = k0 + t / 64, j = j0 + t % 64;
-    tile[t % 64][t / 64] = (kk < p.k && j < p.m) ? __ldg(B + b_offset(kk, j, p.k, p.m, p.packed, p.kw)) : (int16_t)0;
-  }
-  __syncthreads();
-  // each thread writes 8 consecutive kk of one j row (8 bytes to each plane)
-  for (int t = threadIdx.x; t < 64 * 8; t += 256) {
-    const uint32_t jr = t / 8, kq = (t % 8) * 8;
-    const uint32_t j = j0 + jr, kk = k0 + kq;
-    if (j >= p.m || kk >= Kp) continue;
-    uint64_t h = 0, l = 0;
-#pragma unroll
-    for (int e = 0; e < 8; e++) {
-      const int16_t v = tile[jr][kq + e];
-      h |= (uint64_t)(uint8_t)(v >> 8) << (8 * e);
-      l |= (uint64_t)(uint8_t)(v & 0xFF) << (8 * e);
-    }
-    const uint64_t off = ((uint64_t)pl * p.m + j) * Kp + kk;
-    *(uint64_t*)(hi + off) = h;
-    *(uint64_t*)(lo + off) = l;
-  }
-}
-
-// Row-major B (m % 8 == 0): a 64 (j) x 128 (kk) tile per CTA, 16-byte loads
-// along j, a shared-memory transpose, 16-byte stores of 16 consecutive kk of
-// one j into each plane.
-__global__ void __launch_bounds__(256) split_b_vec_kernel(MmArgs p, uint32_t Kp, int8_t* hi, uint8_t* lo) {
-  __shared__ int16_t tile[64][136];  // [j][kk], rows padded against bank conflicts
-  const uint32_t j0 = blockIdx.x * 64, k0 = blockIdx.y * 128, pl = blockIdx.z;
-  const int16_t* B = p.b + (uint64_t)pl * p.b_bs;
-#pragma unroll
-  for (int it = 0; it < 4; it++) {
-    const int t = threadIdx.x + it * 256;  // 1024 vectors: 128 kk rows x 8 vectors of 8 j
-    const uint32_t kr = t >> 3, jv = (t & 7) * 8;
-    const uint32_t kk = k0 + kr, j = j0 + jv;
-    int4 v = make_int4(0, 0, 0, 0);
-    if (kk < p.k && j < p.m) v = __ldg((const int4*)(B + (uint64_t)kk * p.m + j));
-    const int16_t* e = (const int16_t*)&v;
-#pragma unroll
-    for (int q = 0; q < 8; q++) tile[jv + q][kr] = e[q];
-  }
-  __syncthreads();
-#pragma unroll
-  for (int it = 0; it < 2; it++) {
-    const int t = threadIdx.x + it * 256;  // 512 = 64 j rows x 8 groups of 16 kk
-    const uint32_t jr = t >> 3, kq = (t & 7) * 16;
-    const uint32_t j = j0 + jr, kk = k0 + kq;
-    if (j >= p.m || kk >= Kp) continue;
+// B of any layout -> MN-major hi / lo planes [plane][k][Np]: 16 consecutive
+// columns of one K row per thread (row-major B goes through split_planes).
+__global__ void __launch_bounds__(256) split_b_gather_kernel(MmArgs p, uint32_t planes, uint32_t Np, int8_t* hi,
+                                                             uint8_t* lo) {
+  const uint64_t per_row = Np / 16, total = (uint64_t)planes * p.k * per_row;
+  for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (uint64_t)gridDim.x * blockDim.x) {
+    const uint64_t row = i / per_row;  // plane * k + kk
+    const uint32_t j0 = (uint32_t)(i - row * per_row) * 16;
+    const uint32_t pl = (uint32_t)(row / p.k), kk = (uint32_t)(row % p.k);
+    const int16_t* B = p.b + (uint64_t)pl * p.b_bs;
     uint32_t h[4], l[4];
 #pragma unroll
     for (int w = 0; w < 4; w++) {
       h[w] = l[w] = 0;
 #pragma unroll
       for (int e = 0; e < 4; e++) {
-        const int16_t v = tile[jr][kq + 4 * w + e];
+        const uint32_t j = j0 + 4 * w + e;
+        const int16_t v = j < p.m ? __ldg(B + b_offset(kk, j, p.k, p.m, p.packed, p.kw)) : (int16_t)0;
         h[w] |= (uint32_t)(uint8_t)(v >> 8) << (8 * e);
         l[w] |= (uint32_t)(uint8_t)(v & 0xFF) << (8 * e);
       }
     }
-    const uint64_t off = ((uint64_t)pl * p.m + j) * Kp + kk;
-    *(int4*)(hi + off) = make_int4((int)h[0], (int)h[1], (int)h[2], (int)h[3]);
-    *(int4*)(lo + off) = make_int4((int)l[0], (int)l[1], (int)l[2], (int)l[3]);
+    *(int4*)(hi + row * Np + j0) = make_int4((int)h[0], (int)h[1], (int)h[2], (int)h[3]);
+    *(int4*)(lo + row * Np + j0) = make_int4((int)l[0], (int)l[1], (int)l[2], (int)l[3]);
   }
 }
 
@@ -195,8 +152,8 @@ __global__ void mm_small_finish(MmArgs p, const unsigned long long* partial) {
 
 struct Plan {
   bool small;
-  uint32_t Kp, a_planes, b_planes, ksplit, kchunk;
-  size_t a_plane_bytes, b_plane_bytes, bytes;
+  uint32_t Kp, Np, a_planes, b_planes, ksplit, kchunk;
+  size_t a_plane_bytes, b_plane_bytes, partial_bytes, bytes;
 };
 
 Plan plan_of(const corm_matmul_desc* d) {
@@ -214,11 +171,13 @@ Plan plan_of(const corm_matmul_desc* d) {
     return pl;
   }
   pl.Kp = (d->k + 15u) / 16u * 16u;
+  pl.Np = (d->m + 15u) / 16u * 16u;
   pl.a_planes = (d->a_batch_stride == 0 || d->batch == 1) ? 1 : d->batch;
   pl.b_planes = (d->b_batch_stride == 0 || d->batch == 1) ? 1 : d->batch;
   pl.a_plane_bytes = ((size_t)pl.a_planes * d->n * pl.Kp + 255) & ~(size_t)255;
-  pl.b_plane_bytes = ((size_t)pl.b_planes * d->m * pl.Kp + 255) & ~(size_t)255;
-  pl.bytes = 2 * pl.a_plane_bytes + 2 * pl.b_plane_bytes;
+  pl.b_plane_bytes = ((size_t)pl.b_planes * d->k * pl.Np + 255) & ~(size_t)255;  // MN-major [k][Np]
+  pl.partial_bytes = corm::gemm_partial_bytes(d->n, d->m, pl.Kp, d->batch);
+  pl.bytes = 2 * pl.a_plane_bytes + 2 * pl.b_plane_bytes + pl.partial_bytes;
   return pl;
 }
 
@@ -296,17 +255,18 @@ extern "C" int corm_matmul(const corm_matmul_desc* d, corm_stream_t stream) {
   uint8_t* b_lo = w + 2 * pl.a_plane_bytes + pl.b_plane_bytes;
   if (int rc = corm::split_planes(d->a, d->a_batch_stride, pl.a_planes, d->n, d->k, d->k, pl.Kp, a_hi, a_lo, st))
     return rc;
-  if (!d->b_packed && d->gemv_kw <= 1 && d->m % 8 == 0 && ((uintptr_t)d->b & 15) == 0 &&
-      (d->b_batch_stride % 8 == 0 || pl.b_planes == 1)) {
-    dim3 gb((d->m + 63) / 64, (pl.Kp + 127) / 128, pl.b_planes);
-    corm::ProfScope prof_("split_b_vec_kernel", st);
-    split_b_vec_kernel<<<gb, 256, 0, st>>>(p, pl.Kp, b_hi, b_lo);
+  if (!d->b_packed && d->gemv_kw <= 1) {
+    // row-major B is already MN-major: an elementwise split, rows of m padded to Np
+    if (int rc = corm::split_planes(d->b, d->b_batch_stride, pl.b_planes, d->k, d->m, d->m, pl.Np, b_hi, b_lo, st))
+      return rc;
   } else {
-    dim3 gb((d->m + 63) / 64, (pl.Kp + 63) / 64, pl.b_planes);
-    corm::ProfScope prof_("split_b_kernel", st);
-    split_b_kernel<<<gb, 256, 0, st>>>(p, pl.b_planes, pl.Kp, b_hi, b_lo);
+    const uint64_t total = (uint64_t)pl.b_planes * d->k * (pl.Np / 16);
+    {
+      corm::ProfScope prof_("split_b_gather_kernel", st);
+      split_b_gather_kernel<<<corm_blocks(total, 256, 148u * 16u), 256, 0, st>>>(p, pl.b_planes, pl.Np, b_hi, b_lo);
+    }
+    if (int rc = corm::cuda_status("matmul split_b")) return rc;
   }
-  if (int rc = corm::cuda_status("matmul split_b")) return rc;
   corm::GemmJob j{};
   j.a_hi = a_hi;
   j.a_lo = a_lo;
@@ -318,6 +278,10 @@ extern "C" int corm_matmul(const corm_matmul_desc* d, corm_stream_t stream) {
   j.batch = d->batch;
   j.a_planes = pl.a_planes;
   j.b_planes = pl.b_planes;
+  j.b_mn = 1;
+  j.K = d->k;
+  j.cols_p = pl.Np;
+  j.partial = pl.partial_bytes ? (void*)(w + 2 * pl.a_plane_bytes + 2 * pl.b_plane_bytes) : nullptr;
   j.mode = 0;
   j.out = d->c;
   j.out_batch_stride = d->c_batch_stride;
