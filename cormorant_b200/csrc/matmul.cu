@@ -6,12 +6,13 @@
 // _simulate.py:620-633) is the exact sum, its exponent path (:814-835) the
 // int32-wrapped one (CORM_F_WRAP32).
 //
-// n >= 17 rows: the operands are split into int8 planes (A as is, B
-// transposed to K-major) and multiplied on the tensor cores (gemm_i8x4.cu).
-// n <= 16 rows (GEMV-like, HBM-bound on B): a CUDA-core kernel reads int16
-// B once and keeps 2 columns x n rows of int64 sums per thread, splitting K
-// across CTAs (exact integer atomics) when the output alone is too small to
-// fill the GPU.
+// n >= 3 rows: the operands are split into int8 planes (A K-major, B as it
+// lies, MN-major) and multiplied on the tensor cores (gemm_i8x4.cu); the TMA
+// fills the rows of a 128-row tile beyond n with zeros.
+// n <= 2 rows (GEMV, HBM-bound on B): a CUDA-core kernel reads int16 B once
+// and keeps 2 columns x n rows of int64 sums per thread, splitting K across
+// CTAs (exact integer atomics) when the output alone is too small to fill
+// the GPU.
 #include "corm_common.cuh"
 #include "gemm_i8x4.h"
 
@@ -19,7 +20,7 @@ namespace {
 
 constexpr uint32_t kTileM = 32;      // packed-B tile width (platforms/kv260.json kernels.matmul.tile_m)
 constexpr uint32_t kMaxK = 4096;     // platforms/kv260.json kernels.matmul.max_k
-constexpr uint32_t kSmallRows = 16;  // n at or below: CUDA-core path
+constexpr uint32_t kSmallRows = 2;  // n at or below: CUDA-core path (above: tensor cores, M padded by TMA zero fill)
 
 // offset of B[kk][j] (MatmulKernel.h matmul_packed_index / matmul_gemv_index)
 __device__ __forceinline__ uint64_t b_offset(uint32_t kk, uint32_t j, uint32_t k, uint32_t m, uint32_t packed,
