@@ -16,7 +16,7 @@ CORM_OK, CORM_EINVAL, CORM_ELIMIT, CORM_ECUDA, CORM_ENOMEM, CORM_EDEVICE = 0, -1
 F_WRAP32, F_WEIGHT_LOGICAL, F_ACT_RELU, F_ACT_RELU6 = 0x1, 0x2, 0x4, 0x8
 
 # every symbol include/cormorant_b200.h declares
-EXPORTS = ("corm_vectorop", "corm_matmul_workspace_size", "corm_matmul", "corm_conv_workspace_size", "corm_conv",
+EXPORTS = ("corm_vectorop", "corm_matmul_workspace_size", "corm_matmul", "corm_matmul_noalloc", "corm_conv_workspace_size", "corm_conv",
            "corm_pool", "corm_rowops", "corm_act_table", "corm_smx_table", "corm_rowops_table_image",
            "corm_bind_device", "corm_device_status", "corm_launch_count", "corm_profile_enable",
            "corm_profile_read", "corm_version", "corm_last_error")
@@ -85,6 +85,7 @@ def lib() -> C.CDLL:
     L = C.CDLL(LIB_PATH)
     for name, argt in (("corm_vectorop", [C.POINTER(VectorOpDesc), C.c_void_p]),
                        ("corm_matmul", [C.POINTER(MatmulDesc), C.c_void_p]),
+                       ("corm_matmul_noalloc", [C.POINTER(MatmulDesc), C.c_void_p]),
                        ("corm_matmul_workspace_size", [C.POINTER(MatmulDesc), C.POINTER(C.c_size_t)]),
                        ("corm_conv", [C.POINTER(ConvDesc), C.c_void_p]),
                        ("corm_conv_workspace_size", [C.POINTER(ConvDesc), C.POINTER(C.c_size_t)]),

@@ -399,7 +399,7 @@ size_t gemm_partial_bytes(uint32_t rows, uint32_t cols, uint32_t Kp, uint32_t ba
 int gemm_i8x4(const GemmJob& j, cudaStream_t stream) {
   if (j.Kp % 16 || j.Kp == 0 || j.Kp > kGemmMaxK + 128)
     return fail(CORM_ELIMIT, "gemm: K %u outside 1..%u", j.Kp, kGemmMaxK);
-  int* err = device_error_word();
+  int* err = j.err ? j.err : device_error_word();
   if (!err) return fail(CORM_ECUDA, "gemm: error word allocation failed");
   CUtensorMap m_ahi, m_alo, m_bhi, m_blo;
   bool ok = make_map(&m_ahi, j.a_hi, j.Kp, j.rows, j.a_planes) && make_map(&m_alo, j.a_lo, j.Kp, j.rows, j.a_planes);

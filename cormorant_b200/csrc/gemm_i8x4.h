@@ -37,6 +37,7 @@ struct GemmJob {
   uint64_t img_stride;      // mode 1: elements per image (out_ch * P)
   const int16_t* bias;      // mode 1 bias per column (raw), or nullptr
   uint32_t flags;           // CORM_F_WRAP32 | CORM_F_ACT_RELU | CORM_F_ACT_RELU6
+  int* err;                 // status word for the bounded waits; nullptr: the library's per-device word
 };
 
 constexpr uint32_t kGemmMaxK = 32768;

@@ -13,6 +13,8 @@
 // and keeps 2 columns x n rows of int64 sums per thread, splitting K across
 // CTAs (exact integer atomics) when the output alone is too small to fill
 // the GPU.
+#include <mutex>
+
 #include "corm_common.cuh"
 #include "gemm_i8x4.h"
 
@@ -288,5 +290,135 @@ extern "C" int corm_matmul(const corm_matmul_desc* d, corm_stream_t stream) {
   j.out_batch_stride = d->c_batch_stride;
   j.ldc = d->m;
   j.flags = d->flags;
+  return corm::gemm_i8x4(j, st);
+}
+
+// ---------------------------------------------------------------- allocation-free variant
+// corm_matmul_noalloc: the same MatMul job for callers that must not allocate
+// device memory once they are running — a generated inference project whose
+// buffers all come from a pool sized at start-up, or a host whose device
+// memory belongs to another allocator — so they can neither pass a workspace
+// of their own nor let the library grow its scratch with cudaMalloc.  Its
+// scratch (the int8 split planes and the K-split partial sums) is the
+// file-scope array below, which every GPU that loads this library holds until
+// the process exits; jobs needing more than kNoAllocBytes are rejected.
+namespace {
+
+constexpr size_t kNoAllocBytes = 64ull << 20;  // 64 MiB per device
+static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocBytes];
+static __device__ int g_noalloc_status;  // the GEMM's bounded waits report here
+
+struct NoAllocDev {
+  uint8_t* scratch = nullptr;
+  int* status = nullptr;
+};
+NoAllocDev g_noalloc[64];
+std::mutex g_noalloc_mu;
+
+// Once per device, with that device current: the device addresses of the
+// file-scope array and status word (host code only ever sees a stand-in for
+// the symbol itself, never a device address).
+int noalloc_setup(NoAllocDev& out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return corm::fail(CORM_ECUDA, "noalloc: no device");
+  std::lock_guard<std::mutex> lk(g_noalloc_mu);
+  NoAllocDev& s = g_noalloc[dev];
+  if (!s.scratch) {
+    void* p = nullptr;
+    void* q = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess) return corm::fail(CORM_ECUDA, "noalloc: cudaGetSymbolAddress(scratch): %s", cudaGetErrorString(e));
+    e = cudaGetSymbolAddress(&q, g_noalloc_status);
+    if (e != cudaSuccess) return corm::fail(CORM_ECUDA, "noalloc: cudaGetSymbolAddress(status): %s", cudaGetErrorString(e));
+    s.status = (int*)q;
+    s.scratch = (uint8_t*)p;
+  }
+  out = s;
+  return CORM_OK;
+}
+
+}  // namespace
+
+extern "C" int corm_matmul_noalloc(const corm_matmul_desc* d, corm_stream_t stream) {
+  if (int rc = validate(d)) return rc;
+  if (int rc = corm::check_device()) return rc;
+  if (d->n == 0 || d->m == 0 || d->batch == 0) return CORM_OK;
+  if (!d->a || !d->b || !d->c) return corm::fail(CORM_EINVAL, "corm_matmul_noalloc: null operand");
+  cudaStream_t st = (cudaStream_t)stream;
+  MmArgs p{d->a, d->b, d->c, d->n, d->k, d->m, d->batch, d->a_batch_stride, d->b_batch_stride, d->c_batch_stride,
+           d->b_packed, d->gemv_kw, d->flags};
+  if (d->k == 0) {
+    for (uint32_t bt = 0; bt < d->batch; bt++)
+      for (uint32_t r = 0; r < d->n; r++)
+        if (cudaMemsetAsync(d->c + (uint64_t)bt * d->c_batch_stride + (uint64_t)r * d->m, 0, (size_t)d->m * 2, st))
+          return corm::cuda_status("corm_matmul_noalloc memset");
+    return CORM_OK;
+  }
+  const Plan pl = plan_of(d);
+  if (pl.bytes > kNoAllocBytes)
+    return corm::fail(CORM_ELIMIT, "corm_matmul_noalloc: the job needs %zu bytes of scratch, beyond the %zu-byte "
+                      "static scratch (use corm_matmul with a workspace)", pl.bytes, kNoAllocBytes);
+  NoAllocDev na;
+  if (int rc = noalloc_setup(na)) return rc;
+  uint8_t* w = na.scratch;
+  if (pl.small) {
+    unsigned long long* partial = pl.ksplit > 1 ? (unsigned long long*)w : nullptr;
+    if (partial && cudaMemsetAsync(partial, 0, pl.bytes, st) != cudaSuccess) return corm::cuda_status("memset");
+    dim3 grid((d->m + 63) / 64, d->batch, pl.ksplit);
+    if (d->n <= 1) {
+      corm::ProfScope prof_("mm_small_kernel<1>", st);
+      mm_small_kernel<1, 8><<<grid, 256, 0, st>>>(p, pl.kchunk, partial);
+    } else {  // n <= kSmallRows
+      corm::ProfScope prof_("mm_small_kernel<4>", st);
+      mm_small_kernel<4, 8><<<grid, 256, 0, st>>>(p, pl.kchunk, partial);
+    }
+    if (int rc = corm::cuda_status("matmul_noalloc small")) return rc;
+    if (partial) {
+      {
+        corm::ProfScope prof_("mm_small_finish", st);
+        mm_small_finish<<<corm_blocks((uint64_t)d->batch * d->n * d->m, 256), 256, 0, st>>>(p, partial);
+      }
+      return corm::cuda_status("matmul_noalloc small finish");
+    }
+    return CORM_OK;
+  }
+  int8_t* a_hi = (int8_t*)w;
+  uint8_t* a_lo = w + pl.a_plane_bytes;
+  int8_t* b_hi = (int8_t*)(w + 2 * pl.a_plane_bytes);
+  uint8_t* b_lo = w + 2 * pl.a_plane_bytes + pl.b_plane_bytes;
+  if (int rc = corm::split_planes(d->a, d->a_batch_stride, pl.a_planes, d->n, d->k, d->k, pl.Kp, a_hi, a_lo, st))
+    return rc;
+  if (!d->b_packed && d->gemv_kw <= 1) {
+    if (int rc = corm::split_planes(d->b, d->b_batch_stride, pl.b_planes, d->k, d->m, d->m, pl.Np, b_hi, b_lo, st))
+      return rc;
+  } else {
+    const uint64_t total = (uint64_t)pl.b_planes * d->k * (pl.Np / 16);
+    {
+      corm::ProfScope prof_("split_b_gather_kernel", st);
+      split_b_gather_kernel<<<corm_blocks(total, 256, 148u * 16u), 256, 0, st>>>(p, pl.b_planes, pl.Np, b_hi, b_lo);
+    }
+    if (int rc = corm::cuda_status("matmul_noalloc split_b")) return rc;
+  }
+  corm::GemmJob j{};
+  j.a_hi = a_hi;
+  j.a_lo = a_lo;
+  j.b_hi = b_hi;
+  j.b_lo = b_lo;
+  j.rows = d->n;
+  j.cols = d->m;
+  j.Kp = pl.Kp;
+  j.batch = d->batch;
+  j.a_planes = pl.a_planes;
+  j.b_planes = pl.b_planes;
+  j.b_mn = 1;
+  j.K = d->k;
+  j.cols_p = pl.Np;
+  j.partial = pl.partial_bytes ? (void*)(w + 2 * pl.a_plane_bytes + 2 * pl.b_plane_bytes) : nullptr;
+  j.mode = 0;
+  j.out = d->c;
+  j.out_batch_stride = d->c_batch_stride;
+  j.ldc = d->m;
+  j.flags = d->flags;
+  j.err = na.status;
   return corm::gemm_i8x4(j, st);
 }

@@ -91,6 +91,21 @@ typedef struct {
 int corm_matmul_workspace_size(const corm_matmul_desc* d, size_t* bytes);
 int corm_matmul(const corm_matmul_desc* d, corm_stream_t stream);
 
+/* The same MatMul job without any device allocation — no counterpart in the
+ * reference.  For callers that must not allocate device memory once running
+ * (a generated project whose buffers all come from a pool sized at start-up,
+ * or a host whose device memory belongs to another allocator): the job's
+ * scratch is a 64 MiB array compiled into the library, which every GPU that
+ * loads the library holds until the process exits.  d->workspace is ignored;
+ * a job needing more than 64 MiB of scratch returns CORM_ELIMIT.  The first
+ * call on a device looks up the array's device address (no allocation); make
+ * that first call before any stream capture.  Every call shares the array and
+ * it keeps the last call's contents (the job rewrites all it reads), so calls
+ * that overlap on the GPU — on different streams, or from several threads —
+ * race; serialise them.  Never calls cudaMalloc, cudaFree or any allocating
+ * library routine. */
+int corm_matmul_noalloc(const corm_matmul_desc* d, corm_stream_t stream);
+
 /* ---------------------------------------------------------------- Conv
  * Replaces XConvkernel_Set_* / XConvkernel_Start (host_emu.py:372-455;
  * kernels/conv_rtl/model/include/ConvKernel.h:229).  y[n][m][oh][ow] =

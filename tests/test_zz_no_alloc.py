@@ -1,0 +1,77 @@
+"""corm_matmul_noalloc — the MatMul entry point for callers that must not
+allocate device memory once running (a project whose buffers all come from a
+pool sized at start-up, or a host whose device memory belongs to another
+allocator).  Its scratch is a fixed array compiled into the library.
+
+Checks, through the C ABI: on two calls in a row with different operands (the
+second call must not see the first call's leftovers in the shared scratch),
+its output equals corm_matmul's bit for bit (the tolerance of every parity
+test here: none) on the tensor-core path and on the small-n path with a K
+split; a job larger than the scratch is rejected with CORM_ELIMIT.  The file
+is named so that pytest collects it last."""
+import ctypes as C
+
+import numpy as np
+import pytest
+
+torch = pytest.importorskip("torch")
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def lib():
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    from cormorant_b200 import _lib
+    L = _lib.lib()
+    assert L.corm_bind_device(torch.cuda.current_device()) == 0
+    return _lib
+
+
+def _desc(_lib, a, b, c, n, k, m, batch, flags=0, ws=None):
+    d = _lib.MatmulDesc(a.data_ptr(), b.data_ptr(), c.data_ptr(), n, k, m, batch, n * k, k * m, n * m, 0, 0, flags,
+                        None, 0)
+    if ws is not None:
+        d.workspace, d.workspace_bytes = ws.data_ptr(), ws.numel()
+    return d
+
+
+def _run_both(_lib, n, k, m, batch, seed, flags=0):
+    L = _lib.lib()
+    g = torch.Generator(device="cuda")
+    g.manual_seed(seed)
+    a = torch.randint(-32768, 32768, (batch * n * k,), dtype=torch.int16, device="cuda", generator=g)
+    b = torch.randint(-32768, 32768, (batch * k * m,), dtype=torch.int16, device="cuda", generator=g)
+    ref = torch.full((batch * n * m,), -1, dtype=torch.int16, device="cuda")
+    out = torch.full((batch * n * m,), -2, dtype=torch.int16, device="cuda")
+    need = C.c_size_t(0)
+    dr = _desc(_lib, a, b, ref, n, k, m, batch, flags)
+    assert L.corm_matmul_workspace_size(C.byref(dr), C.byref(need)) == 0
+    ws = torch.empty(max(need.value, 256), dtype=torch.uint8, device="cuda")
+    dr = _desc(_lib, a, b, ref, n, k, m, batch, flags, ws)
+    stream = torch.cuda.current_stream().cuda_stream
+    assert L.corm_matmul(C.byref(dr), stream) == 0, L.corm_last_error()
+    dn = _desc(_lib, a, b, out, n, k, m, batch, flags)
+    assert L.corm_matmul_noalloc(C.byref(dn), stream) == 0, L.corm_last_error()
+    torch.cuda.synchronize()
+    return ref.cpu().numpy(), out.cpu().numpy()
+
+
+@pytest.mark.parametrize("shape", [(200, 640, 384, 2), (1, 4096, 96, 1), (7, 1000, 130, 3)],
+                         ids=["tensor_path", "small_n_ksplit", "tensor_ksplit"])
+def test_noalloc_matches_matmul_twice(lib, shape):
+    n, k, m, batch = shape
+    for call, seed in enumerate((11, 12)):
+        ref, out = _run_both(lib, n, k, m, batch, seed, flags=call & 1)
+        assert np.array_equal(out, ref), f"call {call + 1}"
+
+
+def test_noalloc_rejects_oversized(lib):
+    L = lib.lib()
+    a = torch.zeros(8, dtype=torch.int16, device="cuda")
+    d = lib.MatmulDesc(a.data_ptr(), a.data_ptr(), a.data_ptr(), 4096, 4096, 4096, 4, 4096 * 4096, 4096 * 4096,
+                       4096 * 4096, 0, 0, 0, None, 0)
+    rc = L.corm_matmul_noalloc(C.byref(d), torch.cuda.current_stream().cuda_stream)
+    assert rc == lib.CORM_ELIMIT
+    assert b"static scratch" in L.corm_last_error()
