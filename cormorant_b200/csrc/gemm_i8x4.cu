@@ -279,38 +279,49 @@ __global__ void __launch_bounds__(256) gemm_finish_kernel(const EpiArgs ep) {
   }
 }
 
-// ---------------------------------------------------------------- split kernel
+// ---------------------------------------------------------------- split kernels
 // dst (b, r, kk) <- src[b*bs + r*ld + kk]; 16 consecutive kk per thread, two
 // 16-byte loads when the row is 16-byte aligned, 16-byte stores to each plane.
-__global__ void __launch_bounds__(256) split_rows_kernel(const int16_t* __restrict__ src, uint64_t bs, uint32_t rows,
-                                                         uint64_t ld, uint32_t K, uint32_t Kp, uint64_t total16,
-                                                         int8_t* __restrict__ hi, uint8_t* __restrict__ lo) {
-  const uint32_t per_row = Kp / 16;
-  for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total16; i += (uint64_t)gridDim.x * blockDim.x) {
-    const uint64_t row = i / per_row;  // b * rows + r
-    const uint32_t k0 = (uint32_t)(i - row * per_row) * 16;
-    const uint64_t b = row / rows, r = row - b * rows;
-    const int16_t* s = src + b * bs + r * ld + k0;
-    alignas(16) int16_t v[16];
-    if (k0 + 16 <= K && ((uintptr_t)s & 15) == 0) {
-      *(int4*)v = __ldg((const int4*)s);
-      *(int4*)(v + 8) = __ldg((const int4*)(s + 8));
-    } else {
+__device__ __forceinline__ void split16(const SplitSeg& g, uint64_t i) {
+  const uint32_t per_row = g.Kp / 16;
+  const uint64_t row = i / per_row;  // b * rows + r
+  const uint32_t k0 = (uint32_t)(i - row * per_row) * 16;
+  const uint64_t b = row / g.rows, r = row - b * g.rows;
+  const int16_t* s = g.src + b * g.src_bs + r * g.ld + k0;
+  alignas(16) int16_t v[16];
+  if (k0 + 16 <= g.K && ((uintptr_t)s & 15) == 0) {
+    *(int4*)v = __ldg((const int4*)s);
+    *(int4*)(v + 8) = __ldg((const int4*)(s + 8));
+  } else {
 #pragma unroll
-      for (int j = 0; j < 16; j++) v[j] = (k0 + j < K) ? __ldg(s + j) : (int16_t)0;
+    for (int j = 0; j < 16; j++) v[j] = (k0 + j < g.K) ? __ldg(s + j) : (int16_t)0;
+  }
+  uint32_t h[4], l[4];
+#pragma unroll
+  for (int w = 0; w < 4; w++) {
+    h[w] = l[w] = 0;
+#pragma unroll
+    for (int e = 0; e < 4; e++) {
+      h[w] |= (uint32_t)(uint8_t)(v[4 * w + e] >> 8) << (8 * e);
+      l[w] |= (uint32_t)(uint8_t)(v[4 * w + e] & 0xFF) << (8 * e);
     }
-    uint32_t h[4], l[4];
-#pragma unroll
-    for (int w = 0; w < 4; w++) {
-      h[w] = l[w] = 0;
-#pragma unroll
-      for (int e = 0; e < 4; e++) {
-        h[w] |= (uint32_t)(uint8_t)(v[4 * w + e] >> 8) << (8 * e);
-        l[w] |= (uint32_t)(uint8_t)(v[4 * w + e] & 0xFF) << (8 * e);
-      }
-    }
-    *(int4*)(hi + row * Kp + k0) = make_int4((int)h[0], (int)h[1], (int)h[2], (int)h[3]);
-    *(int4*)(lo + row * Kp + k0) = make_int4((int)l[0], (int)l[1], (int)l[2], (int)l[3]);
+  }
+  *(int4*)(g.hi + row * g.Kp + k0) = make_int4((int)h[0], (int)h[1], (int)h[2], (int)h[3]);
+  *(int4*)(g.lo + row * g.Kp + k0) = make_int4((int)l[0], (int)l[1], (int)l[2], (int)l[3]);
+}
+
+__global__ void __launch_bounds__(256) split_rows_kernel(const SplitSeg g, uint64_t total16) {
+  for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total16; i += (uint64_t)gridDim.x * blockDim.x)
+    split16(g, i);
+}
+
+__global__ void __launch_bounds__(256) split2_rows_kernel(const SplitSeg ga, uint64_t na, const SplitSeg gb,
+                                                          uint64_t nb) {
+  for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < na + nb; i += (uint64_t)gridDim.x * blockDim.x) {
+    if (i < na)
+      split16(ga, i);
+    else
+      split16(gb, i - na);
   }
 }
 
@@ -381,14 +392,24 @@ int* device_error_word() {
 
 int split_planes(const int16_t* src, uint64_t src_bs, uint32_t planes, uint32_t rows, uint64_t ld, uint32_t K,
                  uint32_t Kp, int8_t* hi, uint8_t* lo, cudaStream_t stream) {
+  const SplitSeg g{src, src_bs, planes, rows, ld, K, Kp, hi, lo};
   const uint64_t total16 = (uint64_t)planes * rows * (Kp / 16);
   if (total16 == 0) return CORM_OK;
   {
-    corm::ProfScope prof_("split_rows_kernel", stream);
-    split_rows_kernel<<<corm_blocks(total16, 256, 148u * 16u), 256, 0, stream>>>(src, src_bs, rows, ld, K, Kp, total16, hi,
-                                                                              lo);
+    ProfScope prof_("split_rows_kernel", stream);
+    split_rows_kernel<<<corm_blocks(total16, 256, 148u * 16u), 256, 0, stream>>>(g, total16);
   }
   return cuda_status("split_planes");
+}
+
+int split_planes2(const SplitSeg& a, const SplitSeg& b, cudaStream_t stream) {
+  const uint64_t na = (uint64_t)a.planes * a.rows * (a.Kp / 16), nb = (uint64_t)b.planes * b.rows * (b.Kp / 16);
+  if (na + nb == 0) return CORM_OK;
+  {
+    ProfScope prof_("split2_rows_kernel", stream);
+    split2_rows_kernel<<<corm_blocks(na + nb, 256, 148u * 16u), 256, 0, stream>>>(a, na, b, nb);
+  }
+  return cuda_status("split_planes2");
 }
 
 size_t gemm_partial_bytes(uint32_t rows, uint32_t cols, uint32_t Kp, uint32_t batch) {

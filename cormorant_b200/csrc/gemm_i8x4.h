@@ -53,6 +53,18 @@ size_t gemm_partial_bytes(uint32_t rows, uint32_t cols, uint32_t Kp, uint32_t ba
 int split_planes(const int16_t* src, uint64_t src_bs, uint32_t planes, uint32_t rows, uint64_t ld, uint32_t K,
                  uint32_t Kp, int8_t* hi, uint8_t* lo, cudaStream_t stream);
 
+// Two such splits (A and B of one job) in a single launch.
+struct SplitSeg {
+  const int16_t* src;
+  uint64_t src_bs;
+  uint32_t planes, rows;
+  uint64_t ld;
+  uint32_t K, Kp;
+  int8_t* hi;
+  uint8_t* lo;
+};
+int split_planes2(const SplitSeg& a, const SplitSeg& b, cudaStream_t stream);
+
 // Per-device word the kernels' bounded waits write on a timeout.
 int* device_error_word();
 

@@ -10,9 +10,9 @@
 // lies, MN-major) and multiplied on the tensor cores (gemm_i8x4.cu); the TMA
 // fills the rows of a 128-row tile beyond n with zeros.
 // n <= 2 rows (GEMV, HBM-bound on B): a CUDA-core kernel reads int16 B once
-// and keeps 2 columns x n rows of int64 sums per thread, splitting K across
-// CTAs (exact integer atomics) when the output alone is too small to fill
-// the GPU.
+// with 16-byte loads, 8 columns x n rows of int64 sums per lane, splitting K
+// across CTAs (exact integer atomics) when the output alone is too small to
+// fill the GPU.
 #include <mutex>
 
 #include "corm_common.cuh"
@@ -77,71 +77,64 @@ __global__ void __launch_bounds__(256) split_b_gather_kernel(MmArgs p, uint32_t 
   }
 }
 
-// Small-n path (GEMV-like, HBM-bound on B): a CTA covers 64 columns; lane =
-// 2 adjacent columns of a B row (a warp reads 128 contiguous bytes per row);
-// the KW warps split K (interleaved rows), sum in shared memory, and the CTA
-// writes the result or (K split across CTAs) adds it to int64 partials with
-// exact integer atomics.  NR rows x 2 columns of int64 sums per thread.
-template <int NR, int KW>
-__global__ void __launch_bounds__(32 * KW) mm_small_kernel(MmArgs p, uint32_t kchunk, unsigned long long* partial) {
-  __shared__ int16_t As[NR][256];
-  __shared__ long long red[KW][NR][64];
+// GEMV path (n <= 2, HBM-bound on B): a warp owns 256 consecutive columns —
+// 8 per lane, one 16-byte load per B row — over a K range, A values read as
+// warp-wide broadcasts, int64 sums; the K range is split across CTAs (exact
+// integer atomics into int64 partials) when the grid alone would not fill
+// the GPU.
+template <int NR>
+__global__ void __launch_bounds__(128) mm_gemv_kernel(MmArgs p, uint32_t kchunk, unsigned long long* partial) {
   const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  const uint32_t j0 = (blockIdx.x * 4 + w) * 256 + lane * 8;
   const uint32_t bt = blockIdx.y;
-  const uint32_t j = blockIdx.x * 64 + lane * 2;
   const uint32_t k_lo = blockIdx.z * kchunk, k_hi = min(p.k, k_lo + kchunk);
   const int16_t* A = p.a + (uint64_t)bt * p.a_bs;
   const int16_t* B = p.b + (uint64_t)bt * p.b_bs;
-  int64_t acc[NR][2];
+  if (j0 >= p.m) return;
+  int64_t acc[NR][8];
 #pragma unroll
-  for (int r = 0; r < NR; r++) acc[r][0] = acc[r][1] = 0;
-  const bool vec = p.kw <= 1 && !p.packed && (p.m % 2 == 0) && (((uintptr_t)B & 3) == 0);
-  const bool live = j < p.m;
-  for (uint32_t kb = k_lo; kb < k_hi; kb += 256) {
-    const uint32_t kn = min(256u, k_hi - kb);
-    __syncthreads();
-    for (uint32_t t = threadIdx.x; t < NR * 256; t += 32 * KW) {
-      const uint32_t r = t / 256, kk = t % 256;
-      As[r][kk] = (r < p.n && kk < kn) ? __ldg(A + (uint64_t)r * p.k + kb + kk) : (int16_t)0;
-    }
-    __syncthreads();
-    if (!live) continue;
+  for (int r = 0; r < NR; r++)
+#pragma unroll
+    for (int e = 0; e < 8; e++) acc[r][e] = 0;
+  const bool vec = p.kw <= 1 && !p.packed && (p.m % 8 == 0) && (((uintptr_t)B & 15) == 0) && j0 + 8 <= p.m;
+  if (vec) {
 #pragma unroll 4
-    for (uint32_t kk = w; kk < kn; kk += KW) {
-      int32_t b0, b1;
-      if (vec) {
-        const uint32_t v = __ldg((const uint32_t*)(B + (uint64_t)(kb + kk) * p.m + j));
-        b0 = (int16_t)(v & 0xFFFF);
-        b1 = (j + 1 < p.m) ? (int16_t)(v >> 16) : 0;
-      } else {
-        b0 = __ldg(B + b_offset(kb + kk, j, p.k, p.m, p.packed, p.kw));
-        b1 = (j + 1 < p.m) ? __ldg(B + b_offset(kb + kk, j + 1, p.k, p.m, p.packed, p.kw)) : 0;
-      }
+    for (uint32_t kk = k_lo; kk < k_hi; kk++) {
+      alignas(16) int16_t bv[8];
+      *(int4*)bv = __ldg((const int4*)(B + (uint64_t)kk * p.m + j0));
 #pragma unroll
       for (int r = 0; r < NR; r++) {
-        const int32_t a = As[r][kk];
-        acc[r][0] += (int64_t)(a * b0);  // |a b| <= 2^30
-        acc[r][1] += (int64_t)(a * b1);
+        const int32_t a = __ldg(A + (uint64_t)r * p.k + kk);
+#pragma unroll
+        for (int e = 0; e < 8; e++) acc[r][e] += (int64_t)(a * (int32_t)bv[e]);  // |a b| <= 2^30
+      }
+    }
+  } else {
+    for (uint32_t kk = k_lo; kk < k_hi; kk++) {
+      int32_t bv[8];
+#pragma unroll
+      for (int e = 0; e < 8; e++)
+        bv[e] = (j0 + e < p.m) ? __ldg(B + b_offset(kk, j0 + e, p.k, p.m, p.packed, p.kw)) : 0;
+#pragma unroll
+      for (int r = 0; r < NR; r++) {
+        const int32_t a = __ldg(A + (uint64_t)r * p.k + kk);
+#pragma unroll
+        for (int e = 0; e < 8; e++) acc[r][e] += (int64_t)(a * bv[e]);
       }
     }
   }
 #pragma unroll
   for (int r = 0; r < NR; r++) {
-    red[w][r][lane * 2] = acc[r][0];
-    red[w][r][lane * 2 + 1] = acc[r][1];
-  }
-  __syncthreads();
-  for (uint32_t t = threadIdx.x; t < NR * 64; t += 32 * KW) {
-    const uint32_t r = t / 64, c = t % 64, jj = blockIdx.x * 64 + c;
-    if (r >= p.n || jj >= p.m) continue;
-    long long s = 0;
+    if (r >= (int)p.n) continue;
 #pragma unroll
-    for (int q = 0; q < KW; q++) s += red[q][r][c];
-    const uint64_t o = (uint64_t)bt * p.n * p.m + (uint64_t)r * p.m + jj;
-    if (partial)
-      atomicAdd(partial + o, (unsigned long long)s);
-    else
-      p.c[(uint64_t)bt * p.c_bs + (uint64_t)r * p.m + jj] = mm_finish(s, p.flags);
+    for (int e = 0; e < 8; e++) {
+      const uint32_t jj = j0 + e;
+      if (jj >= p.m) continue;
+      if (partial)
+        atomicAdd(partial + (uint64_t)bt * p.n * p.m + (uint64_t)r * p.m + jj, (unsigned long long)acc[r][e]);
+      else
+        p.c[(uint64_t)bt * p.c_bs + (uint64_t)r * p.m + jj] = mm_finish(acc[r][e], p.flags);
+    }
   }
 }
 
@@ -163,11 +156,10 @@ Plan plan_of(const corm_matmul_desc* d) {
   Plan pl{};
   pl.small = d->n <= kSmallRows;
   if (pl.small) {
-    const uint64_t blocks = (uint64_t)((d->m + 63) / 64) * d->batch;
+    const uint64_t blocks = (uint64_t)((d->m + 1023) / 1024) * d->batch;
     uint32_t ks = 1;
-    while (blocks * ks < 4 * 148 && d->k / (ks * 2) >= 256) ks *= 2;
-    pl.ksplit = ks;
-    pl.kchunk = ((d->k + ks - 1) / ks + 255) / 256 * 256;
+    while (blocks * ks < 4 * 148 && d->k / (ks * 2) >= 128) ks *= 2;
+    pl.kchunk = (d->k + ks - 1) / ks;
     pl.ksplit = (d->k + pl.kchunk - 1) / pl.kchunk;
     ks = pl.ksplit;
     pl.bytes = ks > 1 ? (size_t)d->batch * d->n * d->m * 8 : 0;
@@ -227,19 +219,13 @@ extern "C" int corm_matmul(const corm_matmul_desc* d, corm_stream_t stream) {
   if (pl.small) {
     unsigned long long* partial = pl.ksplit > 1 ? (unsigned long long*)ws : nullptr;
     if (partial && cudaMemsetAsync(partial, 0, pl.bytes, st) != cudaSuccess) return corm::cuda_status("memset");
-    dim3 grid((d->m + 63) / 64, d->batch, pl.ksplit);
+    dim3 grid((d->m + 1023) / 1024, d->batch, pl.ksplit);
     if (d->n <= 1) {
-      corm::ProfScope prof_("mm_small_kernel<1>", st);
-      mm_small_kernel<1, 8><<<grid, 256, 0, st>>>(p, pl.kchunk, partial);
-    } else if (d->n <= 4) {
-      corm::ProfScope prof_("mm_small_kernel<4>", st);
-      mm_small_kernel<4, 8><<<grid, 256, 0, st>>>(p, pl.kchunk, partial);
-    } else if (d->n <= 8) {
-      corm::ProfScope prof_("mm_small_kernel<8>", st);
-      mm_small_kernel<8, 8><<<grid, 256, 0, st>>>(p, pl.kchunk, partial);
-    } else {
-      corm::ProfScope prof_("mm_small_kernel<16>", st);
-      mm_small_kernel<16, 4><<<grid, 128, 0, st>>>(p, pl.kchunk, partial);
+      corm::ProfScope prof_("mm_gemv_kernel<1>", st);
+      mm_gemv_kernel<1><<<grid, 128, 0, st>>>(p, pl.kchunk, partial);
+    } else {  // n <= kSmallRows
+      corm::ProfScope prof_("mm_gemv_kernel<2>", st);
+      mm_gemv_kernel<2><<<grid, 128, 0, st>>>(p, pl.kchunk, partial);
     }
     if (int rc = corm::cuda_status("matmul small")) return rc;
     if (partial) {
@@ -256,13 +242,15 @@ extern "C" int corm_matmul(const corm_matmul_desc* d, corm_stream_t stream) {
   uint8_t* a_lo = w + pl.a_plane_bytes;
   int8_t* b_hi = (int8_t*)(w + 2 * pl.a_plane_bytes);
   uint8_t* b_lo = w + 2 * pl.a_plane_bytes + pl.b_plane_bytes;
-  if (int rc = corm::split_planes(d->a, d->a_batch_stride, pl.a_planes, d->n, d->k, d->k, pl.Kp, a_hi, a_lo, st))
-    return rc;
   if (!d->b_packed && d->gemv_kw <= 1) {
-    // row-major B is already MN-major: an elementwise split, rows of m padded to Np
-    if (int rc = corm::split_planes(d->b, d->b_batch_stride, pl.b_planes, d->k, d->m, d->m, pl.Np, b_hi, b_lo, st))
-      return rc;
+    // row-major B is already MN-major: both operands split elementwise in one
+    // launch (B rows of m padded to Np)
+    const corm::SplitSeg sa{d->a, d->a_batch_stride, pl.a_planes, d->n, d->k, d->k, pl.Kp, a_hi, a_lo};
+    const corm::SplitSeg sb{d->b, d->b_batch_stride, pl.b_planes, d->k, d->m, d->m, pl.Np, b_hi, b_lo};
+    if (int rc = corm::split_planes2(sa, sb, st)) return rc;
   } else {
+    if (int rc = corm::split_planes(d->a, d->a_batch_stride, pl.a_planes, d->n, d->k, d->k, pl.Kp, a_hi, a_lo, st))
+      return rc;
     const uint64_t total = (uint64_t)pl.b_planes * d->k * (pl.Np / 16);
     {
       corm::ProfScope prof_("split_b_gather_kernel", st);
@@ -364,13 +352,13 @@ extern "C" int corm_matmul_noalloc(const corm_matmul_desc* d, corm_stream_t stre
   if (pl.small) {
     unsigned long long* partial = pl.ksplit > 1 ? (unsigned long long*)w : nullptr;
     if (partial && cudaMemsetAsync(partial, 0, pl.bytes, st) != cudaSuccess) return corm::cuda_status("memset");
-    dim3 grid((d->m + 63) / 64, d->batch, pl.ksplit);
+    dim3 grid((d->m + 1023) / 1024, d->batch, pl.ksplit);
     if (d->n <= 1) {
-      corm::ProfScope prof_("mm_small_kernel<1>", st);
-      mm_small_kernel<1, 8><<<grid, 256, 0, st>>>(p, pl.kchunk, partial);
+      corm::ProfScope prof_("mm_gemv_kernel<1>", st);
+      mm_gemv_kernel<1><<<grid, 128, 0, st>>>(p, pl.kchunk, partial);
     } else {  // n <= kSmallRows
-      corm::ProfScope prof_("mm_small_kernel<4>", st);
-      mm_small_kernel<4, 8><<<grid, 256, 0, st>>>(p, pl.kchunk, partial);
+      corm::ProfScope prof_("mm_gemv_kernel<2>", st);
+      mm_gemv_kernel<2><<<grid, 128, 0, st>>>(p, pl.kchunk, partial);
     }
     if (int rc = corm::cuda_status("matmul_noalloc small")) return rc;
     if (partial) {
@@ -386,12 +374,13 @@ extern "C" int corm_matmul_noalloc(const corm_matmul_desc* d, corm_stream_t stre
   uint8_t* a_lo = w + pl.a_plane_bytes;
   int8_t* b_hi = (int8_t*)(w + 2 * pl.a_plane_bytes);
   uint8_t* b_lo = w + 2 * pl.a_plane_bytes + pl.b_plane_bytes;
-  if (int rc = corm::split_planes(d->a, d->a_batch_stride, pl.a_planes, d->n, d->k, d->k, pl.Kp, a_hi, a_lo, st))
-    return rc;
   if (!d->b_packed && d->gemv_kw <= 1) {
-    if (int rc = corm::split_planes(d->b, d->b_batch_stride, pl.b_planes, d->k, d->m, d->m, pl.Np, b_hi, b_lo, st))
-      return rc;
+    const corm::SplitSeg sa{d->a, d->a_batch_stride, pl.a_planes, d->n, d->k, d->k, pl.Kp, a_hi, a_lo};
+    const corm::SplitSeg sb{d->b, d->b_batch_stride, pl.b_planes, d->k, d->m, d->m, pl.Np, b_hi, b_lo};
+    if (int rc = corm::split_planes2(sa, sb, st)) return rc;
   } else {
+    if (int rc = corm::split_planes(d->a, d->a_batch_stride, pl.a_planes, d->n, d->k, d->k, pl.Kp, a_hi, a_lo, st))
+      return rc;
     const uint64_t total = (uint64_t)pl.b_planes * d->k * (pl.Np / 16);
     {
       corm::ProfScope prof_("split_b_gather_kernel", st);
