@@ -307,7 +307,15 @@ def main():
             ops.profile_enable(False)
         with open(args.detail, "w") as fh:
             json.dump(per, fh, indent=1)
-    tensor_macs = sum(b * m * k * n for b, m, k, n in problems if m > 16)
+    tensor_probs = [(b, m, k, n) for b, m, k, n in problems if m > 2]
+    tensor_macs = sum(b * m * k * n for b, m, k, n in tensor_probs)
+    # DRAM traffic of the GEMM kernel: one ncu capture of the 4 x 2048 x 4096 x 4096
+    # case (profiles/gemm_i8x4_kernel_matmul_4x2048x4096x4096.md) read 201.43 MB and
+    # wrote 52.52 MB per launch against 268.4 MB of algorithmic bytes (int8 planes of A
+    # and B read once, int16 C written); scaled to the sweep's average launch by its
+    # algorithmic bytes.
+    alg_bytes = sum(b * (2 * m * k + 2 * k * n + 2 * m * n) for b, m, k, n in tensor_probs)
+    ncu_ratio = (201.43e6 + 52.52e6) / 268.4e6
     g_launches, g_ms, _ = prof.get("gemm_i8x4_kernel", (0, 0.0, 0.0))
     peak, peak_src = measure_int8_peak(torch, dev)
     achieved = 8 * tensor_macs / (g_ms * 1e-3) / 1e12 if g_ms else None
@@ -350,8 +358,12 @@ def main():
             "gpu_launches": int(launches_per_step * args.steps),
             "roofline": {"bound": "tensor", "kernel": "gemm_i8x4_kernel", "achieved": round(achieved, 1) if achieved else None,
                          "peak": round(peak, 1), "unit": "TFLOP/s", "frac": round(achieved / peak, 4) if achieved else None,
-                         "traffic": None, "peak_source": peak_src,
-                         "work": "8 int8 tensor ops per int16 MAC (4 int8 products); tensor-path problems only (M > 16)",
+                         "traffic": round(ncu_ratio * alg_bytes / max(g_launches, 1)),
+                         "traffic_note": "bytes per GEMM launch: sweep average of algorithmic bytes (int8 planes + "
+                                         "int16 C) x the DRAM/algorithmic ratio of one ncu capture (%.3f, "
+                                         "4x2048x4096x4096)" % ncu_ratio,
+                         "peak_source": peak_src,
+                         "work": "8 int8 tensor ops per int16 MAC (4 int8 products); tensor-path problems (M > 2)",
                          "gemm_launches_per_step": g_launches, "gemm_ms_per_step": round(g_ms, 4),
                          "all_kernels_ms_per_step": round(step_kernel_ms, 4),
                          "kernels": {k: {"launches": v[0], "ms": round(v[1], 4)} for k, v in sorted(prof.items())}},

@@ -156,9 +156,11 @@ Plan plan_of(const corm_matmul_desc* d) {
   Plan pl{};
   pl.small = d->n <= kSmallRows;
   if (pl.small) {
+    // enough CTAs for several waves: split K down to chunks of 16 rows (a
+    // warp's serial chain of loads is then short)
     const uint64_t blocks = (uint64_t)((d->m + 1023) / 1024) * d->batch;
     uint32_t ks = 1;
-    while (blocks * ks < 4 * 148 && d->k / (ks * 2) >= 128) ks *= 2;
+    while (blocks * ks < 8 * 148 && d->k / (ks * 2) >= 16) ks *= 2;
     pl.kchunk = (d->k + ks - 1) / ks;
     pl.ksplit = (d->k + pl.kchunk - 1) / pl.kchunk;
     ks = pl.ksplit;

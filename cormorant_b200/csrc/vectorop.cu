@@ -46,10 +46,11 @@ __device__ __forceinline__ int32_t vop_act(int32_t r, uint32_t act, uint32_t alp
 
 __device__ __forceinline__ int32_t sat16i(int32_t v) { return v > 32767 ? 32767 : (v < -32768 ? -32768 : v); }
 
-template <bool BINARY>
+// OP and ACT are template parameters: the per-lane work is straight-line code.
+template <int OP, int ACT>
 __global__ void __launch_bounds__(256) vop_elementwise(VopArgs p) {
+  constexpr bool BINARY = OP <= 3;
   const uint64_t words = (uint64_t)p.outer * p.nw;
-  const uint32_t jact = (p.op >= 6 && p.op <= 9) ? p.op - 3 : p.act;
   for (uint64_t w = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; w < words; w += (uint64_t)gridDim.x * blockDim.x) {
     const uint32_t o = (uint32_t)(w / p.nw), j = (uint32_t)(w % p.nw);
     const uint32_t i0 = j * 8;
@@ -60,7 +61,7 @@ __global__ void __launch_bounds__(256) vop_elementwise(VopArgs p) {
     // rows written in order on the hardware: a tail lane of row o survives only
     // where row o + 1's data does not land (lane index < c_inc), or in the last row
     const uint32_t lim = (o + 1 == p.outer) ? p.nw * 8 : min(p.nw * 8, max(p.c_inc, p.size));
-    int16_t xa[8], xb[8], out[8];
+    alignas(16) int16_t xa[8], xb[8], out[8];
     if (lanes == 8 && ((uintptr_t)ar & 15) == 0) {
       *(int4*)xa = __ldg((const int4*)ar);
     } else {
@@ -77,8 +78,8 @@ __global__ void __launch_bounds__(256) vop_elementwise(VopArgs p) {
     }
 #pragma unroll
     for (int l = 0; l < 8; l++) {
-      int32_t r = sat16i(vop_alu(xa[l], BINARY ? xb[l] : 0, p.op));
-      r = vop_act(r, jact, p.alpha, p.table);
+      int32_t r = sat16i(vop_alu(xa[l], BINARY ? xb[l] : 0, OP));
+      r = vop_act(r, ACT, p.alpha, p.table);
       out[l] = l < (int)lanes ? (int16_t)r : (int16_t)0;
     }
     if (i0 + 8 <= lim && ((uintptr_t)cr & 15) == 0) {
@@ -88,6 +89,35 @@ __global__ void __launch_bounds__(256) vop_elementwise(VopArgs p) {
       for (int l = 0; l < 8; l++)
         if (i0 + l < lim) cr[l] = out[l];
     }
+  }
+}
+
+template <int OP>
+void launch_vop_act(const VopArgs& p, uint32_t jact, unsigned blocks, cudaStream_t st) {
+  switch (jact) {
+    case 0: vop_elementwise<OP, 0><<<blocks, 256, 0, st>>>(p); break;
+    case 1: vop_elementwise<OP, 1><<<blocks, 256, 0, st>>>(p); break;
+    case 2: vop_elementwise<OP, 2><<<blocks, 256, 0, st>>>(p); break;
+    case 3: vop_elementwise<OP, 3><<<blocks, 256, 0, st>>>(p); break;
+    case 4: vop_elementwise<OP, 4><<<blocks, 256, 0, st>>>(p); break;
+    case 5: vop_elementwise<OP, 5><<<blocks, 256, 0, st>>>(p); break;
+    default: vop_elementwise<OP, 6><<<blocks, 256, 0, st>>>(p); break;
+  }
+}
+
+void launch_vop(const VopArgs& p, uint32_t op, uint32_t jact, unsigned blocks, cudaStream_t st) {
+  corm::ProfScope prof_("vop_elementwise", st);
+  switch (op) {
+    case 0: launch_vop_act<0>(p, jact, blocks, st); break;
+    case 1: launch_vop_act<1>(p, jact, blocks, st); break;
+    case 2: launch_vop_act<2>(p, jact, blocks, st); break;
+    case 3: launch_vop_act<3>(p, jact, blocks, st); break;
+    case 4: launch_vop_act<4>(p, jact, blocks, st); break;
+    case 5: launch_vop_act<5>(p, jact, blocks, st); break;
+    case 6: vop_elementwise<6, 3><<<blocks, 256, 0, st>>>(p); break;
+    case 7: vop_elementwise<7, 4><<<blocks, 256, 0, st>>>(p); break;
+    case 8: vop_elementwise<8, 5><<<blocks, 256, 0, st>>>(p); break;
+    default: vop_elementwise<9, 6><<<blocks, 256, 0, st>>>(p); break;
   }
 }
 
@@ -133,10 +163,12 @@ __device__ __forceinline__ int64_t warp_reduce_sum(int64_t v) {
 }
 
 // Row mode, GROUP threads per row (32: a warp per row; 256 / 1024: a CTA per
-// row), PER elements per thread held in registers.
+// row), PER elements per thread held in registers as PER / 8 runs of 8
+// consecutive elements (16-byte loads and stores where the row allows).
 template <int GROUP, int PER>
 __global__ void __launch_bounds__(GROUP >= 256 ? GROUP : 256) smx_rows(SmxArgs p) {
   constexpr int ROWS_PER_CTA = GROUP >= 256 ? 1 : 256 / GROUP;
+  constexpr int V = PER / 8;
   __shared__ int32_t s_max[32];
   __shared__ int64_t s_sum[32];
   const int lane_in_group = threadIdx.x % GROUP;
@@ -145,13 +177,23 @@ __global__ void __launch_bounds__(GROUP >= 256 ? GROUP : 256) smx_rows(SmxArgs p
   const bool live = row < p.rows;
   const uint32_t v = live ? smx_valid(row, p) : 0u;
   const int16_t* x = p.a + (size_t)row * p.a_inc;
+  const bool xa = ((uintptr_t)x & 15) == 0;
   int32_t xv[PER];
   int32_t m = INT32_MIN;
 #pragma unroll
-  for (int t = 0; t < PER; t++) {
-    const uint32_t j = lane_in_group + t * GROUP;
-    xv[t] = (live && j < v) ? (int32_t)x[j] : INT32_MIN;
-    m = max(m, xv[t]);
+  for (int q = 0; q < V; q++) {
+    const uint32_t j0 = (q * GROUP + lane_in_group) * 8;
+    if (live && xa && j0 + 8 <= v) {
+      alignas(16) int16_t t8[8];
+      *(int4*)t8 = __ldg((const int4*)(x + j0));
+#pragma unroll
+      for (int e = 0; e < 8; e++) xv[q * 8 + e] = t8[e];
+    } else {
+#pragma unroll
+      for (int e = 0; e < 8; e++) xv[q * 8 + e] = (live && j0 + e < v) ? (int32_t)x[j0 + e] : INT32_MIN;
+    }
+#pragma unroll
+    for (int e = 0; e < 8; e++) m = max(m, xv[q * 8 + e]);
   }
   m = warp_reduce_max(m);
   if (GROUP > 32) {
@@ -163,7 +205,7 @@ __global__ void __launch_bounds__(GROUP >= 256 ? GROUP : 256) smx_rows(SmxArgs p
   int64_t S = 0;
 #pragma unroll
   for (int t = 0; t < PER; t++) {  // xv becomes e (<= 65536) in place
-    const uint32_t j = lane_in_group + t * GROUP;
+    const uint32_t j = ((t / 8) * GROUP + lane_in_group) * 8 + (t % 8);
     xv[t] = (live && j < v) ? (int32_t)smx_e(m, xv[t], p) : 0;
     S += xv[t];
   }
@@ -178,10 +220,20 @@ __global__ void __launch_bounds__(GROUP >= 256 ? GROUP : 256) smx_rows(SmxArgs p
   const uint64_t R = S > 0 ? (1ull << 40) / (uint64_t)S : 0ull;
   int16_t* out = p.c + (size_t)row * p.b_inc;
   const uint32_t lim = (row + 1 == p.rows) ? p.W : min(p.W, max(p.b_inc, p.size));
+  const bool oa = ((uintptr_t)out & 15) == 0;
 #pragma unroll
-  for (int t = 0; t < PER; t++) {
-    const uint32_t j = lane_in_group + t * GROUP;
-    if (j < lim) out[j] = j < v ? smx_p(xv[t], R, p) : (int16_t)0;
+  for (int q = 0; q < V; q++) {
+    const uint32_t j0 = (q * GROUP + lane_in_group) * 8;
+    alignas(16) int16_t o8[8];
+#pragma unroll
+    for (int e = 0; e < 8; e++) o8[e] = (j0 + e < v) ? smx_p(xv[q * 8 + e], R, p) : (int16_t)0;
+    if (oa && j0 + 8 <= lim) {
+      *(int4*)(out + j0) = *(int4*)o8;
+    } else {
+#pragma unroll
+      for (int e = 0; e < 8; e++)
+        if (j0 + e < lim) out[j0 + e] = o8[e];
+    }
   }
   for (uint32_t j = lane_in_group + PER * GROUP; j < lim; j += GROUP) out[j] = 0;  // tail beyond registers
 }
@@ -324,15 +376,6 @@ extern "C" int corm_vectorop(const corm_vectorop_desc* d, corm_stream_t stream) 
                       d->size);
   const uint64_t words = (uint64_t)p.outer * p.nw;
   const unsigned blocks = corm_blocks(words, 256, 148u * 16u);
-  if (d->op <= 3)
-    {
-      corm::ProfScope prof_("vop_elementwise<true>", st);
-      vop_elementwise<true><<<blocks, 256, 0, st>>>(p);
-    }
-  else
-    {
-      corm::ProfScope prof_("vop_elementwise<false>", st);
-      vop_elementwise<false><<<blocks, 256, 0, st>>>(p);
-    }
+  launch_vop(p, d->op, jact, blocks, st);
   return corm::cuda_status("vectorop");
 }
