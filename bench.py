@@ -188,6 +188,7 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-models", action="store_true", help="skip the MNIST / MobileNetV2 forward passes")
     ap.add_argument("--detail", help="write per-problem kernel times of one profiled step to this JSON file")
     ap.add_argument("--case", choices=["gemm", "gemm_small", "vectorop", "softmax", "conv"],
                     help="run one job a few times (a small case for ncu captures) and exit")
@@ -323,6 +324,7 @@ def main():
 
     # VectorOP and Softmax sweeps of the same config
     sweeps = vector_sweeps(torch, ops, dev, stream, flush, args)
+    models = None if args.no_models else bench_models(torch, dev, stream, flush, args, world, rank, pg)
 
     # verification gather (the only collective): per-rank checksum of the outputs
     chk = torch.zeros(1, dtype=torch.int64, device=dev)
@@ -370,6 +372,8 @@ def main():
             "clocks": clk,
             "sweeps": sweeps,
         }
+        if models:
+            line["models"] = models
         if cpu:
             line["cpu_baseline"] = cpu
         if e2e:
@@ -435,6 +439,51 @@ def vector_sweeps(torch, ops, dev, stream, flush, args):
             t2 = _time_graph(torch, stream, flush, g2, args)
             smx[f"{mode}{n}"] = {"ms": round(t2, 4), "GB/s": round(4 * N / (t2 * 1e-3) / 1e9, 1)}
     out["softmax"] = smx
+    return out
+
+
+def bench_models(torch, dev, stream, flush, args, world, rank, pg):
+    """configs[0] (MNIST CNN) and configs[2] (MobileNetV2-1.0, 224x224, batch 256
+    sharded over the ranks): GpuSimulator forward passes on raw int16 inputs,
+    replayed as CUDA graphs; images/s over all ranks, int16 GMAC/s.  On rank 0 at
+    N = 1 the CPU oracle's forward pass of one image is timed beside it."""
+    from cormorant_b200 import workloads as WL
+    from cormorant_b200.simulator import GpuSimulator
+    out = {}
+    cases = [("mnist_b1", lambda: WL.mnist(seed=1, batch=1)), ("mnist_b4096", lambda: WL.mnist(seed=1, batch=4096)),
+             ("mobilenet_v2_224", lambda: WL.mobilenet_v2(seed=3, batch=max(1, 256 // world), res=224))]
+    for name, build in cases:
+        g, feeds, macs_img = build()
+        batch = g.input_tensors[0].shape[0]
+        sim = GpuSimulator(g, device=dev)
+        with torch.cuda.stream(stream):
+            raw = {"x": sim._to_raw(g.input_tensors[0], feeds["x"])}
+            sim.forward_raw(raw)  # weights uploaded, workspaces sized
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            res, _ = sim.forward_raw(raw)
+        ms = _time_graph(torch, stream, flush, graph, args)
+        if pg:
+            t = torch.tensor([ms], dtype=torch.float64, device=dev)
+            pg.all_reduce(t, op=pg.ReduceOp.MAX)
+            ms = float(t.item())
+        imgs = world * batch / (ms * 1e-3)
+        out[name] = {"batch_per_gpu": batch, "ms_per_batch": round(ms, 4), "images_per_s": round(imgs, 1),
+                     "GMAC/s": round(imgs * macs_img / 1e9, 1), "mmac_per_image": round(macs_img / 1e6, 2),
+                     "nodes": len(g.nodes)}
+        if rank == 0 and world == 1 and not args.no_cpu and name != "mnist_b4096":
+            import numpy as np
+
+            from oracle import graph as og
+            g1, f1, _ = build() if batch == 1 else (WL.mobilenet_v2(seed=3, batch=1, res=224) if "mobilenet" in name
+                                                     else WL.mnist(seed=1, batch=1))
+            t0 = time.perf_counter()
+            og.forward(g1, {k: np.asarray(v) for k, v in f1.items()})
+            el = time.perf_counter() - t0
+            out[name]["cpu_oracle_images_per_s"] = round(1.0 / el, 3)
+        del graph, res, sim
+        torch.cuda.empty_cache()
     return out
 
 

@@ -147,18 +147,20 @@ __device__ __forceinline__ int16_t smx_p(int64_t e, uint64_t R, const SmxArgs& p
   return (int16_t)(q > 32767u ? 32767u : q);
 }
 
-template <typename T>
+// reductions over groups of WIDTH consecutive lanes (WIDTH <= 32, a power of 2)
+template <int WIDTH, typename T>
 __device__ __forceinline__ T warp_reduce_max(T v) {
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) {
+  for (int o = WIDTH / 2; o > 0; o >>= 1) {
     T u = __shfl_xor_sync(0xffffffffu, v, o);
     v = u > v ? u : v;
   }
   return v;
 }
+template <int WIDTH>
 __device__ __forceinline__ int64_t warp_reduce_sum(int64_t v) {
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  for (int o = WIDTH / 2; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
   return v;
 }
 
@@ -195,7 +197,7 @@ __global__ void __launch_bounds__(GROUP >= 256 ? GROUP : 256) smx_rows(SmxArgs p
 #pragma unroll
     for (int e = 0; e < 8; e++) m = max(m, xv[q * 8 + e]);
   }
-  m = warp_reduce_max(m);
+  m = warp_reduce_max<(GROUP < 32 ? GROUP : 32)>(m);
   if (GROUP > 32) {
     if ((threadIdx.x & 31) == 0) s_max[threadIdx.x >> 5] = m;
     __syncthreads();
@@ -209,7 +211,7 @@ __global__ void __launch_bounds__(GROUP >= 256 ? GROUP : 256) smx_rows(SmxArgs p
     xv[t] = (live && j < v) ? (int32_t)smx_e(m, xv[t], p) : 0;
     S += xv[t];
   }
-  S = warp_reduce_sum(S);
+  S = warp_reduce_sum<(GROUP < 32 ? GROUP : 32)>(S);
   if (GROUP > 32) {
     if ((threadIdx.x & 31) == 0) s_sum[threadIdx.x >> 5] = S;
     __syncthreads();
@@ -317,7 +319,10 @@ int launch_softmax(const corm_vectorop_desc* d, cudaStream_t st, const corm::Dev
     }
     return corm::cuda_status("softmax_cols");
   }
-  if (d->size <= 256) {
+  if (d->size <= 128) {
+    corm::ProfScope prof_("smx_rows<16,8>", st);
+    smx_rows<16, 8><<<(p.rows + 15) / 16, 256, 0, st>>>(p);
+  } else if (d->size <= 256) {
     {
       corm::ProfScope prof_("smx_rows<32,8>", st);
       smx_rows<32, 8><<<(p.rows + 7) / 8, 256, 0, st>>>(p);
