@@ -188,7 +188,8 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
-    ap.add_argument("--no-models", action="store_true", help="skip the MNIST / MobileNetV2 forward passes")
+    ap.add_argument("--no-models", action="store_true", help="skip the MNIST / MobileNetV2 / BERT forward passes")
+    ap.add_argument("--models", help="comma list of model cases to run (default: all)")
     ap.add_argument("--detail", help="write per-problem kernel times of one profiled step to this JSON file")
     ap.add_argument("--case", choices=["gemm", "gemm_small", "vectorop", "softmax", "conv"],
                     help="run one job a few times (a small case for ncu captures) and exit")
@@ -443,47 +444,53 @@ def vector_sweeps(torch, ops, dev, stream, flush, args):
 
 
 def bench_models(torch, dev, stream, flush, args, world, rank, pg):
-    """configs[0] (MNIST CNN) and configs[2] (MobileNetV2-1.0, 224x224, batch 256
-    sharded over the ranks): GpuSimulator forward passes on raw int16 inputs,
-    replayed as CUDA graphs; images/s over all ranks, int16 GMAC/s.  On rank 0 at
-    N = 1 the CPU oracle's forward pass of one image is timed beside it."""
+    """configs[0] (MNIST CNN), configs[2] (MobileNetV2-1.0, 224x224, batch 256
+    sharded over the ranks) and configs[3] (BERT-base encoder, 64 sequences of
+    384 tokens sharded over the ranks): GpuSimulator forward passes on raw
+    int16 inputs, replayed as CUDA graphs; images/s or tokens/s over all
+    ranks, int16 GMAC/s.  On rank 0 at N = 1 the CPU oracle's forward pass of
+    one image / one sequence is timed beside it."""
     from cormorant_b200 import workloads as WL
     from cormorant_b200.simulator import GpuSimulator
     out = {}
-    cases = [("mnist_b1", lambda: WL.mnist(seed=1, batch=1)), ("mnist_b4096", lambda: WL.mnist(seed=1, batch=4096)),
-             ("mobilenet_v2_224", lambda: WL.mobilenet_v2(seed=3, batch=max(1, 256 // world), res=224))]
-    for name, build in cases:
-        g, feeds, macs_img = build()
-        batch = g.input_tensors[0].shape[0]
+    cases = [("mnist_b1", "images", lambda b: WL.mnist(seed=1, batch=b), 1),
+             ("mnist_b4096", "images", lambda b: WL.mnist(seed=1, batch=b), 4096),
+             ("mobilenet_v2_224", "images", lambda b: WL.mobilenet_v2(seed=3, batch=b, res=224), max(1, 256 // world)),
+             ("bert_base_384", "tokens", lambda b: WL.bert_base(seed=4, batch=b, seq=384), max(1, 64 // world))]
+    for name, unit, build, batch in cases:
+        if args.models and name not in args.models.split(","):
+            continue
+        g, feeds, macs_unit = build(batch)
+        units = batch * (384 if unit == "tokens" else 1)
         sim = GpuSimulator(g, device=dev)
+        keep = [t.onnx_name for t in g.output_tensors]
         with torch.cuda.stream(stream):
             raw = {"x": sim._to_raw(g.input_tensors[0], feeds["x"])}
-            sim.forward_raw(raw)  # weights uploaded, workspaces sized
+            sim.forward_raw(raw, keep=keep)  # weights uploaded, workspaces sized
         torch.cuda.synchronize()
         graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(graph, stream=stream):
-            res, _ = sim.forward_raw(raw)
+            res, _ = sim.forward_raw(raw, keep=keep)
         ms = _time_graph(torch, stream, flush, graph, args)
         if pg:
             t = torch.tensor([ms], dtype=torch.float64, device=dev)
             pg.all_reduce(t, op=pg.ReduceOp.MAX)
             ms = float(t.item())
-        imgs = world * batch / (ms * 1e-3)
-        out[name] = {"batch_per_gpu": batch, "ms_per_batch": round(ms, 4), "images_per_s": round(imgs, 1),
-                     "GMAC/s": round(imgs * macs_img / 1e9, 1), "mmac_per_image": round(macs_img / 1e6, 2),
+        rate = world * units / (ms * 1e-3)
+        out[name] = {"batch_per_gpu": batch, "ms_per_batch": round(ms, 4), f"{unit}_per_s": round(rate, 1),
+                     "GMAC/s": round(rate * macs_unit / 1e9, 1), f"mmac_per_{unit[:-1]}": round(macs_unit / 1e6, 2),
                      "nodes": len(g.nodes)}
+        del graph, res, sim, raw
+        torch.cuda.empty_cache()
         if rank == 0 and world == 1 and not args.no_cpu and name != "mnist_b4096":
             import numpy as np
 
             from oracle import graph as og
-            g1, f1, _ = build() if batch == 1 else (WL.mobilenet_v2(seed=3, batch=1, res=224) if "mobilenet" in name
-                                                     else WL.mnist(seed=1, batch=1))
+            g1, f1, _ = build(1)
             t0 = time.perf_counter()
             og.forward(g1, {k: np.asarray(v) for k, v in f1.items()})
             el = time.perf_counter() - t0
-            out[name]["cpu_oracle_images_per_s"] = round(1.0 / el, 3)
-        del graph, res, sim
-        torch.cuda.empty_cache()
+            out[name][f"cpu_oracle_{unit}_per_s"] = round((384 if unit == "tokens" else 1) / el, 3)
     return out
 
 

@@ -161,7 +161,7 @@ class GpuSimulator:
         tensor visited (or only ``keep``)."""
         tmap = {t.onnx_name: t for t in self._graph.input_tensors}
         raw_in = {name: self._to_raw(tmap[name], v) for name, v in input_arrays.items()}
-        raw, meta = self.forward_raw(raw_in)
+        raw, meta = self.forward_raw(raw_in, keep=keep)
         names = set(keep) if keep is not None else set(raw)
         out = {}
         for name in names:
@@ -172,10 +172,25 @@ class GpuSimulator:
             out[name] = v / np.power(2.0, _exp_of(t))
         return out
 
-    def forward_raw(self, raw_inputs: Dict[str, torch.Tensor]):
+    def forward_raw(self, raw_inputs: Dict[str, torch.Tensor], keep: Optional[Iterable[str]] = None):
         """The pass on int16 device tensors (no host conversion): returns
-        ({name: raw tensor}, {name: TensorInfo})."""
+        ({name: raw tensor}, {name: TensorInfo}).  With ``keep`` (the lean
+        mode of _simulate.py:573-592) every other tensor is released after its
+        last reader, so the allocator reuses its memory."""
         raw: Dict[str, torch.Tensor] = dict(raw_inputs)
+        dying: Dict[int, list] = {}
+        if keep is not None:
+            keep = set(keep)
+            last: Dict[str, int] = {}
+            for i, sn in enumerate(self._graph.nodes):
+                for t in sn.inputs:
+                    if t is not None:
+                        last[t.onnx_name] = i
+                last.setdefault(sn.output.onnx_name, i)
+            wnames = {t.onnx_name for t in self._graph.weight_tensors}
+            for name, i in last.items():
+                if name not in keep and name not in wnames:
+                    dying.setdefault(i, []).append(name)
         meta = {t.onnx_name: t for t in self._graph.input_tensors}
         for t in self._graph.weight_tensors:
             if getattr(t, "data", None) is not None:
@@ -218,6 +233,10 @@ class GpuSimulator:
                              smx_cm=sn.cm, smx_cfg=sn.cfg, smx_mask=sn.n)
             elif kind == "ScheduledNode":
                 y = self._vectorop(sn, get)
+            elif kind == "LayerNormRoNode":
+                y = self._layernorm(sn, get(sn.inputs[0]), get(sn.inputs[1]))
+            elif kind == "TransposeRoNode":
+                y = self._transpose(sn, get(sn.inputs[0]), get(sn.inputs[1]))
             else:
                 raise NotImplementedError(f"GpuSimulator: no sm_100a kernel for node type {kind}")
             if alias_t is not None:  # the fused intermediate is not materialised
@@ -226,6 +245,8 @@ class GpuSimulator:
             else:
                 raw[out_t.onnx_name] = y
                 meta[out_t.onnx_name] = out_t
+            for name in dying.get(i, ()):
+                raw.pop(name, None)
         return raw, meta
 
     # ------------------------------------------------------------ node kernels
@@ -233,6 +254,8 @@ class GpuSimulator:
         A, B, Y = sn.inputs[0], sn.inputs[1], sn.output
         wrap = F_WRAP32 if _has_exp(A, B, Y) else 0
         ash, bsh = list(A.shape), list(B.shape)
+        if len(bsh) == 2 and len(ash) > 2:  # a weight: A's leading dims are rows
+            ash = [int(np.prod(ash[:-1])), ash[-1]]
         if len(bsh) == 1:
             bsh = [bsh[0], 1]
         if len(ash) == 1:
@@ -299,6 +322,40 @@ class GpuSimulator:
                  lp_order=sn.lp_order, count_include_pad=int(bool(sn.count_include_pad)))
         return y
 
+    def _layernorm(self, sn, x, P):
+        """One NORM job (rowops_nodes.py:238-242): eps register E, Bq' shifted by
+        24 + g - bb; rows of n int16 at 2n-byte strides."""
+        from . import rowops_host as RH
+        y = self._alloc(sn.output.numel)
+        ops.rowops(x, None, y, P, op=RH.opword(RH.OP_NORM, ln=True), n=sn.n, rows=sn.rows, blocks=1,
+                   a_s1=2 * sn.n, c_s1=2 * sn.n, eps=int(sn.E), bq_sh=RH.P1_BITS + sn.g - sn.bb,
+                   win_lo=0, win_hi=RH.NO_WINDOW)
+        return y
+
+    def _transpose(self, sn, x, pz):
+        """The node's COPY (a zero P_BCAST entry) or TRANSPOSE (8-row tiles) job
+        (rowops_nodes.py:309-316)."""
+        from . import rowops_host as RH
+        y = self._alloc(sn.output.numel)
+        s1, s2, b1, b2, c1, c2 = sn.strides
+        copy = sn.kind == "copy"
+        op = RH.opword(RH.OP_COPY, p_bcast=True) if copy else RH.opword(RH.OP_XPOSE)
+        ops.rowops(x, None, y, pz if copy else None, op=op, n=sn.n, rows=sn.rows, blocks=sn.blocks,
+                   a_s1=s1, a_s2=s2, b_s1=b1, b_s2=b2, c_s1=c1, c_s2=c2, aux=0 if copy else RH.QIMAGE_R,
+                   win_lo=0, win_hi=RH.NO_WINDOW, a_off=getattr(sn, "a_off", 0))
+        return y
+
+    def _tiled_weight(self, t, size: int) -> torch.Tensor:
+        """A small broadcast weight repeated to ``size`` elements: the same
+        elementwise job with longer rows (a scalar would give rows of one)."""
+        key = ("tiled", t.onnx_name, size)
+        if key not in self._weights:
+            w = self._weight_raw(t)[:t.numel]
+            buf = self._alloc(size)
+            buf[:size].copy_(w.repeat(size // t.numel))
+            self._weights[key] = buf
+        return self._weights[key]
+
     def _vectorop(self, sn, get):
         """The node's kernel call(s): one operand may be a repeating chunk
         (nodes.py:226-305 trailing-contiguous broadcast): outer = numel /
@@ -322,6 +379,17 @@ class GpuSimulator:
         if na != N and nb != N:
             raise NotImplementedError("VectorOP: both operands broadcast")
         size = nb if nb != N else na
+        small_t = b_t if nb != N else a_t
+        if size < 1024 and getattr(small_t, "data", None) is not None:
+            r = 1
+            while size * r * 2 <= 2048 and N % (size * r * 2) == 0:
+                r *= 2
+            if r > 1:
+                size *= r
+                if nb != N:
+                    b = self._tiled_weight(b_t, size)
+                else:
+                    a = self._tiled_weight(a_t, size)
         outer = N // size
         a_inc, b_inc = (size, 0) if nb != N else (0, size)
         # rows need not be on 8-lane words: the kernel writes a row's tail lanes

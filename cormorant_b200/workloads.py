@@ -14,6 +14,7 @@ from typing import Dict, List, Tuple
 import numpy as np
 
 from . import nodes as N
+from . import rowops_host as RH
 
 
 def q88_uniform(rng, shape, lo, hi) -> np.ndarray:
@@ -60,6 +61,26 @@ class NodeFactory:
 
     def softmax(self, x, y, rows, n, cm, cfg):
         self.nodes.append(N.SoftmaxVopNode(inputs=[x], output=y, rows=rows, n=n, cm=cm, cfg=cfg))
+
+    def layernorm(self, x, y, rows, n, gamma, beta, eps):
+        """LayerNorm on the row-ops unit: the parameter block (words as Q8.8
+        values, rowops_nodes.py:96-102) and the registers of the job."""
+        words, g, bb, E = RH.layernorm_job(gamma, beta, n, eps)
+        p = self.tensor(f"{y.onnx_name}__rowops_p", (words.size,), words / 256.0)
+        self.nodes.append(N.LayerNormRoNode(inputs=[x, p], output=y, rows=rows, n=n, eps=eps, g=g, bb=bb, E=E,
+                                            gamma=np.asarray(gamma, np.float64), beta=np.asarray(beta, np.float64)))
+
+    def transpose(self, x, y, in_shape, perm):
+        """A Transpose as one row-ops COPY / TRANSPOSE job (rowops_nodes.py:318-346)."""
+        job = RH.transpose_job(in_shape, perm)
+        if job is None:
+            raise ValueError(f"transpose {in_shape} perm {perm}: not a row-ops job")
+        kind, n, rows, blocks, strides = job
+        pz = self.tensors.get("__rowops_zero_p")
+        if pz is None:
+            pz = self.tensor("__rowops_zero_p", (8,), RH.param_block(0, 0, 0, 0, 0) / 256.0)
+        self.nodes.append(N.TransposeRoNode(inputs=[x, pz], output=y, kind=kind, n=n, rows=rows, blocks=blocks,
+                                            strides=strides, perm=list(perm)))
 
     def graph(self, inputs, outputs):
         return N.Graph(nodes=self.nodes, weight_tensors=self.weights, input_tensors=inputs, output_tensors=outputs)
@@ -171,6 +192,121 @@ def mobilenet_v2(seed: int = 3, batch: int = 1, res: int = 224, classes: int = 1
     f.vop(N.OP_ADD, [mm, BF], lg)
     macs += 1280 * classes
     return f.graph([X], [lg]), {"x": x}, macs
+
+
+# ---------------------------------------------------------------- config 4: BERT-base encoder
+SMX_Q88 = (12102203, 19 | (8 << 8))      # softmax unit registers at Q8.8 (vectorop_smx.scale_regs(8, 1.0))
+
+
+def normal_q88(rng, shape, sigma) -> np.ndarray:
+    """N(0, sigma) reals quantised RNE + saturate to Q8.8 (per-tensor exponent 8)."""
+    return np.clip(np.round(rng.normal(0.0, sigma, size=shape) * 256.0), -32768, 32767) / 256.0
+
+
+def bert_base(seed: int = 4, batch: int = 1, seq: int = 384, layers: int = 12, hidden: int = 768, heads: int = 12,
+              ffn: int = 3072, vocab: int = 30522, qa_head: bool = True, factory: NodeFactory = None):
+    """BERT-base encoder on the kernels, the scheduler's partition of
+    bertsquad (ap_fixed<16,8> throughout): per layer Q / K / V = x W + b
+    (MatMul, VectorOP ADD), head split and K^T as row-ops COPY / TRANSPOSE
+    jobs, scores Q K^T (batched MatMul), MUL 1/8, softmax on the VectorOP unit
+    (row mode), context P V, head merge (COPY), output projection + bias,
+    residual ADD, LayerNorm on the row-ops unit, FFN x W1 + b1 with GELU (erf)
+    fused into the ADD, x W2 + b2, residual ADD, LayerNorm; then the SQuAD
+    head (start / end logits).
+
+    Layout: the batch's sequences are stacked, hidden states [batch * seq][768];
+    the heads are head-major over the whole batch ([heads][batch * seq][64], one
+    COPY job), so every per-(head, sequence) tensor is a contiguous slice and
+    K^T is one TRANSPOSE job over heads * batch blocks.  Full-length
+    sequences (no padding mask).  The word-embedding gather is the
+    reference's host op: the graph input is the gathered rows (ids uniform
+    over ``vocab``); position and token-type embeddings are added on
+    VectorOP.  Weights N(0, 0.02) quantised to Q8.8; LayerNorm gamma =
+    1 + N(0, 0.02), beta = N(0, 0.02) (encoded by the parameter block).
+    Returns (graph, {input: values}, macs_per_token)."""
+    f = factory or NodeFactory()
+    rng = np.random.default_rng(seed)
+    T, D, H, dh = seq, hidden, heads, hidden // heads
+    R = batch * T
+    word = normal_q88(rng, (vocab, D), 0.02)
+    ids = rng.integers(0, vocab, size=(batch, T))
+    x = word[ids]
+    cnt = [0]
+
+    def nm(p):
+        cnt[0] += 1
+        return f"{p}{cnt[0]}"
+
+    def act(shape, p="t"):
+        return f.tensor(nm(p), shape)
+
+    def weight(shape, sigma=0.02, p="w"):
+        v = normal_q88(rng, shape, sigma)
+        return f.tensor(nm(p), v.shape, v)
+
+    def linear(t, k, m):
+        W, B = weight((k, m)), weight((m,), p="b")
+        mm, y = act((R, m), "mm"), act((R, m), "lin")
+        f.matmul(t, W, mm, R, k, m)
+        return mm, B, y
+
+    def ln(t):
+        y = act((R, D), "ln")
+        f.layernorm(t, y, R, D, 1.0 + rng.normal(0.0, 0.02, D), rng.normal(0.0, 0.02, D), 1e-12)
+        return y
+
+    X = f.tensor("x", (batch, T, D))
+    pos, typ = weight((T, D)), weight((D,))
+    e1, e2 = act((batch, T, D), "emb"), act((R, D), "emb")
+    f.vop(N.OP_ADD, [X, pos], e1)
+    f.vop(N.OP_ADD, [e1, typ], e2)
+    h = ln(e2)
+    scale = f.tensor("attn_scale", (1,), np.array([0.125]))
+    for _ in range(layers):
+        heads_out = []
+        for p in ("q", "k", "v"):
+            mm, B, y = linear(h, D, D)
+            f.vop(N.OP_ADD, [mm, B], y)
+            y3 = act((R, H, dh), p + "3")
+            f.reshape(y, y3)
+            hs = act((H * batch, T, dh), p + "h")
+            f.transpose(y3, hs, (R, H, dh), (1, 0, 2))
+            heads_out.append(hs)
+        qh, kh, vh = heads_out
+        kt = act((H * batch, dh, T), "kt")
+        f.transpose(kh, kt, (H * batch, T, dh), (0, 2, 1))
+        sc, ss, pr = act((H * batch, T, T), "sc"), act((H * batch, T, T), "ss"), act((H * batch, T, T), "pr")
+        f.matmul(qh, kt, sc, T, dh, T)
+        f.vop(N.OP_MUL, [sc, scale], ss)
+        f.softmax(ss, pr, H * batch * T, T, *SMX_Q88)
+        ctx = act((H * batch, T, dh), "ctx")
+        f.matmul(pr, vh, ctx, T, T, dh)
+        ctx3 = act((H, R, dh), "ctx3")
+        f.reshape(ctx, ctx3)
+        mg = act((R, H, dh), "merge")
+        f.transpose(ctx3, mg, (H, R, dh), (1, 0, 2))
+        mg2 = act((R, D), "mflat")
+        f.reshape(mg, mg2)
+        mm, B, y = linear(mg2, D, D)
+        f.vop(N.OP_ADD, [mm, B], y)
+        r1 = act((R, D), "res")
+        f.vop(N.OP_ADD, [h, y], r1)
+        h1 = ln(r1)
+        mm, B, y = linear(h1, D, ffn)
+        f.vop(N.OP_ADD, [mm, B], y, act=N.ACT_GELU)
+        mm, B, y2 = linear(y, ffn, D)
+        f.vop(N.OP_ADD, [mm, B], y2)
+        r2 = act((R, D), "res")
+        f.vop(N.OP_ADD, [h1, y2], r2)
+        h = ln(r2)
+    outs = [h]
+    if qa_head:
+        mm, B, y = linear(h, D, 2)
+        lg = f.tensor("qa_logits", (R, 2))
+        f.vop(N.OP_ADD, [mm, B], lg)
+        outs = [lg]
+    macs = layers * (4 * D * D + 2 * D * ffn + 2 * T * D) + (2 * D if qa_head else 0)
+    return f.graph([X], outs), {"x": x}, macs
 
 
 def graph_macs(graph) -> int:

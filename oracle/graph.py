@@ -22,8 +22,10 @@ def forward_raw(graph, raw_inputs):
     for sn in graph.nodes:
         k = type(sn).__name__
         out = sn.output
-        if k in ("MatmulNode", "MatmulConvNode"):                            # :620-633
-            y = spec.matmul_raw(arr[sn.inputs[0].onnx_name], arr[sn.inputs[1].onnx_name])
+        if k in ("MatmulNode", "MatmulConvNode"):                            # :620-633, :814-835
+            wrap = any(getattr(t, a, None) is not None for t in (sn.inputs[0], sn.inputs[1], out)
+                       for a in ("exp", "wexp"))
+            y = spec.matmul_raw(arr[sn.inputs[0].onnx_name], arr[sn.inputs[1].onnx_name], wrap)
         elif k == "ConvNode":                                                # :643-660
             x = arr[sn.inputs[0].onnx_name].reshape(sn.batch, sn.in_ch, sn.in_h, sn.in_w)
             w = arr[sn.inputs[1].onnx_name]
@@ -40,25 +42,26 @@ def forward_raw(graph, raw_inputs):
             x = arr[sn.inputs[0].onnx_name].reshape(sn.rows, sn.n)
             y = spec.softmax_rows(x, sn.n, sn.cm, sn.cfg & 63, (sn.cfg >> 8) & 31)
         elif k == "ScheduledNode":                                           # :721-765
-            a = arr[sn.inputs[0].onnx_name]
+            a = arr[sn.inputs[0].onnx_name].reshape(-1)
             op = sn.op_code
-            N = out.numel if hasattr(out, "numel") else int(np.prod(out.shape))
+            N = int(np.prod(out.shape))
             c = np.zeros(N + 16, np.int16)
             if op <= 3:
-                b = arr[sn.inputs[1].onnx_name]
-                na, nb = a.size, b.size
-                size = nb if nb != N else na
-                a_inc, b_inc = (size, 0) if nb != N else (0, size)
-                for o in range(N // size):   # row by row: rows need not be 8-lane aligned here
-                    cc = np.zeros(size + 16, np.int16)
-                    spec.vectorop_job(a.reshape(-1)[o * a_inc: o * a_inc + size + (0 if a_inc else 0)],
-                                      b.reshape(-1)[o * b_inc: o * b_inc + size], cc, size, op, 1, 0, 0,
-                                      getattr(sn, "act", 0), getattr(sn, "alpha", 0))
-                    c[o * size:(o + 1) * size] = cc[:size]
+                # the broadcast operand repeats (trailing-contiguous, nodes.py:226-305):
+                # elementwise, so it is tiled to the output's length
+                b = arr[sn.inputs[1].onnx_name].reshape(-1)
+                a = np.tile(a, N // a.size) if a.size != N else a
+                b = np.tile(b, N // b.size) if b.size != N else b
+                spec.vectorop_job(a, b, c, N, op, 1, 0, 0, getattr(sn, "act", 0), getattr(sn, "alpha", 0))
             else:
-                spec.vectorop_job(a.reshape(-1), None, c, N, op, 1, 0, 0, getattr(sn, "act", 0),
-                                  getattr(sn, "alpha", 0))
+                spec.vectorop_job(a, None, c, N, op, 1, 0, 0, getattr(sn, "act", 0), getattr(sn, "alpha", 0))
             y = c[:N].astype(np.int64)
+        elif k == "LayerNormRoNode":                                         # rowops_nodes.py:188-192
+            x = arr[sn.inputs[0].onnx_name].reshape(sn.rows, sn.n)
+            y = spec.layer_norm_rows(x, np.ones(sn.n) if sn.gamma is None else sn.gamma,
+                                     np.zeros(sn.n) if sn.beta is None else sn.beta, sn.eps, sn.F, sn.F)
+        elif k == "TransposeRoNode":                                         # rowops_nodes.py:296-298
+            y = np.transpose(arr[sn.inputs[0].onnx_name].reshape(sn.inputs[0].shape), sn.perm)
         else:
             raise NotImplementedError(k)
         arr[out.onnx_name] = np.asarray(y, np.int64).reshape(out.shape)

@@ -703,3 +703,60 @@ def rowops_job(mem: RowOpsMem, op: int, n: int, c1: int, c2: int, a: int, a_s1: 
                     for d in range(L):
                         vals = [mem.rd16(ra + r * b_s1 + 2 * d) for r in range(R)]
                         mem.wr(rc + d * b_s2, b"".join((v & 0xFFFF).to_bytes(2, "little") for v in vals))
+
+
+# --------------------------------------------------------------------------- LayerNorm rows (BERT)
+def ln_gamma_scale(gamma: np.ndarray) -> int:
+    """g with max |round(gamma 2^g)| < 2^31: 30 - floor(log2 max|gamma|) (RS:125-130)."""
+    m = float(np.abs(np.asarray(gamma, np.float64)).max())
+    return 0 if m == 0.0 else 30 - int(math.floor(math.log2(m)))
+
+
+def ln_beta_bits(beta: np.ndarray) -> int:
+    """bb <= 20 with |round(beta 2^bb)| < 2^21 (RS:133-143)."""
+    m = float(np.abs(np.asarray(beta, np.float64)).max()) if np.size(beta) else 0.0
+    bb = 20
+    while bb > 0 and abs(round(m * 2.0 ** bb)) >= (1 << 21):
+        bb -= 1
+    return bb
+
+
+def layer_norm_rows(x: np.ndarray, gamma: np.ndarray, beta: np.ndarray, eps: float, f_x: int = 8,
+                    f_out: int = 8) -> np.ndarray:
+    """LayerNorm of int rows [rows][n] at 2^-f_x to int16 at 2^-f_out, the
+    unit's integer datapath (RS:206-223 norm_params, RS:259-282 layer_norm;
+    RR NORM): exact S1, S2; D = n S2 - S1^2 + E (1 if <= 0); rsqrt_bf(D) =
+    Rm 2^-sh; P1 = floor((n x - S1) Rm / 2^(sh-24)); out = sat16(rne((P1 G +
+    Bq) / 2^(24+g-f_out))) with G = rint(gamma 2^g), Bq = rint(beta 2^bb) <<
+    (24+g-bb), E = rint(eps n^2 2^(2 f_x)).  int64 throughout where the
+    bounds allow, Python integers per row where they do not."""
+    x = np.asarray(x, np.int64)
+    rows, n = x.shape
+    gamma = np.asarray(gamma, np.float64)
+    beta = np.asarray(beta, np.float64)
+    g = ln_gamma_scale(gamma)
+    G = np.rint(gamma * 2.0 ** g).astype(np.int64)
+    bb = ln_beta_bits(beta)
+    Bq = np.rint(beta * 2.0 ** bb).astype(np.int64) << (P1_BITS + g - bb)
+    E = int(round(eps * n * n * 2.0 ** (2 * f_x)))
+    S1 = x.sum(axis=1)
+    S2 = (x * x).sum(axis=1)
+    out = np.empty((rows, n), np.int64)
+    sc = P1_BITS + g - f_out
+    gmax = int(np.abs(G).max()) if n else 0
+    bmax = int(np.abs(Bq).max()) if n else 0
+    for r in range(rows):
+        s1, s2 = int(S1[r]), int(S2[r])
+        D = n * s2 - s1 * s1 + E
+        if D <= 0:
+            D = 1
+        Rm, sh = rsqrt_bf(D)
+        A = n * x[r] - s1
+        amax = int(np.abs(A).max())
+        if amax * Rm < (1 << 62) and ((amax * Rm) >> (sh - P1_BITS)) * gmax + bmax < (1 << 62):
+            P1 = (A * np.int64(Rm)) >> (sh - P1_BITS)
+            out[r] = sat16(rne_shr(P1 * G + Bq, sc))
+        else:
+            vals = [((int(a) * Rm) >> (sh - P1_BITS)) * int(gg) + int(bq) for a, gg, bq in zip(A, G, Bq)]
+            out[r] = [max(min(_rne(v, sc), I16_HI), I16_LO) for v in vals]
+    return out

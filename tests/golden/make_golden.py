@@ -21,6 +21,8 @@ import argparse
 import os
 import sys
 
+import zlib
+
 import numpy as np
 
 HERE = os.path.dirname(os.path.abspath(__file__))
@@ -314,7 +316,8 @@ def make_graph_goldens(ref, out):
     from cormorant_b200 import workloads as WL
     from src.dtype import AP_FIXED_16_8 as D
     from src.tensor import TensorInfo as T
-    from src import nodes as RN, smx_nodes as SN
+    from src import nodes as RN, smx_nodes as SN, rowops_nodes as RON, rowops_spec as RS
+    from src.host_nodes import _collapse
     import onnx
 
     class RefFactory(WL.NodeFactory):
@@ -348,11 +351,44 @@ def make_graph_goldens(ref, out):
             self.nodes.append(SN.SoftmaxVopNode(onnx_node=onnx.NodeProto(), inputs=[x], output=y, rows=rows, n=n,
                                                 cm=cm, cfg=cfg))
 
+        # the row-ops nodes exactly as rowops_nodes.from_onnx_layernorm /
+        # from_onnx_transpose build them (registers from the reference's own spec)
+        def layernorm(self, x, y, rows, n, gamma, beta, eps):
+            G, g, _bq, E = RS.norm_params(gamma, n, eps, 8, beta=beta)
+            bb = RS.beta_bits(beta)
+            words = RS.param_block(G, np.rint(beta * 2.0 ** bb).astype(np.int64), 0, 0, RS.P1_BITS + g - 8)
+            p = RON.param_tensor(self.tensors, f"{y.onnx_name}__rowops_p", words)
+            self.weights.append(p)
+            self.nodes.append(RON.LayerNormRoNode(onnx_node=onnx.NodeProto(), inputs=[x, p, self._tables()], output=y,
+                                                  F=8, rows=rows, n=n, eps=eps, g=int(g), bb=int(bb), E=int(E),
+                                                  gamma=np.asarray(gamma, np.float64),
+                                                  beta=np.asarray(beta, np.float64)))
+
+        def _tables(self):
+            had = RON.TABLES_NAME in self.tensors
+            t = RON.tables_tensor(self.tensors)
+            if not had:
+                self.weights.append(t)
+            return t
+
+        def transpose(self, x, y, in_shape, perm):
+            src = [int(np.prod(in_shape[i + 1:])) for i in range(len(in_shape))]
+            dims, sstr = _collapse([in_shape[p] for p in perm], [src[p] for p in perm])
+            kind, n, rows, blocks, strides = RON.transpose_job(dims, sstr, 2)
+            had = RON.ZERO_P_NAME in self.tensors
+            pz = RON.zero_param_tensor(self.tensors)
+            if not had:
+                self.weights.append(pz)
+            self.nodes.append(RON.TransposeRoNode(onnx_node=onnx.NodeProto(), inputs=[x, pz, self._tables()],
+                                                  output=y, F=8, kind=kind, n=n, rows=rows, blocks=blocks,
+                                                  strides=strides, perm=list(perm), pz=pz))
+
         def graph(self, inputs, outputs):
             return _Graph(self.nodes, self.weights, inputs, outputs)
 
     for name, build in (("mnist_b2", lambda f: WL.mnist(seed=11, batch=2, factory=f)),
-                        ("mbv2_r32_b2", lambda f: WL.mobilenet_v2(seed=13, batch=2, res=32, factory=f))):
+                        ("mbv2_r32_b2", lambda f: WL.mobilenet_v2(seed=13, batch=2, res=32, factory=f)),
+                        ("bert_l2_t32_b2", lambda f: WL.bert_base(seed=17, batch=2, seq=32, layers=2, factory=f))):
         g, feeds, _ = build(RefFactory())
         arrays = _shim(sim, D, g)._forward_pass(feeds)
         outs = {}
@@ -361,6 +397,20 @@ def make_graph_goldens(ref, out):
         # every intermediate too (the fused ones are compared where materialised)
         for sn in g.nodes:
             outs["t_" + sn.output.onnx_name] = np.round(arrays[sn.output.onnx_name] * 256).astype(np.int64)
+        for sn in g.nodes:                   # the row-ops registers the reference derived
+            if type(sn).__name__ == "LayerNormRoNode":
+                outs["r_" + sn.output.onnx_name] = np.array([sn.g, sn.bb, sn.E, sn.rows, sn.n], np.int64)
+                outs["p_" + sn.output.onnx_name] = np.round(np.asarray(sn.inputs[1].data) * 256).astype(np.int64)
+            elif type(sn).__name__ == "TransposeRoNode":
+                outs["r_" + sn.output.onnx_name] = np.array([0 if sn.kind == "copy" else 1, sn.n, sn.rows, sn.blocks,
+                                                             *sn.strides], np.int64)
+        if name.startswith("bert"):
+            # intermediates as CRC-32 of their raw int16 bytes (C order), the
+            # outputs in full: a few KB instead of every activation
+            outs = {(("c" + k[1:]) if k.startswith("t_") else k):
+                    (np.array([zlib.crc32(np.ascontiguousarray(v.astype("<i2")).tobytes())], np.int64)
+                     if k.startswith("t_") else v.astype(np.int16) if k.startswith("out_") else v)
+                    for k, v in outs.items()}
         np.savez_compressed(os.path.join(out, f"sim_graph_{name}.npz"), **outs)
         print(f"sim_graph_{name}.npz: {len(g.nodes)} nodes")
 
