@@ -480,6 +480,16 @@ def bench_models(torch, dev, stream, flush, args, world, rank, pg):
         out[name] = {"batch_per_gpu": batch, "ms_per_batch": round(ms, 4), f"{unit}_per_s": round(rate, 1),
                      "GMAC/s": round(rate * macs_unit / 1e9, 1), f"mmac_per_{unit[:-1]}": round(macs_unit / 1e6, 2),
                      "nodes": len(g.nodes)}
+        if args.detail:  # per-kernel device time of one eager pass (events around each launch)
+            from cormorant_b200 import ops
+            ops.profile_read()
+            ops.profile_enable(True)
+            with torch.cuda.stream(stream):
+                sim.forward_raw(raw, keep=keep)
+            ops.profile_enable(False)
+            prof = ops.profile_read()
+            out[name]["kernels"] = {k: {"launches": v[0], "ms": round(v[1], 4)}
+                                    for k, v in sorted(prof.items(), key=lambda kv: -kv[1][1])}
         del graph, res, sim, raw
         torch.cuda.empty_cache()
         if rank == 0 and world == 1 and not args.no_cpu and name != "mnist_b4096":

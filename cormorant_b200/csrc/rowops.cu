@@ -290,6 +290,157 @@ __global__ void ro_tload(RoArgs q, uint64_t* sig, uint32_t* rsq) {
     }
 }
 
+
+// ---------------------------------------------------------------- fast paths
+// COPY / ADDX on int16 A, B and C with one broadcast parameter entry and rows
+// of whole 16-byte words (n % 8 == 0): a thread per 8-lane word, 16-byte loads
+// and stores.  Identity parameters (sa = sb = sc = 0, Bq' = 0, no SCALE) take
+// an int32 path; any other entry the exact 128-bit formula of ro_rows.
+__global__ void __launch_bounds__(256) ro_stream16(RoArgs q) {
+  const uint32_t code = q.op & 15u;
+  const bool ben = (q.op >> 12) & 1u, relu = (q.op >> 15) & 1u, scale = (q.op >> 17) & 1u;
+  const Param pr = ld_param(q, 0);
+  const bool ident = pr.sa == 0 && pr.sb == 0 && pr.sc == 0 && pr.bq == 0 && !scale;
+  const uint32_t per = q.n >> 3;
+  const uint64_t total = (uint64_t)q.c1 * q.c2 * per;
+  for (uint64_t g = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; g < total; g += (uint64_t)gridDim.x * blockDim.x) {
+    const uint64_t row = g / per;
+    const uint32_t w = (uint32_t)(g - row * per);
+    const uint32_t i1 = (uint32_t)(row % q.c1), i2 = (uint32_t)(row / q.c1);
+    const bool zero_a = (code == 1 || code == 2) && (i1 < q.win_lo || i1 >= q.win_hi);
+    int4 xa = make_int4(0, 0, 0, 0), yb = make_int4(0, 0, 0, 0);
+    if (!zero_a) xa = *(const int4*)(q.a + (uint64_t)i2 * q.a_s2 + (uint64_t)i1 * q.a_s1 + 16ull * w);
+    if (ben) yb = *(const int4*)(q.b + (uint64_t)i2 * q.b_s2 + (uint64_t)i1 * q.b_s1 + 16ull * w);
+    const int16_t* xs = (const int16_t*)&xa;
+    const int16_t* ys = (const int16_t*)&yb;
+    int4 out;
+    int16_t* os = (int16_t*)&out;
+#pragma unroll
+    for (int e = 0; e < 8; e++) {
+      int64_t r;
+      if (ident) {
+        const int32_t v = (int32_t)xs[e] + (int32_t)ys[e];
+        r = v > 32767 ? 32767 : (v < -32768 ? -32768 : v);
+      } else {
+        const __int128 sum = ((__int128)xs[e] << pr.sa) + ((__int128)ys[e] << pr.sb) + ((__int128)pr.bq << q.bq_sh);
+        r = corm_sat16_128(corm_rne_shr128(scale ? sum * (__int128)pr.g : sum, (int)pr.sc));
+      }
+      if (relu && r < 0) r = 0;
+      os[e] = (int16_t)r;
+    }
+    *(int4*)(q.c + (uint64_t)i2 * q.c_s2 + (uint64_t)i1 * q.c_s1 + 16ull * w) = out;
+  }
+}
+
+// XPOSE of 8-row tiles into 16-byte granules (R = 8), through shared memory:
+// a CTA takes XT consecutive tiles (i1) of one block (i2) and XD columns d,
+// reads the 8 XT source rows with 16-byte loads (a row's 128 bytes per 8
+// lanes), then each thread writes the granules of one column d for two
+// consecutive tiles (32 contiguous bytes when c_s1 = 16); lanes run along d,
+// so the shared-memory reads are conflict-free.
+constexpr int XT = 16, XD = 64;
+__global__ void __launch_bounds__(256) ro_xpose8(RoArgs q) {
+  __shared__ __align__(16) int16_t tile[8 * XT][XD + 8];
+  const uint32_t L = q.n;
+  const uint32_t ntg = (q.c1 + XT - 1) / XT, ndg = (L + XD - 1) / XD;
+  const uint64_t units = (uint64_t)q.c2 * ntg * ndg;
+  for (uint64_t u = blockIdx.x; u < units; u += gridDim.x) {
+    const uint32_t dg = (uint32_t)(u % ndg);
+    const uint64_t r2 = u / ndg;
+    const uint32_t tg = (uint32_t)(r2 % ntg), i2 = (uint32_t)(r2 / ntg);
+    const uint32_t t0 = tg * XT, d0 = dg * XD;
+    const uint32_t nt = min((uint32_t)XT, q.c1 - t0), nd = min((uint32_t)XD, L - d0);
+    for (uint32_t i = threadIdx.x; i < 8u * nt * (XD / 8); i += blockDim.x) {
+      const uint32_t rr = i / (XD / 8), ww = i % (XD / 8);
+      if (ww * 8 >= nd) continue;
+      const uint32_t tt = rr >> 3, r = rr & 7u;
+      const uint8_t* src = q.a + (uint64_t)i2 * q.a_s2 + (uint64_t)(t0 + tt) * q.a_s1 + (uint64_t)r * q.b_s1 +
+                           2ull * (d0 + ww * 8);
+      *(int4*)&tile[rr][ww * 8] = *(const int4*)src;
+    }
+    __syncthreads();
+    for (uint32_t i = threadIdx.x; i < nd * (uint32_t)(XT / 2); i += blockDim.x) {
+      const uint32_t d = i % nd, tt0 = 2u * (i / nd);
+      if (tt0 >= nt) continue;
+      uint8_t* dst = q.c + (uint64_t)i2 * q.c_s2 + (uint64_t)(t0 + tt0) * q.c_s1 + (uint64_t)(d0 + d) * q.b_s2;
+#pragma unroll
+      for (int h = 0; h < 2; h++) {
+        if (tt0 + h >= nt) break;
+        int4 v;
+        int16_t* vs = (int16_t*)&v;
+#pragma unroll
+        for (int r = 0; r < 8; r++) vs[r] = tile[(tt0 + h) * 8 + r][d];
+        *(int4*)(dst + (uint64_t)h * q.c_s1) = v;
+      }
+    }
+    __syncthreads();
+  }
+}
+
+// NORM on int16 rows of n <= 4096 elements, one warp per row: the exact sums
+// fit int64 (|S1| < 2^28, S2 < 2^42), D and the output formula as ro_rows.
+// Rows are read once into registers (n % 8 == 0, 16-byte loads): NW_PER
+// 8-lane words per lane, n <= 256 NW_PER.
+template <int NW_PER>
+__global__ void __launch_bounds__(256) ro_norm16(RoArgs q) {
+  const bool ln = (q.op >> 16) & 1u;
+  const bool bcast = (q.op >> 13) & 1u;
+  const int lane = threadIdx.x & 31;
+  const uint32_t words = q.n >> 3;
+  const uint64_t rows = (uint64_t)q.c1 * q.c2;
+  const uint64_t warp0 = ((uint64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const uint64_t nwarps = ((uint64_t)gridDim.x * blockDim.x) >> 5;
+  for (uint64_t row = warp0; row < rows; row += nwarps) {
+    const uint32_t i1 = (uint32_t)(row % q.c1), i2 = (uint32_t)(row / q.c1);
+    const uint8_t* ra = q.a + (uint64_t)i2 * q.a_s2 + (uint64_t)i1 * q.a_s1;
+    uint8_t* rc = q.c + (uint64_t)i2 * q.c_s2 + (uint64_t)i1 * q.c_s1;
+    int4 xv[NW_PER];
+    long long s1 = 0, s2 = 0;
+#pragma unroll
+    for (int k = 0; k < NW_PER; k++) {
+      const uint32_t w = lane + 32u * k;
+      xv[k] = make_int4(0, 0, 0, 0);
+      if (w < words) {
+        xv[k] = *(const int4*)(ra + 16ull * w);
+        const int16_t* xs = (const int16_t*)&xv[k];
+#pragma unroll
+        for (int e = 0; e < 8; e++) {
+          s1 += xs[e];
+          s2 += (long long)xs[e] * xs[e];
+        }
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      s1 += __shfl_xor_sync(0xffffffffu, s1, o);
+      s2 += __shfl_xor_sync(0xffffffffu, s2, o);
+    }
+    __int128 D = ln ? ((__int128)q.n * s2 - (__int128)s1 * s1 + (__int128)q.eps) : ((__int128)s2 + (__int128)q.eps);
+    if (D <= 0) D = 1;
+    uint64_t Rm;
+    int sh;
+    rsqrt_bf(D, Rm, sh, q.rsq);
+    const Param pb = ld_param(q, 0);
+#pragma unroll
+    for (int k = 0; k < NW_PER; k++) {
+      const uint32_t w = lane + 32u * k;
+      if (w >= words) continue;
+      const int16_t* xs = (const int16_t*)&xv[k];
+      int4 out;
+      int16_t* os = (int16_t*)&out;
+#pragma unroll
+      for (int e = 0; e < 8; e++) {
+        const Param pr = bcast ? pb : ld_param(q, 8u * w + e);
+        const long long A = ln ? (long long)q.n * xs[e] - s1 : (long long)xs[e];
+        const long long P1 = (long long)(((__int128)A * (__int128)Rm) >> (sh - 24));
+        const __int128 sv = (__int128)P1 * pr.g + ((__int128)pr.bq << q.bq_sh);
+        os[e] = (int16_t)corm_sat16_128(corm_rne_shr128(sv, (int)pr.sc));
+      }
+      *(int4*)(rc + 16ull * w) = out;
+    }
+  }
+}
+
 }  // namespace
 
 extern "C" int corm_rowops(const corm_rowops_desc* d, corm_stream_t stream) {
@@ -361,6 +512,39 @@ extern "C" int corm_rowops(const corm_rowops_desc* d, corm_stream_t stream) {
   }
   if (op == 7 && ((d->aux & 15u) == 0 || (d->aux & 15u) > 8u)) return CORM_OK;
   const uint64_t rows = (uint64_t)d->rows * d->blocks;
+  const uint32_t ak = (d->op >> 4) & 3u, bk = (d->op >> 6) & 3u, ck = (d->op >> 8) & 3u;
+  const bool i16 = ak == 0 && bk == 0 && ck == 0;
+  const bool bcast = (d->op >> 13) & 1u;
+  if ((op == 1 || op == 2) && i16 && bcast && d->n % 8 == 0) {
+    const uint64_t words = rows * (d->n / 8);
+    {
+      corm::ProfScope prof_("ro_stream16", st);
+      ro_stream16<<<corm_blocks(words, 256, 148u * 16u), 256, 0, st>>>(q);
+    }
+    return corm::cuda_status("rowops stream");
+  }
+  if (op == 7 && (d->aux & 15u) == 8u && d->n % 8 == 0 &&
+      !((C | d->c_s1 | d->c_s2 | d->b_s2) & 15u) && !(d->b_s1 & 15u)) {
+    const uint64_t units = (uint64_t)d->blocks * ((d->rows + XT - 1) / XT) * ((d->n + XD - 1) / XD);
+    {
+      corm::ProfScope prof_("ro_xpose8", st);
+      ro_xpose8<<<(unsigned)(units < 148u * 16u ? units : 148u * 16u), 256, 0, st>>>(q);
+    }
+    return corm::cuda_status("rowops xpose");
+  }
+  if (op == 5 && ak == 0 && d->n % 8 == 0) {
+    {
+      corm::ProfScope prof_("ro_norm16", st);
+      const unsigned grid = corm_blocks(rows, 8, 148u * 16u);
+      if (d->n <= 1024)
+        ro_norm16<4><<<grid, 256, 0, st>>>(q);
+      else if (d->n <= 2048)
+        ro_norm16<8><<<grid, 256, 0, st>>>(q);
+      else
+        ro_norm16<16><<<grid, 256, 0, st>>>(q);
+    }
+    return corm::cuda_status("rowops norm");
+  }
   {
     corm::ProfScope prof_("ro_rows", st);
     ro_rows<<<(unsigned)(rows < 148u * 64u ? rows : 148u * 64u), RO_THREADS, 0, st>>>(q);
