@@ -380,11 +380,28 @@ __global__ void __launch_bounds__(256) ro_xpose8(RoArgs q) {
 // NORM on int16 rows of n <= 4096 elements, one warp per row: the exact sums
 // fit int64 (|S1| < 2^28, S2 < 2^42), D and the output formula as ro_rows.
 // Rows are read once into registers (n % 8 == 0, 16-byte loads): NW_PER
-// 8-lane words per lane, n <= 256 NW_PER.
+// 8-lane words per lane, n <= 256 NW_PER.  The parameter entries (G, Bq',
+// sh_c) are decoded once per CTA into shared memory.  Per element,
+// P1 = (A Rm) >> (sh - 24) is exact in int64 (|A| < 2^29, Rm < 2^32); the
+// sum P1 G + Bq' << bq_sh too while |P1| < 2^31 and bq_sh <= 40, else it is
+// formed in 128 bits.
 template <int NW_PER>
 __global__ void __launch_bounds__(256) ro_norm16(RoArgs q) {
+  extern __shared__ __align__(16) uint8_t ro_smem[];
   const bool ln = (q.op >> 16) & 1u;
   const bool bcast = (q.op >> 13) & 1u;
+  const uint32_t npar = bcast ? 1u : q.n;
+  int32_t* s_g = (int32_t*)ro_smem;
+  int32_t* s_bq = s_g + npar;
+  uint8_t* s_sc = (uint8_t*)(s_bq + npar);
+  for (uint32_t c = threadIdx.x; c < npar; c += blockDim.x) {
+    const int4 e = *(const int4*)(q.p + 16ull * c);
+    s_g[c] = e.x;
+    s_bq[c] = (int32_t)((uint32_t)e.y << 10) >> 10;  // int22, sign-extended
+    s_sc[c] = (uint8_t)(((uint32_t)e.z >> 16) & 63u);
+  }
+  __syncthreads();
+  const bool small_bq = q.bq_sh <= 40u;
   const int lane = threadIdx.x & 31;
   const uint32_t words = q.n >> 3;
   const uint64_t rows = (uint64_t)q.c1 * q.c2;
@@ -420,7 +437,8 @@ __global__ void __launch_bounds__(256) ro_norm16(RoArgs q) {
     uint64_t Rm;
     int sh;
     rsqrt_bf(D, Rm, sh, q.rsq);
-    const Param pb = ld_param(q, 0);
+    const int shp = sh - 24;
+    const long long nn = ln ? (long long)q.n : 1, off = ln ? s1 : 0;
 #pragma unroll
     for (int k = 0; k < NW_PER; k++) {
       const uint32_t w = lane + 32u * k;
@@ -430,11 +448,19 @@ __global__ void __launch_bounds__(256) ro_norm16(RoArgs q) {
       int16_t* os = (int16_t*)&out;
 #pragma unroll
       for (int e = 0; e < 8; e++) {
-        const Param pr = bcast ? pb : ld_param(q, 8u * w + e);
-        const long long A = ln ? (long long)q.n * xs[e] - s1 : (long long)xs[e];
-        const long long P1 = (long long)(((__int128)A * (__int128)Rm) >> (sh - 24));
-        const __int128 sv = (__int128)P1 * pr.g + ((__int128)pr.bq << q.bq_sh);
-        os[e] = (int16_t)corm_sat16_128(corm_rne_shr128(sv, (int)pr.sc));
+        const uint32_t c = bcast ? 0u : 8u * w + e;
+        const long long g = s_g[c], bq = s_bq[c];
+        const int sc = s_sc[c];
+        const long long A = nn * xs[e] - off;
+        const long long P1 = (A * (long long)Rm) >> shp;
+        int64_t r;
+        if (small_bq && P1 > -(1ll << 31) && P1 < (1ll << 31)) {
+          const long long v = corm_rne_shr64(P1 * g + (bq << q.bq_sh), sc);
+          r = v > 32767 ? 32767 : (v < -32768 ? -32768 : v);
+        } else {
+          r = corm_sat16_128(corm_rne_shr128((__int128)P1 * g + ((__int128)bq << q.bq_sh), sc));
+        }
+        os[e] = (int16_t)r;
       }
       *(int4*)(rc + 16ull * w) = out;
     }
@@ -535,13 +561,15 @@ extern "C" int corm_rowops(const corm_rowops_desc* d, corm_stream_t stream) {
   if (op == 5 && ak == 0 && d->n % 8 == 0) {
     {
       corm::ProfScope prof_("ro_norm16", st);
-      const unsigned grid = corm_blocks(rows, 8, 148u * 16u);
+      const unsigned grid = corm_blocks(rows, 8, 148u * 4u);
+      const size_t npar = ((d->op >> 13) & 1u) ? 1u : d->n;
+      const size_t smem = npar * 9u + 16u;  // n <= 4096: under 48 KB
       if (d->n <= 1024)
-        ro_norm16<4><<<grid, 256, 0, st>>>(q);
+        ro_norm16<4><<<grid, 256, smem, st>>>(q);
       else if (d->n <= 2048)
-        ro_norm16<8><<<grid, 256, 0, st>>>(q);
+        ro_norm16<8><<<grid, 256, smem, st>>>(q);
       else
-        ro_norm16<16><<<grid, 256, 0, st>>>(q);
+        ro_norm16<16><<<grid, 256, smem, st>>>(q);
     }
     return corm::cuda_status("rowops norm");
   }

@@ -327,6 +327,21 @@ int launch_softmax(const corm_vectorop_desc* d, cudaStream_t st, const corm::Dev
       corm::ProfScope prof_("smx_rows<32,8>", st);
       smx_rows<32, 8><<<(p.rows + 7) / 8, 256, 0, st>>>(p);
     }
+  } else if (d->size <= 384) {
+    {
+      corm::ProfScope prof_("smx_rows<16,24>", st);
+      smx_rows<16, 24><<<(p.rows + 15) / 16, 256, 0, st>>>(p);
+    }
+  } else if (d->size <= 512) {
+    {
+      corm::ProfScope prof_("smx_rows<32,16>", st);
+      smx_rows<32, 16><<<(p.rows + 7) / 8, 256, 0, st>>>(p);
+    }
+  } else if (d->size <= 768) {
+    {
+      corm::ProfScope prof_("smx_rows<32,24>", st);
+      smx_rows<32, 24><<<(p.rows + 7) / 8, 256, 0, st>>>(p);
+    }
   } else if (d->size <= 1024) {
     {
       corm::ProfScope prof_("smx_rows<32,32>", st);

@@ -137,7 +137,7 @@ def test_vectorop_vs_oracle(ops, op, act):
     assert np.array_equal(c.cpu().numpy(), exp)
 
 
-@pytest.mark.parametrize("n", [1, 7, 128, 255, 1000, 1024, 2048, 4096, 10000])
+@pytest.mark.parametrize("n", [1, 7, 128, 255, 300, 384, 500, 512, 700, 768, 1000, 1024, 2048, 4096, 10000])
 @pytest.mark.parametrize("mask", [0, "full", "causal"])
 def test_softmax_rows(ops, n, mask):
     rng = np.random.default_rng(n)
