@@ -6,11 +6,14 @@
 //               B hi/lo K-major or MN-major, 128 x 128 bytes, 128-byte swizzle,
 //               no multicast) into a STAGES-deep ring that runs across units
 //   warp 1      TMEM owner (512 columns) and MMA issuer: 16 tcgen05.mma
-//               (128x128x32) per K block into HH / MID / LL; waits for the
+//               (128x128x32) per K block into HH / MID / LL (the K steps past
+//               the job's K, zero-filled, are not issued); waits for the
 //               epilogue to drain TMEM before the next unit (tmem_empty)
-//   warps 2..5  epilogue: tcgen05.ld of the three accumulators, int64
-//               recombine, the job's rounding rule and int16 stores — or, for a
-//               K-split unit, exact int64 atomics into a partial-sum buffer that
+//   warps 2..9  epilogue, two warps per TMEM lane quarter (64 columns each):
+//               tcgen05.ld of the three accumulators, int64 recombine and the
+//               job's rounding rule into registers, TMEM released to the next
+//               unit's MMAs, then the int16 stores — or, for a K-split unit,
+//               exact int64 atomics into a partial-sum buffer that
 //               gemm_finish_kernel rounds afterwards
 // Every mbarrier wait is bounded (sm100::mbar_wait); a timeout leaves an error
 // code in the per-device error word and the CTA unwinds (in-flight TMA loads
@@ -32,7 +35,8 @@ constexpr int TILE_BYTES = BM * BK;  // 16 KB (BM == BN)
 constexpr int STAGE_BYTES = 4 * TILE_BYTES;
 constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
 constexpr uint32_t TMEM_COLS = 512;
-constexpr int THREADS = 192;
+constexpr int EPI_WARPS = 8;
+constexpr int THREADS = 64 + 32 * EPI_WARPS;
 constexpr int NUM_SMS = 148;
 
 struct EpiArgs {
@@ -44,7 +48,7 @@ struct EpiArgs {
   uint64_t img_stride;
   const int16_t* bias;
   uint32_t flags;
-  uint32_t num_kb, a_planes, b_planes, b_mn;
+  uint32_t num_kb, a_planes, b_planes, b_mn, K;
   uint32_t tiles_m, tiles_n, batch, splits, kb_per_split;
   unsigned long long* partial;
   int* err;
@@ -107,7 +111,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       sm100::mbar_init(&empty[s], 1);
     }
     sm100::mbar_init(tmem_full, 1);
-    sm100::mbar_init(tmem_empty, 4);
+    sm100::mbar_init(tmem_empty, EPI_WARPS);
     sm100::mbar_init(mma_done, 1);
     sm100::fence_mbar_init();
   }
@@ -181,8 +185,11 @@ __global__ void __launch_bounds__(THREADS, 1)
         // K step of 32 int8: 32 bytes inside a K-major swizzled row, or 32 rows
         // (4 swizzle atoms of 1024 bytes) of an MN-major tile
         const uint64_t b_step = ep.b_mn ? (uint64_t)(4096 >> 4) : (uint64_t)(32 >> 4);
+        const uint32_t krem = ep.K - kb * BK;  // > 0: K steps beyond it only add zeros
+        const int nks = krem >= (uint32_t)BK ? BK / 32 : (int)((krem + 31) / 32);
 #pragma unroll
         for (int ks = 0; ks < BK / 32; ks++) {
+          if (ks >= nks) break;
           const uint64_t adv = (uint64_t)((ks * 32) >> 4), bdv = b_step * ks;
           const uint32_t acc = (kb != w.kb0 || ks) ? 1u : 0u;
           sm100::mma_i8(acc_hh, d_ahi + adv, d_bhi + bdv, ID_SS, acc);
@@ -198,9 +205,11 @@ __global__ void __launch_bounds__(THREADS, 1)
     sm100::mma_commit(mma_done);
     sm100::mbar_wait(mma_done, 0, nullptr, 0, 200000000ll);
   } else if (warp >= 2) {
-    // ---------------- epilogue
+    // ---------------- epilogue: warp (2 + 4 h + j) reads lane quarter (warp % 4),
+    // columns [64 h, 64 h + 64)
     const int q = warp & 3;  // TMEM lane quarter this warp may access
     const uint32_t lane_addr = (uint32_t)(q * 32) << 16;
+    const int h = (warp - 2) >> 2;
     uint32_t i = 0;
     for (uint32_t u = blockIdx.x; u < units; u += gridDim.x, i++) {
       const Unit w = unit_of(ep, u);
@@ -208,20 +217,20 @@ __global__ void __launch_bounds__(THREADS, 1)
       sm100::tc_fence_after();
       const uint32_t r = w.tile_r + q * 32 + lane;
       const bool row_ok = r < ep.rows;
-      for (int cc = 0; cc < BN; cc += 32) {
-        uint32_t hh[32], mid[32], ll[32];
-        sm100::tmem_ld32(tmem + lane_addr + cc, hh);
-        sm100::tmem_ld32(tmem + lane_addr + BN + cc, mid);
-        sm100::tmem_ld32(tmem + lane_addr + 2 * BN + cc, ll);
-        sm100::tmem_ld_wait();
-        if (cc + 32 >= BN) {  // TMEM drained: the next unit's MMAs may start
-          sm100::tc_fence_before();
-          __syncwarp();
-          if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(sm100::smem_u32(tmem_empty)) : "memory");
-        }
-        if (!row_ok) continue;
-        const uint32_t c0 = w.tile_c + cc;
-        if (ep.partial) {
+      if (ep.partial) {
+        for (int cc = 64 * h; cc < 64 * h + 64; cc += 32) {
+          uint32_t hh[32], mid[32], ll[32];
+          sm100::tmem_ld32(tmem + lane_addr + cc, hh);
+          sm100::tmem_ld32(tmem + lane_addr + BN + cc, mid);
+          sm100::tmem_ld32(tmem + lane_addr + 2 * BN + cc, ll);
+          sm100::tmem_ld_wait();
+          if (cc + 32 >= 64 * h + 64) {  // TMEM drained: the next unit's MMAs may start
+            sm100::tc_fence_before();
+            __syncwarp();
+            if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(sm100::smem_u32(tmem_empty)) : "memory");
+          }
+          if (!row_ok) continue;
+          const uint32_t c0 = w.tile_c + cc;
           unsigned long long* dst = ep.partial + ((uint64_t)w.bz * ep.rows + r) * ep.cols + c0;
 #pragma unroll
           for (int j = 0; j < 32; j++) {
@@ -229,31 +238,52 @@ __global__ void __launch_bounds__(THREADS, 1)
             const int64_t acc = ((int64_t)(int32_t)hh[j] << 16) + ((int64_t)(int32_t)mid[j] << 8) + (int64_t)(int32_t)ll[j];
             atomicAdd(dst + j, (unsigned long long)acc);
           }
-        } else if (ep.mode == 0) {
-          int16_t* dst = ep.out + out_offset(ep, w.bz, r, c0);
-          alignas(16) int16_t v[32];
+        }
+        continue;
+      }
+      // the 64 results of this thread's row as int16 pairs, then TMEM released
+      uint32_t v2[32];
 #pragma unroll
-          for (int j = 0; j < 32; j++) {
-            const int64_t acc = ((int64_t)(int32_t)hh[j] << 16) + ((int64_t)(int32_t)mid[j] << 8) + (int64_t)(int32_t)ll[j];
-            v[j] = finish(acc, ep.flags);
+      for (int half = 0; half < 2; half++) {
+        const int cc = 64 * h + 32 * half;
+        uint32_t hh[32], mid[32], ll[32];
+        sm100::tmem_ld32(tmem + lane_addr + cc, hh);
+        sm100::tmem_ld32(tmem + lane_addr + BN + cc, mid);
+        sm100::tmem_ld32(tmem + lane_addr + 2 * BN + cc, ll);
+        sm100::tmem_ld_wait();
+        const uint32_t c0 = w.tile_c + cc;
+#pragma unroll
+        for (int j = 0; j < 32; j += 2) {
+          int64_t a0 = ((int64_t)(int32_t)hh[j] << 16) + ((int64_t)(int32_t)mid[j] << 8) + (int64_t)(int32_t)ll[j];
+          int64_t a1 = ((int64_t)(int32_t)hh[j + 1] << 16) + ((int64_t)(int32_t)mid[j + 1] << 8) +
+                       (int64_t)(int32_t)ll[j + 1];
+          if (ep.mode == 1 && ep.bias) {
+            if (c0 + j < ep.cols) a0 += (int64_t)ep.bias[c0 + j] << 8;
+            if (c0 + j + 1 < ep.cols) a1 += (int64_t)ep.bias[c0 + j + 1] << 8;
           }
-          if (c0 + 32 <= ep.cols && ((uintptr_t)dst & 15) == 0) {
+          v2[16 * half + j / 2] = (uint32_t)(uint16_t)finish(a0, ep.flags) | ((uint32_t)(uint16_t)finish(a1, ep.flags) << 16);
+        }
+      }
+      sm100::tc_fence_before();
+      __syncwarp();
+      if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(sm100::smem_u32(tmem_empty)) : "memory");
+      if (!row_ok) continue;
+      const uint32_t c0 = w.tile_c + 64 * h;
+      if (ep.mode == 0) {
+        int16_t* dst = ep.out + out_offset(ep, w.bz, r, c0);
+        if (c0 + 64 <= ep.cols && ((uintptr_t)dst & 15) == 0) {
 #pragma unroll
-            for (int j = 0; j < 4; j++) ((int4*)dst)[j] = ((const int4*)v)[j];
-          } else {
-#pragma unroll
-            for (int j = 0; j < 32; j++)
-              if (c0 + j < ep.cols) dst[j] = v[j];
-          }
+          for (int j = 0; j < 8; j++) ((int4*)dst)[j] = make_int4((int)v2[4 * j], (int)v2[4 * j + 1], (int)v2[4 * j + 2], (int)v2[4 * j + 3]);
         } else {
 #pragma unroll
-          for (int j = 0; j < 32; j++) {
-            const uint32_t c = c0 + j;
-            if (c >= ep.cols) continue;
-            int64_t acc = ((int64_t)(int32_t)hh[j] << 16) + ((int64_t)(int32_t)mid[j] << 8) + (int64_t)(int32_t)ll[j];
-            if (ep.bias) acc += (int64_t)ep.bias[c] << 8;
-            ep.out[out_offset(ep, 0, r, c)] = finish(acc, ep.flags);
-          }
+          for (int j = 0; j < 64; j++)
+            if (c0 + j < ep.cols) dst[j] = (int16_t)(v2[j / 2] >> (16 * (j & 1)));
+        }
+      } else {
+#pragma unroll
+        for (int j = 0; j < 64; j++) {
+          const uint32_t c = c0 + j;
+          if (c < ep.cols) ep.out[out_offset(ep, 0, r, c)] = (int16_t)(v2[j / 2] >> (16 * (j & 1)));
         }
       }
     }
@@ -448,6 +478,7 @@ int gemm_i8x4(const GemmJob& j, cudaStream_t stream) {
   ep.a_planes = j.a_planes;
   ep.b_planes = j.b_planes;
   ep.b_mn = j.b_mn;
+  ep.K = j.K ? j.K : j.Kp;
   ep.tiles_m = (j.rows + BM - 1) / BM;
   ep.tiles_n = (j.cols + BN - 1) / BN;
   ep.batch = j.batch;
