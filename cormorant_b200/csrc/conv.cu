@@ -13,6 +13,8 @@
 // epilogue adds the bias and stores NCHW (a warp writes 32 consecutive pixels
 // of one channel).  Depthwise: a direct CUDA-core kernel (K = kh*kw is far too
 // short for the tensor cores).
+#include <algorithm>
+
 #include "corm_common.cuh"
 #include "gemm_i8x4.h"
 
@@ -141,6 +143,75 @@ __global__ void __launch_bounds__(256) conv_depthwise(ConvArgs a) {
   }
 }
 
+// Depthwise on shared-memory planes: a CTA takes G (n, m) planes at a time;
+// each plane's input window (rows -pt .. -pt + SH - 1, columns -pl .. -pl +
+// SW - 1, zeros outside the image) is staged in shared memory (a warp per
+// row, lanes along it), its kh x kw taps too; TPP threads per plane then
+// compute the plane's outputs (32-bit products, int64 sums seeded with
+// bias << 8) and store them contiguously.
+template <int KH_, int KW_>
+__global__ void __launch_bounds__(256) conv_dw_plane(ConvArgs a, uint32_t SH, uint32_t SW, uint32_t G, uint32_t TPP) {
+  extern __shared__ int16_t s_in[];  // [G][SH][SW], then [G][KH*KW] taps
+  const uint32_t KH = KH_ ? KH_ : a.KH, KW = KW_ ? KW_ : a.KW, KK = KH * KW;
+  const uint32_t P = a.OH * a.OW, PS = SH * SW;
+  int16_t* s_w = s_in + (size_t)G * PS;
+  const uint64_t planes = (uint64_t)a.batch * a.M;
+  const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = blockDim.x >> 5;
+  const uint32_t g = threadIdx.x / TPP, t = threadIdx.x - g * TPP;
+  for (uint64_t base = (uint64_t)blockIdx.x * G; base < planes; base += (uint64_t)gridDim.x * G) {
+    for (uint32_t row = warp; row < G * SH; row += nwarps) {
+      const uint32_t gg = row / SH, r = row - gg * SH;
+      const uint64_t plane = base + gg;
+      const int ih = (int)r - (int)a.pt;
+      int16_t* dst = s_in + (size_t)gg * PS + (size_t)r * SW;
+      const bool live = plane < planes && ih >= 0 && ih < (int)a.H;
+      const int16_t* src = live ? a.x + ((plane / a.M) * a.C + plane % a.M) * (uint64_t)a.H * a.W + (uint64_t)ih * a.W
+                                : nullptr;
+      for (uint32_t c = lane; c < SW; c += 32) {
+        const int iw = (int)c - (int)a.pl;
+        dst[c] = (live && iw >= 0 && iw < (int)a.W) ? __ldg(src + iw) : (int16_t)0;
+      }
+    }
+    for (uint32_t i = threadIdx.x; i < G * KK; i += blockDim.x) {
+      const uint32_t gg = i / KK, tap = i - gg * KK;
+      const uint64_t plane = base + gg;
+      s_w[i] = plane < planes ? __ldg(a.w + w_offset(a, (uint32_t)(plane % a.M), 0, tap / KW, tap % KW)) : (int16_t)0;
+    }
+    __syncthreads();
+    const uint64_t plane = base + g;
+    if (g < G && plane < planes) {
+      const uint32_t m = (uint32_t)(plane % a.M), n = (uint32_t)(plane / a.M);
+      const int16_t* xin = s_in + (size_t)g * PS;
+      const int16_t* wt = s_w + (size_t)g * KK;
+      int32_t wr[KH_ && KW_ ? KH_ * KW_ : 1];
+      if (KH_ && KW_) {
+#pragma unroll
+        for (int q = 0; q < (KH_ && KW_ ? KH_ * KW_ : 1); q++) wr[q] = wt[q];
+      }
+      const int64_t b0 = a.bias ? (int64_t)a.bias[m] << 8 : 0;
+      int16_t* yp = a.y + (uint64_t)n * a.M * P + y_chan(a, m);
+      for (uint32_t pp = t; pp < P; pp += TPP) {
+        const uint32_t oh = pp / a.OW, ow = pp - oh * a.OW;
+        const int16_t* x0 = xin + (size_t)(oh * a.sh) * SW + ow * a.sw;
+        int64_t acc = b0;
+        if (KH_ && KW_) {
+#pragma unroll
+          for (int i = 0; i < KH_; i++)
+#pragma unroll
+            for (int j = 0; j < KW_; j++)
+              acc += (int64_t)((int32_t)x0[i * a.dh * SW + j * a.dw] * wr[i * KW_ + j]);
+        } else {
+          for (uint32_t i = 0; i < KH; i++)
+            for (uint32_t j = 0; j < KW; j++)
+              acc += (int64_t)((int32_t)x0[i * a.dh * SW + j * a.dw] * (int32_t)wt[i * KW + j]);
+        }
+        yp[pp] = conv_finish(acc, a.flags);
+      }
+    }
+    __syncthreads();
+  }
+}
+
 struct ConvPlan {
   uint32_t K, Kp, Ptot;
   size_t a_bytes, b_bytes, partial_bytes, bytes;
@@ -219,6 +290,25 @@ extern "C" int corm_conv(const corm_conv_desc* d, corm_stream_t stream) {
   a.y_gs = d->y_gs;
   if (d->is_depthwise) {
     const uint64_t total = (uint64_t)d->batch * d->out_ch * P;
+    // staged planes: the input window the outputs read, padded with zeros
+    const uint32_t SH = (d->out_h - 1) * d->stride_h + (d->kh - 1) * d->dilation_h + 1;
+    const uint32_t SW = (d->out_w - 1) * d->stride_w + (d->kw - 1) * d->dilation_w + 1;
+    const uint32_t TPP = P >= 256 ? 256u : (P + 31u) / 32u * 32u;
+    const uint32_t G = 256u / TPP;
+    const size_t smem = ((size_t)G * SH * SW + (size_t)G * d->kh * d->kw) * sizeof(int16_t);
+    if (smem <= 96u * 1024u) {
+      const uint64_t planes = (uint64_t)d->batch * d->out_ch;
+      const unsigned grid = (unsigned)std::min<uint64_t>((planes + G - 1) / G, 148ull * 8ull);
+      corm::ProfScope prof_("conv_dw_plane", st);
+      if (d->kh == 3 && d->kw == 3) {
+        cudaFuncSetAttribute(conv_dw_plane<3, 3>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        conv_dw_plane<3, 3><<<grid, 256, smem, st>>>(a, SH, SW, G, TPP);
+      } else {
+        cudaFuncSetAttribute(conv_dw_plane<0, 0>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        conv_dw_plane<0, 0><<<grid, 256, smem, st>>>(a, SH, SW, G, TPP);
+      }
+      return corm::cuda_status("conv depthwise");
+    }
     {
       corm::ProfScope prof_("conv_depthwise", st);
       conv_depthwise<<<corm_blocks(total, 256, 148u * 16u), 256, 0, st>>>(a);

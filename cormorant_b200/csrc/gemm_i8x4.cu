@@ -279,11 +279,16 @@ __global__ void __launch_bounds__(THREADS, 1)
           for (int j = 0; j < 64; j++)
             if (c0 + j < ep.cols) dst[j] = (int16_t)(v2[j / 2] >> (16 * (j & 1)));
         }
-      } else {
+      } else {  // NCHW: the row's image and pixel once, the channel offset per column
+        const uint32_t n = r / ep.P, p = r - n * ep.P;
+        int16_t* base = ep.out + (uint64_t)n * ep.img_stride + p;
 #pragma unroll
         for (int j = 0; j < 64; j++) {
           const uint32_t c = c0 + j;
-          if (c < ep.cols) ep.out[out_offset(ep, 0, r, c)] = (int16_t)(v2[j / 2] >> (16 * (j & 1)));
+          if (c >= ep.cols) break;
+          const uint64_t coff = ep.y_cn ? (uint64_t)(c % ep.y_cn) * ep.y_cs + (uint64_t)(c / ep.y_cn) * ep.y_gs
+                                        : (uint64_t)c * ep.y_cs;
+          base[coff] = (int16_t)(v2[j / 2] >> (16 * (j & 1)));
         }
       }
     }
