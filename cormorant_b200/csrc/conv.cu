@@ -52,24 +52,38 @@ __device__ __forceinline__ uint64_t y_chan(const ConvArgs& a, uint32_t m) {
   return a.y_cn ? (uint64_t)(m % a.y_cn) * a.CS + (uint64_t)(m / a.y_cn) * a.y_gs : (uint64_t)m * a.CS;
 }
 
-// im2col of x into the hi / lo planes [Ptot][Kp]: a 64 (pixels) x 64 (K) tile per CTA.
+// im2col of x into the hi / lo planes [Ptot][Kp]: a 64 (pixels) x 64 (K) tile
+// per CTA.  A thread keeps one pixel (its image, output row and column worked
+// out once) and gathers 16 K entries, eight loads in flight at a time.
 __global__ void __launch_bounds__(256) im2col_split(ConvArgs a, uint32_t Ptot, uint32_t K, uint32_t Kp, int8_t* hi,
                                                     uint8_t* lo) {
   __shared__ int16_t tile[64][65];  // [p][k]
   const uint32_t p0 = blockIdx.x * 64, k0 = blockIdx.y * 64;
   const uint32_t P = a.OH * a.OW, KK = a.KH * a.KW;
-  for (int t = threadIdx.x; t < 64 * 64; t += 256) {
-    const uint32_t pr = t % 64, kr = t / 64;
-    const uint32_t p = p0 + pr, k = k0 + kr;
-    int16_t v = 0;
-    if (p < Ptot && k < K) {
-      const uint32_t n = p / P, pp = p % P, oh = pp / a.OW, ow = pp % a.OW;
-      const uint32_t c = k / KK, tap = k % KK, i = tap / a.KW, j = tap % a.KW;
-      const int ih = (int)(oh * a.sh + i * a.dh) - (int)a.pt, iw = (int)(ow * a.sw + j * a.dw) - (int)a.pl;
-      if (ih >= 0 && ih < (int)a.H && iw >= 0 && iw < (int)a.W)
-        v = __ldg(a.x + (((uint64_t)n * a.C + c) * a.H + ih) * a.W + iw);
+  const uint32_t pr = threadIdx.x % 64, kr0 = threadIdx.x / 64;
+  const uint32_t p = p0 + pr;
+  const bool pok = p < Ptot;
+  const uint32_t n = pok ? p / P : 0, pp = pok ? p - n * P : 0;
+  const uint32_t oh = pp / a.OW, ow = pp - oh * a.OW;
+  const int ih0 = (int)(oh * a.sh) - (int)a.pt, iw0 = (int)(ow * a.sw) - (int)a.pl;
+  const int16_t* xn = a.x + (uint64_t)n * a.C * a.H * a.W;
+#pragma unroll
+  for (int half = 0; half < 2; half++) {
+    int16_t v[8];
+#pragma unroll
+    for (int u = 0; u < 8; u++) {
+      const uint32_t kr = kr0 + 4 * (8 * half + u), k = k0 + kr;
+      v[u] = 0;
+      if (pok && k < K) {
+        const uint32_t c = KK == 1 ? k : k / KK, tap = KK == 1 ? 0 : k - c * KK;
+        const uint32_t i = KK == 1 ? 0 : tap / a.KW, j = KK == 1 ? 0 : tap - i * a.KW;
+        const int ih = ih0 + (int)(i * a.dh), iw = iw0 + (int)(j * a.dw);
+        if (ih >= 0 && ih < (int)a.H && iw >= 0 && iw < (int)a.W)
+          v[u] = __ldg(xn + ((uint64_t)c * a.H + ih) * a.W + iw);
+      }
     }
-    tile[pr][kr] = v;
+#pragma unroll
+    for (int u = 0; u < 8; u++) tile[pr][kr0 + 4 * (8 * half + u)] = v[u];
   }
   __syncthreads();
   for (int t = threadIdx.x; t < 64 * 8; t += 256) {
@@ -145,8 +159,8 @@ __global__ void __launch_bounds__(256) conv_depthwise(ConvArgs a) {
 
 // Depthwise on shared-memory planes: a CTA takes G (n, m) planes at a time;
 // each plane's input window (rows -pt .. -pt + SH - 1, columns -pl .. -pl +
-// SW - 1, zeros outside the image) is staged in shared memory (a warp per
-// row, lanes along it), its kh x kw taps too; TPP threads per plane then
+// SW - 1, zeros outside the image) is staged in shared memory (coalesced,
+// eight loads in flight per thread), its kh x kw taps too; TPP threads per plane then
 // compute the plane's outputs (32-bit products, int64 sums seeded with
 // bias << 8) and store them contiguously.
 template <int KH_, int KW_>
@@ -156,20 +170,34 @@ __global__ void __launch_bounds__(256) conv_dw_plane(ConvArgs a, uint32_t SH, ui
   const uint32_t P = a.OH * a.OW, PS = SH * SW;
   int16_t* s_w = s_in + (size_t)G * PS;
   const uint64_t planes = (uint64_t)a.batch * a.M;
-  const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = blockDim.x >> 5;
   const uint32_t g = threadIdx.x / TPP, t = threadIdx.x - g * TPP;
+  __shared__ const int16_t* s_src[8];
   for (uint64_t base = (uint64_t)blockIdx.x * G; base < planes; base += (uint64_t)gridDim.x * G) {
-    for (uint32_t row = warp; row < G * SH; row += nwarps) {
-      const uint32_t gg = row / SH, r = row - gg * SH;
-      const uint64_t plane = base + gg;
-      const int ih = (int)r - (int)a.pt;
-      int16_t* dst = s_in + (size_t)gg * PS + (size_t)r * SW;
-      const bool live = plane < planes && ih >= 0 && ih < (int)a.H;
-      const int16_t* src = live ? a.x + ((plane / a.M) * a.C + plane % a.M) * (uint64_t)a.H * a.W + (uint64_t)ih * a.W
-                                : nullptr;
-      for (uint32_t c = lane; c < SW; c += 32) {
-        const int iw = (int)c - (int)a.pl;
-        dst[c] = (live && iw >= 0 && iw < (int)a.W) ? __ldg(src + iw) : (int16_t)0;
+    if (threadIdx.x < G) {
+      const uint64_t plane = base + threadIdx.x;
+      s_src[threadIdx.x] = plane < planes ? a.x + ((plane / a.M) * a.C + plane % a.M) * (uint64_t)a.H * a.W : nullptr;
+    }
+    __syncthreads();
+    // the padded windows as one flat index space; eight independent loads per
+    // thread in flight before their stores
+    const uint32_t total = G * PS;
+    for (uint32_t i0 = threadIdx.x; i0 < total; i0 += blockDim.x * 8u) {
+      int16_t v[8];
+#pragma unroll
+      for (int u = 0; u < 8; u++) {
+        const uint32_t i = i0 + u * blockDim.x;
+        v[u] = 0;
+        if (i < total) {
+          const uint32_t gg = i / PS, rem = i - gg * PS, r = rem / SW, c = rem - r * SW;
+          const int ih = (int)r - (int)a.pt, iw = (int)c - (int)a.pl;
+          const int16_t* src = s_src[gg];
+          if (src && ih >= 0 && ih < (int)a.H && iw >= 0 && iw < (int)a.W) v[u] = __ldg(src + (uint64_t)ih * a.W + iw);
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < 8; u++) {
+        const uint32_t i = i0 + u * blockDim.x;
+        if (i < total) s_in[i] = v[u];
       }
     }
     for (uint32_t i = threadIdx.x; i < G * KK; i += blockDim.x) {
