@@ -159,11 +159,11 @@ __global__ void __launch_bounds__(256) conv_depthwise(ConvArgs a) {
 
 // Depthwise on shared-memory planes: a CTA takes G (n, m) planes at a time;
 // each plane's input window (rows -pt .. -pt + SH - 1, columns -pl .. -pl +
-// SW - 1, zeros outside the image) is staged in shared memory (coalesced,
-// eight loads in flight per thread), its kh x kw taps too; TPP threads per plane then
+// SW - 1, zeros outside the image) is staged in shared memory (a warp per
+// four rows, lanes along them), its kh x kw taps too; TPP threads per plane then
 // compute the plane's outputs (32-bit products, int64 sums seeded with
 // bias << 8) and store them contiguously.
-template <int KH_, int KW_>
+template <int KH_, int KW_, int S_>
 __global__ void __launch_bounds__(256) conv_dw_plane(ConvArgs a, uint32_t SH, uint32_t SW, uint32_t G, uint32_t TPP) {
   extern __shared__ int16_t s_in[];  // [G][SH][SW], then [G][KH*KW] taps
   const uint32_t KH = KH_ ? KH_ : a.KH, KW = KW_ ? KW_ : a.KW, KK = KH * KW;
@@ -178,26 +178,39 @@ __global__ void __launch_bounds__(256) conv_dw_plane(ConvArgs a, uint32_t SH, ui
       s_src[threadIdx.x] = plane < planes ? a.x + ((plane / a.M) * a.C + plane % a.M) * (uint64_t)a.H * a.W : nullptr;
     }
     __syncthreads();
-    // the padded windows as one flat index space; eight independent loads per
-    // thread in flight before their stores
-    const uint32_t total = G * PS;
-    for (uint32_t i0 = threadIdx.x; i0 < total; i0 += blockDim.x * 8u) {
-      int16_t v[8];
+    // the padded windows row by row: a warp takes four rows at a time, lanes
+    // along the columns, so every lane has up to 4 * ceil(SW / 32) loads in flight
+    const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = blockDim.x >> 5;
+    const uint32_t nrows = G * SH;
+    for (uint32_t row0 = warp * 4u; row0 < nrows; row0 += nwarps * 4u) {
+      int16_t v[4][4];
+      const int16_t* srow[4];
 #pragma unroll
-      for (int u = 0; u < 8; u++) {
-        const uint32_t i = i0 + u * blockDim.x;
-        v[u] = 0;
-        if (i < total) {
-          const uint32_t gg = i / PS, rem = i - gg * PS, r = rem / SW, c = rem - r * SW;
-          const int ih = (int)r - (int)a.pt, iw = (int)c - (int)a.pl;
-          const int16_t* src = s_src[gg];
-          if (src && ih >= 0 && ih < (int)a.H && iw >= 0 && iw < (int)a.W) v[u] = __ldg(src + (uint64_t)ih * a.W + iw);
+      for (int rr = 0; rr < 4; rr++) {
+        const uint32_t row = row0 + rr;
+        srow[rr] = nullptr;
+        if (row < nrows) {
+          const uint32_t gg = row / SH, r = row - gg * SH;
+          const int ih = (int)r - (int)a.pt;
+          if (s_src[gg] && ih >= 0 && ih < (int)a.H) srow[rr] = s_src[gg] + (uint64_t)ih * a.W - (int)a.pl;
         }
       }
+      for (uint32_t c0 = 0; c0 < SW; c0 += 128u) {
 #pragma unroll
-      for (int u = 0; u < 8; u++) {
-        const uint32_t i = i0 + u * blockDim.x;
-        if (i < total) s_in[i] = v[u];
+        for (int rr = 0; rr < 4; rr++)
+#pragma unroll
+          for (int cc = 0; cc < 4; cc++) {
+            const uint32_t c = c0 + cc * 32u + lane;
+            const int iw = (int)c - (int)a.pl;
+            v[rr][cc] = (srow[rr] && c < SW && iw >= 0 && iw < (int)a.W) ? __ldg(srow[rr] + c) : (int16_t)0;
+          }
+#pragma unroll
+        for (int rr = 0; rr < 4; rr++)
+#pragma unroll
+          for (int cc = 0; cc < 4; cc++) {
+            const uint32_t c = c0 + cc * 32u + lane;
+            if (row0 + rr < nrows && c < SW) s_in[(size_t)(row0 + rr) * SW + c] = v[rr][cc];
+          }
       }
     }
     for (uint32_t i = threadIdx.x; i < G * KK; i += blockDim.x) {
@@ -211,29 +224,61 @@ __global__ void __launch_bounds__(256) conv_dw_plane(ConvArgs a, uint32_t SH, ui
       const uint32_t m = (uint32_t)(plane % a.M), n = (uint32_t)(plane / a.M);
       const int16_t* xin = s_in + (size_t)g * PS;
       const int16_t* wt = s_w + (size_t)g * KK;
-      int32_t wr[KH_ && KW_ ? KH_ * KW_ : 1];
-      if (KH_ && KW_) {
-#pragma unroll
-        for (int q = 0; q < (KH_ && KW_ ? KH_ * KW_ : 1); q++) wr[q] = wt[q];
-      }
       const int64_t b0 = a.bias ? (int64_t)a.bias[m] << 8 : 0;
       int16_t* yp = a.y + (uint64_t)n * a.M * P + y_chan(a, m);
-      for (uint32_t pp = t; pp < P; pp += TPP) {
-        const uint32_t oh = pp / a.OW, ow = pp - oh * a.OW;
-        const int16_t* x0 = xin + (size_t)(oh * a.sh) * SW + ow * a.sw;
-        int64_t acc = b0;
+      if (S_ > 0) {
+        // 3x3, dilation 1, stride S_: a thread takes a column of NR outputs and
+        // reads the (NR - 1) S_ + 3 input rows they share once
+        constexpr int NR = 4, R = (NR - 1) * (S_ > 0 ? S_ : 1) + 3;
+        int32_t wr[9];
+#pragma unroll
+        for (int q = 0; q < 9; q++) wr[q] = wt[q];
+        const uint32_t items = a.OW * ((a.OH + NR - 1) / NR);
+        for (uint32_t it = t; it < items; it += TPP) {
+          const uint32_t ob = it / a.OW, ow = it - ob * a.OW, oh0 = ob * NR;
+          const int16_t* x0 = xin + (size_t)(oh0 * S_) * SW + ow * S_;
+          const uint32_t rows_ok = SH - oh0 * S_;  // input rows left in the window
+          int64_t acc[NR];
+#pragma unroll
+          for (int r = 0; r < NR; r++) acc[r] = b0;
+#pragma unroll
+          for (int q = 0; q < R; q++) {
+            if ((uint32_t)q >= rows_ok) break;
+            const int32_t x_0 = x0[q * SW], x_1 = x0[q * SW + 1], x_2 = x0[q * SW + 2];
+#pragma unroll
+            for (int r = 0; r < NR; r++) {
+              const int i = q - r * S_;
+              if (i >= 0 && i < 3)
+                acc[r] += (int64_t)(x_0 * wr[3 * i]) + (int64_t)(x_1 * wr[3 * i + 1]) + (int64_t)(x_2 * wr[3 * i + 2]);
+            }
+          }
+#pragma unroll
+          for (int r = 0; r < NR; r++)
+            if (oh0 + r < a.OH) yp[(oh0 + r) * a.OW + ow] = conv_finish(acc[r], a.flags);
+        }
+      } else {
+        int32_t wr[KH_ && KW_ ? KH_ * KW_ : 1];
         if (KH_ && KW_) {
 #pragma unroll
-          for (int i = 0; i < KH_; i++)
-#pragma unroll
-            for (int j = 0; j < KW_; j++)
-              acc += (int64_t)((int32_t)x0[i * a.dh * SW + j * a.dw] * wr[i * KW_ + j]);
-        } else {
-          for (uint32_t i = 0; i < KH; i++)
-            for (uint32_t j = 0; j < KW; j++)
-              acc += (int64_t)((int32_t)x0[i * a.dh * SW + j * a.dw] * (int32_t)wt[i * KW + j]);
+          for (int q = 0; q < (KH_ && KW_ ? KH_ * KW_ : 1); q++) wr[q] = wt[q];
         }
-        yp[pp] = conv_finish(acc, a.flags);
+        for (uint32_t pp = t; pp < P; pp += TPP) {
+          const uint32_t oh = pp / a.OW, ow = pp - oh * a.OW;
+          const int16_t* x0 = xin + (size_t)(oh * a.sh) * SW + ow * a.sw;
+          int64_t acc = b0;
+          if (KH_ && KW_) {
+#pragma unroll
+            for (int i = 0; i < KH_; i++)
+#pragma unroll
+              for (int j = 0; j < KW_; j++)
+                acc += (int64_t)((int32_t)x0[i * a.dh * SW + j * a.dw] * wr[i * KW_ + j]);
+          } else {
+            for (uint32_t i = 0; i < KH; i++)
+              for (uint32_t j = 0; j < KW; j++)
+                acc += (int64_t)((int32_t)x0[i * a.dh * SW + j * a.dw] * (int32_t)wt[i * KW + j]);
+          }
+          yp[pp] = conv_finish(acc, a.flags);
+        }
       }
     }
     __syncthreads();
@@ -328,13 +373,21 @@ extern "C" int corm_conv(const corm_conv_desc* d, corm_stream_t stream) {
       const uint64_t planes = (uint64_t)d->batch * d->out_ch;
       const unsigned grid = (unsigned)std::min<uint64_t>((planes + G - 1) / G, 148ull * 8ull);
       corm::ProfScope prof_("conv_dw_plane", st);
-      if (d->kh == 3 && d->kw == 3) {
-        cudaFuncSetAttribute(conv_dw_plane<3, 3>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        conv_dw_plane<3, 3><<<grid, 256, smem, st>>>(a, SH, SW, G, TPP);
-      } else {
-        cudaFuncSetAttribute(conv_dw_plane<0, 0>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        conv_dw_plane<0, 0><<<grid, 256, smem, st>>>(a, SH, SW, G, TPP);
-      }
+      const bool unit_dil = d->dilation_h == 1 && d->dilation_w == 1;
+      const bool k3 = d->kh == 3 && d->kw == 3;
+      const uint32_t s_eq = d->stride_h == d->stride_w ? d->stride_h : 0;
+      auto launch = [&](auto kern) {
+        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        kern<<<grid, 256, smem, st>>>(a, SH, SW, G, TPP);
+      };
+      if (k3 && unit_dil && s_eq == 1)
+        launch(conv_dw_plane<3, 3, 1>);
+      else if (k3 && unit_dil && s_eq == 2)
+        launch(conv_dw_plane<3, 3, 2>);
+      else if (k3)
+        launch(conv_dw_plane<3, 3, 0>);
+      else
+        launch(conv_dw_plane<0, 0, 0>);
       return corm::cuda_status("conv depthwise");
     }
     {
