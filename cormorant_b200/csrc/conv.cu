@@ -157,30 +157,38 @@ __global__ void __launch_bounds__(256) conv_depthwise(ConvArgs a) {
   }
 }
 
-// Depthwise on shared-memory planes: a CTA takes G (n, m) planes at a time;
-// each plane's input window (rows -pt .. -pt + SH - 1, columns -pl .. -pl +
-// SW - 1, zeros outside the image) is staged in shared memory (a warp per
-// four rows, lanes along them), its kh x kw taps too; TPP threads per plane then
-// compute the plane's outputs (32-bit products, int64 sums seeded with
-// bias << 8) and store them contiguously.
+// Depthwise on shared-memory planes: a CTA takes G (n, m) planes at a time
+// (G sized so the staged windows fill about 32 KB); each plane's input window
+// (rows -pt .. -pt + SH - 1, columns -pl .. -pl + SW - 1, zeros outside the
+// image) is staged in shared memory (a warp per four rows, lanes along them),
+// the taps too; then the CTA's threads walk the G planes' outputs.  3x3
+// kernels of dilation 1 and stride S_ take columns of four outputs that share
+// their input rows; other shapes one output per step.  32-bit products, int64
+// sums seeded with bias << 8.
+constexpr uint32_t kDwMaxG = 64;
 template <int KH_, int KW_, int S_>
-__global__ void __launch_bounds__(256) conv_dw_plane(ConvArgs a, uint32_t SH, uint32_t SW, uint32_t G, uint32_t TPP) {
+__global__ void __launch_bounds__(256) conv_dw_plane(ConvArgs a, uint32_t SH, uint32_t SW, uint32_t G) {
   extern __shared__ int16_t s_in[];  // [G][SH][SW], then [G][KH*KW] taps
+  __shared__ const int16_t* s_src[kDwMaxG];
+  __shared__ int16_t* s_yp[kDwMaxG];
+  __shared__ int64_t s_b0[kDwMaxG];
   const uint32_t KH = KH_ ? KH_ : a.KH, KW = KW_ ? KW_ : a.KW, KK = KH * KW;
   const uint32_t P = a.OH * a.OW, PS = SH * SW;
   int16_t* s_w = s_in + (size_t)G * PS;
   const uint64_t planes = (uint64_t)a.batch * a.M;
-  const uint32_t g = threadIdx.x / TPP, t = threadIdx.x - g * TPP;
-  __shared__ const int16_t* s_src[8];
+  const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = blockDim.x >> 5;
+  constexpr int NR = 4;
+  const uint32_t items = S_ > 0 ? a.OW * ((a.OH + NR - 1) / NR) : P;
   for (uint64_t base = (uint64_t)blockIdx.x * G; base < planes; base += (uint64_t)gridDim.x * G) {
     if (threadIdx.x < G) {
       const uint64_t plane = base + threadIdx.x;
-      s_src[threadIdx.x] = plane < planes ? a.x + ((plane / a.M) * a.C + plane % a.M) * (uint64_t)a.H * a.W : nullptr;
+      const bool live = plane < planes;
+      const uint32_t m = live ? (uint32_t)(plane % a.M) : 0u, n = live ? (uint32_t)(plane / a.M) : 0u;
+      s_src[threadIdx.x] = live ? a.x + ((uint64_t)n * a.C + m) * (uint64_t)a.H * a.W : nullptr;
+      s_yp[threadIdx.x] = live ? a.y + (uint64_t)n * a.M * P + y_chan(a, m) : nullptr;
+      s_b0[threadIdx.x] = live && a.bias ? (int64_t)a.bias[m] << 8 : 0;
     }
     __syncthreads();
-    // the padded windows row by row: a warp takes four rows at a time, lanes
-    // along the columns, so every lane has up to 4 * ceil(SW / 32) loads in flight
-    const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = blockDim.x >> 5;
     const uint32_t nrows = G * SH;
     for (uint32_t row0 = warp * 4u; row0 < nrows; row0 += nwarps * 4u) {
       int16_t v[4][4];
@@ -192,7 +200,7 @@ __global__ void __launch_bounds__(256) conv_dw_plane(ConvArgs a, uint32_t SH, ui
         if (row < nrows) {
           const uint32_t gg = row / SH, r = row - gg * SH;
           const int ih = (int)r - (int)a.pt;
-          if (s_src[gg] && ih >= 0 && ih < (int)a.H) srow[rr] = s_src[gg] + (uint64_t)ih * a.W - (int)a.pl;
+          if (s_src[gg] && ih >= 0 && ih < (int)a.H) srow[rr] = s_src[gg] + (int64_t)ih * a.W - (int64_t)a.pl;
         }
       }
       for (uint32_t c0 = 0; c0 < SW; c0 += 128u) {
@@ -219,66 +227,47 @@ __global__ void __launch_bounds__(256) conv_dw_plane(ConvArgs a, uint32_t SH, ui
       s_w[i] = plane < planes ? __ldg(a.w + w_offset(a, (uint32_t)(plane % a.M), 0, tap / KW, tap % KW)) : (int16_t)0;
     }
     __syncthreads();
-    const uint64_t plane = base + g;
-    if (g < G && plane < planes) {
-      const uint32_t m = (uint32_t)(plane % a.M), n = (uint32_t)(plane / a.M);
+    const uint32_t work = G * items;
+    for (uint32_t idx = threadIdx.x; idx < work; idx += blockDim.x) {
+      const uint32_t g = idx / items, it = idx - g * items;
+      int16_t* yp = s_yp[g];
+      if (!yp) continue;
       const int16_t* xin = s_in + (size_t)g * PS;
       const int16_t* wt = s_w + (size_t)g * KK;
-      const int64_t b0 = a.bias ? (int64_t)a.bias[m] << 8 : 0;
-      int16_t* yp = a.y + (uint64_t)n * a.M * P + y_chan(a, m);
+      const int64_t b0 = s_b0[g];
       if (S_ > 0) {
-        // 3x3, dilation 1, stride S_: a thread takes a column of NR outputs and
-        // reads the (NR - 1) S_ + 3 input rows they share once
-        constexpr int NR = 4, R = (NR - 1) * (S_ > 0 ? S_ : 1) + 3;
+        constexpr int R = (NR - 1) * (S_ > 0 ? S_ : 1) + 3;
+        const uint32_t ob = it / a.OW, ow = it - ob * a.OW, oh0 = ob * NR;
+        const int16_t* x0 = xin + (size_t)(oh0 * S_) * SW + ow * S_;
+        const uint32_t rows_ok = SH - oh0 * S_;  // input rows left in the window
         int32_t wr[9];
 #pragma unroll
         for (int q = 0; q < 9; q++) wr[q] = wt[q];
-        const uint32_t items = a.OW * ((a.OH + NR - 1) / NR);
-        for (uint32_t it = t; it < items; it += TPP) {
-          const uint32_t ob = it / a.OW, ow = it - ob * a.OW, oh0 = ob * NR;
-          const int16_t* x0 = xin + (size_t)(oh0 * S_) * SW + ow * S_;
-          const uint32_t rows_ok = SH - oh0 * S_;  // input rows left in the window
-          int64_t acc[NR];
+        int64_t acc[NR];
 #pragma unroll
-          for (int r = 0; r < NR; r++) acc[r] = b0;
+        for (int r = 0; r < NR; r++) acc[r] = b0;
 #pragma unroll
-          for (int q = 0; q < R; q++) {
-            if ((uint32_t)q >= rows_ok) break;
-            const int32_t x_0 = x0[q * SW], x_1 = x0[q * SW + 1], x_2 = x0[q * SW + 2];
+        for (int q = 0; q < R; q++) {
+          if ((uint32_t)q >= rows_ok) break;
+          const int32_t x_0 = x0[q * SW], x_1 = x0[q * SW + 1], x_2 = x0[q * SW + 2];
 #pragma unroll
-            for (int r = 0; r < NR; r++) {
-              const int i = q - r * S_;
-              if (i >= 0 && i < 3)
-                acc[r] += (int64_t)(x_0 * wr[3 * i]) + (int64_t)(x_1 * wr[3 * i + 1]) + (int64_t)(x_2 * wr[3 * i + 2]);
-            }
+          for (int r = 0; r < NR; r++) {
+            const int i = q - r * S_;
+            if (i >= 0 && i < 3)
+              acc[r] += (int64_t)(x_0 * wr[3 * i]) + (int64_t)(x_1 * wr[3 * i + 1]) + (int64_t)(x_2 * wr[3 * i + 2]);
           }
-#pragma unroll
-          for (int r = 0; r < NR; r++)
-            if (oh0 + r < a.OH) yp[(oh0 + r) * a.OW + ow] = conv_finish(acc[r], a.flags);
         }
+#pragma unroll
+        for (int r = 0; r < NR; r++)
+          if (oh0 + r < a.OH) yp[(oh0 + r) * a.OW + ow] = conv_finish(acc[r], a.flags);
       } else {
-        int32_t wr[KH_ && KW_ ? KH_ * KW_ : 1];
-        if (KH_ && KW_) {
-#pragma unroll
-          for (int q = 0; q < (KH_ && KW_ ? KH_ * KW_ : 1); q++) wr[q] = wt[q];
-        }
-        for (uint32_t pp = t; pp < P; pp += TPP) {
-          const uint32_t oh = pp / a.OW, ow = pp - oh * a.OW;
-          const int16_t* x0 = xin + (size_t)(oh * a.sh) * SW + ow * a.sw;
-          int64_t acc = b0;
-          if (KH_ && KW_) {
-#pragma unroll
-            for (int i = 0; i < KH_; i++)
-#pragma unroll
-              for (int j = 0; j < KW_; j++)
-                acc += (int64_t)((int32_t)x0[i * a.dh * SW + j * a.dw] * wr[i * KW_ + j]);
-          } else {
-            for (uint32_t i = 0; i < KH; i++)
-              for (uint32_t j = 0; j < KW; j++)
-                acc += (int64_t)((int32_t)x0[i * a.dh * SW + j * a.dw] * (int32_t)wt[i * KW + j]);
-          }
-          yp[pp] = conv_finish(acc, a.flags);
-        }
+        const uint32_t oh = it / a.OW, ow = it - oh * a.OW;
+        const int16_t* x0 = xin + (size_t)(oh * a.sh) * SW + ow * a.sw;
+        int64_t acc = b0;
+        for (uint32_t i = 0; i < KH; i++)
+          for (uint32_t j = 0; j < KW; j++)
+            acc += (int64_t)((int32_t)x0[i * a.dh * SW + j * a.dw] * (int32_t)wt[i * KW + j]);
+        yp[it] = conv_finish(acc, a.flags);
       }
     }
     __syncthreads();
@@ -366,9 +355,9 @@ extern "C" int corm_conv(const corm_conv_desc* d, corm_stream_t stream) {
     // staged planes: the input window the outputs read, padded with zeros
     const uint32_t SH = (d->out_h - 1) * d->stride_h + (d->kh - 1) * d->dilation_h + 1;
     const uint32_t SW = (d->out_w - 1) * d->stride_w + (d->kw - 1) * d->dilation_w + 1;
-    const uint32_t TPP = P >= 256 ? 256u : (P + 31u) / 32u * 32u;
-    const uint32_t G = 256u / TPP;
-    const size_t smem = ((size_t)G * SH * SW + (size_t)G * d->kh * d->kw) * sizeof(int16_t);
+    const size_t win = (size_t)SH * SW + (size_t)d->kh * d->kw;  // int16 per plane
+    uint32_t G = (uint32_t)std::min<size_t>(kDwMaxG, std::max<size_t>(1, (32u * 1024u / 2u) / win));
+    const size_t smem = (size_t)G * win * sizeof(int16_t);
     if (smem <= 96u * 1024u) {
       const uint64_t planes = (uint64_t)d->batch * d->out_ch;
       const unsigned grid = (unsigned)std::min<uint64_t>((planes + G - 1) / G, 148ull * 8ull);
@@ -378,14 +367,12 @@ extern "C" int corm_conv(const corm_conv_desc* d, corm_stream_t stream) {
       const uint32_t s_eq = d->stride_h == d->stride_w ? d->stride_h : 0;
       auto launch = [&](auto kern) {
         cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        kern<<<grid, 256, smem, st>>>(a, SH, SW, G, TPP);
+        kern<<<grid, 256, smem, st>>>(a, SH, SW, G);
       };
       if (k3 && unit_dil && s_eq == 1)
         launch(conv_dw_plane<3, 3, 1>);
       else if (k3 && unit_dil && s_eq == 2)
         launch(conv_dw_plane<3, 3, 2>);
-      else if (k3)
-        launch(conv_dw_plane<3, 3, 0>);
       else
         launch(conv_dw_plane<0, 0, 0>);
       return corm::cuda_status("conv depthwise");
