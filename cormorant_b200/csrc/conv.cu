@@ -274,6 +274,82 @@ __global__ void __launch_bounds__(256) conv_dw_plane(ConvArgs a, uint32_t SH, ui
   }
 }
 
+// Depthwise 3x3 (dilation 1, stride S_) on small planes, a warp per plane:
+// the warp zeroes its padded window in shared memory, scatters the plane's
+// H*W inputs into it (flat coalesced loads, eight in flight per lane), reads
+// the nine taps through lanes 0..8, and each lane then computes columns of
+// four outputs that share their input rows.  No block-wide barriers: warps
+// step through planes independently.
+constexpr uint32_t kDwWarpWin = 1024;  // int16 per warp window
+template <int S_>
+__global__ void __launch_bounds__(256) conv_dw_warp(ConvArgs a, uint32_t SH, uint32_t SW) {
+  __shared__ __align__(16) int16_t s_win[8][kDwWarpWin];
+  constexpr int NR = 4, R = (NR - 1) * S_ + 3;
+  const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  int16_t* win = s_win[warp];
+  const uint32_t HW = a.H * a.W, P = a.OH * a.OW, PS = SH * SW;
+  const uint32_t items = a.OW * ((a.OH + NR - 1) / NR);
+  const uint64_t planes = (uint64_t)a.batch * a.M;
+  const uint32_t dr = 32u / a.W, dc = 32u % a.W;  // a lane's step through the plane
+  for (uint64_t plane = (uint64_t)blockIdx.x * 8 + warp; plane < planes; plane += (uint64_t)gridDim.x * 8) {
+    const uint32_t m = (uint32_t)(plane % a.M), n = (uint32_t)(plane / a.M);
+    const int16_t* src = a.x + ((uint64_t)n * a.C + m) * HW;
+    for (uint32_t i = lane; i < (PS + 1) / 2; i += 32) ((uint32_t*)win)[i] = 0u;
+    const int16_t wv = lane < 9 ? __ldg(a.w + w_offset(a, m, 0, lane / 3, lane % 3)) : (int16_t)0;
+    const int64_t b0 = a.bias ? (int64_t)a.bias[m] << 8 : 0;
+    __syncwarp();
+    uint32_t r = lane / a.W, c = lane - r * a.W;
+    for (uint32_t e0 = lane; e0 < HW; e0 += 256) {
+      int16_t v[8];
+      uint32_t pos[8];
+#pragma unroll
+      for (int u = 0; u < 8; u++) {
+        const uint32_t e = e0 + 32u * u;
+        // inputs no output reads (beyond the window) are dropped
+        pos[u] = (r + a.pt < SH && c + a.pl < SW) ? (r + a.pt) * SW + c + a.pl : 0xFFFFFFFFu;
+        v[u] = e < HW ? __ldg(src + e) : (int16_t)0;
+        r += dr;
+        c += dc;
+        if (c >= a.W) {
+          c -= a.W;
+          r++;
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < 8; u++)
+        if (e0 + 32u * u < HW && pos[u] != 0xFFFFFFFFu) win[pos[u]] = v[u];
+    }
+    int32_t wr[9];
+#pragma unroll
+    for (int q = 0; q < 9; q++) wr[q] = __shfl_sync(0xffffffffu, (int32_t)wv, q);
+    __syncwarp();
+    int16_t* yp = a.y + (uint64_t)n * a.M * P + y_chan(a, m);
+    for (uint32_t it = lane; it < items; it += 32) {
+      const uint32_t ob = it / a.OW, ow = it - ob * a.OW, oh0 = ob * NR;
+      const int16_t* x0 = win + (oh0 * S_) * SW + ow * S_;
+      const uint32_t rows_ok = SH - oh0 * S_;
+      int64_t acc[NR];
+#pragma unroll
+      for (int rr = 0; rr < NR; rr++) acc[rr] = b0;
+#pragma unroll
+      for (int q = 0; q < R; q++) {
+        if ((uint32_t)q >= rows_ok) break;
+        const int32_t x_0 = x0[q * SW], x_1 = x0[q * SW + 1], x_2 = x0[q * SW + 2];
+#pragma unroll
+        for (int rr = 0; rr < NR; rr++) {
+          const int i = q - rr * S_;
+          if (i >= 0 && i < 3)
+            acc[rr] += (int64_t)(x_0 * wr[3 * i]) + (int64_t)(x_1 * wr[3 * i + 1]) + (int64_t)(x_2 * wr[3 * i + 2]);
+        }
+      }
+#pragma unroll
+      for (int rr = 0; rr < NR; rr++)
+        if (oh0 + rr < a.OH) yp[(oh0 + rr) * a.OW + ow] = conv_finish(acc[rr], a.flags);
+    }
+    __syncwarp();
+  }
+}
+
 struct ConvPlan {
   uint32_t K, Kp, Ptot;
   size_t a_bytes, b_bytes, partial_bytes, bytes;
@@ -355,6 +431,18 @@ extern "C" int corm_conv(const corm_conv_desc* d, corm_stream_t stream) {
     // staged planes: the input window the outputs read, padded with zeros
     const uint32_t SH = (d->out_h - 1) * d->stride_h + (d->kh - 1) * d->dilation_h + 1;
     const uint32_t SW = (d->out_w - 1) * d->stride_w + (d->kw - 1) * d->dilation_w + 1;
+    const bool dw3 = d->kh == 3 && d->kw == 3 && d->dilation_h == 1 && d->dilation_w == 1 &&
+                     d->stride_h == d->stride_w && (d->stride_h == 1 || d->stride_h == 2);
+    if (dw3 && (size_t)SH * SW <= kDwWarpWin && d->in_w <= 32u * 32u) {
+      const uint64_t planes = (uint64_t)d->batch * d->out_ch;
+      const unsigned grid = (unsigned)std::min<uint64_t>((planes + 7) / 8, 148ull * 8ull);
+      corm::ProfScope prof_("conv_dw_warp", st);
+      if (d->stride_h == 1)
+        conv_dw_warp<1><<<grid, 256, 0, st>>>(a, SH, SW);
+      else
+        conv_dw_warp<2><<<grid, 256, 0, st>>>(a, SH, SW);
+      return corm::cuda_status("conv depthwise");
+    }
     const size_t win = (size_t)SH * SW + (size_t)d->kh * d->kw;  // int16 per plane
     uint32_t G = (uint32_t)std::min<size_t>(kDwMaxG, std::max<size_t>(1, (32u * 1024u / 2u) / win));
     const size_t smem = (size_t)G * win * sizeof(int16_t);

@@ -83,6 +83,15 @@ CONV_CASES = [  # N, C, H, W, M, kh, kw, sh, sw, pt, pl, dh, dw, depthwise, bias
     (1, 32, 9, 9, 32, 3, 3, 1, 1, 2, 2, 2, 2, True, False),
     (3, 40, 7, 9, 70, 5, 3, 1, 2, 2, 1, 1, 1, False, True),
     (1, 160, 7, 7, 960, 1, 1, 1, 1, 0, 0, 1, 1, False, True),
+    # depthwise: warp-per-plane windows (stride 1 / 2, pads 0..2, W above a warp,
+    # an input row no output reads), shared-memory planes (larger windows, 5x5)
+    (3, 24, 14, 14, 24, 3, 3, 1, 1, 1, 1, 1, 1, True, True),
+    (2, 20, 14, 12, 20, 3, 3, 2, 2, 0, 0, 1, 1, True, True),
+    (2, 9, 5, 40, 9, 3, 3, 1, 1, 2, 1, 1, 1, True, False),
+    (1, 17, 7, 7, 17, 3, 3, 2, 2, 1, 1, 1, 1, True, True),
+    (2, 6, 40, 37, 6, 3, 3, 1, 1, 1, 1, 1, 1, True, True),
+    (2, 6, 45, 44, 6, 3, 3, 2, 2, 1, 1, 1, 1, True, True),
+    (1, 5, 30, 30, 5, 5, 5, 1, 1, 2, 2, 1, 1, True, True),
 ]
 
 
