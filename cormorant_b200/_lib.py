@@ -17,6 +17,7 @@ F_WRAP32, F_WEIGHT_LOGICAL, F_ACT_RELU, F_ACT_RELU6 = 0x1, 0x2, 0x4, 0x8
 
 # every symbol include/cormorant_b200.h declares
 EXPORTS = ("corm_vectorop", "corm_matmul_workspace_size", "corm_matmul", "corm_matmul_noalloc", "corm_conv_workspace_size", "corm_conv",
+           "corm_matmul_post", "corm_conv_post",
            "corm_pool", "corm_rowops", "corm_act_table", "corm_smx_table", "corm_rowops_table_image",
            "corm_bind_device", "corm_device_status", "corm_launch_count", "corm_profile_enable",
            "corm_profile_read", "corm_version", "corm_last_error")
@@ -48,6 +49,14 @@ class ConvDesc(C.Structure):
         ["batch", "in_ch", "in_h", "in_w", "out_ch", "out_h", "out_w", "kh", "kw", "stride_h", "stride_w",
          "dilation_h", "dilation_w", "pad_top", "pad_left", "has_bias", "is_depthwise", "y_cs", "y_cn", "y_gs",
          "flags"]) + [("workspace", C.c_void_p), ("workspace_bytes", C.c_size_t)]
+
+
+class PostOp(C.Structure):
+    """corm_postop: the VectorOP job fused into a MatMul / Conv epilogue."""
+    _fields_ = [("b", C.c_void_p)] + _u32_fields(["op", "act", "alpha", "b_mode", "b_is_first"])
+
+
+POST_B_COL, POST_B_SAME, POST_B_SCALAR = 0, 1, 2
 
 
 class PoolDesc(C.Structure):

@@ -8,6 +8,7 @@
 #include <vector>
 
 #include "corm_common.cuh"
+#include "postop.cuh"
 
 namespace corm {
 
@@ -151,6 +152,28 @@ ProfScope::~ProfScope() {
   cudaEventRecord(g_prof[slot].b, stream);
 }
 
+int make_postop(const void* pp, PostOp& out) {
+  out = PostOp{};
+  if (!pp) return CORM_OK;
+  const corm_postop* p = (const corm_postop*)pp;
+  if (!p->b) return fail(CORM_EINVAL, "postop: null operand");
+  if (p->op > 2) return fail(CORM_EINVAL, "postop: op %u (0 ADD, 1 SUB, 2 MUL)", p->op);
+  if (p->act > 6) return fail(CORM_EINVAL, "postop: act %u", p->act);
+  if (p->b_mode > 2) return fail(CORM_EINVAL, "postop: b_mode %u", p->b_mode);
+  if (p->act >= 4) {
+    const DeviceTables* tb = tables();
+    if (!tb) return CORM_ECUDA;
+    out.table = tb->act[p->act];
+  }
+  out.b = p->b;
+  out.op = p->op;
+  out.act = p->act;
+  out.alpha = p->alpha;
+  out.b_mode = p->b_mode;
+  out.rev = p->b_is_first ? 1u : 0u;
+  return CORM_OK;
+}
+
 }  // namespace corm
 
 extern "C" {
@@ -218,5 +241,6 @@ int corm_bind_device(int device) {
 
 const char* corm_version(void) { return "cormorant_b200 0.1 (sm_100a)"; }
 const char* corm_last_error(void) { return corm::g_err; }
+
 
 }  // extern "C"

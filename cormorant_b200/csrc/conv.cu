@@ -30,6 +30,7 @@ struct ConvArgs {
   uint32_t batch, C, H, W, M, OH, OW, KH, KW, sh, sw, dh, dw, pt, pl;
   uint32_t logical, depthwise, flags;
   uint32_t y_cn, CS, y_gs;
+  corm::PostOp post;  // fused VectorOP job (corm_conv_post)
 };
 
 // offset of logical weight w[m][c][i][j] in the job's weight buffer
@@ -133,6 +134,13 @@ __device__ __forceinline__ int16_t conv_finish(int64_t acc, uint32_t flags) {
   return (int16_t)y;
 }
 
+// output element yp[i] of channel m: the rule, then the fused VectorOP job if any
+__device__ __forceinline__ void conv_put(const ConvArgs& a, int16_t* yp, uint64_t i, uint32_t m, int64_t acc) {
+  int16_t v = conv_finish(acc, a.flags);
+  if (a.post.op != corm::kPostNone) v = corm::post_apply(a.post, v, corm::post_b(a.post, (uint64_t)(yp - a.y) + i, m));
+  yp[i] = v;
+}
+
 // Depthwise: one thread per output pixel; the channel's taps in registers.
 __global__ void __launch_bounds__(256) conv_depthwise(ConvArgs a) {
   const uint32_t P = a.OH * a.OW;
@@ -153,7 +161,7 @@ __global__ void __launch_bounds__(256) conv_depthwise(ConvArgs a) {
         acc += (int64_t)((int32_t)__ldg(xc + (uint64_t)ih * a.W + iw) * (int32_t)__ldg(a.w + w_offset(a, m, 0, i, j)));
       }
     }
-    a.y[(uint64_t)n * a.M * P + y_chan(a, m) + pp] = conv_finish(acc, a.flags);
+    conv_put(a, a.y + (uint64_t)n * a.M * P + y_chan(a, m), pp, m, acc);
   }
 }
 
@@ -172,6 +180,7 @@ __global__ void __launch_bounds__(256) conv_dw_plane(ConvArgs a, uint32_t SH, ui
   __shared__ const int16_t* s_src[kDwMaxG];
   __shared__ int16_t* s_yp[kDwMaxG];
   __shared__ int64_t s_b0[kDwMaxG];
+  __shared__ uint32_t s_m[kDwMaxG];
   const uint32_t KH = KH_ ? KH_ : a.KH, KW = KW_ ? KW_ : a.KW, KK = KH * KW;
   const uint32_t P = a.OH * a.OW, PS = SH * SW;
   int16_t* s_w = s_in + (size_t)G * PS;
@@ -187,6 +196,7 @@ __global__ void __launch_bounds__(256) conv_dw_plane(ConvArgs a, uint32_t SH, ui
       s_src[threadIdx.x] = live ? a.x + ((uint64_t)n * a.C + m) * (uint64_t)a.H * a.W : nullptr;
       s_yp[threadIdx.x] = live ? a.y + (uint64_t)n * a.M * P + y_chan(a, m) : nullptr;
       s_b0[threadIdx.x] = live && a.bias ? (int64_t)a.bias[m] << 8 : 0;
+      s_m[threadIdx.x] = m;
     }
     __syncthreads();
     const uint32_t nrows = G * SH;
@@ -259,7 +269,7 @@ __global__ void __launch_bounds__(256) conv_dw_plane(ConvArgs a, uint32_t SH, ui
         }
 #pragma unroll
         for (int r = 0; r < NR; r++)
-          if (oh0 + r < a.OH) yp[(oh0 + r) * a.OW + ow] = conv_finish(acc[r], a.flags);
+          if (oh0 + r < a.OH) conv_put(a, yp, (oh0 + r) * a.OW + ow, s_m[g], acc[r]);
       } else {
         const uint32_t oh = it / a.OW, ow = it - oh * a.OW;
         const int16_t* x0 = xin + (size_t)(oh * a.sh) * SW + ow * a.sw;
@@ -267,7 +277,7 @@ __global__ void __launch_bounds__(256) conv_dw_plane(ConvArgs a, uint32_t SH, ui
         for (uint32_t i = 0; i < KH; i++)
           for (uint32_t j = 0; j < KW; j++)
             acc += (int64_t)((int32_t)x0[i * a.dh * SW + j * a.dw] * (int32_t)wt[i * KW + j]);
-        yp[it] = conv_finish(acc, a.flags);
+        conv_put(a, yp, it, s_m[g], acc);
       }
     }
     __syncthreads();
@@ -344,7 +354,7 @@ __global__ void __launch_bounds__(256) conv_dw_warp(ConvArgs a, uint32_t SH, uin
       }
 #pragma unroll
       for (int rr = 0; rr < NR; rr++)
-        if (oh0 + rr < a.OH) yp[(oh0 + rr) * a.OW + ow] = conv_finish(acc[rr], a.flags);
+        if (oh0 + rr < a.OH) conv_put(a, yp, (oh0 + rr) * a.OW + ow, m, acc[rr]);
     }
     __syncwarp();
   }
@@ -393,14 +403,29 @@ extern "C" int corm_conv_workspace_size(const corm_conv_desc* d, size_t* bytes) 
   return CORM_OK;
 }
 
+namespace {
+int conv_impl(const corm_conv_desc* d, const corm::PostOp& post, cudaStream_t st);
+}
+
 extern "C" int corm_conv(const corm_conv_desc* d, corm_stream_t stream) {
+  return conv_impl(d, corm::PostOp{}, (cudaStream_t)stream);
+}
+
+extern "C" int corm_conv_post(const corm_conv_desc* d, const corm_postop* post, corm_stream_t stream) {
+  corm::PostOp q;
+  if (int rc = corm::make_postop(post, q)) return rc;
+  return conv_impl(d, q, (cudaStream_t)stream);
+}
+
+namespace {
+int conv_impl(const corm_conv_desc* d, const corm::PostOp& post, cudaStream_t st) {
   if (int rc = validate(d)) return rc;
   if (int rc = corm::check_device()) return rc;
   const uint32_t P = d->out_h * d->out_w;
   if ((uint64_t)d->batch * d->out_ch * P == 0) return CORM_OK;
   if (!d->x || !d->weight || !d->y || (d->has_bias && !d->bias)) return corm::fail(CORM_EINVAL, "corm_conv: null operand");
-  cudaStream_t st = (cudaStream_t)stream;
   ConvArgs a{};
+  a.post = post;
   a.x = d->x;
   a.w = d->weight;
   a.bias = d->has_bias ? d->bias : nullptr;
@@ -515,5 +540,7 @@ extern "C" int corm_conv(const corm_conv_desc* d, corm_stream_t stream) {
   j.img_stride = (uint64_t)d->out_ch * P;
   j.bias = a.bias;
   j.flags = d->flags;
+  j.post = post;
   return corm::gemm_i8x4(j, st);
 }
+}  // namespace

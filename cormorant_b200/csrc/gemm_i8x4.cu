@@ -51,6 +51,7 @@ struct EpiArgs {
   uint32_t num_kb, a_planes, b_planes, b_mn, K;
   uint32_t tiles_m, tiles_n, batch, splits, kb_per_split;
   unsigned long long* partial;
+  PostOp post;
   int* err;
 };
 
@@ -70,6 +71,12 @@ __device__ __forceinline__ uint64_t out_offset(const EpiArgs& ep, uint32_t bz, u
   const uint64_t coff = ep.y_cn ? (uint64_t)(c % ep.y_cn) * ep.y_cs + (uint64_t)(c / ep.y_cn) * ep.y_gs
                                 : (uint64_t)c * ep.y_cs;
   return (uint64_t)n * ep.img_stride + coff + p;
+}
+
+// column c's offset within an output row (mode 0: c; mode 1: the y channel pattern)
+__device__ __forceinline__ uint64_t col_offset(const EpiArgs& ep, uint32_t c) {
+  if (ep.mode == 0) return c;
+  return ep.y_cn ? (uint64_t)(c % ep.y_cn) * ep.y_cs + (uint64_t)(c / ep.y_cn) * ep.y_gs : (uint64_t)c * ep.y_cs;
 }
 
 struct Unit {
@@ -241,7 +248,18 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
         continue;
       }
-      // the 64 results of this thread's row as int16 pairs, then TMEM released
+      // the 64 results of this thread's row as int16 pairs, then TMEM released;
+      // a fused VectorOP job reads its operand at the output element's offset
+      const bool has_post = ep.post.op != kPostNone;
+      uint64_t rowbase = 0;
+      if (has_post && row_ok) {
+        if (ep.mode == 0) {
+          rowbase = (uint64_t)w.bz * ep.out_batch_stride + (uint64_t)r * ep.ldc;
+        } else {
+          const uint32_t n = r / ep.P;
+          rowbase = (uint64_t)n * ep.img_stride + (r - n * ep.P);
+        }
+      }
       uint32_t v2[32];
 #pragma unroll
       for (int half = 0; half < 2; half++) {
@@ -261,7 +279,13 @@ __global__ void __launch_bounds__(THREADS, 1)
             if (c0 + j < ep.cols) a0 += (int64_t)ep.bias[c0 + j] << 8;
             if (c0 + j + 1 < ep.cols) a1 += (int64_t)ep.bias[c0 + j + 1] << 8;
           }
-          v2[16 * half + j / 2] = (uint32_t)(uint16_t)finish(a0, ep.flags) | ((uint32_t)(uint16_t)finish(a1, ep.flags) << 16);
+          int16_t y0 = finish(a0, ep.flags), y1 = finish(a1, ep.flags);
+          if (has_post && row_ok) {
+            const uint32_t ca = c0 + j, cb = c0 + j + 1;
+            if (ca < ep.cols) y0 = post_apply(ep.post, y0, post_b(ep.post, rowbase + col_offset(ep, ca), ca));
+            if (cb < ep.cols) y1 = post_apply(ep.post, y1, post_b(ep.post, rowbase + col_offset(ep, cb), cb));
+          }
+          v2[16 * half + j / 2] = (uint32_t)(uint16_t)y0 | ((uint32_t)(uint16_t)y1 << 16);
         }
       }
       sm100::tc_fence_before();
@@ -310,7 +334,10 @@ __global__ void __launch_bounds__(256) gemm_finish_kernel(const EpiArgs ep) {
     const uint32_t r = (uint32_t)(br % ep.rows), bz = (uint32_t)(br / ep.rows);
     int64_t acc = (int64_t)ep.partial[i];
     if (ep.mode == 1 && ep.bias) acc += (int64_t)ep.bias[c] << 8;
-    ep.out[out_offset(ep, ep.mode == 0 ? bz : 0, r, c)] = finish(acc, ep.flags);
+    const uint64_t off = out_offset(ep, ep.mode == 0 ? bz : 0, r, c);
+    int16_t y = finish(acc, ep.flags);
+    if (ep.post.op != kPostNone) y = post_apply(ep.post, y, post_b(ep.post, off, c));
+    ep.out[off] = y;
   }
 }
 
@@ -479,6 +506,7 @@ int gemm_i8x4(const GemmJob& j, cudaStream_t stream) {
   ep.img_stride = j.img_stride;
   ep.bias = j.bias;
   ep.flags = j.flags;
+  ep.post = j.post;
   ep.num_kb = sp.num_kb;
   ep.a_planes = j.a_planes;
   ep.b_planes = j.b_planes;

@@ -14,6 +14,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include "postop.cuh"
+
 namespace corm {
 
 struct GemmJob {
@@ -37,6 +39,7 @@ struct GemmJob {
   uint64_t img_stride;      // mode 1: elements per image (out_ch * P)
   const int16_t* bias;      // mode 1 bias per column (raw), or nullptr
   uint32_t flags;           // CORM_F_WRAP32 | CORM_F_ACT_RELU | CORM_F_ACT_RELU6
+  PostOp post;              // fused VectorOP job on the result (op kPostNone: none)
   int* err;                 // status word for the bounded waits; nullptr: the library's per-device word
 };
 

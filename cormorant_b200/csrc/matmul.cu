@@ -40,6 +40,7 @@ struct MmArgs {
   const int16_t* b;
   int16_t* c;
   uint32_t n, k, m, batch, a_bs, b_bs, c_bs, packed, kw, flags;
+  corm::PostOp post;
 };
 
 __device__ __forceinline__ int16_t mm_finish(int64_t acc, uint32_t flags) {
@@ -130,10 +131,14 @@ __global__ void __launch_bounds__(128) mm_gemv_kernel(MmArgs p, uint32_t kchunk,
     for (int e = 0; e < 8; e++) {
       const uint32_t jj = j0 + e;
       if (jj >= p.m) continue;
-      if (partial)
+      if (partial) {
         atomicAdd(partial + (uint64_t)bt * p.n * p.m + (uint64_t)r * p.m + jj, (unsigned long long)acc[r][e]);
-      else
-        p.c[(uint64_t)bt * p.c_bs + (uint64_t)r * p.m + jj] = mm_finish(acc[r][e], p.flags);
+      } else {
+        const uint64_t off = (uint64_t)bt * p.c_bs + (uint64_t)r * p.m + jj;
+        int16_t y = mm_finish(acc[r][e], p.flags);
+        if (p.post.op != corm::kPostNone) y = corm::post_apply(p.post, y, corm::post_b(p.post, off, jj));
+        p.c[off] = y;
+      }
     }
   }
 }
@@ -142,7 +147,10 @@ __global__ void mm_small_finish(MmArgs p, const unsigned long long* partial) {
   const uint64_t total = (uint64_t)p.batch * p.n * p.m;
   for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (uint64_t)gridDim.x * blockDim.x) {
     const uint64_t bt = i / ((uint64_t)p.n * p.m), rem = i - bt * p.n * p.m;
-    p.c[bt * p.c_bs + rem] = mm_finish((int64_t)partial[i], p.flags);
+    const uint64_t off = bt * p.c_bs + rem;
+    int16_t y = mm_finish((int64_t)partial[i], p.flags);
+    if (p.post.op != corm::kPostNone) y = corm::post_apply(p.post, y, corm::post_b(p.post, off, (uint32_t)(rem % p.m)));
+    p.c[off] = y;
   }
 }
 
@@ -196,14 +204,30 @@ extern "C" int corm_matmul_workspace_size(const corm_matmul_desc* d, size_t* byt
   return CORM_OK;
 }
 
+namespace {
+int matmul_impl(const corm_matmul_desc* d, const corm::PostOp& post, cudaStream_t st);
+}
+
 extern "C" int corm_matmul(const corm_matmul_desc* d, corm_stream_t stream) {
+  return matmul_impl(d, corm::PostOp{}, (cudaStream_t)stream);
+}
+
+extern "C" int corm_matmul_post(const corm_matmul_desc* d, const corm_postop* post, corm_stream_t stream) {
+  corm::PostOp q;
+  if (int rc = corm::make_postop(post, q)) return rc;
+  return matmul_impl(d, q, (cudaStream_t)stream);
+}
+
+namespace {
+int matmul_impl(const corm_matmul_desc* d, const corm::PostOp& post, cudaStream_t st) {
   if (int rc = validate(d)) return rc;
   if (int rc = corm::check_device()) return rc;
   if (d->n == 0 || d->m == 0 || d->batch == 0) return CORM_OK;
   if (!d->a || !d->b || !d->c) return corm::fail(CORM_EINVAL, "corm_matmul: null operand");
-  cudaStream_t st = (cudaStream_t)stream;
+  if (post.op != corm::kPostNone && d->k == 0)
+    return corm::fail(CORM_EINVAL, "corm_matmul_post: k = 0");
   MmArgs p{d->a, d->b, d->c, d->n, d->k, d->m, d->batch, d->a_batch_stride, d->b_batch_stride, d->c_batch_stride,
-           d->b_packed, d->gemv_kw, d->flags};
+           d->b_packed, d->gemv_kw, d->flags, post};
   if (d->k == 0) {  // empty sum: floor(0) = 0 everywhere
     for (uint32_t bt = 0; bt < d->batch; bt++)
       for (uint32_t r = 0; r < d->n; r++)
@@ -280,8 +304,10 @@ extern "C" int corm_matmul(const corm_matmul_desc* d, corm_stream_t stream) {
   j.out_batch_stride = d->c_batch_stride;
   j.ldc = d->m;
   j.flags = d->flags;
+  j.post = post;
   return corm::gemm_i8x4(j, st);
 }
+}  // namespace
 
 // ---------------------------------------------------------------- allocation-free variant
 // corm_matmul_noalloc: the same MatMul job for callers that must not allocate

@@ -58,10 +58,21 @@ def vectorop(a, b, c, *, size, op, outer=1, a_inc=0, b_inc=0, act=0, alpha=0, sm
     check(lib().corm_vectorop(C.byref(d), st))
 
 
+def _post(post):
+    """corm_postop from dict(b=tensor, op, act=0, alpha=0, b_mode=0, b_is_first=0)."""
+    if post is None:
+        return None
+    _i16(post["b"], "post b")
+    return _lib.PostOp(_ptr(post["b"]), post["op"], post.get("act", 0), post.get("alpha", 0) & 0xFFFFFFFF,
+                       post.get("b_mode", 0), int(bool(post.get("b_is_first", 0))))
+
+
 def matmul(a, b, c, *, n, k, m, batch=1, a_batch_stride=0, b_batch_stride=0, c_batch_stride=0, b_packed=0,
-           gemv_kw=0, flags=0, workspace=None):
+           gemv_kw=0, flags=0, workspace=None, post=None):
     """One MatmulKernel job (host_emu.py:338-362).  ``workspace``: a uint8
-    CUDA tensor, or None to take one from torch's allocator."""
+    CUDA tensor, or None to take one from torch's allocator.  ``post``: a
+    VectorOP job fused onto the result (corm_matmul_post), a dict with keys b
+    (int16 tensor), op, act, alpha, b_mode, b_is_first."""
     for t, nm in ((a, "a"), (b, "b"), (c, "c")):
         _i16(t, nm)
     st = _ready()
@@ -73,15 +84,20 @@ def matmul(a, b, c, *, n, k, m, batch=1, a_batch_stride=0, b_batch_stride=0, c_b
         if workspace is None:
             workspace = torch.empty(need.value, dtype=torch.uint8, device=a.device)
         d.workspace, d.workspace_bytes = _ptr(workspace), workspace.numel() * workspace.element_size()
-    check(lib().corm_matmul(C.byref(d), st))
+    q = _post(post)
+    if q is None:
+        check(lib().corm_matmul(C.byref(d), st))
+    else:
+        check(lib().corm_matmul_post(C.byref(d), C.byref(q), st))
     return workspace
 
 
 def conv(x, weight, bias, y, *, batch, in_ch, in_h, in_w, out_ch, out_h, out_w, kh, kw, stride_h=1, stride_w=1,
          dilation_h=1, dilation_w=1, pad_top=0, pad_left=0, has_bias=0, is_depthwise=0, y_cs=0, y_cn=0, y_gs=0,
-         flags=0, workspace=None):
+         flags=0, workspace=None, post=None):
     """One ConvKernel job (host_emu.py:393-455); CORM_F_WEIGHT_LOGICAL in
-    ``flags`` for [M][C][kh][kw] weights instead of the board image."""
+    ``flags`` for [M][C][kh][kw] weights instead of the board image.
+    ``post``: a fused VectorOP job as for ``matmul``."""
     for t, nm in ((x, "x"), (weight, "weight"), (bias, "bias"), (y, "y")):
         _i16(t, nm)
     st = _ready()
@@ -94,7 +110,11 @@ def conv(x, weight, bias, y, *, batch, in_ch, in_h, in_w, out_ch, out_h, out_w, 
         if workspace is None:
             workspace = torch.empty(need.value, dtype=torch.uint8, device=x.device)
         d.workspace, d.workspace_bytes = _ptr(workspace), workspace.numel() * workspace.element_size()
-    check(lib().corm_conv(C.byref(d), st))
+    q = _post(post)
+    if q is None:
+        check(lib().corm_conv(C.byref(d), st))
+    else:
+        check(lib().corm_conv_post(C.byref(d), C.byref(q), st))
     return workspace
 
 

@@ -23,10 +23,13 @@ Numerics per node type, all bit-exact with the reference's branch:
   SoftmaxVopNode               the softmax unit, row mode (smx_nodes.py:121-134)
   ReshapeNode / SpaceToDepth   views / reorders (:662-665, :692-699)
 
-Graph fusion (``fuse=True``): a Relu / Clip(0,6) ScheduledNode whose only input
-is a Conv / MatMul output read by nothing else is folded into that kernel's
-epilogue (CORM_F_ACT_RELU / RELU6) — exact, since max(sat16(v), 0) is what the
-separate node computes — and the intermediate tensor is not materialised.
+Graph fusion (``fuse=True``): a ScheduledNode whose input is a Conv / MatMul
+output read by nothing else is folded into that kernel's epilogue, and the
+intermediate tensor is not materialised: a Relu / Clip(0,6) as an act flag
+(CORM_F_ACT_RELU / RELU6 — max(sat16(v), 0) is what the separate node
+computes), an ADD / SUB / MUL (with its fused act) against a bias row, a
+scalar or a same-shaped tensor as a fused VectorOP job (corm_matmul_post /
+corm_conv_post, bit-exact with the two jobs).
 """
 from __future__ import annotations
 
@@ -123,8 +126,10 @@ class GpuSimulator:
 
     # ------------------------------------------------------------ fusion
     def _fusion_plan(self):
-        """{relu node index: (producer index, act flag)} for Relu / Clip(0,6)
-        nodes folded into a Conv / MatMul epilogue."""
+        """{consumer node index: (producer index, act flag, post)} for the
+        ScheduledNodes folded into a Conv / MatMul epilogue: Relu / Clip(0,6)
+        as an act flag; ADD / SUB / MUL with a bias row (MatMul), a scalar or
+        a same-shaped tensor as a fused VectorOP job (corm_*_post)."""
         nodes = self._graph.nodes
         readers: Dict[str, int] = {}
         for sn in nodes:
@@ -135,18 +140,49 @@ class GpuSimulator:
         producer = {getattr(sn, "output", None).onnx_name: i for i, sn in enumerate(nodes)
                     if getattr(sn, "output", None) is not None}
         plan = {}
+        taken = set()
         for i, sn in enumerate(nodes):
-            if _kind(sn) != "ScheduledNode" or sn.op_code not in (4, 5) or getattr(sn, "act", 0) not in (0,):
+            if _kind(sn) != "ScheduledNode":
                 continue
-            src = sn.inputs[0].onnx_name
-            j = producer.get(src)
-            if j is None or readers.get(src, 0) != 1 or src in outs:
+            op, act = sn.op_code, getattr(sn, "act", 0)
+            if op in (4, 5) and act == 0:
+                cands = [(0, None)]
+            elif op in (0, 1, 2) and len(sn.inputs) == 2:
+                cands = [(0, sn.inputs[1]), (1, sn.inputs[0])]
+            else:
                 continue
-            if _kind(nodes[j]) not in ("ConvNode", "MatmulNode", "MatmulConvNode"):
-                continue
-            if any(j == p for p, _ in plan.values()):
-                continue
-            plan[i] = (j, F_ACT_RELU if sn.op_code == 4 else F_ACT_RELU6)
+            for pos, other in cands:
+                src = sn.inputs[pos].onnx_name
+                j = producer.get(src)
+                if j is None or j in taken or readers.get(src, 0) != 1 or src in outs:
+                    continue
+                pk = _kind(nodes[j])
+                if pk not in ("ConvNode", "MatmulNode", "MatmulConvNode"):
+                    continue
+                if other is None:
+                    plan[i] = (j, F_ACT_RELU if op == 4 else F_ACT_RELU6, None)
+                    taken.add(j)
+                    break
+                # the other operand must exist when the producer runs
+                po = producer.get(other.onnx_name)
+                if po is not None and po > j:
+                    continue
+                N, no = sn.output.numel, other.numel
+                if sn.inputs[pos].numel != N:
+                    continue
+                if no == N:
+                    mode = 1
+                elif no == 1:
+                    mode = 2
+                elif pk != "ConvNode" and no == int(sn.output.shape[-1]) and N % no == 0:
+                    mode = 0
+                else:
+                    continue
+                post = dict(other=other, op=op, act=act, alpha=getattr(sn, "alpha", 0), b_mode=mode,
+                            b_is_first=1 if (op == 1 and pos == 1) else 0)
+                plan[i] = (j, 0, post)
+                taken.add(j)
+                break
         return plan
 
     # ------------------------------------------------------------ forward
@@ -195,7 +231,7 @@ class GpuSimulator:
         for t in self._graph.weight_tensors:
             if getattr(t, "data", None) is not None:
                 meta[t.onnx_name] = t
-        fused_into = {j: (i, flag) for i, (j, flag) in self._plan.items()}
+        fused_into = {j: (i, flag, post) for i, (j, flag, post) in self._plan.items()}
         skip = set(self._plan)
 
         def get(t):
@@ -204,19 +240,23 @@ class GpuSimulator:
             return raw[t.onnx_name]
 
         for i, sn in enumerate(self._graph.nodes):
-            if i in skip:
+            if i in skip:  # folded into its producer's launch
+                for name in dying.get(i, ()):
+                    raw.pop(name, None)
                 continue
             kind = _kind(sn)
             out_t = sn.output
-            flag, alias_t = 0, None
+            flag, alias_t, post = 0, None, None
             if i in fused_into:
-                ri, flag = fused_into[i]
+                ri, flag, pspec = fused_into[i]
                 alias_t = self._graph.nodes[ri].output
+                if pspec is not None:
+                    post = self._post_of(pspec, get)
             if kind in ("MatmulNode", "MatmulConvNode"):
-                y = self._matmul(sn, get(sn.inputs[0]), get(sn.inputs[1]), flag)
+                y = self._matmul(sn, get(sn.inputs[0]), get(sn.inputs[1]), flag, post)
             elif kind == "ConvNode":
                 y = self._conv(sn, get(sn.inputs[0]), get(sn.inputs[1]),
-                               self._bias_raw(sn, sn.inputs[2]) if sn.has_bias else None, flag)
+                               self._bias_raw(sn, sn.inputs[2]) if sn.has_bias else None, flag, post)
             elif kind == "ReshapeNode":
                 y = get(sn.inputs[0])
             elif kind == "PoolNode":
@@ -250,7 +290,14 @@ class GpuSimulator:
         return raw, meta
 
     # ------------------------------------------------------------ node kernels
-    def _matmul(self, sn, a, b, flag):
+    def _post_of(self, pspec, get):
+        """The corm_postop of a fused VectorOP node: its other operand on the
+        device (a small weight broadcast as one scalar, a bias row or a full
+        tensor at the output's offsets)."""
+        return dict(b=get(pspec["other"]), op=pspec["op"], act=pspec["act"], alpha=pspec["alpha"],
+                    b_mode=pspec["b_mode"], b_is_first=pspec["b_is_first"])
+
+    def _matmul(self, sn, a, b, flag, post=None):
         A, B, Y = sn.inputs[0], sn.inputs[1], sn.output
         wrap = F_WRAP32 if _has_exp(A, B, Y) else 0
         ash, bsh = list(A.shape), list(B.shape)
@@ -285,8 +332,11 @@ class GpuSimulator:
             ao = sum((0 if lead_a[q] == 1 else int(idx[q])) * int(a_strides[q]) for q in range(L)) * n * k
             bo = sum((0 if lead_b[q] == 1 else int(idx[q])) * int(b_strides[q]) for q in range(L)) * k * m
             ws = self._workspace(self._mm_ws(n, k, m, inner, a_bs, b_bs))
+            po = post
+            if post is not None and post["b_mode"] == 1:  # a full operand: the slice at this output's offset
+                po = dict(post, b=post["b"][o * inner * n * m:])
             ops.matmul(a[ao:], b[bo:], y[o * inner * n * m:], n=n, k=k, m=m, batch=inner, a_batch_stride=a_bs,
-                       b_batch_stride=b_bs, c_batch_stride=n * m, flags=wrap | flag, workspace=ws)
+                       b_batch_stride=b_bs, c_batch_stride=n * m, flags=wrap | flag, workspace=ws, post=po)
         return y
 
     @staticmethod
@@ -299,7 +349,7 @@ class GpuSimulator:
         _lib.check(_lib.lib().corm_matmul_workspace_size(C.byref(d), C.byref(need)))
         return need.value
 
-    def _conv(self, sn, x, w, b, flag):
+    def _conv(self, sn, x, w, b, flag, post=None):
         wrap = F_WRAP32 if _has_exp(sn.inputs[0], sn.inputs[1], sn.output) else 0
         y = self._alloc(sn.output.numel)
         regs = dict(batch=sn.batch, in_ch=sn.in_ch, in_h=sn.in_h, in_w=sn.in_w, out_ch=sn.out_ch, out_h=sn.out_h,
@@ -311,7 +361,7 @@ class GpuSimulator:
         need = 0 if sn.is_depthwise else 2 * ((sn.batch * sn.out_h * sn.out_w * Kp + 255) // 256 * 256) + \
             2 * ((sn.out_ch * Kp + 255) // 256 * 256)
         ops.conv(x, w, b, y, flags=F_WEIGHT_LOGICAL | wrap | flag,
-                 workspace=self._workspace(need) if need else None, **regs)
+                 workspace=self._workspace(need) if need else None, post=post, **regs)
         return y
 
     def _pool(self, sn, x):

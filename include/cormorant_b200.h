@@ -130,6 +130,30 @@ typedef struct {
 int corm_conv_workspace_size(const corm_conv_desc* d, size_t* bytes);
 int corm_conv(const corm_conv_desc* d, corm_stream_t stream);
 
+/* ---------------------------------------------------------------- fused VectorOP epilogue
+ * No counterpart in the reference: a MatMul or Conv job followed by a
+ * VectorOP job that reads its output, as ONE launch.  The VectorOP job is
+ * c = act(op(y, b)) (or op(b, y) with b_is_first) with y the MatMul / Conv
+ * result exactly as the plain job writes it and b the second operand:
+ * op 0 ADD / 1 SUB -> sat16(x +- z), 2 MUL -> sat16(floor(x z / 2^8)); act is
+ * the VectorOP act register (0 none, 1 ReLU, 2 ReLU6, 3 LeakyReLU with alpha,
+ * 4 SiLU, 5 GELU, 6 GELU-tanh), the activation unit's rounding included.  b
+ * per output column (MatMul) / channel (Conv) — a bias row; at the output's
+ * own element offsets — a residual; or one scalar.  The result replaces y in
+ * the output buffer (y itself is never stored).  Bit-exact with the two jobs
+ * run one after the other. */
+enum { CORM_POST_B_COL = 0, CORM_POST_B_SAME = 1, CORM_POST_B_SCALAR = 2 };
+typedef struct {
+  const int16_t* b;
+  uint32_t op;          /* 0 ADD, 1 SUB, 2 MUL */
+  uint32_t act, alpha;  /* VectorOP act / alpha registers */
+  uint32_t b_mode;      /* CORM_POST_B_* */
+  uint32_t b_is_first;  /* SUB: c = b - y */
+} corm_postop;
+
+int corm_matmul_post(const corm_matmul_desc* d, const corm_postop* post, corm_stream_t stream);
+int corm_conv_post(const corm_conv_desc* d, const corm_postop* post, corm_stream_t stream);
+
 /* ---------------------------------------------------------------- Pool
  * Replaces run_pool / XPoolingkernel (inference-scheduler/src/codegen/
  * _source.py:1548-1580; semantics inference-scheduler/src/codegen/

@@ -29,6 +29,7 @@ def test_struct_sizes():
     assert C.sizeof(_lib.VectorOpDesc) == 3 * 8 + 10 * 4 + 0 * 4
     assert C.sizeof(_lib.MatmulDesc) == 3 * 8 + 10 * 4 + 8 + 8
     assert C.sizeof(_lib.PoolDesc) == 2 * 8 + 17 * 4 + 4
+    assert C.sizeof(_lib.PostOp) == 8 + 5 * 4 + 4
     assert C.sizeof(_lib.RowOpsDesc) == 4 * 4 + 8 + 8 + 8 + 8 + 8 + 8 + 8 + 8 + 4 * 4
 
 
