@@ -248,18 +248,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
         continue;
       }
-      // the 64 results of this thread's row as int16 pairs, then TMEM released;
-      // a fused VectorOP job reads its operand at the output element's offset
-      const bool has_post = ep.post.op != kPostNone;
-      uint64_t rowbase = 0;
-      if (has_post && row_ok) {
-        if (ep.mode == 0) {
-          rowbase = (uint64_t)w.bz * ep.out_batch_stride + (uint64_t)r * ep.ldc;
-        } else {
-          const uint32_t n = r / ep.P;
-          rowbase = (uint64_t)n * ep.img_stride + (r - n * ep.P);
-        }
-      }
+      // the 64 results of this thread's row as int16 pairs, then TMEM released
       uint32_t v2[32];
 #pragma unroll
       for (int half = 0; half < 2; half++) {
@@ -279,19 +268,55 @@ __global__ void __launch_bounds__(THREADS, 1)
             if (c0 + j < ep.cols) a0 += (int64_t)ep.bias[c0 + j] << 8;
             if (c0 + j + 1 < ep.cols) a1 += (int64_t)ep.bias[c0 + j + 1] << 8;
           }
-          int16_t y0 = finish(a0, ep.flags), y1 = finish(a1, ep.flags);
-          if (has_post && row_ok) {
-            const uint32_t ca = c0 + j, cb = c0 + j + 1;
-            if (ca < ep.cols) y0 = post_apply(ep.post, y0, post_b(ep.post, rowbase + col_offset(ep, ca), ca));
-            if (cb < ep.cols) y1 = post_apply(ep.post, y1, post_b(ep.post, rowbase + col_offset(ep, cb), cb));
-          }
-          v2[16 * half + j / 2] = (uint32_t)(uint16_t)y0 | ((uint32_t)(uint16_t)y1 << 16);
+          v2[16 * half + j / 2] = (uint32_t)(uint16_t)finish(a0, ep.flags) | ((uint32_t)(uint16_t)finish(a1, ep.flags) << 16);
         }
       }
       sm100::tc_fence_before();
       __syncwarp();
       if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(sm100::smem_u32(tmem_empty)) : "memory");
       if (!row_ok) continue;
+      if (ep.post.op != kPostNone) {
+        // the fused VectorOP job: its operand for these 64 outputs (every load
+        // issued before any use), then op + act
+        const uint32_t cb = w.tile_c + 64 * h;
+        uint32_t b2[32];
+        uint64_t rowbase;
+        if (ep.mode == 0) {
+          rowbase = (uint64_t)w.bz * ep.out_batch_stride + (uint64_t)r * ep.ldc;
+        } else {
+          const uint32_t n = r / ep.P;
+          rowbase = (uint64_t)n * ep.img_stride + (r - n * ep.P);
+        }
+        const int16_t* bsrc = ep.post.b_mode == 0 ? ep.post.b + cb : ep.post.b + rowbase + cb;
+        if (ep.post.b_mode == 2) {
+          const uint32_t v = (uint16_t)__ldg(ep.post.b);
+#pragma unroll
+          for (int j = 0; j < 32; j++) b2[j] = v | (v << 16);
+        } else if ((ep.mode == 0 || ep.post.b_mode == 0) && cb + 64 <= ep.cols && ((uintptr_t)bsrc & 15) == 0) {
+#pragma unroll
+          for (int j = 0; j < 8; j++) {
+            const int4 t = __ldg((const int4*)bsrc + j);
+            b2[4 * j] = (uint32_t)t.x;
+            b2[4 * j + 1] = (uint32_t)t.y;
+            b2[4 * j + 2] = (uint32_t)t.z;
+            b2[4 * j + 3] = (uint32_t)t.w;
+          }
+        } else {
+#pragma unroll
+          for (int j = 0; j < 64; j += 2) {
+            const uint32_t ca = cb + j, cc2 = cb + j + 1;
+            const uint32_t lo = ca < ep.cols ? (uint16_t)post_b(ep.post, rowbase + col_offset(ep, ca), ca) : 0u;
+            const uint32_t hi = cc2 < ep.cols ? (uint16_t)post_b(ep.post, rowbase + col_offset(ep, cc2), cc2) : 0u;
+            b2[j / 2] = lo | (hi << 16);
+          }
+        }
+#pragma unroll
+        for (int j = 0; j < 32; j++) {
+          const int16_t y0 = post_apply(ep.post, (int16_t)(v2[j] & 0xFFFF), (int16_t)(b2[j] & 0xFFFF));
+          const int16_t y1 = post_apply(ep.post, (int16_t)(v2[j] >> 16), (int16_t)(b2[j] >> 16));
+          v2[j] = (uint32_t)(uint16_t)y0 | ((uint32_t)(uint16_t)y1 << 16);
+        }
+      }
       const uint32_t c0 = w.tile_c + 64 * h;
       if (ep.mode == 0) {
         int16_t* dst = ep.out + out_offset(ep, w.bz, r, c0);

@@ -25,11 +25,17 @@ def test_bert_small_vs_reference(golden, fuse):
     z = golden("sim_graph_bert_l2_t32_b2.npz")
     g, feeds, _ = WL.bert_base(seed=17, batch=2, seq=32, layers=2)
     out = _run(g, feeds, fuse)
+    missing = 0
     for sn in g.nodes:
         name = sn.output.onnx_name
+        if name not in out:  # folded into its producer's epilogue
+            assert fuse
+            missing += 1
+            continue
         crc = zlib.crc32(np.ascontiguousarray(out[name].astype("<i2")).tobytes())
         assert crc == int(z["c_" + name][0]), name
     assert np.array_equal(out["qa_logits"].reshape(z["out_qa_logits"].shape), z["out_qa_logits"])
+    assert (missing > 0) == fuse
 
 
 def test_bert_seq384_one_layer_vs_oracle():
@@ -42,7 +48,8 @@ def test_bert_seq384_one_layer_vs_oracle():
     ref = og.forward(g, feeds)
     for sn in g.nodes:
         name = sn.output.onnx_name
-        assert np.array_equal(out[name], ref[name].reshape(out[name].shape)), name
+        if name in out:
+            assert np.array_equal(out[name], ref[name].reshape(out[name].shape)), name
 
 
 def test_bert_lean_keep():
