@@ -52,8 +52,32 @@ struct EpiArgs {
   uint32_t tiles_m, tiles_n, batch, splits, kb_per_split;
   unsigned long long* partial;
   PostOp post;
+  uint32_t ymode;  // 0: the rule in int32 (small K), 1: in int64, 2: int32 wrap (CORM_F_WRAP32)
   int* err;
 };
+
+// y = floor(acc / 2^8) for acc = 2^16 HH + 2^8 MID + LL + 2^8 bias, i.e.
+// 2^8 HH + MID + bias + floor(LL / 2^8) (LL >= 0), saturated, then the act
+// flags: in int32 when the job's K keeps every term below 2^31, else in
+// int64; under CORM_F_WRAP32 acc is formed modulo 2^32 first.
+__device__ __forceinline__ int32_t sat_act(int32_t y, uint32_t flags) {
+  y = y > 32767 ? 32767 : (y < -32768 ? -32768 : y);
+  if (flags & (CORM_F_ACT_RELU | CORM_F_ACT_RELU6)) y = y < 0 ? 0 : y;
+  if ((flags & CORM_F_ACT_RELU6) && y > 1536) y = 1536;
+  return y;
+}
+
+template <int YMODE>
+__device__ __forceinline__ int16_t combine(uint32_t hh, uint32_t mid, uint32_t ll, int32_t bias, uint32_t flags) {
+  if (YMODE == 0) return (int16_t)sat_act((int32_t)hh * 256 + (int32_t)mid + bias + ((int32_t)ll >> 8), flags);
+  if (YMODE == 2) {
+    const uint32_t acc = (hh << 16) + (mid << 8) + ll + ((uint32_t)bias << 8);
+    return (int16_t)sat_act((int32_t)acc >> 8, flags);
+  }
+  int64_t y = (int64_t)(int32_t)hh * 256 + (int32_t)mid + bias + ((int32_t)ll >> 8);
+  y = y > 32767 ? 32767 : (y < -32768 ? -32768 : y);
+  return (int16_t)sat_act((int32_t)y, flags);
+}
 
 __device__ __forceinline__ int16_t finish(int64_t acc, uint32_t flags) {
   if (flags & CORM_F_WRAP32) acc = corm_wrap32(acc);
@@ -71,6 +95,21 @@ __device__ __forceinline__ uint64_t out_offset(const EpiArgs& ep, uint32_t bz, u
   const uint64_t coff = ep.y_cn ? (uint64_t)(c % ep.y_cn) * ep.y_cs + (uint64_t)(c / ep.y_cn) * ep.y_gs
                                 : (uint64_t)c * ep.y_cs;
   return (uint64_t)n * ep.img_stride + coff + p;
+}
+
+// 32 accumulator columns of one row -> 16 packed int16 pairs (mode 1 adds the bias)
+template <int YMODE>
+__device__ __forceinline__ void combine32(const EpiArgs& ep, const uint32_t* hh, const uint32_t* mid,
+                                          const uint32_t* ll, uint32_t c0, uint32_t* out2) {
+  const bool cbias = ep.mode == 1 && ep.bias;
+#pragma unroll
+  for (int j = 0; j < 32; j += 2) {
+    const int32_t b0 = (cbias && c0 + j < ep.cols) ? ep.bias[c0 + j] : 0;
+    const int32_t b1 = (cbias && c0 + j + 1 < ep.cols) ? ep.bias[c0 + j + 1] : 0;
+    const int16_t y0 = combine<YMODE>(hh[j], mid[j], ll[j], b0, ep.flags);
+    const int16_t y1 = combine<YMODE>(hh[j + 1], mid[j + 1], ll[j + 1], b1, ep.flags);
+    out2[j / 2] = (uint32_t)(uint16_t)y0 | ((uint32_t)(uint16_t)y1 << 16);
+  }
 }
 
 // column c's offset within an output row (mode 0: c; mode 1: the y channel pattern)
@@ -259,17 +298,12 @@ __global__ void __launch_bounds__(THREADS, 1)
         sm100::tmem_ld32(tmem + lane_addr + 2 * BN + cc, ll);
         sm100::tmem_ld_wait();
         const uint32_t c0 = w.tile_c + cc;
-#pragma unroll
-        for (int j = 0; j < 32; j += 2) {
-          int64_t a0 = ((int64_t)(int32_t)hh[j] << 16) + ((int64_t)(int32_t)mid[j] << 8) + (int64_t)(int32_t)ll[j];
-          int64_t a1 = ((int64_t)(int32_t)hh[j + 1] << 16) + ((int64_t)(int32_t)mid[j + 1] << 8) +
-                       (int64_t)(int32_t)ll[j + 1];
-          if (ep.mode == 1 && ep.bias) {
-            if (c0 + j < ep.cols) a0 += (int64_t)ep.bias[c0 + j] << 8;
-            if (c0 + j + 1 < ep.cols) a1 += (int64_t)ep.bias[c0 + j + 1] << 8;
-          }
-          v2[16 * half + j / 2] = (uint32_t)(uint16_t)finish(a0, ep.flags) | ((uint32_t)(uint16_t)finish(a1, ep.flags) << 16);
-        }
+        if (ep.ymode == 0)
+          combine32<0>(ep, hh, mid, ll, c0, v2 + 16 * half);
+        else if (ep.ymode == 1)
+          combine32<1>(ep, hh, mid, ll, c0, v2 + 16 * half);
+        else
+          combine32<2>(ep, hh, mid, ll, c0, v2 + 16 * half);
       }
       sm100::tc_fence_before();
       __syncwarp();
@@ -532,6 +566,11 @@ int gemm_i8x4(const GemmJob& j, cudaStream_t stream) {
   ep.bias = j.bias;
   ep.flags = j.flags;
   ep.post = j.post;
+  {
+    const uint32_t kk = j.K ? j.K : j.Kp;
+    ep.ymode = (j.flags & CORM_F_WRAP32) ? 2u
+               : ((uint64_t)kk * ((1ull << 22) + (1ull << 16) + (1ull << 8)) + (1ull << 15) < (1ull << 31) ? 0u : 1u);
+  }
   ep.num_kb = sp.num_kb;
   ep.a_planes = j.a_planes;
   ep.b_planes = j.b_planes;
