@@ -112,6 +112,48 @@ __device__ __forceinline__ void combine32(const EpiArgs& ep, const uint32_t* hh,
   }
 }
 
+// The fused VectorOP job on 64 packed results: op and act are uniform per job,
+// so each (op, act) pair is its own straight-line loop.
+template <int OPK, int ACTK>
+__device__ __forceinline__ void post64(const PostOp& q, uint32_t* v2, const uint32_t* b2) {
+#pragma unroll
+  for (int j = 0; j < 32; j++) {
+    uint32_t packed = 0;
+#pragma unroll
+    for (int e = 0; e < 2; e++) {
+      const int32_t y = (int16_t)(v2[j] >> (16 * e)), z = (int16_t)(b2[j] >> (16 * e));
+      int32_t r = OPK == 0 ? y + z : (OPK == 1 ? y - z : (OPK == 2 ? z - y : (y * z) >> 8));
+      r = r > 32767 ? 32767 : (r < -32768 ? -32768 : r);
+      if (ACTK == 1) r = r < 0 ? 0 : r;
+      if (ACTK == 2) r = r < 0 ? 0 : (r > 1536 ? 1536 : r);
+      if (ACTK == 3 && r < 0) r = (int32_t)corm_rne_shr64((int64_t)r * (int64_t)(q.alpha & 0xFFFFu), 16);
+      if (ACTK == 4) r = __ldg(q.table + (r + 32768));
+      packed |= (uint32_t)(uint16_t)r << (16 * e);
+    }
+    v2[j] = packed;
+  }
+}
+
+template <int OPK>
+__device__ __forceinline__ void post_act(const PostOp& q, uint32_t* v2, const uint32_t* b2) {
+  switch (q.act) {
+    case 0: post64<OPK, 0>(q, v2, b2); break;
+    case 1: post64<OPK, 1>(q, v2, b2); break;
+    case 2: post64<OPK, 2>(q, v2, b2); break;
+    case 3: post64<OPK, 3>(q, v2, b2); break;
+    default: post64<OPK, 4>(q, v2, b2); break;
+  }
+}
+
+__device__ __forceinline__ void post_dispatch(const PostOp& q, uint32_t* v2, const uint32_t* b2) {
+  if (q.op == 0)
+    post_act<0>(q, v2, b2);
+  else if (q.op == 1)
+    (q.rev ? post_act<2>(q, v2, b2) : post_act<1>(q, v2, b2));
+  else
+    post_act<3>(q, v2, b2);
+}
+
 // column c's offset within an output row (mode 0: c; mode 1: the y channel pattern)
 __device__ __forceinline__ uint64_t col_offset(const EpiArgs& ep, uint32_t c) {
   if (ep.mode == 0) return c;
@@ -344,12 +386,7 @@ __global__ void __launch_bounds__(THREADS, 1)
             b2[j / 2] = lo | (hi << 16);
           }
         }
-#pragma unroll
-        for (int j = 0; j < 32; j++) {
-          const int16_t y0 = post_apply(ep.post, (int16_t)(v2[j] & 0xFFFF), (int16_t)(b2[j] & 0xFFFF));
-          const int16_t y1 = post_apply(ep.post, (int16_t)(v2[j] >> 16), (int16_t)(b2[j] >> 16));
-          v2[j] = (uint32_t)(uint16_t)y0 | ((uint32_t)(uint16_t)y1 << 16);
-        }
+        post_dispatch(ep.post, v2, b2);
       }
       const uint32_t c0 = w.tile_c + 64 * h;
       if (ep.mode == 0) {
