@@ -20,6 +20,7 @@
 // and MMAs waited for, TMEM freed).
 #include <cudaTypedefs.h>
 
+#include <cstring>
 #include <mutex>
 
 #include "corm_common.cuh"
@@ -36,7 +37,6 @@ constexpr int STAGE_BYTES = 4 * TILE_BYTES;
 constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
 constexpr uint32_t TMEM_COLS = 512;
 constexpr int EPI_WARPS = 8;
-constexpr int THREADS = 64 + 32 * EPI_WARPS;
 constexpr int NUM_SMS = 148;
 
 struct EpiArgs {
@@ -52,6 +52,11 @@ struct EpiArgs {
   uint32_t tiles_m, tiles_n, batch, splits, kb_per_split;
   unsigned long long* partial;
   PostOp post;
+  // int16 operands for the in-kernel split (a_bs16 / b_bs16 0: one plane for every batch)
+  const int16_t* a16;
+  const int16_t* b16;
+  uint64_t a_bs16, b_bs16;
+  uint32_t lda, ldb;
   uint32_t ymode;  // 0: the rule in int32 (small K), 1: in int64, 2: int32 wrap (CORM_F_WRAP32)
   int* err;
 };
@@ -97,27 +102,18 @@ __device__ __forceinline__ uint64_t out_offset(const EpiArgs& ep, uint32_t bz, u
   return (uint64_t)n * ep.img_stride + coff + p;
 }
 
-// 32 accumulator columns of one row -> 16 packed int16 pairs (mode 1 adds the bias)
-template <int YMODE>
-__device__ __forceinline__ void combine32(const EpiArgs& ep, const uint32_t* hh, const uint32_t* mid,
-                                          const uint32_t* ll, uint32_t c0, uint32_t* out2) {
-  const bool cbias = ep.mode == 1 && ep.bias;
-#pragma unroll
-  for (int j = 0; j < 32; j += 2) {
-    const int32_t b0 = (cbias && c0 + j < ep.cols) ? ep.bias[c0 + j] : 0;
-    const int32_t b1 = (cbias && c0 + j + 1 < ep.cols) ? ep.bias[c0 + j + 1] : 0;
-    const int16_t y0 = combine<YMODE>(hh[j], mid[j], ll[j], b0, ep.flags);
-    const int16_t y1 = combine<YMODE>(hh[j + 1], mid[j + 1], ll[j + 1], b1, ep.flags);
-    out2[j / 2] = (uint32_t)(uint16_t)y0 | ((uint32_t)(uint16_t)y1 << 16);
-  }
+// column c's offset within an output row (mode 0: c; mode 1: the y channel pattern)
+__device__ __forceinline__ uint64_t col_offset(const EpiArgs& ep, uint32_t c) {
+  if (ep.mode == 0) return c;
+  return ep.y_cn ? (uint64_t)(c % ep.y_cn) * ep.y_cs + (uint64_t)(c / ep.y_cn) * ep.y_gs : (uint64_t)c * ep.y_cs;
 }
 
 // The fused VectorOP job on 64 packed results: op and act are uniform per job,
 // so each (op, act) pair is its own straight-line loop.
-template <int OPK, int ACTK>
+template <int N2, int OPK, int ACTK>
 __device__ __forceinline__ void post64(const PostOp& q, uint32_t* v2, const uint32_t* b2) {
 #pragma unroll
-  for (int j = 0; j < 32; j++) {
+  for (int j = 0; j < N2; j++) {
     uint32_t packed = 0;
 #pragma unroll
     for (int e = 0; e < 2; e++) {
@@ -134,30 +130,87 @@ __device__ __forceinline__ void post64(const PostOp& q, uint32_t* v2, const uint
   }
 }
 
-template <int OPK>
+template <int N2, int OPK>
 __device__ __forceinline__ void post_act(const PostOp& q, uint32_t* v2, const uint32_t* b2) {
   switch (q.act) {
-    case 0: post64<OPK, 0>(q, v2, b2); break;
-    case 1: post64<OPK, 1>(q, v2, b2); break;
-    case 2: post64<OPK, 2>(q, v2, b2); break;
-    case 3: post64<OPK, 3>(q, v2, b2); break;
-    default: post64<OPK, 4>(q, v2, b2); break;
+    case 0: post64<N2, OPK, 0>(q, v2, b2); break;
+    case 1: post64<N2, OPK, 1>(q, v2, b2); break;
+    case 2: post64<N2, OPK, 2>(q, v2, b2); break;
+    case 3: post64<N2, OPK, 3>(q, v2, b2); break;
+    default: post64<N2, OPK, 4>(q, v2, b2); break;
   }
 }
 
+// N2 packed pairs of results (v2) against the operand pairs (b2)
+template <int N2>
 __device__ __forceinline__ void post_dispatch(const PostOp& q, uint32_t* v2, const uint32_t* b2) {
   if (q.op == 0)
-    post_act<0>(q, v2, b2);
+    post_act<N2, 0>(q, v2, b2);
   else if (q.op == 1)
-    (q.rev ? post_act<2>(q, v2, b2) : post_act<1>(q, v2, b2));
+    (q.rev ? post_act<N2, 2>(q, v2, b2) : post_act<N2, 1>(q, v2, b2));
   else
-    post_act<3>(q, v2, b2);
+    post_act<N2, 3>(q, v2, b2);
 }
 
-// column c's offset within an output row (mode 0: c; mode 1: the y channel pattern)
-__device__ __forceinline__ uint64_t col_offset(const EpiArgs& ep, uint32_t c) {
-  if (ep.mode == 0) return c;
-  return ep.y_cn ? (uint64_t)(c % ep.y_cn) * ep.y_cs + (uint64_t)(c / ep.y_cn) * ep.y_gs : (uint64_t)c * ep.y_cs;
+// the fused job's operand for NC consecutive outputs of one row (columns cb ..),
+// packed in pairs; every load issued before any use
+template <int NC>
+__device__ __forceinline__ void post_operand(const EpiArgs& ep, uint64_t rowbase, uint32_t cb, uint32_t* b2) {
+  const int16_t* bsrc = ep.post.b_mode == 0 ? ep.post.b + cb : ep.post.b + rowbase + cb;
+  if (ep.post.b_mode == 2) {
+    const uint32_t v = (uint16_t)__ldg(ep.post.b);
+#pragma unroll
+    for (int j = 0; j < NC / 2; j++) b2[j] = v | (v << 16);
+  } else if ((ep.mode == 0 || ep.post.b_mode == 0) && cb + NC <= ep.cols && ((uintptr_t)bsrc & 15) == 0) {
+#pragma unroll
+    for (int j = 0; j < NC / 8; j++) {
+      const int4 t = __ldg((const int4*)bsrc + j);
+      b2[4 * j] = (uint32_t)t.x;
+      b2[4 * j + 1] = (uint32_t)t.y;
+      b2[4 * j + 2] = (uint32_t)t.z;
+      b2[4 * j + 3] = (uint32_t)t.w;
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < NC; j += 2) {
+      const uint32_t ca = cb + j, cc2 = cb + j + 1;
+      const uint32_t lo = ca < ep.cols ? (uint16_t)post_b(ep.post, rowbase + col_offset(ep, ca), ca) : 0u;
+      const uint32_t hi = cc2 < ep.cols ? (uint16_t)post_b(ep.post, rowbase + col_offset(ep, cc2), cc2) : 0u;
+      b2[j / 2] = lo | (hi << 16);
+    }
+  }
+}
+
+// NC consecutive results of row r (columns c0 ..) to the output
+template <int NC>
+__device__ __forceinline__ void store_row(const EpiArgs& ep, uint32_t bz, uint32_t r, uint32_t c0, const uint32_t* v2) {
+  if (ep.mode == 0) {
+    int16_t* dst = ep.out + out_offset(ep, bz, r, c0);
+    if (c0 + NC <= ep.cols && ((uintptr_t)dst & 15) == 0) {
+#pragma unroll
+      for (int j = 0; j < NC / 8; j++)
+        ((int4*)dst)[j] = make_int4((int)v2[4 * j], (int)v2[4 * j + 1], (int)v2[4 * j + 2], (int)v2[4 * j + 3]);
+    } else {
+#pragma unroll
+      for (int j = 0; j < NC; j++)
+        if (c0 + j < ep.cols) dst[j] = (int16_t)(v2[j / 2] >> (16 * (j & 1)));
+    }
+  } else {  // NCHW: the row's image and pixel once, the channel offset per column
+    const uint32_t n = r / ep.P, p = r - n * ep.P;
+    int16_t* base = ep.out + (uint64_t)n * ep.img_stride + p;
+#pragma unroll
+    for (int j = 0; j < NC; j++) {
+      const uint32_t c = c0 + j;
+      if (c >= ep.cols) break;
+      base[col_offset(ep, c)] = (int16_t)(v2[j / 2] >> (16 * (j & 1)));
+    }
+  }
+}
+
+__device__ __forceinline__ uint64_t row_base(const EpiArgs& ep, uint32_t bz, uint32_t r) {
+  if (ep.mode == 0) return (uint64_t)bz * ep.out_batch_stride + (uint64_t)r * ep.ldc;
+  const uint32_t n = r / ep.P;
+  return (uint64_t)n * ep.img_stride + (r - n * ep.P);
 }
 
 struct Unit {
@@ -177,10 +230,61 @@ __device__ __forceinline__ Unit unit_of(const EpiArgs& ep, uint32_t u) {
   return w;
 }
 
-__global__ void __launch_bounds__(THREADS, 1)
+// Warp roles.  Plane operands (CONV = false): warp 0 lane 0 issues the TMA
+// loads, warp 1 owns TMEM and lane 0 issues the MMAs, warps 2..9 run the
+// epilogue.  int16 operands (CONV = true): warp 0 owns TMEM and issues the
+// MMAs, warps 1..8 load int16 tiles, split them into the hi / lo planes and
+// store them in the 128-byte swizzled layout the MMA descriptors read, warps
+// 9..16 run the epilogue.
+template <bool CONV>
+struct Roles {
+  static constexpr int threads = CONV ? 64 + 32 * (8 + EPI_WARPS) - 32 : 64 + 32 * EPI_WARPS;
+  static constexpr int mma_warp = CONV ? 0 : 1;
+  static constexpr int epi0 = CONV ? 9 : 2;
+  static constexpr int chunk = CONV ? 16 : 32;  // TMEM columns per tcgen05.ld (register budget)
+};
+
+// 16 int16 (two 16-byte words) -> their 16 high bytes and 16 low bytes
+__device__ __forceinline__ void split16_regs(const int4& w0, const int4& w1, int4& hi, int4& lo) {
+  hi.x = (int)__byte_perm((uint32_t)w0.x, (uint32_t)w0.y, 0x7531);
+  hi.y = (int)__byte_perm((uint32_t)w0.z, (uint32_t)w0.w, 0x7531);
+  hi.z = (int)__byte_perm((uint32_t)w1.x, (uint32_t)w1.y, 0x7531);
+  hi.w = (int)__byte_perm((uint32_t)w1.z, (uint32_t)w1.w, 0x7531);
+  lo.x = (int)__byte_perm((uint32_t)w0.x, (uint32_t)w0.y, 0x6420);
+  lo.y = (int)__byte_perm((uint32_t)w0.z, (uint32_t)w0.w, 0x6420);
+  lo.z = (int)__byte_perm((uint32_t)w1.x, (uint32_t)w1.y, 0x6420);
+  lo.w = (int)__byte_perm((uint32_t)w1.z, (uint32_t)w1.w, 0x6420);
+}
+
+template <int CW, int YMODE>
+__device__ __forceinline__ void combine_cw(const EpiArgs& ep, const uint32_t* hh, const uint32_t* mid,
+                                           const uint32_t* ll, uint32_t c0, uint32_t* out2) {
+  const bool cbias = ep.mode == 1 && ep.bias;
+#pragma unroll
+  for (int j = 0; j < CW; j += 2) {
+    const int32_t b0 = (cbias && c0 + j < ep.cols) ? ep.bias[c0 + j] : 0;
+    const int32_t b1 = (cbias && c0 + j + 1 < ep.cols) ? ep.bias[c0 + j + 1] : 0;
+    const int16_t y0 = combine<YMODE>(hh[j], mid[j], ll[j], b0, ep.flags);
+    const int16_t y1 = combine<YMODE>(hh[j + 1], mid[j + 1], ll[j + 1], b1, ep.flags);
+    out2[j / 2] = (uint32_t)(uint16_t)y0 | ((uint32_t)(uint16_t)y1 << 16);
+  }
+}
+
+template <int CW>
+__device__ __forceinline__ void tmem_ld_cw(uint32_t taddr, uint32_t* r) {
+  if (CW == 32)
+    sm100::tmem_ld32(taddr, *reinterpret_cast<uint32_t(*)[32]>(r));
+  else
+    sm100::tmem_ld16(taddr, r);
+}
+
+template <bool CONV>
+__global__ void __launch_bounds__(Roles<CONV>::threads, 1)
     gemm_i8x4_kernel(const __grid_constant__ CUtensorMap map_ahi, const __grid_constant__ CUtensorMap map_alo,
                      const __grid_constant__ CUtensorMap map_bhi, const __grid_constant__ CUtensorMap map_blo,
                      const EpiArgs ep) {
+  using R = Roles<CONV>;
+  constexpr int CW = R::chunk;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
   uint64_t* full = (uint64_t*)(smem + STAGES * STAGE_BYTES);
@@ -195,7 +299,7 @@ __global__ void __launch_bounds__(THREADS, 1)
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; s++) {
-      sm100::mbar_init(&full[s], 1);
+      sm100::mbar_init(&full[s], CONV ? 8 : 1);
       sm100::mbar_init(&empty[s], 1);
     }
     sm100::mbar_init(tmem_full, 1);
@@ -203,13 +307,13 @@ __global__ void __launch_bounds__(THREADS, 1)
     sm100::mbar_init(mma_done, 1);
     sm100::fence_mbar_init();
   }
-  if (warp == 1) sm100::tmem_alloc<TMEM_COLS>(tmem_slot);
+  if (warp == R::mma_warp) sm100::tmem_alloc<TMEM_COLS>(tmem_slot);
   sm100::tc_fence_before();
   __syncthreads();
   sm100::tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp == 0 && lane == 0) {
+  if (!CONV && warp == 0 && lane == 0) {
     // ---------------- TMA producer (ring counter g runs across units)
     sm100::prefetch_tmap(&map_ahi);
     sm100::prefetch_tmap(&map_alo);
@@ -245,7 +349,63 @@ __global__ void __launch_bounds__(THREADS, 1)
       for (uint32_t q = g > (uint32_t)STAGES ? g - STAGES : 0; q < g; q++)
         sm100::mbar_wait(&full[q % STAGES], (q / STAGES) & 1, nullptr, 0, 200000000ll);
     }
-  } else if (warp == 1 && lane == 0) {
+  } else if (CONV && warp >= 1 && warp <= 8) {
+    // ---------------- int16 producers: per stage the A tile (128 rows x 128 K)
+    // and the MN-major B tile (128 K rows x 128 columns), each as 1024 units of
+    // 16 consecutive int16 -> a 16-byte hi unit and a 16-byte lo unit at the
+    // row's swizzled position (unit u of row r at (u ^ (r & 7)) * 16); rows,
+    // K and columns beyond the job are zeros.  K and the column count are
+    // multiples of 8, every base 16-byte aligned (the host checks).
+    const uint32_t pt = (uint32_t)(warp - 1) * 32u + lane;
+    uint32_t g = 0;
+    bool ok = true;
+    for (uint32_t u = blockIdx.x; u < units && ok; u += gridDim.x) {
+      const Unit w = unit_of(ep, u);
+      const int16_t* Ab = ep.a16 + (uint64_t)w.bz * ep.a_bs16;
+      const int16_t* Bb = ep.b16 + (uint64_t)w.bz * ep.b_bs16;
+      for (uint32_t kb = w.kb0; kb < w.kb1; kb++, g++) {
+        const int s = g % STAGES;
+        if (g >= (uint32_t)STAGES && !sm100::mbar_wait(&empty[s], ((g / STAGES) - 1) & 1, ep.err, 101)) {
+          ok = false;
+          break;
+        }
+        uint8_t* st = smem + s * STAGE_BYTES;
+        int4 va[4][2], vb[4][2];
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+          const uint32_t id = pt + 256u * i, row = id >> 3, uu = id & 7u;
+          const int4 z = make_int4(0, 0, 0, 0);
+          // A row tile_r + row, K kb*128 + 16 uu ..
+          const uint32_t ar = w.tile_r + row, ak = kb * BK + uu * 16u;
+          const int16_t* pa = Ab + (uint64_t)ar * ep.lda + ak;
+          const bool ar_ok = ar < ep.rows;
+          va[i][0] = (ar_ok && ak < ep.K) ? __ldg((const int4*)pa) : z;
+          va[i][1] = (ar_ok && ak + 8u < ep.K) ? __ldg((const int4*)pa + 1) : z;
+          // B K row kb*128 + row, columns tile_c + 16 uu ..
+          const uint32_t bk = kb * BK + row, bc = w.tile_c + uu * 16u;
+          const int16_t* pb = Bb + (uint64_t)bk * ep.ldb + bc;
+          const bool bk_ok = bk < ep.K;
+          vb[i][0] = (bk_ok && bc < ep.cols) ? __ldg((const int4*)pb) : z;
+          vb[i][1] = (bk_ok && bc + 8u < ep.cols) ? __ldg((const int4*)pb + 1) : z;
+        }
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+          const uint32_t id = pt + 256u * i, row = id >> 3, uu = id & 7u;
+          const uint32_t off = row * 128u + ((uu ^ (row & 7u)) << 4);
+          int4 hi, lo;
+          split16_regs(va[i][0], va[i][1], hi, lo);
+          *(int4*)(st + off) = hi;
+          *(int4*)(st + TILE_BYTES + off) = lo;
+          split16_regs(vb[i][0], vb[i][1], hi, lo);
+          *(int4*)(st + 2 * TILE_BYTES + off) = hi;
+          *(int4*)(st + 3 * TILE_BYTES + off) = lo;
+        }
+        sm100::fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) sm100::mbar_arrive(&full[s]);
+      }
+    }
+  } else if (warp == R::mma_warp && lane == 0) {
     // ---------------- MMA issuer
     const uint32_t bmaj = ep.b_mn ? (1u << 16) : 0u;
     const uint32_t ID_SS = sm100::idesc_i8(BM, BN, 1, 1) | bmaj;
@@ -292,12 +452,12 @@ __global__ void __launch_bounds__(THREADS, 1)
     // every MMA issued has completed before TMEM is freed
     sm100::mma_commit(mma_done);
     sm100::mbar_wait(mma_done, 0, nullptr, 0, 200000000ll);
-  } else if (warp >= 2) {
-    // ---------------- epilogue: warp (2 + 4 h + j) reads lane quarter (warp % 4),
+  } else if (warp >= R::epi0) {
+    // ---------------- epilogue: warp (epi0 + 4 h + j) reads lane quarter (warp % 4),
     // columns [64 h, 64 h + 64)
     const int q = warp & 3;  // TMEM lane quarter this warp may access
     const uint32_t lane_addr = (uint32_t)(q * 32) << 16;
-    const int h = (warp - 2) >> 2;
+    const int h = (warp - R::epi0) >> 2;
     uint32_t i = 0;
     for (uint32_t u = blockIdx.x; u < units; u += gridDim.x, i++) {
       const Unit w = unit_of(ep, u);
@@ -306,22 +466,22 @@ __global__ void __launch_bounds__(THREADS, 1)
       const uint32_t r = w.tile_r + q * 32 + lane;
       const bool row_ok = r < ep.rows;
       if (ep.partial) {
-        for (int cc = 64 * h; cc < 64 * h + 64; cc += 32) {
-          uint32_t hh[32], mid[32], ll[32];
-          sm100::tmem_ld32(tmem + lane_addr + cc, hh);
-          sm100::tmem_ld32(tmem + lane_addr + BN + cc, mid);
-          sm100::tmem_ld32(tmem + lane_addr + 2 * BN + cc, ll);
+        for (int cc = 64 * h; cc < 64 * h + 64; cc += CW) {
+          uint32_t hh[CW], mid[CW], ll[CW];
+          tmem_ld_cw<CW>(tmem + lane_addr + cc, hh);
+          tmem_ld_cw<CW>(tmem + lane_addr + BN + cc, mid);
+          tmem_ld_cw<CW>(tmem + lane_addr + 2 * BN + cc, ll);
           sm100::tmem_ld_wait();
-          if (cc + 32 >= 64 * h + 64) {  // TMEM drained: the next unit's MMAs may start
+          if (cc + CW >= 64 * h + 64) {  // TMEM drained: the next unit's MMAs may start
             sm100::tc_fence_before();
             __syncwarp();
-            if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(sm100::smem_u32(tmem_empty)) : "memory");
+            if (lane == 0) sm100::mbar_arrive(tmem_empty);
           }
           if (!row_ok) continue;
           const uint32_t c0 = w.tile_c + cc;
           unsigned long long* dst = ep.partial + ((uint64_t)w.bz * ep.rows + r) * ep.cols + c0;
 #pragma unroll
-          for (int j = 0; j < 32; j++) {
+          for (int j = 0; j < CW; j++) {
             if (c0 + j >= ep.cols) continue;
             const int64_t acc = ((int64_t)(int32_t)hh[j] << 16) + ((int64_t)(int32_t)mid[j] << 8) + (int64_t)(int32_t)ll[j];
             atomicAdd(dst + j, (unsigned long long)acc);
@@ -329,93 +489,76 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
         continue;
       }
-      // the 64 results of this thread's row as int16 pairs, then TMEM released
-      uint32_t v2[32];
+      if (CW == 32) {
+        // the 64 results of this thread's row as int16 pairs, then TMEM released,
+        // then the fused job and the stores
+        uint32_t v2[32];
 #pragma unroll
-      for (int half = 0; half < 2; half++) {
-        const int cc = 64 * h + 32 * half;
-        uint32_t hh[32], mid[32], ll[32];
-        sm100::tmem_ld32(tmem + lane_addr + cc, hh);
-        sm100::tmem_ld32(tmem + lane_addr + BN + cc, mid);
-        sm100::tmem_ld32(tmem + lane_addr + 2 * BN + cc, ll);
-        sm100::tmem_ld_wait();
-        const uint32_t c0 = w.tile_c + cc;
-        if (ep.ymode == 0)
-          combine32<0>(ep, hh, mid, ll, c0, v2 + 16 * half);
-        else if (ep.ymode == 1)
-          combine32<1>(ep, hh, mid, ll, c0, v2 + 16 * half);
-        else
-          combine32<2>(ep, hh, mid, ll, c0, v2 + 16 * half);
-      }
-      sm100::tc_fence_before();
-      __syncwarp();
-      if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(sm100::smem_u32(tmem_empty)) : "memory");
-      if (!row_ok) continue;
-      if (ep.post.op != kPostNone) {
-        // the fused VectorOP job: its operand for these 64 outputs (every load
-        // issued before any use), then op + act
-        const uint32_t cb = w.tile_c + 64 * h;
-        uint32_t b2[32];
-        uint64_t rowbase;
-        if (ep.mode == 0) {
-          rowbase = (uint64_t)w.bz * ep.out_batch_stride + (uint64_t)r * ep.ldc;
-        } else {
-          const uint32_t n = r / ep.P;
-          rowbase = (uint64_t)n * ep.img_stride + (r - n * ep.P);
+        for (int part = 0; part < 2; part++) {
+          const int cc = 64 * h + 32 * part;
+          uint32_t hh[32], mid[32], ll[32];
+          tmem_ld_cw<32>(tmem + lane_addr + cc, hh);
+          tmem_ld_cw<32>(tmem + lane_addr + BN + cc, mid);
+          tmem_ld_cw<32>(tmem + lane_addr + 2 * BN + cc, ll);
+          sm100::tmem_ld_wait();
+          const uint32_t c0 = w.tile_c + cc;
+          if (ep.ymode == 0)
+            combine_cw<32, 0>(ep, hh, mid, ll, c0, v2 + 16 * part);
+          else if (ep.ymode == 1)
+            combine_cw<32, 1>(ep, hh, mid, ll, c0, v2 + 16 * part);
+          else
+            combine_cw<32, 2>(ep, hh, mid, ll, c0, v2 + 16 * part);
         }
-        const int16_t* bsrc = ep.post.b_mode == 0 ? ep.post.b + cb : ep.post.b + rowbase + cb;
-        if (ep.post.b_mode == 2) {
-          const uint32_t v = (uint16_t)__ldg(ep.post.b);
-#pragma unroll
-          for (int j = 0; j < 32; j++) b2[j] = v | (v << 16);
-        } else if ((ep.mode == 0 || ep.post.b_mode == 0) && cb + 64 <= ep.cols && ((uintptr_t)bsrc & 15) == 0) {
-#pragma unroll
-          for (int j = 0; j < 8; j++) {
-            const int4 t = __ldg((const int4*)bsrc + j);
-            b2[4 * j] = (uint32_t)t.x;
-            b2[4 * j + 1] = (uint32_t)t.y;
-            b2[4 * j + 2] = (uint32_t)t.z;
-            b2[4 * j + 3] = (uint32_t)t.w;
+        sm100::tc_fence_before();
+        __syncwarp();
+        if (lane == 0) sm100::mbar_arrive(tmem_empty);
+        if (!row_ok) continue;
+        const uint32_t c0 = w.tile_c + 64 * h;
+        if (ep.post.op != kPostNone) {
+          uint32_t b2[32];
+          post_operand<64>(ep, row_base(ep, w.bz, r), c0, b2);
+          post_dispatch<32>(ep.post, v2, b2);
+        }
+        store_row<64>(ep, w.bz, r, c0, v2);
+      } else {
+        // 16 columns at a time (the register budget of the int16-producer layout):
+        // TMEM released after the last chunk's load
+        const uint64_t rb = row_ok && ep.post.op != kPostNone ? row_base(ep, w.bz, r) : 0;
+#pragma unroll 1
+        for (int part = 0; part < 4; part++) {
+          const int cc = 64 * h + 16 * part;
+          uint32_t hh[16], mid[16], ll[16];
+          tmem_ld_cw<16>(tmem + lane_addr + cc, hh);
+          tmem_ld_cw<16>(tmem + lane_addr + BN + cc, mid);
+          tmem_ld_cw<16>(tmem + lane_addr + 2 * BN + cc, ll);
+          sm100::tmem_ld_wait();
+          if (part == 3) {
+            sm100::tc_fence_before();
+            __syncwarp();
+            if (lane == 0) sm100::mbar_arrive(tmem_empty);
           }
-        } else {
-#pragma unroll
-          for (int j = 0; j < 64; j += 2) {
-            const uint32_t ca = cb + j, cc2 = cb + j + 1;
-            const uint32_t lo = ca < ep.cols ? (uint16_t)post_b(ep.post, rowbase + col_offset(ep, ca), ca) : 0u;
-            const uint32_t hi = cc2 < ep.cols ? (uint16_t)post_b(ep.post, rowbase + col_offset(ep, cc2), cc2) : 0u;
-            b2[j / 2] = lo | (hi << 16);
+          if (!row_ok) continue;
+          const uint32_t c0 = w.tile_c + cc;
+          uint32_t v8[8];
+          if (ep.ymode == 0)
+            combine_cw<16, 0>(ep, hh, mid, ll, c0, v8);
+          else if (ep.ymode == 1)
+            combine_cw<16, 1>(ep, hh, mid, ll, c0, v8);
+          else
+            combine_cw<16, 2>(ep, hh, mid, ll, c0, v8);
+          if (ep.post.op != kPostNone) {
+            uint32_t b8[8];
+            post_operand<16>(ep, rb, c0, b8);
+            post_dispatch<8>(ep.post, v8, b8);
           }
-        }
-        post_dispatch(ep.post, v2, b2);
-      }
-      const uint32_t c0 = w.tile_c + 64 * h;
-      if (ep.mode == 0) {
-        int16_t* dst = ep.out + out_offset(ep, w.bz, r, c0);
-        if (c0 + 64 <= ep.cols && ((uintptr_t)dst & 15) == 0) {
-#pragma unroll
-          for (int j = 0; j < 8; j++) ((int4*)dst)[j] = make_int4((int)v2[4 * j], (int)v2[4 * j + 1], (int)v2[4 * j + 2], (int)v2[4 * j + 3]);
-        } else {
-#pragma unroll
-          for (int j = 0; j < 64; j++)
-            if (c0 + j < ep.cols) dst[j] = (int16_t)(v2[j / 2] >> (16 * (j & 1)));
-        }
-      } else {  // NCHW: the row's image and pixel once, the channel offset per column
-        const uint32_t n = r / ep.P, p = r - n * ep.P;
-        int16_t* base = ep.out + (uint64_t)n * ep.img_stride + p;
-#pragma unroll
-        for (int j = 0; j < 64; j++) {
-          const uint32_t c = c0 + j;
-          if (c >= ep.cols) break;
-          const uint64_t coff = ep.y_cn ? (uint64_t)(c % ep.y_cn) * ep.y_cs + (uint64_t)(c / ep.y_cn) * ep.y_gs
-                                        : (uint64_t)c * ep.y_cs;
-          base[coff] = (int16_t)(v2[j / 2] >> (16 * (j & 1)));
+          store_row<16>(ep, w.bz, r, c0, v8);
         }
       }
     }
   }
   sm100::tc_fence_before();
   __syncthreads();
-  if (warp == 1) {
+  if (warp == R::mma_warp) {
     sm100::tc_fence_after();
     sm100::tmem_dealloc<TMEM_COLS>(tmem);
   }
@@ -581,12 +724,21 @@ int gemm_i8x4(const GemmJob& j, cudaStream_t stream) {
   int* err = j.err ? j.err : device_error_word();
   if (!err) return fail(CORM_ECUDA, "gemm: error word allocation failed");
   CUtensorMap m_ahi, m_alo, m_bhi, m_blo;
-  bool ok = make_map(&m_ahi, j.a_hi, j.Kp, j.rows, j.a_planes) && make_map(&m_alo, j.a_lo, j.Kp, j.rows, j.a_planes);
-  if (j.b_mn)
-    ok = ok && make_map(&m_bhi, j.b_hi, j.cols_p, j.K, j.b_planes) && make_map(&m_blo, j.b_lo, j.cols_p, j.K, j.b_planes);
-  else
-    ok = ok && make_map(&m_bhi, j.b_hi, j.Kp, j.cols, j.b_planes) && make_map(&m_blo, j.b_lo, j.Kp, j.cols, j.b_planes);
-  if (!ok) return fail(CORM_ECUDA, "gemm: cuTensorMapEncodeTiled failed");
+  const bool conv = j.a16 != nullptr;  // int16 operands split inside the kernel
+  if (conv) {
+    if (((uintptr_t)j.a16 | (uintptr_t)j.b16) & 15u || j.lda % 8u || j.ldb % 8u || j.a_bs16 % 8u || j.b_bs16 % 8u ||
+        j.K % 8u || j.cols % 8u)
+      return fail(CORM_EINVAL, "gemm: int16 operands not on 16-byte rows");
+    memset(&m_ahi, 0, sizeof m_ahi);
+    m_alo = m_bhi = m_blo = m_ahi;
+  } else {
+    bool ok = make_map(&m_ahi, j.a_hi, j.Kp, j.rows, j.a_planes) && make_map(&m_alo, j.a_lo, j.Kp, j.rows, j.a_planes);
+    if (j.b_mn)
+      ok = ok && make_map(&m_bhi, j.b_hi, j.cols_p, j.K, j.b_planes) && make_map(&m_blo, j.b_lo, j.cols_p, j.K, j.b_planes);
+    else
+      ok = ok && make_map(&m_bhi, j.b_hi, j.Kp, j.cols, j.b_planes) && make_map(&m_blo, j.b_lo, j.Kp, j.cols, j.b_planes);
+    if (!ok) return fail(CORM_ECUDA, "gemm: cuTensorMapEncodeTiled failed");
+  }
   const Split sp = split_of(j.rows, j.cols, j.Kp, j.batch);
   EpiArgs ep{};
   ep.mode = j.mode;
@@ -611,7 +763,13 @@ int gemm_i8x4(const GemmJob& j, cudaStream_t stream) {
   ep.num_kb = sp.num_kb;
   ep.a_planes = j.a_planes;
   ep.b_planes = j.b_planes;
-  ep.b_mn = j.b_mn;
+  ep.b_mn = conv ? 1u : j.b_mn;
+  ep.a16 = j.a16;
+  ep.b16 = j.b16;
+  ep.a_bs16 = j.a_bs16;
+  ep.b_bs16 = j.b_bs16;
+  ep.lda = j.lda;
+  ep.ldb = j.ldb;
   ep.K = j.K ? j.K : j.Kp;
   ep.tiles_m = (j.rows + BM - 1) / BM;
   ep.tiles_n = (j.cols + BN - 1) / BN;
@@ -630,7 +788,8 @@ int gemm_i8x4(const GemmJob& j, cudaStream_t stream) {
   int dev = 0;
   cudaGetDevice(&dev);
   if (!attr_set[dev]) {
-    cudaFuncSetAttribute(gemm_i8x4_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+    cudaFuncSetAttribute(gemm_i8x4_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+    cudaFuncSetAttribute(gemm_i8x4_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
     attr_set[dev] = true;
   }
   const uint64_t units = (uint64_t)sp.tiles * sp.splits;
@@ -638,7 +797,10 @@ int gemm_i8x4(const GemmJob& j, cudaStream_t stream) {
   const unsigned grid = (unsigned)(units < (uint64_t)NUM_SMS ? units : NUM_SMS);
   {
     ProfScope prof_("gemm_i8x4_kernel", stream);
-    gemm_i8x4_kernel<<<grid, THREADS, SMEM_BYTES, stream>>>(m_ahi, m_alo, m_bhi, m_blo, ep);
+    if (conv)
+      gemm_i8x4_kernel<true><<<grid, Roles<true>::threads, SMEM_BYTES, stream>>>(m_ahi, m_alo, m_bhi, m_blo, ep);
+    else
+      gemm_i8x4_kernel<false><<<grid, Roles<false>::threads, SMEM_BYTES, stream>>>(m_ahi, m_alo, m_bhi, m_blo, ep);
   }
   if (int rc = cuda_status("gemm_i8x4")) return rc;
   if (sp.splits > 1) {

@@ -40,6 +40,13 @@ struct GemmJob {
   const int16_t* bias;      // mode 1 bias per column (raw), or nullptr
   uint32_t flags;           // CORM_F_WRAP32 | CORM_F_ACT_RELU | CORM_F_ACT_RELU6
   PostOp post;              // fused VectorOP job on the result (op kPostNone: none)
+  // int16 operands split inside the kernel instead of the planes above (a16 != nullptr):
+  // A [batch][rows][lda] K-major, B [batch][K][ldb] MN-major (b_mn implied), batch
+  // strides in elements (0: shared), 16-byte aligned rows, K and cols multiples of 8
+  const int16_t* a16;
+  const int16_t* b16;
+  uint64_t a_bs16, b_bs16;
+  uint32_t lda, ldb;
   int* err;                 // status word for the bounded waits; nullptr: the library's per-device word
 };
 

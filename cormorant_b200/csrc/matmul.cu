@@ -186,6 +186,71 @@ Plan plan_of(const corm_matmul_desc* d) {
   return pl;
 }
 
+// The tensor-core path of a job with n >= 3 rows.  Row-major B with K and m
+// multiples of 8 on 16-byte aligned rows: the GEMM reads the int16 operands
+// and splits them itself (only a K-split partial-sum buffer in the
+// workspace); otherwise the operands are split into int8 planes first.  The
+// workspace is sized for the second case.
+int tensor_path(const corm_matmul_desc* d, const MmArgs& p, const Plan& pl, uint8_t* w, const corm::PostOp& post,
+                int* err, cudaStream_t st) {
+  const bool direct = !d->b_packed && d->gemv_kw <= 1 && d->k % 8 == 0 && d->m % 8 == 0 &&
+                      !(((uintptr_t)d->a | (uintptr_t)d->b) & 15u) &&
+                      (d->batch == 1 || (d->a_batch_stride % 8 == 0 && d->b_batch_stride % 8 == 0));
+  corm::GemmJob j{};
+  j.rows = d->n;
+  j.cols = d->m;
+  j.Kp = pl.Kp;
+  j.batch = d->batch;
+  j.a_planes = pl.a_planes;
+  j.b_planes = pl.b_planes;
+  j.b_mn = 1;
+  j.K = d->k;
+  j.cols_p = pl.Np;
+  j.mode = 0;
+  j.out = d->c;
+  j.out_batch_stride = d->c_batch_stride;
+  j.ldc = d->m;
+  j.flags = d->flags;
+  j.post = post;
+  j.err = err;
+  if (direct) {
+    j.a16 = d->a;
+    j.b16 = d->b;
+    j.a_bs16 = pl.a_planes == 1 ? 0 : d->a_batch_stride;
+    j.b_bs16 = pl.b_planes == 1 ? 0 : d->b_batch_stride;
+    j.lda = d->k;
+    j.ldb = d->m;
+    j.partial = pl.partial_bytes ? (void*)w : nullptr;
+    return corm::gemm_i8x4(j, st);
+  }
+  int8_t* a_hi = (int8_t*)w;
+  uint8_t* a_lo = w + pl.a_plane_bytes;
+  int8_t* b_hi = (int8_t*)(w + 2 * pl.a_plane_bytes);
+  uint8_t* b_lo = w + 2 * pl.a_plane_bytes + pl.b_plane_bytes;
+  if (!d->b_packed && d->gemv_kw <= 1) {
+    // row-major B is already MN-major: both operands split elementwise in one
+    // launch (B rows of m padded to Np)
+    const corm::SplitSeg sa{d->a, d->a_batch_stride, pl.a_planes, d->n, d->k, d->k, pl.Kp, a_hi, a_lo};
+    const corm::SplitSeg sb{d->b, d->b_batch_stride, pl.b_planes, d->k, d->m, d->m, pl.Np, b_hi, b_lo};
+    if (int rc = corm::split_planes2(sa, sb, st)) return rc;
+  } else {
+    if (int rc = corm::split_planes(d->a, d->a_batch_stride, pl.a_planes, d->n, d->k, d->k, pl.Kp, a_hi, a_lo, st))
+      return rc;
+    const uint64_t total = (uint64_t)pl.b_planes * d->k * (pl.Np / 16);
+    {
+      corm::ProfScope prof_("split_b_gather_kernel", st);
+      split_b_gather_kernel<<<corm_blocks(total, 256, 148u * 16u), 256, 0, st>>>(p, pl.b_planes, pl.Np, b_hi, b_lo);
+    }
+    if (int rc = corm::cuda_status("matmul split_b")) return rc;
+  }
+  j.a_hi = a_hi;
+  j.a_lo = a_lo;
+  j.b_hi = b_hi;
+  j.b_lo = b_lo;
+  j.partial = pl.partial_bytes ? (void*)(w + 2 * pl.a_plane_bytes + 2 * pl.b_plane_bytes) : nullptr;
+  return corm::gemm_i8x4(j, st);
+}
+
 int validate(const corm_matmul_desc* d) {
   if (!d) return corm::fail(CORM_EINVAL, "corm_matmul: null descriptor");
   if (d->k > kMaxK) return corm::fail(CORM_EINVAL, "corm_matmul: k %u beyond max_k %u", d->k, kMaxK);
@@ -263,49 +328,7 @@ int matmul_impl(const corm_matmul_desc* d, const corm::PostOp& post, cudaStream_
     }
     return CORM_OK;
   }
-  uint8_t* w = (uint8_t*)ws;
-  int8_t* a_hi = (int8_t*)w;
-  uint8_t* a_lo = w + pl.a_plane_bytes;
-  int8_t* b_hi = (int8_t*)(w + 2 * pl.a_plane_bytes);
-  uint8_t* b_lo = w + 2 * pl.a_plane_bytes + pl.b_plane_bytes;
-  if (!d->b_packed && d->gemv_kw <= 1) {
-    // row-major B is already MN-major: both operands split elementwise in one
-    // launch (B rows of m padded to Np)
-    const corm::SplitSeg sa{d->a, d->a_batch_stride, pl.a_planes, d->n, d->k, d->k, pl.Kp, a_hi, a_lo};
-    const corm::SplitSeg sb{d->b, d->b_batch_stride, pl.b_planes, d->k, d->m, d->m, pl.Np, b_hi, b_lo};
-    if (int rc = corm::split_planes2(sa, sb, st)) return rc;
-  } else {
-    if (int rc = corm::split_planes(d->a, d->a_batch_stride, pl.a_planes, d->n, d->k, d->k, pl.Kp, a_hi, a_lo, st))
-      return rc;
-    const uint64_t total = (uint64_t)pl.b_planes * d->k * (pl.Np / 16);
-    {
-      corm::ProfScope prof_("split_b_gather_kernel", st);
-      split_b_gather_kernel<<<corm_blocks(total, 256, 148u * 16u), 256, 0, st>>>(p, pl.b_planes, pl.Np, b_hi, b_lo);
-    }
-    if (int rc = corm::cuda_status("matmul split_b")) return rc;
-  }
-  corm::GemmJob j{};
-  j.a_hi = a_hi;
-  j.a_lo = a_lo;
-  j.b_hi = b_hi;
-  j.b_lo = b_lo;
-  j.rows = d->n;
-  j.cols = d->m;
-  j.Kp = pl.Kp;
-  j.batch = d->batch;
-  j.a_planes = pl.a_planes;
-  j.b_planes = pl.b_planes;
-  j.b_mn = 1;
-  j.K = d->k;
-  j.cols_p = pl.Np;
-  j.partial = pl.partial_bytes ? (void*)(w + 2 * pl.a_plane_bytes + 2 * pl.b_plane_bytes) : nullptr;
-  j.mode = 0;
-  j.out = d->c;
-  j.out_batch_stride = d->c_batch_stride;
-  j.ldc = d->m;
-  j.flags = d->flags;
-  j.post = post;
-  return corm::gemm_i8x4(j, st);
+  return tensor_path(d, p, pl, (uint8_t*)ws, post, nullptr, st);
 }
 }  // namespace
 
@@ -398,44 +421,5 @@ extern "C" int corm_matmul_noalloc(const corm_matmul_desc* d, corm_stream_t stre
     }
     return CORM_OK;
   }
-  int8_t* a_hi = (int8_t*)w;
-  uint8_t* a_lo = w + pl.a_plane_bytes;
-  int8_t* b_hi = (int8_t*)(w + 2 * pl.a_plane_bytes);
-  uint8_t* b_lo = w + 2 * pl.a_plane_bytes + pl.b_plane_bytes;
-  if (!d->b_packed && d->gemv_kw <= 1) {
-    const corm::SplitSeg sa{d->a, d->a_batch_stride, pl.a_planes, d->n, d->k, d->k, pl.Kp, a_hi, a_lo};
-    const corm::SplitSeg sb{d->b, d->b_batch_stride, pl.b_planes, d->k, d->m, d->m, pl.Np, b_hi, b_lo};
-    if (int rc = corm::split_planes2(sa, sb, st)) return rc;
-  } else {
-    if (int rc = corm::split_planes(d->a, d->a_batch_stride, pl.a_planes, d->n, d->k, d->k, pl.Kp, a_hi, a_lo, st))
-      return rc;
-    const uint64_t total = (uint64_t)pl.b_planes * d->k * (pl.Np / 16);
-    {
-      corm::ProfScope prof_("split_b_gather_kernel", st);
-      split_b_gather_kernel<<<corm_blocks(total, 256, 148u * 16u), 256, 0, st>>>(p, pl.b_planes, pl.Np, b_hi, b_lo);
-    }
-    if (int rc = corm::cuda_status("matmul_noalloc split_b")) return rc;
-  }
-  corm::GemmJob j{};
-  j.a_hi = a_hi;
-  j.a_lo = a_lo;
-  j.b_hi = b_hi;
-  j.b_lo = b_lo;
-  j.rows = d->n;
-  j.cols = d->m;
-  j.Kp = pl.Kp;
-  j.batch = d->batch;
-  j.a_planes = pl.a_planes;
-  j.b_planes = pl.b_planes;
-  j.b_mn = 1;
-  j.K = d->k;
-  j.cols_p = pl.Np;
-  j.partial = pl.partial_bytes ? (void*)(w + 2 * pl.a_plane_bytes + 2 * pl.b_plane_bytes) : nullptr;
-  j.mode = 0;
-  j.out = d->c;
-  j.out_batch_stride = d->c_batch_stride;
-  j.ldc = d->m;
-  j.flags = d->flags;
-  j.err = na.status;
-  return corm::gemm_i8x4(j, st);
+  return tensor_path(d, p, pl, w, corm::PostOp{}, na.status, st);
 }

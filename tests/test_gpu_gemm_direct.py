@@ -1,0 +1,57 @@
+"""The GEMM that reads int16 operands and splits them into the int8 planes
+in its producer warps (row-major B, K and m multiples of 8, 16-byte rows)
+against the oracle: partial row / column / K tiles, batches with shared
+operands (stride 0), the K split, the int32 wrap, full-range values."""
+import numpy as np
+import pytest
+
+torch = pytest.importorskip("torch")
+
+from oracle import spec  # noqa: E402
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def ops():
+    from cormorant_b200 import ops as o
+    return o
+
+
+CASES = [  # batch, n, k, m, a_shared, b_shared, flags, lo, hi
+    (1, 3, 8, 8, False, False, 0, -32768, 32768),
+    (1, 200, 136, 72, False, False, 0, -3000, 3000),
+    (3, 130, 264, 136, False, True, 0, -32768, 32768),
+    (2, 257, 520, 264, True, False, 1, -32768, 32768),
+    (1, 64, 4096, 64, False, False, 0, -32768, 32768),
+    (4, 384, 64, 384, False, False, 0, -600, 600),
+    (2, 128, 384, 64, False, False, 1, -32768, 32768),
+    (1, 1000, 1024, 1000, False, False, 0, -256, 256),
+]
+
+
+@pytest.mark.parametrize("case", CASES, ids=lambda c: "b%d_n%d_k%d_m%d" % c[:4])
+def test_direct_vs_oracle(ops, case):
+    batch, n, k, m, a_sh, b_sh, flags, lo, hi = case
+    rng = np.random.default_rng(batch * 7 + n + k * 3 + m)
+    A = rng.integers(lo, hi, size=(1 if a_sh else batch, n, k)).astype(np.int16)
+    B = rng.integers(lo, hi, size=(1 if b_sh else batch, k, m)).astype(np.int16)
+    C = torch.full((batch * n * m,), -8531, dtype=torch.int16, device="cuda")
+    ops.matmul(torch.from_numpy(A.reshape(-1)).cuda(), torch.from_numpy(B.reshape(-1)).cuda(), C, n=n, k=k, m=m,
+               batch=batch, a_batch_stride=0 if a_sh else n * k, b_batch_stride=0 if b_sh else k * m,
+               c_batch_stride=n * m, flags=flags)
+    want = spec.matmul_raw(np.broadcast_to(A, (batch, n, k)), np.broadcast_to(B, (batch, k, m)), wrap=bool(flags & 1))
+    assert np.array_equal(C.cpu().numpy().reshape(batch, n, m), want)
+
+
+def test_direct_unaligned_falls_back(ops):
+    """An operand at an odd element offset (not 16-byte aligned) takes the
+    plane-splitting path with the same result."""
+    rng = np.random.default_rng(3)
+    n, k, m = 40, 64, 48
+    A = rng.integers(-32768, 32768, size=n * k + 1).astype(np.int16)
+    B = rng.integers(-32768, 32768, size=(k, m)).astype(np.int16)
+    Ad = torch.from_numpy(A).cuda()
+    C = torch.empty(n * m, dtype=torch.int16, device="cuda")
+    ops.matmul(Ad[1:], torch.from_numpy(B.reshape(-1)).cuda(), C, n=n, k=k, m=m)
+    assert np.array_equal(C.cpu().numpy().reshape(n, m), spec.matmul_raw(A[1:].reshape(n, k), B))
