@@ -187,15 +187,19 @@ Plan plan_of(const corm_matmul_desc* d) {
 }
 
 // The tensor-core path of a job with n >= 3 rows.  Row-major B with K and m
-// multiples of 8 on 16-byte aligned rows: the GEMM reads the int16 operands
-// and splits them itself (only a K-split partial-sum buffer in the
-// workspace); otherwise the operands are split into int8 planes first.  The
-// workspace is sized for the second case.
+// multiples of 8 on 16-byte aligned rows, and 1/n + 1/m above 1/500: the
+// GEMM reads the int16 operands and splits them itself (only a K-split
+// partial-sum buffer in the workspace); otherwise the operands are split into
+// int8 planes first.  The workspace is sized for the second case.
 int tensor_path(const corm_matmul_desc* d, const MmArgs& p, const Plan& pl, uint8_t* w, const corm::PostOp& post,
                 int* err, cudaStream_t st) {
+  // The producer warps sustain fewer bytes in flight than the TMA: for large
+  // tiles of work per operand byte (n and m both above ~1000) the split planes
+  // plus TMA are faster, below it the saved split traffic wins.
   const bool direct = !d->b_packed && d->gemv_kw <= 1 && d->k % 8 == 0 && d->m % 8 == 0 &&
                       !(((uintptr_t)d->a | (uintptr_t)d->b) & 15u) &&
-                      (d->batch == 1 || (d->a_batch_stride % 8 == 0 && d->b_batch_stride % 8 == 0));
+                      (d->batch == 1 || (d->a_batch_stride % 8 == 0 && d->b_batch_stride % 8 == 0)) &&
+                      ((uint64_t)d->n + d->m) * 500u > (uint64_t)d->n * d->m;
   corm::GemmJob j{};
   j.rows = d->n;
   j.cols = d->m;

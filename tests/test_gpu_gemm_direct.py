@@ -26,7 +26,8 @@ CASES = [  # batch, n, k, m, a_shared, b_shared, flags, lo, hi
     (1, 64, 4096, 64, False, False, 0, -32768, 32768),
     (4, 384, 64, 384, False, False, 0, -600, 600),
     (2, 128, 384, 64, False, False, 1, -32768, 32768),
-    (1, 1000, 1024, 1000, False, False, 0, -256, 256),
+    (1, 400, 1024, 400, False, False, 0, -256, 256),
+    (16, 8, 512, 256, False, False, 0, -32768, 32768),
 ]
 
 
