@@ -303,10 +303,20 @@ __global__ void __launch_bounds__(256) ro_stream16(RoArgs q) {
   const bool ident = pr.sa == 0 && pr.sb == 0 && pr.sc == 0 && pr.bq == 0 && !scale;
   const uint32_t per = q.n >> 3;
   const uint64_t total = (uint64_t)q.c1 * q.c2 * per;
+  const bool small = total < (1ull << 32);  // 32-bit index arithmetic
   for (uint64_t g = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; g < total; g += (uint64_t)gridDim.x * blockDim.x) {
-    const uint64_t row = g / per;
-    const uint32_t w = (uint32_t)(g - row * per);
-    const uint32_t i1 = (uint32_t)(row % q.c1), i2 = (uint32_t)(row / q.c1);
+    uint32_t w, i1, i2;
+    if (small) {
+      const uint32_t g32 = (uint32_t)g, row = g32 / per;
+      w = g32 - row * per;
+      i2 = row / q.c1;
+      i1 = row - i2 * q.c1;
+    } else {
+      const uint64_t row = g / per;
+      w = (uint32_t)(g - row * per);
+      i1 = (uint32_t)(row % q.c1);
+      i2 = (uint32_t)(row / q.c1);
+    }
     const bool zero_a = (code == 1 || code == 2) && (i1 < q.win_lo || i1 >= q.win_hi);
     int4 xa = make_int4(0, 0, 0, 0), yb = make_int4(0, 0, 0, 0);
     if (!zero_a) xa = *(const int4*)(q.a + (uint64_t)i2 * q.a_s2 + (uint64_t)i1 * q.a_s1 + 16ull * w);
@@ -385,25 +395,34 @@ __global__ void __launch_bounds__(256) ro_xpose8(RoArgs q) {
 // P1 = (A Rm) >> (sh - 24) is exact in int64 (|A| < 2^29, Rm < 2^32); the
 // sum P1 G + Bq' << bq_sh too while |P1| < 2^31 and bq_sh <= 40, else it is
 // formed in 128 bits.
+// sat16(rne((P1 G + Bq' << bq_sh) / 2^sh_c)) in 128 bits (out of line: rare)
+__device__ __noinline__ int64_t norm_out128(long long P1, int64_t g, int32_t bq, uint32_t bq_sh, int sc) {
+  return corm_sat16_128(corm_rne_shr128((__int128)P1 * g + ((__int128)bq << bq_sh), sc));
+}
+
 template <int NW_PER>
 __global__ void __launch_bounds__(256) ro_norm16(RoArgs q) {
   extern __shared__ __align__(16) uint8_t ro_smem[];
   const bool ln = (q.op >> 16) & 1u;
   const bool bcast = (q.op >> 13) & 1u;
+  const uint32_t words = q.n >> 3;
+  // entry of column c = 8 w + e at [e][w] (lanes read consecutive words):
+  // G, Bq' << bq_sh (int64) and sh_c
   const uint32_t npar = bcast ? 1u : q.n;
-  int32_t* s_g = (int32_t*)ro_smem;
-  int32_t* s_bq = s_g + npar;
-  uint8_t* s_sc = (uint8_t*)(s_bq + npar);
+  int64_t* s_bq = (int64_t*)ro_smem;
+  int32_t* s_g = (int32_t*)(s_bq + npar);
+  uint8_t* s_sc = (uint8_t*)(s_g + npar);
   for (uint32_t c = threadIdx.x; c < npar; c += blockDim.x) {
     const int4 e = *(const int4*)(q.p + 16ull * c);
-    s_g[c] = e.x;
-    s_bq[c] = (int32_t)((uint32_t)e.y << 10) >> 10;  // int22, sign-extended
-    s_sc[c] = (uint8_t)(((uint32_t)e.z >> 16) & 63u);
+    const uint32_t slot = bcast ? 0u : (c & 7u) * words + (c >> 3);
+    s_g[slot] = e.x;
+    const int64_t bq = (int32_t)((uint32_t)e.y << 10) >> 10;  // int22, sign-extended
+    s_bq[slot] = q.bq_sh <= 40u ? bq << q.bq_sh : 0;       // (the 128-bit path shifts itself)
+    s_sc[slot] = (uint8_t)(((uint32_t)e.z >> 16) & 63u);
   }
   __syncthreads();
   const bool small_bq = q.bq_sh <= 40u;
   const int lane = threadIdx.x & 31;
-  const uint32_t words = q.n >> 3;
   const uint64_t rows = (uint64_t)q.c1 * q.c2;
   const uint64_t warp0 = ((uint64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const uint64_t nwarps = ((uint64_t)gridDim.x * blockDim.x) >> 5;
@@ -412,7 +431,8 @@ __global__ void __launch_bounds__(256) ro_norm16(RoArgs q) {
     const uint8_t* ra = q.a + (uint64_t)i2 * q.a_s2 + (uint64_t)i1 * q.a_s1;
     uint8_t* rc = q.c + (uint64_t)i2 * q.c_s2 + (uint64_t)i1 * q.c_s1;
     int4 xv[NW_PER];
-    long long s1 = 0, s2 = 0;
+    int s1 = 0;
+    long long s2 = 0;
 #pragma unroll
     for (int k = 0; k < NW_PER; k++) {
       const uint32_t w = lane + 32u * k;
@@ -423,7 +443,7 @@ __global__ void __launch_bounds__(256) ro_norm16(RoArgs q) {
 #pragma unroll
         for (int e = 0; e < 8; e++) {
           s1 += xs[e];
-          s2 += (long long)xs[e] * xs[e];
+          s2 += xs[e] * xs[e];  // each square < 2^30
         }
       }
     }
@@ -438,7 +458,7 @@ __global__ void __launch_bounds__(256) ro_norm16(RoArgs q) {
     int sh;
     rsqrt_bf(D, Rm, sh, q.rsq);
     const int shp = sh - 24;
-    const long long nn = ln ? (long long)q.n : 1, off = ln ? s1 : 0;
+    const int nn = ln ? (int)q.n : 1, off = ln ? s1 : 0;  // |n x - S1| < 2^28
 #pragma unroll
     for (int k = 0; k < NW_PER; k++) {
       const uint32_t w = lane + 32u * k;
@@ -448,17 +468,17 @@ __global__ void __launch_bounds__(256) ro_norm16(RoArgs q) {
       int16_t* os = (int16_t*)&out;
 #pragma unroll
       for (int e = 0; e < 8; e++) {
-        const uint32_t c = bcast ? 0u : 8u * w + e;
-        const long long g = s_g[c], bq = s_bq[c];
-        const int sc = s_sc[c];
-        const long long A = nn * xs[e] - off;
-        const long long P1 = (A * (long long)Rm) >> shp;
+        const uint32_t slot = bcast ? 0u : (uint32_t)e * words + w;
+        const int64_t g = s_g[slot];
+        const int sc = s_sc[slot];
+        const int A = nn * xs[e] - off;
+        const long long P1 = ((long long)A * (long long)Rm) >> shp;  // |A Rm| < 2^60
         int64_t r;
         if (small_bq && P1 > -(1ll << 31) && P1 < (1ll << 31)) {
-          const long long v = corm_rne_shr64(P1 * g + (bq << q.bq_sh), sc);
+          const long long v = corm_rne_shr64(P1 * g + s_bq[slot], sc);
           r = v > 32767 ? 32767 : (v < -32768 ? -32768 : v);
         } else {
-          r = corm_sat16_128(corm_rne_shr128((__int128)P1 * g + ((__int128)bq << q.bq_sh), sc));
+          r = norm_out128(P1, g, ld_param(q, bcast ? 0u : 8u * w + e).bq, q.bq_sh, sc);
         }
         os[e] = (int16_t)r;
       }
@@ -563,13 +583,17 @@ extern "C" int corm_rowops(const corm_rowops_desc* d, corm_stream_t stream) {
       corm::ProfScope prof_("ro_norm16", st);
       const unsigned grid = corm_blocks(rows, 8, 148u * 4u);
       const size_t npar = ((d->op >> 13) & 1u) ? 1u : d->n;
-      const size_t smem = npar * 9u + 16u;  // n <= 4096: under 48 KB
+      const size_t smem = npar * 13u + 16u;  // n <= 4096: under 64 KB
+      auto launch = [&](auto kern) {
+        if (smem > 48u * 1024u) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        kern<<<grid, 256, smem, st>>>(q);
+      };
       if (d->n <= 1024)
-        ro_norm16<4><<<grid, 256, smem, st>>>(q);
+        launch(ro_norm16<4>);
       else if (d->n <= 2048)
-        ro_norm16<8><<<grid, 256, smem, st>>>(q);
+        launch(ro_norm16<8>);
       else
-        ro_norm16<16><<<grid, 256, smem, st>>>(q);
+        launch(ro_norm16<16>);
     }
     return corm::cuda_status("rowops norm");
   }

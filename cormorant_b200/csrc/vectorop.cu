@@ -164,80 +164,109 @@ __device__ __forceinline__ int64_t warp_reduce_sum(int64_t v) {
   return v;
 }
 
-// Row mode, GROUP threads per row (32: a warp per row; 256 / 1024: a CTA per
-// row), PER elements per thread held in registers as PER / 8 runs of 8
-// consecutive elements (16-byte loads and stores where the row allows).
+// e and P in 32 / 64-bit integer steps: y = (d cm) >> cs with d = m - x <
+// 2^16 and cm < 2^24 (one 32 x 32 -> 64 multiply); e = TAB[y mod 4096] >>
+// (y div 4096) is 0 once the shift reaches 17 (TAB <= 2^16); S <= 2^30 sums in
+// 32 bits; R = 2^40 / S < 2^25 (S >= TAB[0] when a lane is valid), so e R <
+// 2^41 is one 32 x 32 -> 64 multiply.
+__device__ __forceinline__ uint32_t smx_e32(int32_t m, int32_t x, uint32_t cm, uint32_t cs, const int32_t* tab) {
+  const uint64_t y = ((uint64_t)(uint32_t)(m - x) * cm) >> cs;
+  return y >= (17ull << 12) ? 0u : ((uint32_t)tab[y & 4095u] >> (uint32_t)(y >> 12));
+}
+
+__device__ __forceinline__ int16_t smx_p32(uint32_t e, uint32_t R, uint64_t rnd, uint32_t sh) {
+  const uint64_t q = ((uint64_t)e * R + rnd) >> sh;
+  return (int16_t)(q > 32767u ? 32767u : q);
+}
+
+// Row mode, GROUP threads per row (16 / 32: a part of a warp per row; 256 /
+// 1024: a CTA per row), PER elements per thread held in registers as PER / 8
+// runs of 8 consecutive elements (16-byte loads and stores where the row
+// allows).  The TAB is copied into shared memory once per CTA; CTAs then walk
+// row groups.
 template <int GROUP, int PER>
 __global__ void __launch_bounds__(GROUP >= 256 ? GROUP : 256) smx_rows(SmxArgs p) {
-  constexpr int ROWS_PER_CTA = GROUP >= 256 ? 1 : 256 / GROUP;
+  constexpr int NT = GROUP >= 256 ? GROUP : 256;
+  constexpr int ROWS_PER_CTA = NT / GROUP;
   constexpr int V = PER / 8;
+  __shared__ int32_t s_tab[4096];
   __shared__ int32_t s_max[32];
-  __shared__ int64_t s_sum[32];
+  __shared__ uint32_t s_sum[32];
+  for (int i = threadIdx.x; i < 4096; i += NT) s_tab[i] = __ldg(p.tab + i);
+  __syncthreads();
   const int lane_in_group = threadIdx.x % GROUP;
   const int group = threadIdx.x / GROUP;
-  const uint32_t row = blockIdx.x * ROWS_PER_CTA + group;
-  const bool live = row < p.rows;
-  const uint32_t v = live ? smx_valid(row, p) : 0u;
-  const int16_t* x = p.a + (size_t)row * p.a_inc;
-  const bool xa = ((uintptr_t)x & 15) == 0;
-  int32_t xv[PER];
-  int32_t m = INT32_MIN;
+  const uint32_t cm = p.cm, cs = p.cs;
+  const uint64_t rnd = 1ull << (39u - p.fp);
+  const uint32_t psh = 40u - p.fp;
+  const uint32_t ngroups = (p.rows + ROWS_PER_CTA - 1) / ROWS_PER_CTA;
+  for (uint32_t rg = blockIdx.x; rg < ngroups; rg += gridDim.x) {
+    const uint32_t row = rg * ROWS_PER_CTA + group;
+    const bool live = row < p.rows;
+    const uint32_t v = live ? smx_valid(row, p) : 0u;
+    const int16_t* x = p.a + (size_t)row * p.a_inc;
+    const bool xa = ((uintptr_t)x & 15) == 0;
+    int32_t xv[PER];
+    int32_t m = INT32_MIN;
 #pragma unroll
-  for (int q = 0; q < V; q++) {
-    const uint32_t j0 = (q * GROUP + lane_in_group) * 8;
-    if (live && xa && j0 + 8 <= v) {
-      alignas(16) int16_t t8[8];
-      *(int4*)t8 = __ldg((const int4*)(x + j0));
+    for (int q = 0; q < V; q++) {
+      const uint32_t j0 = (q * GROUP + lane_in_group) * 8;
+      if (live && xa && j0 + 8 <= v) {
+        alignas(16) int16_t t8[8];
+        *(int4*)t8 = __ldg((const int4*)(x + j0));
 #pragma unroll
-      for (int e = 0; e < 8; e++) xv[q * 8 + e] = t8[e];
-    } else {
+        for (int e = 0; e < 8; e++) xv[q * 8 + e] = t8[e];
+      } else {
 #pragma unroll
-      for (int e = 0; e < 8; e++) xv[q * 8 + e] = (live && j0 + e < v) ? (int32_t)x[j0 + e] : INT32_MIN;
+        for (int e = 0; e < 8; e++) xv[q * 8 + e] = (live && j0 + e < v) ? (int32_t)x[j0 + e] : INT32_MIN;
+      }
+#pragma unroll
+      for (int e = 0; e < 8; e++) m = max(m, xv[q * 8 + e]);
+    }
+    m = warp_reduce_max<(GROUP < 32 ? GROUP : 32)>(m);
+    if (GROUP > 32) {
+      if ((threadIdx.x & 31) == 0) s_max[threadIdx.x >> 5] = m;
+      __syncthreads();
+      m = INT32_MIN;
+      for (int w = 0; w < GROUP / 32; w++) m = max(m, s_max[w]);
+    }
+    uint32_t S = 0;
+#pragma unroll
+    for (int t = 0; t < PER; t++) {  // xv becomes e (<= 65536) in place
+      const uint32_t j = ((t / 8) * GROUP + lane_in_group) * 8 + (t % 8);
+      xv[t] = (live && j < v) ? (int32_t)smx_e32(m, xv[t], cm, cs, s_tab) : 0;
+      S += (uint32_t)xv[t];
     }
 #pragma unroll
-    for (int e = 0; e < 8; e++) m = max(m, xv[q * 8 + e]);
-  }
-  m = warp_reduce_max<(GROUP < 32 ? GROUP : 32)>(m);
-  if (GROUP > 32) {
-    if ((threadIdx.x & 31) == 0) s_max[threadIdx.x >> 5] = m;
-    __syncthreads();
-    m = INT32_MIN;
-    for (int w = 0; w < GROUP / 32; w++) m = max(m, s_max[w]);
-  }
-  int64_t S = 0;
-#pragma unroll
-  for (int t = 0; t < PER; t++) {  // xv becomes e (<= 65536) in place
-    const uint32_t j = ((t / 8) * GROUP + lane_in_group) * 8 + (t % 8);
-    xv[t] = (live && j < v) ? (int32_t)smx_e(m, xv[t], p) : 0;
-    S += xv[t];
-  }
-  S = warp_reduce_sum<(GROUP < 32 ? GROUP : 32)>(S);
-  if (GROUP > 32) {
-    if ((threadIdx.x & 31) == 0) s_sum[threadIdx.x >> 5] = S;
-    __syncthreads();
-    S = 0;
-    for (int w = 0; w < GROUP / 32; w++) S += s_sum[w];
-  }
-  if (!live) return;
-  const uint64_t R = S > 0 ? (1ull << 40) / (uint64_t)S : 0ull;
-  int16_t* out = p.c + (size_t)row * p.b_inc;
-  const uint32_t lim = (row + 1 == p.rows) ? p.W : min(p.W, max(p.b_inc, p.size));
-  const bool oa = ((uintptr_t)out & 15) == 0;
-#pragma unroll
-  for (int q = 0; q < V; q++) {
-    const uint32_t j0 = (q * GROUP + lane_in_group) * 8;
-    alignas(16) int16_t o8[8];
-#pragma unroll
-    for (int e = 0; e < 8; e++) o8[e] = (j0 + e < v) ? smx_p(xv[q * 8 + e], R, p) : (int16_t)0;
-    if (oa && j0 + 8 <= lim) {
-      *(int4*)(out + j0) = *(int4*)o8;
-    } else {
-#pragma unroll
-      for (int e = 0; e < 8; e++)
-        if (j0 + e < lim) out[j0 + e] = o8[e];
+    for (int o = (GROUP < 32 ? GROUP : 32) / 2; o > 0; o >>= 1) S += __shfl_xor_sync(0xffffffffu, S, o);
+    if (GROUP > 32) {
+      if ((threadIdx.x & 31) == 0) s_sum[threadIdx.x >> 5] = S;
+      __syncthreads();
+      S = 0;
+      for (int w = 0; w < GROUP / 32; w++) S += s_sum[w];
+      __syncthreads();  // s_max / s_sum are rewritten by the next row
     }
+    if (!live) continue;
+    const uint32_t R = S > 0 ? (uint32_t)((1ull << 40) / S) : 0u;
+    int16_t* out = p.c + (size_t)row * p.b_inc;
+    const uint32_t lim = (row + 1 == p.rows) ? p.W : min(p.W, max(p.b_inc, p.size));
+    const bool oa = ((uintptr_t)out & 15) == 0;
+#pragma unroll
+    for (int q = 0; q < V; q++) {
+      const uint32_t j0 = (q * GROUP + lane_in_group) * 8;
+      alignas(16) int16_t o8[8];
+#pragma unroll
+      for (int e = 0; e < 8; e++) o8[e] = (j0 + e < v) ? smx_p32((uint32_t)xv[q * 8 + e], R, rnd, psh) : (int16_t)0;
+      if (oa && j0 + 8 <= lim) {
+        *(int4*)(out + j0) = *(int4*)o8;
+      } else {
+#pragma unroll
+        for (int e = 0; e < 8; e++)
+          if (j0 + e < lim) out[j0 + e] = o8[e];
+      }
+    }
+    for (uint32_t j = lane_in_group + PER * GROUP; j < lim; j += GROUP) out[j] = 0;  // tail beyond registers
   }
-  for (uint32_t j = lane_in_group + PER * GROUP; j < lim; j += GROUP) out[j] = 0;  // tail beyond registers
 }
 
 // Column mode: scores keys-major s[key][query] (row stride a_inc); a CTA
@@ -290,6 +319,9 @@ __global__ void __launch_bounds__(256) smx_cols(SmxArgs p) {
   }
 }
 
+// CTAs for a persistent row-mode launch: at most 8 per SM
+unsigned smx_grid(uint64_t groups) { return (unsigned)(groups < 148u * 8u ? (groups ? groups : 1) : 148u * 8u); }
+
 int launch_softmax(const corm_vectorop_desc* d, cudaStream_t st, const corm::DeviceTables* tb) {
   SmxArgs p{};
   p.a = d->a;
@@ -321,41 +353,41 @@ int launch_softmax(const corm_vectorop_desc* d, cudaStream_t st, const corm::Dev
   }
   if (d->size <= 128) {
     corm::ProfScope prof_("smx_rows<16,8>", st);
-    smx_rows<16, 8><<<(p.rows + 15) / 16, 256, 0, st>>>(p);
+    smx_rows<16, 8><<<smx_grid((p.rows + 15) / 16), 256, 0, st>>>(p);
   } else if (d->size <= 256) {
     {
       corm::ProfScope prof_("smx_rows<32,8>", st);
-      smx_rows<32, 8><<<(p.rows + 7) / 8, 256, 0, st>>>(p);
+      smx_rows<32, 8><<<smx_grid((p.rows + 7) / 8), 256, 0, st>>>(p);
     }
   } else if (d->size <= 384) {
     {
       corm::ProfScope prof_("smx_rows<16,24>", st);
-      smx_rows<16, 24><<<(p.rows + 15) / 16, 256, 0, st>>>(p);
+      smx_rows<16, 24><<<smx_grid((p.rows + 15) / 16), 256, 0, st>>>(p);
     }
   } else if (d->size <= 512) {
     {
       corm::ProfScope prof_("smx_rows<32,16>", st);
-      smx_rows<32, 16><<<(p.rows + 7) / 8, 256, 0, st>>>(p);
+      smx_rows<32, 16><<<smx_grid((p.rows + 7) / 8), 256, 0, st>>>(p);
     }
   } else if (d->size <= 768) {
     {
       corm::ProfScope prof_("smx_rows<32,24>", st);
-      smx_rows<32, 24><<<(p.rows + 7) / 8, 256, 0, st>>>(p);
+      smx_rows<32, 24><<<smx_grid((p.rows + 7) / 8), 256, 0, st>>>(p);
     }
   } else if (d->size <= 1024) {
     {
       corm::ProfScope prof_("smx_rows<32,32>", st);
-      smx_rows<32, 32><<<(p.rows + 7) / 8, 256, 0, st>>>(p);
+      smx_rows<32, 32><<<smx_grid((p.rows + 7) / 8), 256, 0, st>>>(p);
     }
   } else if (d->size <= 4096) {
     {
       corm::ProfScope prof_("smx_rows<256,16>", st);
-      smx_rows<256, 16><<<p.rows, 256, 0, st>>>(p);
+      smx_rows<256, 16><<<smx_grid(p.rows), 256, 0, st>>>(p);
     }
   } else if (d->size <= 16384) {
     {
       corm::ProfScope prof_("smx_rows<1024,16>", st);
-      smx_rows<1024, 16><<<p.rows, 1024, 0, st>>>(p);
+      smx_rows<1024, 16><<<smx_grid(p.rows), 1024, 0, st>>>(p);
     }
   } else {
     return corm::fail(CORM_ELIMIT, "softmax row mode: size %u beyond 16384", d->size);
