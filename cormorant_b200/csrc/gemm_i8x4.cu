@@ -34,8 +34,7 @@ constexpr int BM = 128, BN = 128, BK = 128;  // BK in bytes = int8 elements
 constexpr int STAGES = 3;
 constexpr int TILE_BYTES = BM * BK;  // 16 KB (BM == BN)
 constexpr int STAGE_BYTES = 4 * TILE_BYTES;
-constexpr int STAGING_WARP_BYTES = 32 * 64 * 2;  // an epilogue warp's 32 rows x 64 int16 results
-constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/ + 8 * STAGING_WARP_BYTES;
+constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
 constexpr uint32_t TMEM_COLS = 512;
 constexpr int EPI_WARPS = 8;
 constexpr int NUM_SMS = 148;
@@ -208,67 +207,6 @@ __device__ __forceinline__ void store_row(const EpiArgs& ep, uint32_t bz, uint32
   }
 }
 
-// Row-major output (mode 0) through the warp's staging area: lane l's 64
-// results (row r0 + l) go in as eight 16-byte chunks, chunk c of row l at
-// (c ^ (l & 7)) so eight lanes cover the 32 banks; the warp then reads them
-// back row by row, 8 columns per lane, applies the fused job (operand loads
-// coalesced) and stores 4 rows x 128 bytes per instruction.
-__device__ __forceinline__ void staged_readback(const EpiArgs& ep, uint8_t* stg, int lane, uint32_t bz, uint32_t r0,
-                                                uint32_t c0) {
-  __syncwarp();
-  const bool post = ep.post.op != kPostNone;
-#pragma unroll 2
-  for (int it = 0; it < 8; it++) {
-    const int idx = it * 32 + lane, rr = idx >> 3, c = idx & 7;
-    const uint32_t row = r0 + rr, col = c0 + 8 * c;
-    const int4 t = *(const int4*)(stg + rr * 128 + ((c ^ (rr & 7)) << 4));
-    if (row >= ep.rows || col >= ep.cols) continue;
-    uint32_t v[4] = {(uint32_t)t.x, (uint32_t)t.y, (uint32_t)t.z, (uint32_t)t.w};
-    const uint64_t off = (uint64_t)bz * ep.out_batch_stride + (uint64_t)row * ep.ldc + col;
-    const bool full = col + 8 <= ep.cols;
-    if (post) {
-      uint32_t b[4];
-      const int16_t* bsrc = ep.post.b_mode == 0 ? ep.post.b + col : ep.post.b + off;
-      if (ep.post.b_mode == 2) {
-        const uint32_t sv = (uint16_t)__ldg(ep.post.b);
-        b[0] = b[1] = b[2] = b[3] = sv | (sv << 16);
-      } else if (full && ((uintptr_t)bsrc & 15) == 0) {
-        const int4 bt = __ldg((const int4*)bsrc);
-        b[0] = (uint32_t)bt.x;
-        b[1] = (uint32_t)bt.y;
-        b[2] = (uint32_t)bt.z;
-        b[3] = (uint32_t)bt.w;
-      } else {
-#pragma unroll
-        for (int e = 0; e < 4; e++) {
-          const uint32_t lo = col + 2 * e < ep.cols ? (uint16_t)__ldg(bsrc + 2 * e) : 0u;
-          const uint32_t hi = col + 2 * e + 1 < ep.cols ? (uint16_t)__ldg(bsrc + 2 * e + 1) : 0u;
-          b[e] = lo | (hi << 16);
-        }
-      }
-      post_dispatch<4>(ep.post, v, b);
-    }
-    int16_t* dst = ep.out + off;
-    if (full && ((uintptr_t)dst & 15) == 0) {
-      *(int4*)dst = make_int4((int)v[0], (int)v[1], (int)v[2], (int)v[3]);
-    } else {
-#pragma unroll
-      for (int j = 0; j < 8; j++)
-        if (col + j < ep.cols) dst[j] = (int16_t)(v[j / 2] >> (16 * (j & 1)));
-    }
-  }
-  __syncwarp();
-}
-
-__device__ __forceinline__ void staged_store(const EpiArgs& ep, uint8_t* stg, int lane, uint32_t bz, uint32_t r0,
-                                             uint32_t c0, const uint32_t* v2) {
-#pragma unroll
-  for (int c = 0; c < 8; c++)
-    *(int4*)(stg + lane * 128 + ((c ^ (lane & 7)) << 4)) =
-        make_int4((int)v2[4 * c], (int)v2[4 * c + 1], (int)v2[4 * c + 2], (int)v2[4 * c + 3]);
-  staged_readback(ep, stg, lane, bz, r0, c0);
-}
-
 __device__ __forceinline__ uint64_t row_base(const EpiArgs& ep, uint32_t bz, uint32_t r) {
   if (ep.mode == 0) return (uint64_t)bz * ep.out_batch_stride + (uint64_t)r * ep.ldc;
   const uint32_t n = r / ep.P;
@@ -355,7 +293,6 @@ __global__ void __launch_bounds__(Roles<CONV>::threads, 1)
   uint64_t* tmem_empty = tmem_full + 1;
   uint64_t* mma_done = tmem_empty + 1;
   uint32_t* tmem_slot = (uint32_t*)(mma_done + 1);
-  uint8_t* staging = smem + STAGES * STAGE_BYTES + 256;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t units = ep.batch * ep.tiles_m * ep.tiles_n * ep.splits;
@@ -575,12 +512,8 @@ __global__ void __launch_bounds__(Roles<CONV>::threads, 1)
         sm100::tc_fence_before();
         __syncwarp();
         if (lane == 0) sm100::mbar_arrive(tmem_empty);
-        const uint32_t c0 = w.tile_c + 64 * h;
-        if (ep.mode == 0) {
-          staged_store(ep, staging + (warp - R::epi0) * STAGING_WARP_BYTES, lane, w.bz, w.tile_r + q * 32, c0, v2);
-          continue;
-        }
         if (!row_ok) continue;
+        const uint32_t c0 = w.tile_c + 64 * h;
         if (ep.post.op != kPostNone) {
           uint32_t b2[32];
           post_operand<64>(ep, row_base(ep, w.bz, r), c0, b2);
@@ -588,10 +521,8 @@ __global__ void __launch_bounds__(Roles<CONV>::threads, 1)
         }
         store_row<64>(ep, w.bz, r, c0, v2);
       } else {
-        // 16 columns at a time (the register budget of the int16-producer
-        // layout), each chunk's results into the staging area; TMEM released
-        // after the last chunk's load, then the coalesced stores (mode 0)
-        uint8_t* stg = staging + (warp - R::epi0) * STAGING_WARP_BYTES;
+        // 16 columns at a time (the register budget of the int16-producer layout):
+        // TMEM released after the last chunk's load
         const uint64_t rb = row_ok && ep.post.op != kPostNone ? row_base(ep, w.bz, r) : 0;
 #pragma unroll 1
         for (int part = 0; part < 4; part++) {
@@ -606,6 +537,7 @@ __global__ void __launch_bounds__(Roles<CONV>::threads, 1)
             __syncwarp();
             if (lane == 0) sm100::mbar_arrive(tmem_empty);
           }
+          if (!row_ok) continue;
           const uint32_t c0 = w.tile_c + cc;
           uint32_t v8[8];
           if (ep.ymode == 0)
@@ -614,16 +546,6 @@ __global__ void __launch_bounds__(Roles<CONV>::threads, 1)
             combine_cw<16, 1>(ep, hh, mid, ll, c0, v8);
           else
             combine_cw<16, 2>(ep, hh, mid, ll, c0, v8);
-          if (ep.mode == 0) {
-#pragma unroll
-            for (int c = 0; c < 2; c++) {
-              const int ch = 2 * part + c;
-              *(int4*)(stg + lane * 128 + ((ch ^ (lane & 7)) << 4)) =
-                  make_int4((int)v8[4 * c], (int)v8[4 * c + 1], (int)v8[4 * c + 2], (int)v8[4 * c + 3]);
-            }
-            continue;
-          }
-          if (!row_ok) continue;
           if (ep.post.op != kPostNone) {
             uint32_t b8[8];
             post_operand<16>(ep, rb, c0, b8);
@@ -631,7 +553,6 @@ __global__ void __launch_bounds__(Roles<CONV>::threads, 1)
           }
           store_row<16>(ep, w.bz, r, c0, v8);
         }
-        if (ep.mode == 0) staged_readback(ep, stg, lane, w.bz, w.tile_r + q * 32, w.tile_c + 64 * h);
       }
     }
   }
