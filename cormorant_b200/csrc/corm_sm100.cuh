@@ -111,18 +111,6 @@ __device__ __forceinline__ uint64_t sdesc_sw128(uint32_t smem_addr) {
   return d;
 }
 
-// Shared-memory matrix descriptor: K-major operand, 64-byte swizzle, rows of
-// 64 bytes, 8-row groups 512 bytes apart (SBO), tile base 512-aligned.
-__device__ __forceinline__ uint64_t sdesc_sw64(uint32_t smem_addr) {
-  uint64_t d = 0;
-  d |= (uint64_t)((smem_addr & 0x3FFFF) >> 4);  // start address
-  d |= (uint64_t)1 << 16;                       // LBO (unused for swizzled K-major)
-  d |= (uint64_t)(512 >> 4) << 32;              // SBO
-  d |= (uint64_t)1 << 46;                       // descriptor version (sm_100)
-  d |= (uint64_t)4 << 61;                       // SWIZZLE_64B
-  return d;
-}
-
 // Shared-memory matrix descriptor: MN-major operand, 128-byte swizzle: rows of
 // 128 bytes hold 128 consecutive MN elements of one k, 8-row swizzle atoms of
 // 1024 bytes stacked along K (SBO); one atom along MN (LBO unused at 128).

@@ -2,11 +2,10 @@
 //
 // Persistent: one CTA per SM (6 warps) walks work units = (batch, 128-row
 // tile, 128-column tile, K split), warp-specialised:
-//   warp 0      TMA producer: per 64-byte K block, 4 tiles (A hi/lo K-major
-//               128 x 64 bytes with 64-byte swizzle, B hi/lo K-major likewise or
-//               MN-major 64 K rows x 128 bytes with 128-byte swizzle; no
-//               multicast) into a 6-deep ring that runs across units
-//   warp 1      TMEM owner (512 columns) and MMA issuer: 8 tcgen05.mma
+//   warp 0      TMA producer: per 128-byte K block, 4 tiles (A hi/lo K-major,
+//               B hi/lo K-major or MN-major, 128 x 128 bytes, 128-byte swizzle,
+//               no multicast) into a STAGES-deep ring that runs across units
+//   warp 1      TMEM owner (512 columns) and MMA issuer: 16 tcgen05.mma
 //               (128x128x32) per K block into HH / MID / LL (the K steps past
 //               the job's K, zero-filled, are not issued); waits for the
 //               epilogue to drain TMEM before the next unit (tmem_empty)
@@ -31,9 +30,9 @@
 namespace corm {
 namespace {
 
-constexpr int BM = 128, BN = 128, BK = 64;  // BK in bytes = int8 elements
-constexpr int STAGES = 6;
-constexpr int TILE_BYTES = BM * BK;  // 8 KB (BM == BN)
+constexpr int BM = 128, BN = 128, BK = 128;  // BK in bytes = int8 elements
+constexpr int STAGES = 3;
+constexpr int TILE_BYTES = BM * BK;  // 16 KB (BM == BN)
 constexpr int STAGE_BYTES = 4 * TILE_BYTES;
 constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
 constexpr uint32_t TMEM_COLS = 512;
@@ -351,87 +350,59 @@ __global__ void __launch_bounds__(Roles<CONV>::threads, 1)
         sm100::mbar_wait(&full[q % STAGES], (q / STAGES) & 1, nullptr, 0, 200000000ll);
     }
   } else if (CONV && warp >= 1 && warp <= 8) {
-    // ---------------- int16 producers: per stage the A tile (128 rows x 64 K)
-    // and the MN-major B tile (64 K rows x 128 columns), each as 512 units of
-    // 16 consecutive int16 -> a 16-byte hi unit and a 16-byte lo unit: A unit u
-    // of row r at r * 64 + ((u ^ ((r >> 1) & 3)) << 4) (64-byte swizzle), B
-    // unit u of K row r at r * 128 + ((u ^ (r & 7)) << 4) (128-byte swizzle);
-    // rows, K and columns beyond the job are zeros.  K and the column count
-    // are multiples of 8, every base 16-byte aligned (the host checks).  The
-    // next stage's global loads are issued before this stage's shared-memory
-    // stores (two stages of registers).
+    // ---------------- int16 producers: per stage the A tile (128 rows x 128 K)
+    // and the MN-major B tile (128 K rows x 128 columns), each as 1024 units of
+    // 16 consecutive int16 -> a 16-byte hi unit and a 16-byte lo unit at the
+    // row's swizzled position (unit u of row r at (u ^ (r & 7)) * 16); rows,
+    // K and columns beyond the job are zeros.  K and the column count are
+    // multiples of 8, every base 16-byte aligned (the host checks).
     const uint32_t pt = (uint32_t)(warp - 1) * 32u + lane;
-    struct Regs {
-      int4 a[2][2], b[2][2];
-    };
-    auto load = [&](const Unit& w, uint32_t kb, Regs& v) {
+    uint32_t g = 0;
+    bool ok = true;
+    for (uint32_t u = blockIdx.x; u < units && ok; u += gridDim.x) {
+      const Unit w = unit_of(ep, u);
       const int16_t* Ab = ep.a16 + (uint64_t)w.bz * ep.a_bs16;
       const int16_t* Bb = ep.b16 + (uint64_t)w.bz * ep.b_bs16;
-      const int4 z = make_int4(0, 0, 0, 0);
-#pragma unroll
-      for (int i = 0; i < 2; i++) {
-        const uint32_t id = pt + 256u * i;
-        const uint32_t arow = id >> 2, au = id & 3u;  // A: 128 rows x 4 units
-        const uint32_t ar = w.tile_r + arow, ak = kb * BK + au * 16u;
-        const int16_t* pa = Ab + (uint64_t)ar * ep.lda + ak;
-        const bool ar_ok = ar < ep.rows;
-        v.a[i][0] = (ar_ok && ak < ep.K) ? __ldg((const int4*)pa) : z;
-        v.a[i][1] = (ar_ok && ak + 8u < ep.K) ? __ldg((const int4*)pa + 1) : z;
-        const uint32_t brow = id >> 3, bu = id & 7u;  // B: 64 K rows x 8 units
-        const uint32_t bk = kb * BK + brow, bc = w.tile_c + bu * 16u;
-        const int16_t* pb = Bb + (uint64_t)bk * ep.ldb + bc;
-        const bool bk_ok = bk < ep.K;
-        v.b[i][0] = (bk_ok && bc < ep.cols) ? __ldg((const int4*)pb) : z;
-        v.b[i][1] = (bk_ok && bc + 8u < ep.cols) ? __ldg((const int4*)pb + 1) : z;
-      }
-    };
-    auto store = [&](uint8_t* st, const Regs& v) {
-#pragma unroll
-      for (int i = 0; i < 2; i++) {
-        const uint32_t id = pt + 256u * i;
-        const uint32_t arow = id >> 2, au = id & 3u;
-        const uint32_t aoff = arow * 64u + ((au ^ ((arow >> 1) & 3u)) << 4);
-        int4 hi, lo;
-        split16_regs(v.a[i][0], v.a[i][1], hi, lo);
-        *(int4*)(st + aoff) = hi;
-        *(int4*)(st + TILE_BYTES + aoff) = lo;
-        const uint32_t brow = id >> 3, bu = id & 7u;
-        const uint32_t boff = brow * 128u + ((bu ^ (brow & 7u)) << 4);
-        split16_regs(v.b[i][0], v.b[i][1], hi, lo);
-        *(int4*)(st + 2 * TILE_BYTES + boff) = hi;
-        *(int4*)(st + 3 * TILE_BYTES + boff) = lo;
-      }
-    };
-    uint32_t u = blockIdx.x;
-    if (u < units) {
-      Unit w = unit_of(ep, u);
-      uint32_t kb = w.kb0;
-      Regs cur, nxt;
-      load(w, kb, cur);
-      for (uint32_t g = 0;; g++) {
-        // the position after (u, kb)
-        Unit wn = w;
-        uint32_t un = u, kbn = kb + 1;
-        if (kbn >= w.kb1) {
-          un = u + gridDim.x;
-          if (un < units) {
-            wn = unit_of(ep, un);
-            kbn = wn.kb0;
-          }
-        }
-        const bool more = un < units;
-        if (more) load(wn, kbn, nxt);
+      for (uint32_t kb = w.kb0; kb < w.kb1; kb++, g++) {
         const int s = g % STAGES;
-        if (g >= (uint32_t)STAGES && !sm100::mbar_wait(&empty[s], ((g / STAGES) - 1) & 1, ep.err, 101)) break;
-        store(smem + s * STAGE_BYTES, cur);
+        if (g >= (uint32_t)STAGES && !sm100::mbar_wait(&empty[s], ((g / STAGES) - 1) & 1, ep.err, 101)) {
+          ok = false;
+          break;
+        }
+        uint8_t* st = smem + s * STAGE_BYTES;
+        int4 va[4][2], vb[4][2];
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+          const uint32_t id = pt + 256u * i, row = id >> 3, uu = id & 7u;
+          const int4 z = make_int4(0, 0, 0, 0);
+          // A row tile_r + row, K kb*128 + 16 uu ..
+          const uint32_t ar = w.tile_r + row, ak = kb * BK + uu * 16u;
+          const int16_t* pa = Ab + (uint64_t)ar * ep.lda + ak;
+          const bool ar_ok = ar < ep.rows;
+          va[i][0] = (ar_ok && ak < ep.K) ? __ldg((const int4*)pa) : z;
+          va[i][1] = (ar_ok && ak + 8u < ep.K) ? __ldg((const int4*)pa + 1) : z;
+          // B K row kb*128 + row, columns tile_c + 16 uu ..
+          const uint32_t bk = kb * BK + row, bc = w.tile_c + uu * 16u;
+          const int16_t* pb = Bb + (uint64_t)bk * ep.ldb + bc;
+          const bool bk_ok = bk < ep.K;
+          vb[i][0] = (bk_ok && bc < ep.cols) ? __ldg((const int4*)pb) : z;
+          vb[i][1] = (bk_ok && bc + 8u < ep.cols) ? __ldg((const int4*)pb + 1) : z;
+        }
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+          const uint32_t id = pt + 256u * i, row = id >> 3, uu = id & 7u;
+          const uint32_t off = row * 128u + ((uu ^ (row & 7u)) << 4);
+          int4 hi, lo;
+          split16_regs(va[i][0], va[i][1], hi, lo);
+          *(int4*)(st + off) = hi;
+          *(int4*)(st + TILE_BYTES + off) = lo;
+          split16_regs(vb[i][0], vb[i][1], hi, lo);
+          *(int4*)(st + 2 * TILE_BYTES + off) = hi;
+          *(int4*)(st + 3 * TILE_BYTES + off) = lo;
+        }
         sm100::fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) sm100::mbar_arrive(&full[s]);
-        if (!more) break;
-        cur = nxt;
-        w = wn;
-        u = un;
-        kb = kbn;
       }
     }
   } else if (warp == R::mma_warp && lane == 0) {
@@ -456,9 +427,9 @@ __global__ void __launch_bounds__(Roles<CONV>::threads, 1)
         }
         sm100::tc_fence_after();
         const uint32_t base = sm100::smem_u32(smem + s * STAGE_BYTES);
-        const uint64_t d_ahi = sm100::sdesc_sw64(base), d_alo = sm100::sdesc_sw64(base + TILE_BYTES);
-        const uint64_t d_bhi = ep.b_mn ? sm100::sdesc_sw128_mn(base + 2 * TILE_BYTES) : sm100::sdesc_sw64(base + 2 * TILE_BYTES);
-        const uint64_t d_blo = ep.b_mn ? sm100::sdesc_sw128_mn(base + 3 * TILE_BYTES) : sm100::sdesc_sw64(base + 3 * TILE_BYTES);
+        const uint64_t d_ahi = sm100::sdesc_sw128(base), d_alo = sm100::sdesc_sw128(base + TILE_BYTES);
+        const uint64_t d_bhi = ep.b_mn ? sm100::sdesc_sw128_mn(base + 2 * TILE_BYTES) : sm100::sdesc_sw128(base + 2 * TILE_BYTES);
+        const uint64_t d_blo = ep.b_mn ? sm100::sdesc_sw128_mn(base + 3 * TILE_BYTES) : sm100::sdesc_sw128(base + 3 * TILE_BYTES);
         // K step of 32 int8: 32 bytes inside a K-major swizzled row, or 32 rows
         // (4 swizzle atoms of 1024 bytes) of an MN-major tile
         const uint64_t b_step = ep.b_mn ? (uint64_t)(4096 >> 4) : (uint64_t)(32 >> 4);
@@ -668,18 +639,17 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   return fn;
 }
 
-// [planes][outer][inner] bytes, box box_in x box_out x 1: K-major tiles 64 x 128
-// with 64-byte swizzle, MN-major tiles 128 x 64 with 128-byte swizzle
-bool make_map(CUtensorMap* map, const void* base, uint32_t inner, uint32_t outer, uint32_t planes, bool k_major) {
+// [planes][outer][inner] bytes, box 128 x 128 x 1, 128-byte swizzle
+bool make_map(CUtensorMap* map, const void* base, uint32_t inner, uint32_t outer, uint32_t planes) {
   auto fn = encode_fn();
   if (!fn) return false;
   cuuint64_t dims[3] = {inner, outer, planes};
   cuuint64_t strides[2] = {inner, (cuuint64_t)inner * outer};
-  cuuint32_t box[3] = {k_major ? (cuuint32_t)BK : 128u, k_major ? 128u : (cuuint32_t)BK, 1};
+  cuuint32_t box[3] = {128, 128, 1};
   cuuint32_t estr[3] = {1, 1, 1};
   CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void*>(base), dims, strides, box, estr,
-                  CU_TENSOR_MAP_INTERLEAVE_NONE, k_major ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B,
-                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS;
 }
 
@@ -692,10 +662,10 @@ Split split_of(uint32_t rows, uint32_t cols, uint32_t Kp, uint32_t batch) {
   s.tiles = batch * ((rows + BM - 1) / BM) * ((cols + BN - 1) / BN);
   s.num_kb = (Kp + BK - 1) / BK;
   s.splits = 1;
-  // fewer tiles than SMs: split K (at least 512 K per split) to fill the GPU
-  if (s.tiles < (uint32_t)NUM_SMS && s.num_kb >= 16) {
+  // fewer tiles than SMs: split K (at least 4 K blocks per split) to fill the GPU
+  if (s.tiles < (uint32_t)NUM_SMS && s.num_kb >= 8) {
     uint32_t want = (2 * NUM_SMS + s.tiles - 1) / s.tiles;
-    s.splits = want < s.num_kb / 8 ? want : s.num_kb / 8;
+    s.splits = want < s.num_kb / 4 ? want : s.num_kb / 4;
     if (s.splits < 1) s.splits = 1;
   }
   s.kps = (s.num_kb + s.splits - 1) / s.splits;
@@ -762,14 +732,11 @@ int gemm_i8x4(const GemmJob& j, cudaStream_t stream) {
     memset(&m_ahi, 0, sizeof m_ahi);
     m_alo = m_bhi = m_blo = m_ahi;
   } else {
-    bool ok = make_map(&m_ahi, j.a_hi, j.Kp, j.rows, j.a_planes, true) &&
-              make_map(&m_alo, j.a_lo, j.Kp, j.rows, j.a_planes, true);
+    bool ok = make_map(&m_ahi, j.a_hi, j.Kp, j.rows, j.a_planes) && make_map(&m_alo, j.a_lo, j.Kp, j.rows, j.a_planes);
     if (j.b_mn)
-      ok = ok && make_map(&m_bhi, j.b_hi, j.cols_p, j.K, j.b_planes, false) &&
-           make_map(&m_blo, j.b_lo, j.cols_p, j.K, j.b_planes, false);
+      ok = ok && make_map(&m_bhi, j.b_hi, j.cols_p, j.K, j.b_planes) && make_map(&m_blo, j.b_lo, j.cols_p, j.K, j.b_planes);
     else
-      ok = ok && make_map(&m_bhi, j.b_hi, j.Kp, j.cols, j.b_planes, true) &&
-           make_map(&m_blo, j.b_lo, j.Kp, j.cols, j.b_planes, true);
+      ok = ok && make_map(&m_bhi, j.b_hi, j.Kp, j.cols, j.b_planes) && make_map(&m_blo, j.b_lo, j.Kp, j.cols, j.b_planes);
     if (!ok) return fail(CORM_ECUDA, "gemm: cuTensorMapEncodeTiled failed");
   }
   const Split sp = split_of(j.rows, j.cols, j.Kp, j.batch);
