@@ -36,7 +36,6 @@ constexpr int TILE_BYTES = BM * BK;  // 16 KB (BM == BN)
 constexpr int STAGE_BYTES = 4 * TILE_BYTES;
 constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
 constexpr uint32_t TMEM_COLS = 512;
-constexpr int EPI_WARPS = 8;
 constexpr int NUM_SMS = 148;
 
 struct EpiArgs {
@@ -238,10 +237,14 @@ __device__ __forceinline__ Unit unit_of(const EpiArgs& ep, uint32_t u) {
 // 9..16 run the epilogue.
 template <bool CONV>
 struct Roles {
-  static constexpr int threads = CONV ? 64 + 32 * (8 + EPI_WARPS) - 32 : 64 + 32 * EPI_WARPS;
+  // epilogue warps (4 per column group, one per TMEM lane quarter) and the
+  // columns each drains: 16 x 32 with plane operands, 8 x 64 beside the producers
+  static constexpr int ew = CONV ? 8 : 16;
+  static constexpr int wc = BN * 4 / ew;
+  static constexpr int threads = CONV ? 32 + 32 * 8 + 32 * ew : 64 + 32 * ew;
   static constexpr int mma_warp = CONV ? 0 : 1;
   static constexpr int epi0 = CONV ? 9 : 2;
-  static constexpr int chunk = CONV ? 16 : 32;  // TMEM columns per tcgen05.ld (register budget)
+  static constexpr int chunk = 16;  // TMEM columns per tcgen05.ld (register budget)
 };
 
 // 16 int16 (two 16-byte words) -> their 16 high bytes and 16 low bytes
@@ -303,7 +306,7 @@ __global__ void __launch_bounds__(Roles<CONV>::threads, 1)
       sm100::mbar_init(&empty[s], 1);
     }
     sm100::mbar_init(tmem_full, 1);
-    sm100::mbar_init(tmem_empty, EPI_WARPS);
+    sm100::mbar_init(tmem_empty, R::ew);
     sm100::mbar_init(mma_done, 1);
     sm100::fence_mbar_init();
   }
@@ -466,13 +469,13 @@ __global__ void __launch_bounds__(Roles<CONV>::threads, 1)
       const uint32_t r = w.tile_r + q * 32 + lane;
       const bool row_ok = r < ep.rows;
       if (ep.partial) {
-        for (int cc = 64 * h; cc < 64 * h + 64; cc += CW) {
+        for (int cc = R::wc * h; cc < R::wc * h + R::wc; cc += CW) {
           uint32_t hh[CW], mid[CW], ll[CW];
           tmem_ld_cw<CW>(tmem + lane_addr + cc, hh);
           tmem_ld_cw<CW>(tmem + lane_addr + BN + cc, mid);
           tmem_ld_cw<CW>(tmem + lane_addr + 2 * BN + cc, ll);
           sm100::tmem_ld_wait();
-          if (cc + CW >= 64 * h + 64) {  // TMEM drained: the next unit's MMAs may start
+          if (cc + CW >= R::wc * h + R::wc) {  // TMEM drained: the next unit's MMAs may start
             sm100::tc_fence_before();
             __syncwarp();
             if (lane == 0) sm100::mbar_arrive(tmem_empty);
@@ -489,44 +492,45 @@ __global__ void __launch_bounds__(Roles<CONV>::threads, 1)
         }
         continue;
       }
-      if (CW == 32) {
+      if (!CONV) {
         // the 64 results of this thread's row as int16 pairs, then TMEM released,
         // then the fused job and the stores
-        uint32_t v2[32];
+        constexpr int WC = R::wc;
+        uint32_t v2[WC / 2];
 #pragma unroll
-        for (int part = 0; part < 2; part++) {
-          const int cc = 64 * h + 32 * part;
-          uint32_t hh[32], mid[32], ll[32];
-          tmem_ld_cw<32>(tmem + lane_addr + cc, hh);
-          tmem_ld_cw<32>(tmem + lane_addr + BN + cc, mid);
-          tmem_ld_cw<32>(tmem + lane_addr + 2 * BN + cc, ll);
+        for (int part = 0; part < WC / CW; part++) {
+          const int cc = WC * h + CW * part;
+          uint32_t hh[CW], mid[CW], ll[CW];
+          tmem_ld_cw<CW>(tmem + lane_addr + cc, hh);
+          tmem_ld_cw<CW>(tmem + lane_addr + BN + cc, mid);
+          tmem_ld_cw<CW>(tmem + lane_addr + 2 * BN + cc, ll);
           sm100::tmem_ld_wait();
           const uint32_t c0 = w.tile_c + cc;
           if (ep.ymode == 0)
-            combine_cw<32, 0>(ep, hh, mid, ll, c0, v2 + 16 * part);
+            combine_cw<CW, 0>(ep, hh, mid, ll, c0, v2 + (CW / 2) * part);
           else if (ep.ymode == 1)
-            combine_cw<32, 1>(ep, hh, mid, ll, c0, v2 + 16 * part);
+            combine_cw<CW, 1>(ep, hh, mid, ll, c0, v2 + (CW / 2) * part);
           else
-            combine_cw<32, 2>(ep, hh, mid, ll, c0, v2 + 16 * part);
+            combine_cw<CW, 2>(ep, hh, mid, ll, c0, v2 + (CW / 2) * part);
         }
         sm100::tc_fence_before();
         __syncwarp();
         if (lane == 0) sm100::mbar_arrive(tmem_empty);
         if (!row_ok) continue;
-        const uint32_t c0 = w.tile_c + 64 * h;
+        const uint32_t c0 = w.tile_c + WC * h;
         if (ep.post.op != kPostNone) {
-          uint32_t b2[32];
-          post_operand<64>(ep, row_base(ep, w.bz, r), c0, b2);
-          post_dispatch<32>(ep.post, v2, b2);
+          uint32_t b2[WC / 2];
+          post_operand<WC>(ep, row_base(ep, w.bz, r), c0, b2);
+          post_dispatch<WC / 2>(ep.post, v2, b2);
         }
-        store_row<64>(ep, w.bz, r, c0, v2);
+        store_row<WC>(ep, w.bz, r, c0, v2);
       } else {
         // 16 columns at a time (the register budget of the int16-producer layout):
         // TMEM released after the last chunk's load
         const uint64_t rb = row_ok && ep.post.op != kPostNone ? row_base(ep, w.bz, r) : 0;
 #pragma unroll 1
         for (int part = 0; part < 4; part++) {
-          const int cc = 64 * h + 16 * part;
+          const int cc = R::wc * h + 16 * part;
           uint32_t hh[16], mid[16], ll[16];
           tmem_ld_cw<16>(tmem + lane_addr + cc, hh);
           tmem_ld_cw<16>(tmem + lane_addr + BN + cc, mid);
