@@ -124,19 +124,6 @@ __device__ __forceinline__ uint64_t sdesc_sw128_mn(uint32_t smem_addr) {
   return d;
 }
 
-// Shared-memory matrix descriptor: MN-major operand, 64-byte swizzle: rows of
-// 64 bytes hold 64 consecutive MN elements of one k, 8-row swizzle atoms of
-// 512 bytes stacked along K (SBO); one atom along MN (LBO unused at 64).
-__device__ __forceinline__ uint64_t sdesc_sw64_mn(uint32_t smem_addr) {
-  uint64_t d = 0;
-  d |= (uint64_t)((smem_addr & 0x3FFFF) >> 4);  // start address
-  d |= (uint64_t)(8192 >> 4) << 16;             // LBO: stride between 64-byte MN atoms
-  d |= (uint64_t)(512 >> 4) << 32;              // SBO: stride between 8-row K groups
-  d |= (uint64_t)1 << 46;                       // descriptor version (sm_100)
-  d |= (uint64_t)4 << 61;                       // SWIZZLE_64B
-  return d;
-}
-
 // 32 lanes x 32 columns of 32-bit TMEM -> 32 registers per thread
 __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
   asm volatile(

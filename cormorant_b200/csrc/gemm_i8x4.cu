@@ -1,25 +1,20 @@
 // tcgen05 kind::i8 GEMM with the four-way int16 split (see gemm_i8x4.h).
 //
-// Persistent: one CTA per SM walks work units = (batch, 128-row tile,
-// 64-column tile, K split), warp-specialised:
-//   producer    plane operands: one thread issues the TMA loads, per 128-byte
-//               K block 4 tiles (A hi/lo K-major 128 x 128 bytes, 128-byte
-//               swizzle; B hi/lo MN-major 128 K rows x 64 bytes, 64-byte
-//               swizzle, or K-major 64 x 128 bytes; no multicast); int16
-//               operands: 8 warps load them, split each value into its hi / lo
-//               bytes and store the same swizzled layouts.  A 4-deep ring runs
-//               across units.
-//   MMA         one thread (its warp owns TMEM, 512 columns): 16 tcgen05.mma
-//               (128x64x32) per K block into HH / MID / LL of one of two
-//               accumulator sets (the K steps past the job's K, zero-filled,
-//               are not issued); a set is reused once the epilogue drained it
-//   epilogue    8 warps, two per TMEM lane quarter (32 columns each):
-//               tcgen05.ld of the three accumulators, int64/int32 recombine and
-//               the job's rounding rule into registers, the set released, then
-//               the fused VectorOP job and the int16 stores — or, for a K-split
-//               unit, exact int64 atomics into a partial-sum buffer that
-//               gemm_finish_kernel rounds afterwards.  The drain of unit i
-//               overlaps the MMAs of unit i + 1.
+// Persistent: one CTA per SM (6 warps) walks work units = (batch, 128-row
+// tile, 128-column tile, K split), warp-specialised:
+//   warp 0      TMA producer: per 128-byte K block, 4 tiles (A hi/lo K-major,
+//               B hi/lo K-major or MN-major, 128 x 128 bytes, 128-byte swizzle,
+//               no multicast) into a STAGES-deep ring that runs across units
+//   warp 1      TMEM owner (512 columns) and MMA issuer: 16 tcgen05.mma
+//               (128x128x32) per K block into HH / MID / LL (the K steps past
+//               the job's K, zero-filled, are not issued); waits for the
+//               epilogue to drain TMEM before the next unit (tmem_empty)
+//   warps 2..9  epilogue, two warps per TMEM lane quarter (64 columns each):
+//               tcgen05.ld of the three accumulators, int64 recombine and the
+//               job's rounding rule into registers, TMEM released to the next
+//               unit's MMAs, then the int16 stores — or, for a K-split unit,
+//               exact int64 atomics into a partial-sum buffer that
+//               gemm_finish_kernel rounds afterwards
 // Every mbarrier wait is bounded (sm100::mbar_wait); a timeout leaves an error
 // code in the per-device error word and the CTA unwinds (in-flight TMA loads
 // and MMAs waited for, TMEM freed).
@@ -35,13 +30,10 @@
 namespace corm {
 namespace {
 
-constexpr int BM = 128, BN = 64, BK = 128;  // BK in bytes = int8 elements
-constexpr int STAGES = 4;
-constexpr int TILE_A = BM * BK;  // 16 KB per A plane
-constexpr int TILE_B = BN * BK;  // 8 KB per B plane
-constexpr int STAGE_BYTES = 2 * TILE_A + 2 * TILE_B;
-constexpr int ACC_COLS = 3 * BN;   // HH, MID, LL
-constexpr int TMEM_BUF = 256;      // TMEM column offset of the second accumulator set
+constexpr int BM = 128, BN = 128, BK = 128;  // BK in bytes = int8 elements
+constexpr int STAGES = 3;
+constexpr int TILE_BYTES = BM * BK;  // 16 KB (BM == BN)
+constexpr int STAGE_BYTES = 4 * TILE_BYTES;
 constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
 constexpr uint32_t TMEM_COLS = 512;
 constexpr int NUM_SMS = 148;
@@ -241,17 +233,18 @@ __device__ __forceinline__ Unit unit_of(const EpiArgs& ep, uint32_t u) {
 // loads, warp 1 owns TMEM and lane 0 issues the MMAs, warps 2..9 run the
 // epilogue.  int16 operands (CONV = true): warp 0 owns TMEM and issues the
 // MMAs, warps 1..8 load int16 tiles, split them into the hi / lo planes and
-// store them in the swizzled layouts the MMA descriptors read, warps 9..16
-// run the epilogue.  Epilogue warp (epi0 + 4 h + j) drains TMEM lane quarter
-// (warp % 4), columns [32 h, 32 h + 32) of the 64-column tile.
+// store them in the 128-byte swizzled layout the MMA descriptors read, warps
+// 9..16 run the epilogue.
 template <bool CONV>
 struct Roles {
-  static constexpr int ew = 8;
-  static constexpr int wc = BN * 4 / ew;  // 32
+  // epilogue warps (4 per column group, one per TMEM lane quarter) and the
+  // columns each drains: 16 x 32 with plane operands, 8 x 64 beside the producers
+  static constexpr int ew = CONV ? 8 : 16;
+  static constexpr int wc = BN * 4 / ew;
   static constexpr int threads = CONV ? 32 + 32 * 8 + 32 * ew : 64 + 32 * ew;
   static constexpr int mma_warp = CONV ? 0 : 1;
   static constexpr int epi0 = CONV ? 9 : 2;
-  static constexpr int chunk = 16;  // TMEM columns per tcgen05.ld
+  static constexpr int chunk = 16;  // TMEM columns per tcgen05.ld (register budget)
 };
 
 // 16 int16 (two 16-byte words) -> their 16 high bytes and 16 low bytes
@@ -288,9 +281,6 @@ __device__ __forceinline__ void tmem_ld_cw(uint32_t taddr, uint32_t* r) {
     sm100::tmem_ld16(taddr, r);
 }
 
-// The tile is 128 rows x 64 columns with two TMEM accumulator sets (HH, MID,
-// LL at columns 0 / 64 / 128 and TMEM_BUF + the same): the epilogue drains
-// set i & 1 while the MMAs of the next unit fill the other.
 template <bool CONV>
 __global__ void __launch_bounds__(Roles<CONV>::threads, 1)
     gemm_i8x4_kernel(const __grid_constant__ CUtensorMap map_ahi, const __grid_constant__ CUtensorMap map_alo,
@@ -302,9 +292,9 @@ __global__ void __launch_bounds__(Roles<CONV>::threads, 1)
   uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
   uint64_t* full = (uint64_t*)(smem + STAGES * STAGE_BYTES);
   uint64_t* empty = full + STAGES;
-  uint64_t* tmem_full = empty + STAGES;  // [2]
-  uint64_t* tmem_empty = tmem_full + 2;  // [2]
-  uint64_t* mma_done = tmem_empty + 2;
+  uint64_t* tmem_full = empty + STAGES;
+  uint64_t* tmem_empty = tmem_full + 1;
+  uint64_t* mma_done = tmem_empty + 1;
   uint32_t* tmem_slot = (uint32_t*)(mma_done + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -315,10 +305,8 @@ __global__ void __launch_bounds__(Roles<CONV>::threads, 1)
       sm100::mbar_init(&full[s], CONV ? 8 : 1);
       sm100::mbar_init(&empty[s], 1);
     }
-    for (int b = 0; b < 2; b++) {
-      sm100::mbar_init(&tmem_full[b], 1);
-      sm100::mbar_init(&tmem_empty[b], R::ew);
-    }
+    sm100::mbar_init(tmem_full, 1);
+    sm100::mbar_init(tmem_empty, R::ew);
     sm100::mbar_init(mma_done, 1);
     sm100::fence_mbar_init();
   }
@@ -349,13 +337,13 @@ __global__ void __launch_bounds__(Roles<CONV>::threads, 1)
         sm100::mbar_expect_tx(&full[s], STAGE_BYTES);
         const int x = (int)(kb * BK);
         sm100::tma_load_3d(st, &map_ahi, &full[s], x, (int)w.tile_r, a_z);
-        sm100::tma_load_3d(st + TILE_A, &map_alo, &full[s], x, (int)w.tile_r, a_z);
-        if (ep.b_mn) {  // B planes [plane][K][cols]: box = 64 columns x 128 K rows
-          sm100::tma_load_3d(st + 2 * TILE_A, &map_bhi, &full[s], (int)w.tile_c, x, b_z);
-          sm100::tma_load_3d(st + 2 * TILE_A + TILE_B, &map_blo, &full[s], (int)w.tile_c, x, b_z);
-        } else {        // B planes [plane][cols][Kp]: box = 128 K bytes x 64 columns
-          sm100::tma_load_3d(st + 2 * TILE_A, &map_bhi, &full[s], x, (int)w.tile_c, b_z);
-          sm100::tma_load_3d(st + 2 * TILE_A + TILE_B, &map_blo, &full[s], x, (int)w.tile_c, b_z);
+        sm100::tma_load_3d(st + TILE_BYTES, &map_alo, &full[s], x, (int)w.tile_r, a_z);
+        if (ep.b_mn) {  // B planes [plane][K][cols]: box = 128 columns x 128 K rows
+          sm100::tma_load_3d(st + 2 * TILE_BYTES, &map_bhi, &full[s], (int)w.tile_c, x, b_z);
+          sm100::tma_load_3d(st + 3 * TILE_BYTES, &map_blo, &full[s], (int)w.tile_c, x, b_z);
+        } else {
+          sm100::tma_load_3d(st + 2 * TILE_BYTES, &map_bhi, &full[s], x, (int)w.tile_c, b_z);
+          sm100::tma_load_3d(st + 3 * TILE_BYTES, &map_blo, &full[s], x, (int)w.tile_c, b_z);
         }
       }
     }
@@ -366,12 +354,11 @@ __global__ void __launch_bounds__(Roles<CONV>::threads, 1)
     }
   } else if (CONV && warp >= 1 && warp <= 8) {
     // ---------------- int16 producers: per stage the A tile (128 rows x 128 K)
-    // and the MN-major B tile (128 K rows x 64 columns), as units of 16
-    // consecutive int16 -> a 16-byte hi unit and a 16-byte lo unit.  A unit u
-    // of row r at r * 128 + ((u ^ (r & 7)) << 4) (128-byte swizzle), B unit u
-    // of K row r at r * 64 + ((u ^ ((r >> 1) & 3)) << 4) (64-byte swizzle);
-    // rows, K and columns beyond the job are zeros.  K and the column count
-    // are multiples of 8, every base 16-byte aligned (the host checks).
+    // and the MN-major B tile (128 K rows x 128 columns), each as 1024 units of
+    // 16 consecutive int16 -> a 16-byte hi unit and a 16-byte lo unit at the
+    // row's swizzled position (unit u of row r at (u ^ (r & 7)) * 16); rows,
+    // K and columns beyond the job are zeros.  K and the column count are
+    // multiples of 8, every base 16-byte aligned (the host checks).
     const uint32_t pt = (uint32_t)(warp - 1) * 32u + lane;
     uint32_t g = 0;
     bool ok = true;
@@ -381,31 +368,29 @@ __global__ void __launch_bounds__(Roles<CONV>::threads, 1)
       const int16_t* Bb = ep.b16 + (uint64_t)w.bz * ep.b_bs16;
       for (uint32_t kb = w.kb0; kb < w.kb1; kb++, g++) {
         const int s = g % STAGES;
-        const int4 z = make_int4(0, 0, 0, 0);
-        int4 va[4][2], vb[2][2];
+        if (g >= (uint32_t)STAGES && !sm100::mbar_wait(&empty[s], ((g / STAGES) - 1) & 1, ep.err, 101)) {
+          ok = false;
+          break;
+        }
+        uint8_t* st = smem + s * STAGE_BYTES;
+        int4 va[4][2], vb[4][2];
 #pragma unroll
-        for (int i = 0; i < 4; i++) {  // A: 128 rows x 8 units
+        for (int i = 0; i < 4; i++) {
           const uint32_t id = pt + 256u * i, row = id >> 3, uu = id & 7u;
+          const int4 z = make_int4(0, 0, 0, 0);
+          // A row tile_r + row, K kb*128 + 16 uu ..
           const uint32_t ar = w.tile_r + row, ak = kb * BK + uu * 16u;
           const int16_t* pa = Ab + (uint64_t)ar * ep.lda + ak;
           const bool ar_ok = ar < ep.rows;
           va[i][0] = (ar_ok && ak < ep.K) ? __ldg((const int4*)pa) : z;
           va[i][1] = (ar_ok && ak + 8u < ep.K) ? __ldg((const int4*)pa + 1) : z;
-        }
-#pragma unroll
-        for (int i = 0; i < 2; i++) {  // B: 128 K rows x 4 units
-          const uint32_t id = pt + 256u * i, row = id >> 2, uu = id & 3u;
+          // B K row kb*128 + row, columns tile_c + 16 uu ..
           const uint32_t bk = kb * BK + row, bc = w.tile_c + uu * 16u;
           const int16_t* pb = Bb + (uint64_t)bk * ep.ldb + bc;
           const bool bk_ok = bk < ep.K;
           vb[i][0] = (bk_ok && bc < ep.cols) ? __ldg((const int4*)pb) : z;
           vb[i][1] = (bk_ok && bc + 8u < ep.cols) ? __ldg((const int4*)pb + 1) : z;
         }
-        if (g >= (uint32_t)STAGES && !sm100::mbar_wait(&empty[s], ((g / STAGES) - 1) & 1, ep.err, 101)) {
-          ok = false;
-          break;
-        }
-        uint8_t* st = smem + s * STAGE_BYTES;
 #pragma unroll
         for (int i = 0; i < 4; i++) {
           const uint32_t id = pt + 256u * i, row = id >> 3, uu = id & 7u;
@@ -413,16 +398,10 @@ __global__ void __launch_bounds__(Roles<CONV>::threads, 1)
           int4 hi, lo;
           split16_regs(va[i][0], va[i][1], hi, lo);
           *(int4*)(st + off) = hi;
-          *(int4*)(st + TILE_A + off) = lo;
-        }
-#pragma unroll
-        for (int i = 0; i < 2; i++) {
-          const uint32_t id = pt + 256u * i, row = id >> 2, uu = id & 3u;
-          const uint32_t off = row * 64u + ((uu ^ ((row >> 1) & 3u)) << 4);
-          int4 hi, lo;
+          *(int4*)(st + TILE_BYTES + off) = lo;
           split16_regs(vb[i][0], vb[i][1], hi, lo);
-          *(int4*)(st + 2 * TILE_A + off) = hi;
-          *(int4*)(st + 2 * TILE_A + TILE_B + off) = lo;
+          *(int4*)(st + 2 * TILE_BYTES + off) = hi;
+          *(int4*)(st + 3 * TILE_BYTES + off) = lo;
         }
         sm100::fence_proxy_async_smem();
         __syncwarp();
@@ -436,14 +415,13 @@ __global__ void __launch_bounds__(Roles<CONV>::threads, 1)
     const uint32_t ID_SU = sm100::idesc_i8(BM, BN, 1, 0) | bmaj;
     const uint32_t ID_US = sm100::idesc_i8(BM, BN, 0, 1) | bmaj;
     const uint32_t ID_UU = sm100::idesc_i8(BM, BN, 0, 0) | bmaj;
+    const uint32_t acc_hh = tmem, acc_mid = tmem + BN, acc_ll = tmem + 2 * BN;
     uint32_t g = 0, i = 0;
     bool ok = true;
     for (uint32_t u = blockIdx.x; u < units && ok; u += gridDim.x, i++) {
       const Unit w = unit_of(ep, u);
-      const uint32_t buf = i & 1u;
-      if (i >= 2 && !sm100::mbar_wait(&tmem_empty[buf], ((i >> 1) - 1) & 1, ep.err, 104)) break;
+      if (i > 0 && !sm100::mbar_wait(tmem_empty, (i - 1) & 1, ep.err, 104)) break;
       sm100::tc_fence_after();
-      const uint32_t acc_hh = tmem + buf * TMEM_BUF, acc_mid = acc_hh + BN, acc_ll = acc_hh + 2 * BN;
       for (uint32_t kb = w.kb0; kb < w.kb1; kb++, g++) {
         const int s = g % STAGES;
         if (!sm100::mbar_wait(&full[s], (g / STAGES) & 1, ep.err, 102)) {
@@ -452,13 +430,12 @@ __global__ void __launch_bounds__(Roles<CONV>::threads, 1)
         }
         sm100::tc_fence_after();
         const uint32_t base = sm100::smem_u32(smem + s * STAGE_BYTES);
-        const uint64_t d_ahi = sm100::sdesc_sw128(base), d_alo = sm100::sdesc_sw128(base + TILE_A);
-        const uint32_t bb = base + 2 * TILE_A;
-        const uint64_t d_bhi = ep.b_mn ? sm100::sdesc_sw64_mn(bb) : sm100::sdesc_sw128(bb);
-        const uint64_t d_blo = ep.b_mn ? sm100::sdesc_sw64_mn(bb + TILE_B) : sm100::sdesc_sw128(bb + TILE_B);
-        // K step of 32 int8: 32 bytes inside a K-major swizzled row, or 32 K
-        // rows (4 swizzle atoms of 512 bytes) of the MN-major B tile
-        const uint64_t b_step = ep.b_mn ? (uint64_t)(2048 >> 4) : (uint64_t)(32 >> 4);
+        const uint64_t d_ahi = sm100::sdesc_sw128(base), d_alo = sm100::sdesc_sw128(base + TILE_BYTES);
+        const uint64_t d_bhi = ep.b_mn ? sm100::sdesc_sw128_mn(base + 2 * TILE_BYTES) : sm100::sdesc_sw128(base + 2 * TILE_BYTES);
+        const uint64_t d_blo = ep.b_mn ? sm100::sdesc_sw128_mn(base + 3 * TILE_BYTES) : sm100::sdesc_sw128(base + 3 * TILE_BYTES);
+        // K step of 32 int8: 32 bytes inside a K-major swizzled row, or 32 rows
+        // (4 swizzle atoms of 1024 bytes) of an MN-major tile
+        const uint64_t b_step = ep.b_mn ? (uint64_t)(4096 >> 4) : (uint64_t)(32 >> 4);
         const uint32_t krem = ep.K - kb * BK;  // > 0: K steps beyond it only add zeros
         const int nks = krem >= (uint32_t)BK ? BK / 32 : (int)((krem + 31) / 32);
 #pragma unroll
@@ -473,37 +450,35 @@ __global__ void __launch_bounds__(Roles<CONV>::threads, 1)
         }
         sm100::mma_commit(&empty[s]);
       }
-      if (ok) sm100::mma_commit(&tmem_full[buf]);
+      if (ok) sm100::mma_commit(tmem_full);
     }
     // every MMA issued has completed before TMEM is freed
     sm100::mma_commit(mma_done);
     sm100::mbar_wait(mma_done, 0, nullptr, 0, 200000000ll);
   } else if (warp >= R::epi0) {
-    // ---------------- epilogue
+    // ---------------- epilogue: warp (epi0 + 4 h + j) reads lane quarter (warp % 4),
+    // columns [64 h, 64 h + 64)
     const int q = warp & 3;  // TMEM lane quarter this warp may access
     const uint32_t lane_addr = (uint32_t)(q * 32) << 16;
     const int h = (warp - R::epi0) >> 2;
-    constexpr int WC = R::wc;
     uint32_t i = 0;
     for (uint32_t u = blockIdx.x; u < units; u += gridDim.x, i++) {
       const Unit w = unit_of(ep, u);
-      const uint32_t buf = i & 1u;
-      if (!sm100::mbar_wait(&tmem_full[buf], (i >> 1) & 1, ep.err, 103)) break;
+      if (!sm100::mbar_wait(tmem_full, i & 1, ep.err, 103)) break;
       sm100::tc_fence_after();
-      const uint32_t tb = tmem + lane_addr + buf * TMEM_BUF;
       const uint32_t r = w.tile_r + q * 32 + lane;
       const bool row_ok = r < ep.rows;
       if (ep.partial) {
-        for (int cc = WC * h; cc < WC * h + WC; cc += CW) {
+        for (int cc = R::wc * h; cc < R::wc * h + R::wc; cc += CW) {
           uint32_t hh[CW], mid[CW], ll[CW];
-          tmem_ld_cw<CW>(tb + cc, hh);
-          tmem_ld_cw<CW>(tb + BN + cc, mid);
-          tmem_ld_cw<CW>(tb + 2 * BN + cc, ll);
+          tmem_ld_cw<CW>(tmem + lane_addr + cc, hh);
+          tmem_ld_cw<CW>(tmem + lane_addr + BN + cc, mid);
+          tmem_ld_cw<CW>(tmem + lane_addr + 2 * BN + cc, ll);
           sm100::tmem_ld_wait();
-          if (cc + CW >= WC * h + WC) {  // this set drained: the MMAs two units on may use it
+          if (cc + CW >= R::wc * h + R::wc) {  // TMEM drained: the next unit's MMAs may start
             sm100::tc_fence_before();
             __syncwarp();
-            if (lane == 0) sm100::mbar_arrive(&tmem_empty[buf]);
+            if (lane == 0) sm100::mbar_arrive(tmem_empty);
           }
           if (!row_ok) continue;
           const uint32_t c0 = w.tile_c + cc;
@@ -517,36 +492,72 @@ __global__ void __launch_bounds__(Roles<CONV>::threads, 1)
         }
         continue;
       }
-      // this thread's 32 results as int16 pairs, then the set released, then
-      // the fused job and the stores
-      uint32_t v2[WC / 2];
+      if (!CONV) {
+        // the 64 results of this thread's row as int16 pairs, then TMEM released,
+        // then the fused job and the stores
+        constexpr int WC = R::wc;
+        uint32_t v2[WC / 2];
 #pragma unroll
-      for (int part = 0; part < WC / CW; part++) {
-        const int cc = WC * h + CW * part;
-        uint32_t hh[CW], mid[CW], ll[CW];
-        tmem_ld_cw<CW>(tb + cc, hh);
-        tmem_ld_cw<CW>(tb + BN + cc, mid);
-        tmem_ld_cw<CW>(tb + 2 * BN + cc, ll);
-        sm100::tmem_ld_wait();
-        const uint32_t c0 = w.tile_c + cc;
-        if (ep.ymode == 0)
-          combine_cw<CW, 0>(ep, hh, mid, ll, c0, v2 + (CW / 2) * part);
-        else if (ep.ymode == 1)
-          combine_cw<CW, 1>(ep, hh, mid, ll, c0, v2 + (CW / 2) * part);
-        else
-          combine_cw<CW, 2>(ep, hh, mid, ll, c0, v2 + (CW / 2) * part);
+        for (int part = 0; part < WC / CW; part++) {
+          const int cc = WC * h + CW * part;
+          uint32_t hh[CW], mid[CW], ll[CW];
+          tmem_ld_cw<CW>(tmem + lane_addr + cc, hh);
+          tmem_ld_cw<CW>(tmem + lane_addr + BN + cc, mid);
+          tmem_ld_cw<CW>(tmem + lane_addr + 2 * BN + cc, ll);
+          sm100::tmem_ld_wait();
+          const uint32_t c0 = w.tile_c + cc;
+          if (ep.ymode == 0)
+            combine_cw<CW, 0>(ep, hh, mid, ll, c0, v2 + (CW / 2) * part);
+          else if (ep.ymode == 1)
+            combine_cw<CW, 1>(ep, hh, mid, ll, c0, v2 + (CW / 2) * part);
+          else
+            combine_cw<CW, 2>(ep, hh, mid, ll, c0, v2 + (CW / 2) * part);
+        }
+        sm100::tc_fence_before();
+        __syncwarp();
+        if (lane == 0) sm100::mbar_arrive(tmem_empty);
+        if (!row_ok) continue;
+        const uint32_t c0 = w.tile_c + WC * h;
+        if (ep.post.op != kPostNone) {
+          uint32_t b2[WC / 2];
+          post_operand<WC>(ep, row_base(ep, w.bz, r), c0, b2);
+          post_dispatch<WC / 2>(ep.post, v2, b2);
+        }
+        store_row<WC>(ep, w.bz, r, c0, v2);
+      } else {
+        // 16 columns at a time (the register budget of the int16-producer layout):
+        // TMEM released after the last chunk's load
+        const uint64_t rb = row_ok && ep.post.op != kPostNone ? row_base(ep, w.bz, r) : 0;
+#pragma unroll 1
+        for (int part = 0; part < 4; part++) {
+          const int cc = R::wc * h + 16 * part;
+          uint32_t hh[16], mid[16], ll[16];
+          tmem_ld_cw<16>(tmem + lane_addr + cc, hh);
+          tmem_ld_cw<16>(tmem + lane_addr + BN + cc, mid);
+          tmem_ld_cw<16>(tmem + lane_addr + 2 * BN + cc, ll);
+          sm100::tmem_ld_wait();
+          if (part == 3) {
+            sm100::tc_fence_before();
+            __syncwarp();
+            if (lane == 0) sm100::mbar_arrive(tmem_empty);
+          }
+          if (!row_ok) continue;
+          const uint32_t c0 = w.tile_c + cc;
+          uint32_t v8[8];
+          if (ep.ymode == 0)
+            combine_cw<16, 0>(ep, hh, mid, ll, c0, v8);
+          else if (ep.ymode == 1)
+            combine_cw<16, 1>(ep, hh, mid, ll, c0, v8);
+          else
+            combine_cw<16, 2>(ep, hh, mid, ll, c0, v8);
+          if (ep.post.op != kPostNone) {
+            uint32_t b8[8];
+            post_operand<16>(ep, rb, c0, b8);
+            post_dispatch<8>(ep.post, v8, b8);
+          }
+          store_row<16>(ep, w.bz, r, c0, v8);
+        }
       }
-      sm100::tc_fence_before();
-      __syncwarp();
-      if (lane == 0) sm100::mbar_arrive(&tmem_empty[buf]);
-      if (!row_ok) continue;
-      const uint32_t c0 = w.tile_c + WC * h;
-      if (ep.post.op != kPostNone) {
-        uint32_t b2[WC / 2];
-        post_operand<WC>(ep, row_base(ep, w.bz, r), c0, b2);
-        post_dispatch<WC / 2>(ep.post, v2, b2);
-      }
-      store_row<WC>(ep, w.bz, r, c0, v2);
     }
   }
   sm100::tc_fence_before();
@@ -632,17 +643,16 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   return fn;
 }
 
-// [planes][outer][inner] bytes, box box_in x box_out x 1 with the given swizzle
-bool make_map(CUtensorMap* map, const void* base, uint32_t inner, uint32_t outer, uint32_t planes, uint32_t box_in,
-              uint32_t box_out, CUtensorMapSwizzle swz) {
+// [planes][outer][inner] bytes, box 128 x 128 x 1, 128-byte swizzle
+bool make_map(CUtensorMap* map, const void* base, uint32_t inner, uint32_t outer, uint32_t planes) {
   auto fn = encode_fn();
   if (!fn) return false;
   cuuint64_t dims[3] = {inner, outer, planes};
   cuuint64_t strides[2] = {inner, (cuuint64_t)inner * outer};
-  cuuint32_t box[3] = {box_in, box_out, 1};
+  cuuint32_t box[3] = {128, 128, 1};
   cuuint32_t estr[3] = {1, 1, 1};
   CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void*>(base), dims, strides, box, estr,
-                  CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS;
 }
@@ -726,15 +736,11 @@ int gemm_i8x4(const GemmJob& j, cudaStream_t stream) {
     memset(&m_ahi, 0, sizeof m_ahi);
     m_alo = m_bhi = m_blo = m_ahi;
   } else {
-    const auto S128 = CU_TENSOR_MAP_SWIZZLE_128B, S64 = CU_TENSOR_MAP_SWIZZLE_64B;
-    bool ok = make_map(&m_ahi, j.a_hi, j.Kp, j.rows, j.a_planes, BK, BM, S128) &&
-              make_map(&m_alo, j.a_lo, j.Kp, j.rows, j.a_planes, BK, BM, S128);
-    if (j.b_mn)  // [K][cols]: 64 columns (64-byte swizzle) x 128 K rows
-      ok = ok && make_map(&m_bhi, j.b_hi, j.cols_p, j.K, j.b_planes, BN, BK, S64) &&
-           make_map(&m_blo, j.b_lo, j.cols_p, j.K, j.b_planes, BN, BK, S64);
-    else         // [cols][Kp]: 128 K bytes x 64 columns
-      ok = ok && make_map(&m_bhi, j.b_hi, j.Kp, j.cols, j.b_planes, BK, BN, S128) &&
-           make_map(&m_blo, j.b_lo, j.Kp, j.cols, j.b_planes, BK, BN, S128);
+    bool ok = make_map(&m_ahi, j.a_hi, j.Kp, j.rows, j.a_planes) && make_map(&m_alo, j.a_lo, j.Kp, j.rows, j.a_planes);
+    if (j.b_mn)
+      ok = ok && make_map(&m_bhi, j.b_hi, j.cols_p, j.K, j.b_planes) && make_map(&m_blo, j.b_lo, j.cols_p, j.K, j.b_planes);
+    else
+      ok = ok && make_map(&m_bhi, j.b_hi, j.Kp, j.cols, j.b_planes) && make_map(&m_blo, j.b_lo, j.Kp, j.cols, j.b_planes);
     if (!ok) return fail(CORM_ECUDA, "gemm: cuTensorMapEncodeTiled failed");
   }
   const Split sp = split_of(j.rows, j.cols, j.Kp, j.batch);
