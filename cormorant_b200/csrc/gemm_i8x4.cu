@@ -71,12 +71,23 @@ __device__ __forceinline__ int32_t sat_act(int32_t y, uint32_t flags) {
   return y;
 }
 
+// YMODE 0: every term below 2^31 (small K), one int32 sum.  1: the sum of
+// MID, floor(LL / 2^8) and the bias fits int32 (K <= 16384): 2^8 HH plus it
+// in one widening multiply-add, saturated through its high word.  3: the
+// general int64 form.  2: CORM_F_WRAP32, the sum modulo 2^32.
 template <int YMODE>
 __device__ __forceinline__ int16_t combine(uint32_t hh, uint32_t mid, uint32_t ll, int32_t bias, uint32_t flags) {
   if (YMODE == 0) return (int16_t)sat_act((int32_t)hh * 256 + (int32_t)mid + bias + ((int32_t)ll >> 8), flags);
   if (YMODE == 2) {
     const uint32_t acc = (hh << 16) + (mid << 8) + ll + ((uint32_t)bias << 8);
     return (int16_t)sat_act((int32_t)acc >> 8, flags);
+  }
+  if (YMODE == 1) {
+    const int32_t t = (int32_t)mid + bias + ((int32_t)ll >> 8);
+    const int64_t y = (int64_t)(int32_t)hh * 256 + t;
+    const int32_t hi = (int32_t)(y >> 32), lo = (int32_t)y;
+    const int32_t y32 = hi == (lo >> 31) ? lo : (hi < 0 ? INT32_MIN : INT32_MAX);
+    return (int16_t)sat_act(y32, flags);
   }
   int64_t y = (int64_t)(int32_t)hh * 256 + (int32_t)mid + bias + ((int32_t)ll >> 8);
   y = y > 32767 ? 32767 : (y < -32768 ? -32768 : y);
@@ -548,8 +559,10 @@ __global__ void __launch_bounds__(Roles<CONV>::threads, 1)
             combine_cw<16, 0>(ep, hh, mid, ll, c0, v8);
           else if (ep.ymode == 1)
             combine_cw<16, 1>(ep, hh, mid, ll, c0, v8);
-          else
+          else if (ep.ymode == 2)
             combine_cw<16, 2>(ep, hh, mid, ll, c0, v8);
+          else
+            combine_cw<16, 3>(ep, hh, mid, ll, c0, v8);
           if (ep.post.op != kPostNone) {
             uint32_t b8[8];
             post_operand<16>(ep, rb, c0, b8);
@@ -761,8 +774,11 @@ int gemm_i8x4(const GemmJob& j, cudaStream_t stream) {
   ep.post = j.post;
   {
     const uint32_t kk = j.K ? j.K : j.Kp;
+    // int32 when K (2^22 + 2^16 + 2^8) + 2^15 < 2^31; the narrow int64 form
+    // while MID + floor(LL / 2^8) + bias < 2^31 (K (2^16 + 2^8) + 2^15)
     ep.ymode = (j.flags & CORM_F_WRAP32) ? 2u
-               : ((uint64_t)kk * ((1ull << 22) + (1ull << 16) + (1ull << 8)) + (1ull << 15) < (1ull << 31) ? 0u : 1u);
+               : ((uint64_t)kk * ((1ull << 22) + (1ull << 16) + (1ull << 8)) + (1ull << 15) < (1ull << 31) ? 0u
+                  : ((uint64_t)kk * ((1ull << 16) + (1ull << 8)) + (1ull << 15) < (1ull << 31) ? 1u : 3u));
   }
   ep.num_kb = sp.num_kb;
   ep.a_planes = j.a_planes;

@@ -56,3 +56,19 @@ def test_direct_unaligned_falls_back(ops):
     C = torch.empty(n * m, dtype=torch.int16, device="cuda")
     ops.matmul(Ad[1:], torch.from_numpy(B.reshape(-1)).cuda(), C, n=n, k=k, m=m)
     assert np.array_equal(C.cpu().numpy().reshape(n, m), spec.matmul_raw(A[1:].reshape(n, k), B))
+
+
+def test_conv_large_k_int64_rule(ops):
+    """A convolution with K = in_ch kh kw above 16384 (the general int64 form of
+    the rule) on full-range values, against the oracle."""
+    rng = np.random.default_rng(11)
+    N, C, H, W, M = 1, 2048, 6, 5, 24
+    x = rng.integers(-32768, 32768, size=(N, C, H, W)).astype(np.int16)
+    w = rng.integers(-32768, 32768, size=(M, C, 3, 3)).astype(np.int16)
+    b = rng.integers(-32768, 32768, size=(M,)).astype(np.int16)
+    y = torch.full((N * M * H * W,), -8531, dtype=torch.int16, device="cuda")
+    ops.conv(torch.from_numpy(x.reshape(-1)).cuda(), torch.from_numpy(w.reshape(-1)).cuda(),
+             torch.from_numpy(b).cuda(), y, batch=N, in_ch=C, in_h=H, in_w=W, out_ch=M, out_h=H, out_w=W, kh=3,
+             kw=3, pad_top=1, pad_left=1, has_bias=1, flags=2)
+    want = spec.conv_raw(x, w, b, 1, 1, 1, 1, 1, 1, H, W, False)
+    assert np.array_equal(y.cpu().numpy().reshape(N, M, H, W), want)
