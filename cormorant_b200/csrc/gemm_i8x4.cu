@@ -56,7 +56,8 @@ struct EpiArgs {
   const int16_t* b16;
   uint64_t a_bs16, b_bs16;
   uint32_t lda, ldb;
-  uint32_t ymode;  // 0: the rule in int32 (small K), 1: in int64, 2: int32 wrap (CORM_F_WRAP32)
+  uint32_t ymode;  // the form of the rule (floor_acc)
+  uint32_t cvar;   // act (0 none, 1 ReLU, 2 Clip(0,6)) * 2 + conv bias
   int* err;
 };
 
@@ -270,17 +271,78 @@ __device__ __forceinline__ void split16_regs(const int4& w0, const int4& w1, int
   lo.w = (int)__byte_perm((uint32_t)w1.z, (uint32_t)w1.w, 0x6420);
 }
 
-template <int CW, int YMODE>
-__device__ __forceinline__ void combine_cw(const EpiArgs& ep, const uint32_t* hh, const uint32_t* mid,
-                                           const uint32_t* ll, uint32_t c0, uint32_t* out2) {
-  const bool cbias = ep.mode == 1 && ep.bias;
+__device__ __forceinline__ int32_t add_sat32(int32_t a, int32_t b) {
+  int32_t d;
+  asm("add.sat.s32 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+
+// two int32 saturated to int16 and packed (lo in bits 0..15)
+__device__ __forceinline__ uint32_t pack_sat16(int32_t lo, int32_t hi) {
+  uint32_t d;
+  asm("cvt.pack.sat.s16.s32 %0, %1, %2;" : "=r"(d) : "r"(hi), "r"(lo));
+  return d;
+}
+
+// floor(acc / 2^8) of one element as an int32 (saturated to int32 where the
+// exact value lies beyond it; the int16 saturation follows).  YMODE 0: one
+// int32 sum.  1: 2^8 HH plus the int32 MID + bias + floor(LL / 2^8) with a
+// saturating add while |HH| < 2^23, the int64 form otherwise.  2: the sum
+// modulo 2^32 (CORM_F_WRAP32).  3: int64.
+template <int YMODE>
+__device__ __forceinline__ int32_t floor_acc(uint32_t hh, uint32_t mid, uint32_t ll, int32_t bias) {
+  if (YMODE == 0) return (int32_t)hh * 256 + (int32_t)mid + bias + ((int32_t)ll >> 8);
+  if (YMODE == 2) return (int32_t)((hh << 16) + (mid << 8) + ll + ((uint32_t)bias << 8)) >> 8;
+  if (YMODE == 1) {
+    const int32_t t = (int32_t)mid + bias + ((int32_t)ll >> 8);
+    const int32_t h = (int32_t)hh;
+    if (__builtin_expect(h >= -(1 << 23) && h < (1 << 23), 1)) return add_sat32(h * 256, t);
+    const int64_t y = (int64_t)h * 256 + t;
+    return y > INT32_MAX ? INT32_MAX : (y < INT32_MIN ? INT32_MIN : (int32_t)y);
+  }
+  const int64_t y = (int64_t)(int32_t)hh * 256 + (int64_t)(int32_t)mid + bias + ((int32_t)ll >> 8);
+  return y > INT32_MAX ? INT32_MAX : (y < INT32_MIN ? INT32_MIN : (int32_t)y);
+}
+
+// CW accumulator columns of one row -> CW / 2 packed int16 pairs: the rule
+// (YMODE), the conv bias (BIAS) and the act flags (ACT 0 none, 1 ReLU, 2
+// Clip(0,6)) as straight-line code
+template <int CW, int YMODE, int ACT, bool BIAS>
+__device__ __forceinline__ void combine_run(const EpiArgs& ep, const uint32_t* hh, const uint32_t* mid,
+                                            const uint32_t* ll, uint32_t c0, uint32_t* out2) {
 #pragma unroll
   for (int j = 0; j < CW; j += 2) {
-    const int32_t b0 = (cbias && c0 + j < ep.cols) ? ep.bias[c0 + j] : 0;
-    const int32_t b1 = (cbias && c0 + j + 1 < ep.cols) ? ep.bias[c0 + j + 1] : 0;
-    const int16_t y0 = combine<YMODE>(hh[j], mid[j], ll[j], b0, ep.flags);
-    const int16_t y1 = combine<YMODE>(hh[j + 1], mid[j + 1], ll[j + 1], b1, ep.flags);
-    out2[j / 2] = (uint32_t)(uint16_t)y0 | ((uint32_t)(uint16_t)y1 << 16);
+    const int32_t b0 = (BIAS && c0 + j < ep.cols) ? ep.bias[c0 + j] : 0;
+    const int32_t b1 = (BIAS && c0 + j + 1 < ep.cols) ? ep.bias[c0 + j + 1] : 0;
+    uint32_t p = pack_sat16(floor_acc<YMODE>(hh[j], mid[j], ll[j], b0),
+                            floor_acc<YMODE>(hh[j + 1], mid[j + 1], ll[j + 1], b1));
+    if (ACT == 1) p = __vmaxs2(p, 0u);
+    if (ACT == 2) p = __vmins2(__vmaxs2(p, 0u), 0x06000600u);
+    out2[j / 2] = p;
+  }
+}
+
+template <int CW, int YMODE>
+__device__ __forceinline__ void combine_ab(const EpiArgs& ep, const uint32_t* hh, const uint32_t* mid,
+                                           const uint32_t* ll, uint32_t c0, uint32_t* out2) {
+  switch (ep.cvar) {  // act * 2 + bias, uniform per job
+    case 0: combine_run<CW, YMODE, 0, false>(ep, hh, mid, ll, c0, out2); break;
+    case 1: combine_run<CW, YMODE, 0, true>(ep, hh, mid, ll, c0, out2); break;
+    case 2: combine_run<CW, YMODE, 1, false>(ep, hh, mid, ll, c0, out2); break;
+    case 3: combine_run<CW, YMODE, 1, true>(ep, hh, mid, ll, c0, out2); break;
+    case 4: combine_run<CW, YMODE, 2, false>(ep, hh, mid, ll, c0, out2); break;
+    default: combine_run<CW, YMODE, 2, true>(ep, hh, mid, ll, c0, out2); break;
+  }
+}
+
+template <int CW>
+__device__ __forceinline__ void combine_any(const EpiArgs& ep, const uint32_t* hh, const uint32_t* mid,
+                                            const uint32_t* ll, uint32_t c0, uint32_t* out2) {
+  switch (ep.ymode) {
+    case 0: combine_ab<CW, 0>(ep, hh, mid, ll, c0, out2); break;
+    case 1: combine_ab<CW, 1>(ep, hh, mid, ll, c0, out2); break;
+    case 2: combine_ab<CW, 2>(ep, hh, mid, ll, c0, out2); break;
+    default: combine_ab<CW, 3>(ep, hh, mid, ll, c0, out2); break;
   }
 }
 
@@ -517,12 +579,7 @@ __global__ void __launch_bounds__(Roles<CONV>::threads, 1)
           tmem_ld_cw<CW>(tmem + lane_addr + 2 * BN + cc, ll);
           sm100::tmem_ld_wait();
           const uint32_t c0 = w.tile_c + cc;
-          if (ep.ymode == 0)
-            combine_cw<CW, 0>(ep, hh, mid, ll, c0, v2 + (CW / 2) * part);
-          else if (ep.ymode == 1)
-            combine_cw<CW, 1>(ep, hh, mid, ll, c0, v2 + (CW / 2) * part);
-          else
-            combine_cw<CW, 2>(ep, hh, mid, ll, c0, v2 + (CW / 2) * part);
+          combine_any<CW>(ep, hh, mid, ll, c0, v2 + (CW / 2) * part);
         }
         sm100::tc_fence_before();
         __syncwarp();
@@ -555,14 +612,7 @@ __global__ void __launch_bounds__(Roles<CONV>::threads, 1)
           if (!row_ok) continue;
           const uint32_t c0 = w.tile_c + cc;
           uint32_t v8[8];
-          if (ep.ymode == 0)
-            combine_cw<16, 0>(ep, hh, mid, ll, c0, v8);
-          else if (ep.ymode == 1)
-            combine_cw<16, 1>(ep, hh, mid, ll, c0, v8);
-          else if (ep.ymode == 2)
-            combine_cw<16, 2>(ep, hh, mid, ll, c0, v8);
-          else
-            combine_cw<16, 3>(ep, hh, mid, ll, c0, v8);
+          combine_any<16>(ep, hh, mid, ll, c0, v8);
           if (ep.post.op != kPostNone) {
             uint32_t b8[8];
             post_operand<16>(ep, rb, c0, b8);
@@ -780,6 +830,8 @@ int gemm_i8x4(const GemmJob& j, cudaStream_t stream) {
                : ((uint64_t)kk * ((1ull << 22) + (1ull << 16) + (1ull << 8)) + (1ull << 15) < (1ull << 31) ? 0u
                   : ((uint64_t)kk * ((1ull << 16) + (1ull << 8)) + (1ull << 15) < (1ull << 31) ? 1u : 3u));
   }
+  ep.cvar = ((j.flags & CORM_F_ACT_RELU6) ? 4u : ((j.flags & CORM_F_ACT_RELU) ? 2u : 0u)) +
+            ((j.mode == 1 && j.bias) ? 1u : 0u);
   ep.num_kb = sp.num_kb;
   ep.a_planes = j.a_planes;
   ep.b_planes = j.b_planes;

@@ -58,11 +58,13 @@ def test_direct_unaligned_falls_back(ops):
     assert np.array_equal(C.cpu().numpy().reshape(n, m), spec.matmul_raw(A[1:].reshape(n, k), B))
 
 
-def test_conv_large_k_int64_rule(ops):
-    """A convolution with K = in_ch kh kw above 16384 (the general int64 form of
-    the rule) on full-range values, against the oracle."""
+@pytest.mark.parametrize("C,H,W", [(2048, 6, 5), (3640, 4, 4)])
+def test_conv_large_k_int64_rule(ops, C, H, W):
+    """Convolutions with K = in_ch kh kw of 18432 (the widening form of the
+    rule) and 32760 (the general int64 form) on full-range values, against
+    the oracle."""
     rng = np.random.default_rng(11)
-    N, C, H, W, M = 1, 2048, 6, 5, 24
+    N, M = 1, 24
     x = rng.integers(-32768, 32768, size=(N, C, H, W)).astype(np.int16)
     w = rng.integers(-32768, 32768, size=(M, C, 3, 3)).astype(np.int16)
     b = rng.integers(-32768, 32768, size=(M,)).astype(np.int16)
