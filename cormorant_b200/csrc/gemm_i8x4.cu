@@ -271,12 +271,6 @@ __device__ __forceinline__ void split16_regs(const int4& w0, const int4& w1, int
   lo.w = (int)__byte_perm((uint32_t)w1.z, (uint32_t)w1.w, 0x6420);
 }
 
-__device__ __forceinline__ int32_t add_sat32(int32_t a, int32_t b) {
-  int32_t d;
-  asm("add.sat.s32 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
-  return d;
-}
-
 // two int32 saturated to int16 and packed (lo in bits 0..15)
 __device__ __forceinline__ uint32_t pack_sat16(int32_t lo, int32_t hi) {
   uint32_t d;
@@ -285,23 +279,21 @@ __device__ __forceinline__ uint32_t pack_sat16(int32_t lo, int32_t hi) {
 }
 
 // floor(acc / 2^8) of one element as an int32 (saturated to int32 where the
-// exact value lies beyond it; the int16 saturation follows).  YMODE 0: one
-// int32 sum.  1: 2^8 HH plus the int32 MID + bias + floor(LL / 2^8) with a
-// saturating add while |HH| < 2^23, the int64 form otherwise.  2: the sum
-// modulo 2^32 (CORM_F_WRAP32).  3: int64.
+// exact value lies beyond it; the int16 saturation follows), branch-free.
+// YMODE 0: one int32 sum (every term below 2^31).  1 (|MID + bias +
+// floor(LL / 2^8)| < 2^29): HH clamped to [-2^22, 2^22) before the shift —
+// a clamped HH puts the sum beyond 2^29 with HH's sign, so the int16 result
+// is the same.  2: the sum modulo 2^32 (CORM_F_WRAP32).  3: int64.
 template <int YMODE>
 __device__ __forceinline__ int32_t floor_acc(uint32_t hh, uint32_t mid, uint32_t ll, int32_t bias) {
   if (YMODE == 0) return (int32_t)hh * 256 + (int32_t)mid + bias + ((int32_t)ll >> 8);
   if (YMODE == 2) return (int32_t)((hh << 16) + (mid << 8) + ll + ((uint32_t)bias << 8)) >> 8;
   if (YMODE == 1) {
-    const int32_t t = (int32_t)mid + bias + ((int32_t)ll >> 8);
-    const int32_t h = (int32_t)hh;
-    if (__builtin_expect(h >= -(1 << 23) && h < (1 << 23), 1)) return add_sat32(h * 256, t);
-    const int64_t y = (int64_t)h * 256 + t;
-    return y > INT32_MAX ? INT32_MAX : (y < INT32_MIN ? INT32_MIN : (int32_t)y);
+    const int32_t h = min(max((int32_t)hh, -(1 << 22)), (1 << 22) - 1);
+    return h * 256 + (int32_t)mid + bias + ((int32_t)ll >> 8);
   }
   const int64_t y = (int64_t)(int32_t)hh * 256 + (int64_t)(int32_t)mid + bias + ((int32_t)ll >> 8);
-  return y > INT32_MAX ? INT32_MAX : (y < INT32_MIN ? INT32_MIN : (int32_t)y);
+  return (int32_t)min(max(y, (int64_t)INT32_MIN), (int64_t)INT32_MAX);
 }
 
 // CW accumulator columns of one row -> CW / 2 packed int16 pairs: the rule
@@ -824,11 +816,11 @@ int gemm_i8x4(const GemmJob& j, cudaStream_t stream) {
   ep.post = j.post;
   {
     const uint32_t kk = j.K ? j.K : j.Kp;
-    // int32 when K (2^22 + 2^16 + 2^8) + 2^15 < 2^31; the narrow int64 form
-    // while MID + floor(LL / 2^8) + bias < 2^31 (K (2^16 + 2^8) + 2^15)
+    // int32 when K (2^22 + 2^16 + 2^8) + 2^15 < 2^31; the clamped-HH form
+    // while MID + floor(LL / 2^8) + bias < 2^29 (K (2^16 + 2^8) + 2^15)
     ep.ymode = (j.flags & CORM_F_WRAP32) ? 2u
                : ((uint64_t)kk * ((1ull << 22) + (1ull << 16) + (1ull << 8)) + (1ull << 15) < (1ull << 31) ? 0u
-                  : ((uint64_t)kk * ((1ull << 16) + (1ull << 8)) + (1ull << 15) < (1ull << 31) ? 1u : 3u));
+                  : ((uint64_t)kk * ((1ull << 16) + (1ull << 8)) + (1ull << 15) < (1ull << 29) ? 1u : 3u));
   }
   ep.cvar = ((j.flags & CORM_F_ACT_RELU6) ? 4u : ((j.flags & CORM_F_ACT_RELU) ? 2u : 0u)) +
             ((j.mode == 1 && j.bias) ? 1u : 0u);

@@ -74,3 +74,31 @@ def test_conv_large_k_int64_rule(ops, C, H, W):
              kw=3, pad_top=1, pad_left=1, has_bias=1, flags=2)
     want = spec.conv_raw(x, w, b, 1, 1, 1, 1, 1, 1, H, W, False)
     assert np.array_equal(y.cpu().numpy().reshape(N, M, H, W), want)
+
+
+@pytest.mark.parametrize("k", [512, 2048, 4096])
+@pytest.mark.parametrize("pattern", ["min_min", "min_max", "cancel"])
+def test_extreme_accumulators(ops, k, pattern):
+    """Operands at the int16 extremes: HH at its largest (-32768 * -32768 over
+    the whole K), of both signs, and MID / LL pulling against HH — the
+    epilogue's forms of floor(acc / 2^8) (int32, clamped HH, int64) agree
+    with the oracle's exact sums."""
+    rng = np.random.default_rng(k)
+    n, m = 130, 72
+    if pattern == "min_min":
+        A = np.full((n, k), -32768, np.int16)
+        B = np.full((k, m), -32768, np.int16)
+    elif pattern == "min_max":
+        A = np.full((n, k), -32768, np.int16)
+        B = np.full((k, m), 32767, np.int16)
+    else:  # hi bytes -128 with lo bytes 255 against lo bytes 0
+        A = np.where(rng.random((n, k)) < 0.5, -32513, -32768).astype(np.int16)
+        B = np.where(rng.random((k, m)) < 0.5, -32768, 255).astype(np.int16)
+    C = torch.empty(n * m, dtype=torch.int16, device="cuda")
+    # the int16-producer path (aligned operands, small n)
+    ops.matmul(torch.from_numpy(A.reshape(-1)).cuda(), torch.from_numpy(B.reshape(-1)).cuda(), C, n=n, k=k, m=m)
+    assert np.array_equal(C.cpu().numpy().reshape(n, m), spec.matmul_raw(A, B))
+    # the plane path: the same sums through split planes and TMA (an unaligned B offset)
+    Bp = np.concatenate([np.zeros(1, np.int16), B.reshape(-1)])
+    ops.matmul(torch.from_numpy(A.reshape(-1)).cuda(), torch.from_numpy(Bp).cuda()[1:], C, n=n, k=k, m=m)
+    assert np.array_equal(C.cpu().numpy().reshape(n, m), spec.matmul_raw(A, B))
