@@ -412,9 +412,13 @@ __global__ void __launch_bounds__(256) ro_norm16(RoArgs q) {
   int64_t* s_bq = (int64_t*)ro_smem;
   int32_t* s_g = (int32_t*)(s_bq + npar);
   uint8_t* s_sc = (uint8_t*)(s_g + npar);
+  __shared__ int s_scmin;
+  if (threadIdx.x == 0) s_scmin = 63;
+  __syncthreads();
   for (uint32_t c = threadIdx.x; c < npar; c += blockDim.x) {
     const int4 e = *(const int4*)(q.p + 16ull * c);
     const uint32_t slot = bcast ? 0u : (c & 7u) * words + (c >> 3);
+    atomicMin(&s_scmin, (int)(((uint32_t)e.z >> 16) & 63u));
     s_g[slot] = e.x;
     const int64_t bq = (int32_t)((uint32_t)e.y << 10) >> 10;  // int22, sign-extended
     s_bq[slot] = q.bq_sh <= 40u ? bq << q.bq_sh : 0;       // (the 128-bit path shifts itself)
@@ -431,7 +435,7 @@ __global__ void __launch_bounds__(256) ro_norm16(RoArgs q) {
     const uint8_t* ra = q.a + (uint64_t)i2 * q.a_s2 + (uint64_t)i1 * q.a_s1;
     uint8_t* rc = q.c + (uint64_t)i2 * q.c_s2 + (uint64_t)i1 * q.c_s1;
     int4 xv[NW_PER];
-    int s1 = 0;
+    int s1 = 0, xmax = -32768, xmin = 32767;
     long long s2 = 0;
 #pragma unroll
     for (int k = 0; k < NW_PER; k++) {
@@ -444,6 +448,8 @@ __global__ void __launch_bounds__(256) ro_norm16(RoArgs q) {
         for (int e = 0; e < 8; e++) {
           s1 += xs[e];
           s2 += xs[e] * xs[e];  // each square < 2^30
+          xmax = max(xmax, (int)xs[e]);
+          xmin = min(xmin, (int)xs[e]);
         }
       }
     }
@@ -451,6 +457,8 @@ __global__ void __launch_bounds__(256) ro_norm16(RoArgs q) {
     for (int o = 16; o > 0; o >>= 1) {
       s1 += __shfl_xor_sync(0xffffffffu, s1, o);
       s2 += __shfl_xor_sync(0xffffffffu, s2, o);
+      xmax = max(xmax, __shfl_xor_sync(0xffffffffu, xmax, o));
+      xmin = min(xmin, __shfl_xor_sync(0xffffffffu, xmin, o));
     }
     __int128 D = ln ? ((__int128)q.n * s2 - (__int128)s1 * s1 + (__int128)q.eps) : ((__int128)s2 + (__int128)q.eps);
     if (D <= 0) D = 1;
@@ -459,6 +467,11 @@ __global__ void __launch_bounds__(256) ro_norm16(RoArgs q) {
     rsqrt_bf(D, Rm, sh, q.rsq);
     const int shp = sh - 24;
     const int nn = ln ? (int)q.n : 1, off = ln ? s1 : 0;  // |n x - S1| < 2^28
+    // the whole row on the 64-bit path when every |P1| < 2^31 (bounded by
+    // the extreme A), Bq' << bq_sh < 2^61 and every sh_c >= 1: no branch per
+    // element; the rare other rows element by element in 128 bits
+    const long long amax = max(llabs((long long)nn * xmax - off), llabs((long long)nn * xmin - off));
+    const bool row_fast = small_bq && s_scmin >= 1 && ((amax * (long long)Rm) >> shp) < (1ll << 31) - 1;
 #pragma unroll
     for (int k = 0; k < NW_PER; k++) {
       const uint32_t w = lane + 32u * k;
@@ -466,21 +479,25 @@ __global__ void __launch_bounds__(256) ro_norm16(RoArgs q) {
       const int16_t* xs = (const int16_t*)&xv[k];
       int4 out;
       int16_t* os = (int16_t*)&out;
+      if (row_fast) {
 #pragma unroll
-      for (int e = 0; e < 8; e++) {
-        const uint32_t slot = bcast ? 0u : (uint32_t)e * words + w;
-        const int64_t g = s_g[slot];
-        const int sc = s_sc[slot];
-        const int A = nn * xs[e] - off;
-        const long long P1 = ((long long)A * (long long)Rm) >> shp;  // |A Rm| < 2^60
-        int64_t r;
-        if (small_bq && P1 > -(1ll << 31) && P1 < (1ll << 31)) {
-          const long long v = corm_rne_shr64(P1 * g + s_bq[slot], sc);
-          r = v > 32767 ? 32767 : (v < -32768 ? -32768 : v);
-        } else {
-          r = norm_out128(P1, g, ld_param(q, bcast ? 0u : 8u * w + e).bq, q.bq_sh, sc);
+        for (int e = 0; e < 8; e++) {
+          const uint32_t slot = bcast ? 0u : (uint32_t)e * words + w;
+          const int A = nn * xs[e] - off;
+          const long long P1 = ((long long)A * (long long)Rm) >> shp;  // |A Rm| < 2^60
+          const long long v = P1 * s_g[slot] + s_bq[slot];
+          const int sc = s_sc[slot];
+          const long long qv = v >> sc, rr = v - (qv << sc), half = 1ll << (sc - 1);
+          const long long y = qv + ((rr > half) | ((rr == half) & (qv & 1)));
+          os[e] = (int16_t)min(max(y, -32768ll), 32767ll);
         }
-        os[e] = (int16_t)r;
+      } else {
+        for (int e = 0; e < 8; e++) {
+          const uint32_t slot = bcast ? 0u : (uint32_t)e * words + w;
+          const int A = nn * xs[e] - off;
+          const long long P1 = ((long long)A * (long long)Rm) >> shp;
+          os[e] = (int16_t)norm_out128(P1, s_g[slot], ld_param(q, bcast ? 0u : 8u * w + e).bq, q.bq_sh, s_sc[slot]);
+        }
       }
       *(int4*)(rc + 16ull * w) = out;
     }

@@ -171,7 +171,9 @@ __device__ __forceinline__ int64_t warp_reduce_sum(int64_t v) {
 // 2^41 is one 32 x 32 -> 64 multiply.
 __device__ __forceinline__ uint32_t smx_e32(int32_t m, int32_t x, uint32_t cm, uint32_t cs, const int32_t* tab) {
   const uint64_t y = ((uint64_t)(uint32_t)(m - x) * cm) >> cs;
-  return y >= (17ull << 12) ? 0u : ((uint32_t)tab[y & 4095u] >> (uint32_t)(y >> 12));
+  const uint32_t yc = (uint32_t)min(y, (uint64_t)(17u << 12) - 1u);  // the table read is unconditional
+  const uint32_t e = (uint32_t)tab[yc & 4095u] >> (yc >> 12);
+  return y >= (17ull << 12) ? 0u : e;
 }
 
 __device__ __forceinline__ int16_t smx_p32(uint32_t e, uint32_t R, uint64_t rnd, uint32_t sh) {
