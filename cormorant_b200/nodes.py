@@ -35,6 +35,7 @@ class TensorInfo:
     wexp: Optional[np.ndarray] = field(default=None, repr=False)
     is_state: bool = False
     init_data: Optional[np.ndarray] = field(default=None, repr=False)
+    dma: Optional[str] = None  # "i32": an int32 DMA tensor at ``exp`` (the LLM residual stream)
 
     @property
     def numel(self) -> int:
@@ -184,6 +185,82 @@ class TransposeRoNode:
     a_off: int = 0
     strides: tuple = (0, 0, 0, 0, 0, 0)
     perm: list = field(default_factory=list)
+    onnx_node: object = None
+
+
+@dataclass
+class ResAddRoNode:
+    """LlmResAdd on the row-ops unit (rowops_nodes.py:400-446): h1 = sat32(h +
+    d << (fr - f_d)), h / h1 int32 DMA tensors at 2^-fr, d int16 at its
+    per-channel exponents; one ADDX job.  inputs [h, d, P]."""
+    inputs: List[TensorInfo]
+    output: TensorInfo
+    rows: int = 1
+    n: int = 1
+    fr: int = 15
+    bcast: bool = True
+    F: int = 8
+    onnx_node: object = None
+
+
+@dataclass
+class RMSNormRoNode:
+    """LlmRMSNorm on the row-ops unit (rowops_nodes.py:449-497): the int32
+    residual at 2^-fr -> int16 at the output's per-channel exponents, NORM
+    (rms); inputs [h, P]."""
+    inputs: List[TensorInfo]
+    output: TensorInfo
+    rows: int = 1
+    n: int = 1
+    fr: int = 15
+    eps: float = 1e-5
+    g: int = 0
+    E: int = 0
+    bcast: bool = False
+    gamma: Optional[np.ndarray] = field(default=None, repr=False)
+    F: int = 8
+    onnx_node: object = None
+
+
+@dataclass
+class WidenRoNode:
+    """LlmWiden on the row-ops unit (rowops_nodes.py:500-537): int16 at
+    per-channel exponents -> the int32 DMA tensor at one exponent, COPY;
+    inputs [x, P]."""
+    inputs: List[TensorInfo]
+    output: TensorInfo
+    rows: int = 1
+    n: int = 1
+    bcast: bool = True
+    F: int = 8
+    onnx_node: object = None
+
+
+@dataclass
+class SiluMulRoNode:
+    """LlmSiluMul on the row-ops unit (rowops_nodes.py:540-583): a = silu(g) *
+    u, MULACT; inputs [g, u, P]."""
+    inputs: List[TensorInfo]
+    output: TensorInfo
+    rows: int = 1
+    n: int = 1
+    bcast: bool = False
+    F: int = 8
+    onnx_node: object = None
+
+
+@dataclass
+class VitGeluVopNode:
+    """VitGelu on VectorOPKernel (vit_nodes.py:580-668): ADD f + ba, then MUL
+    by sc with act GELU (erf) / GELU_TANH, rows runs of n with the [n]
+    operands repeated; inputs [f, ba, sc] (ba / sc constant raw rows),
+    output at 2^-8."""
+    inputs: List[TensorInfo]
+    output: TensorInfo
+    rows: int = 1
+    n: int = 1
+    F: int = 8
+    erf: bool = False
     onnx_node: object = None
 
 

@@ -93,6 +93,50 @@ def layernorm_job(gamma: np.ndarray, beta: Optional[np.ndarray], n: int, eps: fl
     return param_block(G, bqp, 0, 0, P1_BITS + g - F), int(g), int(bb), int(E)
 
 
+def pblock(G, Bq, sh_a, sh_b, sh_c, n: int):
+    """(words, bcast): the parameter block of n columns, one P_BCAST entry
+    when every column's fields are equal (rowops_nodes.py:368-377)."""
+    cols = [np.broadcast_to(np.asarray(v, np.int64), (n,)) for v in (G, Bq, sh_a, sh_b, sh_c)]
+    bcast = all((c == c[0]).all() for c in cols)
+    if bcast:
+        cols = [c[:1] for c in cols]
+    return param_block(*cols), bool(bcast)
+
+
+def resadd_job(fr: int, fd, n: int):
+    """LlmResAdd on the unit: h (int32 at 2^-fr) + d (int16 at fd[c] <= fr) as
+    ADDX with sh_b = fr - fd (rowops_nodes.py:595-611)."""
+    return pblock(0, 0, 0, fr - np.asarray(fd, np.int64), 0, n)
+
+
+def rmsnorm_job(gamma, eps: float, fr: int, fo):
+    """LlmRMSNorm on the unit, int32 rows at 2^-fr -> int16 at fo[c]: (words,
+    bcast, g, E) with G = rint(gamma sqrt(n) 2^g), sh_c = 24 + g - fo
+    (rowops_nodes.py:614-645)."""
+    gamma = np.asarray(gamma, np.float64).reshape(-1)
+    n = gamma.size
+    G, g, _bq, E = norm_params(gamma, n, eps, fr, rms=True)
+    sh_c = P1_BITS + g - np.asarray(fo, np.int64)
+    words, bcast = pblock(G, 0, 0, 0, sh_c, n)
+    return words, bcast, int(g), int(E)
+
+
+def widen_job(fx, fy: int, n: int):
+    """LlmWiden: int16 at fx[c] -> int32 at fy, COPY with sh_a = fy - fx
+    (rowops_nodes.py:648-665)."""
+    return pblock(0, 0, fy - np.asarray(fx, np.int64), 0, 0, n)
+
+
+G_BITS, SILU_BITS = 14, 20
+
+
+def silu_mul_job(fg, fu, fa, n: int):
+    """LlmSiluMul: MULACT with sh_a = 14 - fg, sh_c = 20 + fu - fa
+    (rowops_nodes.py:668-689)."""
+    fg, fu, fa = (np.asarray(v, np.int64) for v in (fg, fu, fa))
+    return pblock(0, 0, G_BITS - fg, 0, SILU_BITS + fu - fa, n)
+
+
 def collapse(dims, sstr):
     """Merge output dims adjacent in the source, drop size-1 dims
     (host_nodes.py:129-148, without the 5-dim padding)."""

@@ -415,10 +415,99 @@ def make_graph_goldens(ref, out):
         print(f"sim_graph_{name}.npz: {len(g.nodes)} nodes")
 
 
+def make_llm_nodes(ref, out):
+    """The LLM kernel nodes on seeded single-node graphs — ResAddRoNode,
+    RMSNormRoNode, WidenRoNode, SiluMulRoNode (rowops_nodes.py:400-583) with
+    their parameter blocks built as the from_llm_* constructors build them,
+    and VitGeluVopNode (vit_nodes.py:580-668) — run through the reference's
+    _forward_pass.  Saved: inputs and outputs as raw integers at their
+    exponents, the parameter words and registers."""
+    sim = _import_reference(ref)
+    from src.dtype import AP_FIXED_16_8 as D
+    from src.tensor import TensorInfo as T
+    from src import rowops_nodes as RON, rowops_spec as RS, vit_nodes as VN
+    import onnx
+    rng = np.random.default_rng(41)
+    res = {}
+
+    def run(node, ins, feeds):
+        g = _Graph([node], [t for t in node.inputs if t.data is not None], ins, [node.output])
+        return _shim(sim, D, g)._forward_pass(feeds)[node.output.onnx_name]
+
+    def ten(name, shape, exp=None, dma=None, data=None):
+        return T(onnx_name=name, shape=list(shape), dtype="float32", data=data,
+                 exp=None if exp is None else np.asarray(exp, np.int64), dma=dma)
+
+    rows, n = 6, 64
+    # ResAdd: h int32 at 2^-15, d int16 at per-channel exponents <= 15
+    fr, fd = 15, rng.integers(8, 16, n)
+    hraw = rng.integers(-(1 << 28), 1 << 28, (rows, n))
+    draw = rng.integers(-32768, 32768, (rows, n))
+    tens = {}
+    h, d, y = ten("h", (rows, n), fr, "i32"), ten("d", (rows, n), fd), ten("y", (rows, n), fr, "i32")
+    pt, bc = RON._pblock(tens, "y__p", 0, 0, 0, fr - fd, 0, n)
+    node = RON.ResAddRoNode(onnx_node=onnx.NodeProto(), inputs=[h, d, pt, RON.tables_tensor(tens)], output=y,
+                            F=8, rows=rows, n=n, fr=fr, bcast=bc)
+    yv = run(node, [h, d], {"h": hraw / 2.0 ** fr, "d": draw / np.power(2.0, fd)[None, :]})
+    res.update(resadd_h=hraw, resadd_d=draw, resadd_fd=fd, resadd_y=np.rint(yv * 2.0 ** fr).astype(np.int64),
+               resadd_p=np.rint(np.asarray(pt.data, np.float64) * 256).astype(np.int64), resadd_bc=np.array([bc]))
+    # RMSNorm: int32 rows at 2^-15 -> int16 at per-channel exponents (one per channel of a row)
+    gamma = 1.0 + 0.1 * rng.standard_normal(n)
+    fo = rng.integers(10, 13, n)
+    hraw = rng.integers(-(1 << 24), 1 << 24, (rows, n))
+    h, y = ten("h", (rows, n), fr, "i32"), ten("y", (rows, n), fo)
+    G, g, _bq, E = RS.norm_params(gamma, n, 1e-5, fr, rms=True)
+    pt, bc = RON._pblock(tens, "y__p2", G, 0, 0, 0, RS.P1_BITS + g - fo, n)
+    node = RON.RMSNormRoNode(onnx_node=onnx.NodeProto(), inputs=[h, pt, RON.tables_tensor(tens)], output=y, F=8,
+                             rows=rows, n=n, fr=fr, eps=1e-5, g=int(g), E=int(E), bcast=bc, gamma=gamma)
+    yv = run(node, [h], {"h": hraw / 2.0 ** fr})
+    res.update(rms_h=hraw, rms_gamma=gamma, rms_fo=fo, rms_y=np.rint(yv * np.power(2.0, fo)[None, :]).astype(np.int64),
+               rms_p=np.rint(np.asarray(pt.data, np.float64) * 256).astype(np.int64),
+               rms_regs=np.array([int(bc), int(g), int(E)], np.int64))
+    # Widen: int16 at fx[c] -> int32 at 12
+    fx, fy = rng.integers(4, 13, n), 12
+    xraw = rng.integers(-32768, 32768, (rows, n))
+    x, y = ten("x", (rows, n), fx), ten("y", (rows, n), fy, "i32")
+    pt, bc = RON._pblock(tens, "y__p3", 0, 0, fy - fx, 0, 0, n)
+    node = RON.WidenRoNode(onnx_node=onnx.NodeProto(), inputs=[x, pt, RON.tables_tensor(tens)], output=y, F=8,
+                           rows=rows, n=n, bcast=bc)
+    yv = run(node, [x], {"x": xraw / np.power(2.0, fx)[None, :]})
+    res.update(widen_x=xraw, widen_fx=fx, widen_y=np.rint(yv * 2.0 ** fy).astype(np.int64),
+               widen_p=np.rint(np.asarray(pt.data, np.float64) * 256).astype(np.int64))
+    # SiluMul: g at fg[c] <= 14, u at fu[c], a at fa[c]
+    fg, fu, fa = rng.integers(6, 15, n), rng.integers(8, 13, n), rng.integers(8, 13, n)
+    graw = rng.integers(-32768, 32768, (rows, n))
+    uraw = rng.integers(-32768, 32768, (rows, n))
+    gt, ut, y = ten("g", (rows, n), fg), ten("u", (rows, n), fu), ten("y", (rows, n), fa)
+    pt, bc = RON._pblock(tens, "y__p4", 0, 0, RS.G_BITS - fg, 0, RS.SILU_BITS + fu - fa, n)
+    node = RON.SiluMulRoNode(onnx_node=onnx.NodeProto(), inputs=[gt, ut, pt, RON.tables_tensor(tens)], output=y, F=8,
+                             rows=rows, n=n, bcast=bc)
+    yv = run(node, [gt, ut], {"g": graw / np.power(2.0, fg)[None, :], "u": uraw / np.power(2.0, fu)[None, :]})
+    res.update(silu_g=graw, silu_u=uraw, silu_fg=fg, silu_fu=fu, silu_fa=fa,
+               silu_y=np.rint(yv * np.power(2.0, fa)[None, :]).astype(np.int64),
+               silu_p=np.rint(np.asarray(pt.data, np.float64) * 256).astype(np.int64))
+    # VitGelu: f at ff[c], ba / sc raw rows; erf and tanh
+    ff = rng.integers(6, 12, n)
+    fraw = rng.integers(-32768, 32768, (rows, n))
+    ba = rng.integers(-4000, 4000, n)
+    sc = rng.integers(1, 600, n)
+    for erf in (False, True):
+        f = ten("f", (rows, n), ff)
+        bat, sct = ten("ba", (n,), data=(ba / 256.0).astype(np.float32)), ten("sc", (n,), data=(sc / 256.0).astype(np.float32))
+        y = ten("y", (rows, n))
+        node = VN.VitGeluVopNode(onnx_node=onnx.NodeProto(), inputs=[f, bat, sct], output=y, rows=rows, n=n, F=8,
+                                 erf=erf)
+        yv = run(node, [f], {"f": fraw / np.power(2.0, ff)[None, :]})
+        res[f"vit_y_{int(erf)}"] = np.rint(yv * 256).astype(np.int64)
+    res.update(vit_f=fraw, vit_ff=ff, vit_ba=ba, vit_sc=sc)
+    np.savez_compressed(os.path.join(out, "sim_llm_nodes.npz"), **res)
+    print("sim_llm_nodes.npz:", len(res), "arrays")
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--ref", default="/root/reference")
-    ap.add_argument("--only", choices=["hw", "sim", "graph"])
+    ap.add_argument("--only", choices=["hw", "sim", "graph", "llm"])
     ap.add_argument("--out", default=HERE)
     args = ap.parse_args()
     if args.only in (None, "hw"):
@@ -427,6 +516,8 @@ def main():
         make_sim(args.ref, args.out)
     if args.only in (None, "graph"):
         make_graph_goldens(args.ref, args.out)
+    if args.only in (None, "llm"):
+        make_llm_nodes(args.ref, args.out)
 
 
 if __name__ == "__main__":
