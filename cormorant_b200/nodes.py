@@ -36,10 +36,20 @@ class TensorInfo:
     is_state: bool = False
     init_data: Optional[np.ndarray] = field(default=None, repr=False)
     dma: Optional[str] = None  # "i32": an int32 DMA tensor at ``exp`` (the LLM residual stream)
+    host: Optional[str] = None  # "i32": a host-memory int32 input (a position, a row count)
+    # (G, D): a state of logical shape [R][G*D] stored group-major [G][R][D] (a KV
+    # cache, every KV head's rows contiguous); group_kw > 1 is the board's row
+    # interleave of the V cache, which the B200 layout does not need (tensor.py:99-111)
+    group_layout: Optional[tuple] = None
+    group_kw: int = 1
 
     @property
     def numel(self) -> int:
         return int(np.prod(self.shape)) if self.shape else 1
+
+    @property
+    def is_host(self) -> bool:
+        return self.host is not None
 
 
 @dataclass
@@ -261,6 +271,126 @@ class VitGeluVopNode:
     n: int = 1
     F: int = 8
     erf: bool = False
+    onnx_node: object = None
+
+
+@dataclass
+class AttnPrepRoNode:
+    """LlmAttnPrep of a prefill on the row-ops unit (rowops_nodes.py:893-1145):
+    RoPE of q0 / k0 (cos / sin rows of positions pos + t from the ``raw``
+    table, B offset pos 8 HD), v re-rounded to the V cache's exponents, the
+    q.K^T image qx [KV][HD][G T] (TRANSPOSE of 8-row tiles), and the rows
+    [pos, pos + n) of both caches (group-major states, written in place).
+    inputs = [q0, k0, v, pos, (n), ck, cv, qs, ks, (vs), raw, pq, pk, (pvb),
+    pz, tables]; the named fields point into them."""
+    inputs: List[TensorInfo]
+    output: TensorInfo
+    T: int = 1
+    H: int = 1
+    KV: int = 1
+    HD: int = 16
+    C: int = 16
+    Q: int = 16
+    K: int = 1
+    first: bool = False
+    has_n: bool = True
+    v_direct: bool = False
+    pq_bc: bool = False
+    pk_bc: bool = False
+    pv_bc: bool = True
+    fq: Optional[np.ndarray] = field(default=None, repr=False)
+    cos: Optional[np.ndarray] = field(default=None, repr=False)
+    sin: Optional[np.ndarray] = field(default=None, repr=False)
+    q0: Optional[TensorInfo] = field(default=None, repr=False)
+    k0: Optional[TensorInfo] = field(default=None, repr=False)
+    v: Optional[TensorInfo] = field(default=None, repr=False)
+    pos: Optional[TensorInfo] = field(default=None, repr=False)
+    n_t: Optional[TensorInfo] = field(default=None, repr=False)
+    ck: Optional[TensorInfo] = field(default=None, repr=False)
+    cv: Optional[TensorInfo] = field(default=None, repr=False)
+    qs: Optional[TensorInfo] = field(default=None, repr=False)
+    ks: Optional[TensorInfo] = field(default=None, repr=False)
+    vs: Optional[TensorInfo] = field(default=None, repr=False)
+    raw: Optional[TensorInfo] = field(default=None, repr=False)
+    pq: Optional[TensorInfo] = field(default=None, repr=False)
+    pk: Optional[TensorInfo] = field(default=None, repr=False)
+    pvb: Optional[TensorInfo] = field(default=None, repr=False)
+    pz: Optional[TensorInfo] = field(default=None, repr=False)
+    F: int = 8
+    onnx_node: object = None
+
+    @property
+    def G(self) -> int:
+        return self.H // self.KV
+
+
+@dataclass
+class LlmAttnConvNode:
+    """One q.K^T (``kind`` "qk") or P.V ("pv") call of KV group ``group``
+    (llm_nodes.py:1183-1423) over keys = roundup(pos + n, Q) — a runtime
+    count from the host inputs pos / n — or keys = C (``static``; a static
+    q.K^T over the cache rows r0 .. r0 + nr - 1 when nr > 0): raw int16
+    operands, the int32 sum wraps, floor / 2^8, saturated.  inputs = [weight,
+    x, pos, (n)] or [weight, x]."""
+    inputs: List[TensorInfo]
+    output: TensorInfo
+    kind: str = "qk"
+    group: int = 0
+    T: int = 1
+    H: int = 1
+    KV: int = 1
+    HD: int = 16
+    C: int = 16
+    Q: int = 16
+    F: int = 8
+    static: bool = False
+    has_n: bool = True
+    r0: int = 0
+    nr: int = 0
+    onnx_node: object = None
+
+    @property
+    def G(self) -> int:
+        return self.H // self.KV
+
+
+@dataclass
+class LlmAttnSoftmaxVopNode:
+    """The prefill softmax of KV group ``group`` on VectorOP's unit, column
+    mode (smx_nodes.py:284-340): per head h' < G one call over s [C][G T]
+    (columns h' T ..) -> P rows h' T .. over keys = roundup(pos + n, Q), row
+    t valid over j < min(keys, pos + 1 + t) (``causal``), else every row over
+    j < max(min(keys, pos + n) - prefix_lm, 1); registers cm[h'], cfg[h'].
+    inputs = [s, pos, (n)]."""
+    inputs: List[TensorInfo]
+    output: TensorInfo
+    T: int = 1
+    G: int = 1
+    C: int = 16
+    Q: int = 16
+    group: int = 0
+    has_n: bool = True
+    causal: bool = True
+    prefix_lm: bool = False
+    cm: List[int] = field(default_factory=list)
+    cfg: List[int] = field(default_factory=list)
+    F: int = 8
+    onnx_node: object = None
+
+
+@dataclass
+class LlmAttnMergeNode:
+    """The P.V outputs o_g [G T][HD] (raw) -> pv [T][H HD] in head order,
+    pv[t][(g G + h') HD + d] = o_g[h' T + t][d], a raw copy
+    (llm_nodes.py:1560-1660); R row splits with G = 1."""
+    inputs: List[TensorInfo]
+    output: TensorInfo
+    T: int = 1
+    H: int = 1
+    KV: int = 1
+    HD: int = 16
+    R: int = 1
+    F: int = 8
     onnx_node: object = None
 
 

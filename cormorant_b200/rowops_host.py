@@ -137,6 +137,48 @@ def silu_mul_job(fg, fu, fa, n: int):
     return pblock(0, 0, G_BITS - fg, 0, SILU_BITS + fu - fa, n)
 
 
+ROPE_BITS = 23
+
+
+def rope_table_words(cos: np.ndarray, sin: np.ndarray) -> np.ndarray:
+    """The cos / sin table a ROPE job streams as B (rowops_nodes.py:705-725):
+    one row per position of 2 HD int32 — cos then sin, each float32 [C][HD/2]
+    table repeated over both halves, as int24 rint(v 2^23) — as int16 words
+    (little-endian halves)."""
+    cos = np.asarray(cos, np.float32).astype(np.float64)
+    sin = np.asarray(sin, np.float32).astype(np.float64)
+    cr = np.rint(np.concatenate([cos, cos], axis=1) * 2.0 ** ROPE_BITS).astype(np.int64)
+    sr = np.rint(np.concatenate([sin, sin], axis=1) * 2.0 ** ROPE_BITS).astype(np.int64)
+    rows = np.ascontiguousarray(np.concatenate([cr, sr], axis=1).astype(np.int32))
+    return rows.reshape(-1).view(np.int16).astype(np.int64)
+
+
+def rope_params(fx, nh: int, HD: int, f_out):
+    """(sa, sb, sc) per column of a ROPE job over nh heads of HD at the input's
+    per-channel exponents fx [nh HD] to f_out (per head or per channel): both
+    products brought to the finer exponent of the rotation pair, then one
+    rounding by fp + 23 - f_out (rowops_nodes.py:1190-1200)."""
+    fx = np.asarray(fx, np.int64).reshape(nh, HD)
+    half = HD // 2
+    frot = np.concatenate([fx[:, half:], fx[:, :half]], axis=1)
+    fp = np.maximum(fx, frot)
+    fo = np.broadcast_to(np.asarray(f_out, np.int64).reshape(nh, -1), (nh, HD))
+    sa, sb, sc = fp - fx, fp - frot, fp + ROPE_BITS - fo
+    if (sa > 63).any() or (sb > 63).any() or (sc < 0).any() or (sc > 63).any():
+        raise ValueError("rope_params: exponents beyond the unit's shifts")
+    return sa.reshape(-1), sb.reshape(-1), sc.reshape(-1)
+
+
+def vround_params(fv, fvc):
+    """(sa, sc) of the COPY that re-rounds v (fv) to the V cache's exponents
+    fvc: up by fvc - fv or down (RNE) by fv - fvc (rowops_nodes.py:1211-1216)."""
+    fv, fvc = np.asarray(fv, np.int64), np.asarray(fvc, np.int64)
+    sa, sc = np.maximum(fvc - fv, 0), np.maximum(fv - fvc, 0)
+    if (sa > 63).any() or (sc > 63).any():
+        raise ValueError("vround_params: exponents beyond the unit's shifts")
+    return sa, sc
+
+
 def collapse(dims, sstr):
     """Merge output dims adjacent in the source, drop size-1 dims
     (host_nodes.py:129-148, without the 5-dim padding)."""

@@ -209,26 +209,97 @@ class GpuSimulator:
     def forward_pass(self, input_arrays: Dict[str, np.ndarray], states=None,
                      keep: Optional[Iterable[str]] = None) -> Dict[str, np.ndarray]:
         """_simulate.py:541-769 on the device; returns float64 values of every
-        tensor visited (or only ``keep``)."""
+        tensor visited (or only ``keep``, plus the states).  ``states``
+        ({name: float64 logical array}) are updated IN PLACE, as the
+        reference's are; None: fresh copies of the initial values."""
         tmap = {t.onnx_name: t for t in self._graph.input_tensors}
-        raw_in = {name: self._to_raw(tmap[name], v) for name, v in input_arrays.items()}
-        raw, meta = self.forward_raw(raw_in, keep=keep)
+        raw_in = {}
+        for name, v in input_arrays.items():
+            t = tmap[name]
+            if getattr(t, "host", None) is not None:   # a host int (pos, n): stays on the host
+                if t.host != "i32":
+                    raise NotImplementedError(f"GpuSimulator: host tensor kind {t.host}")
+                raw_in[name] = np.asarray(v).astype(np.int64).reshape(-1)
+            else:
+                raw_in[name] = self._to_raw(t, v)
+        dev_states = self.states_to_device(states)
+        raw, meta = self.forward_raw(raw_in, keep=keep, states=dev_states)
         names = set(keep) if keep is not None else set(raw)
         out = {}
         for name in names:
-            if name not in raw:
+            if name not in raw or name in dev_states:
                 continue
             t = meta[name]
+            if isinstance(raw[name], np.ndarray):
+                out[name] = raw[name].astype(np.float64).reshape(t.shape)
+                continue
             v = raw[name][:t.numel].cpu().numpy().astype(np.float64).reshape(t.shape)
             out[name] = v / np.power(2.0, _exp_of(t))
+        for t in self._graph.state_tensors:
+            vals = self.state_values(t, dev_states[t.onnx_name])
+            if states is not None:
+                states[t.onnx_name][...] = vals.reshape(np.shape(states[t.onnx_name]))
+            out[t.onnx_name] = vals
         return out
 
-    def forward_raw(self, raw_inputs: Dict[str, torch.Tensor], keep: Optional[Iterable[str]] = None):
+    # ------------------------------------------------------------ states
+    def initial_states(self) -> Dict[str, np.ndarray]:
+        """_simulate.py:775-782: fresh float64 copies of every state's initial value."""
+        return {t.onnx_name: (np.zeros(t.shape) if getattr(t, "init_data", None) is None
+                              else np.array(t.init_data, np.float64).reshape(t.shape))
+                for t in self._graph.state_tensors}
+
+    @staticmethod
+    def _group_major(t, raw: np.ndarray, to_device: bool) -> np.ndarray:
+        """A group-major state (group_layout (G, D)): logical [R][G D] <->
+        storage [G][R][D]."""
+        gl = getattr(t, "group_layout", None)
+        if not gl:
+            return raw
+        G, D = int(gl[0]), int(gl[1])
+        R = t.numel // (G * D)
+        if to_device:
+            return np.ascontiguousarray(raw.reshape(R, G, D).transpose(1, 0, 2))
+        return np.ascontiguousarray(raw.reshape(G, R, D).transpose(1, 0, 2)).reshape(t.shape)
+
+    def states_to_device(self, states=None) -> Dict[str, torch.Tensor]:
+        """The states' storage integers on the device ({name: buffer}; a KV
+        cache group-major), from value arrays (default: the initial values)."""
+        vals = self.initial_states() if states is None else states
+        out = {}
+        for t in self._graph.state_tensors:
+            f = _exp_of(t)
+            v = np.round(np.asarray(vals[t.onnx_name], np.float64).reshape(t.shape) * np.power(2.0, f))
+            if getattr(t, "dma", None) == "i32":
+                raw = np.clip(v, -2147483648.0, 2147483647.0).astype(np.int32)
+                buf = self._alloc32(t.numel)
+            else:
+                raw = np.clip(v, -32768, 32767).astype(np.int16)
+                buf = self._alloc(t.numel)
+            buf[:t.numel].copy_(torch.from_numpy(self._group_major(t, raw, True).reshape(-1)))
+            out[t.onnx_name] = buf
+        return out
+
+    def state_values(self, t, buf: torch.Tensor) -> np.ndarray:
+        """A device state back as its logical float64 values."""
+        raw = buf[:t.numel].cpu().numpy().astype(np.float64)
+        raw = self._group_major(t, raw, False).reshape(t.shape)
+        return raw / np.power(2.0, _exp_of(t))
+
+    def forward_raw(self, raw_inputs: Dict[str, torch.Tensor], keep: Optional[Iterable[str]] = None,
+                    states: Optional[Dict[str, torch.Tensor]] = None):
         """The pass on int16 device tensors (no host conversion): returns
         ({name: raw tensor}, {name: TensorInfo}).  With ``keep`` (the lean
         mode of _simulate.py:573-592) every other tensor is released after its
-        last reader, so the allocator reuses its memory."""
+        last reader, so the allocator reuses its memory.  ``states``: the
+        device states (``states_to_device``), updated in place; host int
+        inputs (pos, n) are numpy arrays."""
         raw: Dict[str, torch.Tensor] = dict(raw_inputs)
+        snames = {t.onnx_name for t in self._graph.state_tensors}
+        if snames:
+            if states is None:
+                states = self.states_to_device()
+            raw.update({k: states[k] for k in snames})
         dying: Dict[int, list] = {}
         if keep is not None:
             keep = set(keep)
@@ -240,9 +311,10 @@ class GpuSimulator:
                 last.setdefault(sn.output.onnx_name, i)
             wnames = {t.onnx_name for t in self._graph.weight_tensors}
             for name, i in last.items():
-                if name not in keep and name not in wnames:
+                if name not in keep and name not in wnames and name not in snames:
                     dying.setdefault(i, []).append(name)
         meta = {t.onnx_name: t for t in self._graph.input_tensors}
+        meta.update({t.onnx_name: t for t in self._graph.state_tensors})
         for t in self._graph.weight_tensors:
             if getattr(t, "data", None) is not None:
                 meta[t.onnx_name] = t
@@ -296,6 +368,14 @@ class GpuSimulator:
                 y = self._llm_rowops(sn, kind, get)
             elif kind == "VitGeluVopNode":
                 y = self._vit_gelu(sn, get)
+            elif kind == "AttnPrepRoNode":
+                y = self._attn_prep(sn, get)
+            elif kind == "LlmAttnConvNode":
+                y = self._attn_conv(sn, get)
+            elif kind == "LlmAttnSoftmaxVopNode":
+                y = self._attn_softmax(sn, get)
+            elif kind == "LlmAttnMergeNode":
+                y = self._attn_merge(sn, get)
             else:
                 raise NotImplementedError(f"GpuSimulator: no sm_100a kernel for node type {kind}")
             if alias_t is not None:  # the fused intermediate is not materialised
@@ -450,6 +530,144 @@ class GpuSimulator:
         geo = dict(size=sn.n, outer=sn.rows, a_inc=sn.n, b_inc=0)
         ops.vectorop(get(sn.inputs[0]), get(sn.inputs[1]), y, op=0, act=0, **geo)
         ops.vectorop(y, get(sn.inputs[2]), y, op=2, act=5 if getattr(sn, "erf", False) else 6, **geo)
+        return y
+
+    # ------------------------------------------------------------ prefill attention
+    def _zero_p(self) -> torch.Tensor:
+        """One all-zero P_BCAST parameter entry (rowops_nodes.py:746-751)."""
+        if "__zero_p" not in self._weights:
+            self._weights["__zero_p"] = torch.zeros(16, dtype=torch.int16, device=self.device)
+        return self._weights["__zero_p"]
+
+    @staticmethod
+    def _host_int(get, t) -> int:
+        return int(np.asarray(get(t)).reshape(-1)[0])
+
+    def _keys(self, sn, get, i_pos: int):
+        """(n, keys) of a runtime key count from the host inputs pos / n
+        (llm_nodes.py:1409-1410; the C run function's llm_keys)."""
+        from .attention import attn_keys
+        pos = self._host_int(get, sn.inputs[i_pos])
+        n = self._host_int(get, sn.inputs[i_pos + 1]) if sn.has_n else sn.T
+        return (pos,) + attn_keys(pos, n, sn.T, sn.C, sn.Q)
+
+    def _attn_prep(self, sn, get):
+        """AttnPrepRoNode's jobs (rowops_nodes.py:985-1037): ROPE q0 -> qs and
+        k0 -> ks over the rows t < n (the cos / sin rows of pos + t), v
+        re-rounded -> vs, the q image per KV group (8-row TRANSPOSE tiles; a
+        decode step's one row: the group's heads as one tile), and COPYs of
+        ks / v(s) into the cache rows [pos, pos + n) of the group-major
+        states, in place.  The staging rows are this pass's own, zeroed, so
+        the image's columns t >= n are 0."""
+        from . import rowops_host as RH
+        from .attention import attn_keys
+        if int(getattr(sn, "F", 8)) != 8:
+            raise NotImplementedError("AttnPrepRoNode: F != 8")
+        T, H, KV, HD, C = sn.T, sn.H, sn.KV, sn.HD, sn.C
+        G = H // KV
+        nq, nk = H * HD, KV * HD
+        pos = self._host_int(get, sn.pos)
+        n, _keys = attn_keys(pos, self._host_int(get, sn.n_t) if sn.has_n else T, T, C, sn.Q)
+        qx = self._alloc(sn.output.numel)
+        qs = self._alloc(T * nq)
+        qs.zero_()
+        NW = RH.NO_WINDOW
+        if n > 0:
+            ks = self._alloc(T * nk)
+            tab = get(sn.raw)
+            I16, I32 = RH.K_I16, RH.K_I32
+            rope = RH.opword(RH.OP_ROPE, I16, I32, I16, b_en=True)
+            ops.rowops(get(sn.q0), tab, qs, get(sn.pq), op=rope | (RH.F_P_BCAST if sn.pq_bc else 0), n=nq, rows=n,
+                       a_s1=2 * nq, b_s1=8 * HD, c_s1=2 * nq, aux=HD, b_off=pos * 8 * HD, win_hi=NW)
+            ops.rowops(get(sn.k0), tab, ks, get(sn.pk), op=rope | (RH.F_P_BCAST if sn.pk_bc else 0), n=nk, rows=n,
+                       a_s1=2 * nk, b_s1=8 * HD, c_s1=2 * nk, aux=HD, b_off=pos * 8 * HD, win_hi=NW)
+            vsrc = get(sn.v)
+            if not sn.v_direct:
+                vs = self._alloc(T * nk)
+                ops.rowops(vsrc, None, vs, get(sn.pvb), op=RH.opword(RH.OP_COPY, p_bcast=bool(sn.pv_bc)), n=nk,
+                           rows=n, a_s1=2 * nk, c_s1=2 * nk, win_hi=NW)
+                vsrc = vs
+            zp, cp = self._zero_p(), RH.opword(RH.OP_COPY, p_bcast=True)
+            for src, cache in ((ks, get(sn.ck)), (vsrc, get(sn.cv))):
+                ops.rowops(src, None, cache, zp, op=cp, n=HD, rows=n, blocks=KV, a_s1=2 * nk, a_s2=2 * HD,
+                           c_s1=2 * HD, c_s2=2 * C * HD, c_off=pos * HD * 2, win_hi=NW)
+        xp = RH.opword(RH.OP_XPOSE)
+        if T == 1:
+            ops.rowops(qs, None, qx, None, op=xp, n=HD, rows=1, blocks=KV, a_s2=2 * G * HD, b_s1=2 * HD, b_s2=2 * G,
+                       c_s2=2 * HD * G, aux=G, win_hi=NW)
+        else:
+            if T % RH.QIMAGE_R:
+                raise NotImplementedError(f"AttnPrepRoNode: {T} rows (the q image's tiles take multiples of 8)")
+            for g in range(KV):
+                ops.rowops(qs, None, qx, None, op=xp, n=HD, rows=T // RH.QIMAGE_R, blocks=G,
+                           a_s1=RH.QIMAGE_R * 2 * nq, a_s2=2 * HD, b_s1=2 * nq, b_s2=2 * G * T, c_s1=2 * RH.QIMAGE_R,
+                           c_s2=2 * T, aux=RH.QIMAGE_R, a_off=g * G * HD * 2, c_off=g * HD * G * T * 2, win_hi=NW)
+        return qx
+
+    def _attn_conv(self, sn, get):
+        """q.K^T: the K cache rows [r0, r0 + keys) of group g (contiguous,
+        group-major) @ the group's q image [HD][G T], rows keys .. C of the
+        scores 0; P.V: P [G T][keys] (its rows compacted from stride C when
+        keys < C, one row-ops COPY) @ the V cache rows [0, keys) of group g.
+        One MatMul job each with the int32 wrap (llm_nodes.py:1407-1423)."""
+        if int(getattr(sn, "F", 8)) != 8:
+            raise NotImplementedError("LlmAttnConvNode: F != 8")
+        T, HD, C, g = sn.T, sn.HD, sn.C, sn.group
+        GT = (sn.H // sn.KV) * T
+        keys = C if sn.static else self._keys(sn, get, 2)[2]
+        w, x = get(sn.inputs[0]), get(sn.inputs[1])
+        y = self._alloc(sn.output.numel)
+        if sn.kind == "qk":
+            rows, r0 = (sn.nr, sn.r0) if sn.nr else (keys, 0)
+            ws = self._workspace(self._mm_ws(rows, HD, GT, 1, 0, 0))
+            ops.matmul(w[(g * C + r0) * HD:], x[g * HD * GT:], y, n=rows, k=HD, m=GT, flags=F_WRAP32, workspace=ws)
+            if not sn.nr and keys < C:
+                y[keys * GT:C * GT].zero_()
+            return y
+        a = w
+        if keys < C:
+            from . import rowops_host as RH
+            a = self._alloc(GT * keys)
+            ops.rowops(w, None, a, self._zero_p(), op=RH.opword(RH.OP_COPY, p_bcast=True), n=keys, rows=GT,
+                       a_s1=2 * C, c_s1=2 * keys, win_hi=RH.NO_WINDOW)
+        ws = self._workspace(self._mm_ws(GT, keys, HD, 1, 0, 0))
+        ops.matmul(a, x[g * C * HD:], y, n=GT, k=keys, m=HD, flags=F_WRAP32, workspace=ws)
+        return y
+
+    def _attn_softmax(self, sn, get):
+        """G column-mode softmax calls (smx_nodes.py:362-383): head h' reads
+        the columns h' T .. of s [C][G T] (a_inc G T) and writes P rows h' T ..
+        at stride C over the first keys columns (the rest 0); the mask
+        register: valid0 = pos + 1, period T (causal), else one valid length."""
+        T, G, C = sn.T, sn.G, sn.C
+        pos, n, keys = self._keys(sn, get, 1)
+        if sn.causal:
+            mask = ((pos + 1) & 0xFFFF) | (T << 16)
+        else:
+            mask = max(min(keys, pos + n) - int(bool(sn.prefix_lm)), 1) & 0xFFFF
+        s = get(sn.inputs[0])
+        y = self._alloc(sn.output.numel)
+        if keys < C:
+            y.zero_()
+        for h in range(G):
+            ops.vectorop(s[h * T:], None, y[h * T * C:], size=keys, op=11, outer=T, a_inc=G * T, b_inc=C,
+                         smx_cm=int(sn.cm[h]), smx_cfg=int(sn.cfg[h]), smx_mask=mask)
+        return y
+
+    def _attn_merge(self, sn, get):
+        """o_g -> pv in head order (llm_nodes.py:1645-1660): per input one
+        row-ops COPY of its heads' rows (rows t, blocks h') to their columns."""
+        from . import rowops_host as RH
+        T, H, KV, HD = sn.T, sn.H, sn.KV, sn.HD
+        R = int(getattr(sn, "R", 1))
+        G = H // KV
+        rows = T // R
+        y = self._alloc(sn.output.numel)
+        zp, cp = self._zero_p(), RH.opword(RH.OP_COPY, p_bcast=True)
+        for i, t in enumerate(sn.inputs):
+            g, r = divmod(i, R)
+            ops.rowops(get(t), None, y, zp, op=cp, n=HD, rows=rows, blocks=G, a_s1=2 * HD, a_s2=2 * HD * rows,
+                       c_s1=2 * H * HD, c_s2=2 * HD, c_off=2 * (r * rows * H * HD + g * G * HD), win_hi=RH.NO_WINDOW)
         return y
 
     def _tiled_weight(self, t, size: int) -> torch.Tensor:

@@ -504,10 +504,166 @@ def make_llm_nodes(ref, out):
     print("sim_llm_nodes.npz:", len(res), "arrays")
 
 
+class _Attr:
+    def __init__(self, name, value):
+        self.name, self.value = name, value
+
+
+class _Node:
+    """What the reference's node factories read of an onnx NodeProto."""
+    def __init__(self, op_type, inputs, outputs, name="", **attrs):
+        self.op_type, self.input, self.output, self.name = op_type, list(inputs), list(outputs), name
+        self.attribute = [_Attr(k, v) for k, v in attrs.items()]
+
+
+def make_llm_attn(ref, out):
+    """The prefill attention chain of one layer on the kernels, as the
+    reference's node factories build it from LlmAttnPrep (rowops = 1) /
+    LlmAttnScores / LlmAttnSoftmax (vsmx = 1) / LlmAttnPV / LlmAttnMerge
+    nodes (rowops_nodes.py:1146-1234, llm_nodes.py:1253-1310, 1457-1491,
+    1618-1636) — AttnPrepRoNode, LlmAttnConvNode, LlmAttnSoftmaxVopNode,
+    LlmAttnMergeNode — run through the reference's _forward_pass over seeded
+    K / V caches.  Cases: a prefill at pos > 0 (runtime keys), one from pos
+    0 with n = T, a non-causal softmax, and the static q.K^T row pieces /
+    P.V of an encoder.  Saved: every input, state and output as raw
+    integers, and the registers the factories derived."""
+    sim = _import_reference(ref)
+    import onnx.helper
+    onnx.helper.get_attribute_value = lambda a: a.value
+    from src.dtype import AP_FIXED_16_8 as D
+    from src.tensor import TensorInfo as TI
+    from src import _rowops_hw_config, _vectorop_hw_config
+    from src import llm_nodes as LN, rowops_nodes as RON
+    from src.host_nodes import HostContext
+    _rowops_hw_config.ROWOPS_UNIT = True
+    _vectorop_hw_config.VECTOROP_SOFTMAX = True
+    rng = np.random.default_rng(43)
+    res = {}
+    T, H, KV, HD, C = 32, 6, 2, 64, 128
+    G = H // KV
+
+    def ten(name, shape, exp=None, **kw):
+        return TI(onnx_name=name, shape=list(shape), dtype="float32",
+                  exp=None if exp is None else np.asarray(exp, np.int64), **kw)
+
+    # exponents: q0 / k0 per channel (the rotation pairs at different ones), the
+    # caches one per KV head (K) / per channel (V), v per channel
+    fq0 = rng.integers(9, 13, H * HD)
+    fk0 = rng.integers(9, 13, KV * HD)
+    fv = rng.integers(9, 13, KV * HD)
+    fq = rng.integers(10, 13, H)
+    fkc = np.repeat(rng.integers(10, 13, KV), HD)
+    fvc = rng.integers(9, 13, KV * HD)
+    fs = fq + fkc[::HD][np.arange(H) // G] - 8
+    fp = rng.integers(12, 15, H)
+    fpv = np.repeat(fp, HD) + np.tile(fvc.reshape(KV, HD), (1, G)).reshape(-1)[:H * HD] - 8
+    ang = np.outer(np.arange(C), 1.0 / (10000.0 ** (np.arange(HD // 2) * 2.0 / HD)))
+    cos, sin = np.cos(ang).astype(np.float32), np.sin(ang).astype(np.float32)
+    res.update(fq0=fq0, fk0=fk0, fv=fv, fq=fq, fkc=fkc, fvc=fvc, fs=fs, fp=fp, fpv=fpv, cos=cos, sin=sin)
+
+    def chain(tag, pos, n, causal=1):
+        tens = {}
+        q0, k0, v = ten("q0", (T, H * HD), fq0), ten("k0", (T, KV * HD), fk0), ten("v", (T, KV * HD), fv)
+        post, nt = ten("pos", (1,), host="i32"), ten("n", (1,), host="i32")
+        ck = ten("ck", (C, KV * HD), fkc, is_state=True, group_layout=(KV, HD))
+        cv = ten("cv", (C, KV * HD), fvc, is_state=True, group_layout=(KV, HD))
+        qs, ks = ten("qs", (T, H * HD), 0, is_state=True), ten("ks", (T, KV * HD), 0, is_state=True)
+        vs = ten("vs", (T, KV * HD), 0, is_state=True)
+        qx = ten("qx", (KV, HD, G * T), 0)
+        for t in (q0, k0, v, post, nt, ck, cv, qs, ks, vs, qx):
+            tens[t.onnx_name] = t
+        tens["cos"], tens["sin"] = ten("cos", cos.shape, data=cos), ten("sin", sin.shape, data=sin)
+        ctx = HostContext(opset=17, consts={"cos": cos, "sin": sin}, frac_bits=8)
+        common = dict(num_heads=H, num_kv_heads=KV, head_dim=HD, key_quantum=16)
+        nodes = [RON.from_llm_attn_prep(
+            _Node("LlmAttnPrep", ["q0", "k0", "v", "pos", "n", "ck", "cv", "cos", "sin", "qs", "ks", "vs"], ["qx"],
+                  qk_kw=1, q_exp=[int(x) for x in fq], rowops=1, first=1, **common), tens, 0, 8, ctx)]
+        for g in range(KV):
+            for nm, shp in ((f"s{g}", (C, G * T)), (f"p{g}", (G * T, C)), (f"o{g}", (G * T, HD))):
+                tens[nm] = ten(nm, shp, 0)
+            nodes.append(LN.LlmAttnConvNode.from_onnx_node(
+                _Node("LlmAttnScores", ["ck", "qx", "pos", "n"], [f"s{g}"], group=g, qk_kw=1, **common), tens, 0, 8,
+                ctx))
+            hs = slice(g * G, (g + 1) * G)
+            nodes.append(LN.LlmAttnSoftmaxNode.from_onnx_node(
+                _Node("LlmAttnSoftmax", [f"s{g}", "pos", "n"], [f"p{g}"], group=g, s_exp=[int(x) for x in fs[hs]],
+                      p_exp=[int(x) for x in fp[hs]], vsmx=1, causal=causal, **common), tens, 0, 8, ctx))
+            nodes.append(LN.LlmAttnConvNode.from_onnx_node(
+                _Node("LlmAttnPV", [f"p{g}", "cv", "pos", "n"], [f"o{g}"], group=g, **common), tens, 0, 8, ctx))
+        tens["pv"] = ten("pv", (T, H * HD), fpv)
+        nodes.append(LN.LlmAttnMergeNode.from_onnx_node(
+            _Node("LlmAttnMerge", [f"o{g}" for g in range(KV)], ["pv"], **common), tens, 0, 8, ctx))
+        wts = list({t.onnx_name: t for nd in nodes for t in nd.inputs if t is not None and t.data is not None}.values())
+        g_ = _Graph(nodes, wts, [q0, k0, v, post, nt], [tens["pv"]])
+        g_.state_tensors = [ck, cv, qs, ks, vs]
+        q0r = rng.integers(-700, 700, (T, H * HD))
+        k0r = rng.integers(-700, 700, (T, KV * HD))
+        vr = rng.integers(-1500, 1500, (T, KV * HD))
+        ckr = rng.integers(-700, 700, (C, KV * HD))
+        cvr = rng.integers(-1500, 1500, (C, KV * HD))
+        p2 = lambda e: np.power(2.0, np.asarray(e, np.float64))[None, :]  # noqa: E731
+        states = {"ck": ckr / p2(fkc), "cv": cvr / p2(fvc), "qs": np.zeros((T, H * HD)),
+                  "ks": np.zeros((T, KV * HD)), "vs": np.zeros((T, KV * HD))}
+        feeds = {"q0": q0r / p2(fq0), "k0": k0r / p2(fk0), "v": vr / p2(fv), "pos": np.array([pos], np.int32),
+                 "n": np.array([n], np.int32)}
+        arr = _shim(sim, D, g_)._forward_pass(feeds, states=states)
+        r = lambda a, e=0: np.rint(np.asarray(a, np.float64) * (p2(e) if np.ndim(e) else 2.0 ** e)).astype(np.int64)  # noqa: E731
+        res.update({f"{tag}_q0": q0r, f"{tag}_k0": k0r, f"{tag}_v": vr, f"{tag}_ck0": ckr, f"{tag}_cv0": cvr,
+                    f"{tag}_posn": np.array([pos, n]), f"{tag}_qx": r(arr["qx"]).reshape(KV, HD, G * T),
+                    f"{tag}_ck": r(states["ck"], fkc), f"{tag}_cv": r(states["cv"], fvc),
+                    f"{tag}_pv": r(arr["pv"], fpv)})
+        for g in range(KV):
+            res.update({f"{tag}_s{g}": r(arr[f"s{g}"]), f"{tag}_p{g}": r(arr[f"p{g}"]), f"{tag}_o{g}": r(arr[f"o{g}"])})
+        if tag == "a":
+            prep, smx = nodes[0], nodes[2]
+            for nm in ("pq", "pk", "pvb"):
+                t = getattr(prep, nm)
+                res[f"w_{nm}"] = np.rint(np.asarray(t.data, np.float64) * 256).astype(np.int64)
+            res["w_bc"] = np.array([prep.pq_bc, prep.pk_bc, prep.pv_bc, prep.v_direct], np.int64)
+            res["w_rope_crc"] = np.array([zlib.crc32(np.rint(np.asarray(prep.raw.data, np.float64) * 256)
+                                                     .astype("<i2").tobytes())], np.int64)
+            res["w_smx"] = np.array([[nd.cm[h], nd.cfg[h]] for nd in nodes[2::3][:KV] for h in range(G)], np.int64)
+            res["w_keys"] = np.array([nd_.C for nd_ in nodes[1:2]], np.int64)
+        print(f"attn {tag}: pos {pos} n {n} keys {LN.attn_keys(pos, n, T, C)[1]}")
+
+    chain("a", 40, 27)          # a prefill at pos 40: keys = roundup(67, 16) = 80
+    chain("b", 0, T)            # from pos 0, every row valid: keys 32
+    chain("c", 60, 20, causal=0)  # an encoder's rows: every row over keys < pos + n
+    chain("d", 120, 32)         # n clamped at the cache end: keys = C
+
+    # static q.K^T row pieces and a static P.V (an encoder's attention, keys = C)
+    tens = {}
+    ctx = HostContext(opset=17, consts={}, frac_bits=8)
+    common = dict(num_heads=H, num_kv_heads=KV, head_dim=HD, key_quantum=16)
+    ck = ten("ck", (C, KV * HD), fkc, is_state=True, group_layout=(KV, HD))
+    cv = ten("cv", (C, KV * HD), fvc, is_state=True, group_layout=(KV, HD))
+    qx = ten("qx", (KV, HD, G * T), 0)
+    for t in (ck, cv, qx):
+        tens[t.onnx_name] = t
+    tens["sr"], tens["ps"], tens["os"] = ten("sr", (48, G * T), 0), ten("ps", (G * T, C), 0), ten("os", (G * T, HD), 0)
+    n1 = LN.LlmAttnConvNode.from_onnx_node(_Node("LlmAttnScores", ["ck", "qx"], ["sr"], group=1, rows=[16, 48],
+                                                 **common), tens, 0, 8, ctx)
+    n2 = LN.LlmAttnConvNode.from_onnx_node(_Node("LlmAttnPV", ["ps", "cv"], ["os"], group=0, **common), tens, 0, 8, ctx)
+    g_ = _Graph([n1, n2], [], [qx, tens["ps"]], [tens["sr"], tens["os"]])
+    g_.state_tensors = [ck, cv]
+    # full-range operands: sums beyond int32 (the wrap) as well as saturated outputs
+    ckr = rng.integers(-32768, 32768, (C, KV * HD)) >> rng.integers(0, 6, (C, 1))
+    cvr = rng.integers(-32768, 32768, (C, KV * HD)) >> rng.integers(0, 6, (C, 1))
+    qxr = rng.integers(-32768, 32768, (KV, HD, G * T)) >> rng.integers(0, 6, (1, 1, G * T))
+    psr = rng.integers(0, 32768, (G * T, C)) >> rng.integers(0, 8, (G * T, 1))
+    p2 = lambda e: np.power(2.0, np.asarray(e, np.float64))[None, :]  # noqa: E731
+    states = {"ck": ckr / p2(fkc), "cv": cvr / p2(fvc)}
+    arr = _shim(sim, D, g_)._forward_pass({"qx": qxr.astype(np.float64), "ps": psr.astype(np.float64)}, states=states)
+    res.update(st_ck=ckr, st_cv=cvr, st_qx=qxr, st_ps=psr, st_sr=np.rint(arr["sr"]).astype(np.int64),
+               st_os=np.rint(arr["os"]).astype(np.int64))
+    np.savez_compressed(os.path.join(out, "sim_llm_attn.npz"), **res)
+    print("sim_llm_attn.npz:", len(res), "arrays")
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--ref", default="/root/reference")
-    ap.add_argument("--only", choices=["hw", "sim", "graph", "llm"])
+    ap.add_argument("--only", choices=["hw", "sim", "graph", "llm", "attn"])
     ap.add_argument("--out", default=HERE)
     args = ap.parse_args()
     if args.only in (None, "hw"):
@@ -518,6 +674,8 @@ def main():
         make_graph_goldens(args.ref, args.out)
     if args.only in (None, "llm"):
         make_llm_nodes(args.ref, args.out)
+    if args.only in (None, "attn"):
+        make_llm_attn(args.ref, args.out)
 
 
 if __name__ == "__main__":
