@@ -450,27 +450,34 @@ def bench_models(torch, dev, stream, flush, args, world, rank, pg):
     int16 inputs, replayed as CUDA graphs; images/s or tokens/s over all
     ranks, int16 GMAC/s.  On rank 0 at N = 1 the CPU oracle's forward pass of
     one image / one sequence is timed beside it."""
+    import numpy as np
+
     from cormorant_b200 import workloads as WL
     from cormorant_b200.simulator import GpuSimulator
     out = {}
     cases = [("mnist_b1", "images", lambda b: WL.mnist(seed=1, batch=b), 1),
              ("mnist_b4096", "images", lambda b: WL.mnist(seed=1, batch=b), 4096),
              ("mobilenet_v2_224", "images", lambda b: WL.mobilenet_v2(seed=3, batch=b, res=224), max(1, 256 // world)),
-             ("bert_base_384", "tokens", lambda b: WL.bert_base(seed=4, batch=b, seq=384), max(1, 64 // world))]
+             ("bert_base_384", "tokens", lambda b: WL.bert_base(seed=4, batch=b, seq=384), max(1, 64 // world)),
+             ("llama360m_prefill512", "tokens", lambda b: WL.llama_prefill(seed=5, batch=b, seq=512),
+              max(1, 64 // world))]
+    seq_of = {"bert_base_384": 384, "llama360m_prefill512": 512}
     for name, unit, build, batch in cases:
         if args.models and name not in args.models.split(","):
             continue
         g, feeds, macs_unit = build(batch)
-        units = batch * (384 if unit == "tokens" else 1)
+        units = batch * seq_of.get(name, 1)
         sim = GpuSimulator(g, device=dev)
         keep = [t.onnx_name for t in g.output_tensors]
         with torch.cuda.stream(stream):
-            raw = {"x": sim._to_raw(g.input_tensors[0], feeds["x"])}
-            sim.forward_raw(raw, keep=keep)  # weights uploaded, workspaces sized
+            raw = {t.onnx_name: (np.asarray(feeds[t.onnx_name]).astype(np.int64).reshape(-1) if t.host
+                                 else sim._to_raw(t, feeds[t.onnx_name])) for t in g.input_tensors}
+            dev_states = sim.states_to_device() if g.state_tensors else None
+            sim.forward_raw(raw, keep=keep, states=dev_states)  # weights uploaded, workspaces sized
         torch.cuda.synchronize()
         graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(graph, stream=stream):
-            res, _ = sim.forward_raw(raw, keep=keep)
+            res, _ = sim.forward_raw(raw, keep=keep, states=dev_states)
         ms = _time_graph(torch, stream, flush, graph, args)
         if pg:
             t = torch.tensor([ms], dtype=torch.float64, device=dev)
@@ -485,22 +492,33 @@ def bench_models(torch, dev, stream, flush, args, world, rank, pg):
             ops.profile_read()
             ops.profile_enable(True)
             with torch.cuda.stream(stream):
-                sim.forward_raw(raw, keep=keep)
+                sim.forward_raw(raw, keep=keep, states=dev_states)
             ops.profile_enable(False)
             prof = ops.profile_read()
             out[name]["kernels"] = {k: {"launches": v[0], "ms": round(v[1], 4)}
                                     for k, v in sorted(prof.items(), key=lambda kv: -kv[1][1])}
-        del graph, res, sim, raw
+        del graph, res, sim, raw, dev_states
         torch.cuda.empty_cache()
-        if rank == 0 and world == 1 and not args.no_cpu and name != "mnist_b4096":
-            import numpy as np
-
+        if rank == 0 and world == 1 and not args.no_cpu and name.startswith("llama"):
+            # the CPU oracle on one layer of one 64-token sequence, scaled to the
+            # full depth (extrapolated: the per-token work of a layer at 64 keys)
+            from oracle import llm
+            g1, f1, _ = WL.llama_prefill(seed=5, batch=1, seq=64, layers=1, vocab=1000)
+            tm = {t.onnx_name: t for t in g1.input_tensors}
+            r1 = {k: (np.asarray(v) if tm[k].host else np.rint(np.asarray(v) * 2.0 ** float(tm[k].exp)).astype(np.int64))
+                  for k, v in f1.items()}
+            t0 = time.perf_counter()
+            llm.forward(g1, r1, {t.onnx_name: np.zeros(t.shape, np.int64) for t in g1.state_tensors})
+            el = (time.perf_counter() - t0) * 32
+            out[name]["cpu_oracle_tokens_per_s"] = round(64 / el, 4)
+            out[name]["cpu_oracle_sample"] = "1 layer x 64 tokens, x32 layers (extrapolated)"
+        elif rank == 0 and world == 1 and not args.no_cpu and name != "mnist_b4096":
             from oracle import graph as og
             g1, f1, _ = build(1)
             t0 = time.perf_counter()
             og.forward(g1, {k: np.asarray(v) for k, v in f1.items()})
             el = time.perf_counter() - t0
-            out[name][f"cpu_oracle_{unit}_per_s"] = round((384 if unit == "tokens" else 1) / el, 3)
+            out[name][f"cpu_oracle_{unit}_per_s"] = round(seq_of.get(name, 1) / el, 3)
     return out
 
 

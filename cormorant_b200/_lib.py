@@ -17,7 +17,8 @@ F_WRAP32, F_WEIGHT_LOGICAL, F_ACT_RELU, F_ACT_RELU6 = 0x1, 0x2, 0x4, 0x8
 
 # every symbol include/cormorant_b200.h declares
 EXPORTS = ("corm_vectorop", "corm_matmul_workspace_size", "corm_matmul", "corm_matmul_noalloc", "corm_conv_workspace_size", "corm_conv",
-           "corm_matmul_post", "corm_conv_post",
+           "corm_matmul_post", "corm_conv_post", "corm_gemm_strided_workspace_size", "corm_gemm_strided",
+           "corm_copy_nd",
            "corm_pool", "corm_rowops", "corm_act_table", "corm_smx_table", "corm_rowops_table_image",
            "corm_bind_device", "corm_device_status", "corm_launch_count", "corm_profile_enable",
            "corm_profile_read", "corm_version", "corm_last_error")
@@ -59,6 +60,20 @@ class PostOp(C.Structure):
 POST_B_COL, POST_B_SAME, POST_B_SCALAR = 0, 1, 2
 
 
+class GemmDesc(C.Structure):
+    """corm_gemm_desc: a strided batch of MatMul jobs (row and batch strides)."""
+    _fields_ = [("a", C.c_void_p), ("b", C.c_void_p), ("c", C.c_void_p)] + _u32_fields(
+        ["n", "k", "m", "batch", "lda", "ldb", "ldc", "b_trans"]) + [
+        ("a_batch_stride", C.c_uint64), ("b_batch_stride", C.c_uint64), ("c_batch_stride", C.c_uint64),
+        ("flags", C.c_uint32), ("workspace", C.c_void_p), ("workspace_bytes", C.c_size_t)]
+
+
+class CopyDesc(C.Structure):
+    """corm_copy_desc: an int16 copy between two strided views of <= 6 dims."""
+    _fields_ = [("src", C.c_void_p), ("dst", C.c_void_p), ("ndim", C.c_uint32), ("dims", C.c_uint32 * 6),
+                ("src_strides", C.c_int64 * 6), ("dst_strides", C.c_int64 * 6)]
+
+
 class PoolDesc(C.Structure):
     _fields_ = [("x", C.c_void_p), ("y", C.c_void_p)] + _u32_fields(
         ["batch", "channels", "in_h", "in_w", "out_h", "out_w", "pool_h", "pool_w", "stride_h", "stride_w",
@@ -98,6 +113,9 @@ def lib() -> C.CDLL:
                        ("corm_matmul_workspace_size", [C.POINTER(MatmulDesc), C.POINTER(C.c_size_t)]),
                        ("corm_conv", [C.POINTER(ConvDesc), C.c_void_p]),
                        ("corm_conv_workspace_size", [C.POINTER(ConvDesc), C.POINTER(C.c_size_t)]),
+                       ("corm_gemm_strided", [C.POINTER(GemmDesc), C.c_void_p]),
+                       ("corm_gemm_strided_workspace_size", [C.POINTER(GemmDesc), C.POINTER(C.c_size_t)]),
+                       ("corm_copy_nd", [C.POINTER(CopyDesc), C.c_void_p]),
                        ("corm_pool", [C.POINTER(PoolDesc), C.c_void_p]),
                        ("corm_rowops", [C.POINTER(RowOpsDesc), C.c_void_p]),
                        ("corm_act_table", [C.c_uint32, C.c_uint32, C.c_void_p]),

@@ -67,21 +67,24 @@ def _param(name: str, words) -> N.TensorInfo:
 def prefill_layer(prefix: str, *, T: int, H: int, KV: int, HD: int, C: int, fq0, fk0, fv, fq, fkc, fvc, fp,
                   cos, sin, q0: N.TensorInfo, k0: N.TensorInfo, v: N.TensorInfo, pos: N.TensorInfo,
                   n: Optional[N.TensorInfo], ck: N.TensorInfo, cv: N.TensorInfo, pv_exp=None,
-                  logit_scale: Optional[float] = None, causal: int = 1, Q: int = KEY_QUANTUM,
+                  logit_scale: Optional[float] = None, causal: int = 1, Q: int = KEY_QUANTUM, batch: int = 1,
                   tensors: Optional[Dict[str, N.TensorInfo]] = None):
     """The node chain of one layer's prefill attention (llama.py:329-402,
     ``group_order`` "ahead1": qk0, then per group softmax / qk of the next /
     pv).  q0 [T][H HD] at fq0, k0 / v [T][KV HD] at fk0 / fv (per channel);
     the caches [C][KV HD] group-major states at fkc (one per KV head, [KV] or
     [KV HD]) / fvc (per KV head or per channel);
-    fq [H] the rotated q's exponents, fp [H] P's.  Returns (nodes, pv)."""
+    fq [H] the rotated q's exponents, fp [H] P's.  ``batch`` B: B sequences
+    at one pos / n stacked (q0 [B T][..], caches [B C][KV HD]; the nodes'
+    batch layouts).  Returns (nodes, pv)."""
     G = H // KV
+    B = int(batch)
     tensors = {} if tensors is None else tensors
     fq0, fk0, fv, fq, fkc, fvc, fp = (np.asarray(a, np.int64) for a in (fq0, fk0, fv, fq, fkc, fvc, fp))
     fkc, fvc = (np.repeat(f, HD) if f.size == KV else np.broadcast_to(f, (KV * HD,)) for f in (fkc, fvc))
-    qx = _t(f"{prefix}.qx", (KV, HD, G * T), 0)
-    qs = _t(f"{prefix}.qs", (T, H * HD), 0, is_state=True)
-    ks = _t(f"{prefix}.ks", (T, KV * HD), 0, is_state=True)
+    qx = _t(f"{prefix}.qx", (KV, HD, G * T) if B == 1 else (KV, B, HD, G * T), 0)
+    qs = _t(f"{prefix}.qs", (B * T, H * HD), 0, is_state=True)
+    ks = _t(f"{prefix}.ks", (B * T, KV * HD), 0, is_state=True)
     sa, sb, sc = RH.rope_params(fq0, H, HD, fq)
     wq, pq_bc = RH.pblock(0, 0, sa, sb, sc, H * HD)
     sa, sb, sc = RH.rope_params(fk0, KV, HD, fkc.reshape(KV, HD)[:, 0])
@@ -92,7 +95,7 @@ def prefill_layer(prefix: str, *, T: int, H: int, KV: int, HD: int, C: int, fq0,
         sa_v, sc_v = RH.vround_params(fv, fvc)
         wv, pv_bc = RH.pblock(0, 0, sa_v, 0, sc_v, KV * HD)
         pvb = _param(f"{prefix}.pv_p", wv)
-        vs = _t(f"{prefix}.vs", (T, KV * HD), 0, is_state=True)
+        vs = _t(f"{prefix}.vs", (B * T, KV * HD), 0, is_state=True)
     raw = _param(f"{prefix}.rope", RH.rope_table_words(cos, sin))
     pq, pk = _param(f"{prefix}.pq", wq), _param(f"{prefix}.pk", wk)
     pz = _param("rowops_p_zero", RH.param_block(0, 0, 0, 0, 0))
@@ -101,14 +104,14 @@ def prefill_layer(prefix: str, *, T: int, H: int, KV: int, HD: int, C: int, fq0,
     prep = N.AttnPrepRoNode(inputs=ins, output=qx, T=T, H=H, KV=KV, HD=HD, C=C, Q=Q, has_n=n is not None,
                             v_direct=v_direct, pq_bc=pq_bc, pk_bc=pk_bc, pv_bc=pv_bc, fq=fq, cos=cos, sin=sin,
                             q0=q0, k0=k0, v=v, pos=pos, n_t=n, ck=ck, cv=cv, qs=qs, ks=ks, vs=vs, raw=raw, pq=pq,
-                            pk=pk, pvb=pvb, pz=pz)
+                            pk=pk, pvb=pvb, pz=pz, batch=B)
     fs = score_exp(fq, fkc.reshape(KV, HD)[:, 0], KV)
     sigma = 1.0 / math.sqrt(HD) if logit_scale is None else float(logit_scale)
     rt = [pos] + ([n] if n is not None else [])
-    s = [_t(f"{prefix}.s{g}", (C, G * T), 0) for g in range(KV)]
-    p = [_t(f"{prefix}.p{g}", (G * T, C), 0) for g in range(KV)]
-    o = [_t(f"{prefix}.o{g}", (G * T, HD), 0) for g in range(KV)]
-    common = dict(T=T, H=H, KV=KV, HD=HD, C=C, Q=Q, has_n=n is not None)
+    s = [_t(f"{prefix}.s{g}", (C, B * G * T), 0) for g in range(KV)]
+    p = [_t(f"{prefix}.p{g}", (B * G * T, C), 0) for g in range(KV)]
+    o = [_t(f"{prefix}.o{g}", (B * G * T, HD), 0) for g in range(KV)]
+    common = dict(T=T, H=H, KV=KV, HD=HD, C=C, Q=Q, has_n=n is not None, batch=B)
 
     def qk(g):
         return N.LlmAttnConvNode(inputs=[ck, qx] + rt, output=s[g], kind="qk", group=g, **common)
@@ -117,7 +120,7 @@ def prefill_layer(prefix: str, *, T: int, H: int, KV: int, HD: int, C: int, fq0,
         regs = [smx_regs(int(fs[g * G + h]), sigma, int(fp[g * G + h])) for h in range(G)]
         return N.LlmAttnSoftmaxVopNode(inputs=[s[g]] + rt, output=p[g], T=T, G=G, C=C, Q=Q, group=g,
                                        has_n=n is not None, causal=causal == 1, prefix_lm=causal == 2,
-                                       cm=[r[0] for r in regs], cfg=[r[1] for r in regs])
+                                       cm=[r[0] for r in regs], cfg=[r[1] for r in regs], batch=B)
 
     def pv_(g):
         return N.LlmAttnConvNode(inputs=[p[g], cv] + rt, output=o[g], kind="pv", group=g, **common)
@@ -130,8 +133,8 @@ def prefill_layer(prefix: str, *, T: int, H: int, KV: int, HD: int, C: int, fq0,
     if pv_exp is None:
         grp = np.arange(H) // G
         pv_exp = (np.repeat(fp, HD) + fvc.reshape(KV, HD)[grp].reshape(-1) - 8)
-    pv = _t(f"{prefix}.pv", (T, H * HD), pv_exp)
-    chain.append(N.LlmAttnMergeNode(inputs=o, output=pv, T=T, H=H, KV=KV, HD=HD))
+    pv = _t(f"{prefix}.pv", (B * T, H * HD), pv_exp)
+    chain.append(N.LlmAttnMergeNode(inputs=o, output=pv, T=T, H=H, KV=KV, HD=HD, batch=B))
     for t in [qx, qs, ks, raw, pq, pk, pz, pv] + s + p + o + ([vs, pvb] if vs is not None else []):
         tensors[t.onnx_name] = t
     return chain, pv

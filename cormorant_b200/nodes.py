@@ -282,7 +282,12 @@ class AttnPrepRoNode:
     q.K^T image qx [KV][HD][G T] (TRANSPOSE of 8-row tiles), and the rows
     [pos, pos + n) of both caches (group-major states, written in place).
     inputs = [q0, k0, v, pos, (n), ck, cv, qs, ks, (vs), raw, pq, pk, (pvb),
-    pz, tables]; the named fields point into them."""
+    pz, tables]; the named fields point into them.
+
+    ``batch`` B > 1 (no counterpart in the reference, whose entries run one
+    sequence): B sequences at the same pos / n, stacked — q0 / k0 / v
+    [B T][..], the caches [B C][KV HD] (stored [KV][B][C][HD]), qx
+    [KV][B][HD][G T]."""
     inputs: List[TensorInfo]
     output: TensorInfo
     T: int = 1
@@ -317,6 +322,7 @@ class AttnPrepRoNode:
     pvb: Optional[TensorInfo] = field(default=None, repr=False)
     pz: Optional[TensorInfo] = field(default=None, repr=False)
     F: int = 8
+    batch: int = 1
     onnx_node: object = None
 
     @property
@@ -331,7 +337,9 @@ class LlmAttnConvNode:
     count from the host inputs pos / n — or keys = C (``static``; a static
     q.K^T over the cache rows r0 .. r0 + nr - 1 when nr > 0): raw int16
     operands, the int32 sum wraps, floor / 2^8, saturated.  inputs = [weight,
-    x, pos, (n)] or [weight, x]."""
+    x, pos, (n)] or [weight, x].  ``batch`` B: B sequences side by side —
+    scores [C][B G T] (sequence b's columns at b G T), P [B G T][C], o
+    [B G T][HD]."""
     inputs: List[TensorInfo]
     output: TensorInfo
     kind: str = "qk"
@@ -347,6 +355,7 @@ class LlmAttnConvNode:
     has_n: bool = True
     r0: int = 0
     nr: int = 0
+    batch: int = 1
     onnx_node: object = None
 
     @property
@@ -361,7 +370,7 @@ class LlmAttnSoftmaxVopNode:
     (columns h' T ..) -> P rows h' T .. over keys = roundup(pos + n, Q), row
     t valid over j < min(keys, pos + 1 + t) (``causal``), else every row over
     j < max(min(keys, pos + n) - prefix_lm, 1); registers cm[h'], cfg[h'].
-    inputs = [s, pos, (n)]."""
+    inputs = [s, pos, (n)]; ``batch`` B: s [C][B G T] -> P [B G T][C]."""
     inputs: List[TensorInfo]
     output: TensorInfo
     T: int = 1
@@ -375,6 +384,7 @@ class LlmAttnSoftmaxVopNode:
     cm: List[int] = field(default_factory=list)
     cfg: List[int] = field(default_factory=list)
     F: int = 8
+    batch: int = 1
     onnx_node: object = None
 
 
@@ -382,7 +392,8 @@ class LlmAttnSoftmaxVopNode:
 class LlmAttnMergeNode:
     """The P.V outputs o_g [G T][HD] (raw) -> pv [T][H HD] in head order,
     pv[t][(g G + h') HD + d] = o_g[h' T + t][d], a raw copy
-    (llm_nodes.py:1560-1660); R row splits with G = 1."""
+    (llm_nodes.py:1560-1660); R row splits with G = 1.  ``batch`` B: o_g
+    [B G T][HD] -> pv [B T][H HD]."""
     inputs: List[TensorInfo]
     output: TensorInfo
     T: int = 1
@@ -391,6 +402,23 @@ class LlmAttnMergeNode:
     HD: int = 16
     R: int = 1
     F: int = 8
+    batch: int = 1
+    onnx_node: object = None
+
+
+@dataclass
+class LlmSelectRowNode:
+    """y = h[n - 1] with n clamped to [1, rows] — the last valid row of a
+    padded prefill (llm_nodes.py:1663-1718); ``res32``: h / y int32 DMA
+    tensors.  inputs = [h, n].  ``batch`` B: h [B rows][d] -> y [B][d], one
+    row per sequence."""
+    inputs: List[TensorInfo]
+    output: TensorInfo
+    rows: int = 1
+    n: int = 1
+    res32: bool = False
+    F: int = 8
+    batch: int = 1
     onnx_node: object = None
 
 

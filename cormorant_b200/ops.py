@@ -92,6 +92,44 @@ def matmul(a, b, c, *, n, k, m, batch=1, a_batch_stride=0, b_batch_stride=0, c_b
     return workspace
 
 
+def gemm_strided(a, b, c, *, n, k, m, batch=1, lda=None, ldb=None, ldc=None, b_trans=False, a_batch_stride=0,
+                 b_batch_stride=0, c_batch_stride=0, flags=0, workspace=None):
+    """A strided batch of MatMul jobs (corm_gemm_strided): element row strides
+    lda / ldb / ldc (default dense), batch strides (0 shares the operand), B
+    transposed ([m][k]) with ``b_trans``."""
+    for t, nm in ((a, "a"), (b, "b"), (c, "c")):
+        _i16(t, nm)
+    st = _ready()
+    lda = k if lda is None else lda
+    ldb = (k if b_trans else m) if ldb is None else ldb
+    ldc = m if ldc is None else ldc
+    d = _lib.GemmDesc(_ptr(a), _ptr(b), _ptr(c), n, k, m, batch, lda, ldb, ldc, int(bool(b_trans)), a_batch_stride,
+                      b_batch_stride, c_batch_stride, flags, None, 0)
+    need = C.c_size_t(0)
+    check(lib().corm_gemm_strided_workspace_size(C.byref(d), C.byref(need)))
+    if need.value:
+        if workspace is None or workspace.numel() * workspace.element_size() < need.value:
+            workspace = torch.empty(need.value, dtype=torch.uint8, device=a.device)
+        d.workspace, d.workspace_bytes = _ptr(workspace), workspace.numel() * workspace.element_size()
+    check(lib().corm_gemm_strided(C.byref(d), st))
+    return workspace
+
+
+def copy_nd(src, dst, dims, src_strides, dst_strides, *, src_off=0, dst_off=0):
+    """dst[dst_off + sum x_i dst_strides[i]] = src[src_off + sum x_i
+    src_strides[i]] over the index box ``dims`` (<= 6 dims, element strides)."""
+    _i16(src, "src")
+    _i16(dst, "dst")
+    nd = len(dims)
+    if not 1 <= nd <= 6 or len(src_strides) != nd or len(dst_strides) != nd:
+        raise ValueError("copy_nd: 1..6 dims with one stride each")
+    st = _ready()
+    pad = lambda v, f: list(v) + [f] * (6 - nd)  # noqa: E731
+    d = _lib.CopyDesc(_ptr(src) + 2 * src_off, _ptr(dst) + 2 * dst_off, nd, (C.c_uint32 * 6)(*pad(dims, 1)),
+                      (C.c_int64 * 6)(*pad(src_strides, 0)), (C.c_int64 * 6)(*pad(dst_strides, 0)))
+    check(lib().corm_copy_nd(C.byref(d), st))
+
+
 def conv(x, weight, bias, y, *, batch, in_ch, in_h, in_w, out_ch, out_h, out_w, kh, kw, stride_h=1, stride_w=1,
          dilation_h=1, dilation_w=1, pad_top=0, pad_left=0, has_bias=0, is_depthwise=0, y_cs=0, y_cn=0, y_gs=0,
          flags=0, workspace=None, post=None):

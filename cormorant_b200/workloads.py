@@ -325,3 +325,126 @@ def graph_macs(graph) -> int:
 
 def shapes_summary(graph) -> List[Tuple[str, list]]:
     return [(type(sn).__name__, list(sn.output.shape)) for sn in graph.nodes]
+
+
+def _encode_weight(w: np.ndarray, f_w: int) -> np.ndarray:
+    """A constant MatMul weight at its rank-1 exponent f_w (numeric.py:199-255):
+    raw = RNE(w 2^f_w) saturated, carried as raw / 2^8 (the tensor's data)."""
+    raw = np.clip(np.round(np.asarray(w, np.float64) * 2.0 ** f_w), -32768, 32767)
+    return raw / 256.0
+
+
+# exponents of the Llama prefill (per tensor): the int32 residual, RMSNorm
+# outputs, projections, the rotated q / the caches, P, the attention output,
+# the MLP's, the logits
+LLAMA_EXP = dict(fr=15, fx=12, fq0=13, fk0=13, fv=13, fq=10, fkc=10, fvc=9, fp=12, fo=13, fg=13, fu=13, fa=13,
+                 fd=13, fl=11)
+
+
+def llama_prefill(seed: int = 5, batch: int = 1, seq: int = 512, layers: int = 32, hidden: int = 960, heads: int = 15,
+                  kv_heads: int = 5, head_dim: int = 64, ffn: int = 2560, vocab: int = 49152, theta: float = 1e5,
+                  cache: int = None, eps: float = 1e-5, exps: dict = None):
+    """The prefill of a Llama-family decoder (SmolLM2-360M shape by default)
+    on the kernels, as the scheduler's LLM entries lower it with the row-ops
+    unit and the softmax unit (src/llama.py:329-402 with rowops = vsmx = 1):
+    per layer RMSNorm (int32 residual -> int16), the q / k / v projections
+    (MatMul), the prefill attention chain (AttnPrepRoNode: RoPE theta and the
+    KV-cache rows; per KV group q.K^T, the column softmax and P.V; the head
+    merge), the output projection, ResAdd, RMSNorm, gate / up, SiLU(g) u,
+    down, ResAdd; then the last valid row of every sequence
+    (LlmSelectRowNode), the final RMSNorm and the LM head.
+
+    ``batch`` sequences of ``seq`` tokens at pos 0 (n = seq), stacked; the
+    KV caches of ``cache`` rows (default seq + 128, room for the decode
+    steps) are group-major states.  The embedding lookup is the reference's
+    host op: the graph input is the gathered rows of a N(0, 0.02) table as the
+    int32 residual.  Weights N(0, 0.02) (norm weights 1) at the rank-1
+    exponents the per-tensor activation exponents ``exps`` give.  Returns
+    (graph, {input: values}, macs_per_token)."""
+    from . import attention as AT
+    E = dict(LLAMA_EXP, **(exps or {}))
+    rng = np.random.default_rng(seed)
+    B, T, D, H, KV, HD = batch, seq, hidden, heads, kv_heads, head_dim
+    C = T + 128 if cache is None else cache
+    C = -(-C // AT.KEY_QUANTUM) * AT.KEY_QUANTUM
+    R = B * T
+    nq, nk = H * HD, KV * HD
+    weights: List[N.TensorInfo] = []
+    states: List[N.TensorInfo] = []
+    nodes: list = []
+
+    def ten(name, shape, exp=None, **kw):
+        return N.TensorInfo(name, list(shape), exp=None if exp is None else np.asarray(exp, np.int64), **kw)
+
+    def param(name, words):
+        t = ten(name, (len(words),), data=np.asarray(words, np.float64) / 256.0)
+        weights.append(t)
+        return t
+
+    def linear(name, x, f_in, k, m, f_out, rows=R):
+        w = ten(name + ".w", (k, m), data=_encode_weight(rng.normal(0.0, 0.02, (k, m)), f_out + 8 - f_in))
+        weights.append(w)
+        y = ten(name, (rows, m), f_out)
+        nodes.append(N.MatmulNode(inputs=[x, w], output=y, n=rows, k=k, m=m, batch=1))
+        return y
+
+    def rmsnorm(name, h, f_out, rows=R):
+        gamma = np.ones(D)
+        words, bc, g, Ev = RH.rmsnorm_job(gamma, eps, E["fr"], np.full(D, f_out))
+        y = ten(name, (rows, D), f_out)
+        nodes.append(N.RMSNormRoNode(inputs=[h, param(name + ".p", words)], output=y, rows=rows, n=D, fr=E["fr"],
+                                     eps=eps, g=g, E=Ev, bcast=bc, gamma=gamma))
+        return y
+
+    def resadd(name, h, d, f_d):
+        words, bc = RH.resadd_job(E["fr"], np.full(D, f_d), D)
+        y = ten(name, (R, D), E["fr"], dma="i32")
+        nodes.append(N.ResAddRoNode(inputs=[h, d, param(name + ".p", words)], output=y, rows=R, n=D, fr=E["fr"],
+                                    bcast=bc))
+        return y
+
+    inv = 1.0 / theta ** (np.arange(0, HD, 2, dtype=np.float64) / HD)
+    ang = np.outer(np.arange(C, dtype=np.float64), inv)
+    cos, sin = np.cos(ang).astype(np.float32), np.sin(ang).astype(np.float32)
+    h = h0 = ten("h0", (R, D), E["fr"], dma="i32")
+    pos, n_t = ten("pos", (1,), host="i32"), ten("n", (1,), host="i32")
+    emb = rng.normal(0.0, 0.02, (vocab, D))
+    ids = rng.integers(0, vocab, size=(B, T))
+    feeds = {"h0": emb[ids].reshape(R, D), "pos": np.array([0]), "n": np.array([T])}
+    for li in range(L := layers):
+        p = f"l{li}"
+        x = rmsnorm(p + ".x", h, E["fx"])
+        q0 = linear(p + ".q0", x, E["fx"], D, nq, E["fq0"])
+        k0 = linear(p + ".k0", x, E["fx"], D, nk, E["fk0"])
+        v = linear(p + ".v", x, E["fx"], D, nk, E["fv"])
+        ck = ten(p + ".ck", (B * C, nk), E["fkc"], is_state=True, group_layout=(KV, HD))
+        cv = ten(p + ".cv", (B * C, nk), E["fvc"], is_state=True, group_layout=(KV, HD))
+        states += [ck, cv]
+        chain, pv = AT.prefill_layer(p + ".attn", T=T, H=H, KV=KV, HD=HD, C=C, fq0=np.full(nq, E["fq0"]),
+                                     fk0=np.full(nk, E["fk0"]), fv=np.full(nk, E["fv"]), fq=np.full(H, E["fq"]),
+                                     fkc=np.full(KV, E["fkc"]), fvc=np.full(KV, E["fvc"]), fp=np.full(H, E["fp"]),
+                                     cos=cos, sin=sin, q0=q0, k0=k0, v=v, pos=pos, n=n_t, ck=ck, cv=cv, batch=B)
+        for nd in chain:
+            for t in nd.inputs:
+                if t is not None and t.data is not None and all(t is not w for w in weights):
+                    weights.append(t)
+        nodes += chain
+        o = linear(p + ".o", pv, E["fp"] + E["fvc"] - 8, nq, D, E["fo"])
+        h1 = resadd(p + ".h1", h, o, E["fo"])
+        x2 = rmsnorm(p + ".x2", h1, E["fx"])
+        g = linear(p + ".g", x2, E["fx"], D, ffn, E["fg"])
+        u = linear(p + ".u", x2, E["fx"], D, ffn, E["fu"])
+        words, bc = RH.silu_mul_job(np.full(ffn, E["fg"]), np.full(ffn, E["fu"]), np.full(ffn, E["fa"]), ffn)
+        a = ten(p + ".a", (R, ffn), E["fa"])
+        nodes.append(N.SiluMulRoNode(inputs=[g, u, param(p + ".a.p", words)], output=a, rows=R, n=ffn, bcast=bc))
+        d = linear(p + ".d", a, E["fa"], ffn, D, E["fd"])
+        h = resadd(p + ".h2", h1, d, E["fd"])
+    last = ten("h_last", (B, D), E["fr"], dma="i32")
+    nodes.append(N.LlmSelectRowNode(inputs=[h, n_t], output=last, rows=T, n=D, res32=True, batch=B))
+    xf = rmsnorm("xf", last, E["fx"], rows=B)
+    logits = linear("logits", xf, E["fx"], D, vocab, E["fl"], rows=B)
+    g_ = N.Graph(nodes=nodes, weight_tensors=weights, input_tensors=[h0, pos, n_t], output_tensors=[logits],
+                 state_tensors=states)
+    keys = -(-T // AT.KEY_QUANTUM) * AT.KEY_QUANTUM
+    macs = L * (D * (nq + 2 * nk) + nq * D + 3 * D * ffn + 2 * (H // KV) * KV * keys * HD) + D * vocab / T
+    return g_, feeds, macs

@@ -154,6 +154,44 @@ typedef struct {
 int corm_matmul_post(const corm_matmul_desc* d, const corm_postop* post, corm_stream_t stream);
 int corm_conv_post(const corm_conv_desc* d, const corm_postop* post, corm_stream_t stream);
 
+/* ---------------------------------------------------------------- strided batches
+ * No counterpart among the reference's kernel registers: what the simulator
+ * uses to run the attention of many sequences in one launch.
+ *
+ * corm_gemm_strided: the MatMul job's numerics (exact int16 sum; CORM_F_WRAP32
+ * wraps it to int32; floor / 2^8; sat16; CORM_F_ACT_*) on strided operands:
+ * C[b][r][j] at c + b*c_batch_stride + r*ldc + j; A[b][r][kk] at a +
+ * b*a_batch_stride + r*lda + kk; B[b][kk][j] at b + b*b_batch_stride +
+ * kk*ldb + j, or with b_trans at b + ... + j*ldb + kk.  Strides in elements;
+ * a batch stride of 0 shares the operand.  k <= 32768. */
+typedef struct {
+  const int16_t* a;
+  const int16_t* b;
+  int16_t* c;
+  uint32_t n, k, m, batch;
+  uint32_t lda, ldb, ldc, b_trans;
+  uint64_t a_batch_stride, b_batch_stride, c_batch_stride;
+  uint32_t flags;
+  void* workspace; /* NULL: the library's scratch */
+  size_t workspace_bytes;
+} corm_gemm_desc;
+
+int corm_gemm_strided_workspace_size(const corm_gemm_desc* d, size_t* bytes);
+int corm_gemm_strided(const corm_gemm_desc* d, corm_stream_t stream);
+
+/* corm_copy_nd: dst[sum x_i dst_strides[i]] = src[sum x_i src_strides[i]] for
+ * every index x over dims[0..ndim) (outermost first, ndim <= 6, strides in
+ * int16 elements, may be negative).  The views must not overlap. */
+typedef struct {
+  const int16_t* src;
+  int16_t* dst;
+  uint32_t ndim;
+  uint32_t dims[6];
+  int64_t src_strides[6], dst_strides[6];
+} corm_copy_desc;
+
+int corm_copy_nd(const corm_copy_desc* d, corm_stream_t stream);
+
 /* ---------------------------------------------------------------- Pool
  * Replaces run_pool / XPoolingkernel (inference-scheduler/src/codegen/
  * _source.py:1548-1580; semantics inference-scheduler/src/codegen/

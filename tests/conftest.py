@@ -28,3 +28,81 @@ def golden():
             cache[name] = load_golden(name)
         return cache[name]
     return get
+
+
+@pytest.fixture
+def cpu_ops(monkeypatch):
+    """ops.rowops / matmul / vectorop replayed on the oracle's job models over
+    CPU tensors: the host logic of GpuSimulator without a GPU."""
+    import torch
+
+    from cormorant_b200 import ops
+    from cormorant_b200._lib import F_WRAP32
+    from cormorant_b200.simulator import GpuSimulator
+    from oracle import spec
+
+    def np16(t):
+        return t.numpy() if t is not None else None
+
+    def rowops(a, b, c, p, *, op, n, rows=1, blocks=1, a_s1=0, a_s2=0, b_s1=0, b_s2=0, c_s1=0, c_s2=0, eps=0, aux=0,
+               bq_sh=0, win_lo=0, win_hi=0xFFFFFFFF, a_off=0, b_off=0, c_off=0, p_off=0):
+        regions, base, addr = {}, 0, {}
+        for nm, t, off in (("a", a, a_off), ("b", b, b_off), ("c", c, c_off), ("p", p, p_off)):
+            if t is None:
+                addr[nm] = 0
+                continue
+            st = t.untyped_storage()
+            key = st.data_ptr()
+            if key not in regions:
+                regions[key] = (base, st)
+                base += (st.nbytes() + 255) // 256 * 256 + 256
+            addr[nm] = regions[key][0] + (t.data_ptr() - key) + off
+        mem = np.zeros(base, np.uint8)
+        for b0, st in regions.values():
+            mem[b0:b0 + st.nbytes()] = np.frombuffer(bytes(st), np.uint8)
+        m = spec.RowOpsMem(mem)
+        spec.rowops_job(m, op, n, rows, blocks, addr["a"], a_s1, a_s2, addr["b"], b_s1, b_s2, addr["c"], c_s1, c_s2,
+                        addr["p"], eps, aux, bq_sh, win_lo, win_hi)
+        cst = c.untyped_storage()
+        b0 = regions[cst.data_ptr()][0]
+        cst.copy_(torch.frombuffer(bytearray(m.buf[b0:b0 + cst.nbytes()].tobytes()), dtype=torch.uint8).untyped_storage())
+
+    def matmul(a, b, c, *, n, k, m, batch=1, a_batch_stride=0, b_batch_stride=0, c_batch_stride=0, b_packed=0,
+               gemv_kw=0, flags=0, workspace=None, post=None):
+        assert post is None
+        spec.matmul_job(np16(a), np16(b), np16(c), n, k, m, batch, a_batch_stride, b_batch_stride, c_batch_stride,
+                        b_packed, gemv_kw, wrap=bool(flags & F_WRAP32))
+
+    def vectorop(a, b, c, *, size, op, outer=1, a_inc=0, b_inc=0, act=0, alpha=0, smx_cm=0, smx_cfg=0, smx_mask=0):
+        spec.vectorop_job(np16(a), np16(b), np16(c), size, op, outer, a_inc, b_inc, act, alpha, smx_cm, smx_cfg,
+                          smx_mask)
+
+    def view(t, off, dims, strides):
+        a = t.numpy()
+        return np.lib.stride_tricks.as_strided(a[off:], shape=tuple(dims), strides=tuple(2 * x for x in strides),
+                                               writeable=True)
+
+    def gemm_strided(a, b, c, *, n, k, m, batch=1, lda=None, ldb=None, ldc=None, b_trans=False, a_batch_stride=0,
+                     b_batch_stride=0, c_batch_stride=0, flags=0, workspace=None):
+        lda, ldc = k if lda is None else lda, m if ldc is None else ldc
+        ldb = (k if b_trans else m) if ldb is None else ldb
+        A = view(a, 0, (batch, n, k), (a_batch_stride, lda, 1))
+        Bm = view(b, 0, (batch, m, k) if b_trans else (batch, k, m), (b_batch_stride, ldb, 1))
+        if b_trans:
+            Bm = Bm.transpose(0, 2, 1)
+        out = view(c, 0, (batch, n, m), (c_batch_stride, ldc, 1))
+        out[...] = spec.matmul_raw(A.astype(np.int64), Bm.astype(np.int64), bool(flags & F_WRAP32))
+        return workspace
+
+    def copy_nd(src, dst, dims, src_strides, dst_strides, *, src_off=0, dst_off=0):
+        v = view(src, src_off, dims, src_strides).copy()
+        out = view(dst, dst_off, dims, dst_strides)
+        out[...] = v
+
+    monkeypatch.setattr(ops, "gemm_strided", gemm_strided)
+    monkeypatch.setattr(ops, "copy_nd", copy_nd)
+    monkeypatch.setattr(ops, "rowops", rowops)
+    monkeypatch.setattr(ops, "matmul", matmul)
+    monkeypatch.setattr(ops, "vectorop", vectorop)
+    monkeypatch.setattr(GpuSimulator, "_mm_ws", staticmethod(lambda *a: 0))
+    return GpuSimulator

@@ -1,0 +1,79 @@
+"""The Llama prefill graph (workloads.llama_prefill: RMSNorm / projections /
+the prefill attention chain / ResAdd / SiLU(g) u / the LM head on the
+kernels) on the GPU against the CPU oracle (oracle.llm: the row-ops jobs on
+the job model, the attention restatement per sequence), every tensor
+bit-exact, the KV caches included."""
+import numpy as np
+import pytest
+
+
+def _raw_inputs(g, feeds):
+    tm = {t.onnx_name: t for t in g.input_tensors}
+    out = {}
+    for k, v in feeds.items():
+        t = tm[k]
+        f = 0.0 if t.host else np.asarray(t.exp, np.float64)
+        out[k] = np.asarray(v) if t.host else np.rint(np.asarray(v, np.float64) * 2.0 ** f).astype(np.int64)
+    return out
+
+
+def test_llama_oracle_runs_small():
+    """The builder and the CPU oracle on a tiny configuration (no GPU)."""
+    from cormorant_b200 import workloads as WL
+    from oracle import llm
+    g, feeds, macs = WL.llama_prefill(seed=7, batch=2, seq=16, layers=1, hidden=64, heads=4, kv_heads=2,
+                                      head_dim=16, ffn=128, vocab=50)
+    states = {t.onnx_name: np.zeros(t.shape, np.int64) for t in g.state_tensors}
+    arr = llm.forward(g, _raw_inputs(g, feeds), states)
+    lg = arr["logits"]
+    assert lg.shape == (2, 50) and np.abs(lg).max() > 0 and (np.abs(lg) < 32767).mean() > 0.9
+    assert macs > 0
+
+
+def _compare(g, arr, ref, states, rstates):
+    checked = 0
+    for sn in g.nodes:
+        t = sn.output
+        if t.onnx_name not in arr:
+            continue
+        f = np.asarray(8 if t.exp is None else t.exp, np.float64)
+        got = np.rint(np.asarray(arr[t.onnx_name]) * np.power(2.0, f)).astype(np.int64)
+        assert np.array_equal(got.reshape(ref[t.onnx_name].shape), ref[t.onnx_name]), t.onnx_name
+        checked += 1
+    assert checked >= len(g.nodes) // 2
+    for t in g.state_tensors:
+        got = np.rint(states[t.onnx_name] * np.power(2.0, np.asarray(t.exp, np.float64))).astype(np.int64)
+        assert np.array_equal(got, rstates[t.onnx_name]), t.onnx_name
+
+
+def test_llama_host_logic_cpu(cpu_ops):
+    """GpuSimulator's host logic on the Llama graph (every job's registers,
+    the batched attention's strides, the states) with its kernel calls
+    replayed on the oracle's job models, against the oracle's forward pass."""
+    from cormorant_b200 import workloads as WL
+    from oracle import llm
+    g, feeds, _ = WL.llama_prefill(seed=8, batch=2, seq=16, layers=1, hidden=64, heads=4, kv_heads=2, head_dim=16,
+                                   ffn=128, vocab=50)
+    states = {t.onnx_name: np.zeros(t.shape) for t in g.state_tensors}
+    arr = cpu_ops(g, device="cpu").forward_pass(feeds, states=states)
+    rstates = {t.onnx_name: np.zeros(t.shape, np.int64) for t in g.state_tensors}
+    ref = llm.forward(g, _raw_inputs(g, feeds), rstates)
+    _compare(g, arr, ref, states, rstates)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("fuse", [False, True])
+def test_gpu_llama_prefill_vs_oracle(fuse):
+    torch = pytest.importorskip("torch")
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    from cormorant_b200 import workloads as WL
+    from cormorant_b200.simulator import GpuSimulator
+    from oracle import llm
+    g, feeds, _ = WL.llama_prefill(seed=9, batch=2, seq=32, layers=2, vocab=1000)
+    sim = GpuSimulator(g, fuse=fuse)
+    states = {t.onnx_name: np.zeros(t.shape) for t in g.state_tensors}
+    arr = sim.forward_pass(feeds, states=states)
+    rstates = {t.onnx_name: np.zeros(t.shape, np.int64) for t in g.state_tensors}
+    ref = llm.forward(g, _raw_inputs(g, feeds), rstates)
+    _compare(g, arr, ref, states, rstates)

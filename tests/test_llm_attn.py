@@ -116,66 +116,70 @@ def test_oracle_static_matches_reference(z):
     assert np.array_equal(A.attn_pv(z["st_ps"], z["st_cv"], 0, HD=HD, keys=C), z["st_os"])
 
 
-@pytest.fixture
-def cpu_ops(monkeypatch):
-    """ops.rowops / matmul / vectorop replayed on the oracle's job models over
-    CPU tensors: the host logic of GpuSimulator without a GPU."""
-    import torch
-
-    from cormorant_b200 import ops
-    from cormorant_b200._lib import F_WRAP32
-    from cormorant_b200.simulator import GpuSimulator
-    from oracle import spec
-
-    def np16(t):
-        return t.numpy() if t is not None else None
-
-    def rowops(a, b, c, p, *, op, n, rows=1, blocks=1, a_s1=0, a_s2=0, b_s1=0, b_s2=0, c_s1=0, c_s2=0, eps=0, aux=0,
-               bq_sh=0, win_lo=0, win_hi=0xFFFFFFFF, a_off=0, b_off=0, c_off=0, p_off=0):
-        regions, base, addr = {}, 0, {}
-        for nm, t, off in (("a", a, a_off), ("b", b, b_off), ("c", c, c_off), ("p", p, p_off)):
-            if t is None:
-                addr[nm] = 0
-                continue
-            st = t.untyped_storage()
-            key = st.data_ptr()
-            if key not in regions:
-                regions[key] = (base, st)
-                base += (st.nbytes() + 255) // 256 * 256 + 256
-            addr[nm] = regions[key][0] + (t.data_ptr() - key) + off
-        mem = np.zeros(base, np.uint8)
-        for b0, st in regions.values():
-            mem[b0:b0 + st.nbytes()] = np.frombuffer(bytes(st), np.uint8)
-        m = spec.RowOpsMem(mem)
-        spec.rowops_job(m, op, n, rows, blocks, addr["a"], a_s1, a_s2, addr["b"], b_s1, b_s2, addr["c"], c_s1, c_s2,
-                        addr["p"], eps, aux, bq_sh, win_lo, win_hi)
-        cst = c.untyped_storage()
-        b0 = regions[cst.data_ptr()][0]
-        cst.copy_(torch.frombuffer(bytearray(m.buf[b0:b0 + cst.nbytes()].tobytes()), dtype=torch.uint8).untyped_storage())
-
-    def matmul(a, b, c, *, n, k, m, batch=1, a_batch_stride=0, b_batch_stride=0, c_batch_stride=0, b_packed=0,
-               gemv_kw=0, flags=0, workspace=None, post=None):
-        assert post is None
-        spec.matmul_job(np16(a), np16(b), np16(c), n, k, m, batch, a_batch_stride, b_batch_stride, c_batch_stride,
-                        b_packed, gemv_kw, wrap=bool(flags & F_WRAP32))
-
-    def vectorop(a, b, c, *, size, op, outer=1, a_inc=0, b_inc=0, act=0, alpha=0, smx_cm=0, smx_cfg=0, smx_mask=0):
-        spec.vectorop_job(np16(a), np16(b), np16(c), size, op, outer, a_inc, b_inc, act, alpha, smx_cm, smx_cfg,
-                          smx_mask)
-
-    monkeypatch.setattr(ops, "rowops", rowops)
-    monkeypatch.setattr(ops, "matmul", matmul)
-    monkeypatch.setattr(ops, "vectorop", vectorop)
-    monkeypatch.setattr(GpuSimulator, "_mm_ws", staticmethod(lambda *a: 0))
-    return GpuSimulator
-
-
 @pytest.mark.parametrize("tag", ["a", "c"])
 def test_simulator_host_logic_cpu(z, cpu_ops, tag):
     g, _ = _chain(z, CASES[tag])
     feeds, states = _feeds(z, tag)
     arr = cpu_ops(g, device="cpu").forward_pass(feeds, states=states)
     _check(z, tag, arr, states)
+
+
+def _batched(z, B, tag="a"):
+    """B sequences at case ``tag``'s pos / n: sequence b's inputs and caches
+    are case tag's rolled by b rows (distinct data, one golden source)."""
+    ten = lambda name, shape, exp=None, **kw: N.TensorInfo(  # noqa: E731
+        name, list(shape), exp=None if exp is None else np.asarray(exp, np.int64), **kw)
+    q0, k0, v = (ten("q0", (B * T, H * HD), z["fq0"]), ten("k0", (B * T, KV * HD), z["fk0"]),
+                 ten("v", (B * T, KV * HD), z["fv"]))
+    pos, n = ten("pos", (1,), host="i32"), ten("n", (1,), host="i32")
+    ck = ten("ck", (B * C, KV * HD), z["fkc"], is_state=True, group_layout=(KV, HD))
+    cv = ten("cv", (B * C, KV * HD), z["fvc"], is_state=True, group_layout=(KV, HD))
+    regs = np.array([AT.smx_regs(int(f), 1.0 / np.sqrt(HD), int(p)) for f, p in
+                     zip(AT.score_exp(z["fq"], z["fkc"][::HD], KV), z["fp"])])
+    nodes, pv = AT.prefill_layer("l0", T=T, H=H, KV=KV, HD=HD, C=C, fq0=z["fq0"], fk0=z["fk0"], fv=z["fv"],
+                                 fq=z["fq"], fkc=z["fkc"][::HD], fvc=z["fvc"], fp=z["fp"], cos=z["cos"],
+                                 sin=z["sin"], q0=q0, k0=k0, v=v, pos=pos, n=n, ck=ck, cv=cv, batch=B)
+    wts = list({t.onnx_name: t for nd in nodes for t in nd.inputs if t is not None and t.data is not None}.values())
+    g = N.Graph(nodes=nodes, weight_tensors=wts, input_tensors=[q0, k0, v, pos, n], output_tensors=[pv],
+                state_tensors=[ck, cv])
+    roll = lambda a, b: np.roll(a, b, axis=0)  # noqa: E731
+    raw = {k: np.concatenate([roll(z[f"{tag}_{k}"], b) for b in range(B)]) for k in ("q0", "k0", "v", "ck0", "cv0")}
+    p2 = lambda e: np.power(2.0, np.asarray(e, np.float64))[None, :]  # noqa: E731
+    posn = [int(x) for x in z[f"{tag}_posn"]]
+    feeds = {"q0": raw["q0"] / p2(z["fq0"]), "k0": raw["k0"] / p2(z["fk0"]), "v": raw["v"] / p2(z["fv"]),
+             "pos": np.array([posn[0]]), "n": np.array([posn[1]])}
+    states = {"ck": raw["ck0"] / p2(z["fkc"]), "cv": raw["cv0"] / p2(z["fvc"])}
+    return g, feeds, states, raw, posn, regs
+
+
+def _check_batched(z, B, arr, states, raw, posn, regs):
+    """Every sequence against the oracle run on its own."""
+    from oracle import attn as A
+    p2 = lambda e: np.power(2.0, np.asarray(e, np.float64))[None, :]  # noqa: E731
+    pv = np.rint(arr["l0.pv"] * p2(z["fpv"])).astype(np.int64)
+    ck = np.rint(states["ck"] * p2(z["fkc"])).astype(np.int64)
+    cv = np.rint(states["cv"] * p2(z["fvc"])).astype(np.int64)
+    for b in range(B):
+        ck0, cv0 = raw["ck0"][b * C:(b + 1) * C].copy(), raw["cv0"][b * C:(b + 1) * C].copy()
+        sl = slice(b * T, (b + 1) * T)
+        out = A.prefill_layer(raw["q0"][sl], raw["k0"][sl], raw["v"][sl], posn[0], posn[1], T=T, H=H, KV=KV, HD=HD,
+                              C=C, fq0=z["fq0"], fk0=z["fk0"], fv=z["fv"], fq=z["fq"], fkc=z["fkc"], fvc=z["fvc"],
+                              cos=z["cos"], sin=z["sin"], ck=ck0, cv=cv0, cm=regs[:, 0], cfg=regs[:, 1])
+        assert np.array_equal(pv[sl], out["pv"]), b
+        assert np.array_equal(ck[b * C:(b + 1) * C], ck0) and np.array_equal(cv[b * C:(b + 1) * C], cv0), b
+        qx = np.rint(arr["l0.qx"]).astype(np.int64).reshape(KV, B, HD, G * T)
+        assert np.array_equal(qx[:, b], out["qx"]), b
+        for g in range(KV):
+            s = np.rint(arr[f"l0.s{g}"]).astype(np.int64).reshape(C, B, G * T)
+            assert np.array_equal(s[:, b], out[f"s{g}"]), (b, g)
+            p = np.rint(arr[f"l0.p{g}"]).astype(np.int64).reshape(B, G * T, C)
+            assert np.array_equal(p[b], out[f"p{g}"]), (b, g)
+
+
+def test_simulator_batched_cpu(z, cpu_ops):
+    g, feeds, states, raw, posn, regs = _batched(z, 3)
+    arr = cpu_ops(g, device="cpu").forward_pass(feeds, states=states)
+    _check_batched(z, 3, arr, states, raw, posn, regs)
 
 
 # --------------------------------------------------------------------------- GPU
@@ -219,3 +223,13 @@ def test_gpu_static_rows_and_pv(z, sim_cls):
                                   states=states)
     assert np.array_equal(np.rint(arr["sr"]).astype(np.int64), z["st_sr"])
     assert np.array_equal(np.rint(arr["os"]).astype(np.int64), z["st_os"])
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("tag,B", [("a", 5), ("d", 2)])
+def test_gpu_prefill_attention_batched(z, sim_cls, tag, B):
+    """B sequences in one pass (the batched launches) against the oracle run
+    per sequence."""
+    g, feeds, states, raw, posn, regs = _batched(z, B, tag)
+    arr = sim_cls(g).forward_pass(feeds, states=states)
+    _check_batched(z, B, arr, states, raw, posn, regs)
