@@ -400,12 +400,13 @@ __device__ __noinline__ int64_t norm_out128(long long P1, int64_t g, int32_t bq,
   return corm_sat16_128(corm_rne_shr128((__int128)P1 * g + ((__int128)bq << bq_sh), sc));
 }
 
-template <int NW_PER>
+template <int NW_PER, int AK>
 __global__ void __launch_bounds__(256) ro_norm16(RoArgs q) {
+  constexpr uint32_t EPW = AK ? 4u : 8u;  // elements per 16-byte word of A
   extern __shared__ __align__(16) uint8_t ro_smem[];
   const bool ln = (q.op >> 16) & 1u;
   const bool bcast = (q.op >> 13) & 1u;
-  const uint32_t words = q.n >> 3;
+  const uint32_t words = q.n / EPW;
   // entry of column c = 8 w + e at [e][w] (lanes read consecutive words):
   // G, Bq' << bq_sh (int64) and sh_c
   const uint32_t npar = bcast ? 1u : q.n;
@@ -417,7 +418,7 @@ __global__ void __launch_bounds__(256) ro_norm16(RoArgs q) {
   __syncthreads();
   for (uint32_t c = threadIdx.x; c < npar; c += blockDim.x) {
     const int4 e = *(const int4*)(q.p + 16ull * c);
-    const uint32_t slot = bcast ? 0u : (c & 7u) * words + (c >> 3);
+    const uint32_t slot = bcast ? 0u : (c % EPW) * words + c / EPW;
     atomicMin(&s_scmin, (int)(((uint32_t)e.z >> 16) & 63u));
     s_g[slot] = e.x;
     const int64_t bq = (int32_t)((uint32_t)e.y << 10) >> 10;  // int22, sign-extended
@@ -435,56 +436,66 @@ __global__ void __launch_bounds__(256) ro_norm16(RoArgs q) {
     const uint8_t* ra = q.a + (uint64_t)i2 * q.a_s2 + (uint64_t)i1 * q.a_s1;
     uint8_t* rc = q.c + (uint64_t)i2 * q.c_s2 + (uint64_t)i1 * q.c_s1;
     int4 xv[NW_PER];
-    int s1 = 0, xmax = -32768, xmin = 32767;
-    long long s2 = 0;
+    long long s1 = 0, xmax = AK ? INT32_MIN : -32768, xmin = AK ? INT32_MAX : 32767;
+    long long s2 = 0;           // int16 rows: every partial sum < 2^42
+    unsigned __int128 s2w = 0;  // int32 rows: squares up to 2^62
 #pragma unroll
     for (int k = 0; k < NW_PER; k++) {
       const uint32_t w = lane + 32u * k;
       xv[k] = make_int4(0, 0, 0, 0);
       if (w < words) {
         xv[k] = *(const int4*)(ra + 16ull * w);
-        const int16_t* xs = (const int16_t*)&xv[k];
 #pragma unroll
-        for (int e = 0; e < 8; e++) {
-          s1 += xs[e];
-          s2 += xs[e] * xs[e];  // each square < 2^30
-          xmax = max(xmax, (int)xs[e]);
-          xmin = min(xmin, (int)xs[e]);
+        for (int e = 0; e < (int)EPW; e++) {
+          const long long x = AK ? (long long)((const int32_t*)&xv[k])[e] : (long long)((const int16_t*)&xv[k])[e];
+          s1 += x;
+          if (AK)
+            s2w += (unsigned __int128)(x * x);
+          else
+            s2 += x * x;  // each square < 2^30
+          xmax = max(xmax, x);
+          xmin = min(xmin, x);
         }
       }
     }
+    unsigned long long lo = AK ? (unsigned long long)s2w : (unsigned long long)s2;
+    unsigned long long hi = AK ? (unsigned long long)(s2w >> 64) : 0ull;
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) {
       s1 += __shfl_xor_sync(0xffffffffu, s1, o);
-      s2 += __shfl_xor_sync(0xffffffffu, s2, o);
+      const unsigned long long lo2 = __shfl_xor_sync(0xffffffffu, lo, o);
+      const unsigned long long hi2 = __shfl_xor_sync(0xffffffffu, hi, o);
+      const unsigned long long sum = lo + lo2;
+      hi += hi2 + (sum < lo ? 1ull : 0ull);
+      lo = sum;
       xmax = max(xmax, __shfl_xor_sync(0xffffffffu, xmax, o));
       xmin = min(xmin, __shfl_xor_sync(0xffffffffu, xmin, o));
     }
-    __int128 D = ln ? ((__int128)q.n * s2 - (__int128)s1 * s1 + (__int128)q.eps) : ((__int128)s2 + (__int128)q.eps);
+    const __int128 S2 = (__int128)(((unsigned __int128)hi << 64) | lo);
+    __int128 D = ln ? ((__int128)q.n * S2 - (__int128)s1 * s1 + (__int128)q.eps) : (S2 + (__int128)q.eps);
     if (D <= 0) D = 1;
     uint64_t Rm;
     int sh;
     rsqrt_bf(D, Rm, sh, q.rsq);
     const int shp = sh - 24;
-    const int nn = ln ? (int)q.n : 1, off = ln ? s1 : 0;  // |n x - S1| < 2^28
+    const long long nn = ln ? (long long)q.n : 1, off = ln ? s1 : 0;  // int16: |n x - S1| < 2^28; int32 rows: RMS only
     // the whole row on the 64-bit path when every |P1| < 2^31 (bounded by
     // the extreme A), Bq' << bq_sh < 2^61 and every sh_c >= 1: no branch per
     // element; the rare other rows element by element in 128 bits
-    const long long amax = max(llabs((long long)nn * xmax - off), llabs((long long)nn * xmin - off));
-    const bool row_fast = small_bq && s_scmin >= 1 && ((amax * (long long)Rm) >> shp) < (1ll << 31) - 1;
+    const long long amax = max(llabs(nn * xmax - off), llabs(nn * xmin - off));
+    const bool row_fast = small_bq && s_scmin >= 1 && (((__int128)amax * (__int128)Rm) >> shp) < (1ll << 31) - 1;
 #pragma unroll
     for (int k = 0; k < NW_PER; k++) {
       const uint32_t w = lane + 32u * k;
       if (w >= words) continue;
-      const int16_t* xs = (const int16_t*)&xv[k];
-      int4 out;
-      int16_t* os = (int16_t*)&out;
+      int16_t os[EPW];
       if (row_fast) {
 #pragma unroll
-        for (int e = 0; e < 8; e++) {
+        for (int e = 0; e < (int)EPW; e++) {
           const uint32_t slot = bcast ? 0u : (uint32_t)e * words + w;
-          const int A = nn * xs[e] - off;
-          const long long P1 = ((long long)A * (long long)Rm) >> shp;  // |A Rm| < 2^60
+          const long long x = AK ? (long long)((const int32_t*)&xv[k])[e] : (long long)((const int16_t*)&xv[k])[e];
+          const long long A = nn * x - off;
+          const long long P1 = (A * (long long)Rm) >> shp;  // |A Rm| < 2^63 (int32 rows: |A| <= 2^31)
           const long long v = P1 * s_g[slot] + s_bq[slot];
           const int sc = s_sc[slot];
           const long long qv = v >> sc, rr = v - (qv << sc), half = 1ll << (sc - 1);
@@ -492,15 +503,203 @@ __global__ void __launch_bounds__(256) ro_norm16(RoArgs q) {
           os[e] = (int16_t)min(max(y, -32768ll), 32767ll);
         }
       } else {
-        for (int e = 0; e < 8; e++) {
+        for (int e = 0; e < (int)EPW; e++) {
           const uint32_t slot = bcast ? 0u : (uint32_t)e * words + w;
-          const int A = nn * xs[e] - off;
-          const long long P1 = ((long long)A * (long long)Rm) >> shp;
-          os[e] = (int16_t)norm_out128(P1, s_g[slot], ld_param(q, bcast ? 0u : 8u * w + e).bq, q.bq_sh, s_sc[slot]);
+          const long long x = AK ? (long long)((const int32_t*)&xv[k])[e] : (long long)((const int16_t*)&xv[k])[e];
+          const long long P1 = (long long)(((__int128)(nn * x - off) * (__int128)Rm) >> shp);
+          os[e] = (int16_t)norm_out128(P1, s_g[slot], ld_param(q, bcast ? 0u : EPW * w + e).bq, q.bq_sh, s_sc[slot]);
         }
       }
-      *(int4*)(rc + 16ull * w) = out;
+      if (AK) {
+        int2 o2;
+        memcpy(&o2, os, 8);
+        *(int2*)(rc + 8ull * w) = o2;
+      } else {
+        int4 o4;
+        memcpy(&o4, os, 16);
+        *(int4*)(rc + 16ull * w) = o4;
+      }
     }
+  }
+}
+
+// COPY / ADDX on int16 / int32 rows and MULACT on int16 rows, any parameter
+// block, n % 8 == 0: a thread per 8 elements (16- or 32-byte loads and
+// stores), the entries decoded once per CTA into shared memory.  The exact
+// sums of ro_rows in int64 when the job's shifts keep every term below 2^60
+// (checked per CTA over the block: ADDX |x| << sa, |y| << sb, Bq' << bq_sh,
+// no SCALE; MULACT sa <= 23, so |g << sa| < 2^38 and every product < 2^62),
+// else in 128 bits.
+template <int N_>
+__device__ __forceinline__ void ld8(const uint8_t* p, int kind, int64_t (&v)[N_]) {
+  if (kind == 0) {
+    const int4 w = *(const int4*)p;
+    const int16_t* s = (const int16_t*)&w;
+#pragma unroll
+    for (int e = 0; e < 8; e++) v[e] = s[e];
+  } else {
+    const int4 w0 = *(const int4*)p, w1 = *(const int4*)(p + 16);
+    const int32_t* s0 = (const int32_t*)&w0;
+    const int32_t* s1 = (const int32_t*)&w1;
+#pragma unroll
+    for (int e = 0; e < 4; e++) {
+      v[e] = s0[e];
+      v[4 + e] = s1[e];
+    }
+  }
+}
+
+template <int CODE, int AK, int BK, int CK>
+__global__ void __launch_bounds__(256) ro_stream_any(RoArgs q) {
+  extern __shared__ __align__(16) uint8_t ro_smem[];
+  const bool ben = (q.op >> 12) & 1u, relu = (q.op >> 15) & 1u, scale = (q.op >> 17) & 1u;
+  const bool bcast = (q.op >> 13) & 1u;
+  const uint32_t npar = bcast ? 1u : q.n;
+  int32_t* s_g = (int32_t*)ro_smem;
+  int32_t* s_bq = s_g + npar;
+  uint8_t* s_sa = (uint8_t*)(s_bq + npar);
+  uint8_t* s_sb = s_sa + npar;
+  uint8_t* s_sc = s_sb + npar;
+  __shared__ int s_max_sa, s_max_sb;
+  if (threadIdx.x == 0) s_max_sa = s_max_sb = 0;
+  __syncthreads();
+  for (uint32_t c = threadIdx.x; c < npar; c += blockDim.x) {
+    const Param pr = ld_param(q, c);
+    s_g[c] = pr.g;
+    s_bq[c] = pr.bq;
+    s_sa[c] = (uint8_t)pr.sa;
+    s_sb[c] = (uint8_t)pr.sb;
+    s_sc[c] = (uint8_t)pr.sc;
+    atomicMax(&s_max_sa, (int)pr.sa);
+    atomicMax(&s_max_sb, (int)pr.sb);
+  }
+  __syncthreads();
+  const int abits = AK ? 31 : 15, bbits = BK ? 31 : 15;
+  const bool fast = CODE == 4 ? s_max_sa <= 23
+                              : (!scale && abits + s_max_sa <= 60 && bbits + s_max_sb <= 60 && 21 + (int)q.bq_sh <= 60);
+  const uint32_t per = q.n >> 3;
+  const uint64_t total = (uint64_t)q.c1 * q.c2 * per;
+  for (uint64_t gi = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; gi < total; gi += (uint64_t)gridDim.x * blockDim.x) {
+    const uint64_t row = gi / per;
+    const uint32_t w = (uint32_t)(gi - row * per);
+    const uint32_t i1 = (uint32_t)(row % q.c1), i2 = (uint32_t)(row / q.c1);
+    int64_t x[8], y[8], r[8];
+    const bool zero_a = CODE != 4 && (i1 < q.win_lo || i1 >= q.win_hi);
+    if (zero_a) {
+#pragma unroll
+      for (int e = 0; e < 8; e++) x[e] = 0;
+    } else {
+      ld8(q.a + (uint64_t)i2 * q.a_s2 + (uint64_t)i1 * q.a_s1 + (AK ? 32ull : 16ull) * w, AK, x);
+    }
+    if (ben) {
+      ld8(q.b + (uint64_t)i2 * q.b_s2 + (uint64_t)i1 * q.b_s1 + (BK ? 32ull : 16ull) * w, BK, y);
+    } else {
+#pragma unroll
+      for (int e = 0; e < 8; e++) y[e] = 0;
+    }
+#pragma unroll
+    for (int e = 0; e < 8; e++) {
+      const uint32_t c = bcast ? 0u : 8u * w + e;
+      const int sa = s_sa[c], sb = s_sb[c], sc = s_sc[c];
+      if (CODE == 4) {  // MULACT: sat16(rne(silu_q(g << sa) u / 2^sh_c))
+        const int64_t gv = (int64_t)((uint64_t)x[e] << sa);
+        if (fast) {
+          const int64_t sl = corm_rne_shr64(gv * sig_q(gv, q.sig), 14 + 24 - 20);
+          r[e] = corm_sat16(corm_rne_shr64(sl * y[e], sc));
+        } else {
+          r[e] = corm_sat16_128(corm_rne_shr128((__int128)silu_q(gv, q.sig) * y[e], sc));
+        }
+      } else {
+        int64_t v;
+        if (fast) {
+          v = corm_rne_shr64((x[e] << sa) + (y[e] << sb) + ((int64_t)s_bq[c] << q.bq_sh), sc);
+          v = CK == 0 ? corm_sat16(v) : corm_sat32(v);
+        } else {
+          const __int128 s = ((__int128)x[e] << sa) + ((__int128)y[e] << sb) + ((__int128)s_bq[c] << q.bq_sh);
+          const __int128 t = corm_rne_shr128(scale ? s * (__int128)s_g[c] : s, sc);
+          v = CK == 0 ? corm_sat16_128(t) : corm_sat32_128(t);
+        }
+        r[e] = (relu && v < 0) ? 0 : v;
+      }
+    }
+    uint8_t* rc = q.c + (uint64_t)i2 * q.c_s2 + (uint64_t)i1 * q.c_s1;
+    if (CK == 0 || CODE == 4) {
+      int4 o;
+      int16_t* os = (int16_t*)&o;
+#pragma unroll
+      for (int e = 0; e < 8; e++) os[e] = (int16_t)r[e];
+      *(int4*)(rc + 16ull * w) = o;
+    } else {
+      int4 o0, o1;
+      int32_t* p0 = (int32_t*)&o0;
+      int32_t* p1 = (int32_t*)&o1;
+#pragma unroll
+      for (int e = 0; e < 4; e++) {
+        p0[e] = (int32_t)r[e];
+        p1[e] = (int32_t)r[4 + e];
+      }
+      *(int4*)(rc + 32ull * w) = o0;
+      *(int4*)(rc + 32ull * w + 16) = o1;
+    }
+  }
+}
+
+// ROPE over int16 rows of heads of HD (HD % 16 == 0, n % HD == 0): a thread
+// per 8 elements of one head half, 16-byte loads of x and of the partner half,
+// 32-byte loads of the cos / sin words of row B; x c << sa + rot(x) s << sb
+// exactly in int64 when every shift is at most 23 (|x c| <= 2^38), else in 128
+// bits; one RNE by sh_c, sat16.
+__global__ void __launch_bounds__(256) ro_rope_fast(RoArgs q) {
+  extern __shared__ __align__(16) uint8_t ro_smem[];
+  const bool bcast = (q.op >> 13) & 1u;
+  const uint32_t npar = bcast ? 1u : q.n;
+  uint8_t* s_sa = ro_smem;
+  uint8_t* s_sb = s_sa + npar;
+  uint8_t* s_sc = s_sb + npar;
+  __shared__ int s_max;
+  if (threadIdx.x == 0) s_max = 0;
+  __syncthreads();
+  for (uint32_t c = threadIdx.x; c < npar; c += blockDim.x) {
+    const Param pr = ld_param(q, c);
+    s_sa[c] = (uint8_t)pr.sa;
+    s_sb[c] = (uint8_t)pr.sb;
+    s_sc[c] = (uint8_t)pr.sc;
+    atomicMax(&s_max, (int)max(pr.sa, pr.sb));
+  }
+  __syncthreads();
+  const bool fast = s_max <= 23;
+  const uint32_t HD = q.aux & 0xFFFu, half = HD / 2u;
+  const uint32_t per = q.n >> 3;
+  const uint64_t total = (uint64_t)q.c1 * q.c2 * per;
+  for (uint64_t gi = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; gi < total; gi += (uint64_t)gridDim.x * blockDim.x) {
+    const uint64_t row = gi / per;
+    const uint32_t w = (uint32_t)(gi - row * per);
+    const uint32_t i1 = (uint32_t)(row % q.c1), i2 = (uint32_t)(row / q.c1);
+    const uint8_t* ra = q.a + (uint64_t)i2 * q.a_s2 + (uint64_t)i1 * q.a_s1;
+    const uint8_t* rb = q.b + (uint64_t)i2 * q.b_s2 + (uint64_t)i1 * q.b_s1;
+    const uint32_t c0 = 8u * w, d0 = c0 % HD;
+    const bool lo_half = d0 < half;
+    const int4 xw = *(const int4*)(ra + 2ull * c0);
+    const int4 pw = *(const int4*)(ra + 2ull * (lo_half ? c0 + half : c0 - half));
+    const int4 c_0 = *(const int4*)(rb + 4ull * d0), c_1 = *(const int4*)(rb + 4ull * d0 + 16);
+    const int4 s_0 = *(const int4*)(rb + 4ull * (HD + d0)), s_1 = *(const int4*)(rb + 4ull * (HD + d0) + 16);
+    const int16_t* xs = (const int16_t*)&xw;
+    const int16_t* ps = (const int16_t*)&pw;
+    int4 o;
+    int16_t* os = (int16_t*)&o;
+#pragma unroll
+    for (int e = 0; e < 8; e++) {
+      const uint32_t c = bcast ? 0u : c0 + e;
+      const int64_t cs = e < 4 ? ((const int32_t*)&c_0)[e] : ((const int32_t*)&c_1)[e - 4];
+      const int64_t sn = e < 4 ? ((const int32_t*)&s_0)[e] : ((const int32_t*)&s_1)[e - 4];
+      const int64_t x = xs[e], rot = lo_half ? -(int64_t)ps[e] : (int64_t)ps[e];
+      const int sa = s_sa[c], sb = s_sb[c], sc = s_sc[c];
+      if (fast)
+        os[e] = (int16_t)corm_sat16(corm_rne_shr64(((x * cs) << sa) + ((rot * sn) << sb), sc));
+      else
+        os[e] = (int16_t)corm_sat16_128(corm_rne_shr128(((__int128)(x * cs) << sa) + ((__int128)(rot * sn) << sb), sc));
+    }
+    *(int4*)(q.c + (uint64_t)i2 * q.c_s2 + (uint64_t)i1 * q.c_s1 + 2ull * c0) = o;
   }
 }
 
@@ -586,6 +785,33 @@ extern "C" int corm_rowops(const corm_rowops_desc* d, corm_stream_t stream) {
     }
     return corm::cuda_status("rowops stream");
   }
+  if (op == 6 && ak == 0 && bk == 1 && ck == 0 && !(d->b_s1 & 15u) && !(d->b_s2 & 15u)) {
+    // (HD % 16 == 0 and n % HD == 0 were checked above; the B rows 16-byte aligned)
+    const size_t smem = (((d->op >> 13) & 1u) ? 1u : d->n) * 3u;
+    corm::ProfScope prof_("ro_rope_fast", st);
+    ro_rope_fast<<<corm_blocks(rows * (d->n / 8), 256, 148u * 4u), 256, smem, st>>>(q);
+    return corm::cuda_status("rowops rope");
+  }
+  if (((op == 1 || op == 2) && ak <= 1 && bk <= 1 && ck <= 1 && d->n % 8 == 0) || (op == 4 && i16 && d->n % 8 == 0)) {
+    const size_t npar = bcast ? 1u : d->n;
+    const size_t smem = npar * 11u;  // n <= 4096: under 48 KB
+    const unsigned grid = corm_blocks(rows * (d->n / 8), 256, 148u * 4u);
+    auto launch = [&](auto kern) { kern<<<grid, 256, smem, st>>>(q); };
+    corm::ProfScope prof_(op == 4 ? "ro_mulact" : "ro_stream_any", st);
+    const int sel = op == 4 ? 8 : (int)(ak * 4 + bk * 2 + ck);
+    switch (sel) {
+      case 0: launch(ro_stream_any<2, 0, 0, 0>); break;
+      case 1: launch(ro_stream_any<2, 0, 0, 1>); break;
+      case 2: launch(ro_stream_any<2, 0, 1, 0>); break;
+      case 3: launch(ro_stream_any<2, 0, 1, 1>); break;
+      case 4: launch(ro_stream_any<2, 1, 0, 0>); break;
+      case 5: launch(ro_stream_any<2, 1, 0, 1>); break;
+      case 6: launch(ro_stream_any<2, 1, 1, 0>); break;
+      case 7: launch(ro_stream_any<2, 1, 1, 1>); break;
+      default: launch(ro_stream_any<4, 0, 0, 0>); break;
+    }
+    return corm::cuda_status("rowops stream");
+  }
   if (op == 7 && (d->aux & 15u) == 8u && d->n % 8 == 0 &&
       !((C | d->c_s1 | d->c_s2 | d->b_s2) & 15u) && !(d->b_s1 & 15u)) {
     const uint64_t units = (uint64_t)d->blocks * ((d->rows + XT - 1) / XT) * ((d->n + XD - 1) / XD);
@@ -595,9 +821,10 @@ extern "C" int corm_rowops(const corm_rowops_desc* d, corm_stream_t stream) {
     }
     return corm::cuda_status("rowops xpose");
   }
-  if (op == 5 && ak == 0 && d->n % 8 == 0) {
+  const bool ln = (d->op >> 16) & 1u;
+  if (op == 5 && d->n % 8 == 0 && ck == 0 && (ak == 0 || (ak == 1 && !ln && d->n <= 2048))) {
     {
-      corm::ProfScope prof_("ro_norm16", st);
+      corm::ProfScope prof_(ak ? "ro_norm32" : "ro_norm16", st);
       const unsigned grid = corm_blocks(rows, 8, 148u * 4u);
       const size_t npar = ((d->op >> 13) & 1u) ? 1u : d->n;
       const size_t smem = npar * 13u + 16u;  // n <= 4096: under 64 KB
@@ -605,12 +832,17 @@ extern "C" int corm_rowops(const corm_rowops_desc* d, corm_stream_t stream) {
         if (smem > 48u * 1024u) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         kern<<<grid, 256, smem, st>>>(q);
       };
-      if (d->n <= 1024)
-        launch(ro_norm16<4>);
-      else if (d->n <= 2048)
-        launch(ro_norm16<8>);
-      else
-        launch(ro_norm16<16>);
+      // 16-byte words per row: n / 8 (int16) or n / 4 (int32, n <= 2048), <= 32 NW_PER
+      const uint32_t words = ak ? d->n / 4u : d->n / 8u;
+      if (ak == 0) {
+        if (words <= 128) launch(ro_norm16<4, 0>);
+        else if (words <= 256) launch(ro_norm16<8, 0>);
+        else launch(ro_norm16<16, 0>);
+      } else {
+        if (words <= 128) launch(ro_norm16<4, 1>);
+        else if (words <= 256) launch(ro_norm16<8, 1>);
+        else launch(ro_norm16<16, 1>);
+      }
     }
     return corm::cuda_status("rowops norm");
   }

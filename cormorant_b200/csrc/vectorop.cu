@@ -321,6 +321,90 @@ __global__ void __launch_bounds__(256) smx_cols(SmxArgs p) {
   }
 }
 
+// Column mode with 16-byte loads and stores (size % 8 == 0, a_inc % 8 == 0,
+// 16-byte aligned a): tiles of 32 query columns staged transposed in shared
+// memory — query c's keys at s_x[base(c) + j], base(c) = c KP + 16 (c / 8),
+// the skew putting the four 8-column words of a key pair in distinct banks —
+// then a warp per query: the max, the sum of e and the P row, 8 keys per lane
+// per step.  Same arithmetic as smx_cols; CTAs walk the tiles (the TAB copied
+// into shared memory once per CTA).
+__device__ __forceinline__ uint32_t smx_tbase(uint32_t c, uint32_t KP) { return c * KP + 16u * (c >> 3); }
+
+__global__ void __launch_bounds__(256) smx_cols_t(SmxArgs p) {
+  extern __shared__ __align__(16) uint8_t smx_sm[];
+  int32_t* s_tab = (int32_t*)smx_sm;
+  int16_t* s_x = (int16_t*)(s_tab + 4096);
+  const uint32_t KP = p.size + 8u;
+  for (int i = threadIdx.x; i < 4096; i += 256) s_tab[i] = __ldg(p.tab + i);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t cm = p.cm, cs = p.cs;
+  const uint64_t rnd = 1ull << (39u - p.fp);
+  const uint32_t psh = 40u - p.fp;
+  const uint32_t tiles = (p.rows + 31u) / 32u;
+  for (uint32_t tile = blockIdx.x; tile < tiles; tile += gridDim.x) {
+    const uint32_t q0 = tile * 32u;
+    __syncthreads();  // the previous tile's reads (and the TAB copy) are done
+    for (uint32_t idx = threadIdx.x; idx < (p.size / 2u) * 4u; idx += 256u) {
+      const uint32_t jp = idx >> 2, part = idx & 3u;
+      if (q0 + 8u * part >= p.rows) continue;
+      const int16_t* src = p.a + (size_t)(2u * jp) * p.a_inc + q0 + 8u * part;
+      const int4 w0 = __ldg((const int4*)src), w1 = __ldg((const int4*)(src + p.a_inc));
+      const int16_t* v0 = (const int16_t*)&w0;
+      const int16_t* v1 = (const int16_t*)&w1;
+#pragma unroll
+      for (int e = 0; e < 8; e++) {
+        const uint32_t c = 8u * part + e;
+        *(uint32_t*)(s_x + smx_tbase(c, KP) + 2u * jp) = (uint32_t)(uint16_t)v0[e] | ((uint32_t)(uint16_t)v1[e] << 16);
+      }
+    }
+    __syncthreads();
+    for (uint32_t r = warp; r < 32u; r += 8u) {
+      const uint32_t q = q0 + r;
+      if (q >= p.rows) break;
+      const uint32_t v = smx_valid(q, p);
+      const int16_t* xs = s_x + smx_tbase(r, KP);
+      int32_t m = INT32_MIN;
+      for (uint32_t j0 = 8u * lane; j0 < v; j0 += 256u) {
+        const int4 w = *(const int4*)(xs + j0);
+        const int16_t* t8 = (const int16_t*)&w;
+#pragma unroll
+        for (int e = 0; e < 8; e++)
+          if (j0 + e < v) m = max(m, (int32_t)t8[e]);
+      }
+      m = warp_reduce_max<32>(m);
+      uint32_t S = 0;
+      for (uint32_t j0 = 8u * lane; j0 < v; j0 += 256u) {
+        const int4 w = *(const int4*)(xs + j0);
+        const int16_t* t8 = (const int16_t*)&w;
+#pragma unroll
+        for (int e = 0; e < 8; e++)
+          if (j0 + e < v) S += smx_e32(m, t8[e], cm, cs, s_tab);
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) S += __shfl_xor_sync(0xffffffffu, S, o);
+      const uint32_t R = S > 0 ? (uint32_t)((1ull << 40) / S) : 0u;
+      int16_t* out = p.c + (size_t)q * p.b_inc;
+      const uint32_t lim = (q + 1 == p.rows) ? p.W : min(p.W, max(p.b_inc, p.size));
+      const bool oa = ((uintptr_t)out & 15) == 0;
+      for (uint32_t j0 = 8u * lane; j0 < lim; j0 += 256u) {
+        alignas(16) int16_t o8[8];
+        const int4 w = *(const int4*)(xs + j0);
+        const int16_t* t8 = (const int16_t*)&w;
+#pragma unroll
+        for (int e = 0; e < 8; e++)
+          o8[e] = (j0 + e < v) ? smx_p32(smx_e32(m, t8[e], cm, cs, s_tab), R, rnd, psh) : (int16_t)0;
+        if (oa && j0 + 8 <= lim) {
+          *(int4*)(out + j0) = *(int4*)o8;
+        } else {
+#pragma unroll
+          for (int e = 0; e < 8; e++)
+            if (j0 + e < lim) out[j0 + e] = o8[e];
+        }
+      }
+    }
+  }
+}
+
 // CTAs for a persistent row-mode launch: at most 8 per SM
 unsigned smx_grid(uint64_t groups) { return (unsigned)(groups < 148u * 8u ? (groups ? groups : 1) : 148u * 8u); }
 
@@ -343,6 +427,16 @@ int launch_softmax(const corm_vectorop_desc* d, cudaStream_t st, const corm::Dev
   if (p.rows == 0) return CORM_OK;
   if (p.rows > 1 && p.b_inc < p.size)
     return corm::fail(CORM_EINVAL, "softmax: output rows overlap (b_inc %u < size %u)", p.b_inc, p.size);
+  if (col && d->size % 8 == 0 && d->size <= 2048 && d->a_inc % 8 == 0 && !((uintptr_t)d->a & 15u)) {
+    const size_t smem = 4096 * sizeof(int32_t) + (32 * ((size_t)d->size + 8) + 16 * 4) * sizeof(int16_t);
+    cudaFuncSetAttribute(smx_cols_t, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    const uint32_t tiles = (p.rows + 31) / 32;
+    {
+      corm::ProfScope prof_("smx_cols_t", st);
+      smx_cols_t<<<tiles < 148u * 4u ? tiles : 148u * 4u, 256, smem, st>>>(p);
+    }
+    return corm::cuda_status("softmax_cols");
+  }
   if (col) {
     const size_t smem = (size_t)d->size * 16 * sizeof(int16_t);
     if (smem > 200 * 1024) return corm::fail(CORM_ELIMIT, "softmax column mode: %u keys beyond 6400", d->size);

@@ -295,6 +295,9 @@ class GpuSimulator:
         device states (``states_to_device``), updated in place; host int
         inputs (pos, n) are numpy arrays."""
         raw: Dict[str, torch.Tensor] = dict(raw_inputs)
+        # lean mode: a tensor outside ``keep`` is never observed, so parts no
+        # reader takes (the scores / P past the key count) need not be zeroed
+        self._observed = None if keep is None else set(keep)
         snames = {t.onnx_name for t in self._graph.state_tensors}
         if snames:
             if states is None:
@@ -535,6 +538,11 @@ class GpuSimulator:
         return y
 
     # ------------------------------------------------------------ prefill attention
+    def _seen(self, t) -> bool:
+        """Whether the pass returns tensor t (every tensor outside lean mode)."""
+        obs = getattr(self, "_observed", None)
+        return obs is None or t.onnx_name in obs
+
     @staticmethod
     def _host_int(get, t) -> int:
         return int(np.asarray(get(t)).reshape(-1)[0])
@@ -611,7 +619,7 @@ class GpuSimulator:
             self._ws = ops.gemm_strided(w[(g * B * C + r0) * HD:], x[g * B * HD * GT:], y, n=rows, k=HD, m=GT, batch=B,
                              lda=HD, ldb=GT, ldc=B * GT, a_batch_stride=C * HD, b_batch_stride=HD * GT,
                              c_batch_stride=GT, flags=F_WRAP32, workspace=self._ws)
-            if not sn.nr and keys < C:
+            if not sn.nr and keys < C and self._seen(sn.output):
                 y[keys * B * GT:C * B * GT].zero_()
             return y
         self._ws = ops.gemm_strided(w, x[g * B * C * HD:], y, n=GT, k=keys, m=HD, batch=B, lda=C, ldb=HD, ldc=HD,
@@ -636,7 +644,7 @@ class GpuSimulator:
             mask = max(min(keys, pos + n) - int(bool(sn.prefix_lm)), 1) & 0xFFFF
         s = get(sn.inputs[0])
         y = self._alloc(sn.output.numel)
-        if keys < C:
+        if keys < C and self._seen(sn.output):
             y.zero_()
         regs = [(int(sn.cm[h]), int(sn.cfg[h])) for h in range(G)]
         if all(r == regs[0] for r in regs):

@@ -118,3 +118,101 @@ def test_norm16(ops, n, ln, bcast):
                 eps=int(rng.integers(0, 1 << 20)), bq_sh=int(rng.integers(0, 30)))
     got, want = _run(ops, mem, offs, regs)
     assert np.array_equal(got, want)
+
+
+def _params(rng, n, bcast, **ranges):
+    """n (or one) random entries; ranges: field -> (lo, hi)."""
+    out = []
+    for _ in range(1 if bcast else n):
+        f = {k: int(rng.integers(lo, hi)) for k, (lo, hi) in ranges.items()}
+        out.append(_pentry(**f))
+    return np.concatenate(out)
+
+
+@pytest.mark.parametrize("n", [8, 960, 2048])
+@pytest.mark.parametrize("bcast", [False, True])
+@pytest.mark.parametrize("small", [False, True])
+def test_norm32_rms(ops, n, bcast, small):
+    """NORM (RMS) on int32 rows (the LLM residual): ro_norm16<., 1>."""
+    rng = np.random.default_rng(n + 2 * bcast + small)
+    rows, blocks = 4, 2
+    a_s1 = 4 * n + 16
+    a_s2 = a_s1 * rows
+    c_s1, c_s2 = 2 * n, 2 * n * rows + 32
+    p = _params(rng, n, bcast, g=(1, 1 << 30), bq=(-(1 << 21), 1 << 21), sc=(24, 50))
+    mem, offs = _image(rng, a_s2 * blocks, 16, p, c_s2 * blocks)
+    if small:  # residual-like values
+        vals = rng.integers(-(1 << 20), 1 << 20, a_s2 * blocks // 4).astype("<i4")
+        mem[offs["a"]:offs["a"] + a_s2 * blocks] = vals.view(np.uint8)
+    op = 5 | (1 << 4) | (spec.F_P_BCAST if bcast else 0)
+    regs = dict(op=op, n=n, rows=rows, blocks=blocks, a_s1=a_s1, a_s2=a_s2, c_s1=c_s1, c_s2=c_s2,
+                eps=int(rng.integers(0, 1 << 40)), bq_sh=int(rng.integers(0, 30)))
+    got, want = _run(ops, mem, offs, regs)
+    assert np.array_equal(got, want)
+
+
+KINDS = [(ak, bk, ck) for ak in (0, 1) for bk in (0, 1) for ck in (0, 1)]
+
+
+@pytest.mark.parametrize("kinds", KINDS)
+@pytest.mark.parametrize("variant", ["small", "wide", "relu_window", "scale"])
+def test_stream_any(ops, kinds, variant):
+    """COPY / ADDX on int16 / int32 rows with per-column entries
+    (ro_stream_any): int64 shifts, the 128-bit fallback (wide shifts,
+    SCALE), RELU and the row window."""
+    ak, bk, ck = kinds
+    rng = np.random.default_rng(sum(k << i for i, k in enumerate(kinds)) + 17 * len(variant))
+    n, rows, blocks = 96, 5, 2
+    nb = lambda k: 2 if k == 0 else 4  # noqa: E731
+    a_s1, b_s1, c_s1 = nb(ak) * n + 16, nb(bk) * n + 32, nb(ck) * n
+    a_s2, b_s2, c_s2 = a_s1 * rows, b_s1 * rows + 16, c_s1 * rows + 48
+    sh = dict(small=(0, 12), wide=(20, 40), relu_window=(0, 6), scale=(0, 4))[variant]
+    p = _params(rng, n, False, g=(-(1 << 20), 1 << 20), bq=(-(1 << 21), 1 << 21), sa=sh, sb=sh, sc=(0, 30))
+    mem, offs = _image(rng, a_s2 * blocks, b_s2 * blocks, p, c_s2 * blocks)
+    op = 2 | (ak << 4) | (bk << 6) | (ck << 8) | spec.F_B_EN
+    if variant == "relu_window":
+        op |= spec.F_RELU
+    if variant == "scale":
+        op |= spec.F_SCALE
+    win = (1, 4) if variant == "relu_window" else (0, 0xFFFFFFFF)
+    regs = dict(op=op, n=n, rows=rows, blocks=blocks, a_s1=a_s1, a_s2=a_s2, b_s1=b_s1, b_s2=b_s2, c_s1=c_s1,
+                c_s2=c_s2, bq_sh=int(rng.integers(0, 20)), win_lo=win[0], win_hi=win[1])
+    got, want = _run(ops, mem, offs, regs)
+    assert np.array_equal(got, want)
+
+
+@pytest.mark.parametrize("bcast", [False, True])
+@pytest.mark.parametrize("sa_hi", [9, 30])
+def test_mulact_fast(ops, bcast, sa_hi):
+    """MULACT (SiLU(g) u) on int16 rows: int64 path (sa <= 23) and the
+    128-bit fallback."""
+    rng = np.random.default_rng(5 + bcast + sa_hi)
+    n, rows, blocks = 2560 // 4, 3, 2
+    s1 = 2 * n + 16
+    p = _params(rng, n, bcast, sa=(0, sa_hi), sc=(10, 30))
+    mem, offs = _image(rng, s1 * rows * blocks, s1 * rows * blocks, p, 2 * n * rows * blocks)
+    op = 4 | spec.F_B_EN | (spec.F_P_BCAST if bcast else 0)
+    regs = dict(op=op, n=n, rows=rows, blocks=blocks, a_s1=s1, a_s2=s1 * rows, b_s1=s1, b_s2=s1 * rows,
+                c_s1=2 * n, c_s2=2 * n * rows)
+    got, want = _run(ops, mem, offs, regs)
+    assert np.array_equal(got, want)
+
+
+@pytest.mark.parametrize("HD,heads", [(64, 15), (128, 2), (16, 3)])
+@pytest.mark.parametrize("bcast,sh_hi", [(False, 4), (True, 3), (False, 40)])
+def test_rope_fast(ops, HD, heads, bcast, sh_hi):
+    """ROPE on int16 rows (ro_rope_fast): cos / sin rows of 2 HD int24 words,
+    per-column or broadcast shifts, the 128-bit fallback for shifts > 23."""
+    rng = np.random.default_rng(HD + heads + sh_hi)
+    n, rows, blocks = HD * heads, 6, 2
+    a_s1 = 2 * n + 16
+    b_s1 = 8 * HD
+    p = _params(rng, n, bcast, sa=(0, sh_hi), sb=(0, sh_hi), sc=(20, 50))
+    cs = rng.integers(-(1 << 23), (1 << 23) + 1, (rows, 2 * HD)).astype("<i4").view(np.uint8).reshape(-1)
+    mem, offs = _image(rng, a_s1 * rows * blocks, b_s1 * rows, p, 2 * n * rows * blocks)
+    mem[offs["b"]:offs["b"] + cs.size] = cs
+    op = 6 | (1 << 6) | spec.F_B_EN | (spec.F_P_BCAST if bcast else 0)
+    regs = dict(op=op, n=n, rows=rows, blocks=blocks, a_s1=a_s1, a_s2=a_s1 * rows, b_s1=b_s1, b_s2=0,
+                c_s1=2 * n, c_s2=2 * n * rows, aux=HD)
+    got, want = _run(ops, mem, offs, regs)
+    assert np.array_equal(got, want)
