@@ -74,6 +74,13 @@ __device__ __forceinline__ int64_t corm_rne_shr64(int64_t x, int k) {
   int64_t half = (int64_t)1 << (k - 1);
   return q + ((r > half || (r == half && (q & 1))) ? 1 : 0);
 }
+// the same for |x| < 2^62, 0 <= k <= 63, without the remainder: adding
+// 2^(k-1) - 1 plus the parity of floor(x / 2^k) carries into the quotient
+// exactly when the remainder is above half, or equal to it with an odd quotient
+__device__ __forceinline__ int64_t corm_rne_shr64f(int64_t x, int k) {
+  if (k == 0) return x;
+  return (x + ((int64_t)1 << (k - 1)) - 1 + ((x >> k) & 1)) >> k;
+}
 __device__ __forceinline__ int64_t corm_sat16_128(__int128 x) {
   return x > 32767 ? 32767 : (x < -32768 ? -32768 : (int64_t)x);
 }

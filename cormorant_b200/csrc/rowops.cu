@@ -301,6 +301,8 @@ __global__ void __launch_bounds__(256) ro_stream16(RoArgs q) {
   const bool ben = (q.op >> 12) & 1u, relu = (q.op >> 15) & 1u, scale = (q.op >> 17) & 1u;
   const Param pr = ld_param(q, 0);
   const bool ident = pr.sa == 0 && pr.sb == 0 && pr.sc == 0 && pr.bq == 0 && !scale;
+  // every term below 2^60: the exact sum in int64
+  const bool wide64 = !scale && pr.sa <= 45u && pr.sb <= 45u && q.bq_sh <= 39u;
   const uint32_t per = q.n >> 3;
   const uint64_t total = (uint64_t)q.c1 * q.c2 * per;
   const bool small = total < (1ull << 32);  // 32-bit index arithmetic
@@ -331,6 +333,9 @@ __global__ void __launch_bounds__(256) ro_stream16(RoArgs q) {
       if (ident) {
         const int32_t v = (int32_t)xs[e] + (int32_t)ys[e];
         r = v > 32767 ? 32767 : (v < -32768 ? -32768 : v);
+      } else if (wide64) {
+        r = corm_sat16(corm_rne_shr64f(((int64_t)xs[e] << pr.sa) + ((int64_t)ys[e] << pr.sb) +
+                                      ((int64_t)pr.bq << q.bq_sh), (int)pr.sc));
       } else {
         const __int128 sum = ((__int128)xs[e] << pr.sa) + ((__int128)ys[e] << pr.sb) + ((__int128)pr.bq << q.bq_sh);
         r = corm_sat16_128(corm_rne_shr128(scale ? sum * (__int128)pr.g : sum, (int)pr.sc));
@@ -401,7 +406,7 @@ __device__ __noinline__ int64_t norm_out128(long long P1, int64_t g, int32_t bq,
 }
 
 template <int NW_PER, int AK>
-__global__ void __launch_bounds__(256) ro_norm16(RoArgs q) {
+__global__ void __launch_bounds__(256, 2) ro_norm16(RoArgs q) {
   constexpr uint32_t EPW = AK ? 4u : 8u;  // elements per 16-byte word of A
   extern __shared__ __align__(16) uint8_t ro_smem[];
   const bool ln = (q.op >> 16) & 1u;
@@ -447,12 +452,13 @@ __global__ void __launch_bounds__(256) ro_norm16(RoArgs q) {
         xv[k] = *(const int4*)(ra + 16ull * w);
 #pragma unroll
         for (int e = 0; e < (int)EPW; e++) {
-          const long long x = AK ? (long long)((const int32_t*)&xv[k])[e] : (long long)((const int16_t*)&xv[k])[e];
+          const int32_t xi = AK ? ((const int32_t*)&xv[k])[e] : (int32_t)((const int16_t*)&xv[k])[e];
+          const long long x = xi;
           s1 += x;
           if (AK)
-            s2w += (unsigned __int128)(x * x);
+            s2w += (unsigned long long)((long long)xi * xi);  // a 32 x 32 -> 64-bit product
           else
-            s2 += x * x;  // each square < 2^30
+            s2 += (long long)(xi * xi);  // each square < 2^30
           xmax = max(xmax, x);
           xmin = min(xmin, x);
         }
@@ -493,10 +499,11 @@ __global__ void __launch_bounds__(256) ro_norm16(RoArgs q) {
 #pragma unroll
         for (int e = 0; e < (int)EPW; e++) {
           const uint32_t slot = bcast ? 0u : (uint32_t)e * words + w;
-          const long long x = AK ? (long long)((const int32_t*)&xv[k])[e] : (long long)((const int16_t*)&xv[k])[e];
-          const long long A = nn * x - off;
-          const long long P1 = (A * (long long)Rm) >> shp;  // |A Rm| < 2^63 (int32 rows: |A| <= 2^31)
-          const long long v = P1 * s_g[slot] + s_bq[slot];
+          const int32_t xi = AK ? ((const int32_t*)&xv[k])[e] : (int32_t)((const int16_t*)&xv[k])[e];
+          // int32 rows (RMS): A = x; |A Rm| < 2^63
+          const long long A = AK ? (long long)xi : nn * xi - off;
+          const long long P1 = (AK ? (long long)xi * (long long)(uint32_t)Rm : A * (long long)Rm) >> shp;
+          const long long v = (long long)(int32_t)P1 * s_g[slot] + s_bq[slot];  // |P1| < 2^31 on this path
           const int sc = s_sc[slot];
           const long long qv = v >> sc, rr = v - (qv << sc), half = 1ll << (sc - 1);
           const long long y = qv + ((rr > half) | ((rr == half) & (qv & 1)));
@@ -604,15 +611,28 @@ __global__ void __launch_bounds__(256) ro_stream_any(RoArgs q) {
       if (CODE == 4) {  // MULACT: sat16(rne(silu_q(g << sa) u / 2^sh_c))
         const int64_t gv = (int64_t)((uint64_t)x[e] << sa);
         if (fast) {
-          const int64_t sl = corm_rne_shr64(gv * sig_q(gv, q.sig), 14 + 24 - 20);
-          r[e] = corm_sat16(corm_rne_shr64(sl * y[e], sc));
+          // |g| >= 16 at 2^-14: sigma is 1 or 0 and silu_q(g) = 64 g or 0;
+          // below, g, the table step and silu_q(g) fit 32 bits
+          int64_t sl;
+          if (gv >= ((int64_t)16 << 14) || gv <= -((int64_t)16 << 14)) {
+            sl = gv > 0 ? gv * 64 : 0;
+          } else {
+            const int32_t g32 = (int32_t)gv;
+            const uint32_t a = (uint32_t)(g32 < 0 ? -g32 : g32);
+            const uint64_t ent = __ldg(q.sig + (a >> 6));
+            const uint32_t t = (uint32_t)ent & 0x1FFFFFFu, dl = (uint32_t)(ent >> 25) & 0xFFFFFFu;
+            uint32_t sg = t + ((dl * (a & 63u)) >> 6);
+            if (g32 < 0) sg = (1u << 24) - sg;
+            sl = corm_rne_shr64f((int64_t)g32 * (int64_t)(int32_t)sg, 14 + 24 - 20);
+          }
+          r[e] = corm_sat16(corm_rne_shr64f(sl * y[e], sc));
         } else {
           r[e] = corm_sat16_128(corm_rne_shr128((__int128)silu_q(gv, q.sig) * y[e], sc));
         }
       } else {
         int64_t v;
         if (fast) {
-          v = corm_rne_shr64((x[e] << sa) + (y[e] << sb) + ((int64_t)s_bq[c] << q.bq_sh), sc);
+          v = corm_rne_shr64f((x[e] << sa) + (y[e] << sb) + ((int64_t)s_bq[c] << q.bq_sh), sc);
           v = CK == 0 ? corm_sat16(v) : corm_sat32(v);
         } else {
           const __int128 s = ((__int128)x[e] << sa) + ((__int128)y[e] << sb) + ((__int128)s_bq[c] << q.bq_sh);
@@ -647,8 +667,8 @@ __global__ void __launch_bounds__(256) ro_stream_any(RoArgs q) {
 // ROPE over int16 rows of heads of HD (HD % 16 == 0, n % HD == 0): a thread
 // per 8 elements of one head half, 16-byte loads of x and of the partner half,
 // 32-byte loads of the cos / sin words of row B; x c << sa + rot(x) s << sb
-// exactly in int64 when every shift is at most 23 (|x c| <= 2^38), else in 128
-// bits; one RNE by sh_c, sat16.
+// exactly in int64 when every shift is at most 22 (|x c| <= 2^38), else in 128
+// bits (shifts above 22); one RNE by sh_c, sat16.
 __global__ void __launch_bounds__(256) ro_rope_fast(RoArgs q) {
   extern __shared__ __align__(16) uint8_t ro_smem[];
   const bool bcast = (q.op >> 13) & 1u;
@@ -667,7 +687,7 @@ __global__ void __launch_bounds__(256) ro_rope_fast(RoArgs q) {
     atomicMax(&s_max, (int)max(pr.sa, pr.sb));
   }
   __syncthreads();
-  const bool fast = s_max <= 23;
+  const bool fast = s_max <= 22;  // each product below 2^60 after its shift
   const uint32_t HD = q.aux & 0xFFFu, half = HD / 2u;
   const uint32_t per = q.n >> 3;
   const uint64_t total = (uint64_t)q.c1 * q.c2 * per;
@@ -695,7 +715,7 @@ __global__ void __launch_bounds__(256) ro_rope_fast(RoArgs q) {
       const int64_t x = xs[e], rot = lo_half ? -(int64_t)ps[e] : (int64_t)ps[e];
       const int sa = s_sa[c], sb = s_sb[c], sc = s_sc[c];
       if (fast)
-        os[e] = (int16_t)corm_sat16(corm_rne_shr64(((x * cs) << sa) + ((rot * sn) << sb), sc));
+        os[e] = (int16_t)corm_sat16(corm_rne_shr64f(((x * cs) << sa) + ((rot * sn) << sb), sc));
       else
         os[e] = (int16_t)corm_sat16_128(corm_rne_shr128(((__int128)(x * cs) << sa) + ((__int128)(rot * sn) << sb), sc));
     }

@@ -128,6 +128,7 @@ struct SmxArgs {
   uint32_t size, rows, a_inc, b_inc, W;
   uint32_t cm, cs, fp, valid0, period;
   const int32_t* tab;
+  uint32_t cm8, csm8;  // cm << 8 and cs - 8 (the 32-bit path, 8 <= cs <= 39)
 };
 
 __device__ __forceinline__ uint32_t smx_valid(uint32_t q, const SmxArgs& p) {
@@ -181,12 +182,34 @@ __device__ __forceinline__ int16_t smx_p32(uint32_t e, uint32_t R, uint64_t rnd,
   return (int16_t)(q > 32767u ? 32767u : q);
 }
 
+// The same two steps in 32-bit halves when 8 <= Cs <= 39 and 40 - f_p < 32
+// (FC): y = floor(d Cm / 2^Cs) = umulhi(d 2^16, Cm 2^8) >> (Cs - 8) for
+// d = m - x < 2^16 and Cm < 2^24 (both factors below 2^32, the high word is
+// floor(d Cm / 2^8)); P = (e R + 2^(sh-1)) >> sh by a funnel shift (e R <
+// 2^41, sh >= 9: the quotient fits 32 bits).
+template <bool FC>
+__device__ __forceinline__ uint32_t smx_e(int32_t m, int32_t x, const SmxArgs& p, const int32_t* tab) {
+  if (!FC) return smx_e32(m, x, p.cm, p.cs, tab);
+  const uint32_t y = __umulhi((uint32_t)(m - x) << 16, p.cm8) >> p.csm8;
+  const uint32_t yc = min(y, (17u << 12) - 1u);
+  const uint32_t e = (uint32_t)tab[yc & 4095u] >> (yc >> 12);
+  return y >= (17u << 12) ? 0u : e;
+}
+
+template <bool FC>
+__device__ __forceinline__ int16_t smx_pq(uint32_t e, uint32_t R, uint64_t rnd, uint32_t sh) {
+  if (!FC) return smx_p32(e, R, rnd, sh);
+  const uint64_t t = (uint64_t)e * R + rnd;
+  const uint32_t q = __funnelshift_r((uint32_t)t, (uint32_t)(t >> 32), sh);
+  return (int16_t)min(q, 32767u);
+}
+
 // Row mode, GROUP threads per row (16 / 32: a part of a warp per row; 256 /
 // 1024: a CTA per row), PER elements per thread held in registers as PER / 8
 // runs of 8 consecutive elements (16-byte loads and stores where the row
 // allows).  The TAB is copied into shared memory once per CTA; CTAs then walk
 // row groups.
-template <int GROUP, int PER>
+template <int GROUP, int PER, bool FC>
 __global__ void __launch_bounds__(GROUP >= 256 ? GROUP : 256) smx_rows(SmxArgs p) {
   constexpr int NT = GROUP >= 256 ? GROUP : 256;
   constexpr int ROWS_PER_CTA = NT / GROUP;
@@ -198,7 +221,6 @@ __global__ void __launch_bounds__(GROUP >= 256 ? GROUP : 256) smx_rows(SmxArgs p
   __syncthreads();
   const int lane_in_group = threadIdx.x % GROUP;
   const int group = threadIdx.x / GROUP;
-  const uint32_t cm = p.cm, cs = p.cs;
   const uint64_t rnd = 1ull << (39u - p.fp);
   const uint32_t psh = 40u - p.fp;
   const uint32_t ngroups = (p.rows + ROWS_PER_CTA - 1) / ROWS_PER_CTA;
@@ -236,7 +258,7 @@ __global__ void __launch_bounds__(GROUP >= 256 ? GROUP : 256) smx_rows(SmxArgs p
 #pragma unroll
     for (int t = 0; t < PER; t++) {  // xv becomes e (<= 65536) in place
       const uint32_t j = ((t / 8) * GROUP + lane_in_group) * 8 + (t % 8);
-      xv[t] = (live && j < v) ? (int32_t)smx_e32(m, xv[t], cm, cs, s_tab) : 0;
+      xv[t] = (live && j < v) ? (int32_t)smx_e<FC>(m, xv[t], p, s_tab) : 0;
       S += (uint32_t)xv[t];
     }
 #pragma unroll
@@ -258,7 +280,7 @@ __global__ void __launch_bounds__(GROUP >= 256 ? GROUP : 256) smx_rows(SmxArgs p
       const uint32_t j0 = (q * GROUP + lane_in_group) * 8;
       alignas(16) int16_t o8[8];
 #pragma unroll
-      for (int e = 0; e < 8; e++) o8[e] = (j0 + e < v) ? smx_p32((uint32_t)xv[q * 8 + e], R, rnd, psh) : (int16_t)0;
+      for (int e = 0; e < 8; e++) o8[e] = (j0 + e < v) ? smx_pq<FC>((uint32_t)xv[q * 8 + e], R, rnd, psh) : (int16_t)0;
       if (oa && j0 + 8 <= lim) {
         *(int4*)(out + j0) = *(int4*)o8;
       } else {
@@ -325,11 +347,13 @@ __global__ void __launch_bounds__(256) smx_cols(SmxArgs p) {
 // 16-byte aligned a): tiles of 32 query columns staged transposed in shared
 // memory — query c's keys at s_x[base(c) + j], base(c) = c KP + 16 (c / 8),
 // the skew putting the four 8-column words of a key pair in distinct banks —
-// then a warp per query: the max, the sum of e and the P row, 8 keys per lane
-// per step.  Same arithmetic as smx_cols; CTAs walk the tiles (the TAB copied
+// then 8 lanes per query (4 queries per warp), each lane taking WPL words of
+// 8 keys for the max, the sum and the P row (held in registers with their e
+// values while STORE_E, else read again from shared memory and e recomputed).  Same arithmetic as smx_cols; CTAs walk the tiles (the TAB copied
 // into shared memory once per CTA).
 __device__ __forceinline__ uint32_t smx_tbase(uint32_t c, uint32_t KP) { return c * KP + 16u * (c >> 3); }
 
+template <int WPL, bool STORE_E, bool FC>
 __global__ void __launch_bounds__(256) smx_cols_t(SmxArgs p) {
   extern __shared__ __align__(16) uint8_t smx_sm[];
   int32_t* s_tab = (int32_t*)smx_sm;
@@ -337,7 +361,6 @@ __global__ void __launch_bounds__(256) smx_cols_t(SmxArgs p) {
   const uint32_t KP = p.size + 8u;
   for (int i = threadIdx.x; i < 4096; i += 256) s_tab[i] = __ldg(p.tab + i);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const uint32_t cm = p.cm, cs = p.cs;
   const uint64_t rnd = 1ull << (39u - p.fp);
   const uint32_t psh = 40u - p.fp;
   const uint32_t tiles = (p.rows + 31u) / 32u;
@@ -358,41 +381,70 @@ __global__ void __launch_bounds__(256) smx_cols_t(SmxArgs p) {
       }
     }
     __syncthreads();
-    for (uint32_t r = warp; r < 32u; r += 8u) {
-      const uint32_t q = q0 + r;
-      if (q >= p.rows) break;
-      const uint32_t v = smx_valid(q, p);
-      const int16_t* xs = s_x + smx_tbase(r, KP);
-      int32_t m = INT32_MIN;
-      for (uint32_t j0 = 8u * lane; j0 < v; j0 += 256u) {
-        const int4 w = *(const int4*)(xs + j0);
-        const int16_t* t8 = (const int16_t*)&w;
+    // a warp per 4 queries, 8 lanes per query, WPL words of 8 keys per lane
+    const uint32_t r = (uint32_t)warp * 4u + ((uint32_t)lane >> 3), sl = (uint32_t)lane & 7u;
+    const uint32_t q = q0 + r;
+    const bool live = q < p.rows;
+    const uint32_t v = live ? smx_valid(q, p) : 0u;
+    const int16_t* xs = s_x + smx_tbase(r, KP);
+    int4 xw[STORE_E ? WPL : 1];
+    int32_t m = INT32_MIN;
+#pragma unroll(STORE_E ? WPL : 1)
+    for (int k = 0; k < WPL; k++) {
+      const uint32_t j0 = 8u * (sl + 8u * k);
+      const int4 w = j0 < p.size ? *(const int4*)(xs + j0) : make_int4(0, 0, 0, 0);
+      if constexpr (STORE_E) xw[k] = w;
+      const int16_t* t8 = (const int16_t*)&w;
 #pragma unroll
-        for (int e = 0; e < 8; e++)
-          if (j0 + e < v) m = max(m, (int32_t)t8[e]);
+      for (int e = 0; e < 8; e++)
+        if (j0 + e < v) m = max(m, (int32_t)t8[e]);
+    }
+    m = warp_reduce_max<8>(m);
+    uint32_t ev[STORE_E ? WPL * 8 : 1];
+    uint32_t S = 0;
+#pragma unroll(STORE_E ? WPL : 1)
+    for (int k = 0; k < WPL; k++) {
+      const uint32_t j0 = 8u * (sl + 8u * k);
+      int4 w;
+      if constexpr (STORE_E)
+        w = xw[k];
+      else
+        w = j0 < p.size ? *(const int4*)(xs + j0) : make_int4(0, 0, 0, 0);
+      const int16_t* t8 = (const int16_t*)&w;
+#pragma unroll
+      for (int e = 0; e < 8; e++) {
+        const uint32_t ee = (j0 + e < v) ? smx_e<FC>(m, t8[e], p, s_tab) : 0u;
+        if constexpr (STORE_E) ev[k * 8 + e] = ee;
+        S += ee;
       }
-      m = warp_reduce_max<32>(m);
-      uint32_t S = 0;
-      for (uint32_t j0 = 8u * lane; j0 < v; j0 += 256u) {
-        const int4 w = *(const int4*)(xs + j0);
-        const int16_t* t8 = (const int16_t*)&w;
+    }
 #pragma unroll
-        for (int e = 0; e < 8; e++)
-          if (j0 + e < v) S += smx_e32(m, t8[e], cm, cs, s_tab);
-      }
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) S += __shfl_xor_sync(0xffffffffu, S, o);
+    for (int o = 4; o > 0; o >>= 1) S += __shfl_xor_sync(0xffffffffu, S, o);
+    if (live) {
       const uint32_t R = S > 0 ? (uint32_t)((1ull << 40) / S) : 0u;
       int16_t* out = p.c + (size_t)q * p.b_inc;
       const uint32_t lim = (q + 1 == p.rows) ? p.W : min(p.W, max(p.b_inc, p.size));
       const bool oa = ((uintptr_t)out & 15) == 0;
-      for (uint32_t j0 = 8u * lane; j0 < lim; j0 += 256u) {
-        alignas(16) int16_t o8[8];
-        const int4 w = *(const int4*)(xs + j0);
+#pragma unroll(STORE_E ? WPL : 1)
+      for (int k = 0; k < WPL; k++) {
+        const uint32_t j0 = 8u * (sl + 8u * k);
+        if (j0 >= lim) break;
+        int4 w;
+        if constexpr (STORE_E)
+          w = xw[k];
+        else
+          w = *(const int4*)(xs + j0);
         const int16_t* t8 = (const int16_t*)&w;
+        alignas(16) int16_t o8[8];
 #pragma unroll
-        for (int e = 0; e < 8; e++)
-          o8[e] = (j0 + e < v) ? smx_p32(smx_e32(m, t8[e], cm, cs, s_tab), R, rnd, psh) : (int16_t)0;
+        for (int e = 0; e < 8; e++) {
+          uint32_t ee;
+          if constexpr (STORE_E)
+            ee = ev[k * 8 + e];
+          else
+            ee = (j0 + e < v) ? smx_e<FC>(m, t8[e], p, s_tab) : 0u;
+          o8[e] = (j0 + e < v) ? smx_pq<FC>(ee, R, rnd, psh) : (int16_t)0;
+        }
         if (oa && j0 + 8 <= lim) {
           *(int4*)(out + j0) = *(int4*)o8;
         } else {
@@ -408,6 +460,14 @@ __global__ void __launch_bounds__(256) smx_cols_t(SmxArgs p) {
 // CTAs for a persistent row-mode launch: at most 8 per SM
 unsigned smx_grid(uint64_t groups) { return (unsigned)(groups < 148u * 8u ? (groups ? groups : 1) : 148u * 8u); }
 
+template <int G, int P>
+void launch_rows(const SmxArgs& p, unsigned grid, unsigned threads, bool fc, cudaStream_t st) {
+  if (fc)
+    smx_rows<G, P, true><<<grid, threads, 0, st>>>(p);
+  else
+    smx_rows<G, P, false><<<grid, threads, 0, st>>>(p);
+}
+
 int launch_softmax(const corm_vectorop_desc* d, cudaStream_t st, const corm::DeviceTables* tb) {
   SmxArgs p{};
   p.a = d->a;
@@ -422,18 +482,33 @@ int launch_softmax(const corm_vectorop_desc* d, cudaStream_t st, const corm::Dev
   p.valid0 = d->smx_mask & 0xFFFFu;
   p.period = d->smx_mask >> 16;
   p.tab = tb->smx_tab;
+  p.cm8 = p.cm << 8;
+  p.csm8 = p.cs >= 8u ? p.cs - 8u : 0u;
+  const bool fc = p.cs >= 8u && p.cs <= 39u && 40u - p.fp < 32u;
   const bool col = d->op == 11;
   p.rows = col ? (d->outer & ~15u) : d->outer;
   if (p.rows == 0) return CORM_OK;
   if (p.rows > 1 && p.b_inc < p.size)
     return corm::fail(CORM_EINVAL, "softmax: output rows overlap (b_inc %u < size %u)", p.b_inc, p.size);
-  if (col && d->size % 8 == 0 && d->size <= 2048 && d->a_inc % 8 == 0 && !((uintptr_t)d->a & 15u)) {
+  if (col && d->size % 8 == 0 && d->size <= 1024 && d->a_inc % 8 == 0 && !((uintptr_t)d->a & 15u)) {
     const size_t smem = 4096 * sizeof(int32_t) + (32 * ((size_t)d->size + 8) + 16 * 4) * sizeof(int16_t);
-    cudaFuncSetAttribute(smx_cols_t, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     const uint32_t tiles = (p.rows + 31) / 32;
+    const unsigned grid = tiles < 148u * 4u ? tiles : 148u * 4u;
+    auto launch = [&](auto kf, auto ks) {
+      cudaFuncSetAttribute(kf, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+      cudaFuncSetAttribute(ks, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+      if (fc)
+        kf<<<grid, 256, smem, st>>>(p);
+      else
+        ks<<<grid, 256, smem, st>>>(p);
+    };
     {
       corm::ProfScope prof_("smx_cols_t", st);
-      smx_cols_t<<<tiles < 148u * 4u ? tiles : 148u * 4u, 256, smem, st>>>(p);
+      if (d->size <= 64) launch(smx_cols_t<1, true, true>, smx_cols_t<1, true, false>);
+      else if (d->size <= 128) launch(smx_cols_t<2, true, true>, smx_cols_t<2, true, false>);
+      else if (d->size <= 256) launch(smx_cols_t<4, true, true>, smx_cols_t<4, true, false>);
+      else if (d->size <= 512) launch(smx_cols_t<8, false, true>, smx_cols_t<8, false, false>);
+      else launch(smx_cols_t<16, false, true>, smx_cols_t<16, false, false>);
     }
     return corm::cuda_status("softmax_cols");
   }
@@ -449,41 +524,41 @@ int launch_softmax(const corm_vectorop_desc* d, cudaStream_t st, const corm::Dev
   }
   if (d->size <= 128) {
     corm::ProfScope prof_("smx_rows<16,8>", st);
-    smx_rows<16, 8><<<smx_grid((p.rows + 15) / 16), 256, 0, st>>>(p);
+    launch_rows<16, 8>(p, smx_grid((p.rows + 15) / 16), 256, fc, st);
   } else if (d->size <= 256) {
     {
       corm::ProfScope prof_("smx_rows<32,8>", st);
-      smx_rows<32, 8><<<smx_grid((p.rows + 7) / 8), 256, 0, st>>>(p);
+      launch_rows<32, 8>(p, smx_grid((p.rows + 7) / 8), 256, fc, st);
     }
   } else if (d->size <= 384) {
     {
       corm::ProfScope prof_("smx_rows<16,24>", st);
-      smx_rows<16, 24><<<smx_grid((p.rows + 15) / 16), 256, 0, st>>>(p);
+      launch_rows<16, 24>(p, smx_grid((p.rows + 15) / 16), 256, fc, st);
     }
   } else if (d->size <= 512) {
     {
       corm::ProfScope prof_("smx_rows<32,16>", st);
-      smx_rows<32, 16><<<smx_grid((p.rows + 7) / 8), 256, 0, st>>>(p);
+      launch_rows<32, 16>(p, smx_grid((p.rows + 7) / 8), 256, fc, st);
     }
   } else if (d->size <= 768) {
     {
       corm::ProfScope prof_("smx_rows<32,24>", st);
-      smx_rows<32, 24><<<smx_grid((p.rows + 7) / 8), 256, 0, st>>>(p);
+      launch_rows<32, 24>(p, smx_grid((p.rows + 7) / 8), 256, fc, st);
     }
   } else if (d->size <= 1024) {
     {
       corm::ProfScope prof_("smx_rows<32,32>", st);
-      smx_rows<32, 32><<<smx_grid((p.rows + 7) / 8), 256, 0, st>>>(p);
+      launch_rows<32, 32>(p, smx_grid((p.rows + 7) / 8), 256, fc, st);
     }
   } else if (d->size <= 4096) {
     {
       corm::ProfScope prof_("smx_rows<256,16>", st);
-      smx_rows<256, 16><<<smx_grid(p.rows), 256, 0, st>>>(p);
+      launch_rows<256, 16>(p, smx_grid(p.rows), 256, fc, st);
     }
   } else if (d->size <= 16384) {
     {
       corm::ProfScope prof_("smx_rows<1024,16>", st);
-      smx_rows<1024, 16><<<smx_grid(p.rows), 1024, 0, st>>>(p);
+      launch_rows<1024, 16>(p, smx_grid(p.rows), 1024, fc, st);
     }
   } else {
     return corm::fail(CORM_ELIMIT, "softmax row mode: size %u beyond 16384", d->size);
