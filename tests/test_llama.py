@@ -59,12 +59,6 @@ def test_llama_host_logic_cpu(cpu_ops):
     rstates = {t.onnx_name: np.zeros(t.shape, np.int64) for t in g.state_tensors}
     ref = llm.forward(g, _raw_inputs(g, feeds), rstates)
     _compare(g, arr, ref, states, rstates)
-    # lean mode (only the logits observed: the parts past the key count left unwritten)
-    st2 = {t.onnx_name: np.zeros(t.shape) for t in g.state_tensors}
-    lean = sim.forward_pass(feeds, states=st2, keep=["logits"])
-    assert np.array_equal(np.rint(lean["logits"] * 2.0 ** 11).astype(np.int64), ref["logits"])
-    for t in g.state_tensors:
-        assert np.array_equal(st2[t.onnx_name], states[t.onnx_name]), t.onnx_name
 
 
 @pytest.mark.gpu
