@@ -462,6 +462,8 @@ def bench_models(torch, dev, stream, flush, args, world, rank, pg):
              ("llama360m_prefill512", "tokens", lambda b: WL.llama_prefill(seed=5, batch=b, seq=512),
               max(1, 64 // world))]
     seq_of = {"bert_base_384": 384, "llama360m_prefill512": 512}
+    if not args.models or "llama360m_decode128" in args.models.split(","):
+        out["llama360m_decode128"] = bench_llama_decode(torch, dev, stream, flush, args, world, pg)
     for name, unit, build, batch in cases:
         if args.models and name not in args.models.split(","):
             continue
@@ -519,6 +521,55 @@ def bench_models(torch, dev, stream, flush, args, world, rank, pg):
             og.forward(g1, {k: np.asarray(v) for k, v in f1.items()})
             el = time.perf_counter() - t0
             out[name][f"cpu_oracle_{unit}_per_s"] = round(seq_of.get(name, 1) / el, 3)
+    return out
+
+
+def bench_llama_decode(torch, dev, stream, flush, args, world, pg, steps=128):
+    """configs[4]'s decode: after the 512-token prefill of 64 / N sequences,
+    ``steps`` greedy decode steps (pos 512 .. 639): per step the device greedy
+    step (argmax + embedding row) and one decode-step pass (the host softmax
+    on the device), each captured as its own CUDA graph (the key count and
+    the cache row are registers of the step); a timed step replays all of
+    them.  Tokens/s over all ranks."""
+    import numpy as np
+
+    from cormorant_b200 import workloads as WL
+    from cormorant_b200.llm_runner import LlamaRunner
+    B = max(1, 64 // world)
+    m = WL.LlamaModel(seed=5, batch=B, seq=512)
+    r = LlamaRunner(m, device=dev)
+    ids = torch.empty((steps, B), dtype=torch.int32, device=dev)
+    with torch.cuda.stream(stream):
+        lg0 = r.prefill()
+        r.decode_step(lg0, steps - 1)  # the largest key count: workspaces and tables sized before capture
+    torch.cuda.synchronize()
+    pool = torch.cuda.graph_pool_handle()
+    graphs, lg = [], lg0
+    for i in range(steps):
+        gr = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gr, stream=stream, pool=pool):
+            lg = r.decode_step(lg, i, ids[i])
+        graphs.append(gr)
+
+    class _Seq:
+        def replay(self):
+            for gr in graphs:
+                gr.replay()
+    ms = _time_graph(torch, stream, flush, _Seq(), args)
+    if pg:
+        t = torch.tensor([ms], dtype=torch.float64, device=dev)
+        pg.all_reduce(t, op=pg.ReduceOp.MAX)
+        ms = float(t.item())
+    keys_avg = float(np.mean([-(-(512 + i + 1) // 16) * 16 for i in range(steps)]))
+    macs = m.macs_per_token(keys_avg, prefill=False)
+    rate = world * B * steps / (ms * 1e-3)
+    out = {"batch_per_gpu": B, "steps": steps, "ms_per_decode_run": round(ms, 3),
+           "ms_per_token_step": round(ms / steps, 4), "tokens_per_s": round(rate, 1),
+           "GMAC/s": round(rate * macs / 1e9, 1), "mmac_per_token": round(macs / 1e6, 2),
+           "graph_nodes_per_step": len(m.decode_graph.nodes),
+           "first_ids": ids[0, :4].cpu().tolist()}
+    del graphs, r
+    torch.cuda.empty_cache()
     return out
 
 

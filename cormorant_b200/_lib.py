@@ -18,7 +18,7 @@ F_WRAP32, F_WEIGHT_LOGICAL, F_ACT_RELU, F_ACT_RELU6 = 0x1, 0x2, 0x4, 0x8
 # every symbol include/cormorant_b200.h declares
 EXPORTS = ("corm_vectorop", "corm_matmul_workspace_size", "corm_matmul", "corm_matmul_noalloc", "corm_conv_workspace_size", "corm_conv",
            "corm_matmul_post", "corm_conv_post", "corm_gemm_strided_workspace_size", "corm_gemm_strided",
-           "corm_copy_nd",
+           "corm_copy_nd", "corm_llm_attn_softmax", "corm_greedy_embed",
            "corm_pool", "corm_rowops", "corm_act_table", "corm_smx_table", "corm_rowops_table_image",
            "corm_bind_device", "corm_device_status", "corm_launch_count", "corm_profile_enable",
            "corm_profile_read", "corm_version", "corm_last_error")
@@ -74,6 +74,18 @@ class CopyDesc(C.Structure):
                 ("src_strides", C.c_int64 * 6), ("dst_strides", C.c_int64 * 6)]
 
 
+class LlmSmxDesc(C.Structure):
+    """corm_llm_smx_desc: the host's p12 softmax of one KV group."""
+    _fields_ = [("s", C.c_void_p), ("p", C.c_void_p), ("tab", C.c_void_p), ("ip", C.c_void_p)] + _u32_fields(
+        ["pos", "n", "T", "G", "C", "Q", "window", "batch"]) + [("s_stride", C.c_uint64), ("p_stride", C.c_uint64)]
+
+
+class GreedyDesc(C.Structure):
+    """corm_greedy_desc: argmax of each logits row and its embedding row."""
+    _fields_ = [("logits", C.c_void_p), ("table", C.c_void_p), ("out", C.c_void_p), ("ids", C.c_void_p)] + \
+        _u32_fields(["batch", "vocab", "dim"]) + [("ld", C.c_uint64)]
+
+
 class PoolDesc(C.Structure):
     _fields_ = [("x", C.c_void_p), ("y", C.c_void_p)] + _u32_fields(
         ["batch", "channels", "in_h", "in_w", "out_h", "out_w", "pool_h", "pool_w", "stride_h", "stride_w",
@@ -116,6 +128,8 @@ def lib() -> C.CDLL:
                        ("corm_gemm_strided", [C.POINTER(GemmDesc), C.c_void_p]),
                        ("corm_gemm_strided_workspace_size", [C.POINTER(GemmDesc), C.POINTER(C.c_size_t)]),
                        ("corm_copy_nd", [C.POINTER(CopyDesc), C.c_void_p]),
+                       ("corm_llm_attn_softmax", [C.POINTER(LlmSmxDesc), C.c_void_p]),
+                       ("corm_greedy_embed", [C.POINTER(GreedyDesc), C.c_void_p]),
                        ("corm_pool", [C.POINTER(PoolDesc), C.c_void_p]),
                        ("corm_rowops", [C.POINTER(RowOpsDesc), C.c_void_p]),
                        ("corm_act_table", [C.c_uint32, C.c_uint32, C.c_void_p]),

@@ -49,6 +49,20 @@ def smx_regs(f_s: int, sigma: float, f_p: int) -> Tuple[int, int]:
     return cm, (cs & 63) | ((int(f_p) & 31) << 8)
 
 
+_SEXP: Dict[Tuple[int, float], np.ndarray] = {}
+
+
+def sexp_table(f: int, scale: float) -> np.ndarray:
+    """The host softmax's exp table of score exponent f: e[k] = exp(-k 2^-f
+    scale), k in [0, 65536), with the C library's exp in this operation order
+    (llm_nodes.py:357-364)."""
+    key = (int(f), float(scale))
+    if key not in _SEXP:
+        d = 2.0 ** int(f)
+        _SEXP[key] = np.array([math.exp(-k / d * scale) for k in range(65536)])
+    return _SEXP[key]
+
+
 def score_exp(fq, fk, KV: int, F: int = 8) -> np.ndarray:
     """Per query head the q.K^T scores' exponent f_q + f_k(its KV head) - F
     (graph_builder.py:197-200)."""
@@ -68,7 +82,7 @@ def prefill_layer(prefix: str, *, T: int, H: int, KV: int, HD: int, C: int, fq0,
                   cos, sin, q0: N.TensorInfo, k0: N.TensorInfo, v: N.TensorInfo, pos: N.TensorInfo,
                   n: Optional[N.TensorInfo], ck: N.TensorInfo, cv: N.TensorInfo, pv_exp=None,
                   logit_scale: Optional[float] = None, causal: int = 1, Q: int = KEY_QUANTUM, batch: int = 1,
-                  tensors: Optional[Dict[str, N.TensorInfo]] = None):
+                  softmax: str = "unit", tensors: Optional[Dict[str, N.TensorInfo]] = None):
     """The node chain of one layer's prefill attention (llama.py:329-402,
     ``group_order`` "ahead1": qk0, then per group softmax / qk of the next /
     pv).  q0 [T][H HD] at fq0, k0 / v [T][KV HD] at fk0 / fv (per channel);
@@ -76,7 +90,9 @@ def prefill_layer(prefix: str, *, T: int, H: int, KV: int, HD: int, C: int, fq0,
     [KV HD]) / fvc (per KV head or per channel);
     fq [H] the rotated q's exponents, fp [H] P's.  ``batch`` B: B sequences
     at one pos / n stacked (q0 [B T][..], caches [B C][KV HD]; the nodes'
-    batch layouts).  Returns (nodes, pv)."""
+    batch layouts).  ``softmax`` "host": the host's p12 softmax
+    (LlmAttnSoftmaxNode — a decode step's, llama.py:383-392 without vsmx)
+    instead of the unit's.  Returns (nodes, pv)."""
     G = H // KV
     B = int(batch)
     tensors = {} if tensors is None else tensors
@@ -117,6 +133,11 @@ def prefill_layer(prefix: str, *, T: int, H: int, KV: int, HD: int, C: int, fq0,
         return N.LlmAttnConvNode(inputs=[ck, qx] + rt, output=s[g], kind="qk", group=g, **common)
 
     def smx(g):
+        if softmax == "host":
+            hs = slice(g * G, (g + 1) * G)
+            return N.LlmAttnSoftmaxNode(inputs=[s[g]] + rt, output=p[g], T=T, G=G, C=C, Q=Q, group=g, scale=sigma,
+                                        fs=fs[hs].copy(), fp=np.asarray(fp[hs]).copy(), has_n=n is not None,
+                                        causal=causal == 1, prefix_lm=causal == 2, batch=B)
         regs = [smx_regs(int(fs[g * G + h]), sigma, int(fp[g * G + h])) for h in range(G)]
         return N.LlmAttnSoftmaxVopNode(inputs=[s[g]] + rt, output=p[g], T=T, G=G, C=C, Q=Q, group=g,
                                        has_n=n is not None, causal=causal == 1, prefix_lm=causal == 2,

@@ -389,6 +389,32 @@ class LlmAttnSoftmaxVopNode:
 
 
 @dataclass
+class LlmAttnSoftmaxNode:
+    """The host's p12 softmax of KV group ``group`` (llm_nodes.py:1426-1557; a
+    decode step's, or a prefill's without the softmax unit): s [C][G T] ->
+    P [G T][C], rows t < n over keys j <= pos + t (window W: j > pos + t -
+    W), exp tables of the score exponents fs[h'] at ``scale``, P at fp[h'].
+    inputs = [s, pos, (n)]; ``batch`` B: s [C][B G T] -> P [B G T][C]."""
+    inputs: List[TensorInfo]
+    output: TensorInfo
+    T: int = 1
+    G: int = 1
+    C: int = 16
+    Q: int = 16
+    group: int = 0
+    scale: float = 1.0
+    fs: Optional[np.ndarray] = field(default=None, repr=False)
+    fp: Optional[np.ndarray] = field(default=None, repr=False)
+    has_n: bool = True
+    causal: bool = True
+    prefix_lm: bool = False
+    window: int = 0
+    F: int = 8
+    batch: int = 1
+    onnx_node: object = None
+
+
+@dataclass
 class LlmAttnMergeNode:
     """The P.V outputs o_g [G T][HD] (raw) -> pv [T][H HD] in head order,
     pv[t][(g G + h') HD + d] = o_g[h' T + t][d], a raw copy

@@ -130,6 +130,33 @@ def copy_nd(src, dst, dims, src_strides, dst_strides, *, src_off=0, dst_off=0):
     check(lib().corm_copy_nd(C.byref(d), st))
 
 
+def llm_attn_softmax(s, p, tab, ip, *, pos, n, T, G, rows, Q=16, window=0, batch=1, s_stride=None, p_stride=None):
+    """The host's p12 softmax of one KV group (corm_llm_attn_softmax): scores
+    s [rows][s_stride] int16 (rows = the cache rows C), P rows of ``rows``
+    entries at p_stride, tab float64 [G][65536], ip float64 [G] (2^f_p per
+    head)."""
+    _i16(s, "s")
+    _i16(p, "p")
+    if tab.dtype != torch.float64 or ip.dtype != torch.float64:
+        raise CormError(_lib.CORM_EINVAL, "tab / ip must be float64")
+    st = _ready()
+    d = _lib.LlmSmxDesc(_ptr(s), _ptr(p), _ptr(tab), _ptr(ip), pos, n, T, G, rows, Q, window, batch,
+                        batch * G * T if s_stride is None else s_stride, rows if p_stride is None else p_stride)
+    check(lib().corm_llm_attn_softmax(C.byref(d), st))
+
+
+def greedy_embed(logits, table, out, ids=None, *, batch, vocab, dim, ld=None):
+    """corm_greedy_embed: ids = first argmax of each int16 logits row; out
+    (int32) = those rows of the int32 table."""
+    _i16(logits, "logits")
+    if table.dtype != torch.int32 or out.dtype != torch.int32 or (ids is not None and ids.dtype != torch.int32):
+        raise CormError(_lib.CORM_EINVAL, "table / out / ids must be int32")
+    st = _ready()
+    d = _lib.GreedyDesc(_ptr(logits), _ptr(table), _ptr(out), _ptr(ids), batch, vocab, dim,
+                        vocab if ld is None else ld)
+    check(lib().corm_greedy_embed(C.byref(d), st))
+
+
 def conv(x, weight, bias, y, *, batch, in_ch, in_h, in_w, out_ch, out_h, out_w, kh, kw, stride_h=1, stride_w=1,
          dilation_h=1, dilation_w=1, pad_top=0, pad_left=0, has_bias=0, is_depthwise=0, y_cs=0, y_cn=0, y_gs=0,
          flags=0, workspace=None, post=None):

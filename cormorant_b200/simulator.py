@@ -75,11 +75,13 @@ def _has_exp(*ts) -> bool:
 class GpuSimulator:
     """Forward pass of a node graph on the current CUDA device."""
 
-    def __init__(self, graph, fuse: bool = True, device=None):
+    def __init__(self, graph, fuse: bool = True, device=None, share=None):
+        """``share``: another GpuSimulator whose device weights (and tables)
+        this one reuses — the prefill and decode graphs of one model."""
         self._graph = graph
         self.device = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
         self.fuse = fuse
-        self._weights: Dict[str, torch.Tensor] = {}
+        self._weights: Dict[str, torch.Tensor] = share._weights if share is not None else {}
         self._ws: Optional[torch.Tensor] = None
         self._plan = self._fusion_plan() if fuse else {}
 
@@ -377,6 +379,8 @@ class GpuSimulator:
                 y = self._attn_conv(sn, get)
             elif kind == "LlmAttnSoftmaxVopNode":
                 y = self._attn_softmax(sn, get)
+            elif kind == "LlmAttnSoftmaxNode":
+                y = self._attn_softmax_host(sn, get)
             elif kind == "LlmAttnMergeNode":
                 y = self._attn_merge(sn, get)
             elif kind == "LlmSelectRowNode":
@@ -655,6 +659,29 @@ class GpuSimulator:
             for h in range(G):
                 ops.vectorop(s[b * GT + h * T:], None, y[(b * GT + h * T) * C:], size=keys, op=11, outer=T,
                              a_inc=B * GT, b_inc=C, smx_cm=regs[h][0], smx_cfg=regs[h][1], smx_mask=mask)
+        return y
+
+    def _attn_softmax_host(self, sn, get):
+        """The host's p12 softmax on the device (corm_llm_attn_softmax): the
+        float64 exp tables of the group's score exponents (built once on the
+        host with libm, as the generated code's init does) and 2^f_p."""
+        from .attention import sexp_table
+        if not sn.causal:
+            raise NotImplementedError("LlmAttnSoftmaxNode: causal = 0 / 2 run on the softmax unit only")
+        B = int(getattr(sn, "batch", 1))
+        fs = tuple(int(v) for v in np.asarray(sn.fs).reshape(-1))
+        fp = tuple(int(v) for v in np.asarray(sn.fp).reshape(-1))
+        key = ("sexp", fs, fp, float(sn.scale))
+        if key not in self._weights:
+            tab = np.concatenate([sexp_table(f, float(sn.scale)) for f in fs])
+            self._weights[key] = (torch.from_numpy(tab).to(self.device),
+                                  torch.tensor([2.0 ** f for f in fp], dtype=torch.float64, device=self.device))
+        tab, ip = self._weights[key]
+        pos = self._host_int(get, sn.inputs[1])
+        n = self._host_int(get, sn.inputs[2]) if sn.has_n else sn.T
+        y = self._alloc(sn.output.numel)
+        ops.llm_attn_softmax(get(sn.inputs[0]), y, tab, ip, pos=pos, n=max(n, 0), T=sn.T, G=sn.G, rows=sn.C, Q=sn.Q,
+                             window=int(getattr(sn, "window", 0)), batch=B)
         return y
 
     def _attn_merge(self, sn, get):

@@ -341,110 +341,164 @@ LLAMA_EXP = dict(fr=15, fx=12, fq0=13, fk0=13, fv=13, fq=10, fkc=10, fvc=9, fp=1
                  fd=13, fl=11)
 
 
+class LlamaModel:
+    """A Llama-family decoder on the kernels (SmolLM2-360M shape by default):
+    its weights, KV-cache states and embedding table, and the node graphs of a
+    prefill (``prefill_graph``) and of one decode step (``decode_graph``) that
+    share them, as the scheduler's LLM entries lower the model with the
+    row-ops unit (src/llama.py:329-402 with rowops = 1): per layer RMSNorm
+    (the int32 residual -> int16), the q / k / v projections (MatMul), the
+    attention chain (AttnPrepRoNode: RoPE and the KV-cache rows; per KV group
+    q.K^T, the softmax and P.V; the head merge), the output projection,
+    ResAdd, RMSNorm, gate / up, SiLU(g) u, down, ResAdd; then the final
+    RMSNorm and the LM head.  The prefill runs the softmax on VectorOP's unit
+    (vsmx = 1) and ends with the last valid row of every sequence
+    (LlmSelectRowNode); a decode step (one row, no n) runs the host's p12
+    softmax, as the reference's decode entries do.
+
+    ``batch`` sequences side by side (the nodes' batch layouts), ``seq``
+    prefill tokens at pos 0, KV caches of ``cache`` rows (default seq + 128)
+    as group-major states.  The embedding lookup is the reference's host op:
+    a graph input is the gathered rows of a N(0, 0.02) table as the int32
+    residual.  Weights N(0, 0.02) (norm weights 1) at the rank-1 exponents the
+    per-tensor activation exponents ``exps`` give."""
+
+    def __init__(self, seed: int = 5, batch: int = 1, seq: int = 512, layers: int = 32, hidden: int = 960,
+                 heads: int = 15, kv_heads: int = 5, head_dim: int = 64, ffn: int = 2560, vocab: int = 49152,
+                 theta: float = 1e5, cache: int = None, eps: float = 1e-5, exps: dict = None):
+        from . import attention as AT
+        self.E = E = dict(LLAMA_EXP, **(exps or {}))
+        rng = np.random.default_rng(seed)
+        self.B, self.T, self.D, self.H, self.KV, self.HD = batch, seq, hidden, heads, kv_heads, head_dim
+        self.L, self.ffn, self.vocab, self.eps = layers, ffn, vocab, eps
+        C = seq + 128 if cache is None else cache
+        self.C = C = -(-C // AT.KEY_QUANTUM) * AT.KEY_QUANTUM
+        D, nq, nk = hidden, heads * head_dim, kv_heads * head_dim
+        self.w = []
+        for li in range(layers):
+            lw = {}
+            for nm, (k, m, f_in, f_out) in dict(q0=(D, nq, E["fx"], E["fq0"]), k0=(D, nk, E["fx"], E["fk0"]),
+                                                v=(D, nk, E["fx"], E["fv"]),
+                                                o=(nq, D, E["fp"] + E["fvc"] - 8, E["fo"]),
+                                                g=(D, ffn, E["fx"], E["fg"]), u=(D, ffn, E["fx"], E["fu"]),
+                                                d=(ffn, D, E["fa"], E["fd"])).items():
+                lw[nm] = N.TensorInfo(f"l{li}.{nm}.w", [k, m],
+                                      data=_encode_weight(rng.normal(0.0, 0.02, (k, m)), f_out + 8 - f_in))
+            self.w.append(lw)
+        self.w_lm = N.TensorInfo("logits.w", [D, vocab],
+                                 data=_encode_weight(rng.normal(0.0, 0.02, (D, vocab)), E["fl"] + 8 - E["fx"]))
+        self.states = []
+        for li in range(layers):
+            for nm, f in (("ck", E["fkc"]), ("cv", E["fvc"])):
+                self.states.append(N.TensorInfo(f"l{li}.{nm}", [batch * C, nk], exp=np.asarray(f, np.int64),
+                                                is_state=True, group_layout=(kv_heads, head_dim)))
+        inv = 1.0 / theta ** (np.arange(0, head_dim, 2, dtype=np.float64) / head_dim)
+        ang = np.outer(np.arange(C, dtype=np.float64), inv)
+        self.cos, self.sin = np.cos(ang).astype(np.float32), np.sin(ang).astype(np.float32)
+        self.emb = rng.normal(0.0, 0.02, (vocab, D))
+        self.ids = rng.integers(0, vocab, size=(batch, seq))
+        self.prefill_graph = self._graph(seq, prefill=True)
+        self.decode_graph = self._graph(1, prefill=False)
+        self.prefill_feeds = {"h0": self.emb[self.ids].reshape(batch * seq, D), "pos": np.array([0]),
+                              "n": np.array([seq])}
+
+    def _graph(self, T: int, prefill: bool):
+        from . import attention as AT
+        E, B, D, H, KV, HD, C = self.E, self.B, self.D, self.H, self.KV, self.HD, self.C
+        nq, nk, ffn, R = H * HD, KV * HD, self.ffn, B * T
+        weights: List[N.TensorInfo] = []
+        nodes: list = []
+        tag = "p" if prefill else "d"
+
+        def ten(name, shape, exp=None, **kw):
+            return N.TensorInfo(f"{tag}.{name}", list(shape), exp=None if exp is None else np.asarray(exp, np.int64),
+                                **kw)
+
+        def param(name, words):
+            t = N.TensorInfo(name, [len(words)], data=np.asarray(words, np.float64) / 256.0)
+            weights.append(t)
+            return t
+
+        def linear(name, x, w, f_out, rows=R):
+            weights.append(w)
+            k, m = w.shape
+            y = ten(name, (rows, m), f_out)
+            nodes.append(N.MatmulNode(inputs=[x, w], output=y, n=rows, k=k, m=m, batch=1))
+            return y
+
+        def rmsnorm(name, h, f_out, rows=R):
+            words, bc, g, Ev = RH.rmsnorm_job(np.ones(D), self.eps, E["fr"], np.full(D, f_out))
+            y = ten(name, (rows, D), f_out)
+            nodes.append(N.RMSNormRoNode(inputs=[h, param("rms.p", words)], output=y, rows=rows, n=D, fr=E["fr"],
+                                         eps=self.eps, g=g, E=Ev, bcast=bc, gamma=np.ones(D)))
+            return y
+
+        def resadd(name, h, d, f_d):
+            words, bc = RH.resadd_job(E["fr"], np.full(D, f_d), D)
+            y = ten(name, (R, D), E["fr"], dma="i32")
+            nodes.append(N.ResAddRoNode(inputs=[h, d, param(f"resadd{f_d}.p", words)], output=y, rows=R, n=D,
+                                        fr=E["fr"], bcast=bc))
+            return y
+
+        h = h0 = N.TensorInfo("h0" if prefill else "h_step", [R, D], exp=np.asarray(E["fr"], np.int64), dma="i32")
+        pos = N.TensorInfo("pos", [1], host="i32")
+        n_t = N.TensorInfo("n", [1], host="i32") if prefill else None
+        for li in range(self.L):
+            lw = self.w[li]
+            x = rmsnorm(f"l{li}.x", h, E["fx"])
+            q0 = linear(f"l{li}.q0", x, lw["q0"], E["fq0"])
+            k0 = linear(f"l{li}.k0", x, lw["k0"], E["fk0"])
+            v = linear(f"l{li}.v", x, lw["v"], E["fv"])
+            ck, cv = self.states[2 * li], self.states[2 * li + 1]
+            chain, pv = AT.prefill_layer(f"{tag}.l{li}.attn", T=T, H=H, KV=KV, HD=HD, C=C, fq0=np.full(nq, E["fq0"]),
+                                         fk0=np.full(nk, E["fk0"]), fv=np.full(nk, E["fv"]), fq=np.full(H, E["fq"]),
+                                         fkc=np.full(KV, E["fkc"]), fvc=np.full(KV, E["fvc"]),
+                                         fp=np.full(H, E["fp"]), cos=self.cos, sin=self.sin, q0=q0, k0=k0, v=v,
+                                         pos=pos, n=n_t, ck=ck, cv=cv, batch=B,
+                                         softmax="unit" if prefill else "host")
+            for nd in chain:
+                for t in nd.inputs:
+                    if t is not None and t.data is not None and all(t is not w for w in weights):
+                        weights.append(t)
+            nodes += chain
+            o = linear(f"l{li}.o", pv, lw["o"], E["fo"])
+            h1 = resadd(f"l{li}.h1", h, o, E["fo"])
+            x2 = rmsnorm(f"l{li}.x2", h1, E["fx"])
+            g = linear(f"l{li}.g", x2, lw["g"], E["fg"])
+            u = linear(f"l{li}.u", x2, lw["u"], E["fu"])
+            words, bc = RH.silu_mul_job(np.full(ffn, E["fg"]), np.full(ffn, E["fu"]), np.full(ffn, E["fa"]), ffn)
+            a = ten(f"l{li}.a", (R, ffn), E["fa"])
+            nodes.append(N.SiluMulRoNode(inputs=[g, u, param("silumul.p", words)], output=a, rows=R, n=ffn,
+                                         bcast=bc))
+            d = linear(f"l{li}.d", a, lw["d"], E["fd"])
+            h = resadd(f"l{li}.h2", h1, d, E["fd"])
+        if prefill:
+            last = ten("h_last", (B, D), E["fr"], dma="i32")
+            nodes.append(N.LlmSelectRowNode(inputs=[h, n_t], output=last, rows=T, n=D, res32=True, batch=B))
+            h = last
+        xf = rmsnorm("xf", h, E["fx"], rows=B)
+        logits = linear("logits", xf, self.w_lm, E["fl"], rows=B)
+        ins = [h0, pos] + ([n_t] if prefill else [])
+        weights = list({w.onnx_name: w for w in weights}.values())
+        return N.Graph(nodes=nodes, weight_tensors=weights, input_tensors=ins, output_tensors=[logits],
+                       state_tensors=list(self.states))
+
+    def macs_per_token(self, keys: int, prefill: bool = True) -> float:
+        """Int16 MACs per token of a pass: the projections, the attention at
+        ``keys`` keys (masked keys included, as the kernels run them) and the
+        LM head (once per sequence in a prefill of T tokens)."""
+        D, H, KV, HD, ffn = self.D, self.H, self.KV, self.HD, self.ffn
+        nq, nk = H * HD, KV * HD
+        per_layer = D * (nq + 2 * nk) + nq * D + 3 * D * ffn + 2 * H * keys * HD
+        return self.L * per_layer + D * self.vocab / (self.T if prefill else 1)
+
+
 def llama_prefill(seed: int = 5, batch: int = 1, seq: int = 512, layers: int = 32, hidden: int = 960, heads: int = 15,
                   kv_heads: int = 5, head_dim: int = 64, ffn: int = 2560, vocab: int = 49152, theta: float = 1e5,
                   cache: int = None, eps: float = 1e-5, exps: dict = None):
-    """The prefill of a Llama-family decoder (SmolLM2-360M shape by default)
-    on the kernels, as the scheduler's LLM entries lower it with the row-ops
-    unit and the softmax unit (src/llama.py:329-402 with rowops = vsmx = 1):
-    per layer RMSNorm (int32 residual -> int16), the q / k / v projections
-    (MatMul), the prefill attention chain (AttnPrepRoNode: RoPE theta and the
-    KV-cache rows; per KV group q.K^T, the column softmax and P.V; the head
-    merge), the output projection, ResAdd, RMSNorm, gate / up, SiLU(g) u,
-    down, ResAdd; then the last valid row of every sequence
-    (LlmSelectRowNode), the final RMSNorm and the LM head.
-
-    ``batch`` sequences of ``seq`` tokens at pos 0 (n = seq), stacked; the
-    KV caches of ``cache`` rows (default seq + 128, room for the decode
-    steps) are group-major states.  The embedding lookup is the reference's
-    host op: the graph input is the gathered rows of a N(0, 0.02) table as the
-    int32 residual.  Weights N(0, 0.02) (norm weights 1) at the rank-1
-    exponents the per-tensor activation exponents ``exps`` give.  Returns
-    (graph, {input: values}, macs_per_token)."""
+    """The prefill of ``LlamaModel``: (graph, {input: values}, macs_per_token)."""
     from . import attention as AT
-    E = dict(LLAMA_EXP, **(exps or {}))
-    rng = np.random.default_rng(seed)
-    B, T, D, H, KV, HD = batch, seq, hidden, heads, kv_heads, head_dim
-    C = T + 128 if cache is None else cache
-    C = -(-C // AT.KEY_QUANTUM) * AT.KEY_QUANTUM
-    R = B * T
-    nq, nk = H * HD, KV * HD
-    weights: List[N.TensorInfo] = []
-    states: List[N.TensorInfo] = []
-    nodes: list = []
-
-    def ten(name, shape, exp=None, **kw):
-        return N.TensorInfo(name, list(shape), exp=None if exp is None else np.asarray(exp, np.int64), **kw)
-
-    def param(name, words):
-        t = ten(name, (len(words),), data=np.asarray(words, np.float64) / 256.0)
-        weights.append(t)
-        return t
-
-    def linear(name, x, f_in, k, m, f_out, rows=R):
-        w = ten(name + ".w", (k, m), data=_encode_weight(rng.normal(0.0, 0.02, (k, m)), f_out + 8 - f_in))
-        weights.append(w)
-        y = ten(name, (rows, m), f_out)
-        nodes.append(N.MatmulNode(inputs=[x, w], output=y, n=rows, k=k, m=m, batch=1))
-        return y
-
-    def rmsnorm(name, h, f_out, rows=R):
-        gamma = np.ones(D)
-        words, bc, g, Ev = RH.rmsnorm_job(gamma, eps, E["fr"], np.full(D, f_out))
-        y = ten(name, (rows, D), f_out)
-        nodes.append(N.RMSNormRoNode(inputs=[h, param(name + ".p", words)], output=y, rows=rows, n=D, fr=E["fr"],
-                                     eps=eps, g=g, E=Ev, bcast=bc, gamma=gamma))
-        return y
-
-    def resadd(name, h, d, f_d):
-        words, bc = RH.resadd_job(E["fr"], np.full(D, f_d), D)
-        y = ten(name, (R, D), E["fr"], dma="i32")
-        nodes.append(N.ResAddRoNode(inputs=[h, d, param(name + ".p", words)], output=y, rows=R, n=D, fr=E["fr"],
-                                    bcast=bc))
-        return y
-
-    inv = 1.0 / theta ** (np.arange(0, HD, 2, dtype=np.float64) / HD)
-    ang = np.outer(np.arange(C, dtype=np.float64), inv)
-    cos, sin = np.cos(ang).astype(np.float32), np.sin(ang).astype(np.float32)
-    h = h0 = ten("h0", (R, D), E["fr"], dma="i32")
-    pos, n_t = ten("pos", (1,), host="i32"), ten("n", (1,), host="i32")
-    emb = rng.normal(0.0, 0.02, (vocab, D))
-    ids = rng.integers(0, vocab, size=(B, T))
-    feeds = {"h0": emb[ids].reshape(R, D), "pos": np.array([0]), "n": np.array([T])}
-    for li in range(L := layers):
-        p = f"l{li}"
-        x = rmsnorm(p + ".x", h, E["fx"])
-        q0 = linear(p + ".q0", x, E["fx"], D, nq, E["fq0"])
-        k0 = linear(p + ".k0", x, E["fx"], D, nk, E["fk0"])
-        v = linear(p + ".v", x, E["fx"], D, nk, E["fv"])
-        ck = ten(p + ".ck", (B * C, nk), E["fkc"], is_state=True, group_layout=(KV, HD))
-        cv = ten(p + ".cv", (B * C, nk), E["fvc"], is_state=True, group_layout=(KV, HD))
-        states += [ck, cv]
-        chain, pv = AT.prefill_layer(p + ".attn", T=T, H=H, KV=KV, HD=HD, C=C, fq0=np.full(nq, E["fq0"]),
-                                     fk0=np.full(nk, E["fk0"]), fv=np.full(nk, E["fv"]), fq=np.full(H, E["fq"]),
-                                     fkc=np.full(KV, E["fkc"]), fvc=np.full(KV, E["fvc"]), fp=np.full(H, E["fp"]),
-                                     cos=cos, sin=sin, q0=q0, k0=k0, v=v, pos=pos, n=n_t, ck=ck, cv=cv, batch=B)
-        for nd in chain:
-            for t in nd.inputs:
-                if t is not None and t.data is not None and all(t is not w for w in weights):
-                    weights.append(t)
-        nodes += chain
-        o = linear(p + ".o", pv, E["fp"] + E["fvc"] - 8, nq, D, E["fo"])
-        h1 = resadd(p + ".h1", h, o, E["fo"])
-        x2 = rmsnorm(p + ".x2", h1, E["fx"])
-        g = linear(p + ".g", x2, E["fx"], D, ffn, E["fg"])
-        u = linear(p + ".u", x2, E["fx"], D, ffn, E["fu"])
-        words, bc = RH.silu_mul_job(np.full(ffn, E["fg"]), np.full(ffn, E["fu"]), np.full(ffn, E["fa"]), ffn)
-        a = ten(p + ".a", (R, ffn), E["fa"])
-        nodes.append(N.SiluMulRoNode(inputs=[g, u, param(p + ".a.p", words)], output=a, rows=R, n=ffn, bcast=bc))
-        d = linear(p + ".d", a, E["fa"], ffn, D, E["fd"])
-        h = resadd(p + ".h2", h1, d, E["fd"])
-    last = ten("h_last", (B, D), E["fr"], dma="i32")
-    nodes.append(N.LlmSelectRowNode(inputs=[h, n_t], output=last, rows=T, n=D, res32=True, batch=B))
-    xf = rmsnorm("xf", last, E["fx"], rows=B)
-    logits = linear("logits", xf, E["fx"], D, vocab, E["fl"], rows=B)
-    g_ = N.Graph(nodes=nodes, weight_tensors=weights, input_tensors=[h0, pos, n_t], output_tensors=[logits],
-                 state_tensors=states)
-    keys = -(-T // AT.KEY_QUANTUM) * AT.KEY_QUANTUM
-    macs = L * (D * (nq + 2 * nk) + nq * D + 3 * D * ffn + 2 * (H // KV) * KV * keys * HD) + D * vocab / T
-    return g_, feeds, macs
+    m = LlamaModel(seed=seed, batch=batch, seq=seq, layers=layers, hidden=hidden, heads=heads, kv_heads=kv_heads,
+                   head_dim=head_dim, ffn=ffn, vocab=vocab, theta=theta, cache=cache, eps=eps, exps=exps)
+    keys = -(-seq // AT.KEY_QUANTUM) * AT.KEY_QUANTUM
+    return m.prefill_graph, m.prefill_feeds, m.macs_per_token(keys)

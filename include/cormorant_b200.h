@@ -192,6 +192,42 @@ typedef struct {
 
 int corm_copy_nd(const corm_copy_desc* d, corm_stream_t stream);
 
+/* ---------------------------------------------------------------- LLM host operations
+ * corm_llm_attn_softmax replaces the host's LlmAttnSoftmax (llm_nodes.py:
+ * 1426-1557; C: llm_attn_softmax, llm_nodes.py:2978-3048), the softmax of a
+ * decode step: per query column (b G T + h' T + t) of the scores [C][s_stride]
+ * the row of P at p + col * p_stride, C entries.  tab: [G][65536] float64,
+ * head h' at h' * 65536 (exp(-k 2^-f_s scale), the reference's sexp_table);
+ * ip: [G] float64 2^f_p.  n is clamped as the generated code clamps it;
+ * window 0: none. */
+typedef struct {
+  const int16_t* s;
+  int16_t* p;
+  const double* tab;
+  const double* ip;
+  uint32_t pos, n, T, G, C, Q, window, batch;
+  uint64_t s_stride, p_stride;
+} corm_llm_smx_desc;
+
+int corm_llm_attn_softmax(const corm_llm_smx_desc* d, corm_stream_t stream);
+
+/* corm_greedy_embed: between two greedy decode steps, per sequence b the
+ * next token id = the first index of the largest of logits[b * ld + 0 ..
+ * vocab) (int16 at one exponent: LlmDequant then the caller's argmax) and its
+ * row of table (int32 [vocab][dim], the embedding as the residual: LlmEmbed,
+ * llm_nodes.py:466-560) into out[b * dim ..]; ids (may be NULL) receives the
+ * ids. */
+typedef struct {
+  const int16_t* logits;
+  const int32_t* table;
+  int32_t* out;
+  int32_t* ids;
+  uint32_t batch, vocab, dim;
+  uint64_t ld;
+} corm_greedy_desc;
+
+int corm_greedy_embed(const corm_greedy_desc* d, corm_stream_t stream);
+
 /* ---------------------------------------------------------------- Pool
  * Replaces run_pool / XPoolingkernel (inference-scheduler/src/codegen/
  * _source.py:1548-1580; semantics inference-scheduler/src/codegen/

@@ -153,3 +153,44 @@ def prefill_layer(q0, k0, v, pos, n_in, *, T, H, KV, HD, C, fq0, fk0, fv, fq, fk
         out[f"s{g}"], out[f"p{g}"], out[f"o{g}"] = s, p, o[-1]
     out["pv"] = attn_merge(o, T=T, H=H, KV=KV, HD=HD)
     return out
+
+
+_SEXP = {}
+
+
+def sexp_table(f: int, scale: float) -> np.ndarray:
+    """e[k] = exp(-k 2^-f scale) for k in [0, 65536), libm exp in this
+    operation order (LN:357-364)."""
+    import math
+    key = (int(f), float(scale))
+    if key not in _SEXP:
+        d = 2.0 ** int(f)
+        _SEXP[key] = np.array([math.exp(-k / d * scale) for k in range(65536)])
+    return _SEXP[key]
+
+
+def attn_softmax_host(s, *, T: int, G: int, C: int, pos: int, n_in: int, fs, fp, scale: float, window: int = 0,
+                      Q: int = 16) -> np.ndarray:
+    """The host's p12 softmax of one KV group (LN:1532-1557): for rows t < n
+    of head h', keys j <= pos + t (and j > pos + t - W with a window): m =
+    max, e = sexp_table(f_s[h'])[m - raw], the sum left to right in float64,
+    P = RNE(fl(e / sum) 2^f_p[h']) saturated; every other entry 0."""
+    n, _keys = attn_keys(pos, n_in, T, C, Q)
+    s = np.asarray(s, np.int64)
+    P = np.zeros((G * T, C), np.int64)
+    if n == 0:
+        return P
+    S = pos + n
+    j = np.arange(S)[None, :]
+    t = np.arange(n)[:, None]
+    mask = j <= pos + t
+    if window:
+        mask &= j > pos + t - window
+    for hh in range(G):
+        raw = s[:S, hh * T:hh * T + n].T
+        m = np.where(mask, raw, -(1 << 20)).max(-1, keepdims=True)
+        k = np.where(mask, m - raw, 0)
+        e = np.where(mask, sexp_table(int(fs[hh]), scale)[k], 0.0)
+        p = e / np.cumsum(e, -1)[..., -1:]
+        P[hh * T:hh * T + n, :S] = np.clip(np.round(p * 2.0 ** int(fp[hh])), -32768, 32767).astype(np.int64)
+    return P

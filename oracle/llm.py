@@ -113,6 +113,13 @@ def forward(graph, raw_inputs: dict, raw_states: dict) -> dict:
             y = np.concatenate([A.attn_softmax(s[:, b], T=sn.T, G=sn.G, C=C, keys=keys, pos=pos, n=n,
                                                causal=sn.causal, prefix_lm=sn.prefix_lm, cm=sn.cm, cfg=sn.cfg)
                                 for b in range(B)], axis=0)
+        elif k == "LlmAttnSoftmaxNode":                                     # LN:1532-1557
+            B, C, GT = sn.batch, sn.C, sn.G * sn.T
+            s = ins[0].reshape(C, B, GT)
+            y = np.concatenate([A.attn_softmax_host(s[:, b], T=sn.T, G=sn.G, C=C, pos=hi(sn.inputs[1]),
+                                                    n_in=hi(sn.inputs[2]) if sn.has_n else sn.T, fs=sn.fs, fp=sn.fp,
+                                                    scale=sn.scale, window=sn.window, Q=sn.Q) for b in range(B)],
+                               axis=0)
         elif k == "LlmAttnMergeNode":                                       # LN:1645-1657
             B, T, HD, G = sn.batch, sn.T, sn.HD, sn.H // sn.KV
             y = np.concatenate([A.attn_merge([o.reshape(B, G * T, HD)[b] for o in ins], T=T, H=sn.H, KV=sn.KV, HD=HD)
@@ -126,3 +133,23 @@ def forward(graph, raw_inputs: dict, raw_states: dict) -> dict:
             raise NotImplementedError(k)
         arr[sn.output.onnx_name] = np.asarray(y, np.int64).reshape(sn.output.shape)
     return arr
+
+
+def greedy_decode(model, raw_states: dict, prefill_logits: np.ndarray, steps: int):
+    """Greedy decode steps on the oracle after a prefill (the states already
+    hold its cache rows): the first argmax of each sequence's logits, its
+    embedding row as the int32 residual (RNE at the residual's exponent), one
+    decode-step pass at pos = T + i.  Returns (ids [steps][B], logits of every
+    step)."""
+    g = model.decode_graph
+    out = g.output_tensors[0].onnx_name
+    emb_raw = np.rint(model.emb * 2.0 ** model.E["fr"]).astype(np.int64)
+    lg = np.asarray(prefill_logits, np.int64)
+    ids, logits = [], []
+    for i in range(steps):
+        nxt = lg.argmax(axis=1)
+        ids.append(nxt)
+        arr = forward(g, {"h_step": emb_raw[nxt], "pos": np.array([model.T + i])}, raw_states)
+        lg = arr[out]
+        logits.append(lg)
+    return np.stack(ids), logits

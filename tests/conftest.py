@@ -99,6 +99,38 @@ def cpu_ops(monkeypatch):
         out = view(dst, dst_off, dims, dst_strides)
         out[...] = v
 
+    def llm_attn_softmax(s, p, tab, ip, *, pos, n, T, G, rows, Q=16, window=0, batch=1, s_stride=None,
+                         p_stride=None):
+        C = rows
+        from oracle import attn as A
+        S = s.numpy()[:C * batch * G * T].reshape(C, batch * G * T)
+        out = p.numpy()
+        tabs = tab.numpy().reshape(G, 65536)
+        ipv = ip.numpy()
+        nn, _keys = A.attn_keys(pos, n, T, C, Q)
+        for col in range(batch * G * T):
+            hh, t = (col % (G * T)) // T, col % T
+            row = np.zeros(C, np.int64)
+            if t < nn:
+                nk = pos + t + 1
+                j0 = nk - window if (window and nk > window) else 0
+                r = S[j0:nk, col].astype(np.int64)
+                e = tabs[hh][r.max() - r]
+                ssum = 0.0
+                for v in e:
+                    ssum += v
+                row[j0:nk] = np.minimum(np.rint((e / ssum) * ipv[hh]), 32767)
+            out[col * C:(col + 1) * C] = row
+
+    def greedy_embed(logits, table, out, ids=None, *, batch, vocab, dim, ld=None):
+        lg = logits.numpy()[:batch * (ld or vocab)].reshape(batch, ld or vocab)[:, :vocab]
+        nxt = lg.argmax(axis=1)
+        out.numpy()[:batch * dim] = table.numpy()[nxt].reshape(-1)
+        if ids is not None:
+            ids.numpy()[:batch] = nxt
+
+    monkeypatch.setattr(ops, "llm_attn_softmax", llm_attn_softmax)
+    monkeypatch.setattr(ops, "greedy_embed", greedy_embed)
     monkeypatch.setattr(ops, "gemm_strided", gemm_strided)
     monkeypatch.setattr(ops, "copy_nd", copy_nd)
     monkeypatch.setattr(ops, "rowops", rowops)

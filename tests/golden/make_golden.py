@@ -660,10 +660,63 @@ def make_llm_attn(ref, out):
     print("sim_llm_attn.npz:", len(res), "arrays")
 
 
+def make_llm_smx_host(ref, out):
+    """LlmAttnSoftmaxNode (llm_nodes.py:1426-1557, the host's p12 softmax of a
+    decode step or a prefill without the unit) from the reference's node
+    factory, run through its _forward_pass on seeded scores: a decode step
+    (T = 1, no n), a prefill (T = 8, n = 5) and a sliding window (W = 6).
+    Saved: the scores, pos / n, the exponents and P as raw integers."""
+    sim = _import_reference(ref)
+    import onnx.helper
+    onnx.helper.get_attribute_value = lambda a: a.value
+    from src.dtype import AP_FIXED_16_8 as D
+    from src.tensor import TensorInfo as TI
+    from src import llm_nodes as LN
+    from src.host_nodes import HostContext
+    rng = np.random.default_rng(47)
+    res = {}
+    H, KV, HD, C = 6, 2, 64, 64
+    G = H // KV
+    fs = rng.integers(9, 13, G)
+    fp = rng.integers(12, 15, G)
+    res.update(fs=fs, fp=fp)
+    cases = {"dec": (1, 37, None, 0, None), "pre": (8, 20, 5, 0, None), "win": (8, 30, 8, 6, None),
+             "scl": (8, 10, 8, 0, 0.2)}
+    for tag, (T, pos, n, W, scale) in cases.items():
+        tens = {}
+        s = TI(onnx_name="s", shape=[C, G * T], dtype="float32", exp=np.asarray(0, np.int64))
+        y = TI(onnx_name="p", shape=[G * T, C], dtype="float32", exp=np.asarray(0, np.int64))
+        post = TI(onnx_name="pos", shape=[1], dtype="float32", host="i32")
+        nt = TI(onnx_name="n", shape=[1], dtype="float32", host="i32")
+        for t in (s, y, post, nt):
+            tens[t.onnx_name] = t
+        attrs = dict(num_heads=H, num_kv_heads=KV, head_dim=HD, key_quantum=16, group=1,
+                     s_exp=[int(v) for v in fs], p_exp=[int(v) for v in fp])
+        if W:
+            attrs["window"] = W
+        if scale is not None:
+            attrs["logit_scale"] = repr(float(scale))
+        ins = ["s", "pos"] + (["n"] if n is not None else [""])
+        node = LN.LlmAttnSoftmaxNode.from_onnx_node(_Node("LlmAttnSoftmax", ins, ["p"], **attrs), tens, 0, 8,
+                                                   HostContext(opset=17, consts={}, frac_bits=8))
+        sraw = rng.integers(-6000, 6000, (C, G * T))
+        sraw[:, :1] = rng.integers(-32768, 32768, (C, 1))      # a full-range column
+        g_ = _Graph([node], [], [s, post] + ([nt] if n is not None else []), [y])
+        feeds = {"s": sraw.astype(np.float64), "pos": np.array([pos], np.int32)}
+        if n is not None:
+            feeds["n"] = np.array([n], np.int32)
+        arr = _shim(sim, D, g_)._forward_pass(feeds)
+        res.update({f"{tag}_s": sraw, f"{tag}_p": np.rint(arr["p"]).astype(np.int64),
+                    f"{tag}_regs": np.array([T, pos, -1 if n is None else n, W], np.int64),
+                    f"{tag}_scale": np.array([node.scale])})
+    np.savez_compressed(os.path.join(out, "sim_llm_smx_host.npz"), **res)
+    print("sim_llm_smx_host.npz:", len(res), "arrays")
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--ref", default="/root/reference")
-    ap.add_argument("--only", choices=["hw", "sim", "graph", "llm", "attn"])
+    ap.add_argument("--only", choices=["hw", "sim", "graph", "llm", "attn", "smx"])
     ap.add_argument("--out", default=HERE)
     args = ap.parse_args()
     if args.only in (None, "hw"):
@@ -676,6 +729,8 @@ def main():
         make_llm_nodes(args.ref, args.out)
     if args.only in (None, "attn"):
         make_llm_attn(args.ref, args.out)
+    if args.only in (None, "smx"):
+        make_llm_smx_host(args.ref, args.out)
 
 
 if __name__ == "__main__":

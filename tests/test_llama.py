@@ -25,7 +25,7 @@ def test_llama_oracle_runs_small():
                                       head_dim=16, ffn=128, vocab=50)
     states = {t.onnx_name: np.zeros(t.shape, np.int64) for t in g.state_tensors}
     arr = llm.forward(g, _raw_inputs(g, feeds), states)
-    lg = arr["logits"]
+    lg = arr[g.output_tensors[0].onnx_name]
     assert lg.shape == (2, 50) and np.abs(lg).max() > 0 and (np.abs(lg) < 32767).mean() > 0.9
     assert macs > 0
 
@@ -79,7 +79,45 @@ def test_gpu_llama_prefill_vs_oracle(fuse):
     _compare(g, arr, ref, states, rstates)
     # lean mode (only the logits observed: the parts past the key count left unwritten)
     st2 = {t.onnx_name: np.zeros(t.shape) for t in g.state_tensors}
-    lean = sim.forward_pass(feeds, states=st2, keep=["logits"])
-    assert np.array_equal(np.rint(lean["logits"] * 2.0 ** 11).astype(np.int64), ref["logits"])
+    out = g.output_tensors[0].onnx_name
+    lean = sim.forward_pass(feeds, states=st2, keep=[out])
+    assert np.array_equal(np.rint(lean[out] * 2.0 ** 11).astype(np.int64), ref[out])
     for t in g.state_tensors:
         assert np.array_equal(st2[t.onnx_name], states[t.onnx_name]), t.onnx_name
+
+
+def _decode_vs_oracle(runner, model, steps):
+    from oracle import llm
+    ids = runner.generate(steps)
+    rstates = {t.onnx_name: np.zeros(t.shape, np.int64) for t in model.prefill_graph.state_tensors}
+    ref = llm.forward(model.prefill_graph, _raw_inputs(model.prefill_graph, model.prefill_feeds), rstates)
+    rids, rlog = llm.greedy_decode(model, rstates, ref[model.prefill_graph.output_tensors[0].onnx_name], steps)
+    assert np.array_equal(np.stack(ids), rids)
+    last = runner.last_logits[:model.B * model.vocab].cpu().numpy().astype(np.int64).reshape(model.B, model.vocab)
+    assert np.array_equal(last, rlog[-1])
+    for t in model.prefill_graph.state_tensors:
+        got = runner.pre.state_values(t, runner.states[t.onnx_name])
+        got = np.rint(got * np.power(2.0, np.asarray(t.exp, np.float64))).astype(np.int64)
+        assert np.array_equal(got, rstates[t.onnx_name]), t.onnx_name
+
+
+def test_llama_decode_host_logic_cpu(cpu_ops):
+    """Prefill then greedy decode steps (the decode-step graph with the host
+    softmax, the device greedy step) with the kernel calls replayed on the
+    oracle's job models, against the oracle's own loop."""
+    from cormorant_b200 import workloads as WL
+    from cormorant_b200.llm_runner import LlamaRunner
+    m = WL.LlamaModel(seed=12, batch=2, seq=16, layers=1, hidden=64, heads=4, kv_heads=2, head_dim=16, ffn=128,
+                      vocab=50)
+    _decode_vs_oracle(LlamaRunner(m, device="cpu"), m, 3)
+
+
+@pytest.mark.gpu
+def test_gpu_llama_decode_vs_oracle():
+    torch = pytest.importorskip("torch")
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    from cormorant_b200 import workloads as WL
+    from cormorant_b200.llm_runner import LlamaRunner
+    m = WL.LlamaModel(seed=13, batch=2, seq=32, layers=2, vocab=1000)
+    _decode_vs_oracle(LlamaRunner(m), m, 4)
