@@ -19,6 +19,7 @@ F_WRAP32, F_WEIGHT_LOGICAL, F_ACT_RELU, F_ACT_RELU6 = 0x1, 0x2, 0x4, 0x8
 EXPORTS = ("corm_vectorop", "corm_matmul_workspace_size", "corm_matmul", "corm_matmul_noalloc", "corm_conv_workspace_size", "corm_conv",
            "corm_matmul_post", "corm_conv_post", "corm_gemm_strided_workspace_size", "corm_gemm_strided",
            "corm_copy_nd", "corm_llm_attn_softmax", "corm_greedy_embed",
+           "corm_llm_decode_attn",
            "corm_pool", "corm_rowops", "corm_act_table", "corm_smx_table", "corm_rowops_table_image",
            "corm_bind_device", "corm_device_status", "corm_launch_count", "corm_profile_enable",
            "corm_profile_read", "corm_version", "corm_last_error")
@@ -86,6 +87,13 @@ class GreedyDesc(C.Structure):
         _u32_fields(["batch", "vocab", "dim"]) + [("ld", C.c_uint64)]
 
 
+class DecodeAttnDesc(C.Structure):
+    """corm_llm_decode_attn_desc: a decode step's attention of every group."""
+    _fields_ = [("qx", C.c_void_p), ("kc", C.c_void_p), ("vc", C.c_void_p), ("tab", C.c_void_p), ("ip", C.c_void_p),
+                ("o", C.c_void_p)] + _u32_fields(["pos", "B", "KV", "G", "HD", "C", "Q", "window"]) + [
+                ("o_stride", C.c_uint64)]
+
+
 class PoolDesc(C.Structure):
     _fields_ = [("x", C.c_void_p), ("y", C.c_void_p)] + _u32_fields(
         ["batch", "channels", "in_h", "in_w", "out_h", "out_w", "pool_h", "pool_w", "stride_h", "stride_w",
@@ -130,6 +138,7 @@ def lib() -> C.CDLL:
                        ("corm_copy_nd", [C.POINTER(CopyDesc), C.c_void_p]),
                        ("corm_llm_attn_softmax", [C.POINTER(LlmSmxDesc), C.c_void_p]),
                        ("corm_greedy_embed", [C.POINTER(GreedyDesc), C.c_void_p]),
+                       ("corm_llm_decode_attn", [C.POINTER(DecodeAttnDesc), C.c_void_p]),
                        ("corm_pool", [C.POINTER(PoolDesc), C.c_void_p]),
                        ("corm_rowops", [C.POINTER(RowOpsDesc), C.c_void_p]),
                        ("corm_act_table", [C.c_uint32, C.c_uint32, C.c_void_p]),

@@ -150,3 +150,166 @@ extern "C" int corm_greedy_embed(const corm_greedy_desc* d, corm_stream_t stream
   }
   return corm::cuda_status("greedy_embed");
 }
+
+// ---------------------------------------------------------------- decode attention
+// corm_llm_decode_attn — one decode step's attention of every KV group and
+// sequence in one launch (a CTA per (sequence, group)): the q.K^T of the
+// group's G query heads (LlmAttnConvNode "qk": the exact int16 sum, int32
+// wrap, floor / 2^8, sat16), the host's p12 softmax of each head (as
+// llm_smx_kernel), the P.V (LlmAttnConvNode "pv", the same rule), written
+// straight into the merged rows (LlmAttnMergeNode).  Only the keys the
+// softmax reads are scored (P is 0 elsewhere, so the P.V sums are the same).
+namespace {
+
+__device__ __forceinline__ int16_t kernel_out16(long long acc) {
+  const int32_t w = (int32_t)(uint32_t)(unsigned long long)acc;  // the int32 accumulator wraps
+  const int32_t y = w >> 8;                                       // floor / 2^8
+  return (int16_t)(y > 32767 ? 32767 : (y < -32768 ? -32768 : y));
+}
+
+template <int G>
+__global__ void __launch_bounds__(256) decode_attn_kernel(corm_llm_decode_attn_desc d, uint32_t n, uint32_t nk,
+                                                          uint32_t j0) {
+  extern __shared__ __align__(16) uint8_t da_sm[];
+  const uint32_t HD = d.HD, C = d.C;
+  const uint32_t b = blockIdx.x % d.B, g = blockIdx.x / d.B;
+  const uint32_t span = nk - j0;                       // keys the softmax reads
+  double* e = (double*)da_sm;                          // [G][span]
+  double* sums = e + (size_t)G * span;                 // [G]
+  int32_t* q = (int32_t*)(sums + G);                   // [HD][G]
+  int16_t* S = (int16_t*)(q + HD * G);                 // [G][span] scores, then P
+  __shared__ int32_t s_max[8][8];
+  __shared__ long long s_acc[1024];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int16_t* qx = d.qx + ((uint64_t)g * d.B + b) * HD * G;
+  for (uint32_t i = tid; i < HD * G; i += blockDim.x) q[i] = qx[i];
+  __syncthreads();
+  const int16_t* K = d.kc + ((uint64_t)g * d.B + b) * C * HD;
+  const int16_t* V = d.vc + ((uint64_t)g * d.B + b) * C * HD;
+  int16_t* out = d.o + (uint64_t)b * d.o_stride + (uint64_t)g * G * HD;
+  if (n == 0) {  // no valid row: P = 0, so every P.V sum is 0
+    for (uint32_t i = tid; i < G * HD; i += blockDim.x) out[i] = 0;
+    return;
+  }
+  // scores of the keys j0 .. nk - 1: a thread per key, the K row in 16-byte words
+#pragma unroll 2
+  for (uint32_t jj = tid; jj < span; jj += blockDim.x) {
+    const int16_t* kr = K + (uint64_t)(j0 + jj) * HD;
+    long long acc[G];
+#pragma unroll
+    for (int h = 0; h < G; h++) acc[h] = 0;
+    for (uint32_t d0 = 0; d0 < HD; d0 += 8) {
+      const int4 w = *(const int4*)(kr + d0);
+      const int16_t* kv = (const int16_t*)&w;
+#pragma unroll
+      for (int e8 = 0; e8 < 8; e8++)
+#pragma unroll
+        for (int h = 0; h < G; h++) acc[h] += (long long)(kv[e8] * q[(d0 + e8) * G + h]);
+    }
+#pragma unroll
+    for (int h = 0; h < G; h++) S[h * span + jj] = kernel_out16(acc[h]);
+  }
+  __syncthreads();
+  // per head: the max, e in order, the sum left to right (one thread per head), P
+  for (int h = 0; h < G; h++) {
+    int32_t m = INT32_MIN;
+    for (uint32_t jj = tid; jj < span; jj += blockDim.x) m = max(m, (int32_t)S[h * span + jj]);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = max(m, __shfl_xor_sync(0xffffffffu, m, o));
+    if (lane == 0) s_max[h & 7][warp] = m;
+    __syncthreads();
+    m = s_max[h & 7][0];
+    for (int w = 1; w < (int)(blockDim.x >> 5); w++) m = max(m, s_max[h & 7][w]);
+    const double* tab = d.tab + (uint64_t)(g * G + h) * 65536u;
+#pragma unroll 4
+    for (uint32_t jj = tid; jj < span; jj += blockDim.x) e[h * span + jj] = __ldg(tab + (m - (int32_t)S[h * span + jj]));
+    __syncthreads();
+  }
+  if (tid < G) {
+    double sum = 0.0;
+#pragma unroll 8
+    for (uint32_t jj = 0; jj < span; jj++) sum += e[tid * span + jj];  // in key order
+    sums[tid] = sum;
+  }
+  __syncthreads();
+  for (uint32_t i = tid; i < G * span; i += blockDim.x) {
+    const uint32_t h = i / span;
+    const double qv = rint((e[i] / sums[h]) * d.ip[g * G + h]);
+    S[i] = (int16_t)(qv > 32767.0 ? 32767.0 : qv);  // P replaces the scores
+  }
+  __syncthreads();
+  // P.V: HD columns x (256 / HD) key groups, int64 sums, reduced in shared memory
+  const uint32_t groups = blockDim.x / HD, col = tid % HD, kg = tid / HD;
+  long long acc[G];
+#pragma unroll
+  for (int h = 0; h < G; h++) acc[h] = 0;
+  if (kg < groups)
+    for (uint32_t base = kg; base < span; base += 8u * groups) {  // 8 loads in flight per thread
+      int32_t vv[8];
+#pragma unroll
+      for (int u = 0; u < 8; u++) {
+        const uint32_t jj = base + u * groups;
+        vv[u] = jj < span ? (int32_t)__ldg(V + (uint64_t)(j0 + jj) * HD + col) : 0;
+      }
+#pragma unroll
+      for (int u = 0; u < 8; u++) {
+        const uint32_t jj = base + u * groups;
+        if (jj < span) {
+#pragma unroll
+          for (int h = 0; h < G; h++) acc[h] += (long long)(S[h * span + jj] * vv[u]);
+        }
+      }
+    }
+#pragma unroll
+  for (int h = 0; h < G; h++) {
+    if (kg < groups) s_acc[kg * HD + col] = acc[h];
+    __syncthreads();
+    if (tid < (int)HD) {
+      long long t = 0;
+      for (uint32_t k2 = 0; k2 < groups; k2++) t += s_acc[k2 * HD + tid];
+      out[h * HD + tid] = kernel_out16(t);
+    }
+    __syncthreads();
+  }
+}
+
+}  // namespace
+
+extern "C" int corm_llm_decode_attn(const corm_llm_decode_attn_desc* d, corm_stream_t stream) {
+  if (!d) return corm::fail(CORM_EINVAL, "corm_llm_decode_attn: null descriptor");
+  if (int rc = corm::check_device()) return rc;
+  if (!d->qx || !d->kc || !d->vc || !d->tab || !d->ip || !d->o)
+    return corm::fail(CORM_EINVAL, "corm_llm_decode_attn: null buffer");
+  if (d->B == 0 || d->KV == 0) return CORM_OK;
+  if (d->G == 0 || d->G > 8 || d->HD == 0 || d->HD % 8 || 256 % d->HD || d->HD * 4 > 1024 || d->Q == 0 ||
+      d->C % d->Q || d->o_stride < (uint64_t)d->KV * d->G * d->HD)
+    return corm::fail(CORM_EINVAL, "corm_llm_decode_attn: G %u (<= 8), HD %u (a divisor of 256, % 8), C %% Q",
+                      d->G, d->HD);
+  if (((uintptr_t)d->kc | (uintptr_t)d->vc) & 15u) return corm::fail(CORM_EINVAL, "corm_llm_decode_attn: unaligned caches");
+  // one query row (T = 1, n = 1) clamped as LlmAttention: none past the cache
+  const uint32_t n = d->pos >= d->C ? 0u : 1u;
+  const uint32_t nk = n ? d->pos + 1u : 1u;
+  const uint32_t j0 = (n && d->window && nk > d->window) ? nk - d->window : 0u;
+  const size_t span = nk - j0;
+  const size_t smem = d->G * span * 8 + d->G * 8 + (size_t)d->HD * d->G * 4 + d->G * span * 2 + 16;
+  if (smem > 200 * 1024) return corm::fail(CORM_ELIMIT, "corm_llm_decode_attn: %zu keys beyond the shared memory", span);
+  cudaStream_t st = (cudaStream_t)stream;
+  auto launch = [&](auto kern) {
+    if (smem > 48 * 1024) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    kern<<<d->B * d->KV, 256, smem, st>>>(*d, n, nk, j0);
+  };
+  {
+    corm::ProfScope prof_("decode_attn_kernel", st);
+    switch (d->G) {
+      case 1: launch(decode_attn_kernel<1>); break;
+      case 2: launch(decode_attn_kernel<2>); break;
+      case 3: launch(decode_attn_kernel<3>); break;
+      case 4: launch(decode_attn_kernel<4>); break;
+      case 5: launch(decode_attn_kernel<5>); break;
+      case 6: launch(decode_attn_kernel<6>); break;
+      case 7: launch(decode_attn_kernel<7>); break;
+      default: launch(decode_attn_kernel<8>); break;
+    }
+  }
+  return corm::cuda_status("llm_decode_attn");
+}

@@ -145,6 +145,19 @@ def llm_attn_softmax(s, p, tab, ip, *, pos, n, T, G, rows, Q=16, window=0, batch
     check(lib().corm_llm_attn_softmax(C.byref(d), st))
 
 
+def llm_decode_attn(qx, kc, vc, tab, ip, o, *, pos, B, KV, G, HD, rows, Q=16, window=0, o_stride=None):
+    """corm_llm_decode_attn: a decode step's q.K^T, host softmax, P.V and head
+    merge of every KV group and sequence (caches of ``rows`` rows)."""
+    for t, nm in ((qx, "qx"), (kc, "kc"), (vc, "vc"), (o, "o")):
+        _i16(t, nm)
+    if tab.dtype != torch.float64 or ip.dtype != torch.float64:
+        raise CormError(_lib.CORM_EINVAL, "tab / ip must be float64")
+    st = _ready()
+    d = _lib.DecodeAttnDesc(_ptr(qx), _ptr(kc), _ptr(vc), _ptr(tab), _ptr(ip), _ptr(o), pos, B, KV, G, HD, rows, Q,
+                            window, KV * G * HD if o_stride is None else o_stride)
+    check(lib().corm_llm_decode_attn(C.byref(d), st))
+
+
 def greedy_embed(logits, table, out, ids=None, *, batch, vocab, dim, ld=None):
     """corm_greedy_embed: ids = first argmax of each int16 logits row; out
     (int32) = those rows of the int32 table."""

@@ -314,6 +314,12 @@ class GpuSimulator:
                     if t is not None:
                         last[t.onnx_name] = i
                 last.setdefault(sn.output.onnx_name, i)
+            # a fused decode attention reads its blocks' inputs at the merge
+            for mi, info in (self._decode_attn_plan(keep) if self.fuse else {}).items():
+                for j in info["nodes"]:
+                    for t in self._graph.nodes[j].inputs:
+                        if t is not None:
+                            last[t.onnx_name] = max(last.get(t.onnx_name, mi), mi)
             wnames = {t.onnx_name for t in self._graph.weight_tensors}
             for name, i in last.items():
                 if name not in keep and name not in wnames and name not in snames:
@@ -325,6 +331,9 @@ class GpuSimulator:
                 meta[t.onnx_name] = t
         fused_into = {j: (i, flag, post) for i, (j, flag, post) in self._plan.items()}
         skip = set(self._plan)
+        attn_fused = self._decode_attn_plan(keep) if (self.fuse and keep is not None) else {}
+        for _mi, info in attn_fused.items():
+            skip |= set(info["nodes"])
 
         def get(t):
             if t.onnx_name not in raw:
@@ -381,6 +390,8 @@ class GpuSimulator:
                 y = self._attn_softmax(sn, get)
             elif kind == "LlmAttnSoftmaxNode":
                 y = self._attn_softmax_host(sn, get)
+            elif kind == "LlmAttnMergeNode" and i in attn_fused:
+                y = self._decode_attn(sn, attn_fused[i], get)
             elif kind == "LlmAttnMergeNode":
                 y = self._attn_merge(sn, get)
             elif kind == "LlmSelectRowNode":
@@ -464,13 +475,24 @@ class GpuSimulator:
                     out_w=sn.out_w, kh=sn.kh, kw=sn.kw, stride_h=sn.stride_h, stride_w=sn.stride_w,
                     dilation_h=sn.dilation_h, dilation_w=sn.dilation_w, pad_top=sn.pad_top, pad_left=sn.pad_left,
                     has_bias=int(bool(sn.has_bias)), is_depthwise=int(bool(sn.is_depthwise)))
-        K = sn.in_ch * sn.kh * sn.kw
-        Kp = (K + 15) // 16 * 16
-        need = 0 if sn.is_depthwise else 2 * ((sn.batch * sn.out_h * sn.out_w * Kp + 255) // 256 * 256) + \
-            2 * ((sn.out_ch * Kp + 255) // 256 * 256)
+        need = self._conv_ws(regs, F_WEIGHT_LOGICAL | wrap | flag)
         ops.conv(x, w, b, y, flags=F_WEIGHT_LOGICAL | wrap | flag,
                  workspace=self._workspace(need) if need else None, post=post, **regs)
         return y
+
+    @staticmethod
+    def _conv_ws(regs, flags) -> int:
+        """Bytes of scratch the library asks for the conv job (its split planes
+        and K-split partial sums)."""
+        import ctypes as C
+
+        from . import _lib
+        d = _lib.ConvDesc(0, 0, 0, 0, *(int(regs[k]) for k in (
+            "batch", "in_ch", "in_h", "in_w", "out_ch", "out_h", "out_w", "kh", "kw", "stride_h", "stride_w",
+            "dilation_h", "dilation_w", "pad_top", "pad_left", "has_bias", "is_depthwise")), 0, 0, 0, flags, None, 0)
+        need = C.c_size_t(0)
+        _lib.check(_lib.lib().corm_conv_workspace_size(C.byref(d), C.byref(need)))
+        return need.value
 
     def _pool(self, sn, x):
         y = self._alloc(sn.output.numel)
@@ -682,6 +704,82 @@ class GpuSimulator:
         y = self._alloc(sn.output.numel)
         ops.llm_attn_softmax(get(sn.inputs[0]), y, tab, ip, pos=pos, n=max(n, 0), T=sn.T, G=sn.G, rows=sn.C, Q=sn.Q,
                              window=int(getattr(sn, "window", 0)), batch=B)
+        return y
+
+    def _decode_attn_plan(self, keep) -> dict:
+        """{merge node index: plan} for the decode steps' attention blocks whose
+        intermediates nobody observes: per KV group a q.K^T (T = 1, no n, all
+        keys), the host softmax and the P.V, merged — run as one
+        corm_llm_decode_attn launch at the merge."""
+        key = frozenset(keep)
+        cache = self.__dict__.setdefault("_attn_plans", {})
+        if key in cache:
+            return cache[key]
+        nodes = self._graph.nodes
+        producer = {sn.output.onnx_name: i for i, sn in enumerate(nodes)}
+        readers: Dict[str, int] = {}
+        for sn in nodes:
+            for t in sn.inputs:
+                if t is not None:
+                    readers[t.onnx_name] = readers.get(t.onnx_name, 0) + 1
+        plans = {}
+        for mi, mn in enumerate(nodes):
+            if _kind(mn) != "LlmAttnMergeNode" or int(getattr(mn, "R", 1)) != 1 or mn.T != 1:
+                continue
+            idx, qks, smxs, pvs, ok = [], [], [], [], True
+            for g, o in enumerate(mn.inputs):
+                pi = producer.get(o.onnx_name)
+                pv = nodes[pi] if pi is not None else None
+                if pv is None or _kind(pv) != "LlmAttnConvNode" or pv.kind != "pv" or pv.group != g:
+                    ok = False
+                    break
+                si = producer.get(pv.inputs[0].onnx_name)
+                sm = nodes[si] if si is not None else None
+                if sm is None or _kind(sm) != "LlmAttnSoftmaxNode" or sm.group != g or not sm.causal:
+                    ok = False
+                    break
+                qi = producer.get(sm.inputs[0].onnx_name)
+                qk = nodes[qi] if qi is not None else None
+                if qk is None or _kind(qk) != "LlmAttnConvNode" or qk.kind != "qk" or qk.group != g or qk.nr:
+                    ok = False
+                    break
+                for nd in (qk, sm, pv):
+                    if nd.T != 1 or getattr(nd, "has_n", True) or getattr(nd, "static", False) or \
+                            nd.output.onnx_name in keep or readers.get(nd.output.onnx_name, 0) != 1:
+                        ok = False
+                if qks and (qk.inputs[1].onnx_name != qks[0].inputs[1].onnx_name or
+                            qk.inputs[0].onnx_name != qks[0].inputs[0].onnx_name or
+                            pv.inputs[1].onnx_name != pvs[0].inputs[1].onnx_name or
+                            sm.window != smxs[0].window or sm.scale != smxs[0].scale):
+                    ok = False
+                idx += [qi, si, pi]
+                qks.append(qk)
+                smxs.append(sm)
+                pvs.append(pv)
+            if ok and qks and len(qks) == mn.KV:
+                plans[mi] = {"nodes": idx, "qk": qks, "smx": smxs, "pv": pvs}
+        cache[key] = plans
+        return plans
+
+    def _decode_attn(self, mn, plan, get):
+        """The fused decode attention (corm_llm_decode_attn) of a plan: the
+        exp tables of every head's score exponent, 2^f_p per head."""
+        from .attention import sexp_table
+        qk0, sm0 = plan["qk"][0], plan["smx"][0]
+        G, B = sm0.G, int(getattr(sm0, "batch", 1))
+        fs = tuple(int(v) for sm in plan["smx"] for v in np.asarray(sm.fs).reshape(-1))
+        fp = tuple(int(v) for sm in plan["smx"] for v in np.asarray(sm.fp).reshape(-1))
+        key = ("sexp", fs, fp, float(sm0.scale))
+        if key not in self._weights:
+            tab = np.concatenate([sexp_table(f, float(sm0.scale)) for f in fs])
+            self._weights[key] = (torch.from_numpy(tab).to(self.device),
+                                  torch.tensor([2.0 ** f for f in fp], dtype=torch.float64, device=self.device))
+        tab, ip = self._weights[key]
+        pos = self._host_int(get, qk0.inputs[2])
+        y = self._alloc(mn.output.numel)
+        ops.llm_decode_attn(get(qk0.inputs[1]), get(qk0.inputs[0]), get(plan["pv"][0].inputs[1]), tab, ip, y, pos=pos,
+                            B=B, KV=mn.KV, G=G, HD=mn.HD, rows=qk0.C, Q=qk0.Q, window=int(getattr(sm0, "window", 0)),
+                            o_stride=mn.H * mn.HD)
         return y
 
     def _attn_merge(self, sn, get):

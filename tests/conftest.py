@@ -129,6 +129,34 @@ def cpu_ops(monkeypatch):
         if ids is not None:
             ids.numpy()[:batch] = nxt
 
+    def llm_decode_attn(qx, kc, vc, tab, ip, o, *, pos, B, KV, G, HD, rows, Q=16, window=0, o_stride=None):
+        from oracle import attn as A
+        C = rows
+        q = qx.numpy()[:KV * B * HD * G].astype(np.int64).reshape(KV, B, HD, G)
+        K = kc.numpy()[:KV * B * C * HD].astype(np.int64).reshape(KV, B, C, HD)
+        V = vc.numpy()[:KV * B * C * HD].astype(np.int64).reshape(KV, B, C, HD)
+        tabs = tab.numpy().reshape(KV * G, 65536)
+        out = o.numpy()
+        ost = KV * G * HD if o_stride is None else o_stride
+        n, keys = A.attn_keys(pos, 1, 1, C, Q)
+        for b in range(B):
+            for g in range(KV):
+                s = A.kernel_out(K[g, b, :keys] @ q[g, b])                 # [keys][G]
+                P = np.zeros((G, C), np.int64)
+                if n:
+                    nk = pos + 1
+                    j0 = nk - window if (window and nk > window) else 0
+                    for h in range(G):
+                        r = s[j0:nk, h]
+                        e = tabs[g * G + h][r.max() - r]
+                        ssum = 0.0
+                        for v in e:
+                            ssum += v
+                        P[h, j0:nk] = np.minimum(np.rint((e / ssum) * ip.numpy()[g * G + h]), 32767)
+                ob = A.kernel_out(P[:, :keys] @ V[g, b, :keys])            # [G][HD]
+                out[b * ost + g * G * HD: b * ost + (g + 1) * G * HD] = ob.reshape(-1)
+
+    monkeypatch.setattr(ops, "llm_decode_attn", llm_decode_attn)
     monkeypatch.setattr(ops, "llm_attn_softmax", llm_attn_softmax)
     monkeypatch.setattr(ops, "greedy_embed", greedy_embed)
     monkeypatch.setattr(ops, "gemm_strided", gemm_strided)
