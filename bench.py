@@ -191,7 +191,8 @@ def main():
     ap.add_argument("--no-models", action="store_true", help="skip the MNIST / MobileNetV2 / BERT forward passes")
     ap.add_argument("--models", help="comma list of model cases to run (default: all)")
     ap.add_argument("--detail", help="write per-problem kernel times of one profiled step to this JSON file")
-    ap.add_argument("--case", choices=["gemm", "gemm_small", "vectorop", "softmax", "conv"],
+    ap.add_argument("--case", choices=["gemm", "gemm_small", "vectorop", "softmax", "conv", "llama_prefill",
+                                       "llama_decode"],
                     help="run one job a few times (a small case for ncu captures) and exit")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
@@ -568,6 +569,16 @@ def bench_llama_decode(torch, dev, stream, flush, args, world, pg, steps=128):
            "GMAC/s": round(rate * macs / 1e9, 1), "mmac_per_token": round(macs / 1e6, 2),
            "graph_nodes_per_step": len(m.decode_graph.nodes),
            "first_ids": ids[0, :4].cpu().tolist()}
+    if args.detail:  # per-kernel device time of one eager decode step
+        from cormorant_b200 import ops
+        ops.profile_read()
+        ops.profile_enable(True)
+        with torch.cuda.stream(stream):
+            r.decode_step(lg0, 0)
+        ops.profile_enable(False)
+        prof = ops.profile_read()
+        out["kernels"] = {k: {"launches": v[0], "ms": round(v[1], 4)}
+                          for k, v in sorted(prof.items(), key=lambda kv: -kv[1][1])}
     del graphs, r
     torch.cuda.empty_cache()
     return out
@@ -653,6 +664,16 @@ def run_case(args):
         x, p = ri(N, -2048, 2048), torch.empty(N, dtype=torch.int16, device="cuda")
         fn = lambda: ops.vectorop(x, None, p, size=1024, op=10, outer=N // 1024, a_inc=1024, b_inc=1024,  # noqa
                                   smx_cm=12102203, smx_cfg=19 | (8 << 8), smx_mask=1024)
+    elif args.case in ("llama_prefill", "llama_decode"):
+        # two layers of the config-5 model (every kernel of a layer, a layer's
+        # shapes): the prefill of 16 sequences x 512 tokens, or after it one
+        # decode step of the 16 (lean passes, as the bench runs them)
+        from cormorant_b200 import workloads as WL
+        from cormorant_b200.llm_runner import LlamaRunner
+        m = WL.LlamaModel(seed=5, batch=16, seq=512, layers=2)
+        r = LlamaRunner(m)
+        lg = r.prefill()
+        fn = (lambda: r.prefill()) if args.case == "llama_prefill" else (lambda: r.decode_step(lg, 0))  # noqa
     else:
         x = ri(64 * 144 * 56 * 56)
         w = ri(24 * 144, -64, 64)
