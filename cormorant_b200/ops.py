@@ -222,6 +222,26 @@ def rowops(a, b, c, p, *, op, n, rows=1, blocks=1, a_s1=0, a_s2=0, b_s1=0, b_s2=
     check(lib().corm_rowops(C.byref(d), st))
 
 
+def rowops_chain(jobs):
+    """A descriptor chain (corm_rowops_chain): ``jobs`` a list of dicts with
+    the keys of ``rowops`` (a, b, c, p as tensors or raw addresses, plus byte
+    offsets), run in order, at most 16."""
+    st = _ready()
+
+    def addr(t, off):
+        return (_ptr(t) + off) if t is not None else 0
+    arr = (_lib.RowOpsDesc * max(1, len(jobs)))()
+    for k, j in enumerate(jobs):
+        g = lambda key, dflt=0: j.get(key, dflt)  # noqa: E731
+        arr[k] = _lib.RowOpsDesc(j["op"], j["n"], g("rows", 1), g("blocks", 1), addr(g("a", None), g("a_off")),
+                                 g("a_s1") & 0xFFFFFFFF, g("a_s2") & 0xFFFFFFFF, addr(g("b", None), g("b_off")),
+                                 g("b_s1") & 0xFFFFFFFF, g("b_s2") & 0xFFFFFFFF, addr(g("c", None), g("c_off")),
+                                 g("c_s1") & 0xFFFFFFFF, g("c_s2") & 0xFFFFFFFF, addr(g("p", None), g("p_off")),
+                                 g("eps") & 0xFFFFFFFFFFFFFFFF, g("aux"), g("bq_sh"), g("win_lo") & 0xFFFFFFFF,
+                                 g("win_hi", 0xFFFFFFFF) & 0xFFFFFFFF)
+    check(lib().corm_rowops_chain(arr, len(jobs), st))
+
+
 def device_status() -> int:
     """Synchronise and return (and clear) the kernels' timeout status word."""
     _ready()

@@ -228,6 +228,27 @@ typedef struct {
 
 int corm_greedy_embed(const corm_greedy_desc* d, corm_stream_t stream);
 
+/* corm_llm_decode_attn: one decode step's attention (T = 1) of every KV group
+ * of B sequences in one launch — per (sequence b, group g) the q.K^T of the
+ * group's G heads over the cache rows the softmax reads (LlmAttnConvNode
+ * "qk": exact sum, int32 wrap, floor / 2^8, sat16), the host's p12 softmax
+ * (as corm_llm_attn_softmax), the P.V (LlmAttnConvNode "pv") and the head
+ * merge (LlmAttnMergeNode): o[b * o_stride + (g G + h') HD + d].  qx: the q
+ * image [KV][B][HD][G]; kc / vc: the caches [KV][B][C][HD]; tab: [KV G][65536]
+ * float64 per head; ip: [KV G] float64 2^f_p.  G <= 8, HD a divisor of 256. */
+typedef struct {
+  const int16_t* qx;
+  const int16_t* kc;
+  const int16_t* vc;
+  const double* tab;
+  const double* ip;
+  int16_t* o;
+  uint32_t pos, B, KV, G, HD, C, Q, window;
+  uint64_t o_stride;
+} corm_llm_decode_attn_desc;
+
+int corm_llm_decode_attn(const corm_llm_decode_attn_desc* d, corm_stream_t stream);
+
 /* ---------------------------------------------------------------- Pool
  * Replaces run_pool / XPoolingkernel (inference-scheduler/src/codegen/
  * _source.py:1548-1580; semantics inference-scheduler/src/codegen/
@@ -266,6 +287,11 @@ typedef struct {
 } corm_rowops_desc;
 
 int corm_rowops(const corm_rowops_desc* d, corm_stream_t stream);
+/* A descriptor chain (host_emu.py:731-749, rowops_ref.h:428-441): the jobs in
+ * order, at most 16, each seeing the writes of the ones before.  Every job
+ * (chained or not) keeps the unit's parameter RAM: a job that streams
+ * parameters loads it from p unless P_KEEP, and a P_KEEP job reads it. */
+int corm_rowops_chain(const corm_rowops_desc* jobs, uint32_t count, corm_stream_t stream);
 
 /* ---------------------------------------------------------------- host-side helpers (no GPU) */
 /* The activation unit's output for every Q8.8 input (raw -32768 .. 32767 at

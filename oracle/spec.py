@@ -606,11 +606,27 @@ def _fold_elem(x: int, m: int, s: int) -> int:
     return -q if x < 0 else q
 
 
+class ParamRAM:
+    """The unit's parameter RAM between jobs (RR:86-95): column c's entry at
+    ram[c], or with a broadcast load every column reads entry 0 (the load
+    writes index 0 of all four banks); ``valid`` once a job has loaded."""
+
+    def __init__(self):
+        self.ram = [(0, 0, 0, 0, 0)] * 4096
+        self.valid = False
+        self.bcast = False
+
+    def at(self, c: int):
+        return self.ram[(c & 3) if self.bcast else c]
+
+
 def rowops_job(mem: RowOpsMem, op: int, n: int, c1: int, c2: int, a: int, a_s1: int, a_s2: int, b: int,
                b_s1: int, b_s2: int, c: int, c_s1: int, c_s2: int, p: int, eps: int = 0, aux: int = 0,
-               bq_sh: int = 0, win_lo: int = 0, win_hi: int = 0xFFFFFFFF) -> None:
-    """One RowOpsKernel job on ``mem`` (RR:259-427, HE:611-730), without the
-    parameter-RAM state (a P_KEEP job reads its block from p)."""
+               bq_sh: int = 0, win_lo: int = 0, win_hi: int = 0xFFFFFFFF, ps: Optional[ParamRAM] = None) -> None:
+    """One RowOpsKernel job on ``mem`` (RR:259-427, HE:611-730).  ``ps``: the
+    parameter RAM carried between the jobs of a chain (RR:262-276) — a job
+    with work loads it from p unless it is P_KEEP (and the RAM holds a load),
+    and a P_KEEP job reads it; without ``ps`` a P_KEEP job reads p."""
     code = op & 15
     if code == RO_TLOAD:
         return
@@ -635,8 +651,19 @@ def rowops_job(mem: RowOpsMem, op: int, n: int, c1: int, c2: int, a: int, a_s1: 
     if n == 0 or c1 == 0 or c2 == 0 or n > 4096:
         return
     nb = lambda kd: 2 if kd == K_I16 else 4  # noqa: E731
-    P = [_param(mem, p, cc, bool(bcast)) for cc in range(1 if bcast else n)]
-    prm = (lambda cc: P[0]) if bcast else (lambda cc: P[cc])
+    keep = bool(op & F_P_KEEP) and ps is not None and ps.valid
+    if code in (RO_COPY, RO_ADDX, RO_DEQUANT, RO_MULACT, RO_GATE, RO_NORM, RO_ROPE) and keep:
+        prm = ps.at
+    else:
+        P = [_param(mem, p, cc, bool(bcast)) for cc in range(1 if bcast else n)]
+        prm = (lambda cc: P[0]) if bcast else (lambda cc: P[cc])
+        if ps is not None and code in (RO_COPY, RO_ADDX, RO_DEQUANT, RO_MULACT, RO_GATE, RO_NORM, RO_ROPE):
+            ram = list(ps.ram)
+            if bcast:
+                ram[0:4] = [P[0]] * 4
+            else:
+                ram[0:n] = P
+            ps.ram, ps.valid, ps.bcast = ram, True, bool(bcast)
     for i2 in range(c2):
         for i1 in range(c1):
             ra, rb, rc = a + i2 * a_s2 + i1 * a_s1, b + i2 * b_s2 + i1 * b_s1, c + i2 * c_s2 + i1 * c_s1
