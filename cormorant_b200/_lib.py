@@ -19,7 +19,8 @@ F_WRAP32, F_WEIGHT_LOGICAL, F_ACT_RELU, F_ACT_RELU6 = 0x1, 0x2, 0x4, 0x8
 EXPORTS = ("corm_vectorop", "corm_matmul_workspace_size", "corm_matmul", "corm_matmul_noalloc", "corm_conv_workspace_size", "corm_conv",
            "corm_matmul_post", "corm_conv_post", "corm_gemm_strided_workspace_size", "corm_gemm_strided",
            "corm_copy_nd", "corm_llm_attn_softmax", "corm_greedy_embed",
-           "corm_llm_decode_attn", "corm_rowops_chain",
+           "corm_llm_decode_attn", "corm_rowops_chain", "corm_rowops_chain_dev",
+           "corm_stream_done",
            "corm_pool", "corm_rowops", "corm_act_table", "corm_smx_table", "corm_rowops_table_image",
            "corm_bind_device", "corm_device_status", "corm_launch_count", "corm_profile_enable",
            "corm_profile_read", "corm_version", "corm_last_error")

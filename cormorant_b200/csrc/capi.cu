@@ -244,3 +244,10 @@ const char* corm_last_error(void) { return corm::g_err; }
 
 
 }  // extern "C"
+
+extern "C" int corm_stream_done(corm_stream_t stream) {
+  const cudaError_t e = cudaStreamQuery((cudaStream_t)stream);
+  if (e == cudaSuccess) return 1;
+  if (e == cudaErrorNotReady) return 0;
+  return corm::cuda_status("corm_stream_done");
+}

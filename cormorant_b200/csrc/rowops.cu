@@ -769,6 +769,32 @@ extern "C" int corm_rowops_chain(const corm_rowops_desc* jobs, uint32_t count, c
   return CORM_OK;
 }
 
+extern "C" int corm_rowops_chain_dev(const void* desc, uint32_t count, corm_stream_t stream) {
+  if (!desc && count) return corm::fail(CORM_EINVAL, "corm_rowops_chain_dev: null descriptor list");
+  if (int rc = corm::check_device()) return rc;
+  const uint32_t nj = count > 16u ? 16u : count;
+  if (!nj) return CORM_OK;
+  uint32_t w[16 * 32];
+  cudaStream_t st = (cudaStream_t)stream;
+  // the list lives in device memory (the board's DDR): read it in stream order
+  if (cudaMemcpyAsync(w, desc, 128u * nj, cudaMemcpyDeviceToHost, st) != cudaSuccess ||
+      cudaStreamSynchronize(st) != cudaSuccess)
+    return corm::cuda_status("rowops chain descriptors");
+  corm_rowops_desc jobs[16];
+  for (uint32_t k = 0; k < nj; k++) {
+    const uint32_t* d = w + 32 * k;
+    auto u64 = [&](int i) { return (uint64_t)d[i] | ((uint64_t)d[i + 1] << 32); };
+    corm_rowops_desc& j = jobs[k];
+    j.op = d[0]; j.n = d[1]; j.rows = d[2]; j.blocks = d[3];
+    j.a = (const void*)(uintptr_t)u64(4); j.a_s1 = d[6]; j.a_s2 = d[7];
+    j.b = (const void*)(uintptr_t)u64(8); j.b_s1 = d[10]; j.b_s2 = d[11];
+    j.c = (void*)(uintptr_t)u64(12); j.c_s1 = d[14]; j.c_s2 = d[15];
+    j.p = (const void*)(uintptr_t)u64(16); j.eps = u64(18);
+    j.aux = d[20]; j.bq_sh = d[21]; j.win_lo = d[22]; j.win_hi = d[23];
+  }
+  return corm_rowops_chain(jobs, nj, stream);
+}
+
 namespace {
 int rowops_job(const corm_rowops_desc* d0, cudaStream_t st) {
   const uint32_t op = d0->op & 15u;

@@ -292,6 +292,12 @@ int corm_rowops(const corm_rowops_desc* d, corm_stream_t stream);
  * (chained or not) keeps the unit's parameter RAM: a job that streams
  * parameters loads it from p unless P_KEEP, and a P_KEEP job reads it. */
 int corm_rowops_chain(const corm_rowops_desc* jobs, uint32_t count, corm_stream_t stream);
+/* The same with the board's descriptor list in device memory: count 128-byte
+ * descriptors at desc, words 0..23 the registers 0x10..0x6C in order (op, n,
+ * rows, blocks, a lo / hi, a_s1, a_s2, b lo / hi, b_s1, b_s2, c lo / hi, c_s1,
+ * c_s2, p lo / hi, eps lo / hi, aux, bq_sh, win_lo, win_hi).  Reads the list
+ * in stream order (a synchronisation of the stream), then runs the chain. */
+int corm_rowops_chain_dev(const void* desc, uint32_t count, corm_stream_t stream);
 
 /* ---------------------------------------------------------------- host-side helpers (no GPU) */
 /* The activation unit's output for every Q8.8 input (raw -32768 .. 32767 at
@@ -311,6 +317,9 @@ int corm_bind_device(int device);
  * kernels' bounded waits set when a wait times out (0 = none).  Replaces the
  * reference's kernel_wait timeout accounting (runtime/inference_irq.c:259-264). */
 int corm_device_status(int* code);
+/* 1 when every job issued to the stream has finished, 0 while work remains
+ * (the drivers' IsDone / IsIdle), or a negative CUDA error. */
+int corm_stream_done(corm_stream_t stream);
 /* Library version string and the last error message of the calling thread. */
 /* Tracing (the analogue of the reference's per-layer profiling aggregates,
  * runtime/inference_prof.h): corm_launch_count() counts every kernel launch of
