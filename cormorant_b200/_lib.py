@@ -92,7 +92,9 @@ class DecodeAttnDesc(C.Structure):
     """corm_llm_decode_attn_desc: a decode step's attention of every group."""
     _fields_ = [("qx", C.c_void_p), ("kc", C.c_void_p), ("vc", C.c_void_p), ("tab", C.c_void_p), ("ip", C.c_void_p),
                 ("o", C.c_void_p)] + _u32_fields(["pos", "B", "KV", "G", "HD", "C", "Q", "window"]) + [
-                ("o_stride", C.c_uint64)]
+                ("o_stride", C.c_uint64), ("q0", C.c_void_p), ("k0", C.c_void_p), ("v0", C.c_void_p),
+                ("ldq", C.c_uint64), ("ldk", C.c_uint64), ("ldv", C.c_uint64), ("rope", C.c_void_p),
+                ("pq", C.c_void_p), ("pk", C.c_void_p), ("pv", C.c_void_p), ("prep", C.c_uint32)]
 
 
 class PoolDesc(C.Structure):

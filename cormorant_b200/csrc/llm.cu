@@ -181,11 +181,58 @@ __global__ void __launch_bounds__(256) decode_attn_kernel(corm_llm_decode_attn_d
   __shared__ int32_t s_max[8][8];
   __shared__ long long s_acc[1024];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int16_t* qx = d.qx + ((uint64_t)g * d.B + b) * HD * G;
-  for (uint32_t i = tid; i < HD * G; i += blockDim.x) q[i] = qx[i];
-  __syncthreads();
-  const int16_t* K = d.kc + ((uint64_t)g * d.B + b) * C * HD;
-  const int16_t* V = d.vc + ((uint64_t)g * d.B + b) * C * HD;
+  int16_t* Kw = d.kc + ((uint64_t)g * d.B + b) * C * HD;
+  int16_t* Vw = d.vc + ((uint64_t)g * d.B + b) * C * HD;
+  if (d.prep & 1u) {
+    // the step's AttnPrep: RoPE of this group's k row and of its G q heads (the
+    // cos / sin row of pos), v re-rounded, the new cache rows written
+    const uint32_t half = HD / 2;
+    const int32_t* cs_row = d.rope + (uint64_t)d.pos * 2u * HD;
+    const int16_t* k0 = d.k0 + (uint64_t)b * d.ldk + g * HD;
+    const int16_t* v0 = d.v0 + (uint64_t)b * d.ldv + g * HD;
+    for (uint32_t i = tid; i < (G + 2) * HD; i += blockDim.x) {
+      const uint32_t dd = i % HD, part = i / HD;  // parts 0 .. G-1: q heads, G: k, G + 1: v
+      if (part <= (uint32_t)G && n == 0) {
+        if (part < (uint32_t)G) q[dd * G + part] = 0;  // no valid row: a zero image
+        continue;
+      }
+      if (part == (uint32_t)G + 1) {
+        if (n == 0) continue;
+        const int16_t x = v0[dd];
+        int16_t y = x;
+        if (!(d.prep & 16u)) {
+          const uint8_t* e = (const uint8_t*)d.pv + 16u * ((d.prep & 8u) ? 0u : g * HD + dd);
+          int32_t bq;
+          memcpy(&bq, e + 4, 4);
+          bq = (int32_t)((uint32_t)bq << 10) >> 10;
+          const __int128 sum = ((__int128)x << (e[8] & 63u)) + (__int128)bq;
+          y = (int16_t)corm_sat16_128(corm_rne_shr128(sum, (int)(e[10] & 63u)));
+        }
+        Vw[(uint64_t)d.pos * HD + dd] = y;
+        continue;
+      }
+      const bool is_k = part == (uint32_t)G;
+      const int16_t* src = is_k ? k0 : d.q0 + (uint64_t)b * d.ldq + (g * G + part) * HD;
+      const uint32_t col = is_k ? g * HD + dd : (g * G + part) * HD + dd;
+      const uint8_t* e = (const uint8_t*)(is_k ? d.pk : d.pq) +
+                         16u * ((d.prep & (is_k ? 4u : 2u)) ? 0u : col);
+      const int64_t x = src[dd];
+      const int64_t rot = dd < half ? -(int64_t)src[dd + half] : (int64_t)src[dd - half];
+      const __int128 sum = ((__int128)(x * cs_row[dd]) << (e[8] & 63u)) +
+                           ((__int128)(rot * cs_row[HD + dd]) << (e[9] & 63u));
+      const int16_t y = (int16_t)corm_sat16_128(corm_rne_shr128(sum, (int)(e[10] & 63u)));
+      if (is_k)
+        Kw[(uint64_t)d.pos * HD + dd] = y;
+      else
+        q[dd * G + part] = y;
+    }
+  } else {
+    const int16_t* qx = d.qx + ((uint64_t)g * d.B + b) * HD * G;
+    for (uint32_t i = tid; i < HD * G; i += blockDim.x) q[i] = qx[i];
+  }
+  __syncthreads();  // the new cache rows and the q image visible to the block
+  const int16_t* K = Kw;
+  const int16_t* V = Vw;
   int16_t* out = d.o + (uint64_t)b * d.o_stride + (uint64_t)g * G * HD;
   if (n == 0) {  // no valid row: P = 0, so every P.V sum is 0
     for (uint32_t i = tid; i < G * HD; i += blockDim.x) out[i] = 0;
@@ -278,8 +325,11 @@ __global__ void __launch_bounds__(256) decode_attn_kernel(corm_llm_decode_attn_d
 extern "C" int corm_llm_decode_attn(const corm_llm_decode_attn_desc* d, corm_stream_t stream) {
   if (!d) return corm::fail(CORM_EINVAL, "corm_llm_decode_attn: null descriptor");
   if (int rc = corm::check_device()) return rc;
-  if (!d->qx || !d->kc || !d->vc || !d->tab || !d->ip || !d->o)
+  if ((!d->qx && !(d->prep & 1u)) || !d->kc || !d->vc || !d->tab || !d->ip || !d->o)
     return corm::fail(CORM_EINVAL, "corm_llm_decode_attn: null buffer");
+  if ((d->prep & 1u) && (!d->q0 || !d->k0 || !d->v0 || !d->rope || !d->pq || !d->pk ||
+                         (!(d->prep & 16u) && !d->pv) || d->HD % 16))
+    return corm::fail(CORM_EINVAL, "corm_llm_decode_attn: the fused AttnPrep needs q0 / k0 / v0, rope and entries");
   if (d->B == 0 || d->KV == 0) return CORM_OK;
   if (d->G == 0 || d->G > 8 || d->HD == 0 || d->HD % 8 || 256 % d->HD || d->HD * 4 > 1024 || d->Q == 0 ||
       d->C % d->Q || d->o_stride < (uint64_t)d->KV * d->G * d->HD)

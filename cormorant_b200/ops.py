@@ -145,9 +145,12 @@ def llm_attn_softmax(s, p, tab, ip, *, pos, n, T, G, rows, Q=16, window=0, batch
     check(lib().corm_llm_attn_softmax(C.byref(d), st))
 
 
-def llm_decode_attn(qx, kc, vc, tab, ip, o, *, pos, B, KV, G, HD, rows, Q=16, window=0, o_stride=None):
+def llm_decode_attn(qx, kc, vc, tab, ip, o, *, pos, B, KV, G, HD, rows, Q=16, window=0, o_stride=None, prep=None):
     """corm_llm_decode_attn: a decode step's q.K^T, host softmax, P.V and head
-    merge of every KV group and sequence (caches of ``rows`` rows)."""
+    merge of every KV group and sequence (caches of ``rows`` rows).
+    ``prep``: the step's AttnPrep fused in — a dict with q0, k0, v0 (int16
+    rows), ldq, ldk, ldv, rope (the int32 cos / sin table as int16 words), pq,
+    pk, pv (parameter entries), pq_bc, pk_bc, pv_bc, v_direct; qx unused."""
     for t, nm in ((qx, "qx"), (kc, "kc"), (vc, "vc"), (o, "o")):
         _i16(t, nm)
     if tab.dtype != torch.float64 or ip.dtype != torch.float64:
@@ -155,6 +158,13 @@ def llm_decode_attn(qx, kc, vc, tab, ip, o, *, pos, B, KV, G, HD, rows, Q=16, wi
     st = _ready()
     d = _lib.DecodeAttnDesc(_ptr(qx), _ptr(kc), _ptr(vc), _ptr(tab), _ptr(ip), _ptr(o), pos, B, KV, G, HD, rows, Q,
                             window, KV * G * HD if o_stride is None else o_stride)
+    if prep is not None:
+        d.q0, d.k0, d.v0 = _ptr(prep["q0"]), _ptr(prep["k0"]), _ptr(prep["v0"])
+        d.ldq, d.ldk, d.ldv = prep["ldq"], prep["ldk"], prep["ldv"]
+        d.rope, d.pq, d.pk = _ptr(prep["rope"]), _ptr(prep["pq"]), _ptr(prep["pk"])
+        d.pv = _ptr(prep.get("pv"))
+        d.prep = 1 | (2 if prep.get("pq_bc") else 0) | (4 if prep.get("pk_bc") else 0) | \
+            (8 if prep.get("pv_bc") else 0) | (16 if prep.get("v_direct") else 0)
     check(lib().corm_llm_decode_attn(C.byref(d), st))
 
 

@@ -601,7 +601,8 @@ class GpuSimulator:
         n, _keys = attn_keys(pos, self._host_int(get, sn.n_t) if sn.has_n else T, T, C, sn.Q)
         qx = self._alloc(sn.output.numel)
         qs = self._alloc(B * T * nq)
-        qs.zero_()
+        if n < T:  # rows t >= n of the image stay 0 (every row below n is written)
+            qs.zero_()
         NW = RH.NO_WINDOW
         if n > 0:
             ks = self._alloc(B * T * nk)
@@ -757,7 +758,18 @@ class GpuSimulator:
                 smxs.append(sm)
                 pvs.append(pv)
             if ok and qks and len(qks) == mn.KV:
-                plans[mi] = {"nodes": idx, "qk": qks, "smx": smxs, "pv": pvs}
+                plan = {"nodes": idx, "qk": qks, "smx": smxs, "pv": pvs}
+                # the step's AttnPrep too, when its q image feeds only this block
+                qx = qks[0].inputs[1].onnx_name
+                ri = producer.get(qx)
+                pr = nodes[ri] if ri is not None else None
+                if pr is not None and _kind(pr) == "AttnPrepRoNode" and pr.T == 1 and not pr.has_n and \
+                        int(getattr(pr, "batch", 1)) == int(getattr(smxs[0], "batch", 1)) and qx not in keep and \
+                        readers.get(qx, 0) == len(qks) and pr.ck.onnx_name == qks[0].inputs[0].onnx_name and \
+                        pr.cv.onnx_name == pvs[0].inputs[1].onnx_name and pr.HD % 16 == 0:
+                    plan["prep"] = pr
+                    plan["nodes"] = idx + [ri]
+                plans[mi] = plan
         cache[key] = plans
         return plans
 
@@ -777,9 +789,18 @@ class GpuSimulator:
         tab, ip = self._weights[key]
         pos = self._host_int(get, qk0.inputs[2])
         y = self._alloc(mn.output.numel)
-        ops.llm_decode_attn(get(qk0.inputs[1]), get(qk0.inputs[0]), get(plan["pv"][0].inputs[1]), tab, ip, y, pos=pos,
-                            B=B, KV=mn.KV, G=G, HD=mn.HD, rows=qk0.C, Q=qk0.Q, window=int(getattr(sm0, "window", 0)),
-                            o_stride=mn.H * mn.HD)
+        prep, qx = None, None
+        pr = plan.get("prep")
+        if pr is not None:
+            prep = dict(q0=get(pr.q0), k0=get(pr.k0), v0=get(pr.v), ldq=pr.H * pr.HD, ldk=pr.KV * pr.HD,
+                        ldv=pr.KV * pr.HD, rope=get(pr.raw), pq=get(pr.pq), pk=get(pr.pk),
+                        pv=None if pr.v_direct else get(pr.pvb), pq_bc=pr.pq_bc, pk_bc=pr.pk_bc, pv_bc=pr.pv_bc,
+                        v_direct=pr.v_direct)
+        else:
+            qx = get(qk0.inputs[1])
+        ops.llm_decode_attn(qx, get(qk0.inputs[0]), get(plan["pv"][0].inputs[1]), tab, ip, y, pos=pos, B=B, KV=mn.KV,
+                            G=G, HD=mn.HD, rows=qk0.C, Q=qk0.Q, window=int(getattr(sm0, "window", 0)),
+                            o_stride=mn.H * mn.HD, prep=prep)
         return y
 
     def _attn_merge(self, sn, get):

@@ -238,13 +238,30 @@ int corm_greedy_embed(const corm_greedy_desc* d, corm_stream_t stream);
  * float64 per head; ip: [KV G] float64 2^f_p.  G <= 8, HD a divisor of 256. */
 typedef struct {
   const int16_t* qx;
-  const int16_t* kc;
-  const int16_t* vc;
+  int16_t* kc;
+  int16_t* vc;
   const double* tab;
   const double* ip;
   int16_t* o;
   uint32_t pos, B, KV, G, HD, C, Q, window;
   uint64_t o_stride;
+  /* The step's AttnPrep fused in (prep bit 0; AttnPrepRoNode with one row,
+   * rowops_nodes.py:1112-1143): per sequence b the rows q0 / k0 / v0 at
+   * b * ldq / ldk / ldv — RoPE of q0 (entries pq) into the q image (qx is
+   * then unused) and of k0 (entries pk) into K cache row pos, v0 re-rounded
+   * (entries pv; prep bit 4: copied as is) into V cache row pos; rope: the
+   * table [C][2 HD] int32 (cos then sin at 2^-23); prep bits 1 / 2 / 3:
+   * pq / pk / pv are one broadcast entry.  The cache rows are written once
+   * per (sequence, group), before its scores read them. */
+  const int16_t* q0;
+  const int16_t* k0;
+  const int16_t* v0;
+  uint64_t ldq, ldk, ldv;
+  const int32_t* rope;
+  const void* pq;
+  const void* pk;
+  const void* pv;
+  uint32_t prep;
 } corm_llm_decode_attn_desc;
 
 int corm_llm_decode_attn(const corm_llm_decode_attn_desc* d, corm_stream_t stream);

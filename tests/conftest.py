@@ -129,10 +129,51 @@ def cpu_ops(monkeypatch):
         if ids is not None:
             ids.numpy()[:batch] = nxt
 
-    def llm_decode_attn(qx, kc, vc, tab, ip, o, *, pos, B, KV, G, HD, rows, Q=16, window=0, o_stride=None):
+    def llm_decode_attn(qx, kc, vc, tab, ip, o, *, pos, B, KV, G, HD, rows, Q=16, window=0, o_stride=None,
+                        prep=None):
         from oracle import attn as A
         C = rows
-        q = qx.numpy()[:KV * B * HD * G].astype(np.int64).reshape(KV, B, HD, G)
+        if prep is not None:  # the fused AttnPrep: RoPE / re-round by the entries, the cache rows of pos
+            ents = lambda t, bc, cnt: np.frombuffer(t.numpy().tobytes()[:16 * (1 if bc else cnt)],  # noqa: E731
+                                                    np.uint8).reshape(-1, 16)
+            tabw = np.frombuffer(prep["rope"].numpy().tobytes()[:C * 8 * HD], "<i4").astype(np.int64).reshape(C, 2 * HD)
+            cs, sn = tabw[pos, :HD], tabw[pos, HD:]
+            half = HD // 2
+
+            def rope_rows(x, e, nh):
+                x = x.astype(np.int64).reshape(-1, nh, HD)
+                rot = np.concatenate([-x[..., half:], x[..., :half]], -1)
+                sa = np.broadcast_to(e[:, 8].astype(np.int64) & 63, (nh * HD,)).reshape(nh, HD)
+                sb = np.broadcast_to(e[:, 9].astype(np.int64) & 63, (nh * HD,)).reshape(nh, HD)
+                sc = np.broadcast_to(e[:, 10].astype(np.int64) & 63, (nh * HD,)).reshape(nh, HD)
+                return spec.sat16(spec.rne_shr(((x * cs) << sa) + ((rot * sn) << sb), sc))
+            H = KV * G
+            q0 = prep["q0"].numpy()[:B * H * HD].reshape(B, H * HD)
+            k0 = prep["k0"].numpy()[:B * KV * HD].reshape(B, KV * HD)
+            v0 = prep["v0"].numpy()[:B * KV * HD].reshape(B, KV * HD).astype(np.int64)
+            qr = rope_rows(q0, ents(prep["pq"], prep["pq_bc"], H * HD), H)          # [B][H][HD]
+            kr = rope_rows(k0, ents(prep["pk"], prep["pk_bc"], KV * HD), KV)        # [B][KV][HD]
+            if prep["v_direct"]:
+                vr = v0
+            else:
+                e = ents(prep["pv"], prep["pv_bc"], KV * HD)
+                sa = np.broadcast_to(e[:, 8].astype(np.int64) & 63, (KV * HD,))
+                sc = np.broadcast_to(e[:, 10].astype(np.int64) & 63, (KV * HD,))
+                bq = np.broadcast_to(e[:, 4:8].copy().view("<i4").reshape(-1).astype(np.int64), (KV * HD,))
+                bq = ((bq << 42) >> 42)
+                vr = spec.sat16(spec.rne_shr((v0 << sa) + bq, sc))
+            kcn, vcn = kc.numpy(), vc.numpy()
+            if pos < C:
+                for b in range(B):
+                    for g in range(KV):
+                        base = ((g * B + b) * C + pos) * HD
+                        kcn[base:base + HD] = kr[b, g]
+                        vcn[base:base + HD] = vr.reshape(B, KV, HD)[b, g]
+            q = np.zeros((KV, B, HD, G), np.int64)
+            if pos < C:
+                q = qr.reshape(B, KV, G, HD).transpose(1, 0, 3, 2)
+        else:
+            q = qx.numpy()[:KV * B * HD * G].astype(np.int64).reshape(KV, B, HD, G)
         K = kc.numpy()[:KV * B * C * HD].astype(np.int64).reshape(KV, B, C, HD)
         V = vc.numpy()[:KV * B * C * HD].astype(np.int64).reshape(KV, B, C, HD)
         tabs = tab.numpy().reshape(KV * G, 65536)
