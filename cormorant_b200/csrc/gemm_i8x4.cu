@@ -1,25 +1,32 @@
 // tcgen05 kind::i8 GEMM with the four-way int16 split (see gemm_i8x4.h).
 //
-// Persistent: one CTA per SM (6 warps) walks work units = (batch, 128-row
-// tile, 128-column tile, K split), warp-specialised:
-//   warp 0      TMA producer: per 128-byte K block, 4 tiles (A hi/lo K-major,
-//               B hi/lo K-major or MN-major, 128 x 128 bytes, 128-byte swizzle,
-//               no multicast) into a STAGES-deep ring that runs across units
-//   warp 1      TMEM owner (512 columns) and MMA issuer: 16 tcgen05.mma
-//               (128x128x32) per K block into HH / MID / LL (the K steps past
-//               the job's K, zero-filled, are not issued); waits for the
-//               epilogue to drain TMEM before the next unit (tmem_empty)
-//   warps 2..9  epilogue, two warps per TMEM lane quarter (64 columns each):
-//               tcgen05.ld of the three accumulators, int64 recombine and the
-//               job's rounding rule into registers, TMEM released to the next
-//               unit's MMAs, then the int16 stores — or, for a K-split unit,
-//               exact int64 atomics into a partial-sum buffer that
-//               gemm_finish_kernel rounds afterwards
+// Persistent: one CTA per SM (18 warps) walks work units = (batch, 128-row
+// tile, 128-column tile, K split), warp-specialised.  Plane operands (int8
+// hi / lo planes split beforehand):
+//   warp 0       TMA producer: per 128-byte K block, 4 tiles (A hi/lo K-major,
+//                B hi/lo K-major or MN-major, 128 x 128 bytes, 128-byte swizzle,
+//                no multicast) into a STAGES-deep ring that runs across units
+//   warp 1       TMEM owner (512 columns) and MMA issuer: 16 tcgen05.mma
+//                (128x128x32) per K block into HH / MID / LL (the K steps past
+//                the job's K, zero-filled, are not issued); waits for the
+//                epilogue to drain TMEM before the next unit (tmem_empty)
+//   warps 2..17  epilogue, four warps per TMEM lane quarter (32 columns each):
+//                tcgen05.ld of the three accumulators, int64 recombine and the
+//                job's rounding rule into registers, TMEM released to the next
+//                unit's MMAs, then the int16 stores — or, for a K-split unit,
+//                exact int64 atomics into a partial-sum buffer that
+//                gemm_finish_kernel rounds afterwards
+// int16 operands (split inside the kernel): warp 0 owns TMEM and issues the
+// MMAs, warp 17 lane 0 loads the raw int16 tiles by TMA (unswizzled, 64 KB a
+// stage) into the stage's own bytes, warps 1..8 split them in place into the
+// swizzled planes (a named barrier between reading and writing), warps 9..16
+// run the epilogue (two warps per lane quarter).
 // Every mbarrier wait is bounded (sm100::mbar_wait); a timeout leaves an error
 // code in the per-device error word and the CTA unwinds (in-flight TMA loads
 // and MMAs waited for, TMEM freed).
 #include <cudaTypedefs.h>
 
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 
@@ -59,6 +66,8 @@ struct EpiArgs {
   uint32_t ymode;  // the form of the rule (floor_acc)
   uint32_t cvar;   // act (0 none, 1 ReLU, 2 Clip(0,6)) * 2 + conv bias
   int* err;
+  uint32_t raw_tma;  // int16 operands: raw tiles by TMA (map_ahi: A, map_bhi: B) into the stage
+  uint32_t a_box_rows, b_pitch;  // raw boxes: A rows (<= 128) and the B row's bytes (<= 256)
 };
 
 // y = floor(acc / 2^8) for acc = 2^16 HH + 2^8 MID + LL + 2^8 bias, i.e.
@@ -244,18 +253,20 @@ __device__ __forceinline__ Unit unit_of(const EpiArgs& ep, uint32_t u) {
 // Warp roles.  Plane operands (CONV = false): warp 0 lane 0 issues the TMA
 // loads, warp 1 owns TMEM and lane 0 issues the MMAs, warps 2..9 run the
 // epilogue.  int16 operands (CONV = true): warp 0 owns TMEM and issues the
-// MMAs, warps 1..8 load int16 tiles, split them into the hi / lo planes and
-// store them in the 128-byte swizzled layout the MMA descriptors read, warps
-// 9..16 run the epilogue.
+// MMAs, warps 1..8 split int16 tiles into the hi / lo planes in the 128-byte
+// swizzled layout the MMA descriptors read, warps 9..16 run the epilogue and
+// warp 17 lane 0 loads the raw int16 tiles by TMA into the stage they are
+// split in (ep.raw_tma; otherwise warps 1..8 load them with plain loads).
 template <bool CONV>
 struct Roles {
   // epilogue warps (4 per column group, one per TMEM lane quarter) and the
   // columns each drains: 16 x 32 with plane operands, 8 x 64 beside the producers
   static constexpr int ew = CONV ? 8 : 16;
   static constexpr int wc = BN * 4 / ew;
-  static constexpr int threads = CONV ? 32 + 32 * 8 + 32 * ew : 64 + 32 * ew;
+  static constexpr int threads = CONV ? 32 + 32 * 8 + 32 * ew + 32 : 64 + 32 * ew;
   static constexpr int mma_warp = CONV ? 0 : 1;
   static constexpr int epi0 = CONV ? 9 : 2;
+  static constexpr int tma_warp = CONV ? 9 + ew : 0;  // int16 operands: the raw-tile loads
   static constexpr int chunk = 16;  // TMEM columns per tcgen05.ld (register budget)
 };
 
@@ -360,7 +371,9 @@ __global__ void __launch_bounds__(Roles<CONV>::threads, 1)
   uint64_t* tmem_full = empty + STAGES;
   uint64_t* tmem_empty = tmem_full + 1;
   uint64_t* mma_done = tmem_empty + 1;
-  uint32_t* tmem_slot = (uint32_t*)(mma_done + 1);
+  uint64_t* raw_full = mma_done + 1;  // int16 raw tiles landed (CONV with raw_tma)
+  uint32_t* tmem_slot = (uint32_t*)(raw_full + STAGES);
+  uint32_t* abort_at = tmem_slot + 1;  // first ring step a splitting warp gave up at
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t units = ep.batch * ep.tiles_m * ep.tiles_n * ep.splits;
@@ -369,7 +382,9 @@ __global__ void __launch_bounds__(Roles<CONV>::threads, 1)
     for (int s = 0; s < STAGES; s++) {
       sm100::mbar_init(&full[s], CONV ? 8 : 1);
       sm100::mbar_init(&empty[s], 1);
+      if (CONV) sm100::mbar_init(&raw_full[s], 1);
     }
+    if (CONV) *abort_at = 0xFFFFFFFFu;
     sm100::mbar_init(tmem_full, 1);
     sm100::mbar_init(tmem_empty, R::ew);
     sm100::mbar_init(mma_done, 1);
@@ -416,6 +431,98 @@ __global__ void __launch_bounds__(Roles<CONV>::threads, 1)
       // let the loads already issued land before the CTA's shared memory goes away
       for (uint32_t q = g > (uint32_t)STAGES ? g - STAGES : 0; q < g; q++)
         sm100::mbar_wait(&full[q % STAGES], (q / STAGES) & 1, nullptr, 0, 200000000ll);
+    }
+  } else if (CONV && warp == R::tma_warp && lane == 0 && ep.raw_tma) {
+    // ---------------- raw int16 tiles by TMA: per stage the A tile (128 rows x
+    // 128 K, 32 KB, over the A hi / lo planes) and the MN-major B tile (128 K
+    // rows x 128 columns, over the B planes), unswizzled, zero-filled beyond
+    // the job; the splitting warps convert them in place
+    sm100::prefetch_tmap(&map_ahi);
+    sm100::prefetch_tmap(&map_bhi);
+    uint32_t g = 0;
+    bool ok = true;
+    for (uint32_t u = blockIdx.x; u < units && ok; u += gridDim.x) {
+      const Unit w = unit_of(ep, u);
+      const int a_z = ep.a_bs16 ? (int)w.bz : 0, b_z = ep.b_bs16 ? (int)w.bz : 0;
+      for (uint32_t kb = w.kb0; kb < w.kb1; kb++, g++) {
+        const int s = g % STAGES;
+        if (g >= (uint32_t)STAGES && !sm100::mbar_wait(&empty[s], ((g / STAGES) - 1) & 1, ep.err, 106)) {
+          ok = false;
+          break;
+        }
+        uint8_t* st = smem + s * STAGE_BYTES;
+        sm100::mbar_expect_tx(&raw_full[s], ep.a_box_rows * 256u + BK * ep.b_pitch);
+        const int x = (int)(kb * BK);
+        sm100::tma_load_3d(st, &map_ahi, &raw_full[s], x, (int)w.tile_r, a_z);
+        sm100::tma_load_3d(st + 2 * TILE_BYTES, &map_bhi, &raw_full[s], (int)w.tile_c, x, b_z);
+      }
+    }
+    // the loads issued land before the CTA's shared memory goes away
+    for (uint32_t q = g > (uint32_t)STAGES ? g - STAGES : 0; q < g; q++)
+      sm100::mbar_wait(&raw_full[q % STAGES], (q / STAGES) & 1, nullptr, 0, 200000000ll);
+  } else if (CONV && warp >= 1 && warp <= 8 && ep.raw_tma) {
+    // ---------------- in-place split of the raw tiles: each thread reads its 8
+    // A chunks and 8 B chunks (8 consecutive int16 of a row, 16 bytes; 16 chunks
+    // to a 256-byte raw row, 8 lanes reading 128 contiguous bytes), the 256
+    // splitting threads meet at a named barrier, then each writes the chunk's 8
+    // hi and 8 lo bytes at their swizzled plane positions (16-byte unit u of row
+    // r at (u ^ (r & 7)) * 16, the chunk in its half).  A rows and B columns
+    // past the job are left as they are: they only reach accumulator rows /
+    // columns the epilogue does not store.  The decision to stop (a bounded
+    // wait ran out) is read after the barrier from abort_at, so every
+    // splitting thread leaves at the same ring step.
+    // chunk i of this thread: row row0 + 16 i, chunk c of the row (the same c and
+    // row & 7 for every i, so every address is a base plus a constant)
+    const uint32_t pt = (uint32_t)(warp - 1) * 32u + lane, row0 = pt >> 4, c = pt & 15u;
+    const uint32_t off0 = row0 * 128u + (((c >> 1) ^ (row0 & 7u)) << 4) + ((c & 1u) << 3);
+    uint32_t g = 0;
+    bool stop = false;
+    for (uint32_t u = blockIdx.x; u < units && !stop; u += gridDim.x) {
+      const Unit w = unit_of(ep, u);
+      const uint32_t nrow = ep.rows - w.tile_r, ncol = ep.cols - w.tile_c;
+      for (uint32_t kb = w.kb0; kb < w.kb1; kb++, g++) {
+        const int s = g % STAGES;
+        const bool okw = sm100::mbar_wait(&raw_full[s], (g / STAGES) & 1, ep.err, 105);
+        if (!okw) atomicMin(abort_at, g);
+        uint8_t* st = smem + s * STAGE_BYTES;
+        // (after a run-out wait the words read are not used: every thread stops below)
+        int4 va[8], vb[8];
+        const uint8_t* ra = st + row0 * 256u + c * 16u;
+        const uint8_t* rb = st + 2 * TILE_BYTES + row0 * ep.b_pitch + c * 16u;
+        const uint32_t bstep = 16u * ep.b_pitch;
+        const bool b_in = c * 8u < ncol;
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+          if (row0 + 16u * i < nrow) va[i] = *(const int4*)(ra + 4096 * i);
+          if (b_in) vb[i] = *(const int4*)(rb + bstep * i);
+        }
+        asm volatile("bar.sync 1, 256;" ::: "memory");
+        if (*(volatile uint32_t*)abort_at <= g) {
+          stop = true;
+          break;
+        }
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+          const uint32_t off = off0 + 2048u * i;
+          if (row0 + 16u * i < nrow) {
+            const int4 v = va[i];
+            *(uint2*)(st + off) = make_uint2(__byte_perm((uint32_t)v.x, (uint32_t)v.y, 0x7531),
+                                             __byte_perm((uint32_t)v.z, (uint32_t)v.w, 0x7531));
+            *(uint2*)(st + TILE_BYTES + off) = make_uint2(__byte_perm((uint32_t)v.x, (uint32_t)v.y, 0x6420),
+                                                          __byte_perm((uint32_t)v.z, (uint32_t)v.w, 0x6420));
+          }
+          if (b_in) {
+            const int4 v = vb[i];
+            *(uint2*)(st + 2 * TILE_BYTES + off) = make_uint2(__byte_perm((uint32_t)v.x, (uint32_t)v.y, 0x7531),
+                                                              __byte_perm((uint32_t)v.z, (uint32_t)v.w, 0x7531));
+            *(uint2*)(st + 3 * TILE_BYTES + off) = make_uint2(__byte_perm((uint32_t)v.x, (uint32_t)v.y, 0x6420),
+                                                              __byte_perm((uint32_t)v.z, (uint32_t)v.w, 0x6420));
+          }
+        }
+        sm100::fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) sm100::mbar_arrive(&full[s]);
+      }
     }
   } else if (CONV && warp >= 1 && warp <= 8) {
     // ---------------- int16 producers: per stage the A tile (128 rows x 128 K)
@@ -520,7 +627,7 @@ __global__ void __launch_bounds__(Roles<CONV>::threads, 1)
     // every MMA issued has completed before TMEM is freed
     sm100::mma_commit(mma_done);
     sm100::mbar_wait(mma_done, 0, nullptr, 0, 200000000ll);
-  } else if (warp >= R::epi0) {
+  } else if (warp >= R::epi0 && (!CONV || warp < R::epi0 + R::ew)) {
     // ---------------- epilogue: warp (epi0 + 4 h + j) reads lane quarter (warp % 4),
     // columns [64 h, 64 h + 64)
     const int q = warp & 3;  // TMEM lane quarter this warp may access
@@ -712,6 +819,23 @@ bool make_map(CUtensorMap* map, const void* base, uint32_t inner, uint32_t outer
   return r == CUDA_SUCCESS;
 }
 
+// int16 (as 16-bit words) [planes][outer][inner] with row stride ld and plane stride ps
+// (elements), box box_inner x box_outer x 1, unswizzled, zero fill beyond the extents
+bool make_raw_map(CUtensorMap* map, const int16_t* base, uint32_t inner, uint32_t outer, uint64_t ld,
+                  uint32_t planes, uint64_t ps, uint32_t box_inner, uint32_t box_outer) {
+  auto fn = encode_fn();
+  if (!fn) return false;
+  if (planes <= 1) ps = ld * outer;  // unused extent of one: any valid stride
+  cuuint64_t dims[3] = {inner, outer, planes};
+  cuuint64_t strides[2] = {ld * 2, ps * 2};
+  cuuint32_t box[3] = {box_inner, box_outer, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT16, 3, const_cast<int16_t*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
 struct Split {
   uint32_t tiles, num_kb, splits, kps;
 };
@@ -784,12 +908,22 @@ int gemm_i8x4(const GemmJob& j, cudaStream_t stream) {
   if (!err) return fail(CORM_ECUDA, "gemm: error word allocation failed");
   CUtensorMap m_ahi, m_alo, m_bhi, m_blo;
   const bool conv = j.a16 != nullptr;  // int16 operands split inside the kernel
+  bool raw_tma = false;
+  uint32_t a_box_rows = BM, b_box_cols = BN;
   if (conv) {
     if (((uintptr_t)j.a16 | (uintptr_t)j.b16) & 15u || j.lda % 8u || j.ldb % 8u || j.a_bs16 % 8u || j.b_bs16 % 8u ||
         j.K % 8u || j.cols % 8u)
       return fail(CORM_EINVAL, "gemm: int16 operands not on 16-byte rows");
     memset(&m_ahi, 0, sizeof m_ahi);
     m_alo = m_bhi = m_blo = m_ahi;
+    // raw tiles by TMA where both maps encode (A [batch][rows][K], B [batch][K][cols])
+    const char* ldg = getenv("CORM_GEMM_LDG_PRODUCERS");  // "1": the plain-load producers instead
+    // a job of fewer than 128 rows / columns: boxes that size (multiples of 8)
+    a_box_rows = j.rows < (uint32_t)BM ? (j.rows + 7u) & ~7u : (uint32_t)BM;
+    b_box_cols = j.cols < (uint32_t)BN ? (j.cols + 7u) & ~7u : (uint32_t)BN;
+    raw_tma = !(ldg && ldg[0] == '1') &&
+              make_raw_map(&m_ahi, j.a16, j.K, j.rows, j.lda, j.a_bs16 ? j.batch : 1, j.a_bs16, BK, a_box_rows) &&
+              make_raw_map(&m_bhi, j.b16, j.cols, j.K, j.ldb, j.b_bs16 ? j.batch : 1, j.b_bs16, b_box_cols, BK);
   } else {
     bool ok = make_map(&m_ahi, j.a_hi, j.Kp, j.rows, j.a_planes) && make_map(&m_alo, j.a_lo, j.Kp, j.rows, j.a_planes);
     if (j.b_mn)
@@ -842,6 +976,9 @@ int gemm_i8x4(const GemmJob& j, cudaStream_t stream) {
   ep.kb_per_split = sp.kps;
   ep.partial = nullptr;
   ep.err = err;
+  ep.raw_tma = raw_tma ? 1u : 0u;
+  ep.a_box_rows = a_box_rows;
+  ep.b_pitch = b_box_cols * 2u;
   if (sp.splits > 1) {
     if (!j.partial) return fail(CORM_ENOMEM, "gemm: K-split job without a partial-sum buffer");
     ep.partial = (unsigned long long*)j.partial;

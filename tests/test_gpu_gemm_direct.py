@@ -1,5 +1,5 @@
 """The GEMM that reads int16 operands and splits them into the int8 planes
-in its producer warps (row-major B, K and m multiples of 8, 16-byte rows)
+inside the kernel (row-major B, K and m multiples of 8, 16-byte rows)
 against the oracle: partial row / column / K tiles, batches with shared
 operands (stride 0), the K split, the int32 wrap, full-range values."""
 import numpy as np
@@ -31,8 +31,13 @@ CASES = [  # batch, n, k, m, a_shared, b_shared, flags, lo, hi
 ]
 
 
+@pytest.mark.parametrize("producers", ["tma", "ldg"])
 @pytest.mark.parametrize("case", CASES, ids=lambda c: "b%d_n%d_k%d_m%d" % c[:4])
-def test_direct_vs_oracle(ops, case):
+def test_direct_vs_oracle(ops, case, producers, monkeypatch):
+    """Both producer forms: raw int16 tiles by TMA split in shared memory (the
+    default) and plain loads split in registers (CORM_GEMM_LDG_PRODUCERS=1)."""
+    if producers == "ldg":
+        monkeypatch.setenv("CORM_GEMM_LDG_PRODUCERS", "1")
     batch, n, k, m, a_sh, b_sh, flags, lo, hi = case
     rng = np.random.default_rng(batch * 7 + n + k * 3 + m)
     A = rng.integers(lo, hi, size=(1 if a_sh else batch, n, k)).astype(np.int16)
