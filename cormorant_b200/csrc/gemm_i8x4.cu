@@ -845,8 +845,12 @@ Split split_of(uint32_t rows, uint32_t cols, uint32_t Kp, uint32_t batch) {
   s.tiles = batch * ((rows + BM - 1) / BM) * ((cols + BN - 1) / BN);
   s.num_kb = (Kp + BK - 1) / BK;
   s.splits = 1;
-  // fewer tiles than SMs: split K (at least 4 K blocks per split) to fill the GPU
-  if (s.tiles < (uint32_t)NUM_SMS && s.num_kb >= 8) {
+  // at most half the SMs busy and 12 or more K blocks: split K (at least 4 K
+  // blocks per split) to fill the GPU.  A split costs a memset, int64 atomics
+  // and a rounding pass over the whole output, which only pay for themselves
+  // when the serial K walk is long and the grid is far from full (splitting
+  // 8 K blocks, or 128 tiles of K 4096 three ways, measured slower).
+  if (s.tiles * 2 <= (uint32_t)NUM_SMS && s.num_kb >= 12) {
     uint32_t want = (2 * NUM_SMS + s.tiles - 1) / s.tiles;
     s.splits = want < s.num_kb / 4 ? want : s.num_kb / 4;
     if (s.splits < 1) s.splits = 1;

@@ -107,3 +107,17 @@ def test_extreme_accumulators(ops, k, pattern):
     Bp = np.concatenate([np.zeros(1, np.int16), B.reshape(-1)])
     ops.matmul(torch.from_numpy(A.reshape(-1)).cuda(), torch.from_numpy(Bp).cuda()[1:], C, n=n, k=k, m=m)
     assert np.array_equal(C.cpu().numpy().reshape(n, m), spec.matmul_raw(A, B))
+
+
+@pytest.mark.parametrize("shape", [(1, 1024, 1536, 1024), (1, 1032, 2048, 1000)], ids=["n1024", "n1032"])
+def test_plane_ksplit_vs_oracle(ops, shape):
+    """Jobs large enough for the plane path with few tiles and a long K: the
+    K split (int64 partial sums, then the rounding pass) on split planes."""
+    batch, n, k, m = shape
+    rng = np.random.default_rng(n + k)
+    A = rng.integers(-32768, 32768, size=(batch, n, k)).astype(np.int16)
+    B = rng.integers(-32768, 32768, size=(batch, k, m)).astype(np.int16)
+    C = torch.empty(batch * n * m, dtype=torch.int16, device="cuda")
+    ops.matmul(torch.from_numpy(A.reshape(-1)).cuda(), torch.from_numpy(B.reshape(-1)).cuda(), C, n=n, k=k, m=m,
+               batch=batch, a_batch_stride=n * k, b_batch_stride=k * m, c_batch_stride=n * m)
+    assert np.array_equal(C.cpu().numpy().reshape(batch, n, m), spec.matmul_raw(A, B))
