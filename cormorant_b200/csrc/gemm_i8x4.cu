@@ -43,6 +43,9 @@ constexpr int TILE_BYTES = BM * BK;  // 16 KB (BM == BN)
 constexpr int STAGE_BYTES = 4 * TILE_BYTES;
 constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
 constexpr uint32_t TMEM_COLS = 512;
+// TMEM columns: HH [0, 128), MID [128, 256), LL [256, 384); int16 operands
+// with raw tiles: A buffer b (hi 32 columns, lo 32 columns) at 384 + 64 b
+constexpr uint32_t A_TMEM = 384;
 constexpr int NUM_SMS = 148;
 
 struct EpiArgs {
@@ -372,7 +375,8 @@ __global__ void __launch_bounds__(Roles<CONV>::threads, 1)
   uint64_t* tmem_empty = tmem_full + 1;
   uint64_t* mma_done = tmem_empty + 1;
   uint64_t* raw_full = mma_done + 1;  // int16 raw tiles landed (CONV with raw_tma)
-  uint32_t* tmem_slot = (uint32_t*)(raw_full + STAGES);
+  uint64_t* a_free = raw_full + STAGES;  // the MMAs reading TMEM A buffer 0 / 1 are done
+  uint32_t* tmem_slot = (uint32_t*)(a_free + 2);
   uint32_t* abort_at = tmem_slot + 1;  // first ring step a splitting warp gave up at
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -383,6 +387,10 @@ __global__ void __launch_bounds__(Roles<CONV>::threads, 1)
       sm100::mbar_init(&full[s], CONV ? 8 : 1);
       sm100::mbar_init(&empty[s], 1);
       if (CONV) sm100::mbar_init(&raw_full[s], 1);
+    }
+    if (CONV) {
+      sm100::mbar_init(&a_free[0], 1);
+      sm100::mbar_init(&a_free[1], 1);
     }
     if (CONV) *abort_at = 0xFFFFFFFFu;
     sm100::mbar_init(tmem_full, 1);
@@ -433,10 +441,10 @@ __global__ void __launch_bounds__(Roles<CONV>::threads, 1)
         sm100::mbar_wait(&full[q % STAGES], (q / STAGES) & 1, nullptr, 0, 200000000ll);
     }
   } else if (CONV && warp == R::tma_warp && lane == 0 && ep.raw_tma) {
-    // ---------------- raw int16 tiles by TMA: per stage the A tile (128 rows x
-    // 128 K, 32 KB, over the A hi / lo planes) and the MN-major B tile (128 K
-    // rows x 128 columns, over the B planes), unswizzled, zero-filled beyond
-    // the job; the splitting warps convert them in place
+    // ---------------- raw int16 tiles by TMA: per stage the A tile (up to 128
+    // rows x 128 K as two halves of 64 K, 128-byte swizzle, over the A plane
+    // bytes) and the MN-major B tile (128 K rows x up to 128 columns,
+    // unswizzled, over the B planes), zero-filled beyond the job
     sm100::prefetch_tmap(&map_ahi);
     sm100::prefetch_tmap(&map_bhi);
     uint32_t g = 0;
@@ -454,6 +462,7 @@ __global__ void __launch_bounds__(Roles<CONV>::threads, 1)
         sm100::mbar_expect_tx(&raw_full[s], ep.a_box_rows * 256u + BK * ep.b_pitch);
         const int x = (int)(kb * BK);
         sm100::tma_load_3d(st, &map_ahi, &raw_full[s], x, (int)w.tile_r, a_z);
+        sm100::tma_load_3d(st + ep.a_box_rows * 128u, &map_ahi, &raw_full[s], x + 64, (int)w.tile_r, a_z);
         sm100::tma_load_3d(st + 2 * TILE_BYTES, &map_bhi, &raw_full[s], (int)w.tile_c, x, b_z);
       }
     }
@@ -461,20 +470,27 @@ __global__ void __launch_bounds__(Roles<CONV>::threads, 1)
     for (uint32_t q = g > (uint32_t)STAGES ? g - STAGES : 0; q < g; q++)
       sm100::mbar_wait(&raw_full[q % STAGES], (q / STAGES) & 1, nullptr, 0, 200000000ll);
   } else if (CONV && warp >= 1 && warp <= 8 && ep.raw_tma) {
-    // ---------------- in-place split of the raw tiles: each thread reads its 8
-    // A chunks and 8 B chunks (8 consecutive int16 of a row, 16 bytes; 16 chunks
-    // to a 256-byte raw row, 8 lanes reading 128 contiguous bytes), the 256
-    // splitting threads meet at a named barrier, then each writes the chunk's 8
-    // hi and 8 lo bytes at their swizzled plane positions (16-byte unit u of row
-    // r at (u ^ (r & 7)) * 16, the chunk in its half).  A rows and B columns
-    // past the job are left as they are: they only reach accumulator rows /
+    // ---------------- split of the raw tiles.  A goes to tensor memory: warp w
+    // owns TMEM lane quarter q = w % 4 (rows 32 q + lane) and K half hk (warps
+    // 1..4: K bytes 0..63 of the block, 5..8: 64..127); each lane reads its
+    // row's 8 chunks of 16 bytes from the 128-byte-swizzled raw half-tile
+    // (8 consecutive rows hit 8 distinct bank groups), splits them and stores
+    // 16 hi and 16 lo words with tcgen05.st into the stage's A buffer (two
+    // buffers, the MMAs of stage g - 2 waited for through a_free).  B is split
+    // in place: each thread reads its 8 chunks (8 consecutive int16 of a K row,
+    // 16 chunks to a 256-byte raw row, 8 lanes reading 128 contiguous bytes),
+    // the 256 splitting threads meet at a named barrier, then each writes the
+    // chunk's 8 hi and 8 lo bytes at their swizzled plane positions (16-byte
+    // unit u of row r at (u ^ (r & 7)) * 16, the chunk in its half).  A rows and
+    // B columns past the job are not split: they only reach accumulator rows /
     // columns the epilogue does not store.  The decision to stop (a bounded
     // wait ran out) is read after the barrier from abort_at, so every
     // splitting thread leaves at the same ring step.
-    // chunk i of this thread: row row0 + 16 i, chunk c of the row (the same c and
-    // row & 7 for every i, so every address is a base plus a constant)
+    // B chunk i of this thread: K row row0 + 16 i, chunk c of the row (the same c
+    // and row & 7 for every i, so every address is a base plus a constant)
     const uint32_t pt = (uint32_t)(warp - 1) * 32u + lane, row0 = pt >> 4, c = pt & 15u;
     const uint32_t off0 = row0 * 128u + (((c >> 1) ^ (row0 & 7u)) << 4) + ((c & 1u) << 3);
+    const uint32_t aq = (uint32_t)(warp & 3), ahk = (uint32_t)(warp - 1) >> 2, arow = aq * 32u + lane;
     uint32_t g = 0;
     bool stop = false;
     for (uint32_t u = blockIdx.x; u < units && !stop; u += gridDim.x) {
@@ -482,36 +498,44 @@ __global__ void __launch_bounds__(Roles<CONV>::threads, 1)
       const uint32_t nrow = ep.rows - w.tile_r, ncol = ep.cols - w.tile_c;
       for (uint32_t kb = w.kb0; kb < w.kb1; kb++, g++) {
         const int s = g % STAGES;
-        const bool okw = sm100::mbar_wait(&raw_full[s], (g / STAGES) & 1, ep.err, 105);
+        bool okw = sm100::mbar_wait(&raw_full[s], (g / STAGES) & 1, ep.err, 105);
+        if (g >= 2) okw = sm100::mbar_wait(&a_free[g & 1], ((g >> 1) - 1) & 1, ep.err, 109) && okw;
         if (!okw) atomicMin(abort_at, g);
+        sm100::tc_fence_after();  // the TMEM buffer's readers are done (a_free)
         uint8_t* st = smem + s * STAGE_BYTES;
-        // (after a run-out wait the words read are not used: every thread stops below)
-        int4 va[8], vb[8];
-        const uint8_t* ra = st + row0 * 256u + c * 16u;
+        // (after a run-out wait the words are not used: every thread stops below)
+        if (aq * 32u < nrow) {  // warp-uniform: the quarter holds rows of the job
+          const uint8_t* ra = st + ahk * (ep.a_box_rows * 128u) + arow * 128u;
+          uint32_t hi[16], lo[16];
+#pragma unroll
+          for (int k = 0; k < 8; k++) {
+            int4 v = make_int4(0, 0, 0, 0);
+            if (arow < nrow) v = *(const int4*)(ra + (((uint32_t)k ^ (arow & 7u)) << 4));
+            hi[2 * k] = __byte_perm((uint32_t)v.x, (uint32_t)v.y, 0x7531);
+            hi[2 * k + 1] = __byte_perm((uint32_t)v.z, (uint32_t)v.w, 0x7531);
+            lo[2 * k] = __byte_perm((uint32_t)v.x, (uint32_t)v.y, 0x6420);
+            lo[2 * k + 1] = __byte_perm((uint32_t)v.z, (uint32_t)v.w, 0x6420);
+          }
+          const uint32_t ta = tmem + ((aq * 32u) << 16) + A_TMEM + 64u * (g & 1u) + 16u * ahk;
+          sm100::tmem_st16(ta, hi);
+          sm100::tmem_st16(ta + 32u, lo);
+        }
+        int4 vb[8];
         const uint8_t* rb = st + 2 * TILE_BYTES + row0 * ep.b_pitch + c * 16u;
         const uint32_t bstep = 16u * ep.b_pitch;
         const bool b_in = c * 8u < ncol;
 #pragma unroll
-        for (int i = 0; i < 8; i++) {
-          if (row0 + 16u * i < nrow) va[i] = *(const int4*)(ra + 4096 * i);
+        for (int i = 0; i < 8; i++)
           if (b_in) vb[i] = *(const int4*)(rb + bstep * i);
-        }
         asm volatile("bar.sync 1, 256;" ::: "memory");
         if (*(volatile uint32_t*)abort_at <= g) {
           stop = true;
           break;
         }
+        if (b_in) {
 #pragma unroll
-        for (int i = 0; i < 8; i++) {
-          const uint32_t off = off0 + 2048u * i;
-          if (row0 + 16u * i < nrow) {
-            const int4 v = va[i];
-            *(uint2*)(st + off) = make_uint2(__byte_perm((uint32_t)v.x, (uint32_t)v.y, 0x7531),
-                                             __byte_perm((uint32_t)v.z, (uint32_t)v.w, 0x7531));
-            *(uint2*)(st + TILE_BYTES + off) = make_uint2(__byte_perm((uint32_t)v.x, (uint32_t)v.y, 0x6420),
-                                                          __byte_perm((uint32_t)v.z, (uint32_t)v.w, 0x6420));
-          }
-          if (b_in) {
+          for (int i = 0; i < 8; i++) {
+            const uint32_t off = off0 + 2048u * i;
             const int4 v = vb[i];
             *(uint2*)(st + 2 * TILE_BYTES + off) = make_uint2(__byte_perm((uint32_t)v.x, (uint32_t)v.y, 0x7531),
                                                               __byte_perm((uint32_t)v.z, (uint32_t)v.w, 0x7531));
@@ -519,6 +543,8 @@ __global__ void __launch_bounds__(Roles<CONV>::threads, 1)
                                                               __byte_perm((uint32_t)v.z, (uint32_t)v.w, 0x6420));
           }
         }
+        sm100::tmem_st_wait();
+        sm100::tc_fence_before();
         sm100::fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) sm100::mbar_arrive(&full[s]);
@@ -588,6 +614,7 @@ __global__ void __launch_bounds__(Roles<CONV>::threads, 1)
     const uint32_t ID_US = sm100::idesc_i8(BM, BN, 0, 1) | bmaj;
     const uint32_t ID_UU = sm100::idesc_i8(BM, BN, 0, 0) | bmaj;
     const uint32_t acc_hh = tmem, acc_mid = tmem + BN, acc_ll = tmem + 2 * BN;
+    const bool a_tm = CONV && ep.raw_tma;  // A from the TMEM buffers the splitting warps fill
     uint32_t g = 0, i = 0;
     bool ok = true;
     for (uint32_t u = blockIdx.x; u < units && ok; u += gridDim.x, i++) {
@@ -610,17 +637,32 @@ __global__ void __launch_bounds__(Roles<CONV>::threads, 1)
         const uint64_t b_step = ep.b_mn ? (uint64_t)(4096 >> 4) : (uint64_t)(32 >> 4);
         const uint32_t krem = ep.K - kb * BK;  // > 0: K steps beyond it only add zeros
         const int nks = krem >= (uint32_t)BK ? BK / 32 : (int)((krem + 31) / 32);
+        if (a_tm) {  // A hi / lo from the stage's TMEM buffer: 8 columns per K step of 32
+          const uint32_t t_ahi = tmem + A_TMEM + 64u * (g & 1u), t_alo = t_ahi + 32u;
 #pragma unroll
-        for (int ks = 0; ks < BK / 32; ks++) {
-          if (ks >= nks) break;
-          const uint64_t adv = (uint64_t)((ks * 32) >> 4), bdv = b_step * ks;
-          const uint32_t acc = (kb != w.kb0 || ks) ? 1u : 0u;
-          sm100::mma_i8(acc_hh, d_ahi + adv, d_bhi + bdv, ID_SS, acc);
-          sm100::mma_i8(acc_mid, d_ahi + adv, d_blo + bdv, ID_SU, acc);
-          sm100::mma_i8(acc_mid, d_alo + adv, d_bhi + bdv, ID_US, 1u);
-          sm100::mma_i8(acc_ll, d_alo + adv, d_blo + bdv, ID_UU, acc);
+          for (int ks = 0; ks < BK / 32; ks++) {
+            if (ks >= nks) break;
+            const uint64_t bdv = b_step * ks;
+            const uint32_t acc = (kb != w.kb0 || ks) ? 1u : 0u;
+            sm100::mma_i8_ta(acc_hh, t_ahi + 8 * ks, d_bhi + bdv, ID_SS, acc);
+            sm100::mma_i8_ta(acc_mid, t_ahi + 8 * ks, d_blo + bdv, ID_SU, acc);
+            sm100::mma_i8_ta(acc_mid, t_alo + 8 * ks, d_bhi + bdv, ID_US, 1u);
+            sm100::mma_i8_ta(acc_ll, t_alo + 8 * ks, d_blo + bdv, ID_UU, acc);
+          }
+        } else {
+#pragma unroll
+          for (int ks = 0; ks < BK / 32; ks++) {
+            if (ks >= nks) break;
+            const uint64_t adv = (uint64_t)((ks * 32) >> 4), bdv = b_step * ks;
+            const uint32_t acc = (kb != w.kb0 || ks) ? 1u : 0u;
+            sm100::mma_i8(acc_hh, d_ahi + adv, d_bhi + bdv, ID_SS, acc);
+            sm100::mma_i8(acc_mid, d_ahi + adv, d_blo + bdv, ID_SU, acc);
+            sm100::mma_i8(acc_mid, d_alo + adv, d_bhi + bdv, ID_US, 1u);
+            sm100::mma_i8(acc_ll, d_alo + adv, d_blo + bdv, ID_UU, acc);
+          }
         }
         sm100::mma_commit(&empty[s]);
+        if (a_tm) sm100::mma_commit(&a_free[g & 1u]);
       }
       if (ok) sm100::mma_commit(tmem_full);
     }
@@ -820,9 +862,10 @@ bool make_map(CUtensorMap* map, const void* base, uint32_t inner, uint32_t outer
 }
 
 // int16 (as 16-bit words) [planes][outer][inner] with row stride ld and plane stride ps
-// (elements), box box_inner x box_outer x 1, unswizzled, zero fill beyond the extents
+// (elements), box box_inner x box_outer x 1, unswizzled or 128-byte swizzled
+// (box_inner 64), zero fill beyond the extents
 bool make_raw_map(CUtensorMap* map, const int16_t* base, uint32_t inner, uint32_t outer, uint64_t ld,
-                  uint32_t planes, uint64_t ps, uint32_t box_inner, uint32_t box_outer) {
+                  uint32_t planes, uint64_t ps, uint32_t box_inner, uint32_t box_outer, bool sw128) {
   auto fn = encode_fn();
   if (!fn) return false;
   if (planes <= 1) ps = ld * outer;  // unused extent of one: any valid stride
@@ -831,7 +874,8 @@ bool make_raw_map(CUtensorMap* map, const int16_t* base, uint32_t inner, uint32_
   cuuint32_t box[3] = {box_inner, box_outer, 1};
   cuuint32_t estr[3] = {1, 1, 1};
   CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT16, 3, const_cast<int16_t*>(base), dims, strides, box, estr,
-                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, sw128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS;
 }
@@ -926,8 +970,8 @@ int gemm_i8x4(const GemmJob& j, cudaStream_t stream) {
     a_box_rows = j.rows < (uint32_t)BM ? (j.rows + 7u) & ~7u : (uint32_t)BM;
     b_box_cols = j.cols < (uint32_t)BN ? (j.cols + 7u) & ~7u : (uint32_t)BN;
     raw_tma = !(ldg && ldg[0] == '1') &&
-              make_raw_map(&m_ahi, j.a16, j.K, j.rows, j.lda, j.a_bs16 ? j.batch : 1, j.a_bs16, BK, a_box_rows) &&
-              make_raw_map(&m_bhi, j.b16, j.cols, j.K, j.ldb, j.b_bs16 ? j.batch : 1, j.b_bs16, b_box_cols, BK);
+              make_raw_map(&m_ahi, j.a16, j.K, j.rows, j.lda, j.a_bs16 ? j.batch : 1, j.a_bs16, BK / 2, a_box_rows, true) &&
+              make_raw_map(&m_bhi, j.b16, j.cols, j.K, j.ldb, j.b_bs16 ? j.batch : 1, j.b_bs16, b_box_cols, BK, false);
   } else {
     bool ok = make_map(&m_ahi, j.a_hi, j.Kp, j.rows, j.a_planes) && make_map(&m_alo, j.a_lo, j.Kp, j.rows, j.a_planes);
     if (j.b_mn)
