@@ -327,18 +327,14 @@ def shapes_summary(graph) -> List[Tuple[str, list]]:
     return [(type(sn).__name__, list(sn.output.shape)) for sn in graph.nodes]
 
 
-def _encode_weight(w: np.ndarray, f_w: int) -> np.ndarray:
-    """A constant MatMul weight at its rank-1 exponent f_w (numeric.py:199-255):
-    raw = RNE(w 2^f_w) saturated, carried as raw / 2^8 (the tensor's data)."""
-    raw = np.clip(np.round(np.asarray(w, np.float64) * 2.0 ** f_w), -32768, 32767)
-    return raw / 256.0
-
-
 # exponents of the Llama prefill (per tensor): the int32 residual, RMSNorm
 # outputs, projections, the rotated q / the caches, P, the attention output,
 # the MLP's, the logits
 LLAMA_EXP = dict(fr=15, fx=12, fq0=13, fk0=13, fv=13, fq=10, fkc=10, fvc=9, fp=12, fo=13, fg=13, fu=13, fa=13,
                  fd=13, fl=11)
+# the formats-table class of each (src/llama.py:413-455): x serves x, x2 and xf
+_LLAMA_CLASS = dict(fr="res", fx="x", fq0="q0", fk0="k0", fv="v", fq="q", fkc="k", fvc="vc", fp="p", fo="o", fg="g",
+                    fu="u", fa="a", fd="d", fl="logits")
 
 
 class LlamaModel:
@@ -367,7 +363,13 @@ class LlamaModel:
                  heads: int = 15, kv_heads: int = 5, head_dim: int = 64, ffn: int = 2560, vocab: int = 49152,
                  theta: float = 1e5, cache: int = None, eps: float = 1e-5, exps: dict = None):
         from . import attention as AT
-        self.E = E = dict(LLAMA_EXP, **(exps or {}))
+        from . import numeric as NU
+        E = dict(LLAMA_EXP, **(exps or {}))
+        per_class = {_LLAMA_CLASS[k]: v for k, v in E.items()}
+        per_class.update(x2=E["fx"], xf=E["fx"])
+        # the exponent table the lowering reads (one exponent per tensor class)
+        self.formats = fm = NU.LlamaFormats.per_tensor(per_class, L=layers, H=heads, KV=kv_heads, HD=head_dim)
+        self.E = E
         rng = np.random.default_rng(seed)
         self.B, self.T, self.D, self.H, self.KV, self.HD = batch, seq, hidden, heads, kv_heads, head_dim
         self.L, self.ffn, self.vocab, self.eps = layers, ffn, vocab, eps
@@ -377,16 +379,22 @@ class LlamaModel:
         self.w = []
         for li in range(layers):
             lw = {}
-            for nm, (k, m, f_in, f_out) in dict(q0=(D, nq, E["fx"], E["fq0"]), k0=(D, nk, E["fx"], E["fk0"]),
-                                                v=(D, nk, E["fx"], E["fv"]),
-                                                o=(nq, D, E["fp"] + E["fvc"] - 8, E["fo"]),
-                                                g=(D, ffn, E["fx"], E["fg"]), u=(D, ffn, E["fx"], E["fu"]),
-                                                d=(ffn, D, E["fa"], E["fd"])).items():
-                lw[nm] = N.TensorInfo(f"l{li}.{nm}.w", [k, m],
-                                      data=_encode_weight(rng.normal(0.0, 0.02, (k, m)), f_out + 8 - f_in))
+            # each weight at wexp[i][j] = f_out[j] + 8 - f_in[i] from the table
+            # (the o projection reads the P.V output, f_p + f_vc - 8 per channel)
+            for nm, (k, m, f_in, f_out) in dict(
+                    q0=(D, nq, fm.get("x", li, D), fm.get("q0", li, nq)),
+                    k0=(D, nk, fm.get("x", li, D), fm.get("k0", li, nk)),
+                    v=(D, nk, fm.get("x", li, D), fm.get("v", li, nk)),
+                    o=(nq, D, fm.pv(li), fm.get("o", li, D)),
+                    g=(D, ffn, fm.get("x2", li, D), fm.get("g", li, ffn)),
+                    u=(D, ffn, fm.get("x2", li, D), fm.get("u", li, ffn)),
+                    d=(ffn, D, fm.get("a", li, ffn), fm.get("d", li, D))).items():
+                data, _, _ = NU.encode_matmul_weight(rng.normal(0.0, 0.02, (k, m)), f_in, f_out)
+                lw[nm] = N.TensorInfo(f"l{li}.{nm}.w", [k, m], data=data)
             self.w.append(lw)
-        self.w_lm = N.TensorInfo("logits.w", [D, vocab],
-                                 data=_encode_weight(rng.normal(0.0, 0.02, (D, vocab)), E["fl"] + 8 - E["fx"]))
+        data, _, _ = NU.encode_matmul_weight(rng.normal(0.0, 0.02, (D, vocab)), fm.get("xf", layers, D),
+                                             fm.get("logits", layers, vocab))
+        self.w_lm = N.TensorInfo("logits.w", [D, vocab], data=data)
         self.states = []
         for li in range(layers):
             for nm, f in (("ck", E["fkc"]), ("cv", E["fvc"])):

@@ -13,11 +13,12 @@ reference, so everything the tests need is written here).
    ``rowops_spec``) on seeded inputs, imported through the inert ``onnx``
    stand-in in ``_onnx_stub``.
 
-    python tests/golden/make_golden.py [--ref /root/reference] [--only hw|sim]
+    python tests/golden/make_golden.py [--ref /root/reference] [--only hw|sim|graph|llm|attn|smx|numeric]
 """
 from __future__ import annotations
 
 import argparse
+import json
 import os
 import sys
 
@@ -713,10 +714,105 @@ def make_llm_smx_host(ref, out):
     print("sim_llm_smx_host.npz:", len(res), "arrays")
 
 
+def make_numeric(ref, out):
+    """The exponent planner: the reference's weight encodings
+    (src/numeric.py encode_matmul_weights / encode_conv_weights) on MatMul and
+    Conv nodes with per-tensor and per-channel exponents, and its Llama
+    formats lookups (src/llama.py Formats: K / V caches, P.V, scores, the
+    residual).  Weights are seeded float32; the fixture keeps the inputs and
+    the encoded raw words, exponents and saturation counts (for the large
+    MatMul, which crosses the row-block boundary, CRCs of them)."""
+    _import_reference(ref)
+    import types
+    import onnx
+    from src import numeric as NU, nodes as N
+    from src.dtype import AP_FIXED_16_8 as D
+    from src.tensor import TensorInfo as T
+    from src.graph_builder import score_exp
+    from src.llama import Formats
+    nd = onnx.NodeProto()
+    rng = np.random.default_rng(11)
+    res = {}
+    mm_cases = [  # tag, batch, K, M, f_in (scalar or [K]), f_out, weight scale
+        ("mm_t", 1, 24, 40, 11, 10, 0.05),
+        ("mm_ch", 1, 32, 48, rng.integers(6, 14, 32), rng.integers(8, 13, 48), 0.2),
+        ("mm_wide", 2, 16, 24, rng.integers(-3, 20, 16), rng.integers(-10, 25, 24), 1.5),
+        ("mm_sat", 1, 20, 12, 4, 14, 3.0),
+    ]
+    for tag, bt, K, M, fi, fo, sc in mm_cases:
+        w = (rng.standard_normal((bt, K, M) if bt > 1 else (K, M)) * sc).astype(np.float32)
+        A = T(onnx_name="a", shape=[1, 5, K], dtype="float32", exp=np.asarray(fi))
+        B = T(onnx_name="w_" + tag, shape=list(w.shape), dtype="float32", data=w.copy())
+        C = T(onnx_name="c", shape=[1, 5, M], dtype="float32", exp=np.asarray(fo))
+        node = N.MatmulNode(onnx_node=nd, inputs=[A, B], output=C, n=5, k=K, m=M, batch=bt)
+        sat = NU.encode_matmul_weights([node], D)
+        res[f"{tag}_w"], res[f"{tag}_fin"], res[f"{tag}_fout"] = w, np.asarray(fi), np.asarray(fo)
+        res[f"{tag}_raw"] = np.round(B.data.astype(np.float64) * 256).astype(np.int64)
+        res[f"{tag}_wexp"] = np.asarray(B.wexp)
+        res[f"{tag}_wexp_dtype"] = np.array([np.dtype(B.wexp.dtype).itemsize])
+        res[f"{tag}_sat"] = np.array([sat["w_" + tag]])
+    # a weight of 2^21 elements: two row blocks of the encoding
+    K, M = 2048, 1024
+    brng = np.random.default_rng(12345)  # its own stream: the test regenerates the weight
+    w = (brng.standard_normal((K, M)) * 0.03).astype(np.float32)
+    fi, fo = brng.integers(9, 13, K), brng.integers(9, 12, M)
+    B = T(onnx_name="w_big", shape=[K, M], dtype="float32", data=w.copy())
+    node = N.MatmulNode(onnx_node=nd, inputs=[T(onnx_name="a", shape=[1, 2, K], dtype="float32", exp=fi), B],
+                        output=T(onnx_name="c", shape=[1, 2, M], dtype="float32", exp=fo), n=2, k=K, m=M, batch=1)
+    sat = NU.encode_matmul_weights([node], D)
+    raw = np.round(B.data.astype(np.float64) * 256).astype(np.int16)
+    res["mm_big_seed"] = np.array([12345])
+    res["mm_big_crc"] = np.array([zlib.crc32(raw.tobytes()), zlib.crc32(np.ascontiguousarray(B.wexp).tobytes()),
+                                  sat["w_big"], np.dtype(B.wexp.dtype).itemsize], np.int64)
+    res["mm_big_fin"], res["mm_big_fout"] = fi, fo
+    res["mm_big_w_crc"] = np.array([zlib.crc32(w.tobytes())], np.int64)
+    # convs: per tensor / per channel, standard / depthwise, with bias
+    conv_cases = [  # tag, C, M, kh, kw, depthwise, fx, fy (scalars: exp; vectors: chexp)
+        ("cv_t", 6, 8, 3, 3, False, 11, 10),
+        ("cv_tdw", 8, 8, 3, 3, True, 12, 9),
+        ("cv_ch", 6, 5, 1, 3, False, rng.integers(8, 13, 6), rng.integers(7, 12, 5)),
+        ("cv_chdw", 7, 7, 3, 1, True, rng.integers(8, 13, 7), rng.integers(7, 12, 7)),
+        ("cv_sat", 4, 3, 1, 1, False, 6, 14),
+    ]
+    for tag, C, M, kh, kw, dw, fx, fy in conv_cases:
+        w = (rng.standard_normal((M, 1 if dw else C, kh, kw)) * (2.0 if tag == "cv_sat" else 0.1)).astype(np.float32)
+        b = (rng.standard_normal(M) * 0.5).astype(np.float32)
+        per_ch = np.ndim(fx) > 0
+        X = T(onnx_name="x", shape=[1, C, 4, 6], dtype="float32", **({"chexp": np.asarray(fx)} if per_ch else {"exp": np.asarray(fx)}))
+        Y = T(onnx_name="y", shape=[1, M, 4 - kh + 1, 6 - kw + 1], dtype="float32",
+              **({"chexp": np.asarray(fy)} if per_ch else {"exp": np.asarray(fy)}))
+        W = T(onnx_name="w_" + tag, shape=list(w.shape), dtype="float32", data=w.copy())
+        Bt = T(onnx_name="b_" + tag, shape=[M], dtype="float32", data=b.copy())
+        node = N.ConvNode(onnx_node=nd, inputs=[X, W, Bt], output=Y, batch=1, in_ch=C, in_h=4, in_w=6, out_ch=M,
+                          out_h=4 - kh + 1, out_w=6 - kw + 1, kh=kh, kw=kw, stride_h=1, stride_w=1, dilation_h=1,
+                          dilation_w=1, pad_top=0, pad_left=0, has_bias=True, is_depthwise=dw)
+        sat = NU.encode_conv_weights([node], D)
+        res[f"{tag}_w"], res[f"{tag}_b"] = w, b
+        res[f"{tag}_fx"], res[f"{tag}_fy"] = np.asarray(fx), np.asarray(fy)
+        res[f"{tag}_wraw"] = np.round(W.data.astype(np.float64) * 256).astype(np.int64).reshape(w.shape)
+        res[f"{tag}_braw"] = np.round(Bt.data.astype(np.float64) * 256).astype(np.int64).reshape(-1)[:M]
+        res[f"{tag}_wexp"], res[f"{tag}_bexp"] = np.asarray(W.wexp), np.asarray(Bt.wexp)
+        res[f"{tag}_sat"] = np.array([sat["w_" + tag], sat["b_" + tag]])
+    # Llama formats lookups on a table with per-head and per-channel entries
+    cfg = types.SimpleNamespace(L=2, H=6, KV=2, HD=4)
+    exps = {"q@0": [10, 11, 10, 9, 10, 12], "k@0": [10, 11], "p@0": 12, "v@0": 13, "x@0": 12,
+            "q@1": 10, "k@1": [9, 10], "p@1": [12, 12, 11, 12, 13, 12], "v@1": list(range(8, 16)),
+            "vc@1": [9] * 8, "s@1": [3, 4, 5, 6, 7, 8], "pv@1": list(range(24)), "res@2": 16}
+    fm = Formats({"exponents": exps, "policy": "test"}, cfg)
+    res["fm_exps"] = np.frombuffer(json.dumps(exps).encode(), np.uint8)
+    for li in range(2):
+        res[f"fm_k{li}"], res[f"fm_v{li}"], res[f"fm_pv{li}"] = fm.k_cache(li), fm.v_cache(li), fm.pv(li)
+        res[f"fm_s{li}"] = (fm.heads("s", li, 6) if f"s@{li}" in fm.exp
+                            else score_exp(fm.heads("q", li, 6), fm.heads("k", li, 2), 2))
+    res["fm_res"] = np.array([fm.res_bits])
+    np.savez_compressed(os.path.join(out, "sim_numeric.npz"), **res)
+    print("sim_numeric.npz:", len(res), "arrays")
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--ref", default="/root/reference")
-    ap.add_argument("--only", choices=["hw", "sim", "graph", "llm", "attn", "smx"])
+    ap.add_argument("--only", choices=["hw", "sim", "graph", "llm", "attn", "smx", "numeric"])
     ap.add_argument("--out", default=HERE)
     args = ap.parse_args()
     if args.only in (None, "hw"):
@@ -731,6 +827,8 @@ def main():
         make_llm_attn(args.ref, args.out)
     if args.only in (None, "smx"):
         make_llm_smx_host(args.ref, args.out)
+    if args.only in (None, "numeric"):
+        make_numeric(args.ref, args.out)
 
 
 if __name__ == "__main__":
