@@ -191,8 +191,8 @@ def main():
     ap.add_argument("--no-models", action="store_true", help="skip the MNIST / MobileNetV2 / BERT forward passes")
     ap.add_argument("--models", help="comma list of model cases to run (default: all)")
     ap.add_argument("--detail", help="write per-problem kernel times of one profiled step to this JSON file")
-    ap.add_argument("--case", choices=["gemm", "gemm_small", "vectorop", "softmax", "conv", "llama_prefill",
-                                       "llama_decode"],
+    ap.add_argument("--case", choices=["gemm", "gemm_small", "gemm_int16", "vectorop", "softmax", "conv",
+                                       "llama_prefill", "llama_decode"],
                     help="run one job a few times (a small case for ncu captures) and exit")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
@@ -650,8 +650,11 @@ def run_case(args):
     g = torch.Generator(device="cuda")
     g.manual_seed(5)
     ri = lambda n, lo=-256, hi=256: torch.randint(lo, hi, (n,), dtype=torch.int16, device="cuda", generator=g)  # noqa
-    if args.case in ("gemm", "gemm_small"):
-        b, m, k, n = (4, 2048, 4096, 4096) if args.case == "gemm" else (16, 8, 4096, 4096)
+    if args.case in ("gemm", "gemm_small", "gemm_int16"):
+        # the split-plane form, the int16 form with 8 rows, the int16 form with A
+        # in TMEM on a compute-heavy job (the sweep's 16 x 2048 x 4096 x 256)
+        b, m, k, n = {"gemm": (4, 2048, 4096, 4096), "gemm_small": (16, 8, 4096, 4096),
+                      "gemm_int16": (16, 2048, 4096, 256)}[args.case]
         A, B, C = ri(b * m * k), ri(b * k * n), torch.empty(b * m * n, dtype=torch.int16, device="cuda")
         fn = lambda: ops.matmul(A, B, C, n=m, k=k, m=n, batch=b, a_batch_stride=m * k, b_batch_stride=k * n,  # noqa
                                 c_batch_stride=m * n)
