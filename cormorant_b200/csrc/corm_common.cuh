@@ -5,6 +5,8 @@
 #include <stdint.h>
 
 #include <cstdio>
+#include <cstdlib>
+#include <utility>
 #include <string>
 
 #include "cormorant_b200.h"
@@ -92,4 +94,36 @@ static inline unsigned corm_blocks(size_t work, unsigned per_block, unsigned cap
   size_t b = (work + per_block - 1) / per_block;
   if (b < 1) b = 1;
   return (unsigned)(b > cap ? cap : b);
+}
+
+// ---------------------------------------------------------------- programmatic dependent launch
+// A kernel launched with corm_launch_pdl may start while the kernel before it
+// on the stream is still running: it must call corm_pdl_wait() before its first
+// global-memory access (the wait returns once the previous grid has completed
+// and its writes are visible), and calls corm_pdl_trigger() to let the next
+// kernel launch early in turn.  Only the launch latency and the prologue
+// overlap; every read and write stays ordered after the previous kernel.
+__device__ __forceinline__ void corm_pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void corm_pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+// CORM_NO_PDL=1: plain launches (for comparisons)
+static inline bool corm_pdl_enabled() {
+  const char* e = getenv("CORM_NO_PDL");
+  return !(e && e[0] == '1');
+}
+
+template <typename... KArgs, typename... Args>
+static inline cudaError_t corm_launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                                          cudaStream_t st, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = corm_pdl_enabled() ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
 }

@@ -14,8 +14,8 @@
 //                tcgen05.ld of the three accumulators, int64 recombine and the
 //                job's rounding rule into registers, TMEM released to the next
 //                unit's MMAs, then the int16 stores — or, for a K-split unit,
-//                exact int64 atomics into a partial-sum buffer that
-//                gemm_finish_kernel rounds afterwards
+//                the exact int64 sums into the split's slot of a partial-sum
+//                buffer that gemm_finish_kernel adds and rounds afterwards
 // int16 operands (split inside the kernel): warp 0 owns TMEM and issues the
 // MMAs, warp 17 lane 0 loads the raw int16 tiles by TMA (unswizzled, 64 KB a
 // stage) into the stage's own bytes, warps 1..8 split them in place into the
@@ -403,6 +403,9 @@ __global__ void __launch_bounds__(Roles<CONV>::threads, 1)
   __syncthreads();
   sm100::tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  // the prologue above overlaps the previous kernel; global memory only after it
+  corm_pdl_wait();
+  corm_pdl_trigger();
 
   if (!CONV && warp == 0 && lane == 0) {
     // ---------------- TMA producer (ring counter g runs across units)
@@ -696,12 +699,15 @@ __global__ void __launch_bounds__(Roles<CONV>::threads, 1)
           }
           if (!row_ok) continue;
           const uint32_t c0 = w.tile_c + cc;
-          unsigned long long* dst = ep.partial + ((uint64_t)w.bz * ep.rows + r) * ep.cols + c0;
+          // this split's slot of the partial sums ([split][batch][rows][cols])
+          unsigned long long* dst = ep.partial +
+                                    ((uint64_t)(w.kb0 / ep.kb_per_split) * ep.batch + w.bz) * ep.rows * ep.cols +
+                                    (uint64_t)r * ep.cols + c0;
 #pragma unroll
           for (int j = 0; j < CW; j++) {
             if (c0 + j >= ep.cols) continue;
             const int64_t acc = ((int64_t)(int32_t)hh[j] << 16) + ((int64_t)(int32_t)mid[j] << 8) + (int64_t)(int32_t)ll[j];
-            atomicAdd(dst + j, (unsigned long long)acc);
+            dst[j] = (unsigned long long)acc;
           }
         }
         continue;
@@ -772,14 +778,20 @@ __global__ void __launch_bounds__(Roles<CONV>::threads, 1)
   }
 }
 
-// K-split units summed exactly in int64; this applies the bias and the rule.
+// K-split units: each split's int64 sums in its own slot (every element of
+// every slot written once, no memset, no atomics); this adds them, applies
+// the bias and the rule.
 __global__ void __launch_bounds__(256) gemm_finish_kernel(const EpiArgs ep) {
+  corm_pdl_wait();
+  corm_pdl_trigger();
   const uint64_t total = (uint64_t)ep.batch * ep.rows * ep.cols;
   for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (uint64_t)gridDim.x * blockDim.x) {
     const uint32_t c = (uint32_t)(i % ep.cols);
     const uint64_t br = i / ep.cols;
     const uint32_t r = (uint32_t)(br % ep.rows), bz = (uint32_t)(br / ep.rows);
-    int64_t acc = (int64_t)ep.partial[i];
+    unsigned long long sum = 0;  // the splits' slots in split order (exact integer sums)
+    for (uint32_t sp = 0; sp < ep.splits; sp++) sum += __ldg(ep.partial + sp * total + i);
+    int64_t acc = (int64_t)sum;
     if (ep.mode == 1 && ep.bias) acc += (int64_t)ep.bias[c] << 8;
     const uint64_t off = out_offset(ep, ep.mode == 0 ? bz : 0, r, c);
     int16_t y = finish(acc, ep.flags);
@@ -820,12 +832,16 @@ __device__ __forceinline__ void split16(const SplitSeg& g, uint64_t i) {
 }
 
 __global__ void __launch_bounds__(256) split_rows_kernel(const SplitSeg g, uint64_t total16) {
+  corm_pdl_wait();
+  corm_pdl_trigger();
   for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total16; i += (uint64_t)gridDim.x * blockDim.x)
     split16(g, i);
 }
 
 __global__ void __launch_bounds__(256) split2_rows_kernel(const SplitSeg ga, uint64_t na, const SplitSeg gb,
                                                           uint64_t nb) {
+  corm_pdl_wait();
+  corm_pdl_trigger();
   for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < na + nb; i += (uint64_t)gridDim.x * blockDim.x) {
     if (i < na)
       split16(ga, i);
@@ -929,7 +945,7 @@ int split_planes(const int16_t* src, uint64_t src_bs, uint32_t planes, uint32_t 
   if (total16 == 0) return CORM_OK;
   {
     ProfScope prof_("split_rows_kernel", stream);
-    split_rows_kernel<<<corm_blocks(total16, 256, 148u * 16u), 256, 0, stream>>>(g, total16);
+    corm_launch_pdl(split_rows_kernel, dim3(corm_blocks(total16, 256, 148u * 16u)), dim3(256), 0, stream, g, total16);
   }
   return cuda_status("split_planes");
 }
@@ -939,14 +955,15 @@ int split_planes2(const SplitSeg& a, const SplitSeg& b, cudaStream_t stream) {
   if (na + nb == 0) return CORM_OK;
   {
     ProfScope prof_("split2_rows_kernel", stream);
-    split2_rows_kernel<<<corm_blocks(na + nb, 256, 148u * 16u), 256, 0, stream>>>(a, na, b, nb);
+    corm_launch_pdl(split2_rows_kernel, dim3(corm_blocks(na + nb, 256, 148u * 16u)), dim3(256), 0, stream, a, na, b,
+                    nb);
   }
   return cuda_status("split_planes2");
 }
 
 size_t gemm_partial_bytes(uint32_t rows, uint32_t cols, uint32_t Kp, uint32_t batch) {
   const Split sp = split_of(rows, cols, Kp, batch);
-  return sp.splits > 1 ? (((size_t)batch * rows * cols * 8 + 255) & ~(size_t)255) : 0;
+  return sp.splits > 1 ? (((size_t)sp.splits * batch * rows * cols * 8 + 255) & ~(size_t)255) : 0;
 }
 
 int gemm_i8x4(const GemmJob& j, cudaStream_t stream) {
@@ -1030,8 +1047,6 @@ int gemm_i8x4(const GemmJob& j, cudaStream_t stream) {
   if (sp.splits > 1) {
     if (!j.partial) return fail(CORM_ENOMEM, "gemm: K-split job without a partial-sum buffer");
     ep.partial = (unsigned long long*)j.partial;
-    if (cudaMemsetAsync(j.partial, 0, (size_t)j.batch * j.rows * j.cols * 8, stream) != cudaSuccess)
-      return cuda_status("gemm partial memset");
   }
   static bool attr_set[64];
   int dev = 0;
@@ -1047,15 +1062,18 @@ int gemm_i8x4(const GemmJob& j, cudaStream_t stream) {
   {
     ProfScope prof_("gemm_i8x4_kernel", stream);
     if (conv)
-      gemm_i8x4_kernel<true><<<grid, Roles<true>::threads, SMEM_BYTES, stream>>>(m_ahi, m_alo, m_bhi, m_blo, ep);
+      corm_launch_pdl(gemm_i8x4_kernel<true>, dim3(grid), dim3(Roles<true>::threads), SMEM_BYTES, stream, m_ahi, m_alo,
+                      m_bhi, m_blo, ep);
     else
-      gemm_i8x4_kernel<false><<<grid, Roles<false>::threads, SMEM_BYTES, stream>>>(m_ahi, m_alo, m_bhi, m_blo, ep);
+      corm_launch_pdl(gemm_i8x4_kernel<false>, dim3(grid), dim3(Roles<false>::threads), SMEM_BYTES, stream, m_ahi,
+                      m_alo, m_bhi, m_blo, ep);
   }
   if (int rc = cuda_status("gemm_i8x4")) return rc;
   if (sp.splits > 1) {
     {
       ProfScope prof_("gemm_finish_kernel", stream);
-      gemm_finish_kernel<<<corm_blocks((uint64_t)j.batch * j.rows * j.cols, 256), 256, 0, stream>>>(ep);
+      corm_launch_pdl(gemm_finish_kernel, dim3(corm_blocks((uint64_t)j.batch * j.rows * j.cols, 256)), dim3(256), 0,
+                      stream, ep);
     }
     return cuda_status("gemm_finish");
   }

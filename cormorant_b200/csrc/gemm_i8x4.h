@@ -28,7 +28,7 @@ struct GemmJob {
   // B planes: K-major [planes][cols][Kp] (b_mn = 0), or MN-major [planes][K][cols_p]
   // with cols_p = cols rounded up to 16 (b_mn = 1)
   uint32_t b_mn, K, cols_p;
-  // K-split partial sums (int64 [batch][rows][cols]), gemm_partial_bytes() bytes, or nullptr
+  // K-split partial sums (int64 [split][batch][rows][cols]), gemm_partial_bytes() bytes, or nullptr
   void* partial;
   // epilogue addressing
   int mode;                 // 0: out[b*obs + r*ldc + c]; 1: conv NCHW y[n][pattern(c)][p], r = n*P + p

@@ -80,11 +80,14 @@ __global__ void __launch_bounds__(256) split_b_gather_kernel(MmArgs p, uint32_t 
 
 // GEMV path (n <= 2, HBM-bound on B): a warp owns 256 consecutive columns —
 // 8 per lane, one 16-byte load per B row — over a K range, A values read as
-// warp-wide broadcasts, int64 sums; the K range is split across CTAs (exact
-// integer atomics into int64 partials) when the grid alone would not fill
-// the GPU.
+// warp-wide broadcasts, int64 sums; the K range is split across CTAs when the
+// grid alone would not fill the GPU, each range's sums stored in its own
+// int64 slot (no memset, no atomics) and added in range order by
+// mm_small_finish.
 template <int NR>
 __global__ void __launch_bounds__(128) mm_gemv_kernel(MmArgs p, uint32_t kchunk, unsigned long long* partial) {
+  corm_pdl_wait();
+  corm_pdl_trigger();
   const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
   const uint32_t j0 = (blockIdx.x * 4 + w) * 256 + lane * 8;
   const uint32_t bt = blockIdx.y;
@@ -131,8 +134,8 @@ __global__ void __launch_bounds__(128) mm_gemv_kernel(MmArgs p, uint32_t kchunk,
     for (int e = 0; e < 8; e++) {
       const uint32_t jj = j0 + e;
       if (jj >= p.m) continue;
-      if (partial) {
-        atomicAdd(partial + (uint64_t)bt * p.n * p.m + (uint64_t)r * p.m + jj, (unsigned long long)acc[r][e]);
+      if (partial) {  // this K range's slot: every (slot, batch, row, column) written once
+        partial[(((uint64_t)blockIdx.z * p.batch + bt) * p.n + r) * p.m + jj] = (unsigned long long)acc[r][e];
       } else {
         const uint64_t off = (uint64_t)bt * p.c_bs + (uint64_t)r * p.m + jj;
         int16_t y = mm_finish(acc[r][e], p.flags);
@@ -143,12 +146,17 @@ __global__ void __launch_bounds__(128) mm_gemv_kernel(MmArgs p, uint32_t kchunk,
   }
 }
 
-__global__ void mm_small_finish(MmArgs p, const unsigned long long* partial) {
+// the K ranges' int64 sums added in range order (exact: integer addition)
+__global__ void mm_small_finish(MmArgs p, const unsigned long long* partial, uint32_t ks) {
+  corm_pdl_wait();
+  corm_pdl_trigger();
   const uint64_t total = (uint64_t)p.batch * p.n * p.m;
   for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (uint64_t)gridDim.x * blockDim.x) {
     const uint64_t bt = i / ((uint64_t)p.n * p.m), rem = i - bt * p.n * p.m;
     const uint64_t off = bt * p.c_bs + rem;
-    int16_t y = mm_finish((int64_t)partial[i], p.flags);
+    unsigned long long acc = 0;
+    for (uint32_t z = 0; z < ks; z++) acc += __ldg(partial + z * total + i);
+    int16_t y = mm_finish((int64_t)acc, p.flags);
     if (p.post.op != corm::kPostNone) y = corm::post_apply(p.post, y, corm::post_b(p.post, off, (uint32_t)(rem % p.m)));
     p.c[off] = y;
   }
@@ -172,7 +180,7 @@ Plan plan_of(const corm_matmul_desc* d) {
     pl.kchunk = (d->k + ks - 1) / ks;
     pl.ksplit = (d->k + pl.kchunk - 1) / pl.kchunk;
     ks = pl.ksplit;
-    pl.bytes = ks > 1 ? (size_t)d->batch * d->n * d->m * 8 : 0;
+    pl.bytes = ks > 1 ? (size_t)ks * d->batch * d->n * d->m * 8 : 0;  // a slot per K range
     return pl;
   }
   pl.Kp = (d->k + 15u) / 16u * 16u;
@@ -313,20 +321,20 @@ int matmul_impl(const corm_matmul_desc* d, const corm::PostOp& post, cudaStream_
   }
   if (pl.small) {
     unsigned long long* partial = pl.ksplit > 1 ? (unsigned long long*)ws : nullptr;
-    if (partial && cudaMemsetAsync(partial, 0, pl.bytes, st) != cudaSuccess) return corm::cuda_status("memset");
     dim3 grid((d->m + 1023) / 1024, d->batch, pl.ksplit);
     if (d->n <= 1) {
       corm::ProfScope prof_("mm_gemv_kernel<1>", st);
-      mm_gemv_kernel<1><<<grid, 128, 0, st>>>(p, pl.kchunk, partial);
+      corm_launch_pdl(mm_gemv_kernel<1>, grid, dim3(128), 0, st, p, pl.kchunk, partial);
     } else {  // n <= kSmallRows
       corm::ProfScope prof_("mm_gemv_kernel<2>", st);
-      mm_gemv_kernel<2><<<grid, 128, 0, st>>>(p, pl.kchunk, partial);
+      corm_launch_pdl(mm_gemv_kernel<2>, grid, dim3(128), 0, st, p, pl.kchunk, partial);
     }
     if (int rc = corm::cuda_status("matmul small")) return rc;
     if (partial) {
       {
         corm::ProfScope prof_("mm_small_finish", st);
-        mm_small_finish<<<corm_blocks((uint64_t)d->batch * d->n * d->m, 256), 256, 0, st>>>(p, partial);
+        corm_launch_pdl(mm_small_finish, dim3(corm_blocks((uint64_t)d->batch * d->n * d->m, 256)), dim3(256), 0, st, p,
+                        (const unsigned long long*)partial, pl.ksplit);
       }
       return corm::cuda_status("matmul small finish");
     }
@@ -406,20 +414,20 @@ extern "C" int corm_matmul_noalloc(const corm_matmul_desc* d, corm_stream_t stre
   uint8_t* w = na.scratch;
   if (pl.small) {
     unsigned long long* partial = pl.ksplit > 1 ? (unsigned long long*)w : nullptr;
-    if (partial && cudaMemsetAsync(partial, 0, pl.bytes, st) != cudaSuccess) return corm::cuda_status("memset");
     dim3 grid((d->m + 1023) / 1024, d->batch, pl.ksplit);
     if (d->n <= 1) {
       corm::ProfScope prof_("mm_gemv_kernel<1>", st);
-      mm_gemv_kernel<1><<<grid, 128, 0, st>>>(p, pl.kchunk, partial);
+      corm_launch_pdl(mm_gemv_kernel<1>, grid, dim3(128), 0, st, p, pl.kchunk, partial);
     } else {  // n <= kSmallRows
       corm::ProfScope prof_("mm_gemv_kernel<2>", st);
-      mm_gemv_kernel<2><<<grid, 128, 0, st>>>(p, pl.kchunk, partial);
+      corm_launch_pdl(mm_gemv_kernel<2>, grid, dim3(128), 0, st, p, pl.kchunk, partial);
     }
     if (int rc = corm::cuda_status("matmul_noalloc small")) return rc;
     if (partial) {
       {
         corm::ProfScope prof_("mm_small_finish", st);
-        mm_small_finish<<<corm_blocks((uint64_t)d->batch * d->n * d->m, 256), 256, 0, st>>>(p, partial);
+        corm_launch_pdl(mm_small_finish, dim3(corm_blocks((uint64_t)d->batch * d->n * d->m, 256)), dim3(256), 0, st, p,
+                        (const unsigned long long*)partial, pl.ksplit);
       }
       return corm::cuda_status("matmul_noalloc small finish");
     }
