@@ -58,6 +58,8 @@ __device__ __forceinline__ uint64_t y_chan(const ConvArgs& a, uint32_t m) {
 // out once) and gathers 16 K entries, eight loads in flight at a time.
 __global__ void __launch_bounds__(256) im2col_split(ConvArgs a, uint32_t Ptot, uint32_t K, uint32_t Kp, int8_t* hi,
                                                     uint8_t* lo) {
+  corm_pdl_wait();
+  corm_pdl_trigger();
   __shared__ int16_t tile[64][65];  // [p][k]
   const uint32_t p0 = blockIdx.x * 64, k0 = blockIdx.y * 64;
   const uint32_t P = a.OH * a.OW, KK = a.KH * a.KW;
@@ -105,6 +107,8 @@ __global__ void __launch_bounds__(256) im2col_split(ConvArgs a, uint32_t Ptot, u
 
 // weights (any layout) -> planes [M][Kp], K index (c*kh + i)*kw + j
 __global__ void __launch_bounds__(256) weight_split(ConvArgs a, uint32_t K, uint32_t Kp, int8_t* hi, uint8_t* lo) {
+  corm_pdl_wait();
+  corm_pdl_trigger();
   const uint64_t total = (uint64_t)a.M * (Kp / 8);
   const uint32_t KK = a.KH * a.KW;
   for (uint64_t idx = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; idx < total; idx += (uint64_t)gridDim.x * blockDim.x) {
@@ -143,6 +147,8 @@ __device__ __forceinline__ void conv_put(const ConvArgs& a, int16_t* yp, uint64_
 
 // Depthwise: one thread per output pixel; the channel's taps in registers.
 __global__ void __launch_bounds__(256) conv_depthwise(ConvArgs a) {
+  corm_pdl_wait();
+  corm_pdl_trigger();
   const uint32_t P = a.OH * a.OW;
   const uint64_t total = (uint64_t)a.batch * a.M * P;
   for (uint64_t idx = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; idx < total; idx += (uint64_t)gridDim.x * blockDim.x) {
@@ -176,6 +182,8 @@ __global__ void __launch_bounds__(256) conv_depthwise(ConvArgs a) {
 constexpr uint32_t kDwMaxG = 64;
 template <int KH_, int KW_, int S_>
 __global__ void __launch_bounds__(256) conv_dw_plane(ConvArgs a, uint32_t SH, uint32_t SW, uint32_t G) {
+  corm_pdl_wait();
+  corm_pdl_trigger();
   extern __shared__ int16_t s_in[];  // [G][SH][SW], then [G][KH*KW] taps
   __shared__ const int16_t* s_src[kDwMaxG];
   __shared__ int16_t* s_yp[kDwMaxG];
@@ -293,6 +301,8 @@ __global__ void __launch_bounds__(256) conv_dw_plane(ConvArgs a, uint32_t SH, ui
 constexpr uint32_t kDwWarpWin = 1024;  // int16 per warp window
 template <int S_>
 __global__ void __launch_bounds__(256) conv_dw_warp(ConvArgs a, uint32_t SH, uint32_t SW) {
+  corm_pdl_wait();
+  corm_pdl_trigger();
   __shared__ __align__(16) int16_t s_win[8][kDwWarpWin];
   constexpr int NR = 4, R = (NR - 1) * S_ + 3;
   const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -463,9 +473,9 @@ int conv_impl(const corm_conv_desc* d, const corm::PostOp& post, cudaStream_t st
       const unsigned grid = (unsigned)std::min<uint64_t>((planes + 7) / 8, 148ull * 8ull);
       corm::ProfScope prof_("conv_dw_warp", st);
       if (d->stride_h == 1)
-        conv_dw_warp<1><<<grid, 256, 0, st>>>(a, SH, SW);
+        corm_launch_pdl(conv_dw_warp<1>, dim3(grid), dim3(256), 0, st, a, SH, SW);
       else
-        conv_dw_warp<2><<<grid, 256, 0, st>>>(a, SH, SW);
+        corm_launch_pdl(conv_dw_warp<2>, dim3(grid), dim3(256), 0, st, a, SH, SW);
       return corm::cuda_status("conv depthwise");
     }
     const size_t win = (size_t)SH * SW + (size_t)d->kh * d->kw;  // int16 per plane
@@ -480,7 +490,7 @@ int conv_impl(const corm_conv_desc* d, const corm::PostOp& post, cudaStream_t st
       const uint32_t s_eq = d->stride_h == d->stride_w ? d->stride_h : 0;
       auto launch = [&](auto kern) {
         cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        kern<<<grid, 256, smem, st>>>(a, SH, SW, G);
+        corm_launch_pdl(kern, dim3(grid), dim3(256), smem, st, a, SH, SW, G);
       };
       if (k3 && unit_dil && s_eq == 1)
         launch(conv_dw_plane<3, 3, 1>);
@@ -492,7 +502,7 @@ int conv_impl(const corm_conv_desc* d, const corm::PostOp& post, cudaStream_t st
     }
     {
       corm::ProfScope prof_("conv_depthwise", st);
-      conv_depthwise<<<corm_blocks(total, 256, 148u * 16u), 256, 0, st>>>(a);
+      corm_launch_pdl(conv_depthwise, dim3(corm_blocks(total, 256, 148u * 16u)), dim3(256), 0, st, a);
     }
     return corm::cuda_status("conv depthwise");
   }
@@ -509,12 +519,12 @@ int conv_impl(const corm_conv_desc* d, const corm::PostOp& post, cudaStream_t st
   dim3 gi((pl.Ptot + 63) / 64, (pl.Kp + 63) / 64);
   {
     corm::ProfScope prof_("im2col_split", st);
-    im2col_split<<<gi, 256, 0, st>>>(a, pl.Ptot, pl.K, pl.Kp, a_hi, a_lo);
+    corm_launch_pdl(im2col_split, dim3(gi), dim3(256), 0, st, a, pl.Ptot, pl.K, pl.Kp, a_hi, a_lo);
   }
   if (int rc = corm::cuda_status("conv im2col")) return rc;
   {
     corm::ProfScope prof_("weight_split", st);
-    weight_split<<<corm_blocks((uint64_t)d->out_ch * (pl.Kp / 8), 256), 256, 0, st>>>(a, pl.K, pl.Kp, b_hi, b_lo);
+    corm_launch_pdl(weight_split, dim3(corm_blocks((uint64_t)d->out_ch * (pl.Kp / 8), 256)), dim3(256), 0, st, a, pl.K, pl.Kp, b_hi, b_lo);
   }
   if (int rc = corm::cuda_status("conv weight split")) return rc;
   corm::GemmJob j{};

@@ -403,9 +403,10 @@ __global__ void __launch_bounds__(Roles<CONV>::threads, 1)
   __syncthreads();
   sm100::tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  // the prologue above overlaps the previous kernel; global memory only after it
+  // the prologue above overlaps the previous kernel; global memory only after
+  // it.  The next kernel may launch once every CTA's epilogue reaches its last
+  // unit (below): an early launch would park its CTAs beside a long GEMM.
   corm_pdl_wait();
-  corm_pdl_trigger();
 
   if (!CONV && warp == 0 && lane == 0) {
     // ---------------- TMA producer (ring counter g runs across units)
@@ -681,6 +682,7 @@ __global__ void __launch_bounds__(Roles<CONV>::threads, 1)
     uint32_t i = 0;
     for (uint32_t u = blockIdx.x; u < units; u += gridDim.x, i++) {
       const Unit w = unit_of(ep, u);
+      if (u + gridDim.x >= units) corm_pdl_trigger();  // this CTA's last unit
       if (!sm100::mbar_wait(tmem_full, i & 1, ep.err, 103)) break;
       sm100::tc_fence_after();
       const uint32_t r = w.tile_r + q * 32 + lane;

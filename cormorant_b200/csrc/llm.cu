@@ -18,6 +18,8 @@ constexpr int kSmxWarps = 8;
 constexpr int kSmxChunk = 256;  // e values staged per warp and step
 
 __global__ void __launch_bounds__(32 * kSmxWarps) llm_smx_kernel(corm_llm_smx_desc d, uint32_t n) {
+  corm_pdl_wait();
+  corm_pdl_trigger();
   __shared__ double s_e[kSmxWarps][kSmxChunk];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t GT = d.G * d.T;
@@ -79,7 +81,7 @@ extern "C" int corm_llm_attn_softmax(const corm_llm_smx_desc* d, corm_stream_t s
   cudaStream_t st = (cudaStream_t)stream;
   {
     corm::ProfScope prof_("llm_smx_kernel", st);
-    llm_smx_kernel<<<(unsigned)((cols + kSmxWarps - 1) / kSmxWarps), 32 * kSmxWarps, 0, st>>>(*d, n);
+    corm_launch_pdl(llm_smx_kernel, dim3((unsigned)((cols + kSmxWarps - 1) / kSmxWarps)), dim3(32 * kSmxWarps), 0, st, *d, n);
   }
   return corm::cuda_status("llm_attn_softmax");
 }
@@ -95,6 +97,8 @@ extern "C" int corm_llm_attn_softmax(const corm_llm_smx_desc* d, corm_stream_t s
 namespace {
 
 __global__ void __launch_bounds__(256) greedy_embed_kernel(corm_greedy_desc d) {
+  corm_pdl_wait();
+  corm_pdl_trigger();
   __shared__ int32_t s_v[8];
   __shared__ uint32_t s_i[8];
   const uint32_t b = blockIdx.x;
@@ -146,7 +150,7 @@ extern "C" int corm_greedy_embed(const corm_greedy_desc* d, corm_stream_t stream
   cudaStream_t st = (cudaStream_t)stream;
   {
     corm::ProfScope prof_("greedy_embed_kernel", st);
-    greedy_embed_kernel<<<d->batch, 256, 0, st>>>(*d);
+    corm_launch_pdl(greedy_embed_kernel, dim3(d->batch), dim3(256), 0, st, *d);
   }
   return corm::cuda_status("greedy_embed");
 }
@@ -170,6 +174,8 @@ __device__ __forceinline__ int16_t kernel_out16(long long acc) {
 template <int G>
 __global__ void __launch_bounds__(256) decode_attn_kernel(corm_llm_decode_attn_desc d, uint32_t n, uint32_t nk,
                                                           uint32_t j0) {
+  corm_pdl_wait();
+  corm_pdl_trigger();
   extern __shared__ __align__(16) uint8_t da_sm[];
   const uint32_t HD = d.HD, C = d.C;
   const uint32_t b = blockIdx.x % d.B, g = blockIdx.x / d.B;
@@ -346,7 +352,7 @@ extern "C" int corm_llm_decode_attn(const corm_llm_decode_attn_desc* d, corm_str
   cudaStream_t st = (cudaStream_t)stream;
   auto launch = [&](auto kern) {
     if (smem > 48 * 1024) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    kern<<<d->B * d->KV, 256, smem, st>>>(*d, n, nk, j0);
+    corm_launch_pdl(kern, dim3(d->B * d->KV), dim3(256), smem, st, *d, n, nk, j0);
   };
   {
     corm::ProfScope prof_("decode_attn_kernel", st);

@@ -55,6 +55,8 @@ __device__ __forceinline__ int16_t mm_finish(int64_t acc, uint32_t flags) {
 // columns of one K row per thread (row-major B goes through split_planes).
 __global__ void __launch_bounds__(256) split_b_gather_kernel(MmArgs p, uint32_t planes, uint32_t Np, int8_t* hi,
                                                              uint8_t* lo) {
+  corm_pdl_wait();
+  corm_pdl_trigger();
   const uint64_t per_row = Np / 16, total = (uint64_t)planes * p.k * per_row;
   for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (uint64_t)gridDim.x * blockDim.x) {
     const uint64_t row = i / per_row;  // plane * k + kk
@@ -251,7 +253,7 @@ int tensor_path(const corm_matmul_desc* d, const MmArgs& p, const Plan& pl, uint
     const uint64_t total = (uint64_t)pl.b_planes * d->k * (pl.Np / 16);
     {
       corm::ProfScope prof_("split_b_gather_kernel", st);
-      split_b_gather_kernel<<<corm_blocks(total, 256, 148u * 16u), 256, 0, st>>>(p, pl.b_planes, pl.Np, b_hi, b_lo);
+      corm_launch_pdl(split_b_gather_kernel, dim3(corm_blocks(total, 256, 148u * 16u)), dim3(256), 0, st, p, pl.b_planes, pl.Np, b_hi, b_lo);
     }
     if (int rc = corm::cuda_status("matmul split_b")) return rc;
   }

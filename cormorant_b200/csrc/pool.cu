@@ -57,6 +57,8 @@ __device__ __forceinline__ int64_t pool_tap(int64_t acc, int32_t v, const PoolAr
 }
 
 __global__ void __launch_bounds__(256) pool_window(PoolArgs p) {
+  corm_pdl_wait();
+  corm_pdl_trigger();
   const uint64_t total = (uint64_t)p.batch * p.channels * p.out_h * p.out_w;
   for (uint64_t idx = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; idx < total;
        idx += (uint64_t)gridDim.x * blockDim.x) {
@@ -82,6 +84,8 @@ __global__ void __launch_bounds__(256) pool_window(PoolArgs p) {
 
 // Global window: one warp per plane (out 1x1, pool = in, stride irrelevant, no padding).
 __global__ void __launch_bounds__(256) pool_global(PoolArgs p) {
+  corm_pdl_wait();
+  corm_pdl_trigger();
   const uint64_t planes = (uint64_t)p.batch * p.channels;
   const uint32_t hw = p.in_h * p.in_w;
   const uint64_t warp = ((uint64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
@@ -126,12 +130,12 @@ extern "C" int corm_pool(const corm_pool_desc* d, corm_stream_t stream) {
     const uint64_t planes = (uint64_t)d->batch * d->channels;
     {
       corm::ProfScope prof_("pool_global", st);
-      pool_global<<<corm_blocks(planes * 32, 256, 148u * 16u), 256, 0, st>>>(p);
+      corm_launch_pdl(pool_global, dim3(corm_blocks(planes * 32, 256, 148u * 16u)), dim3(256), 0, st, p);
     }
   } else {
     {
       corm::ProfScope prof_("pool_window", st);
-      pool_window<<<corm_blocks(total, 256, 148u * 16u), 256, 0, st>>>(p);
+      corm_launch_pdl(pool_window, dim3(corm_blocks(total, 256, 148u * 16u)), dim3(256), 0, st, p);
     }
   }
   return corm::cuda_status("pool");

@@ -138,6 +138,8 @@ __device__ __forceinline__ void zero_tail(uint8_t* row, uint32_t bytes, int t) {
 }
 
 __global__ void __launch_bounds__(RO_THREADS) ro_rows(RoArgs q) {
+  corm_pdl_wait();
+  corm_pdl_trigger();
   const uint32_t code = q.op & 15u;
   const uint32_t ak = (q.op >> 4) & 3u, bk = (q.op >> 6) & 3u, ck = (q.op >> 8) & 3u;
   const bool ben = (q.op >> 12) & 1u, relu = (q.op >> 15) & 1u, ln = (q.op >> 16) & 1u, scale = (q.op >> 17) & 1u;
@@ -250,6 +252,8 @@ __global__ void __launch_bounds__(RO_THREADS) ro_rows(RoArgs q) {
 // at c + 2((k c1 + r) n + c) reads column (int32)b_s2 + r b_s1 + c when it lies
 // in [win_lo, win_hi), else 0 (rowops_ref.h:285-303).
 __global__ void __launch_bounds__(256) ro_fold(RoArgs q) {
+  corm_pdl_wait();
+  corm_pdl_trigger();
   const uint32_t sh = q.aux & 15u, dv = (q.aux >> 4) & 127u;
   const uint64_t total = (uint64_t)q.c2 * q.c1 * q.n;
   const uint64_t end = (total * 2 + 15) & ~15ull;
@@ -268,6 +272,8 @@ __global__ void __launch_bounds__(256) ro_fold(RoArgs q) {
 // TLOAD: the 64 KiB image as rows of 16-byte words, in order; words 0..2047
 // give two sigmoid entries each (49 bits), 2048..4095 four rsqrt entries.
 __global__ void ro_tload(RoArgs q, uint64_t* sig, uint32_t* rsq) {
+  corm_pdl_wait();
+  corm_pdl_trigger();
   uint32_t w = 0;
   const uint32_t ak = (q.op >> 4) & 3u;
   const uint32_t words = ak == 0 ? (q.n + 7u) / 8u : (q.n + 3u) / 4u;
@@ -299,6 +305,8 @@ __global__ void ro_tload(RoArgs q, uint64_t* sig, uint32_t* rsq) {
 // and stores.  Identity parameters (sa = sb = sc = 0, Bq' = 0, no SCALE) take
 // an int32 path; any other entry the exact 128-bit formula of ro_rows.
 __global__ void __launch_bounds__(256) ro_stream16(RoArgs q) {
+  corm_pdl_wait();
+  corm_pdl_trigger();
   const uint32_t code = q.op & 15u;
   const bool ben = (q.op >> 12) & 1u, relu = (q.op >> 15) & 1u, scale = (q.op >> 17) & 1u;
   const Param pr = ld_param(q, 0);
@@ -357,6 +365,8 @@ __global__ void __launch_bounds__(256) ro_stream16(RoArgs q) {
 // so the shared-memory reads are conflict-free.
 constexpr int XT = 16, XD = 64;
 __global__ void __launch_bounds__(256) ro_xpose8(RoArgs q) {
+  corm_pdl_wait();
+  corm_pdl_trigger();
   __shared__ __align__(16) int16_t tile[8 * XT][XD + 8];
   const uint32_t L = q.n;
   const uint32_t ntg = (q.c1 + XT - 1) / XT, ndg = (L + XD - 1) / XD;
@@ -409,6 +419,8 @@ __device__ __noinline__ int64_t norm_out128(long long P1, int64_t g, int32_t bq,
 
 template <int NW_PER, int AK>
 __global__ void __launch_bounds__(256, 2) ro_norm16(RoArgs q) {
+  corm_pdl_wait();
+  corm_pdl_trigger();
   constexpr uint32_t EPW = AK ? 4u : 8u;  // elements per 16-byte word of A
   extern __shared__ __align__(16) uint8_t ro_smem[];
   const bool ln = (q.op >> 16) & 1u;
@@ -560,6 +572,8 @@ __device__ __forceinline__ void ld8(const uint8_t* p, int kind, int64_t (&v)[N_]
 
 template <int CODE, int AK, int BK, int CK>
 __global__ void __launch_bounds__(256) ro_stream_any(RoArgs q) {
+  corm_pdl_wait();
+  corm_pdl_trigger();
   extern __shared__ __align__(16) uint8_t ro_smem[];
   const bool ben = (q.op >> 12) & 1u, relu = (q.op >> 15) & 1u, scale = (q.op >> 17) & 1u;
   const bool bcast = (q.op >> 13) & 1u;
@@ -672,6 +686,8 @@ __global__ void __launch_bounds__(256) ro_stream_any(RoArgs q) {
 // exactly in int64 when every shift is at most 22 (|x c| <= 2^38), else in 128
 // bits (shifts above 22); one RNE by sh_c, sat16.
 __global__ void __launch_bounds__(256) ro_rope_fast(RoArgs q) {
+  corm_pdl_wait();
+  corm_pdl_trigger();
   extern __shared__ __align__(16) uint8_t ro_smem[];
   const bool bcast = (q.op >> 13) & 1u;
   const uint32_t npar = bcast ? 1u : q.n;
@@ -848,7 +864,7 @@ int rowops_job(const corm_rowops_desc* d0, cudaStream_t st) {
     if (d->n == 0 || d->rows == 0 || d->blocks == 0) return CORM_OK;
     {
       corm::ProfScope prof_("ro_tload", st);
-      ro_tload<<<1, 256, 0, st>>>(q, tb->ro_sig, tb->ro_rsq);
+      corm_launch_pdl(ro_tload, dim3(1), dim3(256), 0, st, q, tb->ro_sig, tb->ro_rsq);
     }
     return corm::cuda_status("rowops tload");
   }
@@ -860,7 +876,7 @@ int rowops_job(const corm_rowops_desc* d0, cudaStream_t st) {
     const uint64_t total = (uint64_t)d->n * d->rows * d->blocks;
     {
       corm::ProfScope prof_("ro_fold", st);
-      ro_fold<<<corm_blocks((total + 7) & ~7ull, 256, 148u * 8u), 256, 0, st>>>(q);
+      corm_launch_pdl(ro_fold, dim3(corm_blocks((total + 7) & ~7ull, 256, 148u * 8u)), dim3(256), 0, st, q);
     }
     return corm::cuda_status("rowops fold");
   }
@@ -890,7 +906,7 @@ int rowops_job(const corm_rowops_desc* d0, cudaStream_t st) {
     const uint64_t words = rows * (d->n / 8);
     {
       corm::ProfScope prof_("ro_stream16", st);
-      ro_stream16<<<corm_blocks(words, 256, 148u * 16u), 256, 0, st>>>(q);
+      corm_launch_pdl(ro_stream16, dim3(corm_blocks(words, 256, 148u * 16u)), dim3(256), 0, st, q);
     }
     return corm::cuda_status("rowops stream");
   }
@@ -898,14 +914,14 @@ int rowops_job(const corm_rowops_desc* d0, cudaStream_t st) {
     // (HD % 16 == 0 and n % HD == 0 were checked above; the B rows 16-byte aligned)
     const size_t smem = (((d->op >> 13) & 1u) ? 1u : d->n) * 3u;
     corm::ProfScope prof_("ro_rope_fast", st);
-    ro_rope_fast<<<corm_blocks(rows * (d->n / 8), 256, 148u * 4u), 256, smem, st>>>(q);
+    corm_launch_pdl(ro_rope_fast, dim3(corm_blocks(rows * (d->n / 8), 256, 148u * 4u)), dim3(256), smem, st, q);
     return corm::cuda_status("rowops rope");
   }
   if (((op == 1 || op == 2) && ak <= 1 && bk <= 1 && ck <= 1 && d->n % 8 == 0) || (op == 4 && i16 && d->n % 8 == 0)) {
     const size_t npar = bcast ? 1u : d->n;
     const size_t smem = npar * 11u;  // n <= 4096: under 48 KB
     const unsigned grid = corm_blocks(rows * (d->n / 8), 256, 148u * 4u);
-    auto launch = [&](auto kern) { kern<<<grid, 256, smem, st>>>(q); };
+    auto launch = [&](auto kern) { corm_launch_pdl(kern, dim3(grid), dim3(256), smem, st, q); };
     corm::ProfScope prof_(op == 4 ? "ro_mulact" : "ro_stream_any", st);
     const int sel = op == 4 ? 8 : (int)(ak * 4 + bk * 2 + ck);
     switch (sel) {
@@ -926,7 +942,7 @@ int rowops_job(const corm_rowops_desc* d0, cudaStream_t st) {
     const uint64_t units = (uint64_t)d->blocks * ((d->rows + XT - 1) / XT) * ((d->n + XD - 1) / XD);
     {
       corm::ProfScope prof_("ro_xpose8", st);
-      ro_xpose8<<<(unsigned)(units < 148u * 16u ? units : 148u * 16u), 256, 0, st>>>(q);
+      corm_launch_pdl(ro_xpose8, dim3((unsigned)(units < 148u * 16u ? units : 148u * 16u)), dim3(256), 0, st, q);
     }
     return corm::cuda_status("rowops xpose");
   }
@@ -939,7 +955,7 @@ int rowops_job(const corm_rowops_desc* d0, cudaStream_t st) {
       const size_t smem = npar * 13u + 16u;  // n <= 4096: under 64 KB
       auto launch = [&](auto kern) {
         if (smem > 48u * 1024u) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        kern<<<grid, 256, smem, st>>>(q);
+        corm_launch_pdl(kern, dim3(grid), dim3(256), smem, st, q);
       };
       // 16-byte words per row: n / 8 (int16) or n / 4 (int32, n <= 2048), <= 32 NW_PER
       const uint32_t words = ak ? d->n / 4u : d->n / 8u;
@@ -957,7 +973,7 @@ int rowops_job(const corm_rowops_desc* d0, cudaStream_t st) {
   }
   {
     corm::ProfScope prof_("ro_rows", st);
-    ro_rows<<<(unsigned)(rows < 148u * 64u ? rows : 148u * 64u), RO_THREADS, 0, st>>>(q);
+    corm_launch_pdl(ro_rows, dim3((unsigned)(rows < 148u * 64u ? rows : 148u * 64u)), dim3(RO_THREADS), 0, st, q);
   }
   return corm::cuda_status("rowops");
 }

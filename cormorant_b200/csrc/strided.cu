@@ -57,6 +57,8 @@ int gs_validate(const corm_gemm_desc* d) {
 }
 
 __global__ void gs_zero(corm_gemm_desc d) {
+  corm_pdl_wait();
+  corm_pdl_trigger();
   const uint64_t total = (uint64_t)d.batch * d.n * d.m;
   for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (uint64_t)gridDim.x * blockDim.x) {
     const uint64_t c = i % d.m, r = (i / d.m) % d.n, b = i / ((uint64_t)d.m * d.n);
@@ -82,7 +84,7 @@ extern "C" int corm_gemm_strided(const corm_gemm_desc* d, corm_stream_t stream) 
   if (d->k == 0) {  // the empty sum: floor(0) = 0
     {
       corm::ProfScope prof_("gs_zero", st);
-      gs_zero<<<corm_blocks((uint64_t)d->batch * d->n * d->m, 256), 256, 0, st>>>(*d);
+      corm_launch_pdl(gs_zero, dim3(corm_blocks((uint64_t)d->batch * d->n * d->m, 256)), dim3(256), 0, st, *d);
     }
     return corm::cuda_status("gemm_strided zero");
   }
@@ -176,6 +178,8 @@ __device__ __forceinline__ void cp_offsets(const CopyArgs& a, uint64_t i, int64_
 }
 
 __global__ void __launch_bounds__(256) copy_nd_elem(CopyArgs a) {
+  corm_pdl_wait();
+  corm_pdl_trigger();
   for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < a.total; i += (uint64_t)gridDim.x * blockDim.x) {
     int64_t so, dof;
     cp_offsets(a, i, so, dof);
@@ -186,6 +190,8 @@ __global__ void __launch_bounds__(256) copy_nd_elem(CopyArgs a) {
 // innermost dim contiguous on both sides, a multiple of 8, 16-byte aligned:
 // one 16-byte word per thread
 __global__ void __launch_bounds__(256) copy_nd_vec8(CopyArgs a) {
+  corm_pdl_wait();
+  corm_pdl_trigger();
   const uint64_t words = a.total / 8;
   for (uint64_t w = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; w < words; w += (uint64_t)gridDim.x * blockDim.x) {
     int64_t so, dof;
@@ -197,6 +203,8 @@ __global__ void __launch_bounds__(256) copy_nd_vec8(CopyArgs a) {
 // 32 x 32 tiles over the source's unit-stride dim (is) and the destination's
 // (id): reads along is, writes along id.  Block (tile_s, tile_d, outer index).
 __global__ void __launch_bounds__(256) copy_nd_tiled(CopyArgs a) {
+  corm_pdl_wait();
+  corm_pdl_trigger();
   __shared__ int16_t tile[32][33];
   const uint32_t Ns = a.dims[a.is], Nd = a.dims[a.id];
   const uint32_t tiles_s = (Ns + 31) / 32, tiles_d = (Nd + 31) / 32;
@@ -267,7 +275,7 @@ extern "C" int corm_copy_nd(const corm_copy_desc* d, corm_stream_t stream) {
   if (vec) {
     {
       corm::ProfScope prof_("copy_nd_vec8", st);
-      copy_nd_vec8<<<corm_blocks(a.total / 8, 256, 148u * 16u), 256, 0, st>>>(a);
+      corm_launch_pdl(copy_nd_vec8, dim3(corm_blocks(a.total / 8, 256, 148u * 16u)), dim3(256), 0, st, a);
     }
     return corm::cuda_status("copy_nd");
   }
@@ -276,13 +284,13 @@ extern "C" int corm_copy_nd(const corm_copy_desc* d, corm_stream_t stream) {
     const uint64_t blocks = a.outer * ((a.dims[a.is] + 31) / 32) * ((a.dims[a.id] + 31) / 32);
     {
       corm::ProfScope prof_("copy_nd_tiled", st);
-      copy_nd_tiled<<<(unsigned)(blocks < 148u * 16u ? blocks : 148u * 16u), 256, 0, st>>>(a);
+      corm_launch_pdl(copy_nd_tiled, dim3((unsigned)(blocks < 148u * 16u ? blocks : 148u * 16u)), dim3(256), 0, st, a);
     }
     return corm::cuda_status("copy_nd");
   }
   {
     corm::ProfScope prof_("copy_nd_elem", st);
-    copy_nd_elem<<<corm_blocks(a.total, 256, 148u * 16u), 256, 0, st>>>(a);
+    corm_launch_pdl(copy_nd_elem, dim3(corm_blocks(a.total, 256, 148u * 16u)), dim3(256), 0, st, a);
   }
   return corm::cuda_status("copy_nd");
 }

@@ -49,6 +49,8 @@ __device__ __forceinline__ int32_t sat16i(int32_t v) { return v > 32767 ? 32767 
 // OP and ACT are template parameters: the per-lane work is straight-line code.
 template <int OP, int ACT>
 __global__ void __launch_bounds__(256) vop_elementwise(VopArgs p) {
+  corm_pdl_wait();
+  corm_pdl_trigger();
   constexpr bool BINARY = OP <= 3;
   const uint64_t words = (uint64_t)p.outer * p.nw;
   for (uint64_t w = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; w < words; w += (uint64_t)gridDim.x * blockDim.x) {
@@ -95,13 +97,13 @@ __global__ void __launch_bounds__(256) vop_elementwise(VopArgs p) {
 template <int OP>
 void launch_vop_act(const VopArgs& p, uint32_t jact, unsigned blocks, cudaStream_t st) {
   switch (jact) {
-    case 0: vop_elementwise<OP, 0><<<blocks, 256, 0, st>>>(p); break;
-    case 1: vop_elementwise<OP, 1><<<blocks, 256, 0, st>>>(p); break;
-    case 2: vop_elementwise<OP, 2><<<blocks, 256, 0, st>>>(p); break;
-    case 3: vop_elementwise<OP, 3><<<blocks, 256, 0, st>>>(p); break;
-    case 4: vop_elementwise<OP, 4><<<blocks, 256, 0, st>>>(p); break;
-    case 5: vop_elementwise<OP, 5><<<blocks, 256, 0, st>>>(p); break;
-    default: vop_elementwise<OP, 6><<<blocks, 256, 0, st>>>(p); break;
+    case 0: corm_launch_pdl(vop_elementwise<OP, 0>, dim3(blocks), dim3(256), 0, st, p); break;
+    case 1: corm_launch_pdl(vop_elementwise<OP, 1>, dim3(blocks), dim3(256), 0, st, p); break;
+    case 2: corm_launch_pdl(vop_elementwise<OP, 2>, dim3(blocks), dim3(256), 0, st, p); break;
+    case 3: corm_launch_pdl(vop_elementwise<OP, 3>, dim3(blocks), dim3(256), 0, st, p); break;
+    case 4: corm_launch_pdl(vop_elementwise<OP, 4>, dim3(blocks), dim3(256), 0, st, p); break;
+    case 5: corm_launch_pdl(vop_elementwise<OP, 5>, dim3(blocks), dim3(256), 0, st, p); break;
+    default: corm_launch_pdl(vop_elementwise<OP, 6>, dim3(blocks), dim3(256), 0, st, p); break;
   }
 }
 
@@ -114,10 +116,10 @@ void launch_vop(const VopArgs& p, uint32_t op, uint32_t jact, unsigned blocks, c
     case 3: launch_vop_act<3>(p, jact, blocks, st); break;
     case 4: launch_vop_act<4>(p, jact, blocks, st); break;
     case 5: launch_vop_act<5>(p, jact, blocks, st); break;
-    case 6: vop_elementwise<6, 3><<<blocks, 256, 0, st>>>(p); break;
-    case 7: vop_elementwise<7, 4><<<blocks, 256, 0, st>>>(p); break;
-    case 8: vop_elementwise<8, 5><<<blocks, 256, 0, st>>>(p); break;
-    default: vop_elementwise<9, 6><<<blocks, 256, 0, st>>>(p); break;
+    case 6: corm_launch_pdl(vop_elementwise<6, 3>, dim3(blocks), dim3(256), 0, st, p); break;
+    case 7: corm_launch_pdl(vop_elementwise<7, 4>, dim3(blocks), dim3(256), 0, st, p); break;
+    case 8: corm_launch_pdl(vop_elementwise<8, 5>, dim3(blocks), dim3(256), 0, st, p); break;
+    default: corm_launch_pdl(vop_elementwise<9, 6>, dim3(blocks), dim3(256), 0, st, p); break;
   }
 }
 
@@ -211,6 +213,8 @@ __device__ __forceinline__ int16_t smx_pq(uint32_t e, uint32_t R, uint64_t rnd, 
 // row groups.
 template <int GROUP, int PER, bool FC>
 __global__ void __launch_bounds__(GROUP >= 256 ? GROUP : 256) smx_rows(SmxArgs p) {
+  corm_pdl_wait();
+  corm_pdl_trigger();
   constexpr int NT = GROUP >= 256 ? GROUP : 256;
   constexpr int ROWS_PER_CTA = NT / GROUP;
   constexpr int V = PER / 8;
@@ -297,6 +301,8 @@ __global__ void __launch_bounds__(GROUP >= 256 ? GROUP : 256) smx_rows(SmxArgs p
 // stages 16 query columns of every key in shared memory, then writes P rows
 // (one per query, size keys long) at stride b_inc.
 __global__ void __launch_bounds__(256) smx_cols(SmxArgs p) {
+  corm_pdl_wait();
+  corm_pdl_trigger();
   extern __shared__ int16_t s_x[];  // [size][16]
   __shared__ int32_t s_m[16];
   __shared__ uint64_t s_R[16];
@@ -355,6 +361,8 @@ __device__ __forceinline__ uint32_t smx_tbase(uint32_t c, uint32_t KP) { return 
 
 template <int WPL, bool STORE_E, bool FC>
 __global__ void __launch_bounds__(256) smx_cols_t(SmxArgs p) {
+  corm_pdl_wait();
+  corm_pdl_trigger();
   extern __shared__ __align__(16) uint8_t smx_sm[];
   int32_t* s_tab = (int32_t*)smx_sm;
   int16_t* s_x = (int16_t*)(s_tab + 4096);
@@ -463,9 +471,9 @@ unsigned smx_grid(uint64_t groups) { return (unsigned)(groups < 148u * 8u ? (gro
 template <int G, int P>
 void launch_rows(const SmxArgs& p, unsigned grid, unsigned threads, bool fc, cudaStream_t st) {
   if (fc)
-    smx_rows<G, P, true><<<grid, threads, 0, st>>>(p);
+    corm_launch_pdl(smx_rows<G, P, true>, dim3(grid), dim3(threads), 0, st, p);
   else
-    smx_rows<G, P, false><<<grid, threads, 0, st>>>(p);
+    corm_launch_pdl(smx_rows<G, P, false>, dim3(grid), dim3(threads), 0, st, p);
 }
 
 int launch_softmax(const corm_vectorop_desc* d, cudaStream_t st, const corm::DeviceTables* tb) {
@@ -498,9 +506,9 @@ int launch_softmax(const corm_vectorop_desc* d, cudaStream_t st, const corm::Dev
       cudaFuncSetAttribute(kf, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
       cudaFuncSetAttribute(ks, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
       if (fc)
-        kf<<<grid, 256, smem, st>>>(p);
+        corm_launch_pdl(kf, dim3(grid), dim3(256), smem, st, p);
       else
-        ks<<<grid, 256, smem, st>>>(p);
+        corm_launch_pdl(ks, dim3(grid), dim3(256), smem, st, p);
     };
     {
       corm::ProfScope prof_("smx_cols_t", st);
@@ -518,7 +526,7 @@ int launch_softmax(const corm_vectorop_desc* d, cudaStream_t st, const corm::Dev
     cudaFuncSetAttribute(smx_cols, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     {
       corm::ProfScope prof_("smx_cols", st);
-      smx_cols<<<p.rows / 16, 256, smem, st>>>(p);
+      corm_launch_pdl(smx_cols, dim3(p.rows / 16), dim3(256), smem, st, p);
     }
     return corm::cuda_status("softmax_cols");
   }
