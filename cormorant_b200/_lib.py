@@ -17,7 +17,7 @@ F_WRAP32, F_WEIGHT_LOGICAL, F_ACT_RELU, F_ACT_RELU6 = 0x1, 0x2, 0x4, 0x8
 
 # every symbol include/cormorant_b200.h declares
 EXPORTS = ("corm_vectorop", "corm_matmul_workspace_size", "corm_matmul", "corm_matmul_noalloc", "corm_conv_workspace_size", "corm_conv",
-           "corm_matmul_post", "corm_conv_post", "corm_gemm_strided_workspace_size", "corm_gemm_strided",
+           "corm_matmul_post", "corm_matmul_groups", "corm_conv_post", "corm_gemm_strided_workspace_size", "corm_gemm_strided",
            "corm_copy_nd", "corm_llm_attn_softmax", "corm_greedy_embed",
            "corm_llm_decode_attn", "corm_rowops_chain", "corm_rowops_chain_dev",
            "corm_stream_done",
@@ -45,6 +45,10 @@ class MatmulDesc(C.Structure):
     _fields_ = [("a", C.c_void_p), ("b", C.c_void_p), ("c", C.c_void_p)] + _u32_fields(
         ["n", "k", "m", "batch", "a_batch_stride", "b_batch_stride", "c_batch_stride", "b_packed", "gemv_kw",
          "flags"]) + [("workspace", C.c_void_p), ("workspace_bytes", C.c_size_t)]
+
+
+class OutGroups(C.Structure):
+    _fields_ = [("count", C.c_uint32), ("width", C.c_uint32 * 4), ("out", C.c_void_p * 4)]
 
 
 class ConvDesc(C.Structure):
@@ -133,6 +137,7 @@ def lib() -> C.CDLL:
     for name, argt in (("corm_vectorop", [C.POINTER(VectorOpDesc), C.c_void_p]),
                        ("corm_matmul", [C.POINTER(MatmulDesc), C.c_void_p]),
                        ("corm_matmul_noalloc", [C.POINTER(MatmulDesc), C.c_void_p]),
+                       ("corm_matmul_groups", [C.POINTER(MatmulDesc), C.POINTER(OutGroups), C.c_void_p]),
                        ("corm_matmul_workspace_size", [C.POINTER(MatmulDesc), C.POINTER(C.c_size_t)]),
                        ("corm_conv", [C.POINTER(ConvDesc), C.c_void_p]),
                        ("corm_conv_workspace_size", [C.POINTER(ConvDesc), C.POINTER(C.c_size_t)]),

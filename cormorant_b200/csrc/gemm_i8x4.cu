@@ -69,6 +69,10 @@ struct EpiArgs {
   uint32_t ymode;  // the form of the rule (floor_acc)
   uint32_t cvar;   // act (0 none, 1 ReLU, 2 Clip(0,6)) * 2 + conv bias
   int* err;
+  // mode 2 (column groups): output columns [gc[g], gc[g + 1]) go to their own
+  // row-major [batch][rows][gw[g]] buffer at element offset gbase[g] from out
+  int64_t gbase[4];
+  uint32_t gc[5], gw[4];
   uint32_t raw_tma;  // int16 operands: raw tiles by TMA (map_ahi: A, map_bhi: B) into the stage
   uint32_t a_box_rows, b_pitch;  // raw boxes: A rows (<= 128) and the B row's bytes (<= 256)
 };
@@ -116,9 +120,15 @@ __device__ __forceinline__ int16_t finish(int64_t acc, uint32_t flags) {
 }
 
 // element (bz, r, c) of the output: its address offset (mode 0: row-major with
-// batch stride; mode 1: NCHW with the y channel pattern, r = n * P + p)
+// batch stride; mode 1: NCHW with the y channel pattern, r = n * P + p; mode 2:
+// the column's group buffer, groups of whole 32-column runs)
 __device__ __forceinline__ uint64_t out_offset(const EpiArgs& ep, uint32_t bz, uint32_t r, uint32_t c) {
   if (ep.mode == 0) return (uint64_t)bz * ep.out_batch_stride + (uint64_t)r * ep.ldc + c;
+  if (ep.mode == 2) {
+    const int g = (c >= ep.gc[1]) + (c >= ep.gc[2]) + (c >= ep.gc[3]);
+    const uint64_t w = ep.gw[g];
+    return (uint64_t)ep.gbase[g] + ((uint64_t)bz * ep.rows + r) * w + (c - ep.gc[g]);
+  }
   const uint32_t n = r / ep.P, p = r - n * ep.P;
   const uint64_t coff = ep.y_cn ? (uint64_t)(c % ep.y_cn) * ep.y_cs + (uint64_t)(c / ep.y_cn) * ep.y_gs
                                 : (uint64_t)c * ep.y_cs;
@@ -207,7 +217,7 @@ __device__ __forceinline__ void post_operand(const EpiArgs& ep, uint64_t rowbase
 // NC consecutive results of row r (columns c0 ..) to the output
 template <int NC>
 __device__ __forceinline__ void store_row(const EpiArgs& ep, uint32_t bz, uint32_t r, uint32_t c0, const uint32_t* v2) {
-  if (ep.mode == 0) {
+  if (ep.mode != 1) {  // row-major (mode 2: an NC-column run lies in one group)
     int16_t* dst = ep.out + out_offset(ep, bz, r, c0);
     if (c0 + NC <= ep.cols && ((uintptr_t)dst & 15) == 0) {
 #pragma unroll
@@ -795,7 +805,7 @@ __global__ void __launch_bounds__(256) gemm_finish_kernel(const EpiArgs ep) {
     for (uint32_t sp = 0; sp < ep.splits; sp++) sum += __ldg(ep.partial + sp * total + i);
     int64_t acc = (int64_t)sum;
     if (ep.mode == 1 && ep.bias) acc += (int64_t)ep.bias[c] << 8;
-    const uint64_t off = out_offset(ep, ep.mode == 0 ? bz : 0, r, c);
+    const uint64_t off = out_offset(ep, ep.mode != 1 ? bz : 0, r, c);
     int16_t y = finish(acc, ep.flags);
     if (ep.post.op != kPostNone) y = post_apply(ep.post, y, post_b(ep.post, off, c));
     ep.out[off] = y;
@@ -1003,6 +1013,25 @@ int gemm_i8x4(const GemmJob& j, cudaStream_t stream) {
   EpiArgs ep{};
   ep.mode = j.mode;
   ep.out = j.out;
+  if (j.ngroups > 1) {
+    // column groups: whole 32-column runs each (the epilogue stores runs of up
+    // to 32 columns into one buffer), no fused job, row-major only
+    if (j.ngroups > 4 || j.mode != 0 || j.post.op != kPostNone)
+      return fail(CORM_EINVAL, "gemm: %u output groups (1..4, row-major, no fused job)", j.ngroups);
+    ep.mode = 2;
+    uint32_t c = 0;
+    for (uint32_t g = 0; g < 4; g++) {
+      const bool on = g < j.ngroups;
+      if (on && (!j.gout[g] || j.gw[g] == 0 || ((uintptr_t)j.gout[g] & 1u) || (g + 1 < j.ngroups && j.gw[g] % 32u)))
+        return fail(CORM_EINVAL, "gemm: output group %u (width %u) not a non-empty run of 32 columns", g, j.gw[g]);
+      ep.gc[g] = on ? c : 0xFFFFFFFFu;
+      ep.gw[g] = on ? j.gw[g] : 1u;
+      ep.gbase[g] = on ? ((int64_t)(intptr_t)j.gout[g] - (int64_t)(intptr_t)j.out) / 2 : 0;
+      c += on ? j.gw[g] : 0u;
+    }
+    ep.gc[4] = 0xFFFFFFFFu;
+    if (c != j.cols) return fail(CORM_EINVAL, "gemm: output groups cover %u of %u columns", c, j.cols);
+  }
   ep.out_batch_stride = j.out_batch_stride;
   ep.ldc = j.ldc;
   ep.rows = j.rows;

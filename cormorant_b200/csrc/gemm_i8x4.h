@@ -48,6 +48,12 @@ struct GemmJob {
   uint64_t a_bs16, b_bs16;
   uint32_t lda, ldb;
   int* err;                 // status word for the bounded waits; nullptr: the library's per-device word
+  // mode 0 with ngroups > 1: output columns split into consecutive groups, group g
+  // (gw[g] columns, all but the last a multiple of 32) row-major [batch][rows][gw[g]]
+  // at gout[g]; out is then gout[0]
+  uint32_t ngroups;
+  int16_t* gout[4];
+  uint32_t gw[4];
 };
 
 constexpr uint32_t kGemmMaxK = 32768;

@@ -202,7 +202,7 @@ Plan plan_of(const corm_matmul_desc* d) {
 // partial-sum buffer in the workspace); otherwise the operands are split into
 // int8 planes first.  The workspace is sized for the second case.
 int tensor_path(const corm_matmul_desc* d, const MmArgs& p, const Plan& pl, uint8_t* w, const corm::PostOp& post,
-                int* err, cudaStream_t st) {
+                int* err, cudaStream_t st, const corm_out_groups* grp = nullptr) {
   // The producer warps sustain fewer bytes in flight than the TMA: for large
   // tiles of work per operand byte (n and m both above ~1000) the split planes
   // plus TMA are faster, below it the saved split traffic wins.
@@ -214,6 +214,13 @@ int tensor_path(const corm_matmul_desc* d, const MmArgs& p, const Plan& pl, uint
   j.rows = d->n;
   j.cols = d->m;
   j.Kp = pl.Kp;
+  if (grp) {
+    j.ngroups = grp->count;
+    for (uint32_t g = 0; g < 4 && g < grp->count; g++) {
+      j.gout[g] = grp->out[g];
+      j.gw[g] = grp->width[g];
+    }
+  }
   j.batch = d->batch;
   j.a_planes = pl.a_planes;
   j.b_planes = pl.b_planes;
@@ -436,4 +443,33 @@ extern "C" int corm_matmul_noalloc(const corm_matmul_desc* d, corm_stream_t stre
     return CORM_OK;
   }
   return tensor_path(d, p, pl, w, corm::PostOp{}, na.status, st);
+}
+
+// ---------------------------------------------------------------- column groups
+// corm_matmul_groups: one MatMul job whose output columns go to several
+// buffers — sibling projections (q / k / v, gate / up) over their concatenated
+// weights in one launch.  The tensor-core path only (n > 2), no fused job.
+extern "C" int corm_matmul_groups(const corm_matmul_desc* d, const corm_out_groups* g, corm_stream_t stream) {
+  if (int rc = validate(d)) return rc;
+  if (int rc = corm::check_device()) return rc;
+  if (!g || g->count < 1 || g->count > 4) return corm::fail(CORM_EINVAL, "corm_matmul_groups: 1..4 output groups");
+  if (!d->a || !d->b) return corm::fail(CORM_EINVAL, "corm_matmul_groups: null operand");
+  if (d->n <= kSmallRows || d->k == 0)
+    return corm::fail(CORM_EINVAL, "corm_matmul_groups: n %u / k %u (the tensor-core path: n > %u, k > 0)", d->n, d->k,
+                      kSmallRows);
+  if (d->n == 0 || d->m == 0 || d->batch == 0) return CORM_OK;
+  cudaStream_t st = (cudaStream_t)stream;
+  corm_matmul_desc dd = *d;
+  dd.c = g->out[0];
+  dd.c_batch_stride = d->n * g->width[0];
+  MmArgs p{dd.a, dd.b, dd.c, dd.n, dd.k, dd.m, dd.batch, dd.a_batch_stride, dd.b_batch_stride, dd.c_batch_stride,
+           dd.b_packed, dd.gemv_kw, dd.flags, corm::PostOp{}};
+  const Plan pl = plan_of(&dd);
+  void* ws = d->workspace;
+  if (pl.bytes) {
+    if (ws && d->workspace_bytes < pl.bytes)
+      return corm::fail(CORM_ENOMEM, "corm_matmul_groups: workspace %zu < %zu bytes", d->workspace_bytes, pl.bytes);
+    if (!ws && !(ws = corm::scratch(pl.bytes, st))) return CORM_ENOMEM;
+  }
+  return tensor_path(&dd, p, pl, (uint8_t*)ws, corm::PostOp{}, nullptr, st, g);
 }

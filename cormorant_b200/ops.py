@@ -92,6 +92,35 @@ def matmul(a, b, c, *, n, k, m, batch=1, a_batch_stride=0, b_batch_stride=0, c_b
     return workspace
 
 
+def matmul_groups(a, b, outs, widths, *, n, k, batch=1, a_batch_stride=0, b_batch_stride=0, flags=0,
+                  workspace=None):
+    """One MatMul job over B = [k][sum(widths)] whose output columns go to
+    several buffers (corm_matmul_groups): outs[g] receives the widths[g]
+    columns of group g, row-major [batch][n][widths[g]].  Sibling projections
+    that read the same A run as one launch; n > 2, all widths but the last
+    multiples of 32."""
+    for t, nm in ((a, "a"), (b, "b")):
+        _i16(t, nm)
+    if not 1 <= len(outs) == len(widths) <= 4:
+        raise CormError(_lib.CORM_EINVAL, "matmul_groups: 1..4 outputs, one width each")
+    for t in outs:
+        _i16(t, "out")
+    st = _ready()
+    m = int(sum(widths))
+    d = _lib.MatmulDesc(_ptr(a), _ptr(b), _ptr(outs[0]), n, k, m, batch, a_batch_stride, b_batch_stride,
+                        n * widths[0], 0, 0, flags, None, 0)
+    need = C.c_size_t(0)
+    check(lib().corm_matmul_workspace_size(C.byref(d), C.byref(need)))
+    if need.value:
+        if workspace is None:
+            workspace = torch.empty(need.value, dtype=torch.uint8, device=a.device)
+        d.workspace, d.workspace_bytes = _ptr(workspace), workspace.numel() * workspace.element_size()
+    g = _lib.OutGroups(len(outs), (C.c_uint32 * 4)(*(list(widths) + [0] * (4 - len(widths)))),
+                       (C.c_void_p * 4)(*([_ptr(t) for t in outs] + [None] * (4 - len(outs)))))
+    check(lib().corm_matmul_groups(C.byref(d), C.byref(g), st))
+    return workspace
+
+
 def gemm_strided(a, b, c, *, n, k, m, batch=1, lda=None, ldb=None, ldc=None, b_trans=False, a_batch_stride=0,
                  b_batch_stride=0, c_batch_stride=0, flags=0, workspace=None):
     """A strided batch of MatMul jobs (corm_gemm_strided): element row strides

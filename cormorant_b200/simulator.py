@@ -84,6 +84,7 @@ class GpuSimulator:
         self._weights: Dict[str, torch.Tensor] = share._weights if share is not None else {}
         self._ws: Optional[torch.Tensor] = None
         self._plan = self._fusion_plan() if fuse else {}
+        self._groups = self._sibling_groups() if fuse else {}
 
     # ------------------------------------------------------------ tensors
     def _alloc(self, numel: int) -> torch.Tensor:
@@ -331,6 +332,8 @@ class GpuSimulator:
                 meta[t.onnx_name] = t
         fused_into = {j: (i, flag, post) for i, (j, flag, post) in self._plan.items()}
         skip = set(self._plan)
+        for members in self._groups.values():  # run at their group's first member
+            skip |= set(members[1:])
         attn_fused = self._decode_attn_plan(keep) if (self.fuse and keep is not None) else {}
         for _mi, info in attn_fused.items():
             skip |= set(info["nodes"])
@@ -353,7 +356,14 @@ class GpuSimulator:
                 alias_t = self._graph.nodes[ri].output
                 if pspec is not None:
                     post = self._post_of(pspec, get)
-            if kind in ("MatmulNode", "MatmulConvNode"):
+            if i in self._groups:
+                ys = self._matmul_group(self._groups[i], get)
+                for j, yj in zip(self._groups[i][1:], ys[1:]):
+                    t = self._graph.nodes[j].output
+                    raw[t.onnx_name] = yj
+                    meta[t.onnx_name] = t
+                y = ys[0]
+            elif kind in ("MatmulNode", "MatmulConvNode"):
                 y = self._matmul(sn, get(sn.inputs[0]), get(sn.inputs[1]), flag, post)
             elif kind == "ConvNode":
                 y = self._conv(sn, get(sn.inputs[0]), get(sn.inputs[1]),
@@ -457,6 +467,60 @@ class GpuSimulator:
             ops.matmul(a[ao:], b[bo:], y[o * inner * n * m:], n=n, k=k, m=m, batch=inner, a_batch_stride=a_bs,
                        b_batch_stride=b_bs, c_batch_stride=n * m, flags=wrap | flag, workspace=ws, post=po)
         return y
+
+    def _sibling_groups(self) -> Dict[int, list]:
+        """MatMuls that read the same A with constant 2-D weights of the same K
+        and run no fused job (a layer's q / k / v, its gate / up): runs of up to
+        4, in graph order, all widths but a run's last multiples of 32, and
+        n > 2 rows.  {first index: member indices}; each run is one
+        corm_matmul_groups launch over the column-concatenated weights, at
+        its first member (A and the weights exist there), every output the
+        same as its own MatMul's."""
+        nodes = self._graph.nodes
+        fused_producers = {j for (j, _f, _p) in self._plan.values()}
+        wnames = {t.onnx_name for t in self._graph.weight_tensors}
+        by_a: Dict[tuple, list] = {}
+        for i, sn in enumerate(nodes):
+            if _kind(sn) != "MatmulNode" or i in fused_producers or len(sn.inputs) != 2:
+                continue
+            A, B, Y = sn.inputs[0], sn.inputs[1], sn.output
+            if B.onnx_name not in wnames or getattr(B, "data", None) is None or len(B.shape) != 2 or len(A.shape) < 2:
+                continue
+            n, k = int(np.prod(A.shape[:-1])), int(A.shape[-1])
+            if n <= 2 or k != int(B.shape[0]):
+                continue
+            by_a.setdefault((A.onnx_name, k, _has_exp(A, B, Y)), []).append(i)
+        groups: Dict[int, list] = {}
+        for idx in by_a.values():
+            run: list = []
+            for i in idx + [None]:
+                if i is not None:
+                    run.append(i)
+                if i is None or int(nodes[i].inputs[1].shape[1]) % 32 or len(run) == 4:
+                    if len(run) >= 2:
+                        groups[run[0]] = list(run)
+                    run = []
+        return groups
+
+    def _matmul_group(self, members, get):
+        """One corm_matmul_groups launch for a run of sibling MatMuls: their
+        outputs, in member order."""
+        sns = [self._graph.nodes[j] for j in members]
+        A = sns[0].inputs[0]
+        n, k = int(np.prod(A.shape[:-1])), int(A.shape[-1])
+        widths = [int(sn.inputs[1].shape[1]) for sn in sns]
+        m = sum(widths)
+        key = ("group",) + tuple(sn.inputs[1].onnx_name for sn in sns)
+        if key not in self._weights:  # the weights side by side, once
+            cat = self._alloc(k * m)
+            cat[:k * m].view(k, m).copy_(torch.cat([get(sn.inputs[1])[:k * w].view(k, w)
+                                                    for sn, w in zip(sns, widths)], dim=1))
+            self._weights[key] = cat
+        ys = [self._alloc(sn.output.numel) for sn in sns]
+        wrap = F_WRAP32 if _has_exp(A, sns[0].inputs[1], sns[0].output) else 0
+        ws = self._workspace(self._mm_ws(n, k, m, 1, 0, 0))
+        ops.matmul_groups(get(A), self._weights[key], ys, widths, n=n, k=k, flags=wrap, workspace=ws)
+        return ys
 
     @staticmethod
     def _mm_ws(n, k, m, batch, a_bs, b_bs) -> int:

@@ -152,6 +152,21 @@ typedef struct {
 } corm_postop;
 
 int corm_matmul_post(const corm_matmul_desc* d, const corm_postop* post, corm_stream_t stream);
+
+/* Sibling projections in one launch (no counterpart in the reference): the
+ * MatMul job of d (n > 2 rows) with its m output columns split into count
+ * (1..4) consecutive groups, group g — width[g] columns, all but the last a
+ * multiple of 32 — stored row-major [batch][n][width[g]] at out[g] (batch
+ * stride n * width[g]); d->c and d->c_batch_stride are ignored.  Several
+ * MatMuls that read the same A and constant weights (q / k / v, gate / up)
+ * run as one job over their column-concatenated weights; every output equals
+ * its own MatMul's.  Workspace and errors as corm_matmul. */
+typedef struct {
+  uint32_t count;
+  uint32_t width[4];
+  int16_t* out[4];
+} corm_out_groups;
+int corm_matmul_groups(const corm_matmul_desc* d, const corm_out_groups* g, corm_stream_t stream);
 int corm_conv_post(const corm_conv_desc* d, const corm_postop* post, corm_stream_t stream);
 
 /* ---------------------------------------------------------------- strided batches

@@ -73,6 +73,17 @@ def cpu_ops(monkeypatch):
         spec.matmul_job(np16(a), np16(b), np16(c), n, k, m, batch, a_batch_stride, b_batch_stride, c_batch_stride,
                         b_packed, gemv_kw, wrap=bool(flags & F_WRAP32))
 
+    def matmul_groups(a, b, outs, widths, *, n, k, batch=1, a_batch_stride=0, b_batch_stride=0, flags=0,
+                      workspace=None):
+        assert batch == 1
+        m = sum(widths)
+        y = spec.matmul_raw(np16(a)[:n * k].astype(np.int64).reshape(n, k), np16(b)[:k * m].astype(np.int64).reshape(k, m),
+                            wrap=bool(flags & F_WRAP32))
+        c0 = 0
+        for o, w in zip(outs, widths):
+            np16(o)[:n * w] = y[:, c0:c0 + w].reshape(-1)
+            c0 += w
+
     def vectorop(a, b, c, *, size, op, outer=1, a_inc=0, b_inc=0, act=0, alpha=0, smx_cm=0, smx_cfg=0, smx_mask=0):
         spec.vectorop_job(np16(a), np16(b), np16(c), size, op, outer, a_inc, b_inc, act, alpha, smx_cm, smx_cfg,
                           smx_mask)
@@ -204,6 +215,7 @@ def cpu_ops(monkeypatch):
     monkeypatch.setattr(ops, "copy_nd", copy_nd)
     monkeypatch.setattr(ops, "rowops", rowops)
     monkeypatch.setattr(ops, "matmul", matmul)
+    monkeypatch.setattr(ops, "matmul_groups", matmul_groups)
     monkeypatch.setattr(ops, "vectorop", vectorop)
     monkeypatch.setattr(GpuSimulator, "_mm_ws", staticmethod(lambda *a: 0))
     return GpuSimulator

@@ -107,8 +107,8 @@ def test_llama_decode_host_logic_cpu(cpu_ops):
     oracle's job models, against the oracle's own loop."""
     from cormorant_b200 import workloads as WL
     from cormorant_b200.llm_runner import LlamaRunner
-    m = WL.LlamaModel(seed=12, batch=2, seq=16, layers=1, hidden=64, heads=4, kv_heads=2, head_dim=16, ffn=128,
-                      vocab=50)
+    m = WL.LlamaModel(seed=12, batch=3, seq=16, layers=1, hidden=64, heads=4, kv_heads=2, head_dim=16, ffn=128,
+                      vocab=50)  # 3 sequences: the step's q / k / v and gate / up run as column groups
     _decode_vs_oracle(LlamaRunner(m, device="cpu"), m, 3)
 
 
@@ -119,5 +119,5 @@ def test_gpu_llama_decode_vs_oracle():
         pytest.skip("no CUDA device")
     from cormorant_b200 import workloads as WL
     from cormorant_b200.llm_runner import LlamaRunner
-    m = WL.LlamaModel(seed=13, batch=2, seq=32, layers=2, vocab=1000)
+    m = WL.LlamaModel(seed=13, batch=3, seq=32, layers=2, vocab=1000)  # 3 rows: column-group projections
     _decode_vs_oracle(LlamaRunner(m), m, 4)
