@@ -248,7 +248,8 @@ __global__ void __launch_bounds__(256) decode_attn_kernel(corm_llm_decode_attn_d
 #pragma unroll 2
   for (uint32_t jj = tid; jj < span; jj += blockDim.x) {
     const int16_t* kr = K + (uint64_t)(j0 + jj) * HD;
-    long long acc[G];
+    // the sums modulo 2^32: the rule wraps the accumulator to int32 first
+    uint32_t acc[G];
 #pragma unroll
     for (int h = 0; h < G; h++) acc[h] = 0;
     for (uint32_t d0 = 0; d0 < HD; d0 += 8) {
@@ -257,10 +258,10 @@ __global__ void __launch_bounds__(256) decode_attn_kernel(corm_llm_decode_attn_d
 #pragma unroll
       for (int e8 = 0; e8 < 8; e8++)
 #pragma unroll
-        for (int h = 0; h < G; h++) acc[h] += (long long)(kv[e8] * q[(d0 + e8) * G + h]);
+        for (int h = 0; h < G; h++) acc[h] += (uint32_t)(kv[e8] * q[(d0 + e8) * G + h]);
     }
 #pragma unroll
-    for (int h = 0; h < G; h++) S[h * span + jj] = kernel_out16(acc[h]);
+    for (int h = 0; h < G; h++) S[h * span + jj] = kernel_out16((long long)(int32_t)acc[h]);
   }
   __syncthreads();
   // per head: the max, e in order, the sum left to right (one thread per head), P
@@ -291,36 +292,49 @@ __global__ void __launch_bounds__(256) decode_attn_kernel(corm_llm_decode_attn_d
     S[i] = (int16_t)(qv > 32767.0 ? 32767.0 : qv);  // P replaces the scores
   }
   __syncthreads();
-  // P.V: HD columns x (256 / HD) key groups, int64 sums, reduced in shared memory
-  const uint32_t groups = blockDim.x / HD, col = tid % HD, kg = tid / HD;
-  long long acc[G];
+  // P.V: a thread per 8 columns (one 16-byte V load per key) and key group
+  // (256 / (HD / 8) groups, each taking every groups-th key), sums modulo 2^32
+  // (the rule wraps to int32), the groups reduced in shared memory per head
+  const uint32_t c8n = HD / 8, groups = blockDim.x / c8n, c8 = tid % c8n, kg = tid / c8n;
+  uint32_t acc[G][8];
 #pragma unroll
-  for (int h = 0; h < G; h++) acc[h] = 0;
+  for (int h = 0; h < G; h++)
+#pragma unroll
+    for (int e8 = 0; e8 < 8; e8++) acc[h][e8] = 0;
   if (kg < groups)
-    for (uint32_t base = kg; base < span; base += 8u * groups) {  // 8 loads in flight per thread
-      int32_t vv[8];
+    for (uint32_t base = kg; base < span; base += 4u * groups) {  // 4 rows in flight per thread
+      int4 vv[4];
 #pragma unroll
-      for (int u = 0; u < 8; u++) {
+      for (int u = 0; u < 4; u++) {
         const uint32_t jj = base + u * groups;
-        vv[u] = jj < span ? (int32_t)__ldg(V + (uint64_t)(j0 + jj) * HD + col) : 0;
+        // plain loads: this launch wrote the row at pos (the prep above)
+        vv[u] = jj < span ? *(const int4*)(V + (uint64_t)(j0 + jj) * HD + c8 * 8) : make_int4(0, 0, 0, 0);
       }
 #pragma unroll
-      for (int u = 0; u < 8; u++) {
+      for (int u = 0; u < 4; u++) {
         const uint32_t jj = base + u * groups;
         if (jj < span) {
+          const int16_t* v8 = (const int16_t*)&vv[u];
 #pragma unroll
-          for (int h = 0; h < G; h++) acc[h] += (long long)(S[h * span + jj] * vv[u]);
+          for (int h = 0; h < G; h++) {
+            const int32_t pw = S[h * span + jj];
+#pragma unroll
+            for (int e8 = 0; e8 < 8; e8++) acc[h][e8] += (uint32_t)(pw * (int32_t)v8[e8]);
+          }
         }
       }
     }
+  uint32_t* red = (uint32_t*)s_acc;  // [groups][HD]: groups * HD <= 2 blockDim.x * 4 = 2048
 #pragma unroll
   for (int h = 0; h < G; h++) {
-    if (kg < groups) s_acc[kg * HD + col] = acc[h];
+    if (kg < groups)
+#pragma unroll
+      for (int e8 = 0; e8 < 8; e8++) red[kg * HD + c8 * 8 + e8] = acc[h][e8];
     __syncthreads();
     if (tid < (int)HD) {
-      long long t = 0;
-      for (uint32_t k2 = 0; k2 < groups; k2++) t += s_acc[k2 * HD + tid];
-      out[h * HD + tid] = kernel_out16(t);
+      uint32_t t = 0;
+      for (uint32_t k2 = 0; k2 < groups; k2++) t += red[k2 * HD + tid];
+      out[h * HD + tid] = kernel_out16((long long)(int32_t)t);
     }
     __syncthreads();
   }

@@ -121,3 +121,19 @@ def test_gpu_llama_decode_vs_oracle():
     from cormorant_b200.llm_runner import LlamaRunner
     m = WL.LlamaModel(seed=13, batch=3, seq=32, layers=2, vocab=1000)  # 3 rows: column-group projections
     _decode_vs_oracle(LlamaRunner(m), m, 4)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("dims", [dict(hidden=64, heads=4, kv_heads=2, head_dim=16, ffn=128),
+                                  dict(hidden=256, heads=8, kv_heads=1, head_dim=32, ffn=256)],
+                         ids=["g2_hd16", "g8_hd32"])
+def test_gpu_llama_decode_heads_vs_oracle(dims):
+    """The decode attention launch at other group sizes and head widths (2
+    heads of 16, 8 heads of 32 per KV group) against the oracle's loop."""
+    torch = pytest.importorskip("torch")
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    from cormorant_b200 import workloads as WL
+    from cormorant_b200.llm_runner import LlamaRunner
+    m = WL.LlamaModel(seed=21, batch=3, seq=16, layers=1, vocab=300, **dims)
+    _decode_vs_oracle(LlamaRunner(m), m, 3)
