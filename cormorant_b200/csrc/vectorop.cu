@@ -374,8 +374,17 @@ __global__ void __launch_bounds__(256) smx_cols_t(SmxArgs p) {
   const uint32_t tiles = (p.rows + 31u) / 32u;
   for (uint32_t tile = blockIdx.x; tile < tiles; tile += gridDim.x) {
     const uint32_t q0 = tile * 32u;
+    // the keys any query of the tile reads: valid0 + its largest q mod period
+    // (a causal mask reads about half); the rest of the staging is never used
+    const uint32_t qn = min(31u, p.rows - 1u - q0);
+    uint32_t tmax = 0;
+    if (p.period) {
+      const uint32_t t0 = q0 % p.period;
+      tmax = t0 + qn >= p.period ? p.period - 1u : t0 + qn;
+    }
+    const uint32_t vmax = min(p.size, p.valid0 + tmax);
     __syncthreads();  // the previous tile's reads (and the TAB copy) are done
-    for (uint32_t idx = threadIdx.x; idx < (p.size / 2u) * 4u; idx += 256u) {
+    for (uint32_t idx = threadIdx.x; idx < ((vmax + 1u) / 2u) * 4u; idx += 256u) {
       const uint32_t jp = idx >> 2, part = idx & 3u;
       if (q0 + 8u * part >= p.rows) continue;
       const int16_t* src = p.a + (size_t)(2u * jp) * p.a_inc + q0 + 8u * part;
@@ -400,6 +409,7 @@ __global__ void __launch_bounds__(256) smx_cols_t(SmxArgs p) {
 #pragma unroll(STORE_E ? WPL : 1)
     for (int k = 0; k < WPL; k++) {
       const uint32_t j0 = 8u * (sl + 8u * k);
+      if (j0 >= v) break;  // masked keys: neither max nor e
       const int4 w = j0 < p.size ? *(const int4*)(xs + j0) : make_int4(0, 0, 0, 0);
       if constexpr (STORE_E) xw[k] = w;
       const int16_t* t8 = (const int16_t*)&w;
@@ -413,6 +423,7 @@ __global__ void __launch_bounds__(256) smx_cols_t(SmxArgs p) {
 #pragma unroll(STORE_E ? WPL : 1)
     for (int k = 0; k < WPL; k++) {
       const uint32_t j0 = 8u * (sl + 8u * k);
+      if (j0 >= v) break;
       int4 w;
       if constexpr (STORE_E)
         w = xw[k];
