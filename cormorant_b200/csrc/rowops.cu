@@ -551,6 +551,24 @@ __global__ void __launch_bounds__(256, 2) ro_norm16(RoArgs q) {
 // (checked per CTA over the block: ADDX |x| << sa, |y| << sb, Bq' << bq_sh,
 // no SCALE; MULACT sa <= 23, so |g << sa| < 2^38 and every product < 2^62),
 // else in 128 bits.
+// word g of a streaming job -> (8-element word w of its row, i1, i2): 32-bit
+// divisions when the job has fewer than 2^32 words (a 64-bit division costs
+// several times more, and these kernels are bound by their arithmetic)
+__device__ __forceinline__ void ro_index(uint64_t g, uint32_t per, uint32_t c1, bool small, uint32_t& w, uint32_t& i1,
+                                         uint32_t& i2) {
+  if (small) {
+    const uint32_t g32 = (uint32_t)g, row = g32 / per;
+    w = g32 - row * per;
+    i2 = row / c1;
+    i1 = row - i2 * c1;
+  } else {
+    const uint64_t row = g / per;
+    w = (uint32_t)(g - row * per);
+    i1 = (uint32_t)(row % c1);
+    i2 = (uint32_t)(row / c1);
+  }
+}
+
 template <int N_>
 __device__ __forceinline__ void ld8(const uint8_t* p, int kind, int64_t (&v)[N_]) {
   if (kind == 0) {
@@ -602,10 +620,10 @@ __global__ void __launch_bounds__(256) ro_stream_any(RoArgs q) {
                               : (!scale && abits + s_max_sa <= 60 && bbits + s_max_sb <= 60 && 21 + (int)q.bq_sh <= 60);
   const uint32_t per = q.n >> 3;
   const uint64_t total = (uint64_t)q.c1 * q.c2 * per;
+  const bool small = total < (1ull << 32);
   for (uint64_t gi = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; gi < total; gi += (uint64_t)gridDim.x * blockDim.x) {
-    const uint64_t row = gi / per;
-    const uint32_t w = (uint32_t)(gi - row * per);
-    const uint32_t i1 = (uint32_t)(row % q.c1), i2 = (uint32_t)(row / q.c1);
+    uint32_t w, i1, i2;
+    ro_index(gi, per, q.c1, small, w, i1, i2);
     int64_t x[8], y[8], r[8];
     const bool zero_a = CODE != 4 && (i1 < q.win_lo || i1 >= q.win_hi);
     if (zero_a) {
@@ -709,10 +727,10 @@ __global__ void __launch_bounds__(256) ro_rope_fast(RoArgs q) {
   const uint32_t HD = q.aux & 0xFFFu, half = HD / 2u;
   const uint32_t per = q.n >> 3;
   const uint64_t total = (uint64_t)q.c1 * q.c2 * per;
+  const bool small = total < (1ull << 32);
   for (uint64_t gi = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; gi < total; gi += (uint64_t)gridDim.x * blockDim.x) {
-    const uint64_t row = gi / per;
-    const uint32_t w = (uint32_t)(gi - row * per);
-    const uint32_t i1 = (uint32_t)(row % q.c1), i2 = (uint32_t)(row / q.c1);
+    uint32_t w, i1, i2;
+    ro_index(gi, per, q.c1, small, w, i1, i2);
     const uint8_t* ra = q.a + (uint64_t)i2 * q.a_s2 + (uint64_t)i1 * q.a_s1;
     const uint8_t* rb = q.b + (uint64_t)i2 * q.b_s2 + (uint64_t)i1 * q.b_s1;
     const uint32_t c0 = 8u * w, d0 = c0 % HD;
