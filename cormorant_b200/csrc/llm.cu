@@ -264,21 +264,37 @@ __global__ void __launch_bounds__(256) decode_attn_kernel(corm_llm_decode_attn_d
     for (int h = 0; h < G; h++) S[h * span + jj] = kernel_out16((long long)(int32_t)acc[h]);
   }
   __syncthreads();
-  // per head: the max, e in order, the sum left to right (one thread per head), P
-  for (int h = 0; h < G; h++) {
-    int32_t m = INT32_MIN;
-    for (uint32_t jj = tid; jj < span; jj += blockDim.x) m = max(m, (int32_t)S[h * span + jj]);
+  // per head: the max (every head in one pass), e for every head in one loop
+  // (the table lookups of all heads in flight together), the sum left to right
+  // (one thread per head), P
+  {
+    int32_t mh[G];
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) m = max(m, __shfl_xor_sync(0xffffffffu, m, o));
-    if (lane == 0) s_max[h & 7][warp] = m;
-    __syncthreads();
-    m = s_max[h & 7][0];
-    for (int w = 1; w < (int)(blockDim.x >> 5); w++) m = max(m, s_max[h & 7][w]);
-    const double* tab = d.tab + (uint64_t)(g * G + h) * 65536u;
-#pragma unroll 4
-    for (uint32_t jj = tid; jj < span; jj += blockDim.x) e[h * span + jj] = __ldg(tab + (m - (int32_t)S[h * span + jj]));
-    __syncthreads();
+    for (int h = 0; h < G; h++) mh[h] = INT32_MIN;
+    for (uint32_t jj = tid; jj < span; jj += blockDim.x)
+#pragma unroll
+      for (int h = 0; h < G; h++) mh[h] = max(mh[h], (int32_t)S[h * span + jj]);
+#pragma unroll
+    for (int h = 0; h < G; h++) {
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) mh[h] = max(mh[h], __shfl_xor_sync(0xffffffffu, mh[h], o));
+      if (lane == 0) s_max[h][warp] = mh[h];
+    }
   }
+  __syncthreads();
+  if (tid < G) {
+    int32_t m = s_max[tid][0];
+    for (int w = 1; w < (int)(blockDim.x >> 5); w++) m = max(m, s_max[tid][w]);
+    s_max[tid][0] = m;
+  }
+  __syncthreads();
+#pragma unroll 4
+  for (uint32_t i = tid; i < (uint32_t)G * span; i += blockDim.x) {
+    const uint32_t h = i / span;
+    const double* tab = d.tab + (uint64_t)(g * G + h) * 65536u;
+    e[i] = __ldg(tab + (s_max[h][0] - (int32_t)S[i]));
+  }
+  __syncthreads();
   if (tid < G) {
     double sum = 0.0;
 #pragma unroll 8
