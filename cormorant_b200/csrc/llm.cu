@@ -96,18 +96,33 @@ extern "C" int corm_llm_attn_softmax(const corm_llm_smx_desc* d, corm_stream_t s
 // then the row copy.
 namespace {
 
-__global__ void __launch_bounds__(256) greedy_embed_kernel(corm_greedy_desc d) {
+__global__ void __launch_bounds__(1024) greedy_embed_kernel(corm_greedy_desc d) {
   corm_pdl_wait();
   corm_pdl_trigger();
-  __shared__ int32_t s_v[8];
-  __shared__ uint32_t s_i[8];
+  __shared__ int32_t s_v[32];
+  __shared__ uint32_t s_i[32];
   const uint32_t b = blockIdx.x;
   const int16_t* lg = d.logits + (uint64_t)b * d.ld;
   int32_t best = INT32_MIN;
   uint32_t bi = 0xFFFFFFFFu;
-  for (uint32_t j = threadIdx.x; j < d.vocab; j += blockDim.x) {
+  // 8 logits per 16-byte load where the row is aligned, the rest one by one;
+  // indices ascend per thread, so keeping only a strictly larger value keeps
+  // the first index of a tie
+  const uint32_t nv = ((uintptr_t)lg & 15u) ? 0u : d.vocab / 8u;
+#pragma unroll 4
+  for (uint32_t w = threadIdx.x; w < nv; w += blockDim.x) {
+    const int4 x = __ldg((const int4*)lg + w);
+    const int16_t* x8 = (const int16_t*)&x;
+#pragma unroll
+    for (int e = 0; e < 8; e++)
+      if ((int32_t)x8[e] > best) {
+        best = x8[e];
+        bi = 8u * w + e;
+      }
+  }
+  for (uint32_t j = 8u * nv + threadIdx.x; j < d.vocab; j += blockDim.x) {
     const int32_t v = lg[j];
-    if (v > best) {  // j ascends per thread: the first index of a tie stays
+    if (v > best || (v == best && j < bi)) {
       best = v;
       bi = j;
     }
@@ -150,7 +165,7 @@ extern "C" int corm_greedy_embed(const corm_greedy_desc* d, corm_stream_t stream
   cudaStream_t st = (cudaStream_t)stream;
   {
     corm::ProfScope prof_("greedy_embed_kernel", st);
-    corm_launch_pdl(greedy_embed_kernel, dim3(d->batch), dim3(256), 0, st, *d);
+    corm_launch_pdl(greedy_embed_kernel, dim3(d->batch), dim3(1024), 0, st, *d);
   }
   return corm::cuda_status("greedy_embed");
 }
