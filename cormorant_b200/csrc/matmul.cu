@@ -148,16 +148,23 @@ __global__ void __launch_bounds__(128) mm_gemv_kernel(MmArgs p, uint32_t kchunk,
   }
 }
 
-// the K ranges' int64 sums added in range order (exact: integer addition)
+// the K ranges' int64 sums added (exact integer addition, so in any order):
+// a warp per output, its lanes taking every 32nd range (up to 128 ranges
+// would otherwise be a long chain of loads for one thread)
 __global__ void mm_small_finish(MmArgs p, const unsigned long long* partial, uint32_t ks) {
   corm_pdl_wait();
   corm_pdl_trigger();
   const uint64_t total = (uint64_t)p.batch * p.n * p.m;
-  for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (uint64_t)gridDim.x * blockDim.x) {
+  const uint32_t lane = threadIdx.x & 31u;
+  const uint64_t nwarps = ((uint64_t)gridDim.x * blockDim.x) >> 5;
+  for (uint64_t i = ((uint64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; i < total; i += nwarps) {
+    unsigned long long acc = 0;
+    for (uint32_t z = lane; z < ks; z += 32u) acc += __ldg(partial + z * total + i);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+    if (lane != 0) continue;
     const uint64_t bt = i / ((uint64_t)p.n * p.m), rem = i - bt * p.n * p.m;
     const uint64_t off = bt * p.c_bs + rem;
-    unsigned long long acc = 0;
-    for (uint32_t z = 0; z < ks; z++) acc += __ldg(partial + z * total + i);
     int16_t y = mm_finish((int64_t)acc, p.flags);
     if (p.post.op != corm::kPostNone) y = corm::post_apply(p.post, y, corm::post_b(p.post, off, (uint32_t)(rem % p.m)));
     p.c[off] = y;
@@ -342,8 +349,8 @@ int matmul_impl(const corm_matmul_desc* d, const corm::PostOp& post, cudaStream_
     if (partial) {
       {
         corm::ProfScope prof_("mm_small_finish", st);
-        corm_launch_pdl(mm_small_finish, dim3(corm_blocks((uint64_t)d->batch * d->n * d->m, 256)), dim3(256), 0, st, p,
-                        (const unsigned long long*)partial, pl.ksplit);
+        corm_launch_pdl(mm_small_finish, dim3(corm_blocks((uint64_t)d->batch * d->n * d->m * 32u, 256)), dim3(256), 0,
+                        st, p, (const unsigned long long*)partial, pl.ksplit);
       }
       return corm::cuda_status("matmul small finish");
     }
@@ -435,8 +442,8 @@ extern "C" int corm_matmul_noalloc(const corm_matmul_desc* d, corm_stream_t stre
     if (partial) {
       {
         corm::ProfScope prof_("mm_small_finish", st);
-        corm_launch_pdl(mm_small_finish, dim3(corm_blocks((uint64_t)d->batch * d->n * d->m, 256)), dim3(256), 0, st, p,
-                        (const unsigned long long*)partial, pl.ksplit);
+        corm_launch_pdl(mm_small_finish, dim3(corm_blocks((uint64_t)d->batch * d->n * d->m * 32u, 256)), dim3(256), 0,
+                        st, p, (const unsigned long long*)partial, pl.ksplit);
       }
       return corm::cuda_status("matmul_noalloc small finish");
     }
