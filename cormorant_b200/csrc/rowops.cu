@@ -435,15 +435,19 @@ __global__ void __launch_bounds__(256, 2) ro_norm16(RoArgs q) {
   __shared__ int s_scmin;
   if (threadIdx.x == 0) s_scmin = 63;
   __syncthreads();
+  int scmin = 63;  // per thread, then one shared atomic per warp
   for (uint32_t c = threadIdx.x; c < npar; c += blockDim.x) {
     const int4 e = *(const int4*)(q.p + 16ull * c);
     const uint32_t slot = bcast ? 0u : (c % EPW) * words + c / EPW;
-    atomicMin(&s_scmin, (int)(((uint32_t)e.z >> 16) & 63u));
+    scmin = min(scmin, (int)(((uint32_t)e.z >> 16) & 63u));
     s_g[slot] = e.x;
     const int64_t bq = (int32_t)((uint32_t)e.y << 10) >> 10;  // int22, sign-extended
     s_bq[slot] = q.bq_sh <= 40u ? bq << q.bq_sh : 0;       // (the 128-bit path shifts itself)
     s_sc[slot] = (uint8_t)(((uint32_t)e.z >> 16) & 63u);
   }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) scmin = min(scmin, __shfl_xor_sync(0xffffffffu, scmin, o));
+  if ((threadIdx.x & 31) == 0) atomicMin(&s_scmin, scmin);
   __syncthreads();
   const bool small_bq = q.bq_sh <= 40u;
   const int lane = threadIdx.x & 31;
@@ -604,6 +608,7 @@ __global__ void __launch_bounds__(256) ro_stream_any(RoArgs q) {
   __shared__ int s_max_sa, s_max_sb;
   if (threadIdx.x == 0) s_max_sa = s_max_sb = 0;
   __syncthreads();
+  int msa = 0, msb = 0;  // per thread, then one shared atomic per warp
   for (uint32_t c = threadIdx.x; c < npar; c += blockDim.x) {
     const Param pr = ld_param(q, c);
     s_g[c] = pr.g;
@@ -611,8 +616,17 @@ __global__ void __launch_bounds__(256) ro_stream_any(RoArgs q) {
     s_sa[c] = (uint8_t)pr.sa;
     s_sb[c] = (uint8_t)pr.sb;
     s_sc[c] = (uint8_t)pr.sc;
-    atomicMax(&s_max_sa, (int)pr.sa);
-    atomicMax(&s_max_sb, (int)pr.sb);
+    msa = max(msa, (int)pr.sa);
+    msb = max(msb, (int)pr.sb);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    msa = max(msa, __shfl_xor_sync(0xffffffffu, msa, o));
+    msb = max(msb, __shfl_xor_sync(0xffffffffu, msb, o));
+  }
+  if ((threadIdx.x & 31) == 0) {
+    atomicMax(&s_max_sa, msa);
+    atomicMax(&s_max_sb, msb);
   }
   __syncthreads();
   const int abits = AK ? 31 : 15, bbits = BK ? 31 : 15;
