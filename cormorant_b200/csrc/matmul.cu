@@ -84,8 +84,7 @@ __global__ void __launch_bounds__(256) split_b_gather_kernel(MmArgs p, uint32_t 
 // 8 per lane, one 16-byte load per B row — over a K range, A values read as
 // warp-wide broadcasts, int64 sums; the K range is split across CTAs when the
 // grid alone would not fill the GPU, each range's sums stored in its own
-// int64 slot (no memset, no atomics) and added in range order by
-// mm_small_finish.
+// int64 slot (no memset, no atomics) and added by mm_small_finish.
 template <int NR>
 __global__ void __launch_bounds__(128) mm_gemv_kernel(MmArgs p, uint32_t kchunk, unsigned long long* partial) {
   corm_pdl_wait();
