@@ -137,3 +137,24 @@ def test_gpu_llama_decode_heads_vs_oracle(dims):
     from cormorant_b200.llm_runner import LlamaRunner
     m = WL.LlamaModel(seed=21, batch=3, seq=16, layers=1, vocab=300, **dims)
     _decode_vs_oracle(LlamaRunner(m), m, 3)
+
+
+def test_sibling_groups_host_logic():
+    """Which MatMuls the simulator runs as one column-group launch: per Llama
+    layer q / k / v and gate / up (same A, constant weights, widths in runs of
+    32); none in BERT, whose projections carry a fused bias job; none at two
+    rows or fewer (the GEMV path); none with fusion off."""
+    from cormorant_b200 import workloads as WL
+    from cormorant_b200.simulator import GpuSimulator
+    m = WL.LlamaModel(seed=3, batch=3, seq=16, layers=2, hidden=64, heads=4, kv_heads=2, head_dim=16, ffn=128,
+                      vocab=256)
+    for g in (m.prefill_graph, m.decode_graph):
+        s = GpuSimulator(g, device="cpu")
+        names = sorted(tuple(g.nodes[j].output.onnx_name.split(".")[-1] for j in v) for v in s._groups.values())
+        assert names == [("g", "u")] * 2 + [("q0", "k0", "v")] * 2
+        assert not GpuSimulator(g, fuse=False, device="cpu")._groups
+    bert = WL.bert_base(seed=4, batch=1, seq=32, layers=1)[0]
+    assert not GpuSimulator(bert, device="cpu")._groups
+    m1 = WL.LlamaModel(seed=3, batch=2, seq=16, layers=1, hidden=64, heads=4, kv_heads=2, head_dim=16, ffn=128,
+                       vocab=256)
+    assert not GpuSimulator(m1.decode_graph, device="cpu")._groups  # 2 rows: the GEMV path
