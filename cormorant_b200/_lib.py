@@ -17,7 +17,7 @@ F_WRAP32, F_WEIGHT_LOGICAL, F_ACT_RELU, F_ACT_RELU6 = 0x1, 0x2, 0x4, 0x8
 
 # every symbol include/cormorant_b200.h declares
 EXPORTS = ("corm_vectorop", "corm_matmul_workspace_size", "corm_matmul", "corm_matmul_noalloc", "corm_conv_workspace_size", "corm_conv",
-           "corm_matmul_post", "corm_matmul_groups", "corm_conv_post", "corm_gemm_strided_workspace_size", "corm_gemm_strided",
+           "corm_matmul_post", "corm_matmul_groups", "corm_split_b_planes", "corm_matmul_bplanes", "corm_conv_post", "corm_gemm_strided_workspace_size", "corm_gemm_strided",
            "corm_copy_nd", "corm_llm_attn_softmax", "corm_greedy_embed",
            "corm_llm_decode_attn", "corm_rowops_chain", "corm_rowops_chain_dev",
            "corm_stream_done",
@@ -138,6 +138,10 @@ def lib() -> C.CDLL:
                        ("corm_matmul", [C.POINTER(MatmulDesc), C.c_void_p]),
                        ("corm_matmul_noalloc", [C.POINTER(MatmulDesc), C.c_void_p]),
                        ("corm_matmul_groups", [C.POINTER(MatmulDesc), C.POINTER(OutGroups), C.c_void_p]),
+                       ("corm_split_b_planes", [C.c_void_p, C.c_uint32, C.c_uint32, C.c_void_p, C.c_void_p,
+                                                C.c_void_p]),
+                       ("corm_matmul_bplanes", [C.POINTER(MatmulDesc), C.c_void_p, C.c_void_p, C.POINTER(OutGroups),
+                                                C.c_void_p]),
                        ("corm_matmul_workspace_size", [C.POINTER(MatmulDesc), C.POINTER(C.c_size_t)]),
                        ("corm_conv", [C.POINTER(ConvDesc), C.c_void_p]),
                        ("corm_conv_workspace_size", [C.POINTER(ConvDesc), C.POINTER(C.c_size_t)]),

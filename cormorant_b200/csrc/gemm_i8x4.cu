@@ -74,6 +74,7 @@ struct EpiArgs {
   int64_t gbase[4];
   uint32_t gc[5], gw[4];
   uint32_t raw_tma;  // int16 operands: raw tiles by TMA (map_ahi: A, map_bhi: B) into the stage
+  uint32_t b_tma_planes;  // with raw_tma: B from its split planes (map_bhi / map_blo), only A split here
   uint32_t a_box_rows, b_pitch;  // raw boxes: A rows (<= 128) and the B row's bytes (<= 256)
 };
 
@@ -461,6 +462,7 @@ __global__ void __launch_bounds__(Roles<CONV>::threads, 1)
     // unswizzled, over the B planes), zero-filled beyond the job
     sm100::prefetch_tmap(&map_ahi);
     sm100::prefetch_tmap(&map_bhi);
+    if (ep.b_tma_planes) sm100::prefetch_tmap(&map_blo);
     uint32_t g = 0;
     bool ok = true;
     for (uint32_t u = blockIdx.x; u < units && ok; u += gridDim.x) {
@@ -473,11 +475,18 @@ __global__ void __launch_bounds__(Roles<CONV>::threads, 1)
           break;
         }
         uint8_t* st = smem + s * STAGE_BYTES;
-        sm100::mbar_expect_tx(&raw_full[s], ep.a_box_rows * 256u + BK * ep.b_pitch);
         const int x = (int)(kb * BK);
+        if (ep.b_tma_planes) {  // B split beforehand: its hi / lo planes as the plane path loads them
+          sm100::mbar_expect_tx(&raw_full[s], ep.a_box_rows * 256u + 2 * TILE_BYTES);
+          const int bp_z = ep.b_planes == 1 ? 0 : (int)w.bz;
+          sm100::tma_load_3d(st + 2 * TILE_BYTES, &map_bhi, &raw_full[s], (int)w.tile_c, x, bp_z);
+          sm100::tma_load_3d(st + 3 * TILE_BYTES, &map_blo, &raw_full[s], (int)w.tile_c, x, bp_z);
+        } else {
+          sm100::mbar_expect_tx(&raw_full[s], ep.a_box_rows * 256u + BK * ep.b_pitch);
+          sm100::tma_load_3d(st + 2 * TILE_BYTES, &map_bhi, &raw_full[s], (int)w.tile_c, x, b_z);
+        }
         sm100::tma_load_3d(st, &map_ahi, &raw_full[s], x, (int)w.tile_r, a_z);
         sm100::tma_load_3d(st + ep.a_box_rows * 128u, &map_ahi, &raw_full[s], x + 64, (int)w.tile_r, a_z);
-        sm100::tma_load_3d(st + 2 * TILE_BYTES, &map_bhi, &raw_full[s], (int)w.tile_c, x, b_z);
       }
     }
     // the loads issued land before the CTA's shared memory goes away
@@ -533,6 +542,20 @@ __global__ void __launch_bounds__(Roles<CONV>::threads, 1)
           const uint32_t ta = tmem + ((aq * 32u) << 16) + A_TMEM + 64u * (g & 1u) + 16u * ahk;
           sm100::tmem_st16(ta, hi);
           sm100::tmem_st16(ta + 32u, lo);
+        }
+        if (ep.b_tma_planes) {
+          // B came split: no shared-memory writes here, so no barrier between
+          // the warps; a warp whose wait ran out stops as a whole (the MMA
+          // warp's bounded wait on this stage then runs out too)
+          if (!__all_sync(0xffffffffu, okw)) {
+            stop = true;
+            break;
+          }
+          sm100::tmem_st_wait();
+          sm100::tc_fence_before();
+          __syncwarp();
+          if (lane == 0) sm100::mbar_arrive(&full[s]);
+          continue;
         }
         int4 vb[8];
         const uint8_t* rb = st + 2 * TILE_BYTES + row0 * ep.b_pitch + c * 16u;
@@ -985,9 +1008,19 @@ int gemm_i8x4(const GemmJob& j, cudaStream_t stream) {
   if (!err) return fail(CORM_ECUDA, "gemm: error word allocation failed");
   CUtensorMap m_ahi, m_alo, m_bhi, m_blo;
   const bool conv = j.a16 != nullptr;  // int16 operands split inside the kernel
+  const bool b_planes_in = conv && j.b16 == nullptr;  // A split here, B from its planes
   bool raw_tma = false;
   uint32_t a_box_rows = BM, b_box_cols = BN;
-  if (conv) {
+  if (b_planes_in) {
+    if ((uintptr_t)j.a16 & 15u || j.lda % 8u || j.a_bs16 % 8u || j.K % 8u || !j.b_hi || !j.b_lo)
+      return fail(CORM_EINVAL, "gemm: int16 A not on 16-byte rows, or no B planes");
+    memset(&m_alo, 0, sizeof m_alo);
+    a_box_rows = j.rows < (uint32_t)BM ? (j.rows + 7u) & ~7u : (uint32_t)BM;
+    if (!make_raw_map(&m_ahi, j.a16, j.K, j.rows, j.lda, j.a_bs16 ? j.batch : 1, j.a_bs16, BK / 2, a_box_rows, true) ||
+        !make_map(&m_bhi, j.b_hi, j.cols_p, j.K, j.b_planes) || !make_map(&m_blo, j.b_lo, j.cols_p, j.K, j.b_planes))
+      return fail(CORM_ECUDA, "gemm: cuTensorMapEncodeTiled failed");
+    raw_tma = true;
+  } else if (conv) {
     if (((uintptr_t)j.a16 | (uintptr_t)j.b16) & 15u || j.lda % 8u || j.ldb % 8u || j.a_bs16 % 8u || j.b_bs16 % 8u ||
         j.K % 8u || j.cols % 8u)
       return fail(CORM_EINVAL, "gemm: int16 operands not on 16-byte rows");
@@ -1073,6 +1106,7 @@ int gemm_i8x4(const GemmJob& j, cudaStream_t stream) {
   ep.partial = nullptr;
   ep.err = err;
   ep.raw_tma = raw_tma ? 1u : 0u;
+  ep.b_tma_planes = b_planes_in ? 1u : 0u;
   ep.a_box_rows = a_box_rows;
   ep.b_pitch = b_box_cols * 2u;
   if (sp.splits > 1) {

@@ -42,7 +42,9 @@ struct GemmJob {
   PostOp post;              // fused VectorOP job on the result (op kPostNone: none)
   // int16 operands split inside the kernel instead of the planes above (a16 != nullptr):
   // A [batch][rows][lda] K-major, B [batch][K][ldb] MN-major (b_mn implied), batch
-  // strides in elements (0: shared), 16-byte aligned rows, K and cols multiples of 8
+  // strides in elements (0: shared), 16-byte aligned rows, K and cols multiples of 8.
+  // a16 with b16 == nullptr: A split inside the kernel, B from the MN-major planes
+  // b_hi / b_lo above (b_mn = 1, cols_p)
   const int16_t* a16;
   const int16_t* b16;
   uint64_t a_bs16, b_bs16;

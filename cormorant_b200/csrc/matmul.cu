@@ -479,3 +479,67 @@ extern "C" int corm_matmul_groups(const corm_matmul_desc* d, const corm_out_grou
   }
   return tensor_path(&dd, p, pl, (uint8_t*)ws, corm::PostOp{}, nullptr, st, g);
 }
+
+// ---------------------------------------------------------------- constant weights split once
+// corm_split_b_planes / corm_matmul_bplanes: a weight that many jobs read is
+// split into its int8 hi / lo planes once; the GEMM then loads the planes by
+// TMA and splits only A (into tensor memory) — for few rows, where splitting
+// the weight inside every job is the GEMM's largest cost.
+extern "C" int corm_split_b_planes(const int16_t* b, uint32_t k, uint32_t m, int8_t* hi, uint8_t* lo,
+                                   corm_stream_t stream) {
+  if (int rc = corm::check_device()) return rc;
+  if (!b || !hi || !lo || k == 0 || m == 0) return corm::fail(CORM_EINVAL, "corm_split_b_planes: null buffer or empty");
+  const uint32_t mp = (m + 15u) / 16u * 16u;
+  return corm::split_planes(b, 0, 1, k, m, m, mp, hi, lo, (cudaStream_t)stream);
+}
+
+extern "C" int corm_matmul_bplanes(const corm_matmul_desc* d, const int8_t* b_hi, const uint8_t* b_lo,
+                                   const corm_out_groups* g, corm_stream_t stream) {
+  if (int rc = validate(d)) return rc;
+  if (int rc = corm::check_device()) return rc;
+  if (!d->a || !b_hi || !b_lo || (!g && !d->c)) return corm::fail(CORM_EINVAL, "corm_matmul_bplanes: null operand");
+  if (g && (g->count < 1 || g->count > 4)) return corm::fail(CORM_EINVAL, "corm_matmul_bplanes: 1..4 output groups");
+  if (d->n <= kSmallRows || d->k == 0 || d->k % 8u || ((uintptr_t)d->a & 15u) ||
+      (d->batch > 1 && (d->a_batch_stride % 8u || d->b_batch_stride != 0)) || d->b_packed || d->gemv_kw > 1)
+    return corm::fail(CORM_EINVAL,
+                      "corm_matmul_bplanes: n %u, k %u (n > %u, k a multiple of 8, A on 16-byte rows, one B for "
+                      "every batch, row-major)", d->n, d->k, kSmallRows);
+  if (d->m == 0 || d->batch == 0) return CORM_OK;
+  cudaStream_t st = (cudaStream_t)stream;
+  corm::GemmJob j{};
+  j.rows = d->n;
+  j.cols = d->m;
+  j.Kp = (d->k + 15u) / 16u * 16u;
+  j.batch = d->batch;
+  j.a_planes = d->batch;
+  j.b_planes = 1;
+  j.b_mn = 1;
+  j.K = d->k;
+  j.cols_p = (d->m + 15u) / 16u * 16u;
+  j.mode = 0;
+  j.out = g ? g->out[0] : d->c;
+  j.out_batch_stride = d->c_batch_stride;
+  j.ldc = d->m;
+  j.flags = d->flags;
+  j.a16 = d->a;
+  j.a_bs16 = d->batch == 1 ? 0 : d->a_batch_stride;
+  j.lda = d->k;
+  j.b_hi = b_hi;
+  j.b_lo = b_lo;
+  if (g) {
+    j.ngroups = g->count;
+    for (uint32_t q = 0; q < g->count; q++) {
+      j.gout[q] = g->out[q];
+      j.gw[q] = g->width[q];
+    }
+  }
+  const size_t pb = corm::gemm_partial_bytes(j.rows, j.cols, j.Kp, j.batch);
+  if (pb) {
+    void* ws = d->workspace;
+    if (ws && d->workspace_bytes < pb)
+      return corm::fail(CORM_ENOMEM, "corm_matmul_bplanes: workspace %zu < %zu bytes", d->workspace_bytes, pb);
+    if (!ws && !(ws = corm::scratch(pb, st))) return CORM_ENOMEM;
+    j.partial = ws;
+  }
+  return corm::gemm_i8x4(j, st);
+}

@@ -121,6 +121,43 @@ def matmul_groups(a, b, outs, widths, *, n, k, batch=1, a_batch_stride=0, b_batc
     return workspace
 
 
+def split_b_planes(b, *, k, m):
+    """corm_split_b_planes: the int8 hi / lo planes (MN-major [k][mp], mp = m
+    rounded up to 16) of a constant row-major int16 weight [k][m], for
+    matmul_bplanes."""
+    _i16(b, "b")
+    st = _ready()
+    mp = (m + 15) // 16 * 16
+    hi = torch.empty(k * mp, dtype=torch.int8, device=b.device)
+    lo = torch.empty(k * mp, dtype=torch.uint8, device=b.device)
+    check(lib().corm_split_b_planes(_ptr(b), k, m, _ptr(hi), _ptr(lo), st))
+    return hi, lo
+
+
+def matmul_bplanes(a, planes, c, *, n, k, m, batch=1, a_batch_stride=0, c_batch_stride=0, flags=0, workspace=None,
+                   outs=None, widths=None):
+    """A MatMul job against a weight given as its planes (split_b_planes):
+    the GEMM splits only A.  ``outs`` / ``widths``: output column groups
+    instead of c (as matmul_groups)."""
+    _i16(a, "a")
+    st = _ready()
+    d = _lib.MatmulDesc(_ptr(a), None, _ptr(c) if c is not None else None, n, k, m, batch, a_batch_stride, 0,
+                        c_batch_stride, 0, 0, flags, None, 0)
+    need = C.c_size_t(0)
+    check(lib().corm_matmul_workspace_size(C.byref(d), C.byref(need)))
+    if need.value:
+        if workspace is None:
+            workspace = torch.empty(need.value, dtype=torch.uint8, device=a.device)
+        d.workspace, d.workspace_bytes = _ptr(workspace), workspace.numel() * workspace.element_size()
+    g = None
+    if outs is not None:
+        g = _lib.OutGroups(len(outs), (C.c_uint32 * 4)(*(list(widths) + [0] * (4 - len(widths)))),
+                           (C.c_void_p * 4)(*([_ptr(t) for t in outs] + [None] * (4 - len(outs)))))
+    check(lib().corm_matmul_bplanes(C.byref(d), _ptr(planes[0]), _ptr(planes[1]), C.byref(g) if g is not None else None,
+                                    st))
+    return workspace
+
+
 def gemm_strided(a, b, c, *, n, k, m, batch=1, lda=None, ldb=None, ldc=None, b_trans=False, a_batch_stride=0,
                  b_batch_stride=0, c_batch_stride=0, flags=0, workspace=None):
     """A strided batch of MatMul jobs (corm_gemm_strided): element row strides

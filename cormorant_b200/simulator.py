@@ -456,6 +456,12 @@ class GpuSimulator:
             d -= 1
         a_bs = n * k if inner > 1 else 0
         b_bs = k * m if inner > 1 else 0
+        if (len(bsh) == 2 and len(sn.inputs[1].shape) == 2 and getattr(B, "data", None) is not None and post is None
+                and total == 1 and self._use_bplanes(n, k) and (a.data_ptr() % 16) == 0):
+            ws = self._workspace(self._mm_ws(n, k, m, 1, 0, 0))
+            ops.matmul_bplanes(a, self._planes(B.onnx_name, b, k, m), y, n=n, k=k, m=m, c_batch_stride=n * m,
+                               flags=wrap | flag, workspace=ws)
+            return y
         for o in range(total // inner):
             idx = np.unravel_index(o * inner, lead) if L else ()
             ao = sum((0 if lead_a[q] == 1 else int(idx[q])) * int(a_strides[q]) for q in range(L)) * n * k
@@ -519,8 +525,26 @@ class GpuSimulator:
         ys = [self._alloc(sn.output.numel) for sn in sns]
         wrap = F_WRAP32 if _has_exp(A, sns[0].inputs[1], sns[0].output) else 0
         ws = self._workspace(self._mm_ws(n, k, m, 1, 0, 0))
-        ops.matmul_groups(get(A), self._weights[key], ys, widths, n=n, k=k, flags=wrap, workspace=ws)
+        if self._use_bplanes(n, k):
+            ops.matmul_bplanes(get(A), self._planes(key, self._weights[key], k, m), None, n=n, k=k, m=m, flags=wrap,
+                               workspace=ws, outs=ys, widths=widths)
+        else:
+            ops.matmul_groups(get(A), self._weights[key], ys, widths, n=n, k=k, flags=wrap, workspace=ws)
         return ys
+
+    # few rows against a constant weight: the weight split into its planes once
+    # (cached beside it) and only A split inside each job
+    BPLANES_MAX_ROWS = 256
+
+    @classmethod
+    def _use_bplanes(cls, n, k) -> bool:
+        return 2 < n <= cls.BPLANES_MAX_ROWS and k % 8 == 0
+
+    def _planes(self, key, w, k, m):
+        pk = ("planes",) + (key if isinstance(key, tuple) else (key,))
+        if pk not in self._weights:
+            self._weights[pk] = ops.split_b_planes(w, k=k, m=m)
+        return self._weights[pk]
 
     @staticmethod
     def _mm_ws(n, k, m, batch, a_bs, b_bs) -> int:

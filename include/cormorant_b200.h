@@ -167,6 +167,20 @@ typedef struct {
   int16_t* out[4];
 } corm_out_groups;
 int corm_matmul_groups(const corm_matmul_desc* d, const corm_out_groups* g, corm_stream_t stream);
+
+/* Constant weights split once (no counterpart in the reference): a row-major
+ * int16 B [k][m] becomes its int8 hi / lo planes, MN-major [k][mp] with mp =
+ * m rounded up to 16 (k * mp bytes each, the padding columns zero). */
+int corm_split_b_planes(const int16_t* b, uint32_t k, uint32_t m, int8_t* hi, uint8_t* lo, corm_stream_t stream);
+/* The MatMul job of d with B given as those planes (d->b ignored; one B for
+ * every batch): the GEMM loads the planes and splits only A, inside the
+ * kernel (A on 16-byte rows, k a multiple of 8, n > 2).  g: output column
+ * groups as corm_matmul_groups, or NULL for d->c.  The result equals
+ * corm_matmul's.  For few rows against a weight read by many jobs (a decode
+ * step's projections), where splitting the weight in every job costs most.
+ * Workspace: corm_matmul_workspace_size of d suffices. */
+int corm_matmul_bplanes(const corm_matmul_desc* d, const int8_t* b_hi, const uint8_t* b_lo, const corm_out_groups* g,
+                        corm_stream_t stream);
 int corm_conv_post(const corm_conv_desc* d, const corm_postop* post, corm_stream_t stream);
 
 /* ---------------------------------------------------------------- strided batches

@@ -37,7 +37,7 @@ def cpu_ops(monkeypatch):
     import torch
 
     from cormorant_b200 import ops
-    from cormorant_b200._lib import F_WRAP32
+    from cormorant_b200._lib import F_ACT_RELU, F_ACT_RELU6, F_WRAP32
     from cormorant_b200.simulator import GpuSimulator
     from oracle import spec
 
@@ -79,6 +79,26 @@ def cpu_ops(monkeypatch):
         m = sum(widths)
         y = spec.matmul_raw(np16(a)[:n * k].astype(np.int64).reshape(n, k), np16(b)[:k * m].astype(np.int64).reshape(k, m),
                             wrap=bool(flags & F_WRAP32))
+        c0 = 0
+        for o, w in zip(outs, widths):
+            np16(o)[:n * w] = y[:, c0:c0 + w].reshape(-1)
+            c0 += w
+
+    def split_b_planes(b, *, k, m):
+        return (b, None)  # the fake keeps the int16 weight itself
+
+    def matmul_bplanes(a, planes, c, *, n, k, m, batch=1, a_batch_stride=0, c_batch_stride=0, flags=0,
+                       workspace=None, outs=None, widths=None):
+        assert batch == 1
+        y = spec.matmul_raw(np16(a)[:n * k].astype(np.int64).reshape(n, k),
+                            np16(planes[0])[:k * m].astype(np.int64).reshape(k, m), wrap=bool(flags & F_WRAP32))
+        if flags & (F_ACT_RELU | F_ACT_RELU6):  # a fused ReLU / Clip(0,6)
+            y = np.maximum(y, 0)
+            if flags & F_ACT_RELU6:
+                y = np.minimum(y, 1536)
+        if outs is None:
+            np16(c)[:n * m] = y.reshape(-1)
+            return
         c0 = 0
         for o, w in zip(outs, widths):
             np16(o)[:n * w] = y[:, c0:c0 + w].reshape(-1)
@@ -216,6 +236,8 @@ def cpu_ops(monkeypatch):
     monkeypatch.setattr(ops, "rowops", rowops)
     monkeypatch.setattr(ops, "matmul", matmul)
     monkeypatch.setattr(ops, "matmul_groups", matmul_groups)
+    monkeypatch.setattr(ops, "split_b_planes", split_b_planes)
+    monkeypatch.setattr(ops, "matmul_bplanes", matmul_bplanes)
     monkeypatch.setattr(ops, "vectorop", vectorop)
     monkeypatch.setattr(GpuSimulator, "_mm_ws", staticmethod(lambda *a: 0))
     return GpuSimulator
