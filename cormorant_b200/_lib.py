@@ -16,13 +16,13 @@ CORM_OK, CORM_EINVAL, CORM_ELIMIT, CORM_ECUDA, CORM_ENOMEM, CORM_EDEVICE = 0, -1
 F_WRAP32, F_WEIGHT_LOGICAL, F_ACT_RELU, F_ACT_RELU6 = 0x1, 0x2, 0x4, 0x8
 
 # every symbol include/cormorant_b200.h declares
-EXPORTS = ("corm_vectorop", "corm_matmul_workspace_size", "corm_matmul", "corm_matmul_noalloc", "corm_conv_workspace_size", "corm_conv",
+EXPORTS = ("corm_vectorop", "corm_matmul_workspace_size", "corm_matmul", "corm_matmul_noalloc", "corm_matmul_noalloc_status", "corm_conv_workspace_size", "corm_conv",
            "corm_matmul_post", "corm_matmul_groups", "corm_split_b_planes", "corm_matmul_bplanes", "corm_conv_post", "corm_gemm_strided_workspace_size", "corm_gemm_strided",
            "corm_copy_nd", "corm_llm_attn_softmax", "corm_greedy_embed",
            "corm_llm_decode_attn", "corm_rowops_chain", "corm_rowops_chain_dev",
            "corm_stream_done",
            "corm_pool", "corm_rowops", "corm_act_table", "corm_smx_table", "corm_rowops_table_image",
-           "corm_bind_device", "corm_device_status", "corm_launch_count", "corm_profile_enable",
+           "corm_bind_device", "corm_device_status", "corm_set_wait_limit", "corm_launch_count", "corm_profile_enable",
            "corm_profile_read", "corm_version", "corm_last_error")
 
 
@@ -137,6 +137,8 @@ def lib() -> C.CDLL:
     for name, argt in (("corm_vectorop", [C.POINTER(VectorOpDesc), C.c_void_p]),
                        ("corm_matmul", [C.POINTER(MatmulDesc), C.c_void_p]),
                        ("corm_matmul_noalloc", [C.POINTER(MatmulDesc), C.c_void_p]),
+                       ("corm_matmul_noalloc_status", [C.POINTER(C.c_int), C.c_void_p]),
+                       ("corm_set_wait_limit", [C.c_longlong]),
                        ("corm_matmul_groups", [C.POINTER(MatmulDesc), C.POINTER(OutGroups), C.c_void_p]),
                        ("corm_split_b_planes", [C.c_void_p, C.c_uint32, C.c_uint32, C.c_void_p, C.c_void_p,
                                                 C.c_void_p]),

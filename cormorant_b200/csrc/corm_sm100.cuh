@@ -31,24 +31,56 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
+// Non-blocking probe of the phase (never suspends the thread).
+__device__ __forceinline__ bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Limits below this many cycles are a diagnostic setting: the clock is read on
+// every probe and the probe never suspends, so a wait longer than the limit
+// always runs out.
+constexpr long long kShortWaitLimit = 1ll << 20;
+
 // Wait for the phase of `parity` to complete, giving up after `limit` clock
-// cycles (then *err gets `code` and false is returned).  Every wait of the
+// cycles: then *err gets `code` (the first code wins; the word keeps it until
+// the host reads and clears it), *stop gets 1 and false is returned.  `stop`
+// is a word in the CTA's shared memory: once one role of the CTA has given
+// up, the others' waits return false at their next check instead of running
+// out their own limit.  It is per launch, so a timeout recorded by an earlier
+// launch (still in *err) never cuts a later launch short.  Every wait of the
 // kernels is bounded so that a broken pipeline ends with an error status
 // instead of a hung GPU.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err, int code,
-                                          long long limit = 4000000000ll) {
-  if (mbar_try_wait(bar, parity)) return true;
-  const long long t0 = clock64();
-  for (uint32_t it = 1;; it++) {
+                                          long long limit = 4000000000ll, volatile int* stop = nullptr) {
+  if (limit < kShortWaitLimit) {
+    const long long t0 = clock64();
+    for (;;) {
+      if (mbar_test_wait(bar, parity)) return true;
+      if (stop && *stop) return false;  // another role of this CTA gave up
+      if (clock64() - t0 > limit) break;
+    }
+  } else {
     if (mbar_try_wait(bar, parity)) return true;
-    if ((it & 255u) == 0) {
-      if (clock64() - t0 > limit) {
-        if (err) atomicCAS(err, 0, code);
-        return false;
+    const long long t0 = clock64();
+    for (uint32_t it = 1;; it++) {
+      if (mbar_try_wait(bar, parity)) return true;
+      if ((it & 255u) == 0) {
+        if (clock64() - t0 > limit) break;
+        if (stop && *stop) return false;  // another role of this CTA gave up
       }
-      if (err && *(volatile int*)err) return false;  // another role failed: stop waiting
     }
   }
+  if (err) atomicCAS(err, 0, code);
+  if (stop) *stop = 1;
+  return false;
 }
 
 // ---------------------------------------------------------------- TMA (tiled, no multicast)

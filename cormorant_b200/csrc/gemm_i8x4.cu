@@ -26,6 +26,7 @@
 // and MMAs waited for, TMEM freed).
 #include <cudaTypedefs.h>
 
+#include <atomic>
 #include <cstdlib>
 #include <cstring>
 #include <mutex>
@@ -69,6 +70,7 @@ struct EpiArgs {
   uint32_t ymode;  // the form of the rule (floor_acc)
   uint32_t cvar;   // act (0 none, 1 ReLU, 2 Clip(0,6)) * 2 + conv bias
   int* err;
+  long long wait_limit;  // clock cycles every bounded wait may take (corm_set_wait_limit)
   // mode 2 (column groups): output columns [gc[g], gc[g + 1]) go to their own
   // row-major [batch][rows][gw[g]] buffer at element offset gbase[g] from out
   int64_t gbase[4];
@@ -389,6 +391,7 @@ __global__ void __launch_bounds__(Roles<CONV>::threads, 1)
   uint64_t* a_free = raw_full + STAGES;  // the MMAs reading TMEM A buffer 0 / 1 are done
   uint32_t* tmem_slot = (uint32_t*)(a_free + 2);
   uint32_t* abort_at = tmem_slot + 1;  // first ring step a splitting warp gave up at
+  volatile int* cta_stop = (volatile int*)(abort_at + 1);  // a role of this CTA gave up (bounded waits)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t units = ep.batch * ep.tiles_m * ep.tiles_n * ep.splits;
@@ -404,6 +407,7 @@ __global__ void __launch_bounds__(Roles<CONV>::threads, 1)
       sm100::mbar_init(&a_free[1], 1);
     }
     if (CONV) *abort_at = 0xFFFFFFFFu;
+    *cta_stop = 0;
     sm100::mbar_init(tmem_full, 1);
     sm100::mbar_init(tmem_empty, R::ew);
     sm100::mbar_init(mma_done, 1);
@@ -432,7 +436,7 @@ __global__ void __launch_bounds__(Roles<CONV>::threads, 1)
       const int a_z = ep.a_planes == 1 ? 0 : (int)w.bz, b_z = ep.b_planes == 1 ? 0 : (int)w.bz;
       for (uint32_t kb = w.kb0; kb < w.kb1; kb++, g++) {
         const int s = g % STAGES;
-        if (g >= (uint32_t)STAGES && !sm100::mbar_wait(&empty[s], ((g / STAGES) - 1) & 1, ep.err, 101)) {
+        if (g >= (uint32_t)STAGES && !sm100::mbar_wait(&empty[s], ((g / STAGES) - 1) & 1, ep.err, 101, ep.wait_limit, cta_stop)) {
           ok = false;
           break;
         }
@@ -470,7 +474,7 @@ __global__ void __launch_bounds__(Roles<CONV>::threads, 1)
       const int a_z = ep.a_bs16 ? (int)w.bz : 0, b_z = ep.b_bs16 ? (int)w.bz : 0;
       for (uint32_t kb = w.kb0; kb < w.kb1; kb++, g++) {
         const int s = g % STAGES;
-        if (g >= (uint32_t)STAGES && !sm100::mbar_wait(&empty[s], ((g / STAGES) - 1) & 1, ep.err, 106)) {
+        if (g >= (uint32_t)STAGES && !sm100::mbar_wait(&empty[s], ((g / STAGES) - 1) & 1, ep.err, 106, ep.wait_limit, cta_stop)) {
           ok = false;
           break;
         }
@@ -521,8 +525,8 @@ __global__ void __launch_bounds__(Roles<CONV>::threads, 1)
       const uint32_t nrow = ep.rows - w.tile_r, ncol = ep.cols - w.tile_c;
       for (uint32_t kb = w.kb0; kb < w.kb1; kb++, g++) {
         const int s = g % STAGES;
-        bool okw = sm100::mbar_wait(&raw_full[s], (g / STAGES) & 1, ep.err, 105);
-        if (g >= 2) okw = sm100::mbar_wait(&a_free[g & 1], ((g >> 1) - 1) & 1, ep.err, 109) && okw;
+        bool okw = sm100::mbar_wait(&raw_full[s], (g / STAGES) & 1, ep.err, 105, ep.wait_limit, cta_stop);
+        if (g >= 2) okw = sm100::mbar_wait(&a_free[g & 1], ((g >> 1) - 1) & 1, ep.err, 109, ep.wait_limit, cta_stop) && okw;
         if (!okw) atomicMin(abort_at, g);
         sm100::tc_fence_after();  // the TMEM buffer's readers are done (a_free)
         uint8_t* st = smem + s * STAGE_BYTES;
@@ -603,7 +607,7 @@ __global__ void __launch_bounds__(Roles<CONV>::threads, 1)
       const int16_t* Bb = ep.b16 + (uint64_t)w.bz * ep.b_bs16;
       for (uint32_t kb = w.kb0; kb < w.kb1; kb++, g++) {
         const int s = g % STAGES;
-        if (g >= (uint32_t)STAGES && !sm100::mbar_wait(&empty[s], ((g / STAGES) - 1) & 1, ep.err, 101)) {
+        if (g >= (uint32_t)STAGES && !sm100::mbar_wait(&empty[s], ((g / STAGES) - 1) & 1, ep.err, 101, ep.wait_limit, cta_stop)) {
           ok = false;
           break;
         }
@@ -656,11 +660,11 @@ __global__ void __launch_bounds__(Roles<CONV>::threads, 1)
     bool ok = true;
     for (uint32_t u = blockIdx.x; u < units && ok; u += gridDim.x, i++) {
       const Unit w = unit_of(ep, u);
-      if (i > 0 && !sm100::mbar_wait(tmem_empty, (i - 1) & 1, ep.err, 104)) break;
+      if (i > 0 && !sm100::mbar_wait(tmem_empty, (i - 1) & 1, ep.err, 104, ep.wait_limit, cta_stop)) break;
       sm100::tc_fence_after();
       for (uint32_t kb = w.kb0; kb < w.kb1; kb++, g++) {
         const int s = g % STAGES;
-        if (!sm100::mbar_wait(&full[s], (g / STAGES) & 1, ep.err, 102)) {
+        if (!sm100::mbar_wait(&full[s], (g / STAGES) & 1, ep.err, 102, ep.wait_limit, cta_stop)) {
           ok = false;
           break;
         }
@@ -716,7 +720,7 @@ __global__ void __launch_bounds__(Roles<CONV>::threads, 1)
     for (uint32_t u = blockIdx.x; u < units; u += gridDim.x, i++) {
       const Unit w = unit_of(ep, u);
       if (u + gridDim.x >= units) corm_pdl_trigger();  // this CTA's last unit
-      if (!sm100::mbar_wait(tmem_full, i & 1, ep.err, 103)) break;
+      if (!sm100::mbar_wait(tmem_full, i & 1, ep.err, 103, ep.wait_limit, cta_stop)) break;
       sm100::tc_fence_after();
       const uint32_t r = w.tile_r + q * 32 + lane;
       const bool row_ok = r < ep.rows;
@@ -958,6 +962,11 @@ Split split_of(uint32_t rows, uint32_t cols, uint32_t Kp, uint32_t batch) {
 int* g_err_word[64];
 std::mutex g_err_mu;
 
+// Clock cycles each bounded wait of the GEMM may take before it gives up
+// (about 2 s at the B200's clocks); corm_set_wait_limit changes it.
+constexpr long long kDefaultWaitLimit = 4000000000ll;
+std::atomic<long long> g_wait_limit{kDefaultWaitLimit};
+
 }  // namespace
 
 int* device_error_word() {
@@ -1105,6 +1114,7 @@ int gemm_i8x4(const GemmJob& j, cudaStream_t stream) {
   ep.kb_per_split = sp.kps;
   ep.partial = nullptr;
   ep.err = err;
+  ep.wait_limit = g_wait_limit.load(std::memory_order_relaxed);
   ep.raw_tma = raw_tma ? 1u : 0u;
   ep.b_tma_planes = b_planes_in ? 1u : 0u;
   ep.a_box_rows = a_box_rows;
@@ -1148,14 +1158,25 @@ int gemm_i8x4(const GemmJob& j, cudaStream_t stream) {
 }  // namespace corm
 
 // Reads and clears the per-device word the kernels' bounded waits set on a
-// timeout (synchronises the device first).  0 = no timeout since the last call.
+// timeout (synchronises the device first), and the word of the allocation-free
+// MatMul jobs.  0 = no timeout since the last call.
 extern "C" int corm_device_status(int* code) {
   int* w = corm::device_error_word();
   if (!w) return corm::fail(CORM_ECUDA, "corm_device_status: no error word");
   if (cudaDeviceSynchronize() != cudaSuccess) return corm::cuda_status("corm_device_status");
   int v = 0;
   if (cudaMemcpy(&v, w, sizeof v, cudaMemcpyDeviceToHost) != cudaSuccess) return corm::cuda_status("corm_device_status");
-  if (v) cudaMemset(w, 0, sizeof v);
-  if (code) *code = v;
+  if (v && cudaMemset(w, 0, sizeof v) != cudaSuccess) return corm::cuda_status("corm_device_status");
+  int na = 0;
+  if (int rc = corm::noalloc_status_take(&na, nullptr)) return rc;
+  if (code) *code = v ? v : na;
+  return CORM_OK;
+}
+
+// Bounds every mbarrier wait of the GEMM launches that follow (clock cycles;
+// <= 0 restores the default of about 2 s).  A diagnostic: limits below 2^20
+// cycles read the clock on every probe, so a test can make a wait run out.
+extern "C" int corm_set_wait_limit(long long cycles) {
+  corm::g_wait_limit.store(cycles > 0 ? cycles : corm::kDefaultWaitLimit, std::memory_order_relaxed);
   return CORM_OK;
 }

@@ -86,4 +86,9 @@ int split_planes2(const SplitSeg& a, const SplitSeg& b, cudaStream_t stream);
 // Per-device word the kernels' bounded waits write on a timeout.
 int* device_error_word();
 
+// Read (after the work on `stream` — nullptr: the legacy default stream — has
+// finished) and clear the status word of the allocation-free MatMul jobs on
+// the current device; no allocation.
+int noalloc_status_take(int* code, cudaStream_t stream);
+
 }  // namespace corm

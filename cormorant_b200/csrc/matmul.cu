@@ -405,6 +405,27 @@ int noalloc_setup(NoAllocDev& out) {
 
 }  // namespace
 
+namespace corm {
+int noalloc_status_take(int* code, cudaStream_t st) {
+  int v = 0;
+  cudaError_t e = cudaMemcpyFromSymbolAsync(&v, g_noalloc_status, sizeof v, 0, cudaMemcpyDeviceToHost, st);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+  if (e == cudaSuccess && v) {
+    static const int zero = 0;
+    e = cudaMemcpyToSymbolAsync(g_noalloc_status, &zero, sizeof zero, 0, cudaMemcpyHostToDevice, st);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+  }
+  if (e != cudaSuccess) return fail(CORM_ECUDA, "noalloc status: %s", cudaGetErrorString(e));
+  if (code) *code = v;
+  return CORM_OK;
+}
+}  // namespace corm
+
+extern "C" int corm_matmul_noalloc_status(int* code, corm_stream_t stream) {
+  if (int rc = corm::check_device()) return rc;
+  return corm::noalloc_status_take(code, (cudaStream_t)stream);
+}
+
 extern "C" int corm_matmul_noalloc(const corm_matmul_desc* d, corm_stream_t stream) {
   if (int rc = validate(d)) return rc;
   if (int rc = corm::check_device()) return rc;
@@ -413,11 +434,16 @@ extern "C" int corm_matmul_noalloc(const corm_matmul_desc* d, corm_stream_t stre
   cudaStream_t st = (cudaStream_t)stream;
   MmArgs p{d->a, d->b, d->c, d->n, d->k, d->m, d->batch, d->a_batch_stride, d->b_batch_stride, d->c_batch_stride,
            d->b_packed, d->gemv_kw, d->flags};
-  if (d->k == 0) {
-    for (uint32_t bt = 0; bt < d->batch; bt++)
-      for (uint32_t r = 0; r < d->n; r++)
-        if (cudaMemsetAsync(d->c + (uint64_t)bt * d->c_batch_stride + (uint64_t)r * d->m, 0, (size_t)d->m * 2, st))
-          return corm::cuda_status("corm_matmul_noalloc memset");
+  if (d->k == 0) {  // every output is 0: each batch's n x m run cleared, one call for all of them
+    const size_t run = (size_t)d->n * d->m * 2;
+    cudaError_t e;
+    if (d->batch == 1)
+      e = cudaMemsetAsync(d->c, 0, run, st);
+    else if ((size_t)d->c_batch_stride * 2 >= run)
+      e = cudaMemset2DAsync(d->c, (size_t)d->c_batch_stride * 2, 0, run, d->batch, st);
+    else  // batches that share rows: clear from the first output to the last
+      e = cudaMemsetAsync(d->c, 0, (size_t)(d->batch - 1) * d->c_batch_stride * 2 + run, st);
+    if (e != cudaSuccess) return corm::cuda_status("corm_matmul_noalloc memset");
     return CORM_OK;
   }
   const Plan pl = plan_of(d);

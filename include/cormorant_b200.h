@@ -105,6 +105,13 @@ int corm_matmul(const corm_matmul_desc* d, corm_stream_t stream);
  * race; serialise them.  Never calls cudaMalloc, cudaFree or any allocating
  * library routine. */
 int corm_matmul_noalloc(const corm_matmul_desc* d, corm_stream_t stream);
+/* The timeout status of corm_matmul_noalloc jobs, likewise without allocating:
+ * waits for the work on `stream` to finish, then reads and clears the word the
+ * jobs' bounded waits set when one runs out (*code 0 = none since the last
+ * read; a job that ran out left its output incomplete).  Call it when no
+ * allocation-free job is in flight on another stream.  corm_device_status
+ * reads and clears this word too. */
+int corm_matmul_noalloc_status(int* code, corm_stream_t stream);
 
 /* ---------------------------------------------------------------- Conv
  * Replaces XConvkernel_Set_* / XConvkernel_Start (host_emu.py:372-455;
@@ -363,6 +370,12 @@ int corm_bind_device(int device);
  * kernels' bounded waits set when a wait times out (0 = none).  Replaces the
  * reference's kernel_wait timeout accounting (runtime/inference_irq.c:259-264). */
 int corm_device_status(int* code);
+/* Bounds every mbarrier wait of the tensor-core GEMM launches issued after the
+ * call, in clock cycles (<= 0 restores the default of about 2 s).  A test and
+ * diagnostic knob: below 2^20 cycles the waits read the clock on every probe,
+ * so a short limit makes a GEMM's wait run out on purpose; the launch then
+ * unwinds and reports through the status words above. */
+int corm_set_wait_limit(long long cycles);
 /* 1 when every job issued to the stream has finished, 0 while work remains
  * (the drivers' IsDone / IsIdle), or a negative CUDA error. */
 int corm_stream_done(corm_stream_t stream);

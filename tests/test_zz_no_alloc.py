@@ -7,8 +7,12 @@ Checks, through the C ABI: on two calls in a row with different operands (the
 second call must not see the first call's leftovers in the shared scratch),
 its output equals corm_matmul's bit for bit (the tolerance of every parity
 test here: none) on the tensor-core path and on the small-n path with a K
-split; a job larger than the scratch is rejected with CORM_ELIMIT.  The file
-is named so that pytest collects it last."""
+split; the calls leave the device's free memory unchanged; a job larger than
+the scratch is rejected with CORM_ELIMIT; a job whose bounded waits are made
+to run out (a diagnostic wait limit of a few hundred cycles) returns, its
+timeout is reported once by the status read and then cleared, and the next
+call at the default limit is bit-exact again.  The file is named so that
+pytest collects it last."""
 import ctypes as C
 
 import numpy as np
@@ -75,3 +79,68 @@ def test_noalloc_rejects_oversized(lib):
     rc = L.corm_matmul_noalloc(C.byref(d), torch.cuda.current_stream().cuda_stream)
     assert rc == lib.CORM_ELIMIT
     assert b"static scratch" in L.corm_last_error()
+
+
+def test_noalloc_leaves_free_memory_unchanged(lib):
+    """The entry point's promise: after a first call per kernel (which may load
+    the kernel's code), further calls take no device memory at all."""
+    shapes = [(200, 640, 384, 2), (1, 4096, 96, 1), (7, 2048, 130, 3)]
+    L = lib.lib()
+    stream = torch.cuda.current_stream().cuda_stream
+    bufs = []
+    for n, k, m, batch in shapes:
+        a = torch.randint(-32768, 32768, (batch * n * k,), dtype=torch.int16, device="cuda")
+        b = torch.randint(-32768, 32768, (batch * k * m,), dtype=torch.int16, device="cuda")
+        c = torch.empty(batch * n * m, dtype=torch.int16, device="cuda")
+        bufs.append((a, b, c, n, k, m, batch))
+    for a, b, c, n, k, m, batch in bufs:  # warm-up: every kernel these jobs use loaded once
+        assert L.corm_matmul_noalloc(C.byref(_desc(lib, a, b, c, n, k, m, batch)), stream) == 0
+    torch.cuda.synchronize()
+    free0, _ = torch.cuda.mem_get_info()
+    for _ in range(3):
+        for a, b, c, n, k, m, batch in bufs:
+            assert L.corm_matmul_noalloc(C.byref(_desc(lib, a, b, c, n, k, m, batch)), stream) == 0
+    torch.cuda.synchronize()
+    free1, _ = torch.cuda.mem_get_info()
+    assert free1 == free0
+
+
+@pytest.mark.parametrize("shape", [(256, 4096, 512, 1), (2048, 4096, 2048, 1)], ids=["int16_ksplit", "planes"])
+def test_noalloc_timeout_reported_then_cleared(lib, shape):
+    """A bounded wait that runs out: the launch returns, the status read reports
+    the wait's code once and clears it, and the next job is exact."""
+    n, k, m, batch = shape
+    L = lib.lib()
+    stream = torch.cuda.current_stream().cuda_stream
+    code = C.c_int(-1)
+    assert L.corm_matmul_noalloc_status(C.byref(code), stream) == 0  # start from a clear word
+    a = torch.randint(-32768, 32768, (batch * n * k,), dtype=torch.int16, device="cuda")
+    b = torch.randint(-32768, 32768, (batch * k * m,), dtype=torch.int16, device="cuda")
+    out = torch.zeros(batch * n * m, dtype=torch.int16, device="cuda")
+    try:
+        # 200 cycles: far below one tile load's latency, so the first wait of
+        # every CTA's epilogue runs out
+        assert L.corm_set_wait_limit(200) == 0
+        assert L.corm_matmul_noalloc(C.byref(_desc(lib, a, b, out, n, k, m, batch)), stream) == 0
+        torch.cuda.synchronize()
+    finally:
+        assert L.corm_set_wait_limit(0) == 0
+    assert L.corm_matmul_noalloc_status(C.byref(code), stream) == 0
+    assert 101 <= code.value <= 109, code.value
+    assert L.corm_matmul_noalloc_status(C.byref(code), stream) == 0
+    assert code.value == 0  # read once, then cleared
+    # corm_device_status reads (and clears) the word too
+    try:
+        assert L.corm_set_wait_limit(200) == 0
+        assert L.corm_matmul_noalloc(C.byref(_desc(lib, a, b, out, n, k, m, batch)), stream) == 0
+    finally:
+        assert L.corm_set_wait_limit(0) == 0
+    assert L.corm_device_status(C.byref(code)) == 0
+    assert 101 <= code.value <= 109, code.value
+    assert L.corm_matmul_noalloc_status(C.byref(code), stream) == 0
+    assert code.value == 0
+    # the default limit again: exact, and no timeout recorded
+    ref, got = _run_both(lib, n, k, m, batch, 21)
+    assert np.array_equal(got, ref)
+    assert L.corm_matmul_noalloc_status(C.byref(code), stream) == 0
+    assert code.value == 0
