@@ -126,7 +126,15 @@ class GpuSimulator:
         key = ("bias", t.onnx_name, node.output.onnx_name)
         if key not in self._weights:
             v = np.clip(np.asarray(t.data, np.float64).reshape(-1), -128.0, 127.99609375)
-            if _has_exp(node.output):
+            if getattr(t, "wexp", None) is not None:
+                # encoded at its exponent (numeric.py:258-307: f_b = f_y): data holds
+                # raw / 2^8, the value raw / 2^f_b, so at f_y the raw is round(data 2^8)
+                # 2^(f_y - f_b) — the stored word itself when f_b = f_y
+                M = node.out_ch
+                fy = np.broadcast_to(np.asarray(_exp_of(node.output), np.float64).reshape(-1), (M,))
+                fb = np.broadcast_to(np.asarray(t.wexp, np.float64).reshape(-1), (M,))
+                raw = np.round(np.round(v[:M] * 256.0) * np.power(2.0, fy - fb))
+            elif _has_exp(node.output):
                 fy = _exp_of(node.output)
                 fy = np.asarray(fy, np.float64).reshape(-1) if np.ndim(fy) else fy
                 raw = np.round(np.round(v * 256.0) / 256.0 * np.power(2.0, fy))

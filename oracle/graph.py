@@ -26,12 +26,19 @@ def forward_raw(graph, raw_inputs):
             wrap = any(getattr(t, a, None) is not None for t in (sn.inputs[0], sn.inputs[1], out)
                        for a in ("exp", "wexp"))
             y = spec.matmul_raw(arr[sn.inputs[0].onnx_name], arr[sn.inputs[1].onnx_name], wrap)
-        elif k == "ConvNode":                                                # :643-660
+        elif k == "ConvNode":                                                # :635-660, :784-812
             x = arr[sn.inputs[0].onnx_name].reshape(sn.batch, sn.in_ch, sn.in_h, sn.in_w)
             w = arr[sn.inputs[1].onnx_name]
-            b = arr[sn.inputs[2].onnx_name].reshape(-1) if sn.has_bias else None
+            exp = any(getattr(t, a, None) is not None for t in (sn.inputs[0], sn.inputs[1], out)
+                      for a in ("exp", "wexp", "chexp"))
+            b = None
+            if sn.has_bias:
+                b = arr[sn.inputs[2].onnx_name].reshape(-1)[:sn.out_ch]
+                if exp and getattr(sn.inputs[2], "wexp", None) is None:
+                    # a Q8.8 bias on an exponent conv: its value at f_y (S:805-806)
+                    b = spec.rne_int(b * _conv_fy(out, sn.out_ch) / 256.0)
             y = spec.conv_raw(x, w, b, sn.stride_h, sn.stride_w, sn.pad_top, sn.pad_left, sn.dilation_h,
-                              sn.dilation_w, sn.out_h, sn.out_w, bool(sn.is_depthwise))
+                              sn.dilation_w, sn.out_h, sn.out_w, bool(sn.is_depthwise), wrap=exp)
         elif k == "ReshapeNode":                                             # :662-665
             y = arr[sn.inputs[0].onnx_name]
         elif k == "PoolNode":                                                # :701-719
@@ -66,6 +73,16 @@ def forward_raw(graph, raw_inputs):
             raise NotImplementedError(k)
         arr[out.onnx_name] = np.asarray(y, np.int64).reshape(out.shape)
     return arr
+
+
+def _conv_fy(t, out_ch):
+    """2^f_y per output channel of an exponent conv's output (chexp or exp;
+    Q8.8 without either)."""
+    if getattr(t, "chexp", None) is not None:
+        f = np.asarray(t.chexp, np.float64).reshape(-1)
+    else:
+        f = np.full(out_ch, 8.0 if getattr(t, "exp", None) is None else float(np.asarray(t.exp)))
+    return np.power(2.0, f)
 
 
 def forward(graph, inputs):

@@ -13,7 +13,7 @@ reference, so everything the tests need is written here).
    ``rowops_spec``) on seeded inputs, imported through the inert ``onnx``
    stand-in in ``_onnx_stub``.
 
-    python tests/golden/make_golden.py [--ref /root/reference] [--only hw|sim|graph|llm|attn|smx|numeric]
+    python tests/golden/make_golden.py [--ref /root/reference] [--only hw|sim|graph|llm|attn|smx|numeric|convexp]
 """
 from __future__ import annotations
 
@@ -809,10 +809,81 @@ def make_numeric(ref, out):
     print("sim_numeric.npz:", len(res), "arrays")
 
 
+def make_conv_exp(ref, out):
+    """Convs on tensors with power-of-two exponents (``_SimulateMixin._conv_exp``
+    + ``_conv2d_int``, _simulate.py:784-812, 198-220): weights and biases
+    encoded by the reference's ``numeric.encode_conv_weights``
+    (numeric.py:258-307: f_w = f_y + F - f_x, the bias at f_y), inputs on their
+    exponents' grids, run through the reference's ``_forward_pass``.  Per-tensor
+    and per-channel (chexp) exponents, standard and depthwise, stride /
+    padding / dilation, with and without bias, and cases whose int32
+    accumulator wraps.  The fixture keeps the raw inputs, the encoded raw
+    weight / bias words with their exponents, and the raw outputs."""
+    sim = _import_reference(ref)
+    import onnx
+    from src import numeric as NU, nodes as N
+    from src.dtype import AP_FIXED_16_8 as D
+    from src.tensor import TensorInfo as T
+    nd = onnx.NodeProto()
+    rng = np.random.default_rng(23)
+    res = {}
+    # tag: C, M, H, W, kh, kw, stride, pad, dil, depthwise, bias, fx, fy, x range, weight sigma
+    cases = [
+        ("t3", 6, 8, 9, 7, 3, 3, 1, 1, 1, False, True, 11, 10, 2.0, 0.1),
+        ("tdw", 8, 8, 10, 10, 3, 3, 2, 1, 1, True, True, 12, 9, 1.0, 0.3),
+        ("t1nb", 16, 12, 5, 6, 1, 1, 1, 0, 1, False, False, 10, 11, 3.0, 0.2),
+        ("ch1", 6, 5, 4, 6, 1, 1, 1, 0, 1, False, True, rng.integers(8, 13, 6), rng.integers(7, 12, 5), 2.0, 0.1),
+        ("ch3s2", 5, 7, 11, 9, 3, 3, 2, 1, 1, False, True, rng.integers(8, 13, 5), rng.integers(7, 12, 7), 2.0, 0.1),
+        ("chdw", 7, 7, 8, 9, 3, 3, 1, 2, 2, True, True, rng.integers(8, 13, 7), rng.integers(7, 12, 7), 2.0, 0.2),
+        ("chdw51", 6, 6, 9, 8, 5, 1, 1, 2, 1, True, False, rng.integers(6, 12, 6), rng.integers(9, 13, 6), 4.0, 0.5),
+        # the int32 accumulator wraps: raw inputs near full scale, saturated weights
+        ("wrap", 64, 4, 6, 6, 3, 3, 1, 1, 1, False, True, 6, 14, 500.0, 0.8),
+        ("wrapdw", 4, 4, 7, 7, 7, 7, 1, 3, 1, True, True, 6, 14, 500.0, 0.8),
+        ("wrapch", 32, 6, 5, 5, 3, 3, 1, 1, 1, False, True, rng.integers(5, 8, 32), rng.integers(12, 15, 6), 400.0,
+         0.9),
+    ]
+    for (tag, C, M, H, W_, kh, kw, st, pad, dil, dw, hb, fx, fy, xr, sig) in cases:
+        oh = (H + 2 * pad - (dil * (kh - 1) + 1)) // st + 1
+        ow = (W_ + 2 * pad - (dil * (kw - 1) + 1)) // st + 1
+        per_ch = np.ndim(fx) > 0
+        w = (rng.standard_normal((M, 1 if dw else C, kh, kw)) * sig).astype(np.float32)
+        b = (rng.standard_normal(M) * 0.5).astype(np.float32)
+        fxv = np.asarray(fx, np.int64).reshape(-1) if per_ch else np.full(C, int(fx))
+        xraw = np.clip(np.round(rng.uniform(-xr, xr, size=(2, C, H, W_)) * np.power(2.0, fxv)[None, :, None, None]),
+                       -32768, 32767).astype(np.int64)
+        ekw = (lambda f: {"chexp": np.asarray(f, np.int8)}) if per_ch else (lambda f: {"exp": np.asarray(f)})
+        X = T(onnx_name="x", shape=[2, C, H, W_], dtype="float32", **ekw(fx))
+        Y = T(onnx_name="y", shape=[2, M, oh, ow], dtype="float32", **ekw(fy))
+        Wt = T(onnx_name="w_" + tag, shape=list(w.shape), dtype="float32", data=w.copy())
+        Bt = T(onnx_name="b_" + tag, shape=[M], dtype="float32", data=b.copy())
+        node = N.ConvNode(onnx_node=nd, inputs=[X, Wt, Bt] if hb else [X, Wt], output=Y, batch=2, in_ch=C, in_h=H,
+                          in_w=W_, out_ch=M, out_h=oh, out_w=ow, kh=kh, kw=kw, stride_h=st, stride_w=st,
+                          dilation_h=dil, dilation_w=dil, pad_top=pad, pad_left=pad, has_bias=hb, is_depthwise=dw)
+        NU.encode_conv_weights([node], D)
+        g = _Graph([node], [Wt, Bt] if hb else [Wt], [X], [Y])
+        xv = xraw / np.power(2.0, fxv)[None, :, None, None]
+        yv = _shim(sim, D, g)._forward_pass({"x": xv})["y"]
+        fyv = np.asarray(fy, np.float64).reshape(1, -1, 1, 1) if per_ch else float(fy)
+        yraw = np.round(yv * np.power(2.0, fyv)).astype(np.int64)
+        res[f"{tag}_geo"] = np.array([C, M, H, W_, kh, kw, st, pad, dil, int(dw), int(hb), oh, ow, int(per_ch)])
+        res[f"{tag}_fx"], res[f"{tag}_fy"] = np.asarray(fx), np.asarray(fy)
+        res[f"{tag}_x"] = xraw
+        res[f"{tag}_wraw"] = np.round(Wt.data.astype(np.float64) * 256).astype(np.int64).reshape(w.shape)
+        res[f"{tag}_wexp"] = np.asarray(Wt.wexp, np.int64)
+        if hb:
+            res[f"{tag}_braw"] = np.round(Bt.data.astype(np.float64) * 256).astype(np.int64).reshape(-1)[:M]
+            res[f"{tag}_bexp"] = np.asarray(Bt.wexp, np.int64)
+        res[f"{tag}_y"] = yraw
+        print(f"  {tag}: y {yraw.shape}, max |raw| {int(np.abs(yraw).max())}")
+    res["tags"] = np.array([c[0] for c in cases])
+    np.savez_compressed(os.path.join(out, "sim_conv_exp.npz"), **res)
+    print("sim_conv_exp.npz:", len(cases), "cases")
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--ref", default="/root/reference")
-    ap.add_argument("--only", choices=["hw", "sim", "graph", "llm", "attn", "smx", "numeric"])
+    ap.add_argument("--only", choices=["hw", "sim", "graph", "llm", "attn", "smx", "numeric", "convexp"])
     ap.add_argument("--out", default=HERE)
     args = ap.parse_args()
     if args.only in (None, "hw"):
@@ -829,6 +900,8 @@ def main():
         make_llm_smx_host(args.ref, args.out)
     if args.only in (None, "numeric"):
         make_numeric(args.ref, args.out)
+    if args.only in (None, "convexp"):
+        make_conv_exp(args.ref, args.out)
 
 
 if __name__ == "__main__":
