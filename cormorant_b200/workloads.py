@@ -28,6 +28,19 @@ def he_normal_q88(rng, shape, fan_in) -> np.ndarray:
     return np.clip(np.round(rng.normal(0.0, np.sqrt(2.0 / fan_in), size=shape) * 256.0), -32768, 32767) / 256.0
 
 
+def unit_rng(seed: int, i: int) -> np.random.Generator:
+    """The input stream of unit ``i`` (an image, a sequence) of a seeded
+    configuration.  Weights come from the configuration's own stream, inputs
+    from one stream per unit, so a rank that runs units [first, first +
+    batch) of a sharded batch holds exactly those units' inputs, with the
+    same weights, whatever the split."""
+    return np.random.default_rng([seed, 0x5EED, i])
+
+
+def _per_unit(seed: int, first: int, batch: int, draw) -> np.ndarray:
+    return np.stack([draw(unit_rng(seed, first + i)) for i in range(batch)])
+
+
 class NodeFactory:
     """Builds graph pieces with cormorant_b200.nodes descriptors."""
 
@@ -87,13 +100,14 @@ class NodeFactory:
 
 
 # ---------------------------------------------------------------- config 1: MNIST CNN
-def mnist(seed: int = 1, batch: int = 1, factory: NodeFactory = None):
+def mnist(seed: int = 1, batch: int = 1, factory: NodeFactory = None, first: int = 0):
     """Conv3x3 1->16 +bias, Relu, MaxPool 2x2, Conv3x3 16->32 +bias, Relu,
     MaxPool 2x2, flatten 1568, MatMul 1568x10, Add bias, Softmax (row, Q8.8).
+    Images [first, first + batch) of the seeded input set.
     Returns (graph, {input: values}, macs_per_image)."""
     f = factory or NodeFactory()
     rng = np.random.default_rng(seed)
-    x = q88_uniform(rng, (batch, 1, 28, 28), -1, 1)
+    x = _per_unit(seed, first, batch, lambda r: q88_uniform(r, (1, 28, 28), -1, 1))
     w1, b1 = q88_uniform(rng, (16, 1, 3, 3), -0.25, 0.25), q88_uniform(rng, (16,), -0.25, 0.25)
     w2, b2 = q88_uniform(rng, (32, 16, 3, 3), -0.25, 0.25), q88_uniform(rng, (32,), -0.25, 0.25)
     wf, bf = q88_uniform(rng, (1568, 10), -0.25, 0.25), q88_uniform(rng, (1, 10), -0.25, 0.25)
@@ -127,15 +141,17 @@ MBV2_BLOCKS = [(1, 16, 1, 1), (6, 24, 2, 2), (6, 32, 3, 2), (6, 64, 4, 2), (6, 9
                (6, 320, 1, 1)]  # (expansion t, channels c, repeats n, first stride s)
 
 
-def mobilenet_v2(seed: int = 3, batch: int = 1, res: int = 224, classes: int = 1000, factory: NodeFactory = None):
+def mobilenet_v2(seed: int = 3, batch: int = 1, res: int = 224, classes: int = 1000, factory: NodeFactory = None,
+                 first: int = 0):
     """MobileNetV2-1.0: stem Conv3x3 s2 3->32 + Clip(0,6); inverted residuals
     (1x1 expand x t + Clip, depthwise 3x3 + Clip, 1x1 project, residual Add
     when shapes match); Conv1x1 320->1280 + Clip; GlobalAveragePool; MatMul
     1280 x classes + Add bias.  Batch-norm folded into the conv biases (small
-    seeded values).  Returns (graph, {input: values}, macs_per_image)."""
+    seeded values).  Images [first, first + batch) of the seeded input set.
+    Returns (graph, {input: values}, macs_per_image)."""
     f = factory or NodeFactory()
     rng = np.random.default_rng(seed)
-    x = q88_uniform(rng, (batch, 3, res, res), -1, 1)
+    x = _per_unit(seed, first, batch, lambda r: q88_uniform(r, (3, res, res), -1, 1))
     X = f.tensor("x", x.shape)
     macs = 0
     counter = [0]
@@ -204,7 +220,7 @@ def normal_q88(rng, shape, sigma) -> np.ndarray:
 
 
 def bert_base(seed: int = 4, batch: int = 1, seq: int = 384, layers: int = 12, hidden: int = 768, heads: int = 12,
-              ffn: int = 3072, vocab: int = 30522, qa_head: bool = True, factory: NodeFactory = None):
+              ffn: int = 3072, vocab: int = 30522, qa_head: bool = True, factory: NodeFactory = None, first: int = 0):
     """BERT-base encoder on the kernels, the scheduler's partition of
     bertsquad (ap_fixed<16,8> throughout): per layer Q / K / V = x W + b
     (MatMul, VectorOP ADD), head split and K^T as row-ops COPY / TRANSPOSE
@@ -223,13 +239,14 @@ def bert_base(seed: int = 4, batch: int = 1, seq: int = 384, layers: int = 12, h
     over ``vocab``); position and token-type embeddings are added on
     VectorOP.  Weights N(0, 0.02) quantised to Q8.8; LayerNorm gamma =
     1 + N(0, 0.02), beta = N(0, 0.02) (encoded by the parameter block).
+    Sequences [first, first + batch) of the seeded input set.
     Returns (graph, {input: values}, macs_per_token)."""
     f = factory or NodeFactory()
     rng = np.random.default_rng(seed)
     T, D, H, dh = seq, hidden, heads, hidden // heads
     R = batch * T
     word = normal_q88(rng, (vocab, D), 0.02)
-    ids = rng.integers(0, vocab, size=(batch, T))
+    ids = _per_unit(seed, first, batch, lambda r: r.integers(0, vocab, size=T))
     x = word[ids]
     cnt = [0]
 
@@ -352,8 +369,9 @@ class LlamaModel:
     (LlmSelectRowNode); a decode step (one row, no n) runs the host's p12
     softmax, as the reference's decode entries do.
 
-    ``batch`` sequences side by side (the nodes' batch layouts), ``seq``
-    prefill tokens at pos 0, KV caches of ``cache`` rows (default seq + 128)
+    ``batch`` sequences side by side (the nodes' batch layouts: sequences
+    [first, first + batch) of the seeded input set), ``seq`` prefill tokens
+    at pos 0, KV caches of ``cache`` rows (default seq + 128)
     as group-major states.  The embedding lookup is the reference's host op:
     a graph input is the gathered rows of a N(0, 0.02) table as the int32
     residual.  Weights N(0, 0.02) (norm weights 1) at the rank-1 exponents the
@@ -361,7 +379,7 @@ class LlamaModel:
 
     def __init__(self, seed: int = 5, batch: int = 1, seq: int = 512, layers: int = 32, hidden: int = 960,
                  heads: int = 15, kv_heads: int = 5, head_dim: int = 64, ffn: int = 2560, vocab: int = 49152,
-                 theta: float = 1e5, cache: int = None, eps: float = 1e-5, exps: dict = None):
+                 theta: float = 1e5, cache: int = None, eps: float = 1e-5, exps: dict = None, first: int = 0):
         from . import attention as AT
         from . import numeric as NU
         E = dict(LLAMA_EXP, **(exps or {}))
@@ -404,7 +422,8 @@ class LlamaModel:
         ang = np.outer(np.arange(C, dtype=np.float64), inv)
         self.cos, self.sin = np.cos(ang).astype(np.float32), np.sin(ang).astype(np.float32)
         self.emb = rng.normal(0.0, 0.02, (vocab, D))
-        self.ids = rng.integers(0, vocab, size=(batch, seq))
+        self.first = first
+        self.ids = _per_unit(seed, first, batch, lambda r: r.integers(0, vocab, size=seq))
         self.prefill_graph = self._graph(seq, prefill=True)
         self.decode_graph = self._graph(1, prefill=False)
         self.prefill_feeds = {"h0": self.emb[self.ids].reshape(batch * seq, D), "pos": np.array([0]),
@@ -503,10 +522,10 @@ class LlamaModel:
 
 def llama_prefill(seed: int = 5, batch: int = 1, seq: int = 512, layers: int = 32, hidden: int = 960, heads: int = 15,
                   kv_heads: int = 5, head_dim: int = 64, ffn: int = 2560, vocab: int = 49152, theta: float = 1e5,
-                  cache: int = None, eps: float = 1e-5, exps: dict = None):
+                  cache: int = None, eps: float = 1e-5, exps: dict = None, first: int = 0):
     """The prefill of ``LlamaModel``: (graph, {input: values}, macs_per_token)."""
     from . import attention as AT
     m = LlamaModel(seed=seed, batch=batch, seq=seq, layers=layers, hidden=hidden, heads=heads, kv_heads=kv_heads,
-                   head_dim=head_dim, ffn=ffn, vocab=vocab, theta=theta, cache=cache, eps=eps, exps=exps)
+                   head_dim=head_dim, ffn=ffn, vocab=vocab, theta=theta, cache=cache, eps=eps, exps=exps, first=first)
     keys = -(-seq // AT.KEY_QUANTUM) * AT.KEY_QUANTUM
     return m.prefill_graph, m.prefill_feeds, m.macs_per_token(keys)
