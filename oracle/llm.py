@@ -48,15 +48,21 @@ def _words(t):
     return np.round(np.asarray(t.data, np.float64) * 256.0).astype(np.int64)
 
 
-def forward(graph, raw_inputs: dict, raw_states: dict) -> dict:
+def forward(graph, raw_inputs: dict, raw_states: dict, weights: dict = None) -> dict:
     """{name: raw int64 array} of every tensor; ``raw_states`` (logical raw
-    arrays) are updated in place; host ints (pos, n) pass through."""
+    arrays) are updated in place; host ints (pos, n) pass through.
+    ``weights``: a dict that keeps the weights' raw words between passes of
+    graphs sharing weights.  The words are kept as integer-valued float64 (the
+    MatMul sums read them so; every word is exact in float64)."""
     arr = {k: np.asarray(v, np.int64) for k, v in raw_inputs.items()}
     arr.update(raw_states)
+    wc = {} if weights is None else weights
     for t in graph.weight_tensors:
         if getattr(t, "data", None) is not None and t.onnx_name not in arr:
-            v = np.clip(np.asarray(t.data, np.float64).reshape(t.shape), -128.0, 127.99609375)
-            arr[t.onnx_name] = np.round(v * 256.0).astype(np.int64)
+            if t.onnx_name not in wc:
+                v = np.clip(np.asarray(t.data, np.float64).reshape(t.shape), -128.0, 127.99609375)
+                wc[t.onnx_name] = np.round(v * 256.0)
+            arr[t.onnx_name] = wc[t.onnx_name]
     hi = lambda t: int(np.asarray(arr[t.onnx_name]).reshape(-1)[0])  # noqa: E731
     for sn in graph.nodes:
         k = type(sn).__name__
@@ -135,21 +141,23 @@ def forward(graph, raw_inputs: dict, raw_states: dict) -> dict:
     return arr
 
 
-def greedy_decode(model, raw_states: dict, prefill_logits: np.ndarray, steps: int):
+def greedy_decode(model, raw_states: dict, prefill_logits: np.ndarray, steps: int, weights: dict = None):
     """Greedy decode steps on the oracle after a prefill (the states already
     hold its cache rows): the first argmax of each sequence's logits, its
     embedding row as the int32 residual (RNE at the residual's exponent), one
     decode-step pass at pos = T + i.  Returns (ids [steps][B], logits of every
-    step)."""
+    step).  ``weights``: the raw-word cache of ``forward`` (shared with the
+    prefill's pass, so the weights are converted once)."""
     g = model.decode_graph
     out = g.output_tensors[0].onnx_name
     emb_raw = np.rint(model.emb * 2.0 ** model.E["fr"]).astype(np.int64)
     lg = np.asarray(prefill_logits, np.int64)
     ids, logits = [], []
+    wc = {} if weights is None else weights
     for i in range(steps):
         nxt = lg.argmax(axis=1)
         ids.append(nxt)
-        arr = forward(g, {"h_step": emb_raw[nxt], "pos": np.array([model.T + i])}, raw_states)
+        arr = forward(g, {"h_step": emb_raw[nxt], "pos": np.array([model.T + i])}, raw_states, wc)
         lg = arr[out]
         logits.append(lg)
     return np.stack(ids), logits
