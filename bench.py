@@ -35,6 +35,8 @@ import sys
 import threading
 import time
 
+import numpy as np
+
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
@@ -106,15 +108,19 @@ class ClockSampler:
 
 
 # ---------------------------------------------------------------- CPU side (oracle)
-def cpu_matmul_rate(problems, min_seconds=10.0, seed=0):
+def cpu_sweep_data(problems, seed=0):
+    """The sweep's operands on the host (int16 Q8.8 in [-1, 1))."""
+    rng = np.random.default_rng(seed)
+    return [(rng.integers(-256, 256, size=(b, m, k), dtype=np.int16),
+             rng.integers(-256, 256, size=(b, k, n), dtype=np.int16)) for b, m, k, n in problems]
+
+
+def cpu_matmul_rate(problems, min_seconds=10.0, seed=0, data=None):
     """GMAC/s of the CPU oracle (numpy float64 matmul + floor + saturate) over
     ``problems`` repeated until ``min_seconds`` elapsed."""
-    import numpy as np
-
     from oracle import spec
-    rng = np.random.default_rng(seed)
-    data = [(rng.integers(-256, 256, size=(b, m, k)).astype(np.int16),
-             rng.integers(-256, 256, size=(b, k, n)).astype(np.int16)) for b, m, k, n in problems]
+    if data is None:
+        data = cpu_sweep_data(problems, seed)
     macs, t0 = 0, time.perf_counter()
     while True:
         for (A, B), (b, m, k, n) in zip(data, problems):
@@ -134,12 +140,14 @@ def run_reference(args):
     cores = os.cpu_count() or 1
     os.environ.setdefault("OMP_NUM_THREADS", str(cores))
     os.environ.setdefault("OPENBLAS_NUM_THREADS", str(cores))
-    sample = sweep_problems(batches=(1,))
-    for _ in range(args.warmup):
-        cpu_matmul_rate(sample, min_seconds=0.0)
+    sample = sweep_problems()  # the whole sweep, as the GPU arm times it
+    data = cpu_sweep_data(sample)
+    half = sweep_problems(batches=(1,))
+    for _ in range(args.warmup):  # warm-up (untimed): the batch-1 half, threads and caches started
+        cpu_matmul_rate(half, min_seconds=0.0, data=data[:len(half)])
     rates, secs = [], []
     for _ in range(args.steps):
-        r, el, _ = cpu_matmul_rate(sample, min_seconds=0.0)
+        r, el, _ = cpu_matmul_rate(sample, min_seconds=0.0, data=data)
         rates.append(r)
         secs.append(el)
     value = macs_of(sample) * args.steps / sum(secs) / 1e9
@@ -147,9 +155,11 @@ def run_reference(args):
             "unit": "GMAC/s", "impl": "reference", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": round(1e3 * sum(secs) / args.steps, 3), "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "int16 (exact int64 sums)", "data": "synthetic, seeded",
-            "config": {"workload": "configs[1] op-level MatMul sweep", "step_sample": "batch-1 half (64 problems)"},
+            "config": {"workload": "configs[1] op-level MatMul sweep: M{1,8,128,2048} x K{64,512,1024,4096} x "
+                                   "N{32,256,1024,4096} x batch{1,16}", "problems": len(sample),
+                       "gmac_per_step_per_gpu": round(macs_of(sample) / 1e9, 3)},
             "cpu_baseline": {"value": round(value, 3), "unit": "GMAC/s", "cores": cores, "kind": "port",
-                             "sample": "batch-1 half of the MatMul sweep (64 problems, %.1f GMAC) per step"
+                             "sample": "the whole MatMul sweep (128 problems, %.1f GMAC) per step"
                                        % (macs_of(sample) / 1e9)},
             "e2e": {"value": round(value, 3), "unit": "GMAC/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
@@ -312,29 +322,34 @@ def main():
             json.dump(per, fh, indent=1)
     tensor_probs = [(b, m, k, n) for b, m, k, n in problems if m > 2]
     tensor_macs = sum(b * m * k * n for b, m, k, n in tensor_probs)
-    # DRAM traffic of the GEMM kernel: one ncu capture of the 4 x 2048 x 4096 x 4096
-    # case (profiles/gemm_i8x4_kernel_matmul_4x2048x4096x4096.md) read 201.43 MB and
-    # wrote 52.52 MB per launch against 268.4 MB of algorithmic bytes (int8 planes of A
-    # and B read once, int16 C written); scaled to the sweep's average launch by its
-    # algorithmic bytes.
+    # DRAM traffic of the GEMM kernel per launch: algorithmic bytes (A and B read
+    # once — as int8 planes or as int16, the same bytes — and C written once)
+    # times the DRAM / algorithmic ratio ncu measured for the launch's form: the
+    # split-plane form 0.946 (4 x 2048 x 4096 x 4096: 201.43 MB read + 52.52 MB
+    # written of 268.4 MB), the int16-operand form 1.11 (16 x 2048 x 4096 x 256:
+    # 324.4 + 13.6 MB of 304 MB; A's second read per column-tile pair partly misses L2).
+    def int16_form(m, k, n):  # the library's rule (csrc/matmul.cu tensor_path)
+        return k % 8 == 0 and n % 8 == 0 and (m + n) * 500 > m * n
+    ratio = {False: (201.43e6 + 52.52e6) / 268.4e6, True: (324.4e6 + 13.6e6) / 304e6}
     alg_bytes = sum(b * (2 * m * k + 2 * k * n + 2 * m * n) for b, m, k, n in tensor_probs)
-    ncu_ratio = (201.43e6 + 52.52e6) / 268.4e6
+    dram_bytes = sum(b * (2 * m * k + 2 * k * n + 2 * m * n) * ratio[int16_form(m, k, n)]
+                     for b, m, k, n in tensor_probs)
+    n_int16 = sum(1 for b, m, k, n in tensor_probs if int16_form(m, k, n))
     g_launches, g_ms, _ = prof.get("gemm_i8x4_kernel", (0, 0.0, 0.0))
-    peak, peak_src = measure_int8_peak(torch, dev)
+    live_peak, live_src = measure_int8_peak(torch, dev)
+    with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as fh:
+        bf16 = float(json.load(fh)["bf16_tflops"])
+    peak = 2 * bf16  # dense int8 = 2 x dense bf16 on B200; the pool's measured bf16 burst
     achieved = 8 * tensor_macs / (g_ms * 1e-3) / 1e12 if g_ms else None
     step_kernel_ms = sum(v[1] for v in prof.values())
 
     # VectorOP and Softmax sweeps of the same config
-    sweeps = vector_sweeps(torch, ops, dev, stream, flush, args)
+    sweeps = vector_sweeps(torch, ops, dev, stream, flush, args, rank, world)
     models = None if args.no_models else bench_models(torch, dev, stream, flush, args, world, rank, pg)
 
-    # verification gather (the only collective): per-rank checksum of the outputs
-    chk = torch.zeros(1, dtype=torch.int64, device=dev)
-    for _, _, Cc in bufs:
-        chk += Cc.to(torch.int64).sum()
-    if pg:
-        allc = [torch.zeros_like(chk) for _ in range(world)]
-        pg.all_gather(allc, chk)
+    # verification of the timed sweep's own outputs (after the timed region):
+    # every rank's sampled grids gathered to rank 0 over NCCL and checked there
+    parity = sweep_parity(torch, problems, bufs, dev, rank, world, pg)
 
     e2e = None
     if not args.no_e2e:
@@ -342,10 +357,9 @@ def main():
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
-        sample = sweep_problems(batches=(1,))
-        r, el, macs = cpu_matmul_rate(sample, min_seconds=10.0)
+        r, el, macs = cpu_matmul_rate(problems, min_seconds=5.0)
         cpu = {"value": round(r, 3), "unit": "GMAC/s", "cores": os.cpu_count(), "kind": "port",
-               "sample": "batch-1 half of the MatMul sweep (64 problems), repeated %.1f s" % el}
+               "sample": "the whole MatMul sweep (128 problems), repeated to %.1f s" % el}
 
     if rank == 0:
         line = {
@@ -362,16 +376,22 @@ def main():
             "gpu_launches": int(launches_per_step * args.steps),
             "roofline": {"bound": "tensor", "kernel": "gemm_i8x4_kernel", "achieved": round(achieved, 1) if achieved else None,
                          "peak": round(peak, 1), "unit": "TFLOP/s", "frac": round(achieved / peak, 4) if achieved else None,
-                         "traffic": round(ncu_ratio * alg_bytes / max(g_launches, 1)),
-                         "traffic_note": "bytes per GEMM launch: sweep average of algorithmic bytes (int8 planes + "
-                                         "int16 C) x the DRAM/algorithmic ratio of one ncu capture (%.3f, "
-                                         "4x2048x4096x4096)" % ncu_ratio,
-                         "peak_source": peak_src,
+                         "traffic": round(dram_bytes / max(g_launches, 1)),
+                         "alg_bytes_per_launch": round(alg_bytes / max(g_launches, 1)),
+                         "traffic_note": "DRAM bytes per GEMM launch, sweep average: each launch's algorithmic bytes x "
+                                         "the DRAM/algorithmic ratio ncu measured for its form (split planes 0.946, "
+                                         "int16 operands 1.11; %d of %d launches in the int16 form)"
+                                         % (n_int16, len(tensor_probs)),
+                         "peak_source": "of measured: 2 x MEASURED_PEAKS bf16_tflops burst (%.1f; B200 dense int8 = "
+                                        "2 x dense bf16)" % bf16,
+                         "live_int8_probe": {"peak": round(live_peak, 1), "frac": round(achieved / live_peak, 4)
+                                             if achieved else None, "source": live_src},
                          "work": "8 int8 tensor ops per int16 MAC (4 int8 products); tensor-path problems (M > 2)",
                          "gemm_launches_per_step": g_launches, "gemm_ms_per_step": round(g_ms, 4),
                          "all_kernels_ms_per_step": round(step_kernel_ms, 4),
                          "kernels": {k: {"launches": v[0], "ms": round(v[1], 4)} for k, v in sorted(prof.items())}},
             "clocks": clk,
+            "parity": parity,
             "sweeps": sweeps,
         }
         if models:
@@ -387,88 +407,271 @@ def main():
     return 0
 
 
-def vector_sweeps(torch, ops, dev, stream, flush, args):
-    """VectorOP 4M-element broadcast ops with fused activations, and softmax
-    rows / columns: GB/s over the algorithmic bytes."""
-    from cormorant_b200 import _lib  # noqa: F401
+def _gather_to_root(torch, pg, world, rank, t):
+    """All ranks' equally sized 1-D tensors on rank 0 (all-gather: the
+    verification step, after the timed regions); [t] when running alone."""
+    if not pg:
+        return [t]
+    out = torch.empty(world * t.numel(), dtype=t.dtype, device=t.device)
+    pg.all_gather_into_tensor(out, t)
+    return list(out.split(t.numel())) if rank == 0 else []
+
+
+def sweep_parity(torch, problems, bufs, dev, rank, world, pg):
+    """Every problem of the timed sweep checked exactly at a seeded grid of
+    >= 4096 outputs (its rows of A, columns of B and outputs, gathered on the
+    device; oracle.sampled), on every rank: each rank's grids go to rank 0,
+    which recomputes them with the CPU oracle.  Verification only: it runs
+    after the timed region on the outputs the last timed step wrote."""
+    from oracle import sampled
+    parts, shapes = [], []
+    for i, ((b, m, k, n), (A, B, Cc)) in enumerate(zip(problems, bufs)):
+        idx = sampled.plan(b, m, k, n, seed=i, full_macs=None)
+        subs = sampled.gather_t(A, B, Cc, b, m, k, n, idx)
+        parts += [t.reshape(-1) for t in subs]
+        shapes.append(tuple(tuple(t.shape) for t in subs))
+    got = _gather_to_root(torch, pg, world, rank, torch.cat(parts).contiguous())
+    if rank != 0:
+        return None
+    checked = bad = 0
+    for fl in got:
+        v = fl.cpu().numpy()
+        off = 0
+        for shs in shapes:
+            seg = []
+            for sh in shs:
+                cnt = int(np.prod(sh))
+                seg.append(v[off:off + cnt].reshape(sh))
+                off += cnt
+            c_n, c_bad = sampled.check(*seg)
+            checked += c_n
+            bad += c_bad
+    return {"checked": checked, "mismatches": bad, "ranks": len(got), "problems": len(problems),
+            "method": "per problem and rank, >= 4096 outputs (or all) at a seeded grid, recomputed exactly from "
+                      "their rows of A and columns of B by the CPU oracle; grids gathered to rank 0"}
+
+
+def _time_job(torch, stream, flush, fn, args):
+    """Median device time (ms) of one job captured as a CUDA graph, the L2
+    flushed before every replay (inputs come from HBM)."""
+    with torch.cuda.stream(stream):
+        fn()
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=stream):
+        fn()
+    return _time_graph(torch, stream, flush, g, args)
+
+
+def cpu_vectorop_rate(jobs, size, outer, min_seconds=2.0):
+    """Elements/s of the reference's VectorOP method on the host (the op on
+    the raw operands, then its activation in float64 with the C library's
+    exp / erf / tanh and host_quantize: _simulate.py:721-765,
+    vectorop_act.py:60-79, as the oracle restates them), over ``jobs``."""
+    from oracle import spec
+    rng = np.random.default_rng(7)
+    a = rng.integers(-256, 256, size=(outer, size)).astype(np.int64)
+    b = rng.integers(-256, 256, size=(1, size)).astype(np.int64)
+    b = np.where(b == 0, 1, b)
+    n, t0 = 0, time.perf_counter()
+    while True:
+        for op, act in jobs:
+            if op == 0:
+                r = a + b
+            elif op == 2:
+                r = (a * b) >> 8
+            else:
+                num = a * 256
+                q = np.abs(num) // np.abs(b)
+                r = np.where((num < 0) ^ (b < 0), -q, q)
+            r = spec.sat16(r)
+            spec.host_quantize_raw(spec.act_real(act, r / 256.0))
+            n += a.size
+        el = time.perf_counter() - t0
+        if el >= min_seconds:
+            return n / el, el
+
+
+def cpu_softmax_rate(cases, min_seconds=1.0):
+    """Elements/s of the reference's softmax unit model on the host
+    (vectorop_smx.softmax_raw / softmax_cols, as oracle.spec restates them),
+    over (n, mode) cases of 2^20 elements each."""
+    from oracle import spec
+    rng = np.random.default_rng(8)
+    cm, cs = spec.smx_scale_regs(8, 1.0)
+    data = {n: rng.integers(-2048, 2048, size=((1 << 20) // n, n)).astype(np.int64) for n, _ in cases}
+    cnt, t0 = 0, time.perf_counter()
+    while True:
+        for n, mode in cases:
+            x = data[n] if mode == "row" else np.ascontiguousarray(data[n].T).T  # keys-major storage
+            spec.softmax_rows(x, n, cm, cs, 8)
+            cnt += x.size
+        el = time.perf_counter() - t0
+        if el >= min_seconds:
+            return cnt / el, el
+
+
+def cpu_pool_rate(min_seconds=1.0):
+    """Input elements/s of the reference's pooling model on the host (the
+    oracle's restatement of _pool2d_ref, _simulate.py:230-358) on the two
+    pools of the sweep, a sample of each."""
+    from oracle import spec
+    rng = np.random.default_rng(9)
+    xm = rng.integers(-256, 256, size=(64, 16, 28, 28)).astype(np.int64)
+    xg = rng.integers(-256, 256, size=(8, 1280, 7, 7)).astype(np.int64)
+    cnt, t0 = 0, time.perf_counter()
+    while True:
+        spec.pool_raw(xm, 2, 2, 2, 2, 0, 0, 1, 1, 14, 14, 0, 0, 0)
+        spec.pool_raw(xg, 7, 7, 1, 1, 0, 0, 1, 1, 1, 1, 1, 0, 0)
+        cnt += xm.size + xg.size
+        el = time.perf_counter() - t0
+        if el >= min_seconds:
+            return cnt / el, el
+
+
+def vector_sweeps(torch, ops, dev, stream, flush, args, rank=0, world=1):
+    """configs[1] (b) VectorOP Add / Mul / Div with a broadcast operand
+    (outer x size, stride 0) and fused SiLU / GELU-erf / GELU-tanh, and (c)
+    the softmax unit on rows of 128 / 1024 / 4096 in row and keys-major
+    modes; plus the pooling unit on the configs' pools.  Every job is timed
+    alone (a CUDA graph of the one job, the L2 flushed before each replay,
+    median of the steps); GB/s over the algorithmic bytes (operands read
+    once, outputs written once, a stride-0 operand counted once).  The
+    config's 4M-element VectorOP jobs last a few microseconds, so the same
+    jobs on 64M elements (inputs far above L2) give the HBM roofline; the
+    softmax and pool jobs run on inputs above 100 MB.  The CPU rate of the
+    reference's method on a bounded sample is reported beside each."""
+    with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as fh:
+        hbm = float(json.load(fh).get("hbm_gbs") or 6650.0)
     gen = torch.Generator(device=dev)
     gen.manual_seed(99)
-    N = 1 << 22
-    size, outer = 1024, N // 1024
-    out = {}
-    with torch.cuda.stream(stream):
-        a = torch.randint(-256, 256, (N,), dtype=torch.int16, device=dev, generator=gen)
-        b = torch.randint(-256, 256, (size,), dtype=torch.int16, device=dev, generator=gen)
-        b = torch.where(b == 0, torch.ones_like(b), b)
-        c = torch.empty(N, dtype=torch.int16, device=dev)
     jobs = [(op, act) for op in (0, 2, 3) for act in (4, 5, 6)]
-
-    def vop_all():
+    out = {"hbm_peak_gbs": hbm}
+    for tag, N in (("vectorop", 1 << 22), ("vectorop_64M", 1 << 26)):
+        size, outer = 1024, N // 1024
+        with torch.cuda.stream(stream):
+            a = torch.randint(-256, 256, (N,), dtype=torch.int16, device=dev, generator=gen)
+            b = torch.randint(-256, 256, (size,), dtype=torch.int16, device=dev, generator=gen)
+            b = torch.where(b == 0, torch.ones_like(b), b)
+            c = torch.empty(N, dtype=torch.int16, device=dev)
+        per = {}
         for op, act in jobs:
-            ops.vectorop(a, b, c, size=size, op=op, outer=outer, a_inc=size, b_inc=0, act=act)
-    g = torch.cuda.CUDAGraph()
-    with torch.cuda.stream(stream):
-        vop_all()
-    torch.cuda.synchronize()
-    with torch.cuda.graph(g, stream=stream):
-        vop_all()
-    t = _time_graph(torch, stream, flush, g, args)
-    vbytes = len(jobs) * (4 * N + 2 * size)
-    out["vectorop"] = {"jobs": "ADD/MUL/DIV x SiLU/GELU/GELU-tanh, 4M elem, b broadcast (outer 4096 x size 1024)",
-                       "ms": round(t, 4), "GB/s": round(vbytes / (t * 1e-3) / 1e9, 1),
-                       "bytes_per_elem": 4, "G_elem/s": round(len(jobs) * N / (t * 1e-3) / 1e9, 2)}
-    from cormorant_b200 import ops as o  # noqa: F401
+            nm = f"{('add', '', 'mul', 'div')[op]}_{('', '', '', '', 'silu', 'gelu', 'gelu_tanh')[act]}"
+            per[nm] = _time_job(torch, stream, flush, lambda op=op, act=act: ops.vectorop(
+                a, b, c, size=size, op=op, outer=outer, a_inc=size, b_inc=0, act=act), args)
+        t = sum(per.values())
+        vbytes = len(jobs) * (4 * N + 2 * size)
+        gbs = vbytes / (t * 1e-3) / 1e9
+        out[tag] = {"jobs": f"ADD/MUL/DIV x SiLU/GELU/GELU-tanh, {N >> 20}M elem, b broadcast "
+                            f"(outer {outer} x size {size}, b_inc 0)",
+                    "ms": round(t, 4), "GB/s": round(gbs, 1), "frac_of_measured_hbm": round(gbs / hbm, 3),
+                    "bytes_per_elem": 4, "G_elem/s": round(len(jobs) * N / (t * 1e-3) / 1e9, 2),
+                    "ms_per_job": {k: round(v, 4) for k, v in per.items()}}
+        del a, b, c
     cm, cs = 12102203, 19
     smx = {}
+    N = 1 << 26
+    with torch.cuda.stream(stream):
+        x = torch.randint(-2048, 2048, (N,), dtype=torch.int16, device=dev, generator=gen)
+        p = torch.empty(N, dtype=torch.int16, device=dev)
     for n in (128, 1024, 4096):
         rows = N // n
-        with torch.cuda.stream(stream):
-            x = torch.randint(-2048, 2048, (N,), dtype=torch.int16, device=dev, generator=gen)
-            p = torch.empty(N, dtype=torch.int16, device=dev)
         for mode in ("row", "col"):
             if mode == "row":
-                fn = lambda: ops.vectorop(x, None, p, size=n, op=10, outer=rows, a_inc=n, b_inc=n, smx_cm=cm,  # noqa
-                                          smx_cfg=cs | (8 << 8), smx_mask=n)
+                fn = lambda n=n, rows=rows: ops.vectorop(x, None, p, size=n, op=10, outer=rows, a_inc=n, b_inc=n,  # noqa
+                                                         smx_cm=cm, smx_cfg=cs | (8 << 8), smx_mask=n)
             else:  # keys-major: n keys x rows queries
-                fn = lambda: ops.vectorop(x, None, p, size=n, op=11, outer=rows, a_inc=rows, b_inc=n,  # noqa
-                                          smx_cm=cm, smx_cfg=cs | (8 << 8), smx_mask=n)
-            with torch.cuda.stream(stream):
-                fn()
-            torch.cuda.synchronize()
-            g2 = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(g2, stream=stream):
-                fn()
-            t2 = _time_graph(torch, stream, flush, g2, args)
-            smx[f"{mode}{n}"] = {"ms": round(t2, 4), "GB/s": round(4 * N / (t2 * 1e-3) / 1e9, 1)}
-    out["softmax"] = smx
+                fn = lambda n=n, rows=rows: ops.vectorop(x, None, p, size=n, op=11, outer=rows, a_inc=rows,  # noqa
+                                                         b_inc=n, smx_cm=cm, smx_cfg=cs | (8 << 8), smx_mask=n)
+            t2 = _time_job(torch, stream, flush, fn, args)
+            gbs = 4 * N / (t2 * 1e-3) / 1e9
+            smx[f"{mode}{n}"] = {"ms": round(t2, 4), "GB/s": round(gbs, 1), "frac_of_measured_hbm": round(gbs / hbm, 3)}
+    out["softmax"] = {"elements_per_job": N, "bytes_per_elem": 4, "jobs": smx}
+    del x, p
+    pools = {}
+    for tag, (B, C, H, W, ph, st, oh, pt) in (("maxpool2x2_s2_16x28x28_b4096", (4096, 16, 28, 28, 2, 2, 14, 0)),
+                                               ("gap_1280x7x7_b256", (256, 1280, 7, 7, 7, 1, 1, 1))):
+        with torch.cuda.stream(stream):
+            xin = torch.randint(-256, 256, (B * C * H * W,), dtype=torch.int16, device=dev, generator=gen)
+            y = torch.empty(B * C * oh * oh + 8, dtype=torch.int16, device=dev)
+        fn = lambda xin=xin, y=y, B=B, C=C, H=H, W=W, ph=ph, st=st, oh=oh, pt=pt: ops.pool(  # noqa
+            xin, y, batch=B, channels=C, in_h=H, in_w=W, out_h=oh, out_w=oh, pool_h=ph, pool_w=ph, stride_h=st,
+            stride_w=st, pool_type=pt)
+        tp = _time_job(torch, stream, flush, fn, args)
+        pb = 2 * B * C * (H * W + oh * oh)
+        gbs = pb / (tp * 1e-3) / 1e9
+        pools[tag] = {"ms": round(tp, 4), "GB/s": round(gbs, 1), "frac_of_measured_hbm": round(gbs / hbm, 3),
+                      "bytes": pb}
+        del xin, y
+    out["pool"] = pools
+    if rank == 0 and world == 1 and not args.no_cpu:
+        r, el = cpu_vectorop_rate(jobs, 1024, 512)
+        out["vectorop"]["cpu_baseline"] = {"value": round(r * 4 / 1e9, 4), "unit": "GB/s", "G_elem/s": round(r / 1e9, 5),
+                                           "cores": 1, "kind": "port",
+                                           "sample": "the 9 jobs on 512 x 1024 elements, repeated to %.1f s" % el}
+        r, el = cpu_softmax_rate([(n, md) for n in (128, 1024, 4096) for md in ("row", "col")])
+        out["softmax"]["cpu_baseline"] = {"value": round(r * 4 / 1e9, 4), "unit": "GB/s", "G_elem/s": round(r / 1e9, 5),
+                                          "cores": 1, "kind": "port",
+                                          "sample": "the 6 cases on 2^20 elements each, repeated to %.1f s" % el}
+        r, el = cpu_pool_rate()
+        out["pool"]["cpu_baseline"] = {"value": round(r * 2 / 1e9, 4), "unit": "GB/s (input bytes)",
+                                       "G_elem/s": round(r / 1e9, 5), "cores": 1, "kind": "port",
+                                       "sample": "64 x 16 x 28 x 28 MaxPool and 8 x 1280 x 7 x 7 GAP, repeated to "
+                                                 "%.1f s" % el}
     return out
+
+
+LLAMA_GOLDEN = os.path.join(ROOT, "tests", "golden", "llama_full_s{}.npz")
+
+
+def _crc16(a) -> int:
+    import zlib
+    return zlib.crc32(np.ascontiguousarray(np.asarray(a, np.int64).astype("<i2")).tobytes())
+
+
+def _verify_units(torch, pg, world, rank, unit_out, check):
+    """Each rank's first unit (its raw outputs on the device, as int32)
+    gathered to rank 0, where ``check(r, raw)`` compares it with the CPU
+    oracle's output for that rank's unit (True / False, or None when not
+    checked)."""
+    got = _gather_to_root(torch, pg, world, rank, unit_out.to(torch.int32).reshape(-1).contiguous())
+    if rank != 0:
+        return None
+    res = [check(r, g.cpu().numpy().astype(np.int64)) for r, g in enumerate(got)]
+    done = [x for x in res if x is not None]
+    return {"units_checked": len(done), "mismatching_units": sum(1 for x in done if not x),
+            "ranks_checked": [r for r, x in enumerate(res) if x is not None]}
 
 
 def bench_models(torch, dev, stream, flush, args, world, rank, pg):
     """configs[0] (MNIST CNN), configs[2] (MobileNetV2-1.0, 224x224, batch 256
     sharded over the ranks) and configs[3] (BERT-base encoder, 64 sequences of
-    384 tokens sharded over the ranks): GpuSimulator forward passes on raw
-    int16 inputs, replayed as CUDA graphs; images/s or tokens/s over all
-    ranks, int16 GMAC/s.  On rank 0 at N = 1 the CPU oracle's forward pass of
-    one image / one sequence is timed beside it."""
-    import numpy as np
-
+    384 tokens sharded over the ranks), and configs[4]'s prefill: GpuSimulator
+    forward passes on raw int16 inputs, replayed as CUDA graphs; images/s or
+    tokens/s over all ranks, int16 GMAC/s.  Rank r runs units [r B, (r + 1) B)
+    of the configuration's seeded input set.  After timing, every rank's first
+    unit is gathered to rank 0 and compared with the CPU oracle's output for
+    that unit (the Llama prefill with the oracle's committed golden); on rank
+    0 at N = 1 the oracle's forward pass of one unit is timed too."""
     from cormorant_b200 import workloads as WL
     from cormorant_b200.simulator import GpuSimulator
+    from oracle import graph as og
     out = {}
-    cases = [("mnist_b1", "images", lambda b: WL.mnist(seed=1, batch=b), 1),
-             ("mnist_b4096", "images", lambda b: WL.mnist(seed=1, batch=b), 4096),
-             ("mobilenet_v2_224", "images", lambda b: WL.mobilenet_v2(seed=3, batch=b, res=224), max(1, 256 // world)),
-             ("bert_base_384", "tokens", lambda b: WL.bert_base(seed=4, batch=b, seq=384), max(1, 64 // world)),
-             ("llama360m_prefill512", "tokens", lambda b: WL.llama_prefill(seed=5, batch=b, seq=512),
+    cases = [("mnist_b1", "images", lambda b, f: WL.mnist(seed=1, batch=b, first=f), 1),
+             ("mnist_b4096", "images", lambda b, f: WL.mnist(seed=1, batch=b, first=f), 4096),
+             ("mobilenet_v2_224", "images", lambda b, f: WL.mobilenet_v2(seed=3, batch=b, res=224, first=f),
+              max(1, 256 // world)),
+             ("bert_base_384", "tokens", lambda b, f: WL.bert_base(seed=4, batch=b, seq=384, first=f),
+              max(1, 64 // world)),
+             ("llama360m_prefill512", "tokens", lambda b, f: WL.llama_prefill(seed=5, batch=b, seq=512, first=f),
               max(1, 64 // world))]
     seq_of = {"bert_base_384": 384, "llama360m_prefill512": 512}
     if not args.models or "llama360m_decode128" in args.models.split(","):
-        out["llama360m_decode128"] = bench_llama_decode(torch, dev, stream, flush, args, world, pg)
+        out["llama360m_decode128"] = bench_llama_decode(torch, dev, stream, flush, args, world, rank, pg)
     for name, unit, build, batch in cases:
         if args.models and name not in args.models.split(","):
             continue
-        g, feeds, macs_unit = build(batch)
+        g, feeds, macs_unit = build(batch, rank * batch)
         units = batch * seq_of.get(name, 1)
         sim = GpuSimulator(g, device=dev)
         keep = [t.onnx_name for t in g.output_tensors]
@@ -489,7 +692,7 @@ def bench_models(torch, dev, stream, flush, args, world, rank, pg):
         rate = world * units / (ms * 1e-3)
         out[name] = {"batch_per_gpu": batch, "ms_per_batch": round(ms, 4), f"{unit}_per_s": round(rate, 1),
                      "GMAC/s": round(rate * macs_unit / 1e9, 1), f"mmac_per_{unit[:-1]}": round(macs_unit / 1e6, 2),
-                     "nodes": len(g.nodes)}
+                     "nodes": len(g.nodes), "units_per_rank": f"[rank * {batch}, (rank + 1) * {batch})"}
         if args.detail:  # per-kernel device time of one eager pass (events around each launch)
             from cormorant_b200 import ops
             ops.profile_read()
@@ -500,6 +703,31 @@ def bench_models(torch, dev, stream, flush, args, world, rank, pg):
             prof = ops.profile_read()
             out[name]["kernels"] = {k: {"launches": v[0], "ms": round(v[1], 4)}
                                     for k, v in sorted(prof.items(), key=lambda kv: -kv[1][1])}
+        # verification: each rank's first unit against the CPU oracle on rank 0
+        ot = g.output_tensors[0]
+        per_unit = ot.numel // batch
+        unit_out = res[ot.onnx_name][:per_unit]
+        cpu_s = {}
+
+        def check(r, got, name=name, build=build, batch=batch):
+            first = r * batch
+            if name.startswith("llama"):
+                path = LLAMA_GOLDEN.format(first)
+                if not os.path.exists(path):
+                    return None
+                return _crc16(got) == int(np.load(path)["crc_prefill_logits"][0])
+            if name == "bert_base_384" and r not in (0, world - 1):
+                return None  # seconds of CPU per sequence: the first and the last rank's units
+            if name == "mnist_b4096" and r:
+                return None
+            g1, f1, _ = build(1, first)
+            t0 = time.perf_counter()
+            ref = og.forward(g1, {k: np.asarray(v) for k, v in f1.items()})
+            cpu_s.setdefault(r, time.perf_counter() - t0)
+            return bool(np.array_equal(got, ref[g1.output_tensors[0].onnx_name].reshape(-1)))
+        out[name]["parity"] = _verify_units(torch, pg, world, rank, unit_out, check)
+        if rank == 0 and world == 1 and not args.no_cpu and 0 in cpu_s and name != "mnist_b4096":
+            out[name][f"cpu_oracle_{unit}_per_s"] = round(seq_of.get(name, 1) / cpu_s[0], 3)
         del graph, res, sim, raw, dev_states
         torch.cuda.empty_cache()
         if rank == 0 and world == 1 and not args.no_cpu and name.startswith("llama"):
@@ -515,29 +743,23 @@ def bench_models(torch, dev, stream, flush, args, world, rank, pg):
             el = (time.perf_counter() - t0) * 32
             out[name]["cpu_oracle_tokens_per_s"] = round(64 / el, 4)
             out[name]["cpu_oracle_sample"] = "1 layer x 64 tokens, x32 layers (extrapolated)"
-        elif rank == 0 and world == 1 and not args.no_cpu and name != "mnist_b4096":
-            from oracle import graph as og
-            g1, f1, _ = build(1)
-            t0 = time.perf_counter()
-            og.forward(g1, {k: np.asarray(v) for k, v in f1.items()})
-            el = time.perf_counter() - t0
-            out[name][f"cpu_oracle_{unit}_per_s"] = round(seq_of.get(name, 1) / el, 3)
     return out
 
 
-def bench_llama_decode(torch, dev, stream, flush, args, world, pg, steps=128):
-    """configs[4]'s decode: after the 512-token prefill of 64 / N sequences,
-    ``steps`` greedy decode steps (pos 512 .. 639): per step the device greedy
-    step (argmax + embedding row) and one decode-step pass (the host softmax
-    on the device), each captured as its own CUDA graph (the key count and
-    the cache row are registers of the step); a timed step replays all of
-    them.  Tokens/s over all ranks."""
-    import numpy as np
-
+def bench_llama_decode(torch, dev, stream, flush, args, world, rank, pg, steps=128):
+    """configs[4]'s decode: after the 512-token prefill of 64 / N sequences
+    (rank r: sequences [r B, (r + 1) B)), ``steps`` greedy decode steps (pos
+    512 .. 639): per step the device greedy step (argmax + embedding row) and
+    one decode-step pass (the host softmax on the device), each captured as
+    its own CUDA graph (the key count and the cache row are registers of the
+    step); a timed step replays all of them.  Tokens/s over all ranks.  After
+    timing, each rank's first sequence (its greedy ids and last logits) is
+    gathered to rank 0 and compared with the CPU oracle's golden for that
+    sequence."""
     from cormorant_b200 import workloads as WL
     from cormorant_b200.llm_runner import LlamaRunner
     B = max(1, 64 // world)
-    m = WL.LlamaModel(seed=5, batch=B, seq=512)
+    m = WL.LlamaModel(seed=5, batch=B, seq=512, first=rank * B)
     r = LlamaRunner(m, device=dev)
     ids = torch.empty((steps, B), dtype=torch.int32, device=dev)
     with torch.cuda.stream(stream):
@@ -569,6 +791,20 @@ def bench_llama_decode(torch, dev, stream, flush, args, world, pg, steps=128):
            "GMAC/s": round(rate * macs / 1e9, 1), "mmac_per_token": round(macs / 1e6, 2),
            "graph_nodes_per_step": len(m.decode_graph.nodes),
            "first_ids": ids[0, :4].cpu().tolist()}
+    # verification: every replay runs the same steps over the caches the prefill
+    # left (a step's cache row is written before it is read), so the ids and the
+    # last logits are those of a prefill and 128 greedy steps
+    torch.cuda.synchronize()
+    mine = torch.cat([ids[:, 0].to(torch.int64), lg[:m.vocab].to(torch.int64)])
+
+    def check(rr, got):
+        path = LLAMA_GOLDEN.format(rr * B)
+        if not os.path.exists(path):
+            return None
+        z = np.load(path)
+        return bool(np.array_equal(got[:steps], z["ids"][:steps]) and
+                    _crc16(got[steps:]) == int(z["crc_step_logits"][steps - 1]))
+    out["parity"] = _verify_units(torch, pg, world, rank, mine, check)
     if args.detail:  # per-kernel device time of one eager decode step
         from cormorant_b200 import ops
         ops.profile_read()
