@@ -430,7 +430,7 @@ def sweep_parity(torch, problems, bufs, dev, rank, world, pg):
         subs = sampled.gather_t(A, B, Cc, b, m, k, n, idx)
         parts += [t.reshape(-1) for t in subs]
         shapes.append(tuple(tuple(t.shape) for t in subs))
-    got = _gather_to_root(torch, pg, world, rank, torch.cat(parts).contiguous())
+    got = _gather_to_root(torch, pg, world, rank, torch.cat(parts).to(torch.int32))  # no int16 collectives
     if rank != 0:
         return None
     checked = bad = 0
