@@ -90,7 +90,6 @@ class ExponentTable:
         return expand_exp(entry, n, key)
 
 
-
 def _kv_group(n_heads: int, groups: int) -> np.ndarray:
     """The KV group each of ``n_heads`` query heads reads (consecutive runs)."""
     return np.arange(n_heads) // (n_heads // groups)
