@@ -454,31 +454,83 @@ __global__ void __launch_bounds__(256, 2) ro_norm16(RoArgs q) {
   const uint64_t rows = (uint64_t)q.c1 * q.c2;
   const uint64_t warp0 = ((uint64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const uint64_t nwarps = ((uint64_t)gridDim.x * blockDim.x) >> 5;
+  auto row_in = [&](uint64_t row) {
+    return q.a + (uint64_t)(uint32_t)(row / q.c1) * q.a_s2 + (uint64_t)(uint32_t)(row % q.c1) * q.a_s1;
+  };
+  // the next row of this warp is loaded while the current one is reduced and
+  // written (its loads stay in flight across the iteration)
+  constexpr bool PF = NW_PER <= 8;  // (16 words per lane: no registers to spare for a second row)
+  int4 xn[NW_PER];
+  if (PF && warp0 < rows) {
+    const uint8_t* ra = row_in(warp0);
+#pragma unroll
+    for (int k = 0; k < NW_PER; k++) {
+      const uint32_t w = lane + 32u * k;
+      xn[k] = w < words ? *(const int4*)(ra + 16ull * w) : make_int4(0, 0, 0, 0);
+    }
+  }
   for (uint64_t row = warp0; row < rows; row += nwarps) {
     const uint32_t i1 = (uint32_t)(row % q.c1), i2 = (uint32_t)(row / q.c1);
-    const uint8_t* ra = q.a + (uint64_t)i2 * q.a_s2 + (uint64_t)i1 * q.a_s1;
     uint8_t* rc = q.c + (uint64_t)i2 * q.c_s2 + (uint64_t)i1 * q.c_s1;
     int4 xv[NW_PER];
-    long long s1 = 0, xmax = AK ? INT32_MIN : -32768, xmin = AK ? INT32_MAX : 32767;
+    if (PF) {
+#pragma unroll
+      for (int k = 0; k < NW_PER; k++) xv[k] = xn[k];
+      if (row + nwarps < rows) {
+        const uint8_t* rn = row_in(row + nwarps);
+#pragma unroll
+        for (int k = 0; k < NW_PER; k++) {
+          const uint32_t w = lane + 32u * k;
+          if (w < words) xn[k] = *(const int4*)(rn + 16ull * w);
+        }
+      }
+    } else {
+      const uint8_t* ra = row_in(row);
+#pragma unroll
+      for (int k = 0; k < NW_PER; k++) {
+        const uint32_t w = lane + 32u * k;
+        xv[k] = w < words ? *(const int4*)(ra + 16ull * w) : make_int4(0, 0, 0, 0);
+      }
+    }
+    long long s1 = 0;
+    int32_t xmax = AK ? INT32_MIN : -32768, xmin = AK ? INT32_MAX : 32767;
     long long s2 = 0;           // int16 rows: every partial sum < 2^42
     unsigned __int128 s2w = 0;  // int32 rows: squares up to 2^62
 #pragma unroll
     for (int k = 0; k < NW_PER; k++) {
       const uint32_t w = lane + 32u * k;
-      xv[k] = make_int4(0, 0, 0, 0);
       if (w < words) {
-        xv[k] = *(const int4*)(ra + 16ull * w);
+        if (AK) {
 #pragma unroll
-        for (int e = 0; e < (int)EPW; e++) {
-          const int32_t xi = AK ? ((const int32_t*)&xv[k])[e] : (int32_t)((const int16_t*)&xv[k])[e];
-          const long long x = xi;
-          s1 += x;
-          if (AK)
+          for (int e = 0; e < (int)EPW; e++) {
+            const int32_t xi = ((const int32_t*)&xv[k])[e];
+            s1 += xi;
             s2w += (unsigned long long)((long long)xi * xi);  // a 32 x 32 -> 64-bit product
-          else
-            s2 += (long long)(xi * xi);  // each square < 2^30
-          xmax = max(xmax, x);
-          xmin = min(xmin, x);
+            xmax = max(xmax, xi);
+            xmin = min(xmin, xi);
+          }
+        } else {
+          // int16 pairs: sums of two values and two squares in 32 bits (< 2^31),
+          // the extremes by packed maxima / minima
+          const uint32_t pr[4] = {(uint32_t)xv[k].x, (uint32_t)xv[k].y, (uint32_t)xv[k].z, (uint32_t)xv[k].w};
+          int32_t ps = 0;
+          uint32_t pq = 0, pmax = 0x80008000u, pmin = 0x7FFF7FFFu;
+#pragma unroll
+          for (int t = 0; t < 4; t++) {
+            const int32_t a0 = (int32_t)(int16_t)(pr[t] & 0xFFFFu), a1 = (int32_t)pr[t] >> 16;
+            ps += a0 + a1;
+            pq += (uint32_t)(a0 * a0) + (uint32_t)(a1 * a1);  // 8 squares < 2^33: kept below in 64 bits
+            pmax = __vmaxs2(pmax, pr[t]);
+            pmin = __vmins2(pmin, pr[t]);
+            if (t == 1) {  // four squares < 2^32: flush before the sum can wrap
+              s2 += pq;
+              pq = 0;
+            }
+          }
+          s1 += ps;
+          s2 += pq;
+          xmax = max(xmax, max((int32_t)(int16_t)(pmax & 0xFFFFu), (int32_t)pmax >> 16));
+          xmin = min(xmin, min((int32_t)(int16_t)(pmin & 0xFFFFu), (int32_t)pmin >> 16));
         }
       }
     }
@@ -506,8 +558,11 @@ __global__ void __launch_bounds__(256, 2) ro_norm16(RoArgs q) {
     // the whole row on the 64-bit path when every |P1| < 2^31 (bounded by
     // the extreme A), Bq' << bq_sh < 2^61 and every sh_c >= 1: no branch per
     // element; the rare other rows element by element in 128 bits
-    const long long amax = max(llabs(nn * xmax - off), llabs(nn * xmin - off));
+    const long long amax = max(llabs(nn * (long long)xmax - off), llabs(nn * (long long)xmin - off));
     const bool row_fast = small_bq && s_scmin >= 1 && (((__int128)amax * (__int128)Rm) >> shp) < (1ll << 31) - 1;
+    // A Rm = (n Rm) x - S1 Rm exactly: n Rm < 2^44 and |S1 Rm| < 2^60 for int16
+    // rows (int32 rows, RMS: Rm x, |x Rm| < 2^63)
+    const long long alpha = nn * (long long)Rm, beta = off * (long long)Rm;
 #pragma unroll
     for (int k = 0; k < NW_PER; k++) {
       const uint32_t w = lane + 32u * k;
@@ -518,13 +573,11 @@ __global__ void __launch_bounds__(256, 2) ro_norm16(RoArgs q) {
         for (int e = 0; e < (int)EPW; e++) {
           const uint32_t slot = bcast ? 0u : (uint32_t)e * words + w;
           const int32_t xi = AK ? ((const int32_t*)&xv[k])[e] : (int32_t)((const int16_t*)&xv[k])[e];
-          // int32 rows (RMS): A = x; |A Rm| < 2^63
-          const long long A = AK ? (long long)xi : nn * xi - off;
-          const long long P1 = (AK ? (long long)xi * (long long)(uint32_t)Rm : A * (long long)Rm) >> shp;
+          const long long P1 = (alpha * xi - beta) >> shp;
           const long long v = (long long)(int32_t)P1 * s_g[slot] + s_bq[slot];  // |P1| < 2^31 on this path
           const int sc = s_sc[slot];
-          const long long qv = v >> sc, rr = v - (qv << sc), half = 1ll << (sc - 1);
-          const long long y = qv + ((rr > half) | ((rr == half) & (qv & 1)));
+          // round half to even of v / 2^sc: v + 2^(sc-1) - 1 + (the quotient's low bit)
+          const long long y = (v + ((1ll << (sc - 1)) - 1) + ((v >> sc) & 1)) >> sc;
           os[e] = (int16_t)min(max(y, -32768ll), 32767ll);
         }
       } else {

@@ -131,6 +131,8 @@ struct SmxArgs {
   uint32_t cm, cs, fp, valid0, period;
   const int32_t* tab;
   uint32_t cm8, csm8;  // cm << 8 and cs - 8 (the 32-bit path, 8 <= cs <= 39)
+  uint32_t dm, dm2;    // the first d = m - x whose e is 0 (> 65535: none), dm in both halves
+  uint32_t tabn;       // int32 entries of the shared table ahead of the column kernel's staging
 };
 
 __device__ __forceinline__ uint32_t smx_valid(uint32_t q, const SmxArgs& p) {
@@ -206,22 +208,58 @@ __device__ __forceinline__ int16_t smx_pq(uint32_t e, uint32_t R, uint64_t rnd, 
   return (int16_t)min(q, 32767u);
 }
 
+// e of a score d = m - x below the row maximum.  d < 2^16 and y = floor(d Cm
+// / 2^Cs) grows with d, so e is 0 for every d >= dm, the first d whose y
+// reaches 17 << 12 (the host computes dm).  When dm is small (Q8.8 registers:
+// dm = 3017) every e a job can produce is tabulated once per CTA in shared
+// memory, s_e[d] for d < dm and s_e[dm] = 0, and an element's e is one
+// packed subtract, one packed clamp and one shared-memory read (ET); the
+// arithmetic above is the other path.
+constexpr uint32_t kSmxEMax = 8192;  // largest dm tabulated (32 KB of shared memory)
+
+template <bool FC>
+__device__ __forceinline__ void smx_fill_etab(int32_t* s_e, const SmxArgs& p, int nt) {
+  for (uint32_t d = threadIdx.x; d <= p.dm; d += nt)
+    s_e[d] = d < p.dm ? (int32_t)smx_e<FC>((int32_t)d, 0, p, p.tab) : 0;
+}
+
+// e of the two packed int16 scores of xw (low, high) against the packed row
+// maximum m2: (m - x) mod 2^16 is m - x (0 <= m - x < 2^16), clamped to dm.
+template <bool ET, bool FC>
+__device__ __forceinline__ void smx_e2(uint32_t m2, uint32_t xw, int32_t m, const SmxArgs& p, const int32_t* s_t,
+                                       uint32_t& e0, uint32_t& e1) {
+  if (ET) {
+    const uint32_t di = __vminu2(__vsub2(m2, xw), p.dm2);
+    e0 = (uint32_t)s_t[di & 0xFFFFu];
+    e1 = (uint32_t)s_t[di >> 16];
+  } else {
+    e0 = smx_e<FC>(m, (int32_t)(int16_t)(xw & 0xFFFFu), p, s_t);
+    e1 = smx_e<FC>(m, (int32_t)(int16_t)(xw >> 16), p, s_t);
+  }
+}
+
 // Row mode, GROUP threads per row (16 / 32: a part of a warp per row; 256 /
 // 1024: a CTA per row), PER elements per thread held in registers as PER / 8
 // runs of 8 consecutive elements (16-byte loads and stores where the row
-// allows).  The TAB is copied into shared memory once per CTA; CTAs then walk
-// row groups.
-template <int GROUP, int PER, bool FC>
+// allows), as packed int16 pairs: the row maximum by packed maxima, e by the
+// table (ET) or the arithmetic, every masked element's e forced to 0 per
+// 8-element run (a run wholly inside the valid length takes no mask), so the
+// P of a masked element is 0 with no further test.  The TAB (or the e table)
+// is built in shared memory once per CTA; CTAs then walk row groups.
+template <int GROUP, int PER, bool FC, bool ET>
 __global__ void __launch_bounds__(GROUP >= 256 ? GROUP : 256) smx_rows(SmxArgs p) {
   corm_pdl_wait();
   corm_pdl_trigger();
   constexpr int NT = GROUP >= 256 ? GROUP : 256;
   constexpr int ROWS_PER_CTA = NT / GROUP;
   constexpr int V = PER / 8;
-  __shared__ int32_t s_tab[4096];
-  __shared__ int32_t s_max[32];
+  extern __shared__ int32_t s_t[];  // ET: e by d (dm + 1 entries); else the TAB (4096)
+  __shared__ uint32_t s_max[32];
   __shared__ uint32_t s_sum[32];
-  for (int i = threadIdx.x; i < 4096; i += NT) s_tab[i] = __ldg(p.tab + i);
+  if (ET)
+    smx_fill_etab<FC>(s_t, p, NT);
+  else
+    for (int i = threadIdx.x; i < 4096; i += NT) s_t[i] = __ldg(p.tab + i);
   __syncthreads();
   const int lane_in_group = threadIdx.x % GROUP;
   const int group = threadIdx.x / GROUP;
@@ -234,36 +272,55 @@ __global__ void __launch_bounds__(GROUP >= 256 ? GROUP : 256) smx_rows(SmxArgs p
     const uint32_t v = live ? smx_valid(row, p) : 0u;
     const int16_t* x = p.a + (size_t)row * p.a_inc;
     const bool xa = ((uintptr_t)x & 15) == 0;
-    int32_t xv[PER];
-    int32_t m = INT32_MIN;
+    uint32_t xp[PER / 2];  // packed pairs; masked elements hold INT16_MIN
+    uint32_t mx = 0x80008000u;
 #pragma unroll
     for (int q = 0; q < V; q++) {
       const uint32_t j0 = (q * GROUP + lane_in_group) * 8;
       if (live && xa && j0 + 8 <= v) {
-        alignas(16) int16_t t8[8];
-        *(int4*)t8 = __ldg((const int4*)(x + j0));
-#pragma unroll
-        for (int e = 0; e < 8; e++) xv[q * 8 + e] = t8[e];
+        const int4 w = __ldg((const int4*)(x + j0));
+        xp[4 * q] = (uint32_t)w.x;
+        xp[4 * q + 1] = (uint32_t)w.y;
+        xp[4 * q + 2] = (uint32_t)w.z;
+        xp[4 * q + 3] = (uint32_t)w.w;
       } else {
 #pragma unroll
-        for (int e = 0; e < 8; e++) xv[q * 8 + e] = (live && j0 + e < v) ? (int32_t)x[j0 + e] : INT32_MIN;
+        for (int e = 0; e < 8; e += 2) {
+          const uint32_t lo = (live && j0 + e < v) ? (uint32_t)(uint16_t)x[j0 + e] : 0x8000u;
+          const uint32_t hi = (live && j0 + e + 1 < v) ? (uint32_t)(uint16_t)x[j0 + e + 1] : 0x8000u;
+          xp[4 * q + e / 2] = lo | (hi << 16);
+        }
       }
 #pragma unroll
-      for (int e = 0; e < 8; e++) m = max(m, xv[q * 8 + e]);
+      for (int e = 0; e < 4; e++) mx = __vmaxs2(mx, xp[4 * q + e]);
     }
-    m = warp_reduce_max<(GROUP < 32 ? GROUP : 32)>(m);
+    mx = __vmaxs2(mx, __funnelshift_l(mx, mx, 16));  // both halves: the thread's maximum
+#pragma unroll
+    for (int o = (GROUP < 32 ? GROUP : 32) / 2; o > 0; o >>= 1) mx = __vmaxs2(mx, __shfl_xor_sync(0xffffffffu, mx, o));
     if (GROUP > 32) {
-      if ((threadIdx.x & 31) == 0) s_max[threadIdx.x >> 5] = m;
+      if ((threadIdx.x & 31) == 0) s_max[threadIdx.x >> 5] = mx;
       __syncthreads();
-      m = INT32_MIN;
-      for (int w = 0; w < GROUP / 32; w++) m = max(m, s_max[w]);
+      for (int w = 0; w < GROUP / 32; w++) mx = __vmaxs2(mx, s_max[w]);
     }
+    const int32_t m = (int32_t)(int16_t)(mx & 0xFFFFu);
+    uint32_t ev[PER];
     uint32_t S = 0;
 #pragma unroll
-    for (int t = 0; t < PER; t++) {  // xv becomes e (<= 65536) in place
-      const uint32_t j = ((t / 8) * GROUP + lane_in_group) * 8 + (t % 8);
-      xv[t] = (live && j < v) ? (int32_t)smx_e<FC>(m, xv[t], p, s_tab) : 0;
-      S += (uint32_t)xv[t];
+    for (int q = 0; q < V; q++) {
+      const uint32_t j0 = (q * GROUP + lane_in_group) * 8;
+      const bool whole = live && j0 + 8 <= v;
+#pragma unroll
+      for (int e = 0; e < 8; e += 2) {
+        uint32_t e0, e1;
+        smx_e2<ET, FC>(mx, xp[4 * q + e / 2], m, p, s_t, e0, e1);
+        if (!whole) {
+          e0 = (live && j0 + e < v) ? e0 : 0u;
+          e1 = (live && j0 + e + 1 < v) ? e1 : 0u;
+        }
+        ev[8 * q + e] = e0;
+        ev[8 * q + e + 1] = e1;
+        S += e0 + e1;
+      }
     }
 #pragma unroll
     for (int o = (GROUP < 32 ? GROUP : 32) / 2; o > 0; o >>= 1) S += __shfl_xor_sync(0xffffffffu, S, o);
@@ -282,12 +339,15 @@ __global__ void __launch_bounds__(GROUP >= 256 ? GROUP : 256) smx_rows(SmxArgs p
 #pragma unroll
     for (int q = 0; q < V; q++) {
       const uint32_t j0 = (q * GROUP + lane_in_group) * 8;
-      alignas(16) int16_t o8[8];
+      uint32_t o4[4];  // e = 0 (masked or beyond the row) gives P = 0
 #pragma unroll
-      for (int e = 0; e < 8; e++) o8[e] = (j0 + e < v) ? smx_pq<FC>((uint32_t)xv[q * 8 + e], R, rnd, psh) : (int16_t)0;
+      for (int e = 0; e < 4; e++)
+        o4[e] = (uint32_t)(uint16_t)smx_pq<FC>(ev[8 * q + 2 * e], R, rnd, psh) |
+                ((uint32_t)(uint16_t)smx_pq<FC>(ev[8 * q + 2 * e + 1], R, rnd, psh) << 16);
       if (oa && j0 + 8 <= lim) {
-        *(int4*)(out + j0) = *(int4*)o8;
+        *(int4*)(out + j0) = make_int4((int)o4[0], (int)o4[1], (int)o4[2], (int)o4[3]);
       } else {
+        const int16_t* o8 = (const int16_t*)o4;
 #pragma unroll
         for (int e = 0; e < 8; e++)
           if (j0 + e < lim) out[j0 + e] = o8[e];
@@ -359,15 +419,25 @@ __global__ void __launch_bounds__(256) smx_cols(SmxArgs p) {
 // into shared memory once per CTA).
 __device__ __forceinline__ uint32_t smx_tbase(uint32_t c, uint32_t KP) { return c * KP + 16u * (c >> 3); }
 
-template <int WPL, bool STORE_E, bool FC>
+// A packed pair of scores with the lanes at or past the valid length v set to
+// INT16_MIN (j: the low lane's key), so they never raise the maximum.
+__device__ __forceinline__ uint32_t smx_mask2(uint32_t w, uint32_t j, uint32_t v) {
+  if (j >= v) return 0x80008000u;
+  return j + 1 < v ? w : ((w & 0xFFFFu) | 0x80000000u);
+}
+
+template <int WPL, bool STORE_E, bool FC, bool ET>
 __global__ void __launch_bounds__(256) smx_cols_t(SmxArgs p) {
   corm_pdl_wait();
   corm_pdl_trigger();
   extern __shared__ __align__(16) uint8_t smx_sm[];
-  int32_t* s_tab = (int32_t*)smx_sm;
-  int16_t* s_x = (int16_t*)(s_tab + 4096);
+  int32_t* s_t = (int32_t*)smx_sm;  // ET: e by d; else the TAB
+  int16_t* s_x = (int16_t*)(s_t + p.tabn);
   const uint32_t KP = p.size + 8u;
-  for (int i = threadIdx.x; i < 4096; i += 256) s_tab[i] = __ldg(p.tab + i);
+  if (ET)
+    smx_fill_etab<FC>(s_t, p, 256);
+  else
+    for (int i = threadIdx.x; i < 4096; i += 256) s_t[i] = __ldg(p.tab + i);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint64_t rnd = 1ull << (39u - p.fp);
   const uint32_t psh = 40u - p.fp;
@@ -383,7 +453,7 @@ __global__ void __launch_bounds__(256) smx_cols_t(SmxArgs p) {
       tmax = t0 + qn >= p.period ? p.period - 1u : t0 + qn;
     }
     const uint32_t vmax = min(p.size, p.valid0 + tmax);
-    __syncthreads();  // the previous tile's reads (and the TAB copy) are done
+    __syncthreads();  // the previous tile's reads (and the table) are done
     for (uint32_t idx = threadIdx.x; idx < ((vmax + 1u) / 2u) * 4u; idx += 256u) {
       const uint32_t jp = idx >> 2, part = idx & 3u;
       if (q0 + 8u * part >= p.rows) continue;
@@ -404,37 +474,58 @@ __global__ void __launch_bounds__(256) smx_cols_t(SmxArgs p) {
     const bool live = q < p.rows;
     const uint32_t v = live ? smx_valid(q, p) : 0u;
     const int16_t* xs = s_x + smx_tbase(r, KP);
-    int4 xw[STORE_E ? WPL : 1];
-    int32_t m = INT32_MIN;
+    // every key word this lane reads, masked past v (INT16_MIN) so the
+    // maximum needs no test per key
+    auto word = [&](int k) -> uint4 {
+      const uint32_t j0 = 8u * (sl + 8u * k);
+      if (j0 >= v) return make_uint4(0x80008000u, 0x80008000u, 0x80008000u, 0x80008000u);
+      uint4 w = *(const uint4*)(xs + j0);  // j0 < v <= size: staged
+      if (j0 + 8u > v) {
+        w.x = smx_mask2(w.x, j0, v);
+        w.y = smx_mask2(w.y, j0 + 2u, v);
+        w.z = smx_mask2(w.z, j0 + 4u, v);
+        w.w = smx_mask2(w.w, j0 + 6u, v);
+      }
+      return w;
+    };
+    uint4 xw[STORE_E ? WPL : 1];
+    uint32_t mx = 0x80008000u;
 #pragma unroll(STORE_E ? WPL : 1)
     for (int k = 0; k < WPL; k++) {
-      const uint32_t j0 = 8u * (sl + 8u * k);
-      if (j0 >= v) break;  // masked keys: neither max nor e
-      const int4 w = j0 < p.size ? *(const int4*)(xs + j0) : make_int4(0, 0, 0, 0);
+      if (8u * (sl + 8u * k) >= v) break;
+      const uint4 w = word(k);
       if constexpr (STORE_E) xw[k] = w;
-      const int16_t* t8 = (const int16_t*)&w;
-#pragma unroll
-      for (int e = 0; e < 8; e++)
-        if (j0 + e < v) m = max(m, (int32_t)t8[e]);
+      mx = __vmaxs2(__vmaxs2(mx, w.x), __vmaxs2(__vmaxs2(w.y, w.z), w.w));
     }
-    m = warp_reduce_max<8>(m);
+    mx = __vmaxs2(mx, __funnelshift_l(mx, mx, 16));
+#pragma unroll
+    for (int o = 4; o > 0; o >>= 1) mx = __vmaxs2(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    const int32_t m = (int32_t)(int16_t)(mx & 0xFFFFu);
+    // e of the 8 keys of word k (0 past v)
+    auto e8 = [&](int k, const uint4& w, uint32_t* e) {
+      const uint32_t j0 = 8u * (sl + 8u * k);
+      const uint32_t pr[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+      for (int t = 0; t < 4; t++) smx_e2<ET, FC>(mx, pr[t], m, p, s_t, e[2 * t], e[2 * t + 1]);
+      if (j0 + 8u > v) {
+#pragma unroll
+        for (int t = 0; t < 8; t++) e[t] = j0 + t < v ? e[t] : 0u;
+      }
+    };
     uint32_t ev[STORE_E ? WPL * 8 : 1];
     uint32_t S = 0;
 #pragma unroll(STORE_E ? WPL : 1)
     for (int k = 0; k < WPL; k++) {
-      const uint32_t j0 = 8u * (sl + 8u * k);
-      if (j0 >= v) break;
-      int4 w;
+      if (8u * (sl + 8u * k) >= v) break;
+      uint32_t e[8];
       if constexpr (STORE_E)
-        w = xw[k];
+        e8(k, xw[k], e);
       else
-        w = j0 < p.size ? *(const int4*)(xs + j0) : make_int4(0, 0, 0, 0);
-      const int16_t* t8 = (const int16_t*)&w;
+        e8(k, word(k), e);
 #pragma unroll
-      for (int e = 0; e < 8; e++) {
-        const uint32_t ee = (j0 + e < v) ? smx_e<FC>(m, t8[e], p, s_tab) : 0u;
-        if constexpr (STORE_E) ev[k * 8 + e] = ee;
-        S += ee;
+      for (int t = 0; t < 8; t++) {
+        if constexpr (STORE_E) ev[k * 8 + t] = e[t];
+        S += e[t];
       }
     }
 #pragma unroll
@@ -448,28 +539,28 @@ __global__ void __launch_bounds__(256) smx_cols_t(SmxArgs p) {
       for (int k = 0; k < WPL; k++) {
         const uint32_t j0 = 8u * (sl + 8u * k);
         if (j0 >= lim) break;
-        int4 w;
-        if constexpr (STORE_E)
-          w = xw[k];
-        else
-          w = *(const int4*)(xs + j0);
-        const int16_t* t8 = (const int16_t*)&w;
-        alignas(16) int16_t o8[8];
+        uint32_t e[8];
+        if (j0 >= v) {
 #pragma unroll
-        for (int e = 0; e < 8; e++) {
-          uint32_t ee;
-          if constexpr (STORE_E)
-            ee = ev[k * 8 + e];
-          else
-            ee = (j0 + e < v) ? smx_e<FC>(m, t8[e], p, s_tab) : 0u;
-          o8[e] = (j0 + e < v) ? smx_pq<FC>(ee, R, rnd, psh) : (int16_t)0;
-        }
-        if (oa && j0 + 8 <= lim) {
-          *(int4*)(out + j0) = *(int4*)o8;
+          for (int t = 0; t < 8; t++) e[t] = 0u;
+        } else if constexpr (STORE_E) {
+#pragma unroll
+          for (int t = 0; t < 8; t++) e[t] = ev[k * 8 + t];
         } else {
+          e8(k, word(k), e);
+        }
+        uint32_t o4[4];  // e = 0 gives P = 0
 #pragma unroll
-          for (int e = 0; e < 8; e++)
-            if (j0 + e < lim) out[j0 + e] = o8[e];
+        for (int t = 0; t < 4; t++)
+          o4[t] = (uint32_t)(uint16_t)smx_pq<FC>(e[2 * t], R, rnd, psh) |
+                  ((uint32_t)(uint16_t)smx_pq<FC>(e[2 * t + 1], R, rnd, psh) << 16);
+        if (oa && j0 + 8 <= lim) {
+          *(int4*)(out + j0) = make_int4((int)o4[0], (int)o4[1], (int)o4[2], (int)o4[3]);
+        } else {
+          const int16_t* o8 = (const int16_t*)o4;
+#pragma unroll
+          for (int t = 0; t < 8; t++)
+            if (j0 + t < lim) out[j0 + t] = o8[t];
         }
       }
     }
@@ -481,10 +572,25 @@ unsigned smx_grid(uint64_t groups) { return (unsigned)(groups < 148u * 8u ? (gro
 
 template <int G, int P>
 void launch_rows(const SmxArgs& p, unsigned grid, unsigned threads, bool fc, cudaStream_t st) {
-  if (fc)
-    corm_launch_pdl(smx_rows<G, P, true>, dim3(grid), dim3(threads), 0, st, p);
+  const bool et = p.dm <= kSmxEMax;
+  const size_t smem = et ? ((size_t)p.dm + 1) * sizeof(int32_t) : 4096 * sizeof(int32_t);
+  if (et && fc)
+    corm_launch_pdl(smx_rows<G, P, true, true>, dim3(grid), dim3(threads), smem, st, p);
+  else if (et)
+    corm_launch_pdl(smx_rows<G, P, false, true>, dim3(grid), dim3(threads), smem, st, p);
+  else if (fc)
+    corm_launch_pdl(smx_rows<G, P, true, false>, dim3(grid), dim3(threads), smem, st, p);
   else
-    corm_launch_pdl(smx_rows<G, P, false>, dim3(grid), dim3(threads), 0, st, p);
+    corm_launch_pdl(smx_rows<G, P, false, false>, dim3(grid), dim3(threads), smem, st, p);
+}
+
+// The first d = m - x (0 <= d < 2^16) with floor(d Cm / 2^Cs) >= 17 << 12, so
+// e = 0 from there on; 65536 when no such d exists.
+uint32_t smx_dm(uint32_t cm, uint32_t cs) {
+  if (cm == 0) return 65536u;
+  const unsigned __int128 need = (unsigned __int128)(17u << 12) << cs;  // d Cm >= need
+  const unsigned __int128 d = (need + cm - 1) / cm;
+  return d > 65536u ? 65536u : (uint32_t)d;
 }
 
 int launch_softmax(const corm_vectorop_desc* d, cudaStream_t st, const corm::DeviceTables* tb) {
@@ -503,6 +609,8 @@ int launch_softmax(const corm_vectorop_desc* d, cudaStream_t st, const corm::Dev
   p.tab = tb->smx_tab;
   p.cm8 = p.cm << 8;
   p.csm8 = p.cs >= 8u ? p.cs - 8u : 0u;
+  p.dm = smx_dm(p.cm, p.cs);
+  p.dm2 = p.dm <= 0xFFFFu ? p.dm * 0x10001u : 0xFFFFFFFFu;
   const bool fc = p.cs >= 8u && p.cs <= 39u && 40u - p.fp < 32u;
   const bool col = d->op == 11;
   p.rows = col ? (d->outer & ~15u) : d->outer;
@@ -510,25 +618,33 @@ int launch_softmax(const corm_vectorop_desc* d, cudaStream_t st, const corm::Dev
   if (p.rows > 1 && p.b_inc < p.size)
     return corm::fail(CORM_EINVAL, "softmax: output rows overlap (b_inc %u < size %u)", p.b_inc, p.size);
   if (col && d->size % 8 == 0 && d->size <= 1024 && d->a_inc % 8 == 0 && !((uintptr_t)d->a & 15u)) {
-    const size_t smem = 4096 * sizeof(int32_t) + (32 * ((size_t)d->size + 8) + 16 * 4) * sizeof(int16_t);
+    const bool et = p.dm <= kSmxEMax;
+    p.tabn = et ? (p.dm + 1u + 3u) / 4u * 4u : 4096u;  // keeps the staging 16-byte aligned
+    const size_t smem = (size_t)p.tabn * sizeof(int32_t) + (32 * ((size_t)d->size + 8) + 16 * 4) * sizeof(int16_t);
     const uint32_t tiles = (p.rows + 31) / 32;
     const unsigned grid = tiles < 148u * 4u ? tiles : 148u * 4u;
-    auto launch = [&](auto kf, auto ks) {
-      cudaFuncSetAttribute(kf, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-      cudaFuncSetAttribute(ks, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-      if (fc)
-        corm_launch_pdl(kf, dim3(grid), dim3(256), smem, st, p);
-      else
-        corm_launch_pdl(ks, dim3(grid), dim3(256), smem, st, p);
+    auto launch = [&](auto k_fe, auto k_se, auto k_f, auto k_s) {
+      auto run = [&](auto kern) {
+        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        corm_launch_pdl(kern, dim3(grid), dim3(256), smem, st, p);
+      };
+      if (et && fc) run(k_fe);
+      else if (et) run(k_se);
+      else if (fc) run(k_f);
+      else run(k_s);
     };
+#define CORM_SMX_COLS(W, SE) \
+  launch(smx_cols_t<W, SE, true, true>, smx_cols_t<W, SE, false, true>, smx_cols_t<W, SE, true, false>, \
+         smx_cols_t<W, SE, false, false>)
     {
       corm::ProfScope prof_("smx_cols_t", st);
-      if (d->size <= 64) launch(smx_cols_t<1, true, true>, smx_cols_t<1, true, false>);
-      else if (d->size <= 128) launch(smx_cols_t<2, true, true>, smx_cols_t<2, true, false>);
-      else if (d->size <= 256) launch(smx_cols_t<4, true, true>, smx_cols_t<4, true, false>);
-      else if (d->size <= 512) launch(smx_cols_t<8, false, true>, smx_cols_t<8, false, false>);
-      else launch(smx_cols_t<16, false, true>, smx_cols_t<16, false, false>);
+      if (d->size <= 64) CORM_SMX_COLS(1, true);
+      else if (d->size <= 128) CORM_SMX_COLS(2, true);
+      else if (d->size <= 256) CORM_SMX_COLS(4, true);
+      else if (d->size <= 512) CORM_SMX_COLS(8, false);
+      else CORM_SMX_COLS(16, false);
     }
+#undef CORM_SMX_COLS
     return corm::cuda_status("softmax_cols");
   }
   if (col) {
