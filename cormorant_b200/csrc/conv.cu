@@ -388,6 +388,20 @@ ConvPlan plan_of(const corm_conv_desc* d) {
   return p;
 }
 
+// A 1 x 1 conv at stride 1 without padding, dense NCHW output, on 16-byte
+// aligned operands whose rows are whole 16-byte words (C and H W multiples of
+// 8): the GEMM form W x per image (the weight's board layout equals the
+// logical one when C is a multiple of 8).  A fused job may read a same-shaped
+// operand or a scalar (a per-channel operand would be per row here).
+bool pointwise_gemm(const corm_conv_desc* d, const corm::PostOp& post) {
+  const uint32_t P = d->out_h * d->out_w;
+  return !d->is_depthwise && d->kh == 1 && d->kw == 1 && d->stride_h == 1 && d->stride_w == 1 && d->pad_top == 0 &&
+         d->pad_left == 0 && d->out_h == d->in_h && d->out_w == d->in_w && d->in_ch % 8u == 0 && P % 8u == 0 &&
+         d->y_cn == 0 && (d->y_cs == 0 || d->y_cs == P) && !(((uintptr_t)d->x | (uintptr_t)d->weight) & 15u) &&
+         !((uintptr_t)d->y & 1u) && (post.op == corm::kPostNone || post.b_mode != 0) &&
+         (uint64_t)d->batch * d->in_ch * P < (1ull << 40);
+}
+
 int validate(const corm_conv_desc* d) {
   if (!d) return corm::fail(CORM_EINVAL, "corm_conv: null descriptor");
   if (d->kh == 0 || d->kw == 0 || d->kh > 7 || d->kw > 7)
@@ -505,6 +519,44 @@ int conv_impl(const corm_conv_desc* d, const corm::PostOp& post, cudaStream_t st
       corm_launch_pdl(conv_depthwise, dim3(corm_blocks(total, 256, 148u * 16u)), dim3(256), 0, st, a);
     }
     return corm::cuda_status("conv depthwise");
+  }
+  if (pointwise_gemm(d, post)) {
+    // a 1 x 1 conv at stride 1 is, per image, y[n] (M x P) = W (M x C) x[n] (C x P):
+    // the GEMM reads the int16 weight (K-major) and the image (MN-major) itself,
+    // no im2col and no weight split; the bias is per row (output channel)
+    corm::GemmJob j{};
+    j.rows = d->out_ch;
+    j.cols = P;
+    j.Kp = (d->in_ch + 15u) / 16u * 16u;
+    j.K = d->in_ch;
+    j.batch = d->batch;
+    j.a_planes = 1;
+    j.b_planes = d->batch;
+    j.b_mn = 1;
+    j.cols_p = (P + 15u) / 16u * 16u;
+    j.mode = 0;
+    j.out = d->y;
+    j.out_batch_stride = (uint64_t)d->out_ch * P;
+    j.ldc = P;
+    j.bias = a.bias;
+    j.bias_rows = a.bias ? 1u : 0u;
+    j.flags = d->flags;
+    j.post = post;
+    j.a16 = d->weight;
+    j.b16 = d->x;
+    j.a_bs16 = 0;
+    j.b_bs16 = (uint64_t)d->in_ch * P;
+    j.lda = d->in_ch;
+    j.ldb = P;
+    const size_t pb = corm::gemm_partial_bytes(j.rows, j.cols, j.Kp, j.batch);
+    if (pb) {
+      void* ws = d->workspace;
+      if (ws && d->workspace_bytes < pb)
+        return corm::fail(CORM_ENOMEM, "corm_conv: workspace %zu < %zu bytes", d->workspace_bytes, pb);
+      if (!ws && !(ws = corm::scratch(pb, st))) return CORM_ENOMEM;
+      j.partial = ws;
+    }
+    return corm::gemm_i8x4(j, st);
   }
   const ConvPlan pl = plan_of(d);
   void* ws = d->workspace;

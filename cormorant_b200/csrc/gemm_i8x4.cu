@@ -68,7 +68,8 @@ struct EpiArgs {
   uint64_t a_bs16, b_bs16;
   uint32_t lda, ldb;
   uint32_t ymode;  // the form of the rule (floor_acc)
-  uint32_t cvar;   // act (0 none, 1 ReLU, 2 Clip(0,6)) * 2 + conv bias
+  uint32_t cvar;   // act (0 none, 1 ReLU, 2 Clip(0,6)) * 3 + bias kind (0 none, 1 per column, 2 per row)
+  uint32_t bias_rows;
   int* err;
   long long wait_limit;  // clock cycles every bounded wait may take (corm_set_wait_limit)
   // mode 2 (column groups): output columns [gc[g], gc[g + 1]) go to their own
@@ -324,15 +325,16 @@ __device__ __forceinline__ int32_t floor_acc(uint32_t hh, uint32_t mid, uint32_t
 }
 
 // CW accumulator columns of one row -> CW / 2 packed int16 pairs: the rule
-// (YMODE), the conv bias (BIAS) and the act flags (ACT 0 none, 1 ReLU, 2
-// Clip(0,6)) as straight-line code
-template <int CW, int YMODE, int ACT, bool BIAS>
+// (YMODE), the bias (BK 0 none, 1 per column — a conv's channel —, 2 the
+// row's own, rowb) and the act flags (ACT 0 none, 1 ReLU, 2 Clip(0,6)) as
+// straight-line code
+template <int CW, int YMODE, int ACT, int BK>
 __device__ __forceinline__ void combine_run(const EpiArgs& ep, const uint32_t* hh, const uint32_t* mid,
-                                            const uint32_t* ll, uint32_t c0, uint32_t* out2) {
+                                            const uint32_t* ll, uint32_t c0, uint32_t* out2, int32_t rowb) {
 #pragma unroll
   for (int j = 0; j < CW; j += 2) {
-    const int32_t b0 = (BIAS && c0 + j < ep.cols) ? ep.bias[c0 + j] : 0;
-    const int32_t b1 = (BIAS && c0 + j + 1 < ep.cols) ? ep.bias[c0 + j + 1] : 0;
+    const int32_t b0 = BK == 2 ? rowb : ((BK == 1 && c0 + j < ep.cols) ? ep.bias[c0 + j] : 0);
+    const int32_t b1 = BK == 2 ? rowb : ((BK == 1 && c0 + j + 1 < ep.cols) ? ep.bias[c0 + j + 1] : 0);
     uint32_t p = pack_sat16(floor_acc<YMODE>(hh[j], mid[j], ll[j], b0),
                             floor_acc<YMODE>(hh[j + 1], mid[j + 1], ll[j + 1], b1));
     if (ACT == 1) p = __vmaxs2(p, 0u);
@@ -343,25 +345,28 @@ __device__ __forceinline__ void combine_run(const EpiArgs& ep, const uint32_t* h
 
 template <int CW, int YMODE>
 __device__ __forceinline__ void combine_ab(const EpiArgs& ep, const uint32_t* hh, const uint32_t* mid,
-                                           const uint32_t* ll, uint32_t c0, uint32_t* out2) {
-  switch (ep.cvar) {  // act * 2 + bias, uniform per job
-    case 0: combine_run<CW, YMODE, 0, false>(ep, hh, mid, ll, c0, out2); break;
-    case 1: combine_run<CW, YMODE, 0, true>(ep, hh, mid, ll, c0, out2); break;
-    case 2: combine_run<CW, YMODE, 1, false>(ep, hh, mid, ll, c0, out2); break;
-    case 3: combine_run<CW, YMODE, 1, true>(ep, hh, mid, ll, c0, out2); break;
-    case 4: combine_run<CW, YMODE, 2, false>(ep, hh, mid, ll, c0, out2); break;
-    default: combine_run<CW, YMODE, 2, true>(ep, hh, mid, ll, c0, out2); break;
+                                           const uint32_t* ll, uint32_t c0, uint32_t* out2, int32_t rowb) {
+  switch (ep.cvar) {  // act * 3 + bias kind, uniform per job
+    case 0: combine_run<CW, YMODE, 0, 0>(ep, hh, mid, ll, c0, out2, rowb); break;
+    case 1: combine_run<CW, YMODE, 0, 1>(ep, hh, mid, ll, c0, out2, rowb); break;
+    case 2: combine_run<CW, YMODE, 0, 2>(ep, hh, mid, ll, c0, out2, rowb); break;
+    case 3: combine_run<CW, YMODE, 1, 0>(ep, hh, mid, ll, c0, out2, rowb); break;
+    case 4: combine_run<CW, YMODE, 1, 1>(ep, hh, mid, ll, c0, out2, rowb); break;
+    case 5: combine_run<CW, YMODE, 1, 2>(ep, hh, mid, ll, c0, out2, rowb); break;
+    case 6: combine_run<CW, YMODE, 2, 0>(ep, hh, mid, ll, c0, out2, rowb); break;
+    case 7: combine_run<CW, YMODE, 2, 1>(ep, hh, mid, ll, c0, out2, rowb); break;
+    default: combine_run<CW, YMODE, 2, 2>(ep, hh, mid, ll, c0, out2, rowb); break;
   }
 }
 
 template <int CW>
 __device__ __forceinline__ void combine_any(const EpiArgs& ep, const uint32_t* hh, const uint32_t* mid,
-                                            const uint32_t* ll, uint32_t c0, uint32_t* out2) {
+                                            const uint32_t* ll, uint32_t c0, uint32_t* out2, int32_t rowb = 0) {
   switch (ep.ymode) {
-    case 0: combine_ab<CW, 0>(ep, hh, mid, ll, c0, out2); break;
-    case 1: combine_ab<CW, 1>(ep, hh, mid, ll, c0, out2); break;
-    case 2: combine_ab<CW, 2>(ep, hh, mid, ll, c0, out2); break;
-    default: combine_ab<CW, 3>(ep, hh, mid, ll, c0, out2); break;
+    case 0: combine_ab<CW, 0>(ep, hh, mid, ll, c0, out2, rowb); break;
+    case 1: combine_ab<CW, 1>(ep, hh, mid, ll, c0, out2, rowb); break;
+    case 2: combine_ab<CW, 2>(ep, hh, mid, ll, c0, out2, rowb); break;
+    default: combine_ab<CW, 3>(ep, hh, mid, ll, c0, out2, rowb); break;
   }
 }
 
@@ -724,6 +729,8 @@ __global__ void __launch_bounds__(Roles<CONV>::threads, 1)
       sm100::tc_fence_after();
       const uint32_t r = w.tile_r + q * 32 + lane;
       const bool row_ok = r < ep.rows;
+      // a per-row bias (a 1 x 1 conv as W x; int16 operands only)
+      const int32_t rowb = (CONV && ep.bias_rows && row_ok) ? ep.bias[r] : 0;
       if (ep.partial) {
         for (int cc = R::wc * h; cc < R::wc * h + R::wc; cc += CW) {
           uint32_t hh[CW], mid[CW], ll[CW];
@@ -765,7 +772,7 @@ __global__ void __launch_bounds__(Roles<CONV>::threads, 1)
           tmem_ld_cw<CW>(tmem + lane_addr + 2 * BN + cc, ll);
           sm100::tmem_ld_wait();
           const uint32_t c0 = w.tile_c + cc;
-          combine_any<CW>(ep, hh, mid, ll, c0, v2 + (CW / 2) * part);
+          combine_any<CW>(ep, hh, mid, ll, c0, v2 + (CW / 2) * part, rowb);
         }
         sm100::tc_fence_before();
         __syncwarp();
@@ -798,7 +805,7 @@ __global__ void __launch_bounds__(Roles<CONV>::threads, 1)
           if (!row_ok) continue;
           const uint32_t c0 = w.tile_c + cc;
           uint32_t v8[8];
-          combine_any<16>(ep, hh, mid, ll, c0, v8);
+          combine_any<16>(ep, hh, mid, ll, c0, v8, rowb);
           if (ep.post.op != kPostNone) {
             uint32_t b8[8];
             post_operand<16>(ep, rb, c0, b8);
@@ -832,6 +839,7 @@ __global__ void __launch_bounds__(256) gemm_finish_kernel(const EpiArgs ep) {
     for (uint32_t sp = 0; sp < ep.splits; sp++) sum += __ldg(ep.partial + sp * total + i);
     int64_t acc = (int64_t)sum;
     if (ep.mode == 1 && ep.bias) acc += (int64_t)ep.bias[c] << 8;
+    if (ep.bias_rows && ep.bias) acc += (int64_t)ep.bias[r] << 8;
     const uint64_t off = out_offset(ep, ep.mode != 1 ? bz : 0, r, c);
     int16_t y = finish(acc, ep.flags);
     if (ep.post.op != kPostNone) y = post_apply(ep.post, y, post_b(ep.post, off, c));
@@ -1094,8 +1102,10 @@ int gemm_i8x4(const GemmJob& j, cudaStream_t stream) {
                : ((uint64_t)kk * ((1ull << 22) + (1ull << 16) + (1ull << 8)) + (1ull << 15) < (1ull << 31) ? 0u
                   : ((uint64_t)kk * ((1ull << 16) + (1ull << 8)) + (1ull << 15) < (1ull << 29) ? 1u : 3u));
   }
-  ep.cvar = ((j.flags & CORM_F_ACT_RELU6) ? 4u : ((j.flags & CORM_F_ACT_RELU) ? 2u : 0u)) +
-            ((j.mode == 1 && j.bias) ? 1u : 0u);
+  if (j.bias_rows && (j.mode != 0 || !j.bias)) return fail(CORM_EINVAL, "gemm: a per-row bias needs mode 0 and a bias");
+  ep.bias_rows = j.bias_rows ? 1u : 0u;
+  ep.cvar = ((j.flags & CORM_F_ACT_RELU6) ? 6u : ((j.flags & CORM_F_ACT_RELU) ? 3u : 0u)) +
+            (j.bias_rows ? 2u : ((j.mode == 1 && j.bias) ? 1u : 0u));
   ep.num_kb = sp.num_kb;
   ep.a_planes = j.a_planes;
   ep.b_planes = j.b_planes;

@@ -38,6 +38,7 @@ struct GemmJob {
   uint32_t P, y_cn, y_cs, y_gs;
   uint64_t img_stride;      // mode 1: elements per image (out_ch * P)
   const int16_t* bias;      // mode 1 bias per column (raw), or nullptr
+  uint32_t bias_rows;       // mode 0: `bias` holds one entry per row (a 1x1 conv run as W x per image)
   uint32_t flags;           // CORM_F_WRAP32 | CORM_F_ACT_RELU | CORM_F_ACT_RELU6
   PostOp post;              // fused VectorOP job on the result (op kPostNone: none)
   // int16 operands split inside the kernel instead of the planes above (a16 != nullptr):

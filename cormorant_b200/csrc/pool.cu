@@ -56,15 +56,29 @@ __device__ __forceinline__ int64_t pool_tap(int64_t acc, int32_t v, const PoolAr
   return acc + (int64_t)v * v;
 }
 
+// Any window: one thread per output element.  SMALL: the job has fewer than
+// 2^32 outputs and the index arithmetic runs in 32 bits (64-bit divisions by
+// the runtime extents cost more than the taps).
+template <bool SMALL>
 __global__ void __launch_bounds__(256) pool_window(PoolArgs p) {
   corm_pdl_wait();
   corm_pdl_trigger();
   const uint64_t total = (uint64_t)p.batch * p.channels * p.out_h * p.out_w;
   for (uint64_t idx = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; idx < total;
        idx += (uint64_t)gridDim.x * blockDim.x) {
-    const uint32_t ow = idx % p.out_w;
-    const uint32_t oh = (idx / p.out_w) % p.out_h;
-    const uint64_t nc = idx / ((uint64_t)p.out_w * p.out_h);
+    uint32_t ow, oh;
+    uint64_t nc;
+    if (SMALL) {
+      const uint32_t i32 = (uint32_t)idx, r = i32 / p.out_w;
+      ow = i32 - r * p.out_w;
+      const uint32_t n32 = r / p.out_h;
+      oh = r - n32 * p.out_h;
+      nc = n32;
+    } else {
+      ow = (uint32_t)(idx % p.out_w);
+      oh = (uint32_t)((idx / p.out_w) % p.out_h);
+      nc = idx / ((uint64_t)p.out_w * p.out_h);
+    }
     const int16_t* xp = p.x + nc * p.in_h * p.in_w;
     int64_t acc = p.pool_type == 0 ? INT64_MIN : 0;
     uint32_t taps = 0;
@@ -82,25 +96,74 @@ __global__ void __launch_bounds__(256) pool_window(PoolArgs p) {
   }
 }
 
-// Global window: one warp per plane (out 1x1, pool = in, stride irrelevant, no padding).
+// 2 x 2 windows at stride 2 with no padding or dilation over planes of even
+// width (the MNIST pools): a thread per output, its two input pairs read as two
+// 4-byte words (a warp reads two runs of 128 contiguous bytes), MAX by packed
+// maxima, AVG by the exact sum of the four taps; outputs past the last full
+// window row / column are not produced by such a job (out = floor(in / 2)).
+template <int TYPE>
+__global__ void __launch_bounds__(256) pool_2x2s2(PoolArgs p) {
+  corm_pdl_wait();
+  corm_pdl_trigger();
+  const uint32_t total = p.batch * p.channels * p.out_h * p.out_w;  // < 2^32 (host)
+  for (uint32_t idx = blockIdx.x * blockDim.x + threadIdx.x; idx < total; idx += gridDim.x * blockDim.x) {
+    const uint32_t r = idx / p.out_w, ow = idx - r * p.out_w;
+    const uint32_t nc = r / p.out_h, oh = r - nc * p.out_h;
+    const uint32_t* row0 = (const uint32_t*)(p.x + ((size_t)nc * p.in_h + 2u * oh) * p.in_w) + ow;
+    const uint32_t a = __ldg(row0), b = __ldg(row0 + p.in_w / 2u);
+    int32_t y;
+    if (TYPE == 0) {
+      const uint32_t m2 = __vmaxs2(a, b);
+      y = max((int32_t)(int16_t)(m2 & 0xFFFFu), (int32_t)m2 >> 16);
+    } else {
+      const int64_t acc = (int32_t)(int16_t)(a & 0xFFFFu) + ((int32_t)a >> 16) + (int32_t)(int16_t)(b & 0xFFFFu) +
+                          ((int32_t)b >> 16);
+      y = (int32_t)pool_finish(acc, 4u, p);
+    }
+    p.y[idx] = (int16_t)y;
+  }
+}
+
+// Global window: one thread per (n, c) plane (out 1x1, pool = in, no padding).
+// A warp stages its 32 consecutive planes (contiguous, 16-byte loads when the
+// run is aligned) in shared memory, then each lane reduces its own plane in
+// order; planes larger than the staging buffer are read from global memory.
+constexpr uint32_t kGapStage = 2048;  // int16 per warp: 32 planes of up to 64 elements
 __global__ void __launch_bounds__(256) pool_global(PoolArgs p) {
   corm_pdl_wait();
   corm_pdl_trigger();
+  __shared__ __align__(16) int16_t s_pl[8][kGapStage];
   const uint64_t planes = (uint64_t)p.batch * p.channels;
   const uint32_t hw = p.in_h * p.in_w;
-  const uint64_t warp = ((uint64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint64_t gw0 = ((uint64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const uint64_t nwarps = ((uint64_t)gridDim.x * blockDim.x) >> 5;
-  for (uint64_t pl = warp; pl < planes; pl += nwarps) {
-    const int16_t* xp = p.x + pl * hw;
-    int64_t acc = p.pool_type == 0 ? INT64_MIN : 0;
-    for (uint32_t i = lane; i < hw; i += 32) acc = pool_tap(acc, __ldg(xp + i), p);
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      const int64_t u = __shfl_xor_sync(0xffffffffu, acc, o);
-      acc = p.pool_type == 0 ? (u > acc ? u : acc) : acc + u;
+  const bool staged = 32u * hw <= kGapStage;
+  for (uint64_t base = gw0 * 32u; base < planes; base += nwarps * 32u) {
+    const uint32_t np = (uint32_t)min((uint64_t)32u, planes - base);
+    const int16_t* src = p.x + base * hw;
+    const int16_t* mine;
+    if (staged) {
+      const uint32_t n = np * hw;
+      int16_t* dst = s_pl[warp];
+      if ((((uintptr_t)src) & 15u) == 0) {
+        const uint32_t n8 = n / 8u;
+        for (uint32_t i = lane; i < n8; i += 32) ((int4*)dst)[i] = __ldg((const int4*)src + i);
+        for (uint32_t i = 8u * n8 + lane; i < n; i += 32) dst[i] = __ldg(src + i);
+      } else {
+        for (uint32_t i = lane; i < n; i += 32) dst[i] = __ldg(src + i);
+      }
+      __syncwarp();
+      mine = dst + (size_t)lane * hw;
+    } else {
+      mine = src + (size_t)lane * hw;
     }
-    if (lane == 0) p.y[pl] = (int16_t)pool_finish(acc, hw, p);
+    if ((uint32_t)lane < np) {
+      int64_t acc = p.pool_type == 0 ? INT64_MIN : 0;
+      for (uint32_t i = 0; i < hw; i++) acc = pool_tap(acc, staged ? mine[i] : __ldg(mine + i), p);
+      p.y[base + lane] = (int16_t)pool_finish(acc, hw, p);
+    }
+    __syncwarp();  // the staging is rewritten by the next group
   }
 }
 
@@ -126,17 +189,27 @@ extern "C" int corm_pool(const corm_pool_desc* d, corm_stream_t stream) {
              d->stride_h, d->stride_w, d->pad_top, d->pad_left, d->dil_h, d->dil_w, d->pool_type, d->lp_order,
              d->count_include_pad};
   cudaStream_t st = (cudaStream_t)stream;
-  if (global && d->in_h * d->in_w >= 32) {
+  const bool small = total < (1ull << 32) && (uint64_t)d->batch * d->channels * d->in_h * d->in_w < (1ull << 32);
+  if (global && d->in_h * d->in_w >= 2) {
     const uint64_t planes = (uint64_t)d->batch * d->channels;
     {
       corm::ProfScope prof_("pool_global", st);
-      corm_launch_pdl(pool_global, dim3(corm_blocks(planes * 32, 256, 148u * 16u)), dim3(256), 0, st, p);
+      corm_launch_pdl(pool_global, dim3(corm_blocks((planes + 31) / 32 * 32, 256, 148u * 8u)), dim3(256), 0, st, p);
     }
+  } else if (small && d->pool_type <= 1 && d->pool_h == 2 && d->pool_w == 2 && d->stride_h == 2 && d->stride_w == 2 &&
+             d->pad_top == 0 && d->pad_left == 0 && d->dil_h == 1 && d->dil_w == 1 && d->in_w % 2 == 0 &&
+             d->out_h == d->in_h / 2 && d->out_w == d->in_w / 2 && !((uintptr_t)d->x & 3u)) {
+    corm::ProfScope prof_("pool_2x2s2", st);
+    if (d->pool_type == 0)
+      corm_launch_pdl(pool_2x2s2<0>, dim3(corm_blocks(total, 256, 148u * 16u)), dim3(256), 0, st, p);
+    else
+      corm_launch_pdl(pool_2x2s2<1>, dim3(corm_blocks(total, 256, 148u * 16u)), dim3(256), 0, st, p);
   } else {
-    {
-      corm::ProfScope prof_("pool_window", st);
-      corm_launch_pdl(pool_window, dim3(corm_blocks(total, 256, 148u * 16u)), dim3(256), 0, st, p);
-    }
+    corm::ProfScope prof_("pool_window", st);
+    if (small)
+      corm_launch_pdl(pool_window<true>, dim3(corm_blocks(total, 256, 148u * 16u)), dim3(256), 0, st, p);
+    else
+      corm_launch_pdl(pool_window<false>, dim3(corm_blocks(total, 256, 148u * 16u)), dim3(256), 0, st, p);
   }
   return corm::cuda_status("pool");
 }

@@ -410,13 +410,14 @@ __global__ void __launch_bounds__(256) smx_cols(SmxArgs p) {
 }
 
 // Column mode with 16-byte loads and stores (size % 8 == 0, a_inc % 8 == 0,
-// 16-byte aligned a): tiles of 32 query columns staged transposed in shared
-// memory — query c's keys at s_x[base(c) + j], base(c) = c KP + 16 (c / 8),
-// the skew putting the four 8-column words of a key pair in distinct banks —
-// then 8 lanes per query (4 queries per warp), each lane taking WPL words of
-// 8 keys for the max, the sum and the P row (held in registers with their e
-// values while STORE_E, else read again from shared memory and e recomputed).  Same arithmetic as smx_cols; CTAs walk the tiles (the TAB copied
-// into shared memory once per CTA).
+// 16-byte aligned a, up to 8192 keys): tiles of QT query columns (32, or 8 for
+// columns beyond 1024 keys) staged transposed in shared memory — query c's
+// keys at s_x[base(c) + j], base(c) = c KP + 16 (c / 8), the skew putting the
+// 8-column words of a key pair in distinct banks — then 256 / QT lanes per
+// query, each lane taking WPL words of 8 keys for the max, the sum and the P
+// row (held in registers with their e values while STORE_E, else read again
+// from shared memory and e recomputed).  Same arithmetic as smx_cols; CTAs
+// walk the tiles (the e table or the TAB built in shared memory once per CTA).
 __device__ __forceinline__ uint32_t smx_tbase(uint32_t c, uint32_t KP) { return c * KP + 16u * (c >> 3); }
 
 // A packed pair of scores with the lanes at or past the valid length v set to
@@ -426,8 +427,10 @@ __device__ __forceinline__ uint32_t smx_mask2(uint32_t w, uint32_t j, uint32_t v
   return j + 1 < v ? w : ((w & 0xFFFFu) | 0x80000000u);
 }
 
-template <int WPL, bool STORE_E, bool FC, bool ET>
+template <int QT, int WPL, bool STORE_E, bool FC, bool ET>
 __global__ void __launch_bounds__(256) smx_cols_t(SmxArgs p) {
+  constexpr uint32_t LPQ = 256u / QT;  // lanes per query: 8 (QT 32) or 32 (QT 8, long columns)
+  constexpr uint32_t PARTS = QT / 8;   // 8-query groups of the staging
   corm_pdl_wait();
   corm_pdl_trigger();
   extern __shared__ __align__(16) uint8_t smx_sm[];
@@ -438,15 +441,14 @@ __global__ void __launch_bounds__(256) smx_cols_t(SmxArgs p) {
     smx_fill_etab<FC>(s_t, p, 256);
   else
     for (int i = threadIdx.x; i < 4096; i += 256) s_t[i] = __ldg(p.tab + i);
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint64_t rnd = 1ull << (39u - p.fp);
   const uint32_t psh = 40u - p.fp;
-  const uint32_t tiles = (p.rows + 31u) / 32u;
+  const uint32_t tiles = (p.rows + QT - 1u) / QT;
   for (uint32_t tile = blockIdx.x; tile < tiles; tile += gridDim.x) {
-    const uint32_t q0 = tile * 32u;
+    const uint32_t q0 = tile * QT;
     // the keys any query of the tile reads: valid0 + its largest q mod period
     // (a causal mask reads about half); the rest of the staging is never used
-    const uint32_t qn = min(31u, p.rows - 1u - q0);
+    const uint32_t qn = min(QT - 1u, p.rows - 1u - q0);
     uint32_t tmax = 0;
     if (p.period) {
       const uint32_t t0 = q0 % p.period;
@@ -454,8 +456,8 @@ __global__ void __launch_bounds__(256) smx_cols_t(SmxArgs p) {
     }
     const uint32_t vmax = min(p.size, p.valid0 + tmax);
     __syncthreads();  // the previous tile's reads (and the table) are done
-    for (uint32_t idx = threadIdx.x; idx < ((vmax + 1u) / 2u) * 4u; idx += 256u) {
-      const uint32_t jp = idx >> 2, part = idx & 3u;
+    for (uint32_t idx = threadIdx.x; idx < ((vmax + 1u) / 2u) * PARTS; idx += 256u) {
+      const uint32_t jp = idx / PARTS, part = idx % PARTS;
       if (q0 + 8u * part >= p.rows) continue;
       const int16_t* src = p.a + (size_t)(2u * jp) * p.a_inc + q0 + 8u * part;
       const int4 w0 = __ldg((const int4*)src), w1 = __ldg((const int4*)(src + p.a_inc));
@@ -468,8 +470,8 @@ __global__ void __launch_bounds__(256) smx_cols_t(SmxArgs p) {
       }
     }
     __syncthreads();
-    // a warp per 4 queries, 8 lanes per query, WPL words of 8 keys per lane
-    const uint32_t r = (uint32_t)warp * 4u + ((uint32_t)lane >> 3), sl = (uint32_t)lane & 7u;
+    // LPQ lanes per query, WPL words of 8 keys per lane
+    const uint32_t r = (uint32_t)threadIdx.x / LPQ, sl = (uint32_t)threadIdx.x % LPQ;
     const uint32_t q = q0 + r;
     const bool live = q < p.rows;
     const uint32_t v = live ? smx_valid(q, p) : 0u;
@@ -477,7 +479,7 @@ __global__ void __launch_bounds__(256) smx_cols_t(SmxArgs p) {
     // every key word this lane reads, masked past v (INT16_MIN) so the
     // maximum needs no test per key
     auto word = [&](int k) -> uint4 {
-      const uint32_t j0 = 8u * (sl + 8u * k);
+      const uint32_t j0 = 8u * (sl + LPQ * k);
       if (j0 >= v) return make_uint4(0x80008000u, 0x80008000u, 0x80008000u, 0x80008000u);
       uint4 w = *(const uint4*)(xs + j0);  // j0 < v <= size: staged
       if (j0 + 8u > v) {
@@ -492,18 +494,18 @@ __global__ void __launch_bounds__(256) smx_cols_t(SmxArgs p) {
     uint32_t mx = 0x80008000u;
 #pragma unroll(STORE_E ? WPL : 1)
     for (int k = 0; k < WPL; k++) {
-      if (8u * (sl + 8u * k) >= v) break;
+      if (8u * (sl + LPQ * k) >= v) break;
       const uint4 w = word(k);
       if constexpr (STORE_E) xw[k] = w;
       mx = __vmaxs2(__vmaxs2(mx, w.x), __vmaxs2(__vmaxs2(w.y, w.z), w.w));
     }
     mx = __vmaxs2(mx, __funnelshift_l(mx, mx, 16));
 #pragma unroll
-    for (int o = 4; o > 0; o >>= 1) mx = __vmaxs2(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    for (int o = LPQ / 2; o > 0; o >>= 1) mx = __vmaxs2(mx, __shfl_xor_sync(0xffffffffu, mx, o));
     const int32_t m = (int32_t)(int16_t)(mx & 0xFFFFu);
     // e of the 8 keys of word k (0 past v)
     auto e8 = [&](int k, const uint4& w, uint32_t* e) {
-      const uint32_t j0 = 8u * (sl + 8u * k);
+      const uint32_t j0 = 8u * (sl + LPQ * k);
       const uint32_t pr[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
       for (int t = 0; t < 4; t++) smx_e2<ET, FC>(mx, pr[t], m, p, s_t, e[2 * t], e[2 * t + 1]);
@@ -516,7 +518,7 @@ __global__ void __launch_bounds__(256) smx_cols_t(SmxArgs p) {
     uint32_t S = 0;
 #pragma unroll(STORE_E ? WPL : 1)
     for (int k = 0; k < WPL; k++) {
-      if (8u * (sl + 8u * k) >= v) break;
+      if (8u * (sl + LPQ * k) >= v) break;
       uint32_t e[8];
       if constexpr (STORE_E)
         e8(k, xw[k], e);
@@ -529,7 +531,7 @@ __global__ void __launch_bounds__(256) smx_cols_t(SmxArgs p) {
       }
     }
 #pragma unroll
-    for (int o = 4; o > 0; o >>= 1) S += __shfl_xor_sync(0xffffffffu, S, o);
+    for (int o = LPQ / 2; o > 0; o >>= 1) S += __shfl_xor_sync(0xffffffffu, S, o);
     if (live) {
       const uint32_t R = S > 0 ? (uint32_t)((1ull << 40) / S) : 0u;
       int16_t* out = p.c + (size_t)q * p.b_inc;
@@ -537,7 +539,7 @@ __global__ void __launch_bounds__(256) smx_cols_t(SmxArgs p) {
       const bool oa = ((uintptr_t)out & 15) == 0;
 #pragma unroll(STORE_E ? WPL : 1)
       for (int k = 0; k < WPL; k++) {
-        const uint32_t j0 = 8u * (sl + 8u * k);
+        const uint32_t j0 = 8u * (sl + LPQ * k);
         if (j0 >= lim) break;
         uint32_t e[8];
         if (j0 >= v) {
@@ -617,12 +619,16 @@ int launch_softmax(const corm_vectorop_desc* d, cudaStream_t st, const corm::Dev
   if (p.rows == 0) return CORM_OK;
   if (p.rows > 1 && p.b_inc < p.size)
     return corm::fail(CORM_EINVAL, "softmax: output rows overlap (b_inc %u < size %u)", p.b_inc, p.size);
-  if (col && d->size % 8 == 0 && d->size <= 1024 && d->a_inc % 8 == 0 && !((uintptr_t)d->a & 15u)) {
+  if (col && d->size % 8 == 0 && d->size <= 8192 && d->a_inc % 8 == 0 && !((uintptr_t)d->a & 15u)) {
+    // 32 queries per tile up to 1024 keys; 8 (a warp per query) for longer columns
+    const uint32_t qt = d->size <= 1024 ? 32u : 8u;
     const bool et = p.dm <= kSmxEMax;
     p.tabn = et ? (p.dm + 1u + 3u) / 4u * 4u : 4096u;  // keeps the staging 16-byte aligned
-    const size_t smem = (size_t)p.tabn * sizeof(int32_t) + (32 * ((size_t)d->size + 8) + 16 * 4) * sizeof(int16_t);
-    const uint32_t tiles = (p.rows + 31) / 32;
-    const unsigned grid = tiles < 148u * 4u ? tiles : 148u * 4u;
+    const size_t smem = (size_t)p.tabn * sizeof(int32_t) +
+                        (qt * ((size_t)d->size + 8) + 16 * (qt / 8)) * sizeof(int16_t);
+    const uint32_t tiles = (p.rows + qt - 1) / qt;
+    const unsigned per_sm = smem <= 56u * 1024u ? 4u : (smem <= 112u * 1024u ? 2u : 1u);
+    const unsigned grid = tiles < 148u * per_sm ? tiles : 148u * per_sm;
     auto launch = [&](auto k_fe, auto k_se, auto k_f, auto k_s) {
       auto run = [&](auto kern) {
         cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
@@ -633,16 +639,19 @@ int launch_softmax(const corm_vectorop_desc* d, cudaStream_t st, const corm::Dev
       else if (fc) run(k_f);
       else run(k_s);
     };
-#define CORM_SMX_COLS(W, SE) \
-  launch(smx_cols_t<W, SE, true, true>, smx_cols_t<W, SE, false, true>, smx_cols_t<W, SE, true, false>, \
-         smx_cols_t<W, SE, false, false>)
+#define CORM_SMX_COLS(Q, W, SE) \
+  launch(smx_cols_t<Q, W, SE, true, true>, smx_cols_t<Q, W, SE, false, true>, smx_cols_t<Q, W, SE, true, false>, \
+         smx_cols_t<Q, W, SE, false, false>)
     {
       corm::ProfScope prof_("smx_cols_t", st);
-      if (d->size <= 64) CORM_SMX_COLS(1, true);
-      else if (d->size <= 128) CORM_SMX_COLS(2, true);
-      else if (d->size <= 256) CORM_SMX_COLS(4, true);
-      else if (d->size <= 512) CORM_SMX_COLS(8, false);
-      else CORM_SMX_COLS(16, false);
+      if (d->size <= 64) CORM_SMX_COLS(32, 1, true);
+      else if (d->size <= 128) CORM_SMX_COLS(32, 2, true);
+      else if (d->size <= 256) CORM_SMX_COLS(32, 4, true);
+      else if (d->size <= 512) CORM_SMX_COLS(32, 8, false);
+      else if (d->size <= 1024) CORM_SMX_COLS(32, 16, false);
+      else if (d->size <= 2048) CORM_SMX_COLS(8, 8, false);
+      else if (d->size <= 4096) CORM_SMX_COLS(8, 16, false);
+      else CORM_SMX_COLS(8, 32, false);
     }
 #undef CORM_SMX_COLS
     return corm::cuda_status("softmax_cols");

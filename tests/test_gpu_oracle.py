@@ -83,6 +83,10 @@ CONV_CASES = [  # N, C, H, W, M, kh, kw, sh, sw, pt, pl, dh, dw, depthwise, bias
     (1, 32, 9, 9, 32, 3, 3, 1, 1, 2, 2, 2, 2, True, False),
     (3, 40, 7, 9, 70, 5, 3, 1, 2, 2, 1, 1, 1, False, True),
     (1, 160, 7, 7, 960, 1, 1, 1, 1, 0, 0, 1, 1, False, True),
+    # 1 x 1 at stride 1 on whole 16-byte rows: the GEMM form W x per image (two
+    # row tiles of channels, a batch; a K split with its per-channel bias)
+    (3, 32, 8, 16, 200, 1, 1, 1, 1, 0, 0, 1, 1, False, True),
+    (1, 2048, 4, 4, 40, 1, 1, 1, 1, 0, 0, 1, 1, False, True),
     # depthwise: warp-per-plane windows (stride 1 / 2, pads 0..2, W above a warp,
     # an input row no output reads), shared-memory planes (larger windows, 5x5)
     (3, 24, 14, 14, 24, 3, 3, 1, 1, 1, 1, 1, 1, True, True),
