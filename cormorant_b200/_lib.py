@@ -18,7 +18,8 @@ F_WRAP32, F_WEIGHT_LOGICAL, F_ACT_RELU, F_ACT_RELU6 = 0x1, 0x2, 0x4, 0x8
 # every symbol include/cormorant_b200.h declares
 EXPORTS = ("corm_vectorop", "corm_matmul_workspace_size", "corm_matmul", "corm_matmul_noalloc", "corm_matmul_noalloc_status", "corm_conv_workspace_size", "corm_conv",
            "corm_matmul_post", "corm_matmul_groups", "corm_split_b_planes", "corm_matmul_bplanes", "corm_conv_post", "corm_gemm_strided_workspace_size", "corm_gemm_strided",
-           "corm_copy_nd", "corm_llm_attn_softmax", "corm_greedy_embed",
+           "corm_copy_nd", "corm_llm_attn_softmax", "corm_greedy_embed", "corm_llm_embed", "corm_llm_dequant",
+           "corm_llm_resadd", "corm_llm_rmsnorm", "corm_llm_act_mul", "corm_llm_attn_prep_host",
            "corm_llm_decode_attn", "corm_rowops_chain", "corm_rowops_chain_dev",
            "corm_stream_done",
            "corm_pool", "corm_rowops", "corm_act_table", "corm_smx_table", "corm_rowops_table_image",
@@ -84,6 +85,39 @@ class LlmSmxDesc(C.Structure):
     """corm_llm_smx_desc: the host's p12 softmax of one KV group."""
     _fields_ = [("s", C.c_void_p), ("p", C.c_void_p), ("tab", C.c_void_p), ("ip", C.c_void_p)] + _u32_fields(
         ["pos", "n", "T", "G", "C", "Q", "window", "batch"]) + [("s_stride", C.c_uint64), ("p_stride", C.c_uint64)]
+
+
+class LlmEmbedDesc(C.Structure):
+    """corm_llm_embed_desc: LlmEmbed rows (float32, or the int32 residual)."""
+    _fields_ = [("ids", C.c_void_p), ("table", C.c_void_p), ("out", C.c_void_p)] + _u32_fields(
+        ["n", "rows", "d", "res32"]) + [("f", C.c_int32), ("scale", C.c_float)]
+
+
+class LlmDequantDesc(C.Structure):
+    _fields_ = [("x", C.c_void_p), ("y", C.c_void_p), ("f", C.c_void_p), ("count", C.c_uint64), ("n", C.c_uint32)]
+
+
+class LlmResAddDesc(C.Structure):
+    _fields_ = [("h", C.c_void_p), ("d", C.c_void_p), ("y", C.c_void_p), ("fd", C.c_void_p)] + _u32_fields(
+        ["rows", "n"])
+
+
+class LlmRMSNormDesc(C.Structure):
+    _fields_ = [("h32", C.c_void_p), ("h16", C.c_void_p), ("fh", C.c_void_p), ("y", C.c_void_p),
+                ("gamma", C.c_void_p), ("fy", C.c_void_p), ("eps", C.c_double), ("rows", C.c_uint64)] + _u32_fields(
+        ["n", "W"])
+
+
+class LlmActMulDesc(C.Structure):
+    _fields_ = [("g", C.c_void_p), ("u", C.c_void_p), ("y", C.c_void_p), ("tab", C.c_void_p), ("tab_of", C.c_void_p),
+                ("fu", C.c_void_p), ("fy", C.c_void_p)] + _u32_fields(["rows", "n"])
+
+
+class LlmPrepDesc(C.Structure):
+    _fields_ = [(nm, C.c_void_p) for nm in ("q0", "k0", "v", "kc", "vc", "qx", "cos", "sin", "fq0", "fk0", "fv", "fkc",
+                                            "fvc", "fq")] + _u32_fields(
+        ["pos", "n", "T", "H", "KV", "HD", "C", "Q", "batch"]) + [("ldq", C.c_uint64), ("ldk", C.c_uint64),
+                                                                  ("ldv", C.c_uint64)]
 
 
 class GreedyDesc(C.Structure):
@@ -152,6 +186,12 @@ def lib() -> C.CDLL:
                        ("corm_copy_nd", [C.POINTER(CopyDesc), C.c_void_p]),
                        ("corm_llm_attn_softmax", [C.POINTER(LlmSmxDesc), C.c_void_p]),
                        ("corm_greedy_embed", [C.POINTER(GreedyDesc), C.c_void_p]),
+                       ("corm_llm_embed", [C.POINTER(LlmEmbedDesc), C.c_void_p]),
+                       ("corm_llm_dequant", [C.POINTER(LlmDequantDesc), C.c_void_p]),
+                       ("corm_llm_resadd", [C.POINTER(LlmResAddDesc), C.c_void_p]),
+                       ("corm_llm_rmsnorm", [C.POINTER(LlmRMSNormDesc), C.c_void_p]),
+                       ("corm_llm_act_mul", [C.POINTER(LlmActMulDesc), C.c_void_p]),
+                       ("corm_llm_attn_prep_host", [C.POINTER(LlmPrepDesc), C.c_void_p]),
                        ("corm_llm_decode_attn", [C.POINTER(DecodeAttnDesc), C.c_void_p]),
                        ("corm_pool", [C.POINTER(PoolDesc), C.c_void_p]),
                        ("corm_rowops", [C.POINTER(RowOpsDesc), C.c_void_p]),

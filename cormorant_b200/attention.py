@@ -63,6 +63,31 @@ def sexp_table(f: int, scale: float) -> np.ndarray:
     return _SEXP[key]
 
 
+_ACT: Dict[Tuple[str, int], np.ndarray] = {}
+_GELU_K, _GELU_A = -1.5957691216057308, 0.044715  # -2 sqrt(2 / pi) and the cubic coefficient
+
+
+def act_table(kind: str, f: int) -> np.ndarray:
+    """The host's float64 activation of every raw int16 gate word r (index r +
+    32768) at gate exponent f, g = r 2^-f, with the C library's exp in the
+    reference's operation order (llm_nodes.py:325-349): ``silu`` g / (1 +
+    exp(-g)) (0 for g <= -700), ``gelu`` (tanh form) g / (1 + exp(K (g + A g^3)))
+    (0 where the exponent reaches 700)."""
+    key = (kind, int(f))
+    if key not in _ACT:
+        d = 2.0 ** int(f)
+        t = np.empty(65536)
+        for i in range(65536):
+            g = (i - 32768 + 0.0) / d
+            if kind == "silu":
+                t[i] = g / (1.0 + math.exp(-g)) if g > -700 else 0.0
+            else:
+                z = _GELU_K * (g + _GELU_A * g * g * g)
+                t[i] = g / (1.0 + math.exp(z)) if z < 700.0 else 0.0
+        _ACT[key] = t
+    return _ACT[key]
+
+
 def score_exp(fq, fk, KV: int, F: int = 8) -> np.ndarray:
     """Per query head the q.K^T scores' exponent f_q + f_k(its KV head) - F
     (graph_builder.py:197-200)."""

@@ -19,7 +19,7 @@ INCLUDE = os.path.join(ROOT, "include")
 BUILD = os.path.join(PKG, "_build")
 LIB = os.path.join(PKG, "libcorm_b200.so")
 
-CU_SOURCES = ["capi.cu", "vectorop.cu", "pool.cu", "rowops.cu", "gemm_i8x4.cu", "matmul.cu", "conv.cu", "strided.cu", "llm.cu"]
+CU_SOURCES = ["capi.cu", "vectorop.cu", "pool.cu", "rowops.cu", "gemm_i8x4.cu", "matmul.cu", "conv.cu", "strided.cu", "llm.cu", "llm_host.cu"]
 CPP_SOURCES = ["tables.cpp"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 

@@ -60,7 +60,7 @@ constexpr long long kShortWaitLimit = 1ll << 20;
 // instead of a hung GPU.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err, int code,
                                           long long limit = 4000000000ll, volatile int* stop = nullptr) {
-  if (limit < kShortWaitLimit) {
+  if (limit < kShortWaitLimit) {  // (a compile-time constant limit folds this test away)
     const long long t0 = clock64();
     for (;;) {
       if (mbar_test_wait(bar, parity)) return true;

@@ -48,6 +48,9 @@ constexpr uint32_t TMEM_COLS = 512;
 // with raw tiles: A buffer b (hi 32 columns, lo 32 columns) at 384 + 64 b
 constexpr uint32_t A_TMEM = 384;
 constexpr int NUM_SMS = 148;
+// Clock cycles each bounded wait of the GEMM may take before it gives up
+// (about 2 s at the B200's clocks); corm_set_wait_limit overrides it.
+constexpr long long kWaitDefault = 4000000000ll;
 
 struct EpiArgs {
   int mode;
@@ -378,7 +381,9 @@ __device__ __forceinline__ void tmem_ld_cw(uint32_t taddr, uint32_t* r) {
     sm100::tmem_ld16(taddr, r);
 }
 
-template <bool CONV>
+// DIAG: the bounded waits take the host's diagnostic limit (corm_set_wait_limit)
+// instead of the compile-time default.
+template <bool CONV, bool DIAG>
 __global__ void __launch_bounds__(Roles<CONV>::threads, 1)
     gemm_i8x4_kernel(const __grid_constant__ CUtensorMap map_ahi, const __grid_constant__ CUtensorMap map_alo,
                      const __grid_constant__ CUtensorMap map_bhi, const __grid_constant__ CUtensorMap map_blo,
@@ -441,7 +446,7 @@ __global__ void __launch_bounds__(Roles<CONV>::threads, 1)
       const int a_z = ep.a_planes == 1 ? 0 : (int)w.bz, b_z = ep.b_planes == 1 ? 0 : (int)w.bz;
       for (uint32_t kb = w.kb0; kb < w.kb1; kb++, g++) {
         const int s = g % STAGES;
-        if (g >= (uint32_t)STAGES && !sm100::mbar_wait(&empty[s], ((g / STAGES) - 1) & 1, ep.err, 101, ep.wait_limit, cta_stop)) {
+        if (g >= (uint32_t)STAGES && !sm100::mbar_wait(&empty[s], ((g / STAGES) - 1) & 1, ep.err, 101, DIAG ? ep.wait_limit : kWaitDefault, cta_stop)) {
           ok = false;
           break;
         }
@@ -479,7 +484,7 @@ __global__ void __launch_bounds__(Roles<CONV>::threads, 1)
       const int a_z = ep.a_bs16 ? (int)w.bz : 0, b_z = ep.b_bs16 ? (int)w.bz : 0;
       for (uint32_t kb = w.kb0; kb < w.kb1; kb++, g++) {
         const int s = g % STAGES;
-        if (g >= (uint32_t)STAGES && !sm100::mbar_wait(&empty[s], ((g / STAGES) - 1) & 1, ep.err, 106, ep.wait_limit, cta_stop)) {
+        if (g >= (uint32_t)STAGES && !sm100::mbar_wait(&empty[s], ((g / STAGES) - 1) & 1, ep.err, 106, DIAG ? ep.wait_limit : kWaitDefault, cta_stop)) {
           ok = false;
           break;
         }
@@ -530,8 +535,8 @@ __global__ void __launch_bounds__(Roles<CONV>::threads, 1)
       const uint32_t nrow = ep.rows - w.tile_r, ncol = ep.cols - w.tile_c;
       for (uint32_t kb = w.kb0; kb < w.kb1; kb++, g++) {
         const int s = g % STAGES;
-        bool okw = sm100::mbar_wait(&raw_full[s], (g / STAGES) & 1, ep.err, 105, ep.wait_limit, cta_stop);
-        if (g >= 2) okw = sm100::mbar_wait(&a_free[g & 1], ((g >> 1) - 1) & 1, ep.err, 109, ep.wait_limit, cta_stop) && okw;
+        bool okw = sm100::mbar_wait(&raw_full[s], (g / STAGES) & 1, ep.err, 105, DIAG ? ep.wait_limit : kWaitDefault, cta_stop);
+        if (g >= 2) okw = sm100::mbar_wait(&a_free[g & 1], ((g >> 1) - 1) & 1, ep.err, 109, DIAG ? ep.wait_limit : kWaitDefault, cta_stop) && okw;
         if (!okw) atomicMin(abort_at, g);
         sm100::tc_fence_after();  // the TMEM buffer's readers are done (a_free)
         uint8_t* st = smem + s * STAGE_BYTES;
@@ -612,7 +617,7 @@ __global__ void __launch_bounds__(Roles<CONV>::threads, 1)
       const int16_t* Bb = ep.b16 + (uint64_t)w.bz * ep.b_bs16;
       for (uint32_t kb = w.kb0; kb < w.kb1; kb++, g++) {
         const int s = g % STAGES;
-        if (g >= (uint32_t)STAGES && !sm100::mbar_wait(&empty[s], ((g / STAGES) - 1) & 1, ep.err, 101, ep.wait_limit, cta_stop)) {
+        if (g >= (uint32_t)STAGES && !sm100::mbar_wait(&empty[s], ((g / STAGES) - 1) & 1, ep.err, 101, DIAG ? ep.wait_limit : kWaitDefault, cta_stop)) {
           ok = false;
           break;
         }
@@ -665,11 +670,11 @@ __global__ void __launch_bounds__(Roles<CONV>::threads, 1)
     bool ok = true;
     for (uint32_t u = blockIdx.x; u < units && ok; u += gridDim.x, i++) {
       const Unit w = unit_of(ep, u);
-      if (i > 0 && !sm100::mbar_wait(tmem_empty, (i - 1) & 1, ep.err, 104, ep.wait_limit, cta_stop)) break;
+      if (i > 0 && !sm100::mbar_wait(tmem_empty, (i - 1) & 1, ep.err, 104, DIAG ? ep.wait_limit : kWaitDefault, cta_stop)) break;
       sm100::tc_fence_after();
       for (uint32_t kb = w.kb0; kb < w.kb1; kb++, g++) {
         const int s = g % STAGES;
-        if (!sm100::mbar_wait(&full[s], (g / STAGES) & 1, ep.err, 102, ep.wait_limit, cta_stop)) {
+        if (!sm100::mbar_wait(&full[s], (g / STAGES) & 1, ep.err, 102, DIAG ? ep.wait_limit : kWaitDefault, cta_stop)) {
           ok = false;
           break;
         }
@@ -725,7 +730,7 @@ __global__ void __launch_bounds__(Roles<CONV>::threads, 1)
     for (uint32_t u = blockIdx.x; u < units; u += gridDim.x, i++) {
       const Unit w = unit_of(ep, u);
       if (u + gridDim.x >= units) corm_pdl_trigger();  // this CTA's last unit
-      if (!sm100::mbar_wait(tmem_full, i & 1, ep.err, 103, ep.wait_limit, cta_stop)) break;
+      if (!sm100::mbar_wait(tmem_full, i & 1, ep.err, 103, DIAG ? ep.wait_limit : kWaitDefault, cta_stop)) break;
       sm100::tc_fence_after();
       const uint32_t r = w.tile_r + q * 32 + lane;
       const bool row_ok = r < ep.rows;
@@ -970,10 +975,7 @@ Split split_of(uint32_t rows, uint32_t cols, uint32_t Kp, uint32_t batch) {
 int* g_err_word[64];
 std::mutex g_err_mu;
 
-// Clock cycles each bounded wait of the GEMM may take before it gives up
-// (about 2 s at the B200's clocks); corm_set_wait_limit changes it.
-constexpr long long kDefaultWaitLimit = 4000000000ll;
-std::atomic<long long> g_wait_limit{kDefaultWaitLimit};
+std::atomic<long long> g_wait_limit{kWaitDefault};
 
 }  // namespace
 
@@ -1137,21 +1139,22 @@ int gemm_i8x4(const GemmJob& j, cudaStream_t stream) {
   int dev = 0;
   cudaGetDevice(&dev);
   if (!attr_set[dev]) {
-    cudaFuncSetAttribute(gemm_i8x4_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
-    cudaFuncSetAttribute(gemm_i8x4_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+    cudaFuncSetAttribute(gemm_i8x4_kernel<false, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+    cudaFuncSetAttribute(gemm_i8x4_kernel<true, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+    cudaFuncSetAttribute(gemm_i8x4_kernel<false, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+    cudaFuncSetAttribute(gemm_i8x4_kernel<true, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
     attr_set[dev] = true;
   }
+  const bool diag = ep.wait_limit != kWaitDefault;
   const uint64_t units = (uint64_t)sp.tiles * sp.splits;
   if (units >= (1ull << 31)) return fail(CORM_ELIMIT, "gemm: %llu work units", (unsigned long long)units);
   const unsigned grid = (unsigned)(units < (uint64_t)NUM_SMS ? units : NUM_SMS);
   {
     ProfScope prof_("gemm_i8x4_kernel", stream);
-    if (conv)
-      corm_launch_pdl(gemm_i8x4_kernel<true>, dim3(grid), dim3(Roles<true>::threads), SMEM_BYTES, stream, m_ahi, m_alo,
-                      m_bhi, m_blo, ep);
-    else
-      corm_launch_pdl(gemm_i8x4_kernel<false>, dim3(grid), dim3(Roles<false>::threads), SMEM_BYTES, stream, m_ahi,
-                      m_alo, m_bhi, m_blo, ep);
+    auto kern = conv ? (diag ? gemm_i8x4_kernel<true, true> : gemm_i8x4_kernel<true, false>)
+                     : (diag ? gemm_i8x4_kernel<false, true> : gemm_i8x4_kernel<false, false>);
+    const int threads = conv ? Roles<true>::threads : Roles<false>::threads;
+    corm_launch_pdl(kern, dim3(grid), dim3(threads), SMEM_BYTES, stream, m_ahi, m_alo, m_bhi, m_blo, ep);
   }
   if (int rc = cuda_status("gemm_i8x4")) return rc;
   if (sp.splits > 1) {
@@ -1187,6 +1190,6 @@ extern "C" int corm_device_status(int* code) {
 // <= 0 restores the default of about 2 s).  A diagnostic: limits below 2^20
 // cycles read the clock on every probe, so a test can make a wait run out.
 extern "C" int corm_set_wait_limit(long long cycles) {
-  corm::g_wait_limit.store(cycles > 0 ? cycles : corm::kDefaultWaitLimit, std::memory_order_relaxed);
+  corm::g_wait_limit.store(cycles > 0 ? cycles : corm::kWaitDefault, std::memory_order_relaxed);
   return CORM_OK;
 }

@@ -449,6 +449,132 @@ class LlmSelectRowNode:
 
 
 @dataclass
+class HostTable:
+    """A host-side constant table of an LLM node (llm_nodes.py HostTable):
+    kind f32 / bf16 (float32 values) or i16 (raw words at the output's
+    exponent)."""
+    name: str
+    kind: str
+    data: np.ndarray = field(repr=False)
+
+
+@dataclass
+class LlmEmbedNode:
+    """h[t] = table[clamp(ids[t], 0, rows - 1)] (llm_nodes.py:466-570): float32
+    rows, or with ``res32`` the int32 residual (round half to even at its
+    exponent); ``scale`` a float32 factor.  inputs = [ids] (host int32)."""
+    inputs: List[TensorInfo]
+    output: TensorInfo
+    rows: int = 1
+    d: int = 1
+    n: int = 1
+    image_rows: int = 0
+    res32: bool = False
+    scale: float = 1.0
+    table: Optional[HostTable] = field(default=None, repr=False)
+    F: int = 8
+    onnx_node: object = None
+
+
+@dataclass
+class LlmDequantNode:
+    """y = float32(raw 2^-f[c]) (llm_nodes.py:1722-1750)."""
+    inputs: List[TensorInfo]
+    output: TensorInfo
+    count: int = 1
+    F: int = 8
+    onnx_node: object = None
+
+
+@dataclass
+class LlmToHostNode:
+    """A float32 DMA tensor handed to the host unchanged (llm_nodes.py:1753-1777)."""
+    inputs: List[TensorInfo]
+    output: TensorInfo
+    count: int = 1
+    F: int = 8
+    onnx_node: object = None
+
+
+@dataclass
+class LlmResAddNode:
+    """y = float32((double) h + d) on the float32 residual (llm_nodes.py:572-603)."""
+    inputs: List[TensorInfo]
+    output: TensorInfo
+    rows: int = 1
+    n: int = 1
+    F: int = 8
+    onnx_node: object = None
+
+
+@dataclass
+class LlmRMSNormNode:
+    """y = (h r) gamma, r = 1 / sqrt(sum(h^2) / n + eps) per row of n
+    (llm_nodes.py:618-694): h float32, or int16 rows of W (``i16``: W / n
+    head rows each); y int16 at its per-channel exponents."""
+    inputs: List[TensorInfo]
+    output: TensorInfo
+    rows: int = 1
+    n: int = 1
+    W: int = 1
+    i16: bool = False
+    eps: float = 1e-5
+    gamma: Optional[np.ndarray] = field(default=None, repr=False)
+    F: int = 8
+    onnx_node: object = None
+
+
+@dataclass
+class LlmSiluMulNode:
+    """a = silu(g) u with silu from a libm table over g's raw word per gate
+    exponent (llm_nodes.py:697-746).  inputs = [g, u]."""
+    inputs: List[TensorInfo]
+    output: TensorInfo
+    rows: int = 1
+    n: int = 1
+    F: int = 8
+    onnx_node: object = None
+
+
+@dataclass
+class LlmGeluMulNode(LlmSiluMulNode):
+    """a = gelu_tanh(g) u, the table form of llm_nodes.py:749-791."""
+
+
+@dataclass
+class LlmAttnPrepNode:
+    """LlmAttnPrep's host form (llm_nodes.py:1012-1169): RoPE in float64 with
+    the float32 tables, the K / V cache rows pos + t (t < n) at their
+    exponents, the q.K^T image qx [KV][HD][G T] at fq per head.  inputs =
+    [q0, k0, v, pos, (n), cache_k, cache_v]; ``batch`` B sequences: q0 / k0 /
+    v [B T][..], caches [KV][B][C][HD], qx [KV][B][HD][G T]."""
+    inputs: List[TensorInfo]
+    output: TensorInfo
+    T: int = 1
+    H: int = 1
+    KV: int = 1
+    HD: int = 16
+    C: int = 16
+    kw: int = 1
+    Q: int = 16
+    has_n: bool = True
+    fq: Optional[np.ndarray] = field(default=None, repr=False)
+    cos: Optional[np.ndarray] = field(default=None, repr=False)
+    sin: Optional[np.ndarray] = field(default=None, repr=False)
+    F: int = 8
+    batch: int = 1
+    onnx_node: object = None
+
+    @property
+    def ck(self):
+        return self.inputs[-2]
+
+    @property
+    def cv(self):
+        return self.inputs[-1]
+
+
+@dataclass
 class Graph:
     """What the simulator reads of the reference's OnnxGraph: nodes in
     topological order, weights (with data), graph inputs / outputs, states."""

@@ -211,6 +211,89 @@ def llm_attn_softmax(s, p, tab, ip, *, pos, n, T, G, rows, Q=16, window=0, batch
     check(lib().corm_llm_attn_softmax(C.byref(d), st))
 
 
+def _dtype(t, dt, name):
+    if t.dtype != dt or not t.is_cuda:
+        raise CormError(_lib.CORM_EINVAL, f"{name}: a CUDA {dt} tensor expected, got {t.dtype} on {t.device}")
+
+
+def llm_embed(ids, table, out, *, n, rows, d, res32=False, f=0, scale=1.0):
+    """LlmEmbed (corm_llm_embed): out [n][d] float32 rows, or the int32
+    residual at 2^-f (res32), of table [rows][d] float32 at ids (int32)."""
+    _dtype(ids, torch.int32, "ids")
+    _dtype(table, torch.float32, "table")
+    _dtype(out, torch.int32 if res32 else torch.float32, "out")
+    st = _ready()
+    check(lib().corm_llm_embed(C.byref(_lib.LlmEmbedDesc(_ptr(ids), _ptr(table), _ptr(out), n, rows, d, int(res32), f,
+                                                        float(scale))), st))
+
+
+def llm_dequant(x, y, f, *, count, n):
+    """LlmDequant (corm_llm_dequant): y float32 = x 2^-f[c], f int8 [n]."""
+    _i16(x, "x")
+    _dtype(y, torch.float32, "y")
+    _dtype(f, torch.int8, "f")
+    st = _ready()
+    check(lib().corm_llm_dequant(C.byref(_lib.LlmDequantDesc(_ptr(x), _ptr(y), _ptr(f), count, n)), st))
+
+
+def llm_resadd(h, d, y, fd, *, rows, n):
+    """LlmResAdd on the float32 residual (corm_llm_resadd)."""
+    _dtype(h, torch.float32, "h")
+    _i16(d, "d")
+    _dtype(y, torch.float32, "y")
+    _dtype(fd, torch.int8, "fd")
+    st = _ready()
+    check(lib().corm_llm_resadd(C.byref(_lib.LlmResAddDesc(_ptr(h), _ptr(d), _ptr(y), _ptr(fd), rows, n)), st))
+
+
+def llm_rmsnorm(h, y, gamma, fy, *, rows, n, W, eps, fh=None):
+    """LlmRMSNorm (corm_llm_rmsnorm): h float32 rows of n, or int16 rows of W
+    at fh (int8 [W]); y int16 at fy (int8 [W]); rows = rows of n."""
+    _i16(y, "y")
+    _dtype(gamma, torch.float32, "gamma")
+    _dtype(fy, torch.int8, "fy")
+    if h.dtype == torch.float32:
+        h32, h16, fhp = _ptr(h), None, None
+    else:
+        _i16(h, "h")
+        _dtype(fh, torch.int8, "fh")
+        h32, h16, fhp = None, _ptr(h), _ptr(fh)
+    st = _ready()
+    check(lib().corm_llm_rmsnorm(C.byref(_lib.LlmRMSNormDesc(h32, h16, fhp, _ptr(y), _ptr(gamma), _ptr(fy), float(eps),
+                                                            rows, n, W)), st))
+
+
+def llm_act_mul(g, u, y, tab, tab_of, fu, fy, *, rows, n):
+    """LlmSiluMul / LlmGeluMul (corm_llm_act_mul): tab float64 [tables][65536],
+    tab_of uint8 [n], fu / fy int8 [n]."""
+    for t, nm in ((g, "g"), (u, "u"), (y, "y")):
+        _i16(t, nm)
+    _dtype(tab, torch.float64, "tab")
+    _dtype(tab_of, torch.uint8, "tab_of")
+    _dtype(fu, torch.int8, "fu")
+    _dtype(fy, torch.int8, "fy")
+    st = _ready()
+    check(lib().corm_llm_act_mul(C.byref(_lib.LlmActMulDesc(_ptr(g), _ptr(u), _ptr(y), _ptr(tab), _ptr(tab_of),
+                                                           _ptr(fu), _ptr(fy), rows, n)), st))
+
+
+def llm_attn_prep_host(q0, k0, v, kc, vc, qx, cos, sin, fq0, fk0, fv, fkc, fvc, fq, *, pos, n, T, H, KV, HD, C_,
+                       Q=16, batch=1, ldq=None, ldk=None, ldv=None):
+    """LlmAttnPrep's host form (corm_llm_attn_prep_host) for ``batch``
+    sequences: caches group-major [KV][batch][C_][HD], qx [KV][batch][HD][G T]."""
+    for t, nm in ((q0, "q0"), (k0, "k0"), (v, "v"), (kc, "kc"), (vc, "vc"), (qx, "qx")):
+        _i16(t, nm)
+    _dtype(cos, torch.float32, "cos")
+    _dtype(sin, torch.float32, "sin")
+    for t, nm in ((fq0, "fq0"), (fk0, "fk0"), (fv, "fv"), (fkc, "fkc"), (fvc, "fvc"), (fq, "fq")):
+        _dtype(t, torch.int8, nm)
+    st = _ready()
+    d = _lib.LlmPrepDesc(*[_ptr(t) for t in (q0, k0, v, kc, vc, qx, cos, sin, fq0, fk0, fv, fkc, fvc, fq)], pos, n, T,
+                         H, KV, HD, C_, Q, batch, H * HD if ldq is None else ldq, KV * HD if ldk is None else ldk,
+                         KV * HD if ldv is None else ldv)
+    check(lib().corm_llm_attn_prep_host(C.byref(d), st))
+
+
 def llm_decode_attn(qx, kc, vc, tab, ip, o, *, pos, B, KV, G, HD, rows, Q=16, window=0, o_stride=None, prep=None):
     """corm_llm_decode_attn: a decode step's q.K^T, host softmax, P.V and head
     merge of every KV group and sequence (caches of ``rows`` rows).

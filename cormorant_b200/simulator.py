@@ -68,6 +68,23 @@ def _exp_of(t, frac_bits: int = 8):
     return float(e) if e.ndim == 0 else e
 
 
+def _is_f32(t) -> bool:
+    """A float32 tensor (the float residual stream, a DEQUANT output): its
+    buffer holds values, not raw words at an exponent."""
+    return getattr(t, "host", None) == "f32" or getattr(t, "dma", None) == "f32"
+
+
+def _chan(t, n: int, frac_bits: int = 8) -> np.ndarray:
+    """The exponent of each of the n channels of t's last axis (int64)."""
+    if getattr(t, "chexp", None) is not None:
+        e = np.asarray(t.chexp, np.int64).reshape(-1)
+    elif getattr(t, "exp", None) is not None:
+        e = np.asarray(t.exp, np.int64).reshape(-1)
+    else:
+        e = np.array([frac_bits], np.int64)
+    return np.broadcast_to(e, (n,)) if e.size == 1 else e[:n]
+
+
 def _has_exp(*ts) -> bool:
     return any(getattr(t, a, None) is not None for t in ts for a in ("exp", "wexp", "chexp"))
 
@@ -97,7 +114,15 @@ class GpuSimulator:
         16-byte words (+ one word)."""
         return torch.empty((numel + 3) // 4 * 4 + 4, dtype=torch.int32, device=self.device)
 
+    def _alloc_f32(self, numel: int) -> torch.Tensor:
+        """A float32 tensor (padded to whole 16-byte words, plus one)."""
+        return torch.empty((numel + 3) // 4 * 4 + 4, dtype=torch.float32, device=self.device)
+
     def _to_raw(self, t, values) -> torch.Tensor:
+        if _is_f32(t):  # values as they are, in float32
+            buf = self._alloc_f32(t.numel)
+            buf[:t.numel].copy_(torch.from_numpy(np.asarray(values, np.float32).reshape(-1)))
+            return buf
         f = _exp_of(t)
         v = np.round(np.asarray(values, np.float64).reshape(t.shape) * np.power(2.0, f))
         if getattr(t, "dma", None) == "i32":
@@ -227,7 +252,9 @@ class GpuSimulator:
         raw_in = {}
         for name, v in input_arrays.items():
             t = tmap[name]
-            if getattr(t, "host", None) is not None:   # a host int (pos, n): stays on the host
+            if getattr(t, "host", None) == "f32":     # float32 host rows: on the device as float32
+                raw_in[name] = self._to_raw(t, v)
+            elif getattr(t, "host", None) is not None:   # a host int (pos, n, ids): stays on the host
                 if t.host != "i32":
                     raise NotImplementedError(f"GpuSimulator: host tensor kind {t.host}")
                 raw_in[name] = np.asarray(v).astype(np.int64).reshape(-1)
@@ -245,7 +272,7 @@ class GpuSimulator:
                 out[name] = raw[name].astype(np.float64).reshape(t.shape)
                 continue
             v = raw[name][:t.numel].cpu().numpy().astype(np.float64).reshape(t.shape)
-            out[name] = v / np.power(2.0, _exp_of(t))
+            out[name] = v if _is_f32(t) else v / np.power(2.0, _exp_of(t))
         for t in self._graph.state_tensors:
             vals = self.state_values(t, dev_states[t.onnx_name])
             if states is not None:
@@ -414,6 +441,11 @@ class GpuSimulator:
                 y = self._attn_merge(sn, get)
             elif kind == "LlmSelectRowNode":
                 y = self._select_row(sn, get)
+            elif kind in ("LlmEmbedNode", "LlmDequantNode", "LlmToHostNode", "LlmResAddNode", "LlmRMSNormNode",
+                          "LlmSiluMulNode", "LlmGeluMulNode"):
+                y = self._llm_host(sn, kind, get)
+            elif kind == "LlmAttnPrepNode":
+                y = self._attn_prep_host(sn, get)
             else:
                 raise NotImplementedError(f"GpuSimulator: no sm_100a kernel for node type {kind}")
             if alias_t is not None:  # the fused intermediate is not materialised
@@ -919,6 +951,116 @@ class GpuSimulator:
         for g, t in enumerate(sn.inputs):
             ops.copy_nd(get(t), y, (B, G, T, HD), (G * T * HD, T * HD, HD, 1), (T * nq, HD, nq, 1), dst_off=g * G * HD)
         return y
+
+    def _exps8(self, key, e) -> torch.Tensor:
+        """An exponent vector as a cached int8 device tensor."""
+        k = ("exps8", key, tuple(int(x) for x in e))
+        if k not in self._weights:
+            a = np.asarray(e, np.int64)
+            if (a < -127).any() or (a > 127).any():
+                raise NotImplementedError("exponent outside the int8 range")
+            self._weights[k] = torch.from_numpy(a.astype(np.int8)).to(self.device)
+        return self._weights[k]
+
+    def _llm_host(self, sn, kind, get):
+        """The float host ops of the LLM entries on the device (llm_host.cu):
+        LlmEmbed, LlmDequant, LlmToHost, LlmResAdd, LlmRMSNorm, LlmSiluMul /
+        LlmGeluMul (llm_nodes.py:466-791, 1722-1777)."""
+        from .attention import act_table
+        out_t = sn.output
+        N = out_t.numel
+        if kind == "LlmEmbedNode":
+            if int(getattr(sn, "image_rows", 0)):
+                raise NotImplementedError("LlmEmbedNode: image rows")
+            tb = sn.table
+            res32 = bool(sn.res32)
+            f = 0
+            if res32:
+                fo = _chan(out_t, sn.d)
+                if (fo != fo[0]).any():
+                    raise NotImplementedError("LlmEmbedNode: the residual at per-channel exponents")
+                f = int(fo[0])
+            key = ("embed", tb.name, tb.kind)
+            if key not in self._weights:
+                data = np.asarray(tb.data)
+                vals = (data.astype(np.float64) / 2.0 ** f) if tb.kind == "i16" else data
+                self._weights[key] = torch.from_numpy(np.asarray(vals, np.float32).reshape(-1).copy()).to(self.device)
+            ids = torch.from_numpy(np.asarray(get(sn.inputs[0])).astype(np.int32).reshape(-1)).to(self.device)
+            y = self._alloc32(N) if res32 else self._alloc_f32(N)
+            ops.llm_embed(ids, self._weights[key], y, n=sn.n, rows=sn.rows, d=sn.d, res32=res32, f=f,
+                          scale=float(getattr(sn, "scale", 1.0)))
+            return y
+        if kind == "LlmDequantNode":
+            x = sn.inputs[0]
+            n = int(x.shape[-1])
+            y = self._alloc_f32(N)
+            ops.llm_dequant(get(x), y, self._exps8(x.onnx_name, _chan(x, n)), count=sn.count, n=n)
+            return y
+        if kind == "LlmToHostNode":
+            src = get(sn.inputs[0])
+            y = self._alloc_f32(N)
+            ops.copy_nd(src.view(torch.int16), y.view(torch.int16), (2 * N,), (1,), (1,))
+            return y
+        if kind == "LlmResAddNode":
+            d_t = sn.inputs[1]
+            y = self._alloc_f32(N)
+            ops.llm_resadd(get(sn.inputs[0]), get(d_t), y, self._exps8(d_t.onnx_name, _chan(d_t, sn.n)), rows=sn.rows,
+                           n=sn.n)
+            return y
+        if kind == "LlmRMSNormNode":
+            h_t = sn.inputs[0]
+            W = int(getattr(sn, "W", sn.n))
+            gk = ("gamma", out_t.onnx_name)
+            if gk not in self._weights:
+                self._weights[gk] = torch.from_numpy(np.asarray(sn.gamma, np.float32).reshape(-1).copy()).to(self.device)
+            y = self._alloc(N)
+            fy = self._exps8(out_t.onnx_name, _chan(out_t, W))
+            fh = None if _is_f32(h_t) else self._exps8(h_t.onnx_name, _chan(h_t, W))
+            ops.llm_rmsnorm(get(h_t), y, self._weights[gk], fy, rows=sn.rows, n=sn.n, W=W, eps=float(sn.eps), fh=fh)
+            return y
+        # LlmSiluMulNode / LlmGeluMulNode
+        g_t, u_t = sn.inputs[0], sn.inputs[1]
+        fg = _chan(g_t, sn.n)
+        act = "gelu" if kind == "LlmGeluMulNode" else "silu"
+        uniq = sorted(set(int(v) for v in fg))
+        tk = ("acttab", act, tuple(uniq))
+        if tk not in self._weights:
+            self._weights[tk] = torch.from_numpy(np.concatenate([act_table(act, f) for f in uniq])).to(self.device)
+        ok = ("acttab_of", act, tuple(int(v) for v in fg))
+        if ok not in self._weights:
+            self._weights[ok] = torch.from_numpy(np.array([uniq.index(int(v)) for v in fg], np.uint8)).to(self.device)
+        y = self._alloc(N)
+        ops.llm_act_mul(get(g_t), get(u_t), y, self._weights[tk], self._weights[ok],
+                        self._exps8(u_t.onnx_name, _chan(u_t, sn.n)), self._exps8(out_t.onnx_name, _chan(out_t, sn.n)),
+                        rows=sn.rows, n=sn.n)
+        return y
+
+    def _attn_prep_host(self, sn, get):
+        """LlmAttnPrep's host form (llm_nodes.py:1012-1169) for B sequences:
+        the K / V cache rows pos + t (t < n) of the group-major states written in
+        place and the q image qx[g][b][d][h' T + t] (corm_llm_attn_prep_host)."""
+        from .attention import attn_keys
+        T, H, KV, HD, C = sn.T, sn.H, sn.KV, sn.HD, sn.C
+        B = int(getattr(sn, "batch", 1))
+        if int(getattr(sn, "kw", 1)) != 1:
+            raise NotImplementedError("LlmAttnPrepNode: a q image for qk_kw > 1")
+        q0, k0, v = sn.inputs[0], sn.inputs[1], sn.inputs[2]
+        pos = self._host_int(get, sn.inputs[3])
+        n_in = self._host_int(get, sn.inputs[4]) if sn.has_n else T
+        n, _keys = attn_keys(pos, n_in, T, C, sn.Q)
+        ck, cv = sn.inputs[-2], sn.inputs[-1]
+        tk = ("rope_f32", id(sn.cos), id(sn.sin))
+        if tk not in self._weights:
+            self._weights[tk] = (torch.from_numpy(np.asarray(sn.cos, np.float32).reshape(-1).copy()).to(self.device),
+                                 torch.from_numpy(np.asarray(sn.sin, np.float32).reshape(-1).copy()).to(self.device))
+        cos_t, sin_t = self._weights[tk]
+        qx = self._alloc(sn.output.numel)
+        e = lambda t, w: self._exps8(t.onnx_name, _chan(t, w))  # noqa: E731
+        ops.llm_attn_prep_host(get(q0), get(k0), get(v), get(ck), get(cv), qx, cos_t, sin_t, e(q0, H * HD),
+                               e(k0, KV * HD), e(v, KV * HD), e(ck, KV * HD), e(cv, KV * HD),
+                               self._exps8(("fq", sn.output.onnx_name), np.asarray(sn.fq, np.int64)),
+                               pos=pos, n=n, T=T, H=H, KV=KV, HD=HD, C_=C, Q=sn.Q, batch=B)
+        return qx
 
     def _select_row(self, sn, get):
         """h[n - 1], n clamped to [1, rows] (llm_nodes.py:1713-1717), of every

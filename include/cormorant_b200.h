@@ -247,6 +247,105 @@ typedef struct {
 
 int corm_llm_attn_softmax(const corm_llm_smx_desc* d, corm_stream_t stream);
 
+/* The float host operations of the LLM entries (llm_nodes.py; the policies
+ * that keep the residual stream in float32 on the host), each one launch.
+ * Per-channel exponents are int8 arrays on the device; float64 arithmetic in
+ * the reference's order with round-to-nearest at every step (no fused
+ * multiply-adds); write-back at an exponent = dtype.quantize_exp (RNE,
+ * saturated, NaN -> 0).
+ *
+ * corm_llm_embed replaces LlmEmbed (llm_nodes.py:466-570): out[t][j] =
+ * table[clamp(ids[t], 0, rows - 1)][j] (times scale, a float32 product) as
+ * float32, or with res32 as the int32 residual RNE(v 2^f). */
+typedef struct {
+  const int32_t* ids;
+  const float* table; /* [rows][d] */
+  void* out;          /* float32 or int32 [n][d] */
+  uint32_t n, rows, d, res32;
+  int32_t f;
+  float scale;
+} corm_llm_embed_desc;
+int corm_llm_embed(const corm_llm_embed_desc* d, corm_stream_t stream);
+
+/* corm_llm_dequant replaces LlmDequant (llm_nodes.py:1722-1750): y =
+ * float32(x 2^-f[c]), c = the channel of the last axis (n). */
+typedef struct {
+  const int16_t* x;
+  float* y;
+  const int8_t* f; /* [n] */
+  uint64_t count;
+  uint32_t n;
+} corm_llm_dequant_desc;
+int corm_llm_dequant(const corm_llm_dequant_desc* d, corm_stream_t stream);
+
+/* corm_llm_resadd replaces LlmResAdd (llm_nodes.py:572-603), the float32
+ * residual's add: y = float32((double) h + d 2^-fd[c]). */
+typedef struct {
+  const float* h;
+  const int16_t* d;
+  float* y;
+  const int8_t* fd; /* [n] */
+  uint32_t rows, n;
+} corm_llm_resadd_desc;
+int corm_llm_resadd(const corm_llm_resadd_desc* d, corm_stream_t stream);
+
+/* corm_llm_rmsnorm replaces LlmRMSNorm (llm_nodes.py:618-694): per row of n,
+ * ss = the squares summed left to right, r = 1 / sqrt(ss / n + eps), y =
+ * st((h r) gamma[j], fy[c]).  h: float32 rows (h32), or int16 rows of W at
+ * per-channel exponents fh[c] (h16; a head norm: every row of W holds W / n
+ * rows of n); c = the channel in the row of W; rows counts rows of n. */
+typedef struct {
+  const float* h32;
+  const int16_t* h16;
+  const int8_t* fh; /* [W] with h16 */
+  int16_t* y;
+  const float* gamma; /* [n] */
+  const int8_t* fy;   /* [W] */
+  double eps;
+  uint64_t rows;
+  uint32_t n, W;
+} corm_llm_rmsnorm_desc;
+int corm_llm_rmsnorm(const corm_llm_rmsnorm_desc* d, corm_stream_t stream);
+
+/* corm_llm_act_mul replaces LlmSiluMul / LlmGeluMul (llm_nodes.py:697-791):
+ * y = st(T[g_raw + 32768] u 2^-fu[c], fy[c]) with T the float64 activation
+ * table (libm exp, built by the caller: silu_table / gelu_table of channel
+ * c's gate exponent) at tab + 65536 tab_of[c]. */
+typedef struct {
+  const int16_t* g;
+  const int16_t* u;
+  int16_t* y;
+  const double* tab;     /* [tables][65536] */
+  const uint8_t* tab_of; /* [n] */
+  const int8_t* fu;      /* [n] */
+  const int8_t* fy;      /* [n] */
+  uint32_t rows, n;
+} corm_llm_act_mul_desc;
+int corm_llm_act_mul(const corm_llm_act_mul_desc* d, corm_stream_t stream);
+
+/* corm_llm_attn_prep_host replaces LlmAttnPrep's host form (llm_nodes.py:
+ * 1012-1169) for `batch` sequences at one pos / n: for the rows t < n (n
+ * clamped as attn_keys clamps it) RoPE of q0 / k0 in float64 with the float32
+ * tables' row pos + t, the K and v rows written into the caches' row pos + t
+ * (group-major [KV][batch][C][HD]) at fkc / fvc, and the q.K^T image qx
+ * [KV][batch][HD][G T] = clip(RNE(RoPE(q) 2^fq[h])) (columns t >= n: 0).  q0
+ * [batch T][ldq] at fq0 [H HD], k0 / v [batch T][ldk / ldv] at fk0 / fv [KV
+ * HD]; cos / sin [C][HD / 2] float32. */
+typedef struct {
+  const int16_t* q0;
+  const int16_t* k0;
+  const int16_t* v;
+  int16_t* kc;
+  int16_t* vc;
+  int16_t* qx;
+  const float* cos;
+  const float* sin;
+  const int8_t *fq0, *fk0, *fv, *fkc, *fvc, *fq;
+  uint32_t pos, n, T, H, KV, HD, C, Q, batch;
+  uint64_t ldq, ldk, ldv;
+} corm_llm_prep_desc;
+int corm_llm_attn_prep_host(const corm_llm_prep_desc* d, corm_stream_t stream);
+
 /* corm_greedy_embed: between two greedy decode steps, per sequence b the
  * next token id = the first index of the largest of logits[b * ld + 0 ..
  * vocab) (int16 at one exponent: LlmDequant then the caller's argmax) and its

@@ -13,7 +13,7 @@ reference, so everything the tests need is written here).
    ``rowops_spec``) on seeded inputs, imported through the inert ``onnx``
    stand-in in ``_onnx_stub``.
 
-    python tests/golden/make_golden.py [--ref /root/reference] [--only hw|sim|graph|llm|attn|smx|numeric|convexp]
+    python tests/golden/make_golden.py [--ref /root/reference] [--only hw|sim|graph|llm|attn|smx|numeric|convexp|llmhost]
 """
 from __future__ import annotations
 
@@ -714,6 +714,140 @@ def make_llm_smx_host(ref, out):
     print("sim_llm_smx_host.npz:", len(res), "arrays")
 
 
+def make_llm_host(ref, out):
+    """The LLM host ops (llm_nodes.py:466-1790) from the reference's node
+    factories, run through its _forward_pass on seeded inputs: LlmEmbed (into
+    float32 host rows and into the int32 residual), LlmDequant, LlmToHost,
+    LlmResAdd (float32 residual), LlmRMSNorm (float32 rows; int16 head rows at
+    per-channel exponents), LlmSiluMul / LlmGeluMul (libm tables per gate
+    exponent) and LlmAttnPrep in its host form (float RoPE with the float32
+    tables: a prefill with n, a decode step without).  Saved: inputs and
+    outputs (raw integers at their exponents, float32 as float64)."""
+    sim = _import_reference(ref)
+    import onnx.helper
+    onnx.helper.get_attribute_value = lambda a: a.value
+    from src.dtype import AP_FIXED_16_8 as D
+    from src.tensor import TensorInfo as TI
+    from src import llm_nodes as LN
+    from src.host_nodes import HostContext
+    rng = np.random.default_rng(53)
+    res = {}
+
+    def ten(name, shape, exp=None, **kw):
+        return TI(onnx_name=name, shape=list(shape), dtype="float32",
+                  exp=None if exp is None else np.asarray(exp, np.int64), **kw)
+
+    def run(factory, op, ins, outs, tens, feeds, consts=None, states=None, st_tens=(), **attrs):
+        ctx = HostContext(opset=17, consts=consts or {}, frac_bits=8)
+        node = factory(_Node(op, ins, outs, **attrs), tens, 0, 8, ctx)
+        g_ = _Graph([node], [], [tens[i] for i in ins if i and i in feeds], [tens[o] for o in outs])
+        g_.state_tensors = list(st_tens)
+        arr = _shim(sim, D, g_)._forward_pass(feeds, states=states) if states is not None else \
+            _shim(sim, D, g_)._forward_pass(feeds)
+        return node, arr
+
+    p2 = lambda e: np.power(2.0, np.asarray(e, np.float64))  # noqa: E731
+    rows, n, V = 5, 48, 40
+    # LlmEmbed: float32 rows, and the int32 residual at 2^-15 (ids past the table clamp)
+    tab = (rng.standard_normal((V, n)) * 0.05).astype(np.float32)
+    ids = np.array([3, 0, 39, 17, 45, -2], np.int32)
+    for tag, yk in (("emb_f32", dict(host="f32")), ("emb_res32", dict(exp=15, dma="i32"))):
+        tens = {"ids": ten("ids", (ids.size,), host="i32"), "tab": ten("tab", tab.shape, data=tab),
+                "y": ten("y", (ids.size, n), **yk)}
+        _, arr = run(LN.LlmEmbedNode.from_onnx_node, "LlmEmbed", ["ids", "tab"], ["y"], tens, {"ids": ids},
+                     consts={"tab": tab})
+        y = np.asarray(arr["y"], np.float64)
+        res[f"{tag}_y"] = y if tag == "emb_f32" else np.rint(y * 2.0 ** 15).astype(np.int64)
+    res.update(emb_tab=tab, emb_ids=ids)
+    # LlmDequant: int16 at per-channel exponents -> float32
+    fx = rng.integers(4, 20, n)
+    xr = rng.integers(-32768, 32768, (rows, n))
+    tens = {"x": ten("x", (rows, n), fx), "y": ten("y", (rows, n), host="f32")}
+    _, arr = run(LN.LlmDequantNode.from_onnx_node, "LlmDequant", ["x"], ["y"], tens, {"x": xr / p2(fx)[None, :]})
+    res.update(deq_x=xr, deq_fx=fx, deq_y=np.asarray(arr["y"], np.float64))
+    # LlmToHost: a float32 DMA tensor to the host
+    xf = (rng.standard_normal((rows, n)) * 3).astype(np.float32)
+    tens = {"x": ten("x", (rows, n), dma="f32"), "y": ten("y", (rows, n), host="f32")}
+    _, arr = run(LN.LlmToHostNode.from_onnx_node, "LlmToHost", ["x"], ["y"], tens, {"x": xf.astype(np.float64)})
+    res.update(toh_x=xf, toh_y=np.asarray(arr["y"], np.float64))
+    # LlmResAdd: float32 residual + int16 delta at per-channel exponents
+    h = (rng.standard_normal((rows, n)) * 4).astype(np.float32)
+    fd = rng.integers(8, 16, n)
+    dr = rng.integers(-32768, 32768, (rows, n))
+    tens = {"h": ten("h", (rows, n), host="f32"), "d": ten("d", (rows, n), fd), "y": ten("y", (rows, n), host="f32")}
+    _, arr = run(LN.LlmResAddNode.from_onnx_node, "LlmResAdd", ["h", "d"], ["y"], tens,
+                 {"h": h.astype(np.float64), "d": dr / p2(fd)[None, :]})
+    res.update(radd_h=h, radd_d=dr, radd_fd=fd, radd_y=np.asarray(arr["y"], np.float64))
+    # LlmRMSNorm on float32 rows -> int16 at per-channel exponents
+    gamma = (1.0 + 0.2 * rng.standard_normal(n)).astype(np.float32)
+    fo = rng.integers(10, 14, n)
+    tens = {"h": ten("h", (rows, n), host="f32"), "gamma": ten("gamma", (n,), data=gamma), "y": ten("y", (rows, n), fo)}
+    _, arr = run(LN.LlmRMSNormNode.from_onnx_node, "LlmRMSNorm", ["h", "gamma"], ["y"], tens,
+                 {"h": h.astype(np.float64)}, consts={"gamma": gamma}, axi_eps=b"1e-06")
+    res.update(rms_h=h, rms_gamma=gamma, rms_fo=fo, rms_y=np.rint(np.asarray(arr["y"]) * p2(fo)[None, :]).astype(np.int64))
+    # LlmRMSNorm on int16 head rows: rows of W = 2 n (two heads of n), exponents per channel of W
+    W = 2 * n
+    fh = rng.integers(8, 13, W)
+    fo2 = rng.integers(10, 14, W)
+    hr = rng.integers(-20000, 20000, (rows, W))
+    tens = {"h": ten("h", (rows, W), fh), "gamma": ten("gamma", (n,), data=gamma), "y": ten("y", (rows, W), fo2)}
+    node, arr = run(LN.LlmRMSNormNode.from_onnx_node, "LlmRMSNorm", ["h", "gamma"], ["y"], tens,
+                    {"h": hr / p2(fh)[None, :]}, consts={"gamma": gamma}, epsilon=1e-5)
+    assert node.i16
+    res.update(rms16_h=hr, rms16_fh=fh, rms16_fo=fo2,
+               rms16_y=np.rint(np.asarray(arr["y"]) * p2(fo2)[None, :]).astype(np.int64))
+    # LlmSiluMul / LlmGeluMul: gate at 2-3 exponents, up and out per channel
+    fg = rng.choice([9, 11, 13], n)
+    fu, fa = rng.integers(8, 13, n), rng.integers(9, 14, n)
+    gr = rng.integers(-32768, 32768, (rows, n))
+    ur = rng.integers(-32768, 32768, (rows, n))
+    for tag, fac, op in (("silu", LN.LlmSiluMulNode.from_onnx_node, "LlmSiluMul"),
+                         ("gelu", LN.LlmGeluMulNode.from_onnx_node, "LlmGeluMul")):
+        tens = {"g": ten("g", (rows, n), fg), "u": ten("u", (rows, n), fu), "y": ten("y", (rows, n), fa)}
+        _, arr = run(fac, op, ["g", "u"], ["y"], tens, {"g": gr / p2(fg)[None, :], "u": ur / p2(fu)[None, :]})
+        res[f"{tag}_y"] = np.rint(np.asarray(arr["y"]) * p2(fa)[None, :]).astype(np.int64)
+    res.update(act_g=gr, act_u=ur, act_fg=fg, act_fu=fu, act_fa=fa)
+    # LlmAttnPrep (host): RoPE in float64 with the float32 tables, the caches'
+    # rows at their exponents, the q.K^T image at f_q per head
+    H, KV, HD, C = 6, 2, 32, 64
+    G = H // KV
+    fq0, fk0, fv = rng.integers(9, 13, H * HD), rng.integers(9, 13, KV * HD), rng.integers(9, 13, KV * HD)
+    fq = rng.integers(10, 13, H)
+    fkc, fvc = np.repeat(rng.integers(10, 13, KV), HD), rng.integers(9, 13, KV * HD)
+    ang = np.outer(np.arange(C), 1.0 / (10000.0 ** (np.arange(HD // 2) * 2.0 / HD)))
+    cos, sin = np.cos(ang).astype(np.float32), np.sin(ang).astype(np.float32)
+    res.update(prep_fq0=fq0, prep_fk0=fk0, prep_fv=fv, prep_fq=fq, prep_fkc=fkc, prep_fvc=fvc, prep_cos=cos,
+               prep_sin=sin)
+    for tag, T, pos, nn in (("pre", 8, 20, 5), ("dec", 1, 37, None)):
+        tens = {"q0": ten("q0", (T, H * HD), fq0), "k0": ten("k0", (T, KV * HD), fk0),
+                "v": ten("v", (T, KV * HD), fv), "pos": ten("pos", (1,), host="i32"), "n": ten("n", (1,), host="i32"),
+                "ck": ten("ck", (C, KV * HD), fkc, is_state=True, group_layout=(KV, HD)),
+                "cv": ten("cv", (C, KV * HD), fvc, is_state=True, group_layout=(KV, HD)),
+                "qx": ten("qx", (KV, HD, G * T), 0), "cos": ten("cos", cos.shape, data=cos),
+                "sin": ten("sin", sin.shape, data=sin)}
+        q0r = rng.integers(-20000, 20000, (T, H * HD))
+        k0r = rng.integers(-20000, 20000, (T, KV * HD))
+        vr = rng.integers(-20000, 20000, (T, KV * HD))
+        ckr = rng.integers(-700, 700, (C, KV * HD))
+        cvr = rng.integers(-1500, 1500, (C, KV * HD))
+        states = {"ck": ckr / p2(fkc)[None, :], "cv": cvr / p2(fvc)[None, :]}
+        feeds = {"q0": q0r / p2(fq0)[None, :], "k0": k0r / p2(fk0)[None, :], "v": vr / p2(fv)[None, :],
+                 "pos": np.array([pos], np.int32)}
+        if nn is not None:
+            feeds["n"] = np.array([nn], np.int32)
+        _, arr = run(LN.LlmAttnPrepNode.from_onnx_node, "LlmAttnPrep",
+                     ["q0", "k0", "v", "pos", "n" if nn is not None else "", "ck", "cv", "cos", "sin"], ["qx"], tens,
+                     feeds, consts={"cos": cos, "sin": sin}, states=states, st_tens=[tens["ck"], tens["cv"]],
+                     num_heads=H, num_kv_heads=KV, head_dim=HD, q_exp=[int(x) for x in fq], qk_kw=1, key_quantum=16)
+        res.update({f"prep_{tag}_q0": q0r, f"prep_{tag}_k0": k0r, f"prep_{tag}_v": vr, f"prep_{tag}_ck0": ckr,
+                    f"prep_{tag}_cv0": cvr, f"prep_{tag}_regs": np.array([T, pos, -1 if nn is None else nn]),
+                    f"prep_{tag}_qx": np.rint(np.asarray(arr["qx"], np.float64)).astype(np.int64),
+                    f"prep_{tag}_ck": np.rint(states["ck"] * p2(fkc)[None, :]).astype(np.int64),
+                    f"prep_{tag}_cv": np.rint(states["cv"] * p2(fvc)[None, :]).astype(np.int64)})
+    np.savez_compressed(os.path.join(out, "sim_llm_host.npz"), **res)
+    print("sim_llm_host.npz:", len(res), "arrays")
+
+
 def make_numeric(ref, out):
     """The exponent planner: the reference's weight encodings
     (src/numeric.py encode_matmul_weights / encode_conv_weights) on MatMul and
@@ -883,7 +1017,7 @@ def make_conv_exp(ref, out):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--ref", default="/root/reference")
-    ap.add_argument("--only", choices=["hw", "sim", "graph", "llm", "attn", "smx", "numeric", "convexp"])
+    ap.add_argument("--only", choices=["hw", "sim", "graph", "llm", "attn", "smx", "numeric", "convexp", "llmhost"])
     ap.add_argument("--out", default=HERE)
     args = ap.parse_args()
     if args.only in (None, "hw"):
@@ -902,6 +1036,8 @@ def main():
         make_numeric(args.ref, args.out)
     if args.only in (None, "convexp"):
         make_conv_exp(args.ref, args.out)
+    if args.only in (None, "llmhost"):
+        make_llm_host(args.ref, args.out)
 
 
 if __name__ == "__main__":
