@@ -292,6 +292,96 @@ __global__ void __launch_bounds__(256) conv_dw_plane(ConvArgs a, uint32_t SH, ui
   }
 }
 
+// Depthwise 3x3 (dilation 1, stride S_) on planes whose rows are whole
+// 16-byte words (W a multiple of 8, 16-byte aligned x), dense output: a CTA
+// takes G (n, m) planes at a time and stages each one's input window in
+// shared memory with 16-byte loads, input column iw at column iw + 8 of a
+// padded row of SP = W + 16 entries (zero columns on both sides, zero rows
+// outside the image), so every staged row starts on a 16-byte boundary; the
+// taps follow.  Then each thread computes columns of four outputs that share
+// their input rows, the taps' products accumulated as widening multiply-adds
+// seeded with bias << 8.
+template <int S_>
+__global__ void __launch_bounds__(256) conv_dw_vec(ConvArgs a, uint32_t SH, uint32_t G) {
+  corm_pdl_wait();
+  corm_pdl_trigger();
+  extern __shared__ __align__(16) int16_t s_vin[];  // [G][SH][SP], then [G][16] taps
+  __shared__ int16_t* s_yp[kDwMaxG];
+  __shared__ int64_t s_b0[kDwMaxG];
+  __shared__ uint32_t s_m[kDwMaxG];
+  constexpr int NR = 4, R = (NR - 1) * S_ + 3;
+  const uint32_t SP = a.W + 16u, PS = SH * SP, WV = a.W / 8u;
+  const uint32_t P = a.OH * a.OW;
+  int16_t* s_w = s_vin + (size_t)G * PS;
+  const uint64_t planes = (uint64_t)a.batch * a.M;
+  const uint32_t items = a.OW * ((a.OH + NR - 1) / NR);
+  for (uint64_t base = (uint64_t)blockIdx.x * G; base < planes; base += (uint64_t)gridDim.x * G) {
+    if (threadIdx.x < G) {
+      const uint64_t plane = base + threadIdx.x;
+      const bool live = plane < planes;
+      const uint32_t m = live ? (uint32_t)(plane % a.M) : 0u, n = live ? (uint32_t)(plane / a.M) : 0u;
+      s_yp[threadIdx.x] = live ? a.y + (uint64_t)n * a.M * P + (uint64_t)m * P : nullptr;
+      s_b0[threadIdx.x] = live && a.bias ? (int64_t)a.bias[m] << 8 : 0;
+      s_m[threadIdx.x] = m;
+    }
+    // the windows: per staged row, 8 zero columns, the row's W / 8 words, 8 zero columns
+    const uint32_t wpr = WV + 2u;  // 16-byte words per staged row
+    const uint32_t nwords = G * SH * wpr;
+    for (uint32_t i = threadIdx.x; i < nwords; i += blockDim.x) {
+      const uint32_t row = i / wpr, wc = i - row * wpr;
+      const uint32_t gg = row / SH, r = row - gg * SH;
+      const uint64_t plane = base + gg;
+      const int ih = (int)r - (int)a.pt;
+      int4 v = make_int4(0, 0, 0, 0);
+      if (wc >= 1u && wc <= WV && plane < planes && ih >= 0 && ih < (int)a.H)
+        v = __ldg((const int4*)(a.x + (plane * a.H + (uint64_t)ih) * a.W) + (wc - 1u));
+      ((int4*)(s_vin + (size_t)row * SP))[wc] = v;
+    }
+    for (uint32_t i = threadIdx.x; i < G * 9u; i += blockDim.x) {
+      const uint32_t gg = i / 9u, tap = i - gg * 9u;
+      const uint64_t plane = base + gg;
+      s_w[gg * 16u + tap] =
+          plane < planes ? __ldg(a.w + w_offset(a, (uint32_t)(plane % a.M), 0, tap / 3u, tap % 3u)) : (int16_t)0;
+    }
+    __syncthreads();
+    const uint32_t work = G * items;
+    for (uint32_t idx = threadIdx.x; idx < work; idx += blockDim.x) {
+      const uint32_t g = idx / items, it = idx - g * items;
+      int16_t* yp = s_yp[g];
+      if (!yp) continue;
+      const int16_t* wt = s_w + g * 16u;
+      int32_t wr[9];
+#pragma unroll
+      for (int q = 0; q < 9; q++) wr[q] = wt[q];
+      const uint32_t ob = it / a.OW, ow = it - ob * a.OW, oh0 = ob * NR;
+      // window column c = iw + pl lives at staged column c - pl + 8
+      const int16_t* x0 = s_vin + (size_t)g * PS + (size_t)(oh0 * S_) * SP + ow * S_ + 8u - a.pl;
+      const uint32_t rows_ok = SH - oh0 * S_;
+      long long acc[NR];
+#pragma unroll
+      for (int r = 0; r < NR; r++) acc[r] = s_b0[g];
+#pragma unroll
+      for (int q = 0; q < R; q++) {
+        if ((uint32_t)q >= rows_ok) break;
+        const int32_t x_0 = x0[q * SP], x_1 = x0[q * SP + 1], x_2 = x0[q * SP + 2];
+#pragma unroll
+        for (int r = 0; r < NR; r++) {
+          const int i = q - r * S_;
+          if (i >= 0 && i < 3) {
+            acc[r] += (long long)x_0 * wr[3 * i];
+            acc[r] += (long long)x_1 * wr[3 * i + 1];
+            acc[r] += (long long)x_2 * wr[3 * i + 2];
+          }
+        }
+      }
+#pragma unroll
+      for (int r = 0; r < NR; r++)
+        if (oh0 + r < a.OH) conv_put(a, yp, (oh0 + r) * a.OW + ow, s_m[g], acc[r]);
+    }
+    __syncthreads();
+  }
+}
+
 // Depthwise 3x3 (dilation 1, stride S_) on small planes, a warp per plane:
 // the warp zeroes its padded window in shared memory, scatters the plane's
 // H*W inputs into it (flat coalesced loads, eight in flight per lane), reads
@@ -482,6 +572,27 @@ int conv_impl(const corm_conv_desc* d, const corm::PostOp& post, cudaStream_t st
     const uint32_t SW = (d->out_w - 1) * d->stride_w + (d->kw - 1) * d->dilation_w + 1;
     const bool dw3 = d->kh == 3 && d->kw == 3 && d->dilation_h == 1 && d->dilation_w == 1 &&
                      d->stride_h == d->stride_w && (d->stride_h == 1 || d->stride_h == 2);
+    // whole 16-byte rows and a dense output: the vector-staged planes
+    const bool vec = dw3 && d->in_w % 8u == 0 && !((uintptr_t)d->x & 15u) && d->y_cn == 0 &&
+                     (d->y_cs == 0 || d->y_cs == P) && d->pad_left <= 8u && SW <= d->in_w + 8u + d->pad_left &&
+                     (size_t)SH * (d->in_w + 16u) * 2u <= 96u * 1024u;
+    if (vec) {
+      const size_t plane_b = (size_t)SH * (d->in_w + 16u) * sizeof(int16_t);
+      const uint32_t G = (uint32_t)std::min<size_t>(kDwMaxG, std::max<size_t>(1, (48u * 1024u) / plane_b));
+      const size_t smem = G * plane_b + (size_t)G * 16u * sizeof(int16_t);
+      const uint64_t planes = (uint64_t)d->batch * d->out_ch;
+      const unsigned grid = (unsigned)std::min<uint64_t>((planes + G - 1) / G, 148ull * 8ull);
+      corm::ProfScope prof_("conv_dw_vec", st);
+      auto launch = [&](auto kern) {
+        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        corm_launch_pdl(kern, dim3(grid), dim3(256), smem, st, a, SH, G);
+      };
+      if (d->stride_h == 1)
+        launch(conv_dw_vec<1>);
+      else
+        launch(conv_dw_vec<2>);
+      return corm::cuda_status("conv depthwise");
+    }
     if (dw3 && (size_t)SH * SW <= kDwWarpWin && d->in_w <= 32u * 32u) {
       const uint64_t planes = (uint64_t)d->batch * d->out_ch;
       const unsigned grid = (unsigned)std::min<uint64_t>((planes + 7) / 8, 148ull * 8ull);

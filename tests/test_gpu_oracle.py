@@ -95,6 +95,13 @@ CONV_CASES = [  # N, C, H, W, M, kh, kw, sh, sw, pt, pl, dh, dw, depthwise, bias
     (1, 17, 7, 7, 17, 3, 3, 2, 2, 1, 1, 1, 1, True, True),
     (2, 6, 40, 37, 6, 3, 3, 1, 1, 1, 1, 1, 1, True, True),
     (2, 6, 45, 44, 6, 3, 3, 2, 2, 1, 1, 1, 1, True, True),
+    # depthwise 3x3 on rows of whole 16-byte words (vector-staged windows):
+    # stride 1 / 2, pads 0 / 1 / 2, odd heights, a plane per CTA and several
+    (2, 16, 16, 24, 16, 3, 3, 1, 1, 1, 1, 1, 1, True, True),
+    (1, 8, 32, 32, 8, 3, 3, 2, 2, 1, 1, 1, 1, True, True),
+    (2, 4, 9, 16, 4, 3, 3, 1, 1, 0, 0, 1, 1, True, False),
+    (1, 3, 9, 8, 3, 3, 3, 2, 2, 0, 0, 1, 1, True, True),
+    (1, 5, 20, 112, 5, 3, 3, 2, 2, 2, 2, 1, 1, True, True),
     (1, 5, 30, 30, 5, 5, 5, 1, 1, 2, 2, 1, 1, True, True),
 ]
 
