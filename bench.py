@@ -201,7 +201,8 @@ def main():
     ap.add_argument("--no-models", action="store_true", help="skip the MNIST / MobileNetV2 / BERT forward passes")
     ap.add_argument("--models", help="comma list of model cases to run (default: all)")
     ap.add_argument("--detail", help="write per-problem kernel times of one profiled step to this JSON file")
-    ap.add_argument("--case", choices=["gemm", "gemm_small", "gemm_int16", "vectorop", "softmax", "conv",
+    ap.add_argument("--case", choices=["gemm", "gemm_small", "gemm_int16", "vectorop", "softmax", "softmax_col",
+                                       "layernorm", "rmsnorm32", "dwconv", "pwconv", "maxpool", "conv",
                                        "llama_prefill", "llama_decode"],
                     help="run one job a few times (a small case for ncu captures) and exit")
     args = ap.parse_args()
@@ -903,6 +904,52 @@ def run_case(args):
         x, p = ri(N, -2048, 2048), torch.empty(N, dtype=torch.int16, device="cuda")
         fn = lambda: ops.vectorop(x, None, p, size=1024, op=10, outer=N // 1024, a_inc=1024, b_inc=1024,  # noqa
                                   smx_cm=12102203, smx_cfg=19 | (8 << 8), smx_mask=1024)
+    elif args.case == "softmax_col":  # keys-major, 512 keys x 64K queries (a prefill head group's scores)
+        N = 1 << 25
+        x, p = ri(N, -2048, 2048), torch.empty(N, dtype=torch.int16, device="cuda")
+        fn = lambda: ops.vectorop(x, None, p, size=512, op=11, outer=N // 512, a_inc=N // 512, b_inc=512,  # noqa
+                                  smx_cm=12102203, smx_cfg=19 | (8 << 8), smx_mask=512)
+    elif args.case in ("layernorm", "rmsnorm32"):
+        # BERT's LayerNorm (24576 rows x 768 int16) / Llama's RMSNorm of the
+        # int32 residual (32768 rows x 960), the parameter blocks as the graphs build them
+        import numpy as np
+
+        from cormorant_b200 import rowops_host as RH
+        if args.case == "layernorm":
+            R_, n = 24576, 768
+            words, g_, bb, E = RH.layernorm_job(np.ones(n), np.zeros(n), n, 1e-12)
+            x = ri(R_ * n)
+            op = RH.opword(RH.OP_NORM, ln=True)
+            regs = dict(eps=int(E), bq_sh=RH.P1_BITS + g_ - bb, a_s1=2 * n)
+        else:
+            R_, n = 32768, 960
+            words, bc, g_, E = RH.rmsnorm_job(np.ones(n), 1e-5, 15, np.full(n, 12))
+            x = torch.randint(-(1 << 24), 1 << 24, (R_ * n,), dtype=torch.int32, device="cuda", generator=g)
+            op = RH.opword(RH.OP_NORM, RH.K_I32, RH.K_I16, RH.K_I16, p_bcast=bool(bc))
+            regs = dict(eps=int(E), bq_sh=0, a_s1=4 * n)
+        pw = torch.from_numpy(np.asarray(words, np.int16)).cuda()
+        y = torch.empty(R_ * n + 8, dtype=torch.int16, device="cuda")
+        fn = lambda: ops.rowops(x, None, y, pw, op=op, n=n, rows=R_, blocks=1, c_s1=2 * n, win_lo=0,  # noqa
+                                win_hi=RH.NO_WINDOW, **regs)
+    elif args.case in ("dwconv", "pwconv"):
+        # MobileNetV2's second block at batch 64: the 3x3 stride-2 depthwise over
+        # 96 x 112 x 112, and the 1 x 1 expand 24 -> 144 over 56 x 56
+        if args.case == "dwconv":
+            N_, C_, H_, M_, k, s_, oh = 64, 96, 112, 96, 3, 2, 56
+        else:
+            N_, C_, H_, M_, k, s_, oh = 64, 24, 56, 144, 1, 1, 56
+        x = ri(N_ * C_ * H_ * H_)
+        w = ri(M_ * (1 if args.case == "dwconv" else C_) * k * k, -64, 64)
+        b = ri(M_, -64, 64)
+        y = torch.empty(N_ * M_ * oh * oh, dtype=torch.int16, device="cuda")
+        fn = lambda: ops.conv(x, w, b, y, batch=N_, in_ch=C_, in_h=H_, in_w=H_, out_ch=M_, out_h=oh, out_w=oh,  # noqa
+                              kh=k, kw=k, stride_h=s_, stride_w=s_, pad_top=k // 2, pad_left=k // 2, has_bias=1,
+                              is_depthwise=int(args.case == "dwconv"), flags=2 | 8)
+    elif args.case == "maxpool":  # MNIST's first pool at batch 8192
+        x = ri(8192 * 16 * 28 * 28)
+        y = torch.empty(8192 * 16 * 14 * 14 + 8, dtype=torch.int16, device="cuda")
+        fn = lambda: ops.pool(x, y, batch=8192, channels=16, in_h=28, in_w=28, out_h=14, out_w=14, pool_h=2,  # noqa
+                              pool_w=2, stride_h=2, stride_w=2)
     elif args.case in ("llama_prefill", "llama_decode"):
         # two layers of the config-5 model (every kernel of a layer, a layer's
         # shapes): the prefill of 16 sequences x 512 tokens, or after it one
