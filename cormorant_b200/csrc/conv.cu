@@ -292,6 +292,228 @@ __global__ void __launch_bounds__(256) conv_dw_plane(ConvArgs a, uint32_t SH, ui
   }
 }
 
+// Depthwise 3 x 3 (dilation 1, stride S_ of 1 or 2, left pad PL_ of 0 or 1)
+// as runs of eight outputs.  A CTA takes units of G consecutive (n, m) planes
+// and stages each plane's input in shared memory as rows of SPW 16-byte words,
+// input column iw at staged column iw + 8 (word 0 and the words past the row
+// are zeros) and input row ih at staged row ih + pt (zero rows above and
+// below), so that a run's window is whole 16-byte words: three per input row
+// at stride 1, four at stride 2.  ROWS: the rows themselves are whole words
+// (W % 8 == 0), each staged word one 16-byte load; otherwise the G planes are
+// one contiguous range (G H W a multiple of 8) read in 16-byte words and
+// scattered.  A thread then takes a run of eight columns over NR output rows,
+// each input row read once from shared memory and its values multiplied into
+// every output row that uses it.  The sums run in 32 bits when they cannot
+// leave int32 — under the wrap rule always (the wrapping 32-bit sum is the
+// rule's value), otherwise when |bias| 2^8 + 2^15 sum|w| < 2^31 for the channel
+// — and in 64 bits per output otherwise.
+struct DwGeo {
+  uint32_t G;      // planes per unit
+  uint32_t SHb;    // staged rows per plane
+  uint32_t SPW;    // staged 16-byte words per row
+  uint32_t RUNS;   // runs of eight outputs per output row
+  uint32_t NRG;    // groups of NR output rows per plane
+  uint32_t units;  // ceil(planes / G)
+  uint32_t vst;    // dense 16-byte output rows (OW % 8 == 0, dense y, aligned, no fused job)
+};
+constexpr uint32_t kDw3MaxG = 64;
+constexpr int kDw3NR = 4;
+
+__device__ __forceinline__ void dw3_slow(const ConvArgs& a, const int16_t* win, uint32_t SP, int S, int PL,
+                                      const int16_t* wt, int64_t b0, uint32_t oh0, uint32_t ow0, int16_t* yp,
+                                      uint32_t m) {
+  for (int r = 0; r < kDw3NR; r++) {
+    const uint32_t oh = oh0 + r;
+    if (oh >= a.OH) break;
+    for (int t = 0; t < 8; t++) {
+      const uint32_t ow = ow0 + t;
+      if (ow >= a.OW) break;
+      int64_t acc = b0;
+      for (int ky = 0; ky < 3; ky++)
+        for (int kx = 0; kx < 3; kx++)
+          acc += (int64_t)((int32_t)win[(oh * S + ky) * SP + ow * S + kx + 8 - PL] * (int32_t)wt[3 * ky + kx]);
+      conv_put(a, yp, (uint64_t)oh * a.OW + ow, m, acc);
+    }
+  }
+}
+
+template <int S_, int PL_, bool ROWS>
+__global__ void __launch_bounds__(256) conv_dw3x3(ConvArgs a, DwGeo q) {
+  corm_pdl_wait();
+  corm_pdl_trigger();
+  extern __shared__ __align__(16) int16_t s_in[];  // [G][SHb][SPW * 8]
+  __shared__ int16_t* s_yp[kDw3MaxG];
+  __shared__ int32_t s_b[kDw3MaxG];
+  __shared__ int16_t s_w[kDw3MaxG][10];
+  __shared__ uint32_t s_m[kDw3MaxG];
+  __shared__ uint8_t s_fast[kDw3MaxG];
+  constexpr int NR = kDw3NR;
+  constexpr int QR = (NR - 1) * S_ + 3;  // input rows of a group of NR output rows
+  constexpr int NWIN = S_ == 1 ? 3 : 4;  // window words per input row
+  const uint32_t SP = q.SPW * 8u, PS = q.SHb * SP;
+  const uint32_t HW = a.H * a.W, P = a.OH * a.OW;
+  const uint64_t planes = (uint64_t)a.batch * a.M;
+  const uint32_t RUNSin = (a.W + 7u) / 8u;
+  const bool wrap = (a.flags & CORM_F_WRAP32) != 0;
+  for (uint32_t unit = blockIdx.x; unit < q.units; unit += gridDim.x) {
+    const uint64_t p0 = (uint64_t)unit * q.G;
+    const uint32_t glive = (uint32_t)(planes - p0 < (uint64_t)q.G ? planes - p0 : (uint64_t)q.G);
+    if (threadIdx.x < glive) {
+      const uint64_t plane = p0 + threadIdx.x;
+      const uint32_t m = (uint32_t)(plane % a.M), n = (uint32_t)(plane / a.M);
+      s_yp[threadIdx.x] = a.y + (uint64_t)n * a.M * P + y_chan(a, m);
+      const int32_t b = a.bias ? (int32_t)a.bias[m] : 0;
+      uint32_t sw = 0;
+#pragma unroll
+      for (int t = 0; t < 9; t++) {
+        const int16_t w = __ldg(a.w + w_offset(a, m, 0, t / 3, t % 3));
+        s_w[threadIdx.x][t] = w;
+        sw += (uint32_t)(w < 0 ? -(int32_t)w : (int32_t)w);
+      }
+      s_b[threadIdx.x] = b << 8;
+      s_m[threadIdx.x] = m;
+      // |acc| <= |b| 2^8 + 2^15 sum|w| (sum|w| <= 9 * 2^15 keeps this below 2^63)
+      const int64_t bound = (int64_t)(b < 0 ? -b : b) * 256 + (int64_t)sw * 32768;
+      s_fast[threadIdx.x] = (wrap || bound <= 2147483647ll) ? 1 : 0;
+    }
+    if (ROWS) {
+      // every staged word written once: data, or zeros outside the image / row
+      const uint32_t nw = q.G * q.SHb * q.SPW;
+      for (uint32_t i0 = 0; i0 < nw; i0 += 4u * blockDim.x) {
+        int4 v[4];
+        uint32_t dst[4];
+#pragma unroll
+        for (int k = 0; k < 4; k++) {
+          const uint32_t i = i0 + k * blockDim.x + threadIdx.x;
+          v[k] = make_int4(0, 0, 0, 0);
+          dst[k] = 0xFFFFFFFFu;
+          if (i < nw) {
+            const uint32_t g = i / (q.SHb * q.SPW), rem = i - g * (q.SHb * q.SPW);
+            const uint32_t sr = rem / q.SPW, w = rem - sr * q.SPW;
+            const int ih = (int)sr - (int)a.pt;
+            dst[k] = g * PS + sr * SP + 8u * w;
+            if (g < glive && w >= 1u && w <= RUNSin && ih >= 0 && ih < (int)a.H)
+              v[k] = __ldg((const int4*)(a.x + ((p0 + g) * a.H + (uint32_t)ih) * a.W) + (w - 1u));
+          }
+        }
+#pragma unroll
+        for (int k = 0; k < 4; k++)
+          if (dst[k] != 0xFFFFFFFFu) *(int4*)(s_in + dst[k]) = v[k];
+      }
+    } else {
+      const uint32_t nz = q.G * PS / 8u;
+      for (uint32_t i = threadIdx.x; i < nz; i += blockDim.x) ((int4*)s_in)[i] = make_int4(0, 0, 0, 0);
+      __syncthreads();
+      const uint64_t E = (uint64_t)glive * HW;  // elements of the unit's planes, from p0 H W (a multiple of 8)
+      const uint32_t nw = (uint32_t)((E + 7u) / 8u);
+      const int16_t* src = a.x + p0 * HW;
+      for (uint32_t i0 = 0; i0 < nw; i0 += 4u * blockDim.x) {
+        int4 v[4];
+#pragma unroll
+        for (int k = 0; k < 4; k++) {
+          const uint32_t i = i0 + k * blockDim.x + threadIdx.x;
+          v[k] = make_int4(0, 0, 0, 0);
+          if (8ull * i + 8u <= E) {
+            v[k] = __ldg((const int4*)src + i);
+          } else if (8ull * i < E) {  // the last, partial word
+            uint32_t pr[4] = {0u, 0u, 0u, 0u};
+#pragma unroll
+            for (int t = 0; t < 8; t++)
+              if (8ull * i + t < E) pr[t / 2] |= (uint32_t)(uint16_t)__ldg(src + 8ull * i + t) << (16 * (t & 1));
+            v[k] = make_int4((int)pr[0], (int)pr[1], (int)pr[2], (int)pr[3]);
+          }
+        }
+#pragma unroll
+        for (int k = 0; k < 4; k++) {
+          const uint32_t i = i0 + k * blockDim.x + threadIdx.x;
+          if (8ull * i >= E) continue;
+          const uint32_t f = 8u * i;
+          uint32_t g = f / HW, r = f - g * HW;
+          uint32_t ih = r / a.W, iw = r - ih * a.W;
+          const uint32_t pr[4] = {(uint32_t)v[k].x, (uint32_t)v[k].y, (uint32_t)v[k].z, (uint32_t)v[k].w};
+#pragma unroll
+          for (int t = 0; t < 8; t++) {
+            const uint32_t sr = ih + a.pt;
+            if (f + t < E && sr < q.SHb) s_in[g * PS + sr * SP + iw + 8u] = (int16_t)(pr[t / 2] >> (16 * (t & 1)));
+            if (++iw == a.W) {
+              iw = 0;
+              if (++ih == a.H) {
+                ih = 0;
+                g++;
+              }
+            }
+          }
+        }
+      }
+    }
+    __syncthreads();
+    const uint32_t per_plane = q.NRG * q.RUNS, work = glive * per_plane;
+    for (uint32_t idx = threadIdx.x; idx < work; idx += blockDim.x) {
+      const uint32_t g = idx / per_plane, rem = idx - g * per_plane;
+      const uint32_t rg = rem / q.RUNS, j = rem - rg * q.RUNS;
+      const uint32_t oh0 = rg * NR;
+      const int16_t* win = s_in + g * PS;
+      int16_t* yp = s_yp[g];
+      if (!s_fast[g]) {
+        dw3_slow(a, win, SP, S_, PL_, s_w[g], s_b[g], oh0, 8u * j, yp, s_m[g]);
+        continue;
+      }
+      int32_t w9[9];
+#pragma unroll
+      for (int t = 0; t < 9; t++) w9[t] = s_w[g][t];
+      uint32_t acc[NR][8];
+#pragma unroll
+      for (int r = 0; r < NR; r++)
+#pragma unroll
+        for (int t = 0; t < 8; t++) acc[r][t] = (uint32_t)s_b[g];
+      // the window's first word: S_ 1 -> j, S_ 2 -> 2 j; value v[8 - PL_ + S_ t + kx] is input column S_ (8 j + t) - PL_ + kx
+      const int16_t* row0 = win + (oh0 * S_) * SP + 8u * (S_ == 1 ? j : 2u * j);
+#pragma unroll
+      for (int qr = 0; qr < QR; qr++) {
+        int32_t x[8 * NWIN];
+#pragma unroll
+        for (int u = 0; u < NWIN; u++) {
+          const int4 wv = *(const int4*)(row0 + qr * SP + 8 * u);
+          const uint32_t pr[4] = {(uint32_t)wv.x, (uint32_t)wv.y, (uint32_t)wv.z, (uint32_t)wv.w};
+#pragma unroll
+          for (int h = 0; h < 4; h++) {
+            x[8 * u + 2 * h] = (int32_t)(pr[h] << 16) >> 16;
+            x[8 * u + 2 * h + 1] = (int32_t)pr[h] >> 16;
+          }
+        }
+#pragma unroll
+        for (int r = 0; r < NR; r++) {
+          const int ky = qr - r * S_;
+          if (ky < 0 || ky > 2) continue;
+#pragma unroll
+          for (int t = 0; t < 8; t++) {
+            const int c0 = 8 - PL_ + S_ * t;
+            acc[r][t] += (uint32_t)(x[c0] * w9[3 * ky]) + (uint32_t)(x[c0 + 1] * w9[3 * ky + 1]) +
+                         (uint32_t)(x[c0 + 2] * w9[3 * ky + 2]);
+          }
+        }
+      }
+#pragma unroll
+      for (int r = 0; r < NR; r++) {
+        const uint32_t oh = oh0 + r;
+        if (oh >= a.OH) break;
+        if (q.vst) {
+          int4 o;
+          int16_t* os = (int16_t*)&o;
+#pragma unroll
+          for (int t = 0; t < 8; t++) os[t] = conv_finish((int64_t)(int32_t)acc[r][t], a.flags);
+          *(int4*)(yp + (uint64_t)oh * a.OW + 8u * j) = o;
+        } else {
+#pragma unroll
+          for (int t = 0; t < 8; t++)
+            if (8u * j + t < a.OW) conv_put(a, yp, (uint64_t)oh * a.OW + 8u * j + t, s_m[g], (int64_t)(int32_t)acc[r][t]);
+        }
+      }
+    }
+    __syncthreads();
+  }
+}
+
 // Depthwise 3x3 (dilation 1, stride S_) on planes whose rows are whole
 // 16-byte words (W a multiple of 8, 16-byte aligned x), dense output: a CTA
 // takes G (n, m) planes at a time and stages each one's input window in
@@ -572,6 +794,53 @@ int conv_impl(const corm_conv_desc* d, const corm::PostOp& post, cudaStream_t st
     const uint32_t SW = (d->out_w - 1) * d->stride_w + (d->kw - 1) * d->dilation_w + 1;
     const bool dw3 = d->kh == 3 && d->kw == 3 && d->dilation_h == 1 && d->dilation_w == 1 &&
                      d->stride_h == d->stride_w && (d->stride_h == 1 || d->stride_h == 2);
+    // 3 x 3 as runs of eight outputs over staged planes (left pad 0 or 1, 16-byte aligned x)
+    if (dw3 && d->pad_left <= 1u && !((uintptr_t)d->x & 15u)) {
+      const uint32_t S = d->stride_h, NR = (uint32_t)kDw3NR;
+      DwGeo q{};
+      q.NRG = (d->out_h + NR - 1) / NR;
+      q.RUNS = (d->out_w + 7u) / 8u;
+      const uint32_t runs_in = (d->in_w + 7u) / 8u, HW = d->in_h * d->in_w;
+      q.SHb = (q.NRG * NR - 1) * S + 3;
+      q.SPW = std::max(runs_in + 2u, S == 1 ? q.RUNS + 2u : 2u * q.RUNS + 2u);
+      const size_t plane_b = (size_t)q.SHb * q.SPW * 16u;
+      const bool rows = d->in_w % 8u == 0;
+      // whole planes read as one range: G H W a multiple of 8 keeps every unit's start on a 16-byte boundary
+      uint32_t unit = 1;
+      if (!rows) {
+        unit = 8;
+        while (unit > 1 && (uint64_t)(unit / 2) * HW % 8u == 0) unit /= 2;
+      }
+      uint32_t G = (uint32_t)std::min<size_t>(kDw3MaxG, std::max<size_t>(1, (32u * 1024u) / plane_b));
+      G = std::max(unit, G / unit * unit);
+      const size_t smem = (size_t)G * plane_b;
+      if (G <= kDw3MaxG && smem <= 100u * 1024u) {
+        const uint64_t planes = (uint64_t)d->batch * d->out_ch;
+        q.G = G;
+        q.units = (uint32_t)((planes + G - 1) / G);
+        q.vst = d->out_w % 8u == 0 && d->y_cn == 0 && (d->y_cs == 0 || d->y_cs == P) && !((uintptr_t)d->y & 15u) &&
+                a.post.op == corm::kPostNone;
+        const unsigned per_sm = (unsigned)std::max<size_t>(1, std::min<size_t>(8, (200u * 1024u) / (smem + 4096u)));
+        const unsigned grid = (unsigned)std::min<uint64_t>(q.units, 148ull * per_sm);
+        corm::ProfScope prof_("conv_dw3x3", st);
+        auto launch = [&](auto kern) {
+          cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+          corm_launch_pdl(kern, dim3(grid), dim3(256), smem, st, a, q);
+        };
+        const int pick = (S == 2 ? 4 : 0) + (d->pad_left ? 2 : 0) + (rows ? 1 : 0);
+        switch (pick) {
+          case 0: launch(conv_dw3x3<1, 0, false>); break;
+          case 1: launch(conv_dw3x3<1, 0, true>); break;
+          case 2: launch(conv_dw3x3<1, 1, false>); break;
+          case 3: launch(conv_dw3x3<1, 1, true>); break;
+          case 4: launch(conv_dw3x3<2, 0, false>); break;
+          case 5: launch(conv_dw3x3<2, 0, true>); break;
+          case 6: launch(conv_dw3x3<2, 1, false>); break;
+          default: launch(conv_dw3x3<2, 1, true>); break;
+        }
+        return corm::cuda_status("conv depthwise");
+      }
+    }
     // whole 16-byte rows and a dense output: the vector-staged planes
     const bool vec = dw3 && d->in_w % 8u == 0 && !((uintptr_t)d->x & 15u) && d->y_cn == 0 &&
                      (d->y_cs == 0 || d->y_cs == P) && d->pad_left <= 8u && SW <= d->in_w + 8u + d->pad_left &&

@@ -402,6 +402,12 @@ __global__ void __launch_bounds__(Roles<CONV>::threads, 1)
   uint32_t* tmem_slot = (uint32_t*)(a_free + 2);
   uint32_t* abort_at = tmem_slot + 1;  // first ring step a splitting warp gave up at
   volatile int* cta_stop = (volatile int*)(abort_at + 1);  // a role of this CTA gave up (bounded waits)
+  // The bounded waits: the production kernel has a compile-time limit and no
+  // stop word (once one role has given up the others run out their own
+  // limits; polling the word cost the MatMul sweep 7 %); the diagnostic
+  // instantiation takes the host's limit and stops every role at once.
+  const long long wlim = DIAG ? ep.wait_limit : kWaitDefault;
+  volatile int* const wstop = DIAG ? cta_stop : nullptr;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t units = ep.batch * ep.tiles_m * ep.tiles_n * ep.splits;
@@ -446,7 +452,7 @@ __global__ void __launch_bounds__(Roles<CONV>::threads, 1)
       const int a_z = ep.a_planes == 1 ? 0 : (int)w.bz, b_z = ep.b_planes == 1 ? 0 : (int)w.bz;
       for (uint32_t kb = w.kb0; kb < w.kb1; kb++, g++) {
         const int s = g % STAGES;
-        if (g >= (uint32_t)STAGES && !sm100::mbar_wait(&empty[s], ((g / STAGES) - 1) & 1, ep.err, 101, DIAG ? ep.wait_limit : kWaitDefault, cta_stop)) {
+        if (g >= (uint32_t)STAGES && !sm100::mbar_wait(&empty[s], ((g / STAGES) - 1) & 1, ep.err, 101, wlim, wstop)) {
           ok = false;
           break;
         }
@@ -484,7 +490,7 @@ __global__ void __launch_bounds__(Roles<CONV>::threads, 1)
       const int a_z = ep.a_bs16 ? (int)w.bz : 0, b_z = ep.b_bs16 ? (int)w.bz : 0;
       for (uint32_t kb = w.kb0; kb < w.kb1; kb++, g++) {
         const int s = g % STAGES;
-        if (g >= (uint32_t)STAGES && !sm100::mbar_wait(&empty[s], ((g / STAGES) - 1) & 1, ep.err, 106, DIAG ? ep.wait_limit : kWaitDefault, cta_stop)) {
+        if (g >= (uint32_t)STAGES && !sm100::mbar_wait(&empty[s], ((g / STAGES) - 1) & 1, ep.err, 106, wlim, wstop)) {
           ok = false;
           break;
         }
@@ -535,8 +541,8 @@ __global__ void __launch_bounds__(Roles<CONV>::threads, 1)
       const uint32_t nrow = ep.rows - w.tile_r, ncol = ep.cols - w.tile_c;
       for (uint32_t kb = w.kb0; kb < w.kb1; kb++, g++) {
         const int s = g % STAGES;
-        bool okw = sm100::mbar_wait(&raw_full[s], (g / STAGES) & 1, ep.err, 105, DIAG ? ep.wait_limit : kWaitDefault, cta_stop);
-        if (g >= 2) okw = sm100::mbar_wait(&a_free[g & 1], ((g >> 1) - 1) & 1, ep.err, 109, DIAG ? ep.wait_limit : kWaitDefault, cta_stop) && okw;
+        bool okw = sm100::mbar_wait(&raw_full[s], (g / STAGES) & 1, ep.err, 105, wlim, wstop);
+        if (g >= 2) okw = sm100::mbar_wait(&a_free[g & 1], ((g >> 1) - 1) & 1, ep.err, 109, wlim, wstop) && okw;
         if (!okw) atomicMin(abort_at, g);
         sm100::tc_fence_after();  // the TMEM buffer's readers are done (a_free)
         uint8_t* st = smem + s * STAGE_BYTES;
@@ -617,7 +623,7 @@ __global__ void __launch_bounds__(Roles<CONV>::threads, 1)
       const int16_t* Bb = ep.b16 + (uint64_t)w.bz * ep.b_bs16;
       for (uint32_t kb = w.kb0; kb < w.kb1; kb++, g++) {
         const int s = g % STAGES;
-        if (g >= (uint32_t)STAGES && !sm100::mbar_wait(&empty[s], ((g / STAGES) - 1) & 1, ep.err, 101, DIAG ? ep.wait_limit : kWaitDefault, cta_stop)) {
+        if (g >= (uint32_t)STAGES && !sm100::mbar_wait(&empty[s], ((g / STAGES) - 1) & 1, ep.err, 101, wlim, wstop)) {
           ok = false;
           break;
         }
@@ -670,11 +676,11 @@ __global__ void __launch_bounds__(Roles<CONV>::threads, 1)
     bool ok = true;
     for (uint32_t u = blockIdx.x; u < units && ok; u += gridDim.x, i++) {
       const Unit w = unit_of(ep, u);
-      if (i > 0 && !sm100::mbar_wait(tmem_empty, (i - 1) & 1, ep.err, 104, DIAG ? ep.wait_limit : kWaitDefault, cta_stop)) break;
+      if (i > 0 && !sm100::mbar_wait(tmem_empty, (i - 1) & 1, ep.err, 104, wlim, wstop)) break;
       sm100::tc_fence_after();
       for (uint32_t kb = w.kb0; kb < w.kb1; kb++, g++) {
         const int s = g % STAGES;
-        if (!sm100::mbar_wait(&full[s], (g / STAGES) & 1, ep.err, 102, DIAG ? ep.wait_limit : kWaitDefault, cta_stop)) {
+        if (!sm100::mbar_wait(&full[s], (g / STAGES) & 1, ep.err, 102, wlim, wstop)) {
           ok = false;
           break;
         }
@@ -730,7 +736,7 @@ __global__ void __launch_bounds__(Roles<CONV>::threads, 1)
     for (uint32_t u = blockIdx.x; u < units; u += gridDim.x, i++) {
       const Unit w = unit_of(ep, u);
       if (u + gridDim.x >= units) corm_pdl_trigger();  // this CTA's last unit
-      if (!sm100::mbar_wait(tmem_full, i & 1, ep.err, 103, DIAG ? ep.wait_limit : kWaitDefault, cta_stop)) break;
+      if (!sm100::mbar_wait(tmem_full, i & 1, ep.err, 103, wlim, wstop)) break;
       sm100::tc_fence_after();
       const uint32_t r = w.tile_r + q * 32 + lane;
       const bool row_ok = r < ep.rows;

@@ -311,6 +311,21 @@ extern "C" int corm_matmul_post(const corm_matmul_desc* d, const corm_postop* po
 }
 
 namespace {
+// k = 0: every output is floor(0) = 0.  Each batch's n x m run is cleared, in
+// one call for all of them.
+int clear_outputs(const corm_matmul_desc* d, cudaStream_t st, const char* who) {
+  const size_t run = (size_t)d->n * d->m * 2;
+  cudaError_t e;
+  if (d->batch == 1)
+    e = cudaMemsetAsync(d->c, 0, run, st);
+  else if ((size_t)d->c_batch_stride * 2 >= run)
+    e = cudaMemset2DAsync(d->c, (size_t)d->c_batch_stride * 2, 0, run, d->batch, st);
+  else  // batches that share rows: clear from the first output to the last
+    e = cudaMemsetAsync(d->c, 0, (size_t)(d->batch - 1) * d->c_batch_stride * 2 + run, st);
+  if (e != cudaSuccess) return corm::cuda_status(who);
+  return CORM_OK;
+}
+
 int matmul_impl(const corm_matmul_desc* d, const corm::PostOp& post, cudaStream_t st) {
   if (int rc = validate(d)) return rc;
   if (int rc = corm::check_device()) return rc;
@@ -320,13 +335,7 @@ int matmul_impl(const corm_matmul_desc* d, const corm::PostOp& post, cudaStream_
     return corm::fail(CORM_EINVAL, "corm_matmul_post: k = 0");
   MmArgs p{d->a, d->b, d->c, d->n, d->k, d->m, d->batch, d->a_batch_stride, d->b_batch_stride, d->c_batch_stride,
            d->b_packed, d->gemv_kw, d->flags, post};
-  if (d->k == 0) {  // empty sum: floor(0) = 0 everywhere
-    for (uint32_t bt = 0; bt < d->batch; bt++)
-      for (uint32_t r = 0; r < d->n; r++)
-        if (cudaMemsetAsync(d->c + (uint64_t)bt * d->c_batch_stride + (uint64_t)r * d->m, 0, (size_t)d->m * 2, st))
-          return corm::cuda_status("corm_matmul memset");
-    return CORM_OK;
-  }
+  if (d->k == 0) return clear_outputs(d, st, "corm_matmul");  // empty sum: floor(0) = 0 everywhere
   const Plan pl = plan_of(d);
   void* ws = d->workspace;
   if (pl.bytes) {
@@ -434,18 +443,7 @@ extern "C" int corm_matmul_noalloc(const corm_matmul_desc* d, corm_stream_t stre
   cudaStream_t st = (cudaStream_t)stream;
   MmArgs p{d->a, d->b, d->c, d->n, d->k, d->m, d->batch, d->a_batch_stride, d->b_batch_stride, d->c_batch_stride,
            d->b_packed, d->gemv_kw, d->flags};
-  if (d->k == 0) {  // every output is 0: each batch's n x m run cleared, one call for all of them
-    const size_t run = (size_t)d->n * d->m * 2;
-    cudaError_t e;
-    if (d->batch == 1)
-      e = cudaMemsetAsync(d->c, 0, run, st);
-    else if ((size_t)d->c_batch_stride * 2 >= run)
-      e = cudaMemset2DAsync(d->c, (size_t)d->c_batch_stride * 2, 0, run, d->batch, st);
-    else  // batches that share rows: clear from the first output to the last
-      e = cudaMemsetAsync(d->c, 0, (size_t)(d->batch - 1) * d->c_batch_stride * 2 + run, st);
-    if (e != cudaSuccess) return corm::cuda_status("corm_matmul_noalloc memset");
-    return CORM_OK;
-  }
+  if (d->k == 0) return clear_outputs(d, st, "corm_matmul_noalloc");  // every output is 0
   const Plan pl = plan_of(d);
   if (pl.bytes > kNoAllocBytes)
     return corm::fail(CORM_ELIMIT, "corm_matmul_noalloc: the job needs %zu bytes of scratch, beyond the %zu-byte "

@@ -103,6 +103,22 @@ CONV_CASES = [  # N, C, H, W, M, kh, kw, sh, sw, pt, pl, dh, dw, depthwise, bias
     (1, 3, 9, 8, 3, 3, 3, 2, 2, 0, 0, 1, 1, True, True),
     (1, 5, 20, 112, 5, 3, 3, 2, 2, 2, 2, 1, 1, True, True),
     (1, 5, 30, 30, 5, 5, 5, 1, 1, 2, 2, 1, 1, True, True),
+    # depthwise 3x3 as runs of eight outputs: whole planes read as one range
+    # (H W of 49 / 196 / 143 / 784 elements: units of 8 / 2 / 8 / 1 planes, a
+    # ragged last unit and last word), rows of whole words, strides 1 / 2, left
+    # pads 0 / 1 with top pads 0..2, several row groups and runs per plane
+    (3, 12, 7, 7, 12, 3, 3, 1, 1, 1, 1, 1, 1, True, True),
+    (2, 13, 7, 7, 13, 3, 3, 2, 2, 1, 1, 1, 1, True, True),
+    (3, 10, 14, 14, 10, 3, 3, 2, 2, 1, 1, 1, 1, True, True),
+    (2, 33, 13, 11, 33, 3, 3, 1, 1, 0, 0, 1, 1, True, True),
+    (1, 70, 28, 28, 70, 3, 3, 1, 1, 1, 1, 1, 1, True, False),
+    (2, 9, 28, 28, 9, 3, 3, 2, 2, 1, 1, 1, 1, True, True),
+    (1, 6, 19, 17, 6, 3, 3, 2, 2, 0, 0, 1, 1, True, True),
+    (1, 4, 11, 10, 4, 3, 3, 1, 1, 2, 1, 1, 1, True, True),
+    (2, 3, 57, 56, 3, 3, 3, 2, 2, 1, 1, 1, 1, True, True),
+    (1, 2, 112, 112, 2, 3, 3, 1, 1, 1, 1, 1, 1, True, True),
+    (1, 3, 112, 112, 3, 3, 3, 2, 2, 1, 1, 1, 1, True, True),
+    (2, 5, 12, 40, 5, 3, 3, 2, 2, 0, 1, 1, 1, True, True),
 ]
 
 
@@ -126,6 +142,28 @@ def test_conv_vs_oracle(ops, case, act):
     elif act == 8:
         exp = np.clip(exp, 0, 1536)
     assert np.array_equal(y.cpu().numpy().reshape(N, M, oh, ow), exp)
+
+
+@pytest.mark.parametrize("wrap", [0, 1])
+@pytest.mark.parametrize("shape", [(2, 6, 9, 10, 1), (1, 5, 16, 16, 2)], ids=["flat_s1", "rows_s2"])
+def test_depthwise_full_range(ops, shape, wrap):
+    """Depthwise 3x3 on full-range operands: channels whose sums can leave
+    int32 (the 64-bit path) beside channels whose cannot (the 32-bit path) in
+    one unit; without the wrap rule the exact sums saturate, with it the 32-bit
+    sums wrap as the rule does."""
+    N, C, H, W, s_ = shape
+    rng = np.random.default_rng(31 + C + wrap)
+    x = rnd16(rng, (N, C, H, W), -32768, 32768)
+    w = rnd16(rng, (C, 1, 3, 3), -32768, 32768)
+    w[::2] //= 4096  # even channels: small taps (the bound holds), odd ones full range
+    b = rnd16(rng, (C,), -32768, 32768)
+    oh, ow = (H + 2 - 3) // s_ + 1, (W + 2 - 3) // s_ + 1
+    y = torch.full((N * C * oh * ow,), -8531, dtype=torch.int16, device="cuda")
+    ops.conv(dev(x.reshape(-1)), dev(w.reshape(-1)), dev(b), y, batch=N, in_ch=C, in_h=H, in_w=W, out_ch=C,
+             out_h=oh, out_w=ow, kh=3, kw=3, stride_h=s_, stride_w=s_, pad_top=1, pad_left=1, has_bias=1,
+             is_depthwise=1, flags=2 | wrap)
+    exp = spec.conv_raw(x, w, b, s_, s_, 1, 1, 1, 1, oh, ow, True, wrap=bool(wrap))
+    assert np.array_equal(y.cpu().numpy().reshape(N, C, oh, ow), exp)
 
 
 def test_conv_wrap(ops):

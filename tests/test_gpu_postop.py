@@ -70,6 +70,8 @@ CONVS = [  # N, C, H, W, M, k, s, p, depthwise
     (2, 20, 14, 12, 20, 3, 2, 0, True),
     (2, 6, 40, 37, 6, 3, 1, 1, True),
     (1, 5, 30, 30, 5, 5, 1, 2, True),
+    (2, 8, 16, 16, 8, 3, 2, 1, True),
+    (3, 7, 7, 7, 7, 3, 1, 1, True),
 ]
 
 

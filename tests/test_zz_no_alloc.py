@@ -71,6 +71,27 @@ def test_noalloc_matches_matmul_twice(lib, shape):
         assert np.array_equal(out, ref), f"call {call + 1}"
 
 
+@pytest.mark.parametrize("cbs", [0, 6 * 5, 6 * 5 + 13, 7], ids=["bcast", "dense", "gaps", "overlap"])
+def test_k0_clears_outputs_only(lib, cbs):
+    """K = 0: every output is floor(0) = 0, on both entry points; with a batch
+    stride above n m the words between the batches' outputs are left as they
+    were (one clearing call covers the batches)."""
+    n, m, batch = 6, 5, 3
+    L = lib.lib()
+    stream = torch.cuda.current_stream().cuda_stream
+    a = torch.zeros(8, dtype=torch.int16, device="cuda")
+    span = (batch - 1) * cbs + n * m
+    want = np.full(span + 8, 7, np.int16)
+    for bt in range(batch):
+        want[bt * cbs:bt * cbs + n * m] = 0
+    for fn in (L.corm_matmul, L.corm_matmul_noalloc):
+        c = torch.full((span + 8,), 7, dtype=torch.int16, device="cuda")
+        d = lib.MatmulDesc(a.data_ptr(), a.data_ptr(), c.data_ptr(), n, 0, m, batch, 0, 0, cbs, 0, 0, 0, None, 0)
+        assert fn(C.byref(d), stream) == 0, L.corm_last_error()
+        torch.cuda.synchronize()
+        assert np.array_equal(c.cpu().numpy(), want)
+
+
 def test_noalloc_rejects_oversized(lib):
     L = lib.lib()
     a = torch.zeros(8, dtype=torch.int16, device="cuda")
