@@ -207,7 +207,7 @@ def main():
     ap.add_argument("--models", help="comma list of model cases to run (default: all)")
     ap.add_argument("--detail", help="write per-problem kernel times of one profiled step to this JSON file")
     ap.add_argument("--case", choices=["gemm", "gemm_small", "gemm_int16", "vectorop", "softmax", "softmax_col",
-                                       "layernorm", "rmsnorm32", "dwconv", "pwconv", "maxpool", "conv",
+                                       "layernorm", "rmsnorm32", "dwconv", "dwconv14", "pwconv", "maxpool", "conv",
                                        "llama_prefill", "llama_decode"],
                     help="run one job a few times (a small case for ncu captures) and exit")
     args = ap.parse_args()
@@ -340,13 +340,10 @@ def main():
     macs_step = macs_of(problems)
     value = world * macs_step * args.steps / (total_ms * 1e-3) / 1e9
 
-    # per-kernel times of one eager step (events around every launch)
-    with torch.cuda.stream(stream):
-        flush.zero_()
-        ops.profile_read()
-        ops.profile_enable(True)
-        run_sweep()
-        ops.profile_enable(False)
+    # per-kernel times of one eager step (events around every launch), queued
+    # behind a gate so that the GPU runs them back to back, as in the graph,
+    # and no event interval holds host submission time
+    gated = profiled_step(torch, ops, stream, flush, run_sweep)
     prof = ops.profile_read()
     if args.detail and rank == 0:
         per = []
@@ -432,6 +429,9 @@ def main():
                          "work": "8 int8 tensor ops per int16 MAC (4 int8 products); tensor-path problems (M > 2)",
                          "gemm_launches_per_step": g_launches, "gemm_ms_per_step": round(g_ms, 4),
                          "all_kernels_ms_per_step": round(step_kernel_ms, 4),
+                         "timing": "CUDA events around every launch of one eager step queued behind a sleep kernel "
+                                   "(launches back to back on the GPU, no host time inside an interval: %s)"
+                                   % ("held" if gated else "gate ran out"),
                          "kernels": {k: {"launches": v[0], "ms": round(v[1], 4)} for k, v in sorted(prof.items())}},
             "clocks": clk,
             "parity": parity,
@@ -448,6 +448,31 @@ def main():
         pg.barrier()
         pg.destroy_process_group()
     return 0
+
+
+def profiled_step(torch, ops, stream, flush, fn, gate_ms=40.0):
+    """One eager pass of ``fn`` with the library's per-launch events on,
+    queued behind a bounded sleep kernel (``gate_ms`` of clock cycles) so that
+    every launch is on the stream before the GPU reaches it: the events then
+    time the kernels alone, back to back.  Returns whether the gate held (the
+    GPU was still in the sleep when the host had queued the whole pass); if
+    not, the pass is repeated once with a longer gate."""
+    for _ in range(2):
+        with torch.cuda.stream(stream):
+            flush.zero_()
+            ops.profile_read()
+            torch.cuda._sleep(int(gate_ms * 1e-3 * 2.1e9))
+            gate_end = torch.cuda.Event()
+            gate_end.record(stream)
+            ops.profile_enable(True)
+            fn()
+            ops.profile_enable(False)
+            held = not gate_end.query()
+        torch.cuda.synchronize()
+        if held:
+            return True
+        gate_ms *= 4
+    return False
 
 
 def _gather_to_root(torch, pg, world, rank, t):
@@ -736,13 +761,9 @@ def bench_models(torch, dev, stream, flush, args, world, rank, pg):
         out[name] = {"batch_per_gpu": batch, "ms_per_batch": round(ms, 4), f"{unit}_per_s": round(rate, 1),
                      "GMAC/s": round(rate * macs_unit / 1e9, 1), f"mmac_per_{unit[:-1]}": round(macs_unit / 1e6, 2),
                      "nodes": len(g.nodes), "units_per_rank": f"[rank * {batch}, (rank + 1) * {batch})"}
-        if args.detail:  # per-kernel device time of one eager pass (events around each launch)
+        if args.detail:  # per-kernel device time of one eager pass (events around each launch, gated)
             from cormorant_b200 import ops
-            ops.profile_read()
-            ops.profile_enable(True)
-            with torch.cuda.stream(stream):
-                sim.forward_raw(raw, keep=keep, states=dev_states)
-            ops.profile_enable(False)
+            profiled_step(torch, ops, stream, flush, lambda: sim.forward_raw(raw, keep=keep, states=dev_states))
             prof = ops.profile_read()
             out[name]["kernels"] = {k: {"launches": v[0], "ms": round(v[1], 4)}
                                     for k, v in sorted(prof.items(), key=lambda kv: -kv[1][1])}
@@ -848,13 +869,9 @@ def bench_llama_decode(torch, dev, stream, flush, args, world, rank, pg, steps=1
         return bool(np.array_equal(got[:steps], z["ids"][:steps]) and
                     _crc16(got[steps:]) == int(z["crc_step_logits"][steps - 1]))
     out["parity"] = _verify_units(torch, pg, world, rank, mine, check)
-    if args.detail:  # per-kernel device time of one eager decode step
+    if args.detail:  # per-kernel device time of one eager decode step (events around each launch, gated)
         from cormorant_b200 import ops
-        ops.profile_read()
-        ops.profile_enable(True)
-        with torch.cuda.stream(stream):
-            r.decode_step(lg0, 0)
-        ops.profile_enable(False)
+        profiled_step(torch, ops, stream, flush, lambda: r.decode_step(lg0, 0))
         prof = ops.profile_read()
         out["kernels"] = {k: {"launches": v[0], "ms": round(v[1], 4)}
                           for k, v in sorted(prof.items(), key=lambda kv: -kv[1][1])}
@@ -988,20 +1005,23 @@ def run_case(args):
         y = torch.empty(R_ * n + 8, dtype=torch.int16, device="cuda")
         fn = lambda: ops.rowops(x, None, y, pw, op=op, n=n, rows=R_, blocks=1, c_s1=2 * n, win_lo=0,  # noqa
                                 win_hi=RH.NO_WINDOW, **regs)
-    elif args.case in ("dwconv", "pwconv"):
-        # MobileNetV2's second block at batch 64: the 3x3 stride-2 depthwise over
-        # 96 x 112 x 112, and the 1 x 1 expand 24 -> 144 over 56 x 56
+    elif args.case in ("dwconv", "dwconv14", "pwconv"):
+        # MobileNetV2 at batch 64: the 3x3 stride-2 depthwise over 96 x 112 x
+        # 112 (second block), the 3x3 depthwise over 576 x 14 x 14 (fifth
+        # block), and the 1 x 1 expand 24 -> 144 over 56 x 56
         if args.case == "dwconv":
             N_, C_, H_, M_, k, s_, oh = 64, 96, 112, 96, 3, 2, 56
+        elif args.case == "dwconv14":
+            N_, C_, H_, M_, k, s_, oh = 64, 576, 14, 576, 3, 1, 14
         else:
             N_, C_, H_, M_, k, s_, oh = 64, 24, 56, 144, 1, 1, 56
         x = ri(N_ * C_ * H_ * H_)
-        w = ri(M_ * (1 if args.case == "dwconv" else C_) * k * k, -64, 64)
+        w = ri(M_ * (1 if args.case != "pwconv" else C_) * k * k, -64, 64)
         b = ri(M_, -64, 64)
         y = torch.empty(N_ * M_ * oh * oh, dtype=torch.int16, device="cuda")
         fn = lambda: ops.conv(x, w, b, y, batch=N_, in_ch=C_, in_h=H_, in_w=H_, out_ch=M_, out_h=oh, out_w=oh,  # noqa
                               kh=k, kw=k, stride_h=s_, stride_w=s_, pad_top=k // 2, pad_left=k // 2, has_bias=1,
-                              is_depthwise=int(args.case == "dwconv"), flags=2 | 8)
+                              is_depthwise=int(args.case != "pwconv"), flags=2 | 8)
     elif args.case == "maxpool":  # MNIST's first pool at batch 8192
         x = ri(8192 * 16 * 28 * 28)
         y = torch.empty(8192 * 16 * 14 * 14 + 8, dtype=torch.int16, device="cuda")

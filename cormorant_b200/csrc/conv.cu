@@ -301,12 +301,15 @@ __global__ void __launch_bounds__(256) conv_dw_plane(ConvArgs a, uint32_t SH, ui
 // at stride 1, four at stride 2.  ROWS: the rows themselves are whole words
 // (W % 8 == 0), each staged word one 16-byte load; otherwise the G planes are
 // one contiguous range (G H W a multiple of 8) read in 16-byte words and
-// scattered.  A thread then takes a run of eight columns over NR output rows,
+// scattered.  A thread then takes a run of eight columns over NR_ output rows,
 // each input row read once from shared memory and its values multiplied into
 // every output row that uses it.  The sums run in 32 bits when they cannot
 // leave int32 — under the wrap rule always (the wrapping 32-bit sum is the
 // rule's value), otherwise when |bias| 2^8 + 2^15 sum|w| < 2^31 for the channel
-// — and in 64 bits per output otherwise.
+// — and in 64 bits per output otherwise.  Output rows of whole 16-byte words
+// (vst) are stored from registers; otherwise the unit's outputs are gathered
+// in shared memory and written as one range (16-byte words where the output
+// is dense) or element by element (an output pattern or a fused job).
 struct DwGeo {
   uint32_t G;      // planes per unit
   uint32_t SHb;    // staged rows per plane
@@ -315,66 +318,69 @@ struct DwGeo {
   uint32_t NRG;    // groups of NR output rows per plane
   uint32_t units;  // ceil(planes / G)
   uint32_t vst;    // dense 16-byte output rows (OW % 8 == 0, dense y, aligned, no fused job)
+  uint32_t flat;   // (no vst) dense output, no fused job, y 16-byte aligned and G P % 8 == 0: one range of words
+  uint32_t meta;   // bytes of per-plane data before the staged inputs (a multiple of 16)
 };
-constexpr uint32_t kDw3MaxG = 64;
-constexpr int kDw3NR = 4;
+constexpr uint32_t kDw3MaxG = 128;
 
-__device__ __forceinline__ void dw3_slow(const ConvArgs& a, const int16_t* win, uint32_t SP, int S, int PL,
-                                      const int16_t* wt, int64_t b0, uint32_t oh0, uint32_t ow0, int16_t* yp,
-                                      uint32_t m) {
-  for (int r = 0; r < kDw3NR; r++) {
-    const uint32_t oh = oh0 + r;
-    if (oh >= a.OH) break;
-    for (int t = 0; t < 8; t++) {
-      const uint32_t ow = ow0 + t;
-      if (ow >= a.OW) break;
-      int64_t acc = b0;
+// one output row's eight outputs (from ow0) on the 64-bit path, after the rule
+__device__ __forceinline__ void dw3_slow_row(const int16_t* win, uint32_t SP, int S, int PL, const int16_t* wt,
+                                             int64_t b0, uint32_t oh, uint32_t ow0, uint32_t OW, uint32_t flags,
+                                             int16_t* o8) {
+  for (int t = 0; t < 8; t++) {
+    const uint32_t ow = ow0 + t;
+    int64_t acc = b0;
+    if (ow < OW)
       for (int ky = 0; ky < 3; ky++)
         for (int kx = 0; kx < 3; kx++)
           acc += (int64_t)((int32_t)win[(oh * S + ky) * SP + ow * S + kx + 8 - PL] * (int32_t)wt[3 * ky + kx]);
-      conv_put(a, yp, (uint64_t)oh * a.OW + ow, m, acc);
-    }
+    o8[t] = conv_finish(acc, flags);
   }
 }
 
-template <int S_, int PL_, bool ROWS>
+template <int S_, int PL_, bool ROWS, int NR_>
 __global__ void __launch_bounds__(256) conv_dw3x3(ConvArgs a, DwGeo q) {
   corm_pdl_wait();
   corm_pdl_trigger();
-  extern __shared__ __align__(16) int16_t s_in[];  // [G][SHb][SPW * 8]
-  __shared__ int16_t* s_yp[kDw3MaxG];
-  __shared__ int32_t s_b[kDw3MaxG];
-  __shared__ int16_t s_w[kDw3MaxG][10];
-  __shared__ uint32_t s_m[kDw3MaxG];
-  __shared__ uint8_t s_fast[kDw3MaxG];
-  constexpr int NR = kDw3NR;
+  // dynamic shared memory: per plane its output pointer, bias << 8, channel,
+  // taps and path; then the staged inputs [G][SHb][SPW * 8]; then (no vst) the
+  // outputs [G][P]
+  extern __shared__ __align__(16) uint8_t s_dw[];
+  int16_t** s_yp = (int16_t**)s_dw;
+  int32_t* s_b = (int32_t*)(s_yp + q.G);
+  uint32_t* s_m = (uint32_t*)(s_b + q.G);
+  int16_t(*s_w)[10] = (int16_t(*)[10])(s_m + q.G);
+  uint8_t* s_fast = (uint8_t*)(s_w + q.G);
+  int16_t* s_in = (int16_t*)(s_dw + q.meta);
+  constexpr int NR = NR_;
   constexpr int QR = (NR - 1) * S_ + 3;  // input rows of a group of NR output rows
   constexpr int NWIN = S_ == 1 ? 3 : 4;  // window words per input row
   const uint32_t SP = q.SPW * 8u, PS = q.SHb * SP;
   const uint32_t HW = a.H * a.W, P = a.OH * a.OW;
+  int16_t* s_out = s_in + (size_t)q.G * PS;
   const uint64_t planes = (uint64_t)a.batch * a.M;
   const uint32_t RUNSin = (a.W + 7u) / 8u;
   const bool wrap = (a.flags & CORM_F_WRAP32) != 0;
   for (uint32_t unit = blockIdx.x; unit < q.units; unit += gridDim.x) {
     const uint64_t p0 = (uint64_t)unit * q.G;
     const uint32_t glive = (uint32_t)(planes - p0 < (uint64_t)q.G ? planes - p0 : (uint64_t)q.G);
-    if (threadIdx.x < glive) {
-      const uint64_t plane = p0 + threadIdx.x;
+    for (uint32_t pl = threadIdx.x; pl < glive; pl += blockDim.x) {
+      const uint64_t plane = p0 + pl;
       const uint32_t m = (uint32_t)(plane % a.M), n = (uint32_t)(plane / a.M);
-      s_yp[threadIdx.x] = a.y + (uint64_t)n * a.M * P + y_chan(a, m);
+      s_yp[pl] = a.y + (uint64_t)n * a.M * P + y_chan(a, m);
       const int32_t b = a.bias ? (int32_t)a.bias[m] : 0;
       uint32_t sw = 0;
 #pragma unroll
       for (int t = 0; t < 9; t++) {
         const int16_t w = __ldg(a.w + w_offset(a, m, 0, t / 3, t % 3));
-        s_w[threadIdx.x][t] = w;
+        s_w[pl][t] = w;
         sw += (uint32_t)(w < 0 ? -(int32_t)w : (int32_t)w);
       }
-      s_b[threadIdx.x] = b << 8;
-      s_m[threadIdx.x] = m;
+      s_b[pl] = b << 8;
+      s_m[pl] = m;
       // |acc| <= |b| 2^8 + 2^15 sum|w| (sum|w| <= 9 * 2^15 keeps this below 2^63)
       const int64_t bound = (int64_t)(b < 0 ? -b : b) * 256 + (int64_t)sw * 32768;
-      s_fast[threadIdx.x] = (wrap || bound <= 2147483647ll) ? 1 : 0;
+      s_fast[pl] = (wrap || bound <= 2147483647ll) ? 1 : 0;
     }
     if (ROWS) {
       // every staged word written once: data, or zeros outside the image / row
@@ -453,9 +459,23 @@ __global__ void __launch_bounds__(256) conv_dw3x3(ConvArgs a, DwGeo q) {
       const uint32_t rg = rem / q.RUNS, j = rem - rg * q.RUNS;
       const uint32_t oh0 = rg * NR;
       const int16_t* win = s_in + g * PS;
-      int16_t* yp = s_yp[g];
+      // eight outputs of output row oh (after the rule) to y (whole 16-byte words) or the staging
+      auto emit = [&](uint32_t oh, const int16_t* o8) {
+        if (q.vst) {
+          *(int4*)(s_yp[g] + (uint64_t)oh * a.OW + 8u * j) = *(const int4*)o8;
+        } else {
+          int16_t* so = s_out + g * P + oh * a.OW;
+#pragma unroll
+          for (int t = 0; t < 8; t++)
+            if (8u * j + t < a.OW) so[8u * j + t] = o8[t];
+        }
+      };
       if (!s_fast[g]) {
-        dw3_slow(a, win, SP, S_, PL_, s_w[g], s_b[g], oh0, 8u * j, yp, s_m[g]);
+        __align__(16) int16_t o8[8];
+        for (int r = 0; r < NR && oh0 + r < a.OH; r++) {
+          dw3_slow_row(win, SP, S_, PL_, s_w[g], s_b[g], oh0 + r, 8u * j, a.OW, a.flags, o8);
+          emit(oh0 + r, o8);
+        }
         continue;
       }
       int32_t w9[9];
@@ -495,18 +515,33 @@ __global__ void __launch_bounds__(256) conv_dw3x3(ConvArgs a, DwGeo q) {
       }
 #pragma unroll
       for (int r = 0; r < NR; r++) {
-        const uint32_t oh = oh0 + r;
-        if (oh >= a.OH) break;
-        if (q.vst) {
-          int4 o;
-          int16_t* os = (int16_t*)&o;
+        if (oh0 + r >= a.OH) break;
+        __align__(16) int16_t o8[8];
 #pragma unroll
-          for (int t = 0; t < 8; t++) os[t] = conv_finish((int64_t)(int32_t)acc[r][t], a.flags);
-          *(int4*)(yp + (uint64_t)oh * a.OW + 8u * j) = o;
-        } else {
-#pragma unroll
-          for (int t = 0; t < 8; t++)
-            if (8u * j + t < a.OW) conv_put(a, yp, (uint64_t)oh * a.OW + 8u * j + t, s_m[g], (int64_t)(int32_t)acc[r][t]);
+        for (int t = 0; t < 8; t++) o8[t] = conv_finish((int64_t)(int32_t)acc[r][t], a.flags);
+        emit(oh0 + r, o8);
+      }
+    }
+    if (!q.vst) {
+      __syncthreads();
+      if (q.flat) {  // the unit's outputs are one dense range of y from p0 P (a multiple of 8)
+        const uint32_t E = glive * P, nw = (E + 7u) / 8u;
+        int16_t* dst = a.y + p0 * P;
+        for (uint32_t i = threadIdx.x; i < nw; i += blockDim.x) {
+          if (8u * i + 8u <= E) {
+            ((int4*)dst)[i] = ((const int4*)s_out)[i];
+          } else {
+            for (uint32_t t = 8u * i; t < E; t++) dst[t] = s_out[t];
+          }
+        }
+      } else {  // an output pattern or a fused job: element by element, plane by plane
+        const uint32_t E = glive * P;
+        for (uint32_t i = threadIdx.x; i < E; i += blockDim.x) {
+          const uint32_t g = i / P, e = i - g * P;
+          int16_t v = s_out[i];
+          if (a.post.op != corm::kPostNone)
+            v = corm::post_apply(a.post, v, corm::post_b(a.post, (uint64_t)(s_yp[g] - a.y) + e, s_m[g]));
+          s_yp[g][e] = v;
         }
       }
     }
@@ -796,47 +831,67 @@ int conv_impl(const corm_conv_desc* d, const corm::PostOp& post, cudaStream_t st
                      d->stride_h == d->stride_w && (d->stride_h == 1 || d->stride_h == 2);
     // 3 x 3 as runs of eight outputs over staged planes (left pad 0 or 1, 16-byte aligned x)
     if (dw3 && d->pad_left <= 1u && !((uintptr_t)d->x & 15u)) {
-      const uint32_t S = d->stride_h, NR = (uint32_t)kDw3NR;
+      const uint32_t S = d->stride_h, NR = d->out_h <= 32u ? 2u : 4u;  // small planes: more runs per unit
       DwGeo q{};
       q.NRG = (d->out_h + NR - 1) / NR;
       q.RUNS = (d->out_w + 7u) / 8u;
       const uint32_t runs_in = (d->in_w + 7u) / 8u, HW = d->in_h * d->in_w;
       q.SHb = (q.NRG * NR - 1) * S + 3;
       q.SPW = std::max(runs_in + 2u, S == 1 ? q.RUNS + 2u : 2u * q.RUNS + 2u);
-      const size_t plane_b = (size_t)q.SHb * q.SPW * 16u;
       const bool rows = d->in_w % 8u == 0;
-      // whole planes read as one range: G H W a multiple of 8 keeps every unit's start on a 16-byte boundary
-      uint32_t unit = 1;
-      if (!rows) {
-        unit = 8;
-        while (unit > 1 && (uint64_t)(unit / 2) * HW % 8u == 0) unit /= 2;
-      }
-      uint32_t G = (uint32_t)std::min<size_t>(kDw3MaxG, std::max<size_t>(1, (32u * 1024u) / plane_b));
+      const bool dense = d->y_cn == 0 && (d->y_cs == 0 || d->y_cs == P) && !((uintptr_t)d->y & 15u) &&
+                         a.post.op == corm::kPostNone;
+      q.vst = dense && d->out_w % 8u == 0;
+      // planes per unit in multiples of `unit`: whole planes read as one range
+      // (G H W a multiple of 8) and outputs written as one range (G P a multiple of 8)
+      auto align8 = [](uint64_t n) {
+        uint32_t u = 8;
+        while (u > 1 && (uint64_t)(u / 2) * n % 8u == 0) u /= 2;
+        return u;
+      };
+      const uint32_t unit = std::max(rows ? 1u : align8(HW), (!q.vst && dense) ? align8(P) : 1u);
+      // small planes: CTAs of two warps with units of about 10 KB (many CTAs per
+      // SM, so one CTA's barriers never idle the SM); large planes: 8 warps, 36 KB
+      const bool small = (size_t)q.SHb * q.SPW * 16u <= 4096u;
+      const unsigned threads = small ? 64u : 256u;
+      const size_t target = small ? 10u * 1024u : 36u * 1024u;
+      const size_t plane_b = (size_t)q.SHb * q.SPW * 16u + (q.vst ? 0u : (size_t)P * 2u) + 40u;
+      uint32_t G = (uint32_t)std::min<size_t>(kDw3MaxG, std::max<size_t>(1, target / plane_b));
       G = std::max(unit, G / unit * unit);
-      const size_t smem = (size_t)G * plane_b;
+      q.meta = (G * 40u + 15u) / 16u * 16u;
+      const size_t smem = q.meta + (size_t)G * q.SHb * q.SPW * 16u +
+                          (q.vst ? 0u : ((size_t)G * P * 2u + 15u) / 16u * 16u);
       if (G <= kDw3MaxG && smem <= 100u * 1024u) {
         const uint64_t planes = (uint64_t)d->batch * d->out_ch;
         q.G = G;
         q.units = (uint32_t)((planes + G - 1) / G);
-        q.vst = d->out_w % 8u == 0 && d->y_cn == 0 && (d->y_cs == 0 || d->y_cs == P) && !((uintptr_t)d->y & 15u) &&
-                a.post.op == corm::kPostNone;
-        const unsigned per_sm = (unsigned)std::max<size_t>(1, std::min<size_t>(8, (200u * 1024u) / (smem + 4096u)));
+        q.flat = !q.vst && dense && (uint64_t)G * P % 8u == 0;
+        const size_t per_sm_smem = (220u * 1024u) / (smem + 1024u);
+        const unsigned per_sm = (unsigned)std::max<size_t>(1, std::min<size_t>({per_sm_smem, 2048u / threads, 32u}));
         const unsigned grid = (unsigned)std::min<uint64_t>(q.units, 148ull * per_sm);
         corm::ProfScope prof_("conv_dw3x3", st);
         auto launch = [&](auto kern) {
           cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-          corm_launch_pdl(kern, dim3(grid), dim3(256), smem, st, a, q);
+          corm_launch_pdl(kern, dim3(grid), dim3(threads), smem, st, a, q);
         };
-        const int pick = (S == 2 ? 4 : 0) + (d->pad_left ? 2 : 0) + (rows ? 1 : 0);
+        const int pick = (NR == 2 ? 8 : 0) + (S == 2 ? 4 : 0) + (d->pad_left ? 2 : 0) + (rows ? 1 : 0);
         switch (pick) {
-          case 0: launch(conv_dw3x3<1, 0, false>); break;
-          case 1: launch(conv_dw3x3<1, 0, true>); break;
-          case 2: launch(conv_dw3x3<1, 1, false>); break;
-          case 3: launch(conv_dw3x3<1, 1, true>); break;
-          case 4: launch(conv_dw3x3<2, 0, false>); break;
-          case 5: launch(conv_dw3x3<2, 0, true>); break;
-          case 6: launch(conv_dw3x3<2, 1, false>); break;
-          default: launch(conv_dw3x3<2, 1, true>); break;
+          case 0: launch(conv_dw3x3<1, 0, false, 4>); break;
+          case 1: launch(conv_dw3x3<1, 0, true, 4>); break;
+          case 2: launch(conv_dw3x3<1, 1, false, 4>); break;
+          case 3: launch(conv_dw3x3<1, 1, true, 4>); break;
+          case 4: launch(conv_dw3x3<2, 0, false, 4>); break;
+          case 5: launch(conv_dw3x3<2, 0, true, 4>); break;
+          case 6: launch(conv_dw3x3<2, 1, false, 4>); break;
+          case 7: launch(conv_dw3x3<2, 1, true, 4>); break;
+          case 8: launch(conv_dw3x3<1, 0, false, 2>); break;
+          case 9: launch(conv_dw3x3<1, 0, true, 2>); break;
+          case 10: launch(conv_dw3x3<1, 1, false, 2>); break;
+          case 11: launch(conv_dw3x3<1, 1, true, 2>); break;
+          case 12: launch(conv_dw3x3<2, 0, false, 2>); break;
+          case 13: launch(conv_dw3x3<2, 0, true, 2>); break;
+          case 14: launch(conv_dw3x3<2, 1, false, 2>); break;
+          default: launch(conv_dw3x3<2, 1, true, 2>); break;
         }
         return corm::cuda_status("conv depthwise");
       }

@@ -736,12 +736,13 @@ __global__ void __launch_bounds__(Roles<CONV>::threads, 1)
     for (uint32_t u = blockIdx.x; u < units; u += gridDim.x, i++) {
       const Unit w = unit_of(ep, u);
       if (u + gridDim.x >= units) corm_pdl_trigger();  // this CTA's last unit
-      if (!sm100::mbar_wait(tmem_full, i & 1, ep.err, 103, wlim, wstop)) break;
-      sm100::tc_fence_after();
       const uint32_t r = w.tile_r + q * 32 + lane;
       const bool row_ok = r < ep.rows;
-      // a per-row bias (a 1 x 1 conv as W x; int16 operands only)
+      // a per-row bias (a 1 x 1 conv as W x; int16 operands only), loaded
+      // while the unit's MMAs run
       const int32_t rowb = (CONV && ep.bias_rows && row_ok) ? ep.bias[r] : 0;
+      if (!sm100::mbar_wait(tmem_full, i & 1, ep.err, 103, wlim, wstop)) break;
+      sm100::tc_fence_after();
       if (ep.partial) {
         for (int cc = R::wc * h; cc < R::wc * h + R::wc; cc += CW) {
           uint32_t hh[CW], mid[CW], ll[CW];
