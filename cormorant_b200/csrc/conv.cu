@@ -292,6 +292,111 @@ __global__ void __launch_bounds__(256) conv_dw_plane(ConvArgs a, uint32_t SH, ui
   }
 }
 
+// Convolutions of group 1 with short sums — K = C kh kw <= 32 (the stem's
+// 3 x 3 over 3 channels, 1 x 1 convs over a few channels), few channels out:
+// CUDA cores, a thread per output pixel.  The pixel's K inputs are read once
+// into registers (zero outside the image; each k's offset, row and column
+// step from shared memory); the weights sit in shared memory as int32
+// [k][Mp] (the channels of one k contiguous), so a chunk's 16 weights of one
+// k are four 16-byte reads every lane of the warp shares.  A chunk of 16
+// channels sums in 32 bits when every channel of it satisfies
+// |bias| 2^8 + 2^15 sum|w| < 2^31 (always under the wrap rule: the wrapping
+// 32-bit sum is the rule's value), else in 64 bits.
+constexpr uint32_t kSkMaxK = 32, kSkMC = 16;
+__global__ void __launch_bounds__(256) conv_small_k(ConvArgs a, uint32_t K, uint32_t Mp) {
+  corm_pdl_wait();
+  corm_pdl_trigger();
+  extern __shared__ __align__(16) int32_t s_sk[];  // w [K][Mp], bias << 8 [Mp], fast [Mp / 16]
+  int32_t* s_w = s_sk;
+  int32_t* s_b = s_w + K * Mp;
+  int32_t* s_fast = s_b + Mp;
+  __shared__ int32_t s_off[kSkMaxK];  // x offset of k within the image, relative to the window's corner
+  __shared__ int32_t s_dy[kSkMaxK], s_dx[kSkMaxK];
+  const uint32_t KK = a.KH * a.KW, HW = a.H * a.W;
+  for (uint32_t i = threadIdx.x; i < K * Mp; i += blockDim.x) {
+    const uint32_t k = i / Mp, m = i - k * Mp;
+    const uint32_t c = k / KK, t = k - c * KK;
+    s_w[i] = m < a.M ? (int32_t)__ldg(a.w + w_offset(a, m, c, t / a.KW, t % a.KW)) : 0;
+  }
+  for (uint32_t k = threadIdx.x; k < K; k += blockDim.x) {
+    const uint32_t c = k / KK, t = k - c * KK, i = t / a.KW, j = t - i * a.KW;
+    s_dy[k] = (int32_t)(i * a.dh);
+    s_dx[k] = (int32_t)(j * a.dw);
+    s_off[k] = (int32_t)(c * HW + i * a.dh * a.W + j * a.dw);
+  }
+  const bool wrap = (a.flags & CORM_F_WRAP32) != 0;
+  for (uint32_t m = threadIdx.x; m < Mp; m += blockDim.x) s_b[m] = (m < a.M && a.bias) ? (int32_t)a.bias[m] << 8 : 0;
+  __syncthreads();
+  for (uint32_t ch = threadIdx.x; ch < Mp / kSkMC; ch += blockDim.x) {
+    bool ok = true;
+    for (uint32_t t = 0; t < kSkMC; t++) {
+      const uint32_t m = ch * kSkMC + t;
+      int64_t sw = 0;
+      for (uint32_t k = 0; k < K; k++) sw += s_w[k * Mp + m] < 0 ? -(int64_t)s_w[k * Mp + m] : s_w[k * Mp + m];
+      const int64_t b = s_b[m] < 0 ? -(int64_t)s_b[m] : s_b[m];
+      ok = ok && b + sw * 32768 <= 2147483647ll;
+    }
+    s_fast[ch] = (wrap || ok) ? 1 : 0;
+  }
+  __syncthreads();
+  const uint32_t P = a.OH * a.OW;
+  const uint64_t total = (uint64_t)a.batch * P;
+  for (uint64_t pix = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; pix < total;
+       pix += (uint64_t)gridDim.x * blockDim.x) {
+    const uint32_t n = (uint32_t)(pix / P), p = (uint32_t)(pix - (uint64_t)n * P);
+    const uint32_t oh = p / a.OW, ow = p - oh * a.OW;
+    const int ih0 = (int)(oh * a.sh) - (int)a.pt, iw0 = (int)(ow * a.sw) - (int)a.pl;
+    const int16_t* xb = a.x + (uint64_t)n * a.C * HW;
+    const int64_t corner = (int64_t)ih0 * a.W + iw0;
+    int32_t xv[kSkMaxK];
+#pragma unroll
+    for (uint32_t k = 0; k < kSkMaxK; k++) {
+      xv[k] = 0;
+      if (k < K) {
+        const int ih = ih0 + s_dy[k], iw = iw0 + s_dx[k];
+        if (ih >= 0 && ih < (int)a.H && iw >= 0 && iw < (int)a.W) xv[k] = __ldg(xb + (corner + s_off[k]));
+      }
+    }
+    int16_t* yb = a.y + (uint64_t)n * a.M * P;
+    for (uint32_t ch = 0; ch < Mp / kSkMC; ch++) {
+      const int32_t* wc = s_w + ch * kSkMC;
+      if (s_fast[ch]) {
+        uint32_t acc[kSkMC];
+#pragma unroll
+        for (uint32_t t = 0; t < kSkMC; t++) acc[t] = (uint32_t)s_b[ch * kSkMC + t];
+#pragma unroll
+        for (uint32_t k = 0; k < kSkMaxK; k++) {
+          if (k >= K) break;
+          const int4* wr = (const int4*)(wc + k * Mp);
+#pragma unroll
+          for (uint32_t u = 0; u < kSkMC / 4; u++) {
+            const int4 w4 = wr[u];
+            acc[4 * u] += (uint32_t)(xv[k] * w4.x);
+            acc[4 * u + 1] += (uint32_t)(xv[k] * w4.y);
+            acc[4 * u + 2] += (uint32_t)(xv[k] * w4.z);
+            acc[4 * u + 3] += (uint32_t)(xv[k] * w4.w);
+          }
+        }
+#pragma unroll
+        for (uint32_t t = 0; t < kSkMC; t++) {
+          const uint32_t m = ch * kSkMC + t;
+          if (m < a.M) conv_put(a, yb + y_chan(a, m), p, m, (int64_t)(int32_t)acc[t]);
+        }
+      } else {
+        for (uint32_t t = 0; t < kSkMC; t++) {
+          const uint32_t m = ch * kSkMC + t;
+          if (m >= a.M) break;
+          int64_t acc = s_b[m];
+#pragma unroll
+          for (uint32_t k = 0; k < kSkMaxK; k++)
+            if (k < K) acc += (int64_t)xv[k] * wc[k * Mp + t];
+          conv_put(a, yb + y_chan(a, m), p, m, acc);
+        }
+      }
+    }
+  }
+}
+
 // Depthwise 3 x 3 (dilation 1, stride S_ of 1 or 2, left pad PL_ of 0 or 1)
 // as runs of eight outputs.  A CTA takes units of G consecutive (n, m) planes
 // and stages each plane's input in shared memory as rows of SPW 16-byte words,
@@ -954,6 +1059,16 @@ int conv_impl(const corm_conv_desc* d, const corm::PostOp& post, cudaStream_t st
       corm_launch_pdl(conv_depthwise, dim3(corm_blocks(total, 256, 148u * 16u)), dim3(256), 0, st, a);
     }
     return corm::cuda_status("conv depthwise");
+  }
+  // short sums, few output channels: CUDA cores (no im2col, no split, no GEMM)
+  if (!d->is_depthwise && (uint64_t)d->in_ch * d->kh * d->kw <= kSkMaxK &&
+      (uint64_t)d->out_ch * d->in_ch * d->kh * d->kw <= 4096u) {
+    const uint32_t K = d->in_ch * d->kh * d->kw, Mp = (d->out_ch + kSkMC - 1) / kSkMC * kSkMC;
+    const size_t smem = ((size_t)K * Mp + Mp + Mp / kSkMC) * sizeof(int32_t);
+    const uint64_t total = (uint64_t)d->batch * P;
+    corm::ProfScope prof_("conv_small_k", st);
+    corm_launch_pdl(conv_small_k, dim3(corm_blocks(total, 256, 148u * 8u)), dim3(256), smem, st, a, K, Mp);
+    return corm::cuda_status("conv small k");
   }
   if (pointwise_gemm(d, post)) {
     // a 1 x 1 conv at stride 1 is, per image, y[n] (M x P) = W (M x C) x[n] (C x P):

@@ -166,6 +166,29 @@ def test_depthwise_full_range(ops, shape, wrap):
     assert np.array_equal(y.cpu().numpy().reshape(N, C, oh, ow), exp)
 
 
+@pytest.mark.parametrize("wrap", [0, 1])
+@pytest.mark.parametrize("shape", [(2, 3, 11, 13, 40, 3, 2), (1, 20, 6, 6, 24, 1, 1)], ids=["stem_3x3_s2", "pointwise"])
+def test_small_k_full_range(ops, shape, wrap):
+    """Short sums (K = C kh kw <= 32, few channels out: the CUDA-core kernel)
+    on full-range operands: chunks of 16 channels whose sums can leave int32
+    (the 64-bit path) beside chunks whose cannot (the 32-bit path); without
+    the wrap rule the exact sums saturate, with it the 32-bit sums wrap."""
+    N, C, H, W, M, k, s_ = shape
+    rng = np.random.default_rng(41 + C + wrap)
+    x = rnd16(rng, (N, C, H, W), -32768, 32768)
+    w = rnd16(rng, (M, C, k, k), -32768, 32768)
+    w[:16] //= 4096  # the first chunk: small taps (the bound holds); the rest full range
+    b = rnd16(rng, (M,), -32768, 32768)
+    p_ = k // 2
+    oh, ow = (H + 2 * p_ - k) // s_ + 1, (W + 2 * p_ - k) // s_ + 1
+    y = torch.full((N * M * oh * ow,), -8531, dtype=torch.int16, device="cuda")
+    ops.conv(dev(x.reshape(-1)), dev(w.reshape(-1)), dev(b), y, batch=N, in_ch=C, in_h=H, in_w=W, out_ch=M,
+             out_h=oh, out_w=ow, kh=k, kw=k, stride_h=s_, stride_w=s_, pad_top=p_, pad_left=p_, has_bias=1,
+             flags=2 | wrap)
+    exp = spec.conv_raw(x, w, b, s_, s_, p_, p_, 1, 1, oh, ow, False, wrap=bool(wrap))
+    assert np.array_equal(y.cpu().numpy().reshape(N, M, oh, ow), exp)
+
+
 def test_conv_wrap(ops):
     """Large operands: the exact sum leaves int32; CORM_F_WRAP32 wraps it."""
     rng = np.random.default_rng(9)
