@@ -1060,9 +1060,11 @@ int conv_impl(const corm_conv_desc* d, const corm::PostOp& post, cudaStream_t st
     }
     return corm::cuda_status("conv depthwise");
   }
-  // short sums, few output channels: CUDA cores (no im2col, no split, no GEMM)
-  if (!d->is_depthwise && (uint64_t)d->in_ch * d->kh * d->kw <= kSkMaxK &&
-      (uint64_t)d->out_ch * d->in_ch * d->kh * d->kw <= 4096u) {
+  // short sums, few output channels: CUDA cores (no im2col, no split, no GEMM).
+  // Measured against the GEMM forms on MobileNetV2 at batch 256: the stem
+  // (3 x 3 over 3 channels, 32 out) 0.49 against 0.89 ms, 1 x 1 32 -> 16
+  // 0.33 against 0.40 ms; with 96 or 144 channels out the GEMM is faster.
+  if (!d->is_depthwise && (uint64_t)d->in_ch * d->kh * d->kw <= kSkMaxK && d->out_ch <= 32u) {
     const uint32_t K = d->in_ch * d->kh * d->kw, Mp = (d->out_ch + kSkMC - 1) / kSkMC * kSkMC;
     const size_t smem = ((size_t)K * Mp + Mp + Mp / kSkMC) * sizeof(int32_t);
     const uint64_t total = (uint64_t)d->batch * P;

@@ -71,6 +71,7 @@ CONVS = [  # N, C, H, W, M, k, s, p, depthwise
     (2, 6, 40, 37, 6, 3, 1, 1, True),
     (1, 5, 30, 30, 5, 5, 1, 2, True),
     (2, 8, 16, 16, 8, 3, 2, 1, True),
+    (2, 3, 12, 12, 24, 3, 1, 1, False),
     (3, 7, 7, 7, 7, 3, 1, 1, True),
 ]
 
