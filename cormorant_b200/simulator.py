@@ -102,6 +102,7 @@ class GpuSimulator:
         self._ws: Optional[torch.Tensor] = None
         self._plan = self._fusion_plan() if fuse else {}
         self._groups = self._sibling_groups() if fuse else {}
+        self._pairs = self._rowops_pairs() if fuse else {}
 
     # ------------------------------------------------------------ tensors
     def _alloc(self, numel: int) -> torch.Tensor:
@@ -372,6 +373,7 @@ class GpuSimulator:
         attn_fused = self._decode_attn_plan(keep) if (self.fuse and keep is not None) else {}
         for _mi, info in attn_fused.items():
             skip |= set(info["nodes"])
+        skip |= set(self._pairs.values())
 
         def get(t):
             if t.onnx_name not in raw:
@@ -423,6 +425,11 @@ class GpuSimulator:
                 y = self._layernorm(sn, get(sn.inputs[0]), get(sn.inputs[1]))
             elif kind == "TransposeRoNode":
                 y = self._transpose(sn, get(sn.inputs[0]), get(sn.inputs[1]))
+            elif kind == "ResAddRoNode" and i in self._pairs:
+                nn = self._graph.nodes[self._pairs[i]]
+                y, y2 = self._resadd_norm(sn, nn, get)
+                raw[nn.output.onnx_name] = y2
+                meta[nn.output.onnx_name] = nn.output
             elif kind in ("ResAddRoNode", "RMSNormRoNode", "WidenRoNode", "SiluMulRoNode"):
                 y = self._llm_rowops(sn, kind, get)
             elif kind == "VitGeluVopNode":
@@ -681,6 +688,36 @@ class GpuSimulator:
                        op=RH.opword(RH.OP_MULACT, I16, I16, I16, b_en=True, p_bcast=bc), n=n, rows=rows,
                        a_s1=2 * n, b_s1=2 * n, c_s1=2 * n, win_hi=RH.NO_WINDOW)
         return y
+
+    def _rowops_pairs(self) -> Dict[int, int]:
+        """ResAdd nodes followed at once by the RMSNorm of their sum (a Llama
+        layer's two residual adds): {ResAdd index: RMSNorm index}.  The pair
+        runs as a two-job descriptor chain, which the library executes in one
+        pass over the rows (both outputs written)."""
+        nodes, pairs = self._graph.nodes, {}
+        for i in range(len(nodes) - 1):
+            a, b = nodes[i], nodes[i + 1]
+            if (_kind(a) == "ResAddRoNode" and _kind(b) == "RMSNormRoNode" and
+                    b.inputs[0].onnx_name == a.output.onnx_name and a.n == b.n and a.rows == b.rows):
+                pairs[i] = i + 1
+        return pairs
+
+    def _resadd_norm(self, sa, sb, get):
+        """The ResAdd job and the RMSNorm job of its sum as one chain (the
+        registers of ``_llm_rowops``); returns (the sum, the normed rows)."""
+        from . import rowops_host as RH
+        n, rows = sa.n, sa.rows
+        I16, I32 = RH.K_I16, RH.K_I32
+        h = self._alloc32(sa.output.numel)
+        y = self._alloc(sb.output.numel)
+        ops.rowops_chain([
+            dict(a=get(sa.inputs[0]), b=get(sa.inputs[1]), c=h, p=get(sa.inputs[2]), n=n, rows=rows,
+                 op=RH.opword(RH.OP_ADDX, I32, I16, I32, b_en=True, p_bcast=bool(getattr(sa, "bcast", False))),
+                 a_s1=4 * n, b_s1=2 * n, c_s1=4 * n, win_hi=RH.NO_WINDOW),
+            dict(a=h, c=y, p=get(sb.inputs[1]), n=n, rows=rows,
+                 op=RH.opword(RH.OP_NORM, I32, I16, I16, p_bcast=bool(getattr(sb, "bcast", False))),
+                 a_s1=4 * n, c_s1=2 * n, eps=int(sb.E), win_hi=RH.NO_WINDOW)])
+        return h, y
 
     def _vit_gelu(self, sn, get):
         """VitGelu (vit_nodes.py:649-655): ADD f + ba, then MUL by sc with the

@@ -442,7 +442,10 @@ int corm_rowops(const corm_rowops_desc* d, corm_stream_t stream);
 /* A descriptor chain (host_emu.py:731-749, rowops_ref.h:428-441): the jobs in
  * order, at most 16, each seeing the writes of the ones before.  Every job
  * (chained or not) keeps the unit's parameter RAM: a job that streams
- * parameters loads it from p unless P_KEEP, and a P_KEEP job reads it. */
+ * parameters loads it from p unless P_KEEP, and a P_KEEP job reads it.  An
+ * ADDX of int32 rows and int16 rows into int32 rows followed by the RMS NORM of
+ * its output (a residual add and the next layer's RMSNorm) runs as one pass
+ * over the rows, with the same outputs and the same parameter RAM after it. */
 int corm_rowops_chain(const corm_rowops_desc* jobs, uint32_t count, corm_stream_t stream);
 /* The same with the board's descriptor list in device memory: count 128-byte
  * descriptors at desc, words 0..23 the registers 0x10..0x6C in order (op, n,

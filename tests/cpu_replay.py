@@ -210,6 +210,12 @@ def install(setattr_fn):
     setattr_fn(ops, "gemm_strided", gemm_strided)
     setattr_fn(ops, "copy_nd", copy_nd)
     setattr_fn(ops, "rowops", rowops)
+
+    def rowops_chain(jobs):  # the jobs in order (the library may fuse adjacent ones; the result is the same)
+        for j in jobs:
+            rowops(j.get("a"), j.get("b"), j.get("c"), j.get("p"),
+                   **{k: v for k, v in j.items() if k not in ("a", "b", "c", "p")})
+    setattr_fn(ops, "rowops_chain", rowops_chain)
     setattr_fn(ops, "matmul", matmul)
     setattr_fn(ops, "matmul_groups", matmul_groups)
     setattr_fn(ops, "split_b_planes", split_b_planes)

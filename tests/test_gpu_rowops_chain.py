@@ -92,3 +92,48 @@ def test_param_ram_chains(ops, seed):
     for j in chain1 + chain2 + [lone]:
         spec.rowops_job(m, *j, ps=ps)
     assert np.array_equal(got, m.buf)
+
+
+@pytest.mark.parametrize("case", [(960, 64, False, False, 0), (960, 48, True, True, 5), (256, 33, False, True, 40),
+                                  (2048, 9, True, False, 2)], ids=["llama", "bcast_relu", "n256_bq40", "n2048"])
+def test_addx_norm_pairs(ops, case):
+    """An ADDX of int32 rows and int16 rows into int32 rows followed by the RMS
+    NORM of its output — the pair the library runs as one pass — against the job
+    model run job by job: both outputs, then a P_KEEP COPY that reads the
+    parameter RAM the pair left (the NORM's entries).  Full-range residuals
+    (the ADDX saturating), random entries per column or broadcast."""
+    n, rows, xbc, relu, bq_sh = case
+    rng = np.random.default_rng(n + rows + bq_sh)
+    s1a, s1b, s1y = 4 * n + 32, 2 * n + 16, 2 * n
+    a = rng.integers(-(1 << 31), 1 << 31, rows * s1a // 4).astype("<i4").view(np.uint8)
+    a[: s1a * (rows // 3)] = rng.integers(-(1 << 18), 1 << 18, s1a * (rows // 3) // 4).astype("<i4").view(np.uint8)
+    b = rng.integers(0, 256, rows * s1b).astype(np.uint8)
+    px = _entries(rng, 1 if xbc else n, bq=(-(1 << 21), 1 << 21), sa=(0, 3), sb=(0, 17), sc=(0, 4))
+    pn = _entries(rng, n, g=(1, 1 << 24), bq=(-(1 << 21), 1 << 21), sc=(24, 48))
+    parts = [("a", a), ("b", b), ("px", px), ("pn", pn), ("h", np.zeros(rows * s1a, np.uint8)),
+             ("y", np.zeros(rows * s1y, np.uint8)), ("z", np.zeros(rows * s1y, np.uint8))]
+    offs, cur = {}, 0
+    for nm, arr in parts:
+        offs[nm] = cur
+        cur += (len(arr) + 255) // 256 * 256 + 256
+    mem = np.zeros(cur, np.uint8)
+    for nm, arr in parts:
+        mem[offs[nm]:offs[nm] + len(arr)] = arr
+    I16, I32 = spec.K_I16, spec.K_I32
+    W = 0xFFFFFFFF
+    opx = 2 | (I32 << 4) | (I16 << 6) | (I32 << 8) | spec.F_B_EN | (spec.F_P_BCAST if xbc else 0) | (spec.F_RELU if relu else 0)
+    opn = 5 | (I32 << 4) | (I16 << 8)
+    jx = [opx, n, rows, 1, offs["a"], s1a, 0, offs["b"], s1b, 0, offs["h"], s1a, 0, offs["px"], 0, 0, bq_sh, 0, W]
+    jn = [opn, n, rows, 1, offs["h"], s1a, 0, 0, 0, 0, offs["y"], s1y, 0, offs["pn"], 987654, 0, 7, 0, W]
+    keep = [1 | (I16 << 4) | (I16 << 8) | spec.F_P_KEEP, n, rows, 1, offs["y"], s1y, 0, 0, 0, 0, offs["z"], s1y, 0,
+            offs["a"], 0, 0, 0, 0, W]
+    import torch
+    buf = torch.from_numpy(mem.copy()).cuda()
+    ops.rowops_chain([dict(dict(zip(KEYS, j)), a=buf, b=buf, c=buf, p=buf) for j in (jx, jn)])
+    ops.rowops_chain([dict(dict(zip(KEYS, keep)), a=buf, b=buf, c=buf, p=buf)])
+    got = buf.cpu().numpy()
+    m, ps = spec.RowOpsMem(mem.copy()), spec.ParamRAM()
+    for j in (jx, jn, keep):
+        spec.rowops_job(m, *j, ps=ps)
+    for nm, size in (("h", rows * s1a), ("y", rows * s1y), ("z", rows * s1y)):
+        assert np.array_equal(got[offs[nm]:offs[nm] + size], m.buf[offs[nm]:offs[nm] + size]), nm
