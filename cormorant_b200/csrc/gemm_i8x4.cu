@@ -82,6 +82,9 @@ struct EpiArgs {
   uint32_t raw_tma;  // int16 operands: raw tiles by TMA (map_ahi: A, map_bhi: B) into the stage
   uint32_t b_tma_planes;  // with raw_tma: B from its split planes (map_bhi / map_blo), only A split here
   uint32_t a_box_rows, b_pitch;  // raw boxes: A rows (<= 128) and the B row's bytes (<= 256)
+  // A in TMEM and at most 64 rows: MMAs of M = 64, whose A and accumulator
+  // rows 16 q .. 16 q + 15 sit in TMEM lanes 32 q .. 32 q + 15 (lane quarter q)
+  uint32_t m64;
 };
 
 // y = floor(acc / 2^8) for acc = 2^16 HH + 2^8 MID + LL + 2^8 bias, i.e.
@@ -533,7 +536,11 @@ __global__ void __launch_bounds__(Roles<CONV>::threads, 1)
     // and row & 7 for every i, so every address is a base plus a constant)
     const uint32_t pt = (uint32_t)(warp - 1) * 32u + lane, row0 = pt >> 4, c = pt & 15u;
     const uint32_t off0 = row0 * 128u + (((c >> 1) ^ (row0 & 7u)) << 4) + ((c & 1u) << 3);
-    const uint32_t aq = (uint32_t)(warp & 3), ahk = (uint32_t)(warp - 1) >> 2, arow = aq * 32u + lane;
+    // the A row this lane puts in its TMEM lane (M = 64: lanes 16..31 of a quarter hold none)
+    const uint32_t aq = (uint32_t)(warp & 3), ahk = (uint32_t)(warp - 1) >> 2;
+    const uint32_t arow = ep.m64 ? aq * 16u + (lane & 15u) : aq * 32u + lane;
+    const bool a_lane = !ep.m64 || lane < 16u;
+    const uint32_t q_row0 = ep.m64 ? aq * 16u : aq * 32u;
     uint32_t g = 0;
     bool stop = false;
     for (uint32_t u = blockIdx.x; u < units && !stop; u += gridDim.x) {
@@ -547,13 +554,13 @@ __global__ void __launch_bounds__(Roles<CONV>::threads, 1)
         sm100::tc_fence_after();  // the TMEM buffer's readers are done (a_free)
         uint8_t* st = smem + s * STAGE_BYTES;
         // (after a run-out wait the words are not used: every thread stops below)
-        if (aq * 32u < nrow) {  // warp-uniform: the quarter holds rows of the job
+        if (q_row0 < nrow) {  // warp-uniform: the quarter holds rows of the job
           const uint8_t* ra = st + ahk * (ep.a_box_rows * 128u) + arow * 128u;
           uint32_t hi[16], lo[16];
 #pragma unroll
           for (int k = 0; k < 8; k++) {
             int4 v = make_int4(0, 0, 0, 0);
-            if (arow < nrow) v = *(const int4*)(ra + (((uint32_t)k ^ (arow & 7u)) << 4));
+            if (a_lane && arow < nrow) v = *(const int4*)(ra + (((uint32_t)k ^ (arow & 7u)) << 4));
             hi[2 * k] = __byte_perm((uint32_t)v.x, (uint32_t)v.y, 0x7531);
             hi[2 * k + 1] = __byte_perm((uint32_t)v.z, (uint32_t)v.w, 0x7531);
             lo[2 * k] = __byte_perm((uint32_t)v.x, (uint32_t)v.y, 0x6420);
@@ -666,10 +673,11 @@ __global__ void __launch_bounds__(Roles<CONV>::threads, 1)
   } else if (warp == R::mma_warp && lane == 0) {
     // ---------------- MMA issuer
     const uint32_t bmaj = ep.b_mn ? (1u << 16) : 0u;
-    const uint32_t ID_SS = sm100::idesc_i8(BM, BN, 1, 1) | bmaj;
-    const uint32_t ID_SU = sm100::idesc_i8(BM, BN, 1, 0) | bmaj;
-    const uint32_t ID_US = sm100::idesc_i8(BM, BN, 0, 1) | bmaj;
-    const uint32_t ID_UU = sm100::idesc_i8(BM, BN, 0, 0) | bmaj;
+    const uint32_t mm = ep.m64 ? 64u : (uint32_t)BM;
+    const uint32_t ID_SS = sm100::idesc_i8(mm, BN, 1, 1) | bmaj;
+    const uint32_t ID_SU = sm100::idesc_i8(mm, BN, 1, 0) | bmaj;
+    const uint32_t ID_US = sm100::idesc_i8(mm, BN, 0, 1) | bmaj;
+    const uint32_t ID_UU = sm100::idesc_i8(mm, BN, 0, 0) | bmaj;
     const uint32_t acc_hh = tmem, acc_mid = tmem + BN, acc_ll = tmem + 2 * BN;
     const bool a_tm = CONV && ep.raw_tma;  // A from the TMEM buffers the splitting warps fill
     uint32_t g = 0, i = 0;
@@ -736,8 +744,8 @@ __global__ void __launch_bounds__(Roles<CONV>::threads, 1)
     for (uint32_t u = blockIdx.x; u < units; u += gridDim.x, i++) {
       const Unit w = unit_of(ep, u);
       if (u + gridDim.x >= units) corm_pdl_trigger();  // this CTA's last unit
-      const uint32_t r = w.tile_r + q * 32 + lane;
-      const bool row_ok = r < ep.rows;
+      const uint32_t r = w.tile_r + (ep.m64 ? q * 16 + (lane & 15) : q * 32 + lane);
+      const bool row_ok = (!ep.m64 || lane < 16) && r < ep.rows;
       // a per-row bias (a 1 x 1 conv as W x; int16 operands only), loaded
       // while the unit's MMAs run
       const int32_t rowb = (CONV && ep.bias_rows && row_ok) ? ep.bias[r] : 0;
@@ -1138,6 +1146,7 @@ int gemm_i8x4(const GemmJob& j, cudaStream_t stream) {
   ep.b_tma_planes = b_planes_in ? 1u : 0u;
   ep.a_box_rows = a_box_rows;
   ep.b_pitch = b_box_cols * 2u;
+  ep.m64 = (raw_tma && j.rows <= 64u) ? 1u : 0u;
   if (sp.splits > 1) {
     if (!j.partial) return fail(CORM_ENOMEM, "gemm: K-split job without a partial-sum buffer");
     ep.partial = (unsigned long long*)j.partial;
