@@ -49,7 +49,8 @@ class MatmulDesc(C.Structure):
 
 
 class OutGroups(C.Structure):
-    _fields_ = [("count", C.c_uint32), ("width", C.c_uint32 * 4), ("out", C.c_void_p * 4)]
+    _fields_ = [("count", C.c_uint32), ("width", C.c_uint32 * 4), ("out", C.c_void_p * 4), ("mulact", C.c_uint32),
+                ("ma_sa", C.c_int32), ("ma_sc", C.c_int32)]
 
 
 class ConvDesc(C.Structure):

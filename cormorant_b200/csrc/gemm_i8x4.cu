@@ -34,6 +34,7 @@
 #include "corm_common.cuh"
 #include "corm_sm100.cuh"
 #include "gemm_i8x4.h"
+#include "silu_q.cuh"
 
 namespace corm {
 namespace {
@@ -85,6 +86,11 @@ struct EpiArgs {
   // A in TMEM and at most 64 rows: MMAs of M = 64, whose A and accumulator
   // rows 16 q .. 16 q + 15 sit in TMEM lanes 32 q .. 32 q + 15 (lane quarter q)
   uint32_t m64;
+  // gate / up pairs (GemmJob::mulact): MULACT of each 16-column gate block and
+  // the up block after it, stored at column (block start) / 2
+  uint32_t mulact;
+  int32_t ma_sa, ma_sc;
+  const uint64_t* sig;
 };
 
 // y = floor(acc / 2^8) for acc = 2^16 HH + 2^8 MID + LL + 2^8 bias, i.e.
@@ -247,6 +253,28 @@ __device__ __forceinline__ void store_row(const EpiArgs& ep, uint32_t bz, uint32
       if (c >= ep.cols) break;
       base[col_offset(ep, c)] = (int16_t)(v2[j / 2] >> (16 * (j & 1)));
     }
+  }
+}
+
+// gate / up pairs: the 16 gate values of columns cg .. cg + 15 and the 16 up
+// values after them (packed pairs) -> 16 MULACT results at output column cg / 2
+__device__ __forceinline__ void mulact_store(const EpiArgs& ep, uint32_t bz, uint32_t r, uint32_t cg,
+                                             const uint32_t* g2, const uint32_t* u2) {
+  if (cg >= ep.cols) return;
+  uint32_t o2[8];
+#pragma unroll
+  for (int j = 0; j < 8; j++) {
+    const int16_t lo = corm_mulact((int16_t)(g2[j] & 0xFFFFu), (int16_t)(u2[j] & 0xFFFFu), ep.ma_sa, ep.ma_sc, ep.sig);
+    const int16_t hi = corm_mulact((int16_t)(g2[j] >> 16), (int16_t)(u2[j] >> 16), ep.ma_sa, ep.ma_sc, ep.sig);
+    o2[j] = (uint32_t)(uint16_t)lo | ((uint32_t)(uint16_t)hi << 16);
+  }
+  int16_t* dst = ep.out + (uint64_t)bz * ep.out_batch_stride + (uint64_t)r * ep.ldc + cg / 2;
+  if (((uintptr_t)dst & 15) == 0) {
+    ((int4*)dst)[0] = make_int4((int)o2[0], (int)o2[1], (int)o2[2], (int)o2[3]);
+    ((int4*)dst)[1] = make_int4((int)o2[4], (int)o2[5], (int)o2[6], (int)o2[7]);
+  } else {
+#pragma unroll
+    for (int j = 0; j < 16; j++) dst[j] = (int16_t)(o2[j / 2] >> (16 * (j & 1)));
   }
 }
 
@@ -799,6 +827,10 @@ __global__ void __launch_bounds__(Roles<CONV>::threads, 1)
         if (lane == 0) sm100::mbar_arrive(tmem_empty);
         if (!row_ok) continue;
         const uint32_t c0 = w.tile_c + WC * h;
+        if (ep.mulact) {  // the warp's 32 columns: a gate block, then its up block
+          mulact_store(ep, w.bz, r, c0, v2, v2 + 8);
+          continue;
+        }
         if (ep.post.op != kPostNone) {
           uint32_t b2[WC / 2];
           post_operand<WC>(ep, row_base(ep, w.bz, r), c0, b2);
@@ -809,6 +841,7 @@ __global__ void __launch_bounds__(Roles<CONV>::threads, 1)
         // 16 columns at a time (the register budget of the int16-producer layout):
         // TMEM released after the last chunk's load
         const uint64_t rb = row_ok && ep.post.op != kPostNone ? row_base(ep, w.bz, r) : 0;
+        uint32_t g8[8];  // gate / up pairs: the gate block of the pair (even parts)
 #pragma unroll 1
         for (int part = 0; part < 4; part++) {
           const int cc = R::wc * h + 16 * part;
@@ -826,6 +859,15 @@ __global__ void __launch_bounds__(Roles<CONV>::threads, 1)
           const uint32_t c0 = w.tile_c + cc;
           uint32_t v8[8];
           combine_any<16>(ep, hh, mid, ll, c0, v8, rowb);
+          if (ep.mulact) {
+            if (part & 1) {
+              mulact_store(ep, w.bz, r, c0 - 16, g8, v8);
+            } else {
+#pragma unroll
+              for (int j = 0; j < 8; j++) g8[j] = v8[j];
+            }
+            continue;
+          }
           if (ep.post.op != kPostNone) {
             uint32_t b8[8];
             post_operand<16>(ep, rb, c0, b8);
@@ -1076,7 +1118,11 @@ int gemm_i8x4(const GemmJob& j, cudaStream_t stream) {
       ok = ok && make_map(&m_bhi, j.b_hi, j.Kp, j.cols, j.b_planes) && make_map(&m_blo, j.b_lo, j.Kp, j.cols, j.b_planes);
     if (!ok) return fail(CORM_ECUDA, "gemm: cuTensorMapEncodeTiled failed");
   }
-  const Split sp = split_of(j.rows, j.cols, j.Kp, j.batch);
+  Split sp = split_of(j.rows, j.cols, j.Kp, j.batch);
+  if (j.mulact) {  // gate / up pairs: one K walk per tile (the split's finish has no MULACT)
+    sp.splits = 1;
+    sp.kps = sp.num_kb;
+  }
   EpiArgs ep{};
   ep.mode = j.mode;
   ep.out = j.out;
@@ -1147,6 +1193,17 @@ int gemm_i8x4(const GemmJob& j, cudaStream_t stream) {
   ep.a_box_rows = a_box_rows;
   ep.b_pitch = b_box_cols * 2u;
   ep.m64 = (raw_tma && j.rows <= 64u) ? 1u : 0u;
+  if (j.mulact) {
+    if (j.mode != 0 || j.ngroups > 1 || j.post.op != kPostNone || j.bias || j.cols % 32u || j.ma_sa < 0 ||
+        j.ma_sa > 63 || j.ma_sc < 0 || j.ma_sc > 63)
+      return fail(CORM_EINVAL, "gemm: gate / up pairs need one row-major output, no fused job or bias, cols %% 32 == 0");
+    const DeviceTables* tb = tables();
+    if (!tb) return CORM_ECUDA;
+    ep.mulact = 1;
+    ep.ma_sa = j.ma_sa;
+    ep.ma_sc = j.ma_sc;
+    ep.sig = tb->ro_sig;
+  }
   if (sp.splits > 1) {
     if (!j.partial) return fail(CORM_ENOMEM, "gemm: K-split job without a partial-sum buffer");
     ep.partial = (unsigned long long*)j.partial;

@@ -57,6 +57,11 @@ struct GemmJob {
   uint32_t ngroups;
   int16_t* gout[4];
   uint32_t gw[4];
+  // gate / up pairs: the columns are 16-column blocks alternating gate, up;
+  // out receives MULACT(gate, up) with the shifts ma_sa / ma_sc (the row-ops
+  // unit's SiLU(g << sa) u rounded at sc), [batch][rows][cols / 2] at ldc
+  uint32_t mulact;
+  int32_t ma_sa, ma_sc;
 };
 
 constexpr uint32_t kGemmMaxK = 32768;

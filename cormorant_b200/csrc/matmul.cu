@@ -220,7 +220,11 @@ int tensor_path(const corm_matmul_desc* d, const MmArgs& p, const Plan& pl, uint
   j.rows = d->n;
   j.cols = d->m;
   j.Kp = pl.Kp;
-  if (grp) {
+  if (grp && grp->mulact) {  // gate / up pairs: one output of m / 2 columns
+    j.mulact = 1;
+    j.ma_sa = grp->ma_sa;
+    j.ma_sc = grp->ma_sc;
+  } else if (grp) {
     j.ngroups = grp->count;
     for (uint32_t g = 0; g < 4 && g < grp->count; g++) {
       j.gout[g] = grp->out[g];
@@ -236,7 +240,7 @@ int tensor_path(const corm_matmul_desc* d, const MmArgs& p, const Plan& pl, uint
   j.mode = 0;
   j.out = d->c;
   j.out_batch_stride = d->c_batch_stride;
-  j.ldc = d->m;
+  j.ldc = j.mulact ? d->m / 2 : d->m;
   j.flags = d->flags;
   j.post = post;
   j.err = err;
@@ -488,6 +492,8 @@ extern "C" int corm_matmul_groups(const corm_matmul_desc* d, const corm_out_grou
     return corm::fail(CORM_EINVAL, "corm_matmul_groups: n %u / k %u (the tensor-core path: n > %u, k > 0)", d->n, d->k,
                       kSmallRows);
   if (d->n == 0 || d->m == 0 || d->batch == 0) return CORM_OK;
+  if (g->mulact && (g->count != 1 || d->m % 32u || g->width[0] != d->m / 2 || !g->out[0]))
+    return corm::fail(CORM_EINVAL, "corm_matmul_groups: gate / up pairs need one output of m / 2 columns, m %% 32 == 0");
   cudaStream_t st = (cudaStream_t)stream;
   corm_matmul_desc dd = *d;
   dd.c = g->out[0];
@@ -550,7 +556,15 @@ extern "C" int corm_matmul_bplanes(const corm_matmul_desc* d, const int8_t* b_hi
   j.lda = d->k;
   j.b_hi = b_hi;
   j.b_lo = b_lo;
-  if (g) {
+  if (g && g->mulact) {  // gate / up pairs: one output of m / 2 columns
+    if (g->count != 1 || d->m % 32u || g->width[0] != d->m / 2 || !g->out[0])
+      return corm::fail(CORM_EINVAL, "corm_matmul_bplanes: gate / up pairs need one output of m / 2 columns");
+    j.mulact = 1;
+    j.ma_sa = g->ma_sa;
+    j.ma_sc = g->ma_sc;
+    j.ldc = d->m / 2;
+    j.out_batch_stride = (uint64_t)d->n * (d->m / 2);
+  } else if (g) {
     j.ngroups = g->count;
     for (uint32_t q = 0; q < g->count; q++) {
       j.gout[q] = g->out[q];

@@ -11,6 +11,7 @@
 #include <mutex>
 
 #include "corm_common.cuh"
+#include "silu_q.cuh"
 
 namespace {
 
@@ -87,23 +88,6 @@ __device__ __forceinline__ Param ld_param(const RoArgs& q, uint32_t c) {
   r.sb = e[9] & 63u;
   r.sc = e[10] & 63u;
   return r;
-}
-
-// sigma(g) at 2^-24 for g = gv 2^-14 from the table words (rowops_spec.py:345-358)
-__device__ __forceinline__ int64_t sig_q(int64_t gv, const uint64_t* __restrict__ sig) {
-  const int64_t a = gv < 0 ? -gv : gv;
-  const bool big = a >= ((int64_t)16 << 14);
-  const int64_t ai = big ? ((int64_t)16 << 14) - 1 : a;
-  const uint64_t e = sig[ai >> 6];
-  const int64_t t = (int64_t)(e & 0x1FFFFFFull), dl = (int64_t)((e >> 25) & 0xFFFFFFull), fr = ai & 63;
-  int64_t s = t + ((dl * fr) >> 6);
-  if (big) s = (int64_t)1 << 24;
-  if (gv < 0) s = ((int64_t)1 << 24) - s;
-  return s;
-}
-
-__device__ __forceinline__ int64_t silu_q(int64_t gv, const uint64_t* sig) {
-  return (int64_t)corm_rne_shr128((__int128)gv * sig_q(gv, sig), 14 + 24 - 20);
 }
 
 // float32 bits of v 2^-sh_c, IEEE round to nearest even (rowops_ref.h:190-203)

@@ -92,13 +92,23 @@ def matmul(a, b, c, *, n, k, m, batch=1, a_batch_stride=0, b_batch_stride=0, c_b
     return workspace
 
 
+def _groups(outs, widths, mulact):
+    g = _lib.OutGroups(len(outs), (C.c_uint32 * 4)(*(list(widths) + [0] * (4 - len(widths)))),
+                       (C.c_void_p * 4)(*([_ptr(t) for t in outs] + [None] * (4 - len(outs)))))
+    if mulact is not None:
+        g.mulact, g.ma_sa, g.ma_sc = 1, int(mulact[0]), int(mulact[1])
+    return g
+
+
 def matmul_groups(a, b, outs, widths, *, n, k, batch=1, a_batch_stride=0, b_batch_stride=0, flags=0,
-                  workspace=None):
+                  workspace=None, mulact=None):
     """One MatMul job over B = [k][sum(widths)] whose output columns go to
     several buffers (corm_matmul_groups): outs[g] receives the widths[g]
     columns of group g, row-major [batch][n][widths[g]].  Sibling projections
     that read the same A run as one launch; n > 2, all widths but the last
-    multiples of 32."""
+    multiples of 32.  ``mulact`` = (sa, sc): B's columns are gate / up pairs
+    of 16-column blocks and outs[0] (one output, widths[0] = m / 2) receives
+    their row-ops MULACT (SiLU(g << sa) u rounded at sc)."""
     for t, nm in ((a, "a"), (b, "b")):
         _i16(t, nm)
     if not 1 <= len(outs) == len(widths) <= 4:
@@ -106,7 +116,7 @@ def matmul_groups(a, b, outs, widths, *, n, k, batch=1, a_batch_stride=0, b_batc
     for t in outs:
         _i16(t, "out")
     st = _ready()
-    m = int(sum(widths))
+    m = int(sum(widths)) * (2 if mulact is not None else 1)
     d = _lib.MatmulDesc(_ptr(a), _ptr(b), _ptr(outs[0]), n, k, m, batch, a_batch_stride, b_batch_stride,
                         n * widths[0], 0, 0, flags, None, 0)
     need = C.c_size_t(0)
@@ -115,8 +125,7 @@ def matmul_groups(a, b, outs, widths, *, n, k, batch=1, a_batch_stride=0, b_batc
         if workspace is None:
             workspace = torch.empty(need.value, dtype=torch.uint8, device=a.device)
         d.workspace, d.workspace_bytes = _ptr(workspace), workspace.numel() * workspace.element_size()
-    g = _lib.OutGroups(len(outs), (C.c_uint32 * 4)(*(list(widths) + [0] * (4 - len(widths)))),
-                       (C.c_void_p * 4)(*([_ptr(t) for t in outs] + [None] * (4 - len(outs)))))
+    g = _groups(outs, widths, mulact)
     check(lib().corm_matmul_groups(C.byref(d), C.byref(g), st))
     return workspace
 
@@ -135,10 +144,11 @@ def split_b_planes(b, *, k, m):
 
 
 def matmul_bplanes(a, planes, c, *, n, k, m, batch=1, a_batch_stride=0, c_batch_stride=0, flags=0, workspace=None,
-                   outs=None, widths=None):
+                   outs=None, widths=None, mulact=None):
     """A MatMul job against a weight given as its planes (split_b_planes):
     the GEMM splits only A.  ``outs`` / ``widths``: output column groups
-    instead of c (as matmul_groups)."""
+    instead of c (as matmul_groups); ``mulact``: gate / up pairs (as
+    matmul_groups)."""
     _i16(a, "a")
     st = _ready()
     d = _lib.MatmulDesc(_ptr(a), None, _ptr(c) if c is not None else None, n, k, m, batch, a_batch_stride, 0,
@@ -151,8 +161,7 @@ def matmul_bplanes(a, planes, c, *, n, k, m, batch=1, a_batch_stride=0, c_batch_
         d.workspace, d.workspace_bytes = _ptr(workspace), workspace.numel() * workspace.element_size()
     g = None
     if outs is not None:
-        g = _lib.OutGroups(len(outs), (C.c_uint32 * 4)(*(list(widths) + [0] * (4 - len(widths)))),
-                           (C.c_void_p * 4)(*([_ptr(t) for t in outs] + [None] * (4 - len(outs)))))
+        g = _groups(outs, widths, mulact)
     check(lib().corm_matmul_bplanes(C.byref(d), _ptr(planes[0]), _ptr(planes[1]), C.byref(g) if g is not None else None,
                                     st))
     return workspace

@@ -103,6 +103,7 @@ class GpuSimulator:
         self._plan = self._fusion_plan() if fuse else {}
         self._groups = self._sibling_groups() if fuse else {}
         self._pairs = self._rowops_pairs() if fuse else {}
+        self._mulacts = self._mulact_pairs() if fuse else {}
 
     # ------------------------------------------------------------ tensors
     def _alloc(self, numel: int) -> torch.Tensor:
@@ -374,6 +375,7 @@ class GpuSimulator:
         for _mi, info in attn_fused.items():
             skip |= set(info["nodes"])
         skip |= set(self._pairs.values())
+        skip |= set(self._mulacts.values())
 
         def get(t):
             if t.onnx_name not in raw:
@@ -393,7 +395,11 @@ class GpuSimulator:
                 alias_t = self._graph.nodes[ri].output
                 if pspec is not None:
                     post = self._post_of(pspec, get)
-            if i in self._groups:
+            if i in self._mulacts:  # gate / up and their SiLU(g) u in one launch
+                sm = self._graph.nodes[self._mulacts[i]]
+                y = self._matmul_mulact(self._groups[i], sm, get)
+                out_t = sm.output
+            elif i in self._groups:
                 ys = self._matmul_group(self._groups[i], get)
                 for j, yj in zip(self._groups[i][1:], ys[1:]):
                     t = self._graph.nodes[j].output
@@ -578,6 +584,66 @@ class GpuSimulator:
         else:
             ops.matmul_groups(get(A), self._weights[key], ys, widths, n=n, k=k, flags=wrap, workspace=ws)
         return ys
+
+    def _mulact_pairs(self) -> Dict[int, int]:
+        """Sibling pairs (gate, up) whose two outputs only a SiluMulRoNode
+        reads, with one broadcast parameter entry: {the pair's first index:
+        the SiluMul index}.  The pair runs as one GEMM over the gate / up
+        weights interleaved in 16-column blocks whose epilogue applies the
+        MULACT (corm_matmul_groups with mulact)."""
+        nodes, out = self._graph.nodes, {}
+        readers: Dict[str, int] = {}
+        for sn in nodes:
+            for t in sn.inputs:
+                if t is not None:
+                    readers[t.onnx_name] = readers.get(t.onnx_name, 0) + 1
+        for first, members in self._groups.items():
+            if len(members) != 2:
+                continue
+            g, u = (nodes[j] for j in members)
+            wg, wu = int(g.inputs[1].shape[1]), int(u.inputs[1].shape[1])
+            if wg != wu or wg % 16:
+                continue
+            for j in range(members[1] + 1, len(nodes)):
+                sm = nodes[j]
+                if _kind(sm) != "SiluMulRoNode":
+                    continue
+                if (sm.inputs[0].onnx_name == g.output.onnx_name and sm.inputs[1].onnx_name == u.output.onnx_name and
+                        bool(getattr(sm, "bcast", False)) and readers.get(g.output.onnx_name) == 1 and
+                        readers.get(u.output.onnx_name) == 1 and sm.n == wg):
+                    out[first] = j
+                break
+        return out
+
+    def _matmul_mulact(self, members, sm, get):
+        """The gate / up pair and the SiluMul job of their outputs as one
+        launch: the weights interleaved in 16-column blocks (gate block i,
+        then up block i), once; the MULACT entry's shifts from its parameter
+        words (byte 8 sa, byte 10 sc)."""
+        sg, su = (self._graph.nodes[j] for j in members)
+        A = sg.inputs[0]
+        n, k = int(np.prod(A.shape[:-1])), int(A.shape[-1])
+        ffn = int(sg.inputs[1].shape[1])
+        key = ("mulact", sg.inputs[1].onnx_name, su.inputs[1].onnx_name)
+        if key not in self._weights:
+            wg = get(sg.inputs[1])[:k * ffn].view(k, ffn // 16, 16)
+            wu = get(su.inputs[1])[:k * ffn].view(k, ffn // 16, 16)
+            cat = self._alloc(2 * k * ffn)
+            cat[:2 * k * ffn].view(k, ffn // 16, 2, 16).copy_(torch.stack([wg, wu], dim=2))
+            self._weights[key] = cat
+        pw = np.round(np.asarray(sm.inputs[2].data, np.float64).reshape(-1)[:8] * 256.0).astype(np.int16)
+        words = pw.view(np.uint8)  # (host data: no device read, so the pass can be captured as a graph)
+        sa, sc = int(words[8]) & 63, int(words[10]) & 63
+        y = self._alloc(sm.output.numel)
+        wrap = F_WRAP32 if _has_exp(A, sg.inputs[1], sg.output) else 0
+        ws = self._workspace(self._mm_ws(n, k, 2 * ffn, 1, 0, 0))
+        if self._use_bplanes(n, k):
+            ops.matmul_bplanes(get(A), self._planes(key, self._weights[key], k, 2 * ffn), None, n=n, k=k, m=2 * ffn,
+                               flags=wrap, workspace=ws, outs=[y], widths=[ffn], mulact=(sa, sc))
+        else:
+            ops.matmul_groups(get(A), self._weights[key], [y], [ffn], n=n, k=k, flags=wrap, workspace=ws,
+                              mulact=(sa, sc))
+        return y
 
     # few rows against a constant weight: the weight split into its planes once
     # (cached beside it) and only A split inside each job

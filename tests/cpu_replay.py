@@ -49,12 +49,26 @@ def install(setattr_fn):
         spec.matmul_job(np16(a), np16(b), np16(c), n, k, m, batch, a_batch_stride, b_batch_stride, c_batch_stride,
                         b_packed, gemv_kw, wrap=bool(flags & F_WRAP32))
 
+    def mulact_pairs(y, sa, sc):
+        """Gate / up pairs of 16-column blocks -> the row-ops MULACT of each pair."""
+        n, m = y.shape
+        g = y.reshape(n, m // 32, 2, 16)[:, :, 0, :].reshape(n, m // 2)
+        u = y.reshape(n, m // 32, 2, 16)[:, :, 1, :].reshape(n, m // 2)
+        out = np.empty((n, m // 2), np.int64)
+        for idx in np.ndindex(out.shape):
+            v = spec._rne(spec.silu_q(int(g[idx]) << sa) * int(u[idx]), sc)
+            out[idx] = min(max(v, -32768), 32767)
+        return out
+
     def matmul_groups(a, b, outs, widths, *, n, k, batch=1, a_batch_stride=0, b_batch_stride=0, flags=0,
-                      workspace=None):
+                      workspace=None, mulact=None):
         assert batch == 1
-        m = sum(widths)
+        m = sum(widths) * (2 if mulact is not None else 1)
         y = spec.matmul_raw(np16(a)[:n * k].astype(np.int64).reshape(n, k), np16(b)[:k * m].astype(np.int64).reshape(k, m),
                             wrap=bool(flags & F_WRAP32))
+        if mulact is not None:
+            np16(outs[0])[:n * m // 2] = mulact_pairs(y, *mulact).reshape(-1)
+            return
         c0 = 0
         for o, w in zip(outs, widths):
             np16(o)[:n * w] = y[:, c0:c0 + w].reshape(-1)
@@ -64,10 +78,13 @@ def install(setattr_fn):
         return (b, None)  # the fake keeps the int16 weight itself
 
     def matmul_bplanes(a, planes, c, *, n, k, m, batch=1, a_batch_stride=0, c_batch_stride=0, flags=0,
-                       workspace=None, outs=None, widths=None):
+                       workspace=None, outs=None, widths=None, mulact=None):
         assert batch == 1
         y = spec.matmul_raw(np16(a)[:n * k].astype(np.int64).reshape(n, k),
                             np16(planes[0])[:k * m].astype(np.int64).reshape(k, m), wrap=bool(flags & F_WRAP32))
+        if mulact is not None:
+            np16(outs[0])[:n * m // 2] = mulact_pairs(y, *mulact).reshape(-1)
+            return
         if flags & (F_ACT_RELU | F_ACT_RELU6):  # a fused ReLU / Clip(0,6)
             y = np.maximum(y, 0)
             if flags & F_ACT_RELU6:
