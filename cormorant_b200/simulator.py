@@ -602,7 +602,12 @@ class GpuSimulator:
                 continue
             g, u = (nodes[j] for j in members)
             wg, wu = int(g.inputs[1].shape[1]), int(u.inputs[1].shape[1])
-            if wg != wu or wg % 16:
+            A = g.inputs[0]
+            n, k = int(np.prod(A.shape[:-1])), int(A.shape[-1])
+            # few rows (a decode step): the pair GEMM has few tiles and each
+            # epilogue thread would run all its row's MULACTs; the separate
+            # row-ops job spreads them (measured 32.9 against 29.0 us)
+            if wg != wu or wg % 16 or self._use_bplanes(n, k):
                 continue
             for j in range(members[1] + 1, len(nodes)):
                 sm = nodes[j]

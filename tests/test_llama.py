@@ -46,13 +46,16 @@ def _compare(g, arr, ref, states, rstates):
         assert np.array_equal(got, rstates[t.onnx_name]), t.onnx_name
 
 
-def test_llama_host_logic_cpu(cpu_ops):
+@pytest.mark.parametrize("seq", [16, 144])
+def test_llama_host_logic_cpu(cpu_ops, seq):
     """GpuSimulator's host logic on the Llama graph (every job's registers,
     the batched attention's strides, the states) with its kernel calls
-    replayed on the oracle's job models, against the oracle's forward pass."""
+    replayed on the oracle's job models, against the oracle's forward pass;
+    at 288 rows the gate / up pair and its SiluMul run as one job (the
+    interleaved weights, the MULACT shifts from the parameter words)."""
     from cormorant_b200 import workloads as WL
     from oracle import llm
-    g, feeds, _ = WL.llama_prefill(seed=8, batch=2, seq=16, layers=1, hidden=64, heads=4, kv_heads=2, head_dim=16,
+    g, feeds, _ = WL.llama_prefill(seed=8, batch=2, seq=seq, layers=1, hidden=64, heads=4, kv_heads=2, head_dim=16,
                                    ffn=128, vocab=50)
     states = {t.onnx_name: np.zeros(t.shape) for t in g.state_tensors}
     arr = cpu_ops(g, device="cpu").forward_pass(feeds, states=states)
