@@ -374,6 +374,9 @@ class GpuSimulator:
         attn_fused = self._decode_attn_plan(keep) if (self.fuse and keep is not None) else {}
         for _mi, info in attn_fused.items():
             skip |= set(info["nodes"])
+        # prefill attention with the q image and the scores in their transposed
+        # layouts where nobody observes them (the names of the tensors held so)
+        self._tr = self._attn_transpose_plan(keep) if (self.fuse and keep is not None) else set()
         skip |= set(self._pairs.values())
         skip |= set(self._mulacts.values())
 
@@ -859,6 +862,9 @@ class GpuSimulator:
                 ops.copy_nd(src, cache, (KV, B, n, HD), (HD, T * nk, nk, 1), (B * C * HD, C * HD, HD, 1),
                             dst_off=pos * HD)
         GT = G * T
+        if sn.output.onnx_name in getattr(self, "_tr", ()):  # [KV][B][G T][HD]: rows of HD as ROPE wrote them
+            ops.copy_nd(qs, qx, (KV, B, G, T, HD), (G * HD, T * nq, HD, nq, 1), (B * GT * HD, GT * HD, T * HD, HD, 1))
+            return qx
         ops.copy_nd(qs, qx, (KV, B, G, T, HD), (G * HD, T * nq, HD, nq, 1), (B * HD * GT, HD * GT, T, 1, GT))
         return qx
 
@@ -877,6 +883,14 @@ class GpuSimulator:
         keys = C if sn.static else self._keys(sn, get, 2)[2]
         w, x = get(sn.inputs[0]), get(sn.inputs[1])
         y = self._alloc(sn.output.numel)
+        if sn.kind == "qk" and sn.output.onnx_name in getattr(self, "_tr", ()):
+            # the scores transposed, [B G T][C]: per sequence the q image rows
+            # [G T][HD] @ the K cache rows [0, keys) as B transposed
+            self._ws = ops.gemm_strided(x[g * B * GT * HD:], w[g * B * C * HD:], y, n=GT, k=HD, m=keys, batch=B,
+                                        lda=HD, ldb=HD, ldc=C, b_trans=True, a_batch_stride=GT * HD,
+                                        b_batch_stride=C * HD, c_batch_stride=GT * C, flags=F_WRAP32,
+                                        workspace=self._ws)
+            return y
         if sn.kind == "qk":
             rows, r0 = (sn.nr, sn.r0) if sn.nr else (keys, 0)
             self._ws = ops.gemm_strided(w[(g * B * C + r0) * HD:], x[g * B * HD * GT:], y, n=rows, k=HD, m=GT, batch=B,
@@ -910,6 +924,10 @@ class GpuSimulator:
         if keys < C and self._seen(sn.output):
             y.zero_()
         regs = [(int(sn.cm[h]), int(sn.cfg[h])) for h in range(G)]
+        if sn.inputs[0].onnx_name in getattr(self, "_tr", ()):  # transposed scores: the same P by rows
+            ops.vectorop(s, None, y, size=keys, op=10, outer=B * GT, a_inc=C, b_inc=C, smx_cm=regs[0][0],
+                         smx_cfg=regs[0][1], smx_mask=mask)
+            return y
         if all(r == regs[0] for r in regs):
             ops.vectorop(s, None, y, size=keys, op=11, outer=B * GT, a_inc=B * GT, b_inc=C, smx_cm=regs[0][0],
                          smx_cfg=regs[0][1], smx_mask=mask)
@@ -942,6 +960,50 @@ class GpuSimulator:
         ops.llm_attn_softmax(get(sn.inputs[0]), y, tab, ip, pos=pos, n=max(n, 0), T=sn.T, G=sn.G, rows=sn.C, Q=sn.Q,
                              window=int(getattr(sn, "window", 0)), batch=B)
         return y
+
+    def _attn_transpose_plan(self, keep) -> set:
+        """Names of the prefill attention tensors held transposed in a lean
+        pass: a q image qx [KV][B][HD][G T] as [KV][B][G T][HD] (the ROPE
+        rows copied without a transposition) when every reader of it is a
+        q.K^T over all its keys (no row pieces, not static) and nobody
+        observes it; those q.K^T's scores [C][B G T] as [B G T][C] when their
+        one reader is the unit's column softmax with the same registers for
+        every head, which then runs in row mode (the same P: a column of the
+        scores is a row of their transpose)."""
+        key = frozenset(keep)
+        cache = self.__dict__.setdefault("_tr_plans", {})
+        if key in cache:
+            return cache[key]
+        nodes = self._graph.nodes
+        readers: Dict[str, list] = {}
+        for i, sn in enumerate(nodes):
+            for t in sn.inputs:
+                if t is not None:
+                    readers.setdefault(t.onnx_name, []).append(i)
+        out = set()
+        for sn in nodes:
+            if _kind(sn) != "AttnPrepRoNode" or sn.output.onnx_name in key:
+                continue
+            qn = sn.output.onnx_name
+            convs = [nodes[i] for i in readers.get(qn, [])]
+            ok = bool(convs)
+            scores = []
+            for cn in convs:
+                if (_kind(cn) != "LlmAttnConvNode" or cn.kind != "qk" or cn.static or cn.nr or
+                        cn.inputs[1].onnx_name != qn or cn.output.onnx_name in key):
+                    ok = False
+                    break
+                rs = [nodes[i] for i in readers.get(cn.output.onnx_name, [])]
+                if (len(rs) != 1 or _kind(rs[0]) != "LlmAttnSoftmaxVopNode" or
+                        len({(int(c), int(f)) for c, f in zip(rs[0].cm, rs[0].cfg)}) != 1):
+                    ok = False
+                    break
+                scores.append(cn.output.onnx_name)
+            if ok:
+                out.add(qn)
+                out.update(scores)
+        cache[key] = out
+        return out
 
     def _decode_attn_plan(self, keep) -> dict:
         """{merge node index: plan} for the decode steps' attention blocks whose

@@ -64,6 +64,29 @@ def test_llama_host_logic_cpu(cpu_ops, seq):
     _compare(g, arr, ref, states, rstates)
 
 
+def test_llama_lean_prefill_cpu(cpu_ops):
+    """The lean prefill (only the logits kept): the q image and the scores
+    held transposed, the softmax by rows — with the kernel calls replayed on
+    the oracle's job models, the logits and the caches equal the oracle's."""
+    from cormorant_b200 import workloads as WL
+    from oracle import llm
+    g, feeds, _ = WL.llama_prefill(seed=9, batch=2, seq=32, layers=2, hidden=64, heads=4, kv_heads=2, head_dim=16,
+                                   ffn=128, vocab=50)
+    out = g.output_tensors[0].onnx_name
+    sim = cpu_ops(g, device="cpu")
+    states = {t.onnx_name: np.zeros(t.shape) for t in g.state_tensors}
+    arr = sim.forward_pass(feeds, states=states, keep=[out])
+    assert sim._tr, "no transposed attention in the lean pass"
+    rstates = {t.onnx_name: np.zeros(t.shape, np.int64) for t in g.state_tensors}
+    ref = llm.forward(g, _raw_inputs(g, feeds), rstates)
+    t = g.output_tensors[0]
+    got = np.rint(np.asarray(arr[out]) * np.power(2.0, np.asarray(t.exp, np.float64))).astype(np.int64)
+    assert np.array_equal(got.reshape(ref[out].shape), ref[out])
+    for st in g.state_tensors:
+        v = np.rint(states[st.onnx_name] * np.power(2.0, np.asarray(st.exp, np.float64))).astype(np.int64)
+        assert np.array_equal(v, rstates[st.onnx_name]), st.onnx_name
+
+
 @pytest.mark.gpu
 @pytest.mark.parametrize("fuse", [False, True])
 def test_gpu_llama_prefill_vs_oracle(fuse):
