@@ -443,75 +443,125 @@ __device__ __forceinline__ void dw3_slow_row(const int16_t* win, uint32_t SP, in
   }
 }
 
-template <int S_, int PL_, bool ROWS, int NR_>
+__device__ __forceinline__ void dw_cp_async16(void* smem, const void* gmem) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(smem)), "l"(gmem)
+               : "memory");
+}
+__device__ __forceinline__ void dw_cp_async4(void* smem, const void* gmem) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"((uint32_t)__cvta_generic_to_shared(smem)), "l"(gmem)
+               : "memory");
+}
+__device__ __forceinline__ void dw_cp_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void dw_cp_wait1() { asm volatile("cp.async.wait_group 1;" ::: "memory"); }
+
+// LD: how a unit's planes reach shared memory.  0: one contiguous range read
+// into registers and scattered (any W); 1: each 16-byte word of a row by
+// cp.async (W % 8 == 0); 2: each pair of columns by a 4-byte cp.async (W
+// even).  1 and 2 double-buffer the staging (and the per-plane data): the
+// next unit's copies are in flight while this unit is computed; the padding
+// (zero columns and rows) is written once, as no copy touches it.
+template <int S_, int PL_, int LD, int NR_>
 __global__ void __launch_bounds__(256) conv_dw3x3(ConvArgs a, DwGeo q) {
   corm_pdl_wait();
   corm_pdl_trigger();
-  // dynamic shared memory: per plane its output pointer, bias << 8, channel,
-  // taps and path; then the staged inputs [G][SHb][SPW * 8]; then (no vst) the
-  // outputs [G][P]
+  // dynamic shared memory: per buffer the per-plane data (output pointer,
+  // bias << 8, channel, taps, path); then the staged inputs, per buffer
+  // [G][SHb][SPW * 8]; then (no vst) the outputs [G][P]
+  constexpr bool ASYNC = LD != 0;
+  constexpr int NBUF = ASYNC ? 2 : 1;
   extern __shared__ __align__(16) uint8_t s_dw[];
-  int16_t** s_yp = (int16_t**)s_dw;
-  int32_t* s_b = (int32_t*)(s_yp + q.G);
-  uint32_t* s_m = (uint32_t*)(s_b + q.G);
-  int16_t(*s_w)[10] = (int16_t(*)[10])(s_m + q.G);
-  uint8_t* s_fast = (uint8_t*)(s_w + q.G);
-  int16_t* s_in = (int16_t*)(s_dw + q.meta);
   constexpr int NR = NR_;
   constexpr int QR = (NR - 1) * S_ + 3;  // input rows of a group of NR output rows
   constexpr int NWIN = S_ == 1 ? 3 : 4;  // window words per input row
   const uint32_t SP = q.SPW * 8u, PS = q.SHb * SP;
   const uint32_t HW = a.H * a.W, P = a.OH * a.OW;
-  int16_t* s_out = s_in + (size_t)q.G * PS;
+  int16_t* s_in0 = (int16_t*)(s_dw + NBUF * q.meta);
+  int16_t* s_out = s_in0 + (size_t)NBUF * q.G * PS;
   const uint64_t planes = (uint64_t)a.batch * a.M;
   const uint32_t RUNSin = (a.W + 7u) / 8u;
   const bool wrap = (a.flags & CORM_F_WRAP32) != 0;
-  for (uint32_t unit = blockIdx.x; unit < q.units; unit += gridDim.x) {
+  auto live_of = [&](uint32_t unit) {
     const uint64_t p0 = (uint64_t)unit * q.G;
-    const uint32_t glive = (uint32_t)(planes - p0 < (uint64_t)q.G ? planes - p0 : (uint64_t)q.G);
+    return (uint32_t)(planes - p0 < (uint64_t)q.G ? planes - p0 : (uint64_t)q.G);
+  };
+  // the per-plane data of a unit into buffer k
+  auto fill_meta = [&](uint32_t unit, int k) {
+    uint8_t* mb = s_dw + k * q.meta;
+    int16_t** m_yp = (int16_t**)mb;
+    int32_t* m_b = (int32_t*)(m_yp + q.G);
+    uint32_t* m_m = (uint32_t*)(m_b + q.G);
+    int16_t(*m_w)[10] = (int16_t(*)[10])(m_m + q.G);
+    uint8_t* m_fast = (uint8_t*)(m_w + q.G);
+    const uint64_t p0 = (uint64_t)unit * q.G;
+    const uint32_t glive = live_of(unit);
     for (uint32_t pl = threadIdx.x; pl < glive; pl += blockDim.x) {
       const uint64_t plane = p0 + pl;
       const uint32_t m = (uint32_t)(plane % a.M), n = (uint32_t)(plane / a.M);
-      s_yp[pl] = a.y + (uint64_t)n * a.M * P + y_chan(a, m);
+      m_yp[pl] = a.y + (uint64_t)n * a.M * P + y_chan(a, m);
       const int32_t b = a.bias ? (int32_t)a.bias[m] : 0;
       uint32_t sw = 0;
 #pragma unroll
       for (int t = 0; t < 9; t++) {
         const int16_t w = __ldg(a.w + w_offset(a, m, 0, t / 3, t % 3));
-        s_w[pl][t] = w;
+        m_w[pl][t] = w;
         sw += (uint32_t)(w < 0 ? -(int32_t)w : (int32_t)w);
       }
-      s_b[pl] = b << 8;
-      s_m[pl] = m;
+      m_b[pl] = b << 8;
+      m_m[pl] = m;
       // |acc| <= |b| 2^8 + 2^15 sum|w| (sum|w| <= 9 * 2^15 keeps this below 2^63)
       const int64_t bound = (int64_t)(b < 0 ? -b : b) * 256 + (int64_t)sw * 32768;
-      s_fast[pl] = (wrap || bound <= 2147483647ll) ? 1 : 0;
+      m_fast[pl] = (wrap || bound <= 2147483647ll) ? 1 : 0;
     }
-    if (ROWS) {
-      // every staged word written once: data, or zeros outside the image / row
-      const uint32_t nw = q.G * q.SHb * q.SPW;
-      for (uint32_t i0 = 0; i0 < nw; i0 += 4u * blockDim.x) {
-        int4 v[4];
-        uint32_t dst[4];
-#pragma unroll
-        for (int k = 0; k < 4; k++) {
-          const uint32_t i = i0 + k * blockDim.x + threadIdx.x;
-          v[k] = make_int4(0, 0, 0, 0);
-          dst[k] = 0xFFFFFFFFu;
-          if (i < nw) {
-            const uint32_t g = i / (q.SHb * q.SPW), rem = i - g * (q.SHb * q.SPW);
-            const uint32_t sr = rem / q.SPW, w = rem - sr * q.SPW;
-            const int ih = (int)sr - (int)a.pt;
-            dst[k] = g * PS + sr * SP + 8u * w;
-            if (g < glive && w >= 1u && w <= RUNSin && ih >= 0 && ih < (int)a.H)
-              v[k] = __ldg((const int4*)(a.x + ((p0 + g) * a.H + (uint32_t)ih) * a.W) + (w - 1u));
-          }
-        }
-#pragma unroll
-        for (int k = 0; k < 4; k++)
-          if (dst[k] != 0xFFFFFFFFu) *(int4*)(s_in + dst[k]) = v[k];
+  };
+  // the copies of a unit's rows into staging buffer k (LD 1 / 2)
+  auto issue_loads = [&](uint32_t unit, int k) {
+    int16_t* buf = s_in0 + (size_t)k * q.G * PS;
+    const uint64_t p0 = (uint64_t)unit * q.G;
+    const uint32_t glive = live_of(unit);
+    const uint32_t per_row = LD == 1 ? RUNSin : a.W / 2u, per_plane = a.H * per_row;
+    const uint32_t n = glive * per_plane;
+    for (uint32_t i = threadIdx.x; i < n; i += blockDim.x) {
+      const uint32_t g = i / per_plane, rem = i - g * per_plane;
+      const uint32_t ih = rem / per_row, c = rem - ih * per_row;
+      const uint32_t sr = ih + a.pt;
+      if (sr >= q.SHb) continue;
+      const int16_t* src = a.x + ((p0 + g) * a.H + ih) * a.W;
+      int16_t* dst = buf + g * PS + sr * SP + 8u;
+      if (LD == 1) dw_cp_async16(dst + 8u * c, src + 8u * c);
+      else dw_cp_async4(dst + 2u * c, src + 2u * c);
+    }
+  };
+  if (ASYNC) {
+    const uint32_t nz = NBUF * q.G * PS / 8u;
+    for (uint32_t i = threadIdx.x; i < nz; i += blockDim.x) ((int4*)s_in0)[i] = make_int4(0, 0, 0, 0);
+    __syncthreads();
+    if (blockIdx.x < q.units) {
+      issue_loads(blockIdx.x, 0);
+      fill_meta(blockIdx.x, 0);
+    }
+    dw_cp_commit();
+  }
+  int kb = 0;
+  for (uint32_t unit = blockIdx.x; unit < q.units; unit += gridDim.x, kb ^= (ASYNC ? 1 : 0)) {
+    const uint64_t p0 = (uint64_t)unit * q.G;
+    const uint32_t glive = live_of(unit);
+    int16_t* s_in = s_in0 + (size_t)kb * q.G * PS;
+    uint8_t* mb = s_dw + kb * q.meta;
+    int16_t** s_yp = (int16_t**)mb;
+    int32_t* s_b = (int32_t*)(s_yp + q.G);
+    uint32_t* s_m = (uint32_t*)(s_b + q.G);
+    int16_t(*s_w)[10] = (int16_t(*)[10])(s_m + q.G);
+    uint8_t* s_fast = (uint8_t*)(s_w + q.G);
+    if (ASYNC) {
+      const uint32_t next = unit + gridDim.x;
+      if (next < q.units) {  // the next unit's copies fly while this one is computed
+        issue_loads(next, kb ^ 1);
+        fill_meta(next, kb ^ 1);
       }
+      dw_cp_commit();
+      dw_cp_wait1();  // every group but the newest: this unit's rows have landed
     } else {
+      fill_meta(unit, 0);
       const uint32_t nz = q.G * PS / 8u;
       for (uint32_t i = threadIdx.x; i < nz; i += blockDim.x) ((int4*)s_in)[i] = make_int4(0, 0, 0, 0);
       __syncthreads();
@@ -944,6 +994,11 @@ int conv_impl(const corm_conv_desc* d, const corm::PostOp& post, cudaStream_t st
       q.SHb = (q.NRG * NR - 1) * S + 3;
       q.SPW = std::max(runs_in + 2u, S == 1 ? q.RUNS + 2u : 2u * q.RUNS + 2u);
       const bool rows = d->in_w % 8u == 0;
+      // how the planes reach shared memory: 16-byte words of whole-word rows or
+      // 4-byte pairs of even-width rows by cp.async (double-buffered), else
+      // one contiguous range through registers
+      const int ld = rows ? 1 : (d->in_w % 2u == 0 ? 2 : 0);
+      const uint32_t nbuf = ld ? 2u : 1u;
       const bool dense = d->y_cn == 0 && (d->y_cs == 0 || d->y_cs == P) && !((uintptr_t)d->y & 15u) &&
                          a.post.op == corm::kPostNone;
       q.vst = dense && d->out_w % 8u == 0;
@@ -954,17 +1009,17 @@ int conv_impl(const corm_conv_desc* d, const corm::PostOp& post, cudaStream_t st
         while (u > 1 && (uint64_t)(u / 2) * n % 8u == 0) u /= 2;
         return u;
       };
-      const uint32_t unit = std::max(rows ? 1u : align8(HW), (!q.vst && dense) ? align8(P) : 1u);
+      const uint32_t unit = std::max(ld == 0 ? align8(HW) : 1u, (!q.vst && dense) ? align8(P) : 1u);
       // small planes: CTAs of two warps with units of about 10 KB (many CTAs per
       // SM, so one CTA's barriers never idle the SM); large planes: 8 warps, 36 KB
       const bool small = (size_t)q.SHb * q.SPW * 16u <= 4096u;
       const unsigned threads = small ? 64u : 256u;
       const size_t target = small ? 10u * 1024u : 36u * 1024u;
-      const size_t plane_b = (size_t)q.SHb * q.SPW * 16u + (q.vst ? 0u : (size_t)P * 2u) + 40u;
+      const size_t plane_b = nbuf * ((size_t)q.SHb * q.SPW * 16u + 40u) + (q.vst ? 0u : (size_t)P * 2u);
       uint32_t G = (uint32_t)std::min<size_t>(kDw3MaxG, std::max<size_t>(1, target / plane_b));
       G = std::max(unit, G / unit * unit);
       q.meta = (G * 40u + 15u) / 16u * 16u;
-      const size_t smem = q.meta + (size_t)G * q.SHb * q.SPW * 16u +
+      const size_t smem = nbuf * (q.meta + (size_t)G * q.SHb * q.SPW * 16u) +
                           (q.vst ? 0u : ((size_t)G * P * 2u + 15u) / 16u * 16u);
       if (G <= kDw3MaxG && smem <= 100u * 1024u) {
         const uint64_t planes = (uint64_t)d->batch * d->out_ch;
@@ -979,24 +1034,32 @@ int conv_impl(const corm_conv_desc* d, const corm::PostOp& post, cudaStream_t st
           cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
           corm_launch_pdl(kern, dim3(grid), dim3(threads), smem, st, a, q);
         };
-        const int pick = (NR == 2 ? 8 : 0) + (S == 2 ? 4 : 0) + (d->pad_left ? 2 : 0) + (rows ? 1 : 0);
+        const int pick = ((NR == 2 ? 1 : 0) * 12) + (S == 2 ? 6 : 0) + (d->pad_left ? 3 : 0) + ld;
         switch (pick) {
-          case 0: launch(conv_dw3x3<1, 0, false, 4>); break;
-          case 1: launch(conv_dw3x3<1, 0, true, 4>); break;
-          case 2: launch(conv_dw3x3<1, 1, false, 4>); break;
-          case 3: launch(conv_dw3x3<1, 1, true, 4>); break;
-          case 4: launch(conv_dw3x3<2, 0, false, 4>); break;
-          case 5: launch(conv_dw3x3<2, 0, true, 4>); break;
-          case 6: launch(conv_dw3x3<2, 1, false, 4>); break;
-          case 7: launch(conv_dw3x3<2, 1, true, 4>); break;
-          case 8: launch(conv_dw3x3<1, 0, false, 2>); break;
-          case 9: launch(conv_dw3x3<1, 0, true, 2>); break;
-          case 10: launch(conv_dw3x3<1, 1, false, 2>); break;
-          case 11: launch(conv_dw3x3<1, 1, true, 2>); break;
-          case 12: launch(conv_dw3x3<2, 0, false, 2>); break;
-          case 13: launch(conv_dw3x3<2, 0, true, 2>); break;
-          case 14: launch(conv_dw3x3<2, 1, false, 2>); break;
-          default: launch(conv_dw3x3<2, 1, true, 2>); break;
+          case 0: launch(conv_dw3x3<1, 0, 0, 4>); break;
+          case 1: launch(conv_dw3x3<1, 0, 1, 4>); break;
+          case 2: launch(conv_dw3x3<1, 0, 2, 4>); break;
+          case 3: launch(conv_dw3x3<1, 1, 0, 4>); break;
+          case 4: launch(conv_dw3x3<1, 1, 1, 4>); break;
+          case 5: launch(conv_dw3x3<1, 1, 2, 4>); break;
+          case 6: launch(conv_dw3x3<2, 0, 0, 4>); break;
+          case 7: launch(conv_dw3x3<2, 0, 1, 4>); break;
+          case 8: launch(conv_dw3x3<2, 0, 2, 4>); break;
+          case 9: launch(conv_dw3x3<2, 1, 0, 4>); break;
+          case 10: launch(conv_dw3x3<2, 1, 1, 4>); break;
+          case 11: launch(conv_dw3x3<2, 1, 2, 4>); break;
+          case 12: launch(conv_dw3x3<1, 0, 0, 2>); break;
+          case 13: launch(conv_dw3x3<1, 0, 1, 2>); break;
+          case 14: launch(conv_dw3x3<1, 0, 2, 2>); break;
+          case 15: launch(conv_dw3x3<1, 1, 0, 2>); break;
+          case 16: launch(conv_dw3x3<1, 1, 1, 2>); break;
+          case 17: launch(conv_dw3x3<1, 1, 2, 2>); break;
+          case 18: launch(conv_dw3x3<2, 0, 0, 2>); break;
+          case 19: launch(conv_dw3x3<2, 0, 1, 2>); break;
+          case 20: launch(conv_dw3x3<2, 0, 2, 2>); break;
+          case 21: launch(conv_dw3x3<2, 1, 0, 2>); break;
+          case 22: launch(conv_dw3x3<2, 1, 1, 2>); break;
+          default: launch(conv_dw3x3<2, 1, 2, 2>); break;
         }
         return corm::cuda_status("conv depthwise");
       }
