@@ -207,7 +207,8 @@ def main():
     ap.add_argument("--models", help="comma list of model cases to run (default: all)")
     ap.add_argument("--detail", help="write per-problem kernel times of one profiled step to this JSON file")
     ap.add_argument("--case", choices=["gemm", "gemm_small", "gemm_int16", "vectorop", "softmax", "softmax_col",
-                                       "layernorm", "rmsnorm32", "dwconv", "dwconv14", "pwconv", "maxpool", "conv",
+                                       "layernorm", "rmsnorm32", "dwconv", "dwconv14", "pwconv", "maxpool",
+                                       "addxnorm", "mulact", "conv",
                                        "llama_prefill", "llama_decode"],
                     help="run one job a few times (a small case for ncu captures) and exit")
     args = ap.parse_args()
@@ -1033,6 +1034,36 @@ def run_case(args):
         y = torch.empty(8192 * 16 * 14 * 14 + 8, dtype=torch.int16, device="cuda")
         fn = lambda: ops.pool(x, y, batch=8192, channels=16, in_h=28, in_w=28, out_h=14, out_w=14, pool_h=2,  # noqa
                               pool_w=2, stride_h=2, stride_w=2)
+    elif args.case == "addxnorm":
+        # a Llama layer's residual add + RMSNorm as one chain (the fused row
+        # pass), prefill-sized: 32768 rows of 960, the residual int32 at 2^-15
+        import numpy as np
+
+        from cormorant_b200 import rowops_host as RH
+        R_, n = 32768, 960
+        wx, bx = RH.resadd_job(15, np.full(n, 13), n)
+        wn, bn, g_, E = RH.rmsnorm_job(np.ones(n), 1e-5, 15, np.full(n, 12))
+        h = torch.randint(-(1 << 24), 1 << 24, (R_ * n,), dtype=torch.int32, device="cuda", generator=g)
+        d = ri(R_ * n)
+        h2 = torch.empty(R_ * n, dtype=torch.int32, device="cuda")
+        y = torch.empty(R_ * n + 8, dtype=torch.int16, device="cuda")
+        px = torch.from_numpy(np.asarray(wx, np.int16)).cuda()
+        pn = torch.from_numpy(np.asarray(wn, np.int16)).cuda()
+        jobs = [dict(a=h, b=d, c=h2, p=px, n=n, rows=R_, op=RH.opword(RH.OP_ADDX, RH.K_I32, RH.K_I16, RH.K_I32,
+                                                                       b_en=True, p_bcast=bool(bx)),
+                     a_s1=4 * n, b_s1=2 * n, c_s1=4 * n, win_hi=RH.NO_WINDOW),
+                dict(a=h2, c=y, p=pn, n=n, rows=R_, op=RH.opword(RH.OP_NORM, RH.K_I32, RH.K_I16, RH.K_I16,
+                                                                 p_bcast=bool(bn)),
+                     a_s1=4 * n, c_s1=2 * n, eps=int(E), win_hi=RH.NO_WINDOW)]
+        fn = lambda: ops.rowops_chain(jobs)  # noqa
+    elif args.case == "mulact":
+        # a Llama prefill layer's gate / up pair with SiLU(g) u in its epilogue:
+        # 32768 rows x 960 @ [960 x 2 x 2560], the output 32768 x 2560
+        R_, k, ffn = 32768, 960, 2560
+        A = ri(R_ * k)
+        W = ri(k * 2 * ffn, -64, 64)
+        y = torch.empty(R_ * ffn, dtype=torch.int16, device="cuda")
+        fn = lambda: ops.matmul_groups(A, W, [y], [ffn], n=R_, k=k, flags=1, mulact=(1, 23))  # noqa
     elif args.case in ("llama_prefill", "llama_decode"):
         # two layers of the config-5 model (every kernel of a layer, a layer's
         # shapes): the prefill of 16 sequences x 512 tokens, or after it one
