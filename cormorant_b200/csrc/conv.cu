@@ -986,13 +986,16 @@ int conv_impl(const corm_conv_desc* d, const corm::PostOp& post, cudaStream_t st
                      d->stride_h == d->stride_w && (d->stride_h == 1 || d->stride_h == 2);
     // 3 x 3 as runs of eight outputs over staged planes (left pad 0 or 1, 16-byte aligned x)
     if (dw3 && d->pad_left <= 1u && !((uintptr_t)d->x & 15u)) {
-      const uint32_t S = d->stride_h, NR = d->out_h <= 32u ? 2u : 4u;  // small planes: more runs per unit
+      // two output rows per run on small planes and at stride 2 (more runs per
+      // unit for the threads), four on large planes at stride 1
+      const uint32_t S = d->stride_h, NR = (d->out_h <= 32u || d->stride_h == 2) ? 2u : 4u;
       DwGeo q{};
       q.NRG = (d->out_h + NR - 1) / NR;
       q.RUNS = (d->out_w + 7u) / 8u;
       const uint32_t runs_in = (d->in_w + 7u) / 8u, HW = d->in_h * d->in_w;
       q.SHb = (q.NRG * NR - 1) * S + 3;
       q.SPW = std::max(runs_in + 2u, S == 1 ? q.RUNS + 2u : 2u * q.RUNS + 2u);
+      q.SPW |= 1u;  // an odd number of 16-byte words per row: the runs of a warp, on different rows, use different banks
       const bool rows = d->in_w % 8u == 0;
       // how the planes reach shared memory: 16-byte words of whole-word rows or
       // 4-byte pairs of even-width rows by cp.async (double-buffered), else
@@ -1010,11 +1013,11 @@ int conv_impl(const corm_conv_desc* d, const corm::PostOp& post, cudaStream_t st
         return u;
       };
       const uint32_t unit = std::max(ld == 0 ? align8(HW) : 1u, (!q.vst && dense) ? align8(P) : 1u);
-      // small planes: CTAs of two warps with units of about 10 KB (many CTAs per
+      // small planes: CTAs of two warps with units of about 16 KB (many CTAs per
       // SM, so one CTA's barriers never idle the SM); large planes: 8 warps, 36 KB
       const bool small = (size_t)q.SHb * q.SPW * 16u <= 4096u;
       const unsigned threads = small ? 64u : 256u;
-      const size_t target = small ? 10u * 1024u : 36u * 1024u;
+      const size_t target = small ? 16u * 1024u : 36u * 1024u;
       const size_t plane_b = nbuf * ((size_t)q.SHb * q.SPW * 16u + 40u) + (q.vst ? 0u : (size_t)P * 2u);
       uint32_t G = (uint32_t)std::min<size_t>(kDw3MaxG, std::max<size_t>(1, target / plane_b));
       G = std::max(unit, G / unit * unit);

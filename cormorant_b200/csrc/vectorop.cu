@@ -266,19 +266,37 @@ __global__ void __launch_bounds__(GROUP >= 256 ? GROUP : 256) smx_rows(SmxArgs p
   const uint64_t rnd = 1ull << (39u - p.fp);
   const uint32_t psh = 40u - p.fp;
   const uint32_t ngroups = (p.rows + ROWS_PER_CTA - 1) / ROWS_PER_CTA;
+  // the next row's whole 16-byte words are loaded while this row is worked
+  // (their loads stay in flight across the iteration)
+  int4 xn[V];
+  auto prefetch = [&](uint32_t rgn) {
+    const uint32_t rown = rgn * ROWS_PER_CTA + group;
+    const int16_t* xr = p.a + (size_t)rown * p.a_inc;
+    const bool ok = rgn < ngroups && rown < p.rows && ((uintptr_t)xr & 15) == 0;
+#pragma unroll
+    for (int q = 0; q < V; q++) {
+      const uint32_t j0 = (q * GROUP + lane_in_group) * 8;
+      if (ok && j0 + 8 <= p.size) xn[q] = __ldg((const int4*)(xr + j0));
+    }
+  };
+  prefetch(blockIdx.x);
   for (uint32_t rg = blockIdx.x; rg < ngroups; rg += gridDim.x) {
     const uint32_t row = rg * ROWS_PER_CTA + group;
     const bool live = row < p.rows;
     const uint32_t v = live ? smx_valid(row, p) : 0u;
     const int16_t* x = p.a + (size_t)row * p.a_inc;
     const bool xa = ((uintptr_t)x & 15) == 0;
+    int4 xc[V];
+#pragma unroll
+    for (int q = 0; q < V; q++) xc[q] = xn[q];
+    prefetch(rg + gridDim.x);
     uint32_t xp[PER / 2];  // packed pairs; masked elements hold INT16_MIN
     uint32_t mx = 0x80008000u;
 #pragma unroll
     for (int q = 0; q < V; q++) {
       const uint32_t j0 = (q * GROUP + lane_in_group) * 8;
-      if (live && xa && j0 + 8 <= v) {
-        const int4 w = __ldg((const int4*)(x + j0));
+      if (live && xa && j0 + 8 <= v) {  // (v <= size: the word was prefetched)
+        const int4 w = xc[q];
         xp[4 * q] = (uint32_t)w.x;
         xp[4 * q + 1] = (uint32_t)w.y;
         xp[4 * q + 2] = (uint32_t)w.z;
