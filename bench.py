@@ -47,7 +47,7 @@ BATCHES = (1, 16)
 
 
 # the timed sweep runs the jobs of at most SMALL_MACS MACs concurrently on LANES streams
-SMALL_MACS = 1 << 29
+SMALL_MACS = 1 << 31
 LANES = 4
 
 
@@ -412,7 +412,7 @@ def main():
                                    "N{32,256,1024,4096} x batch{1,16}", "problems": len(problems),
                        "gmac_per_step_per_gpu": round(macs_step / 1e9, 3), "parallelism": f"dp{world} (replicas)",
                        "l2": "256 MB flush between steps; 7.6 GB of distinct operands per step",
-                       "launch": "CUDA graph replay of the sweep: the %d jobs of at most 2^29 MACs first, spread "
+                       "launch": "CUDA graph replay of the sweep: the %d jobs of at most 2^31 MACs first, spread "
                                  "over %d streams, then the other %d in order" % (len(small), LANES, len(large))},
             "gpu_launches": int(launches_per_step * args.steps),
             "roofline": {"bound": "tensor", "kernel": "gemm_i8x4_kernel", "achieved": round(achieved, 1) if achieved else None,
