@@ -1066,11 +1066,12 @@ def run_case(args):
         fn = lambda: ops.matmul_groups(A, W, [y], [ffn], n=R_, k=k, flags=1, mulact=(1, 23))  # noqa
     elif args.case in ("llama_prefill", "llama_decode"):
         # two layers of the config-5 model (every kernel of a layer, a layer's
-        # shapes): the prefill of 16 sequences x 512 tokens, or after it one
-        # decode step of the 16 (lean passes, as the bench runs them)
+        # shapes): the prefill of 16 sequences x 512 tokens, or the prefill of
+        # 64 and after it one decode step of the 64 (the decode bench's batch;
+        # lean passes, as the bench runs them)
         from cormorant_b200 import workloads as WL
         from cormorant_b200.llm_runner import LlamaRunner
-        m = WL.LlamaModel(seed=5, batch=16, seq=512, layers=2)
+        m = WL.LlamaModel(seed=5, batch=64 if args.case == "llama_decode" else 16, seq=512, layers=2)
         r = LlamaRunner(m)
         lg = r.prefill()
         fn = (lambda: r.prefill()) if args.case == "llama_prefill" else (lambda: r.decode_step(lg, 0))  # noqa

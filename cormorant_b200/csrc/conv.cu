@@ -926,6 +926,13 @@ extern "C" int corm_conv_workspace_size(const corm_conv_desc* d, size_t* bytes) 
   if (int rc = validate(d)) return rc;
   if (!bytes) return corm::fail(CORM_EINVAL, "corm_conv_workspace_size: null output");
   *bytes = plan_of(d).bytes;
+  // a 1 x 1 conv that may run as the per-image GEMM W x[n] (its K-split
+  // partial sums; whether it does depends on the operands' alignment and the
+  // fused job, which the size query does not see)
+  if (!d->is_depthwise && d->kh == 1 && d->kw == 1) {
+    const size_t pb = corm::gemm_partial_bytes(d->out_ch, d->out_h * d->out_w, (d->in_ch + 15u) / 16u * 16u, d->batch);
+    if (pb > *bytes) *bytes = pb;
+  }
   return CORM_OK;
 }
 

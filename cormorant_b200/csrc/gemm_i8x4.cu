@@ -893,6 +893,27 @@ __global__ void __launch_bounds__(256) gemm_finish_kernel(const EpiArgs ep) {
   corm_pdl_wait();
   corm_pdl_trigger();
   const uint64_t total = (uint64_t)ep.batch * ep.rows * ep.cols;
+  if (ep.mulact) {
+    // gate / up pairs (no bias, row-major): output column oc of a row reads
+    // gate column 32 (oc / 16) + oc % 16 and the up column 16 after it
+    const uint32_t half = ep.cols / 2;
+    const uint64_t nout = (uint64_t)ep.batch * ep.rows * half;
+    for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < nout; i += (uint64_t)gridDim.x * blockDim.x) {
+      const uint32_t oc = (uint32_t)(i % half);
+      const uint64_t br = i / half;
+      const uint32_t r = (uint32_t)(br % ep.rows), bz = (uint32_t)(br / ep.rows);
+      const uint64_t cg = br * ep.cols + 32u * (oc / 16u) + oc % 16u;
+      unsigned long long sg = 0, su = 0;
+      for (uint32_t sp = 0; sp < ep.splits; sp++) {
+        sg += __ldg(ep.partial + sp * total + cg);
+        su += __ldg(ep.partial + sp * total + cg + 16u);
+      }
+      const int16_t g = finish((int64_t)sg, ep.flags), u = finish((int64_t)su, ep.flags);
+      ep.out[(uint64_t)bz * ep.out_batch_stride + (uint64_t)r * ep.ldc + oc] =
+          corm_mulact(g, u, ep.ma_sa, ep.ma_sc, ep.sig);
+    }
+    return;
+  }
   for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (uint64_t)gridDim.x * blockDim.x) {
     const uint32_t c = (uint32_t)(i % ep.cols);
     const uint64_t br = i / ep.cols;
@@ -1019,6 +1040,9 @@ Split split_of(uint32_t rows, uint32_t cols, uint32_t Kp, uint32_t batch) {
   // and a rounding pass over the whole output, which only pay for themselves
   // when the serial K walk is long and the grid is far from full (splitting
   // 8 K blocks, or 128 tiles of K 4096 three ways, measured slower).
+  // (Splitting the 8 K blocks of a decode step's 64-row projections too, to
+  // one or two blocks a unit, measured slower: 8 layers of the decode step
+  // 0.91 ms unsplit, 1.01 to 1.05 ms split 2, 4 or 8 ways.)
   if (s.tiles * 2 <= (uint32_t)NUM_SMS && s.num_kb >= 12) {
     uint32_t want = (2 * NUM_SMS + s.tiles - 1) / s.tiles;
     s.splits = want < s.num_kb / 4 ? want : s.num_kb / 4;
@@ -1118,11 +1142,7 @@ int gemm_i8x4(const GemmJob& j, cudaStream_t stream) {
       ok = ok && make_map(&m_bhi, j.b_hi, j.Kp, j.cols, j.b_planes) && make_map(&m_blo, j.b_lo, j.Kp, j.cols, j.b_planes);
     if (!ok) return fail(CORM_ECUDA, "gemm: cuTensorMapEncodeTiled failed");
   }
-  Split sp = split_of(j.rows, j.cols, j.Kp, j.batch);
-  if (j.mulact) {  // gate / up pairs: one K walk per tile (the split's finish has no MULACT)
-    sp.splits = 1;
-    sp.kps = sp.num_kb;
-  }
+  const Split sp = split_of(j.rows, j.cols, j.Kp, j.batch);
   EpiArgs ep{};
   ep.mode = j.mode;
   ep.out = j.out;
@@ -1233,8 +1253,8 @@ int gemm_i8x4(const GemmJob& j, cudaStream_t stream) {
   if (sp.splits > 1) {
     {
       ProfScope prof_("gemm_finish_kernel", stream);
-      corm_launch_pdl(gemm_finish_kernel, dim3(corm_blocks((uint64_t)j.batch * j.rows * j.cols, 256)), dim3(256), 0,
-                      stream, ep);
+      const uint64_t nout = (uint64_t)j.batch * j.rows * (j.mulact ? j.cols / 2 : j.cols);
+      corm_launch_pdl(gemm_finish_kernel, dim3(corm_blocks(nout, 256)), dim3(256), 0, stream, ep);
     }
     return cuda_status("gemm_finish");
   }

@@ -186,13 +186,22 @@ __device__ __forceinline__ int16_t kernel_out16(long long acc) {
   return (int16_t)(y > 32767 ? 32767 : (y < -32768 ? -32768 : y));
 }
 
-template <int G>
-__global__ void __launch_bounds__(256) decode_attn_kernel(corm_llm_decode_attn_desc d, uint32_t n, uint32_t nk,
+// HDT: the head dimension at compile time (64), or 0 (d.HD at run time).
+// With HDT a key's K row is one straight run of 16-byte loads (all in flight
+// at once).  Every form loads its first V rows of the P.V before the softmax,
+// so that their latency hides under the softmax's serial float64 sum.  At
+// most 3 heads a group: three CTAs an SM (80 registers), so that a decode
+// step's (sequence, group) CTAs (64 x 5 for the 360M shape) run in one wave.
+// (Holding a thread's first two K rows in registers across the AttnPrep
+// needs 110 registers, two CTAs an SM, two waves: 8 decode layers 1.00
+// against 0.93 ms.)
+template <int G, int HDT>
+__global__ void __launch_bounds__(256, G <= 3 ? 3 : 2) decode_attn_kernel(corm_llm_decode_attn_desc d, uint32_t n, uint32_t nk,
                                                           uint32_t j0) {
   corm_pdl_wait();
   corm_pdl_trigger();
   extern __shared__ __align__(16) uint8_t da_sm[];
-  const uint32_t HD = d.HD, C = d.C;
+  const uint32_t HD = HDT ? (uint32_t)HDT : d.HD, C = d.C;
   const uint32_t b = blockIdx.x % d.B, g = blockIdx.x / d.B;
   const uint32_t span = nk - j0;                       // keys the softmax reads
   double* e = (double*)da_sm;                          // [G][span]
@@ -204,6 +213,14 @@ __global__ void __launch_bounds__(256) decode_attn_kernel(corm_llm_decode_attn_d
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   int16_t* Kw = d.kc + ((uint64_t)g * d.B + b) * C * HD;
   int16_t* Vw = d.vc + ((uint64_t)g * d.B + b) * C * HD;
+  const uint32_t ut = (uint32_t)tid;
+  constexpr int NW = HDT ? HDT / 8 : 1;  // 16-byte words of a K row
+  int4 kA[NW];  // HDT: the K row of the key being scored
+  auto load_k = [&](int4 (&w)[NW], uint32_t jj) {
+    const int4* kr = (const int4*)(Kw + (uint64_t)(j0 + jj) * HD);
+#pragma unroll
+    for (int i = 0; i < NW; i++) w[i] = kr[i];
+  };
   if (d.prep & 1u) {
     // the step's AttnPrep: RoPE of this group's k row and of its G q heads (the
     // cos / sin row of pos), v re-rounded, the new cache rows written
@@ -260,25 +277,59 @@ __global__ void __launch_bounds__(256) decode_attn_kernel(corm_llm_decode_attn_d
     return;
   }
   // scores of the keys j0 .. nk - 1: a thread per key, the K row in 16-byte words
-#pragma unroll 2
-  for (uint32_t jj = tid; jj < span; jj += blockDim.x) {
-    const int16_t* kr = K + (uint64_t)(j0 + jj) * HD;
+  auto score_row = [&](const int4* kw, uint32_t jj) {
     // the sums modulo 2^32: the rule wraps the accumulator to int32 first
     uint32_t acc[G];
 #pragma unroll
     for (int h = 0; h < G; h++) acc[h] = 0;
-    for (uint32_t d0 = 0; d0 < HD; d0 += 8) {
-      const int4 w = *(const int4*)(kr + d0);
-      const int16_t* kv = (const int16_t*)&w;
+#pragma unroll
+    for (int i = 0; i < NW; i++) {
+      const int16_t* kv = (const int16_t*)&kw[i];
 #pragma unroll
       for (int e8 = 0; e8 < 8; e8++)
 #pragma unroll
-        for (int h = 0; h < G; h++) acc[h] += (uint32_t)(kv[e8] * q[(d0 + e8) * G + h]);
+        for (int h = 0; h < G; h++) acc[h] += (uint32_t)(kv[e8] * q[(8 * i + e8) * G + h]);
     }
 #pragma unroll
     for (int h = 0; h < G; h++) S[h * span + jj] = kernel_out16((long long)(int32_t)acc[h]);
+  };
+  if (HDT) {
+    for (uint32_t jj = ut; jj < span; jj += blockDim.x) {
+      load_k(kA, jj);
+      score_row(kA, jj);
+    }
+  } else {
+#pragma unroll 2
+    for (uint32_t jj = tid; jj < span; jj += blockDim.x) {
+      const int16_t* kr = K + (uint64_t)(j0 + jj) * HD;
+      uint32_t acc[G];
+#pragma unroll
+      for (int h = 0; h < G; h++) acc[h] = 0;
+      for (uint32_t d0 = 0; d0 < HD; d0 += 8) {
+        const int4 w = *(const int4*)(kr + d0);
+        const int16_t* kv = (const int16_t*)&w;
+#pragma unroll
+        for (int e8 = 0; e8 < 8; e8++)
+#pragma unroll
+          for (int h = 0; h < G; h++) acc[h] += (uint32_t)(kv[e8] * q[(d0 + e8) * G + h]);
+      }
+#pragma unroll
+      for (int h = 0; h < G; h++) S[h * span + jj] = kernel_out16((long long)(int32_t)acc[h]);
+    }
   }
   __syncthreads();
+  // P.V layout (below): a thread per 8 columns (one 16-byte V load per key)
+  // and key group (256 / (HD / 8) groups, each taking every groups-th key).
+  // The first VU keys of this thread's group are loaded now, in flight across
+  // the softmax (plain loads: this launch wrote the row at pos, the prep above)
+  constexpr int VU = 8;
+  const uint32_t c8n = HD / 8, groups = blockDim.x / c8n, c8 = tid % c8n, kg = tid / c8n;
+  int4 vv[VU];
+#pragma unroll
+  for (int u = 0; u < VU; u++) {
+    const uint32_t jj = kg + u * groups;
+    vv[u] = (kg < groups && jj < span) ? *(const int4*)(V + (uint64_t)(j0 + jj) * HD + c8 * 8) : make_int4(0, 0, 0, 0);
+  }
   // per head: the max (every head in one pass), e for every head in one loop
   // (the table lookups of all heads in flight together), the sum left to right
   // (one thread per head), P
@@ -323,26 +374,24 @@ __global__ void __launch_bounds__(256) decode_attn_kernel(corm_llm_decode_attn_d
     S[i] = (int16_t)(qv > 32767.0 ? 32767.0 : qv);  // P replaces the scores
   }
   __syncthreads();
-  // P.V: a thread per 8 columns (one 16-byte V load per key) and key group
-  // (256 / (HD / 8) groups, each taking every groups-th key), sums modulo 2^32
-  // (the rule wraps to int32), the groups reduced in shared memory per head
-  const uint32_t c8n = HD / 8, groups = blockDim.x / c8n, c8 = tid % c8n, kg = tid / c8n;
+  // P.V: sums modulo 2^32 (the rule wraps to int32), the key groups reduced
+  // in shared memory per head; VU rows in flight per thread
   uint32_t acc[G][8];
 #pragma unroll
   for (int h = 0; h < G; h++)
 #pragma unroll
     for (int e8 = 0; e8 < 8; e8++) acc[h][e8] = 0;
   if (kg < groups)
-    for (uint32_t base = kg; base < span; base += 4u * groups) {  // 4 rows in flight per thread
-      int4 vv[4];
+    for (uint32_t base = kg; base < span; base += (uint32_t)VU * groups) {
+      if (base != kg) {  // (the first rows were loaded before the softmax)
 #pragma unroll
-      for (int u = 0; u < 4; u++) {
-        const uint32_t jj = base + u * groups;
-        // plain loads: this launch wrote the row at pos (the prep above)
-        vv[u] = jj < span ? *(const int4*)(V + (uint64_t)(j0 + jj) * HD + c8 * 8) : make_int4(0, 0, 0, 0);
+        for (int u = 0; u < VU; u++) {
+          const uint32_t jj = base + u * groups;
+          vv[u] = jj < span ? *(const int4*)(V + (uint64_t)(j0 + jj) * HD + c8 * 8) : make_int4(0, 0, 0, 0);
+        }
       }
 #pragma unroll
-      for (int u = 0; u < 4; u++) {
+      for (int u = 0; u < VU; u++) {
         const uint32_t jj = base + u * groups;
         if (jj < span) {
           const int16_t* v8 = (const int16_t*)&vv[u];
@@ -401,15 +450,28 @@ extern "C" int corm_llm_decode_attn(const corm_llm_decode_attn_desc* d, corm_str
   };
   {
     corm::ProfScope prof_("decode_attn_kernel", st);
-    switch (d->G) {
-      case 1: launch(decode_attn_kernel<1>); break;
-      case 2: launch(decode_attn_kernel<2>); break;
-      case 3: launch(decode_attn_kernel<3>); break;
-      case 4: launch(decode_attn_kernel<4>); break;
-      case 5: launch(decode_attn_kernel<5>); break;
-      case 6: launch(decode_attn_kernel<6>); break;
-      case 7: launch(decode_attn_kernel<7>); break;
-      default: launch(decode_attn_kernel<8>); break;
+    if (d->HD == 64) {
+      switch (d->G) {
+        case 1: launch(decode_attn_kernel<1, 64>); break;
+        case 2: launch(decode_attn_kernel<2, 64>); break;
+        case 3: launch(decode_attn_kernel<3, 64>); break;
+        case 4: launch(decode_attn_kernel<4, 64>); break;
+        case 5: launch(decode_attn_kernel<5, 64>); break;
+        case 6: launch(decode_attn_kernel<6, 64>); break;
+        case 7: launch(decode_attn_kernel<7, 64>); break;
+        default: launch(decode_attn_kernel<8, 64>); break;
+      }
+    } else {
+      switch (d->G) {
+        case 1: launch(decode_attn_kernel<1, 0>); break;
+        case 2: launch(decode_attn_kernel<2, 0>); break;
+        case 3: launch(decode_attn_kernel<3, 0>); break;
+        case 4: launch(decode_attn_kernel<4, 0>); break;
+        case 5: launch(decode_attn_kernel<5, 0>); break;
+        case 6: launch(decode_attn_kernel<6, 0>); break;
+        case 7: launch(decode_attn_kernel<7, 0>); break;
+        default: launch(decode_attn_kernel<8, 0>); break;
+      }
     }
   }
   return corm::cuda_status("llm_decode_attn");

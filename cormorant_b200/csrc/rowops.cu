@@ -425,7 +425,12 @@ __device__ __noinline__ int64_t norm_out128(long long P1, int64_t g, int32_t bq,
 // (int32) plus its B (int16), any entries, no SCALE, every row in the window —
 // and written to x's C, which is this job's A (a residual add followed by the
 // RMSNorm of the sum: one pass over the rows instead of two).
-template <int NW_PER, int AK, bool PRE = false>
+// WPR warps per row (1 or 8): with few rows (a decode step's 64) a row's
+// words are spread over WPR warps of one block, whose partial sums meet in
+// shared memory; every warp of the block then forms the row's divisor and
+// writes its own words.  The blocks walk their rows in whole passes (every
+// warp takes each barrier).
+template <int NW_PER, int AK, bool PRE = false, int WPR = 1>
 __global__ void __launch_bounds__(256, 2) ro_norm16(RoArgs q, RoArgs x) {
   corm_pdl_wait();
   if (PRE) {  // the two loads in order: the ADDX job's entries, then this job's
@@ -493,14 +498,17 @@ __global__ void __launch_bounds__(256, 2) ro_norm16(RoArgs q, RoArgs x) {
   const bool small_bq = q.bq_sh <= 40u;
   const int lane = threadIdx.x & 31;
   const uint64_t rows = (uint64_t)q.c1 * q.c2;
-  const uint64_t warp0 = ((uint64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-  const uint64_t nwarps = ((uint64_t)gridDim.x * blockDim.x) >> 5;
+  constexpr uint32_t RPB = 8u / WPR;  // rows of a block per pass (256 threads)
+  const uint32_t wib = threadIdx.x >> 5, wr = wib % WPR;
+  const uint32_t lw = wr * 32u + (uint32_t)lane;  // this lane's first word of the row
+  const uint64_t warp0 = (uint64_t)blockIdx.x * RPB + wib / WPR;
+  const uint64_t nwarps = (uint64_t)gridDim.x * RPB;
   auto row_in = [&](uint64_t row) {
     return q.a + (uint64_t)(uint32_t)(row / q.c1) * q.a_s2 + (uint64_t)(uint32_t)(row % q.c1) * q.a_s1;
   };
   // the next row of this warp is loaded while the current one is reduced and
   // written (its loads stay in flight across the iteration)
-  constexpr bool PF = NW_PER <= 8 && !PRE;  // (16 words per lane: no registers to spare for a second row)
+  constexpr bool PF = NW_PER <= 8 && !PRE && WPR == 1;  // (16 words per lane: no registers to spare for a second row)
   int4 xn[NW_PER];
   if (PF && warp0 < rows) {
     const uint8_t* ra = row_in(warp0);
@@ -510,7 +518,15 @@ __global__ void __launch_bounds__(256, 2) ro_norm16(RoArgs q, RoArgs x) {
       xn[k] = w < words ? *(const int4*)(ra + 16ull * w) : make_int4(0, 0, 0, 0);
     }
   }
-  for (uint64_t row = warp0; row < rows; row += nwarps) {
+  // WPR > 1: the partial sums of the block's warps
+  __shared__ long long s_p1[WPR > 1 ? 8 : 1];
+  __shared__ unsigned long long s_plo[WPR > 1 ? 8 : 1], s_phi[WPR > 1 ? 8 : 1];
+  __shared__ int32_t s_pmax[WPR > 1 ? 8 : 1], s_pmin[WPR > 1 ? 8 : 1];
+  // whole passes: a block leaves when the first row of its pass is past the end
+  const uint64_t row_end = WPR > 1 ? rows + (wib / WPR) : rows;
+  for (uint64_t row = warp0; row < row_end; row += nwarps) {
+    const bool act = WPR == 1 || row < rows;
+    const uint32_t wl = act ? words : 0u;  // words of this row (none past the end)
     const uint32_t i1 = (uint32_t)(row % q.c1), i2 = (uint32_t)(row / q.c1);
     uint8_t* rc = q.c + (uint64_t)i2 * q.c_s2 + (uint64_t)i1 * q.c_s1;
     int4 xv[NW_PER];
@@ -521,8 +537,8 @@ __global__ void __launch_bounds__(256, 2) ro_norm16(RoArgs q, RoArgs x) {
         const uint8_t* rn = row_in(row + nwarps);
 #pragma unroll
         for (int k = 0; k < NW_PER; k++) {
-          const uint32_t w = lane + 32u * k;
-          if (w < words) xn[k] = *(const int4*)(rn + 16ull * w);
+          const uint32_t w = lw + 32u * WPR * k;
+          if (w < wl) xn[k] = *(const int4*)(rn + 16ull * w);
         }
       }
     } else if (PRE) {
@@ -534,17 +550,17 @@ __global__ void __launch_bounds__(256, 2) ro_norm16(RoArgs q, RoArgs x) {
       int2 bv[NW_PER];
 #pragma unroll
       for (int k = 0; k < NW_PER; k++) {
-        const uint32_t w = lane + 32u * k;
-        if (w < words) {
+        const uint32_t w = lw + 32u * WPR * k;
+        if (w < wl) {
           av[k] = *(const int4*)(xa + 16ull * w);
           bv[k] = *(const int2*)(xb + 8ull * w);
         }
       }
 #pragma unroll
       for (int k = 0; k < NW_PER; k++) {
-        const uint32_t w = lane + 32u * k;
+        const uint32_t w = lw + 32u * WPR * k;
         xv[k] = make_int4(0, 0, 0, 0);
-        if (w >= words) continue;
+        if (w >= wl) continue;
         const int32_t ai[4] = {av[k].x, av[k].y, av[k].z, av[k].w};
         const int32_t bi[4] = {(int32_t)(bv[k].x << 16) >> 16, bv[k].x >> 16, (int32_t)(bv[k].y << 16) >> 16,
                                bv[k].y >> 16};
@@ -570,8 +586,8 @@ __global__ void __launch_bounds__(256, 2) ro_norm16(RoArgs q, RoArgs x) {
       const uint8_t* ra = row_in(row);
 #pragma unroll
       for (int k = 0; k < NW_PER; k++) {
-        const uint32_t w = lane + 32u * k;
-        xv[k] = w < words ? *(const int4*)(ra + 16ull * w) : make_int4(0, 0, 0, 0);
+        const uint32_t w = lw + 32u * WPR * k;
+        xv[k] = w < wl ? *(const int4*)(ra + 16ull * w) : make_int4(0, 0, 0, 0);
       }
     }
     long long s1 = 0;
@@ -580,8 +596,8 @@ __global__ void __launch_bounds__(256, 2) ro_norm16(RoArgs q, RoArgs x) {
     unsigned __int128 s2w = 0;  // int32 rows: squares up to 2^62
 #pragma unroll
     for (int k = 0; k < NW_PER; k++) {
-      const uint32_t w = lane + 32u * k;
-      if (w < words) {
+      const uint32_t w = lw + 32u * WPR * k;
+      if (w < wl) {
         if (AK) {
 #pragma unroll
           for (int e = 0; e < (int)EPW; e++) {
@@ -629,6 +645,29 @@ __global__ void __launch_bounds__(256, 2) ro_norm16(RoArgs q, RoArgs x) {
       xmax = max(xmax, __shfl_xor_sync(0xffffffffu, xmax, o));
       xmin = min(xmin, __shfl_xor_sync(0xffffffffu, xmin, o));
     }
+    if (WPR > 1) {  // the row's WPR warps: their partial sums in shared memory, combined by each
+      if (lane == 0) {
+        s_p1[wib] = s1;
+        s_plo[wib] = lo;
+        s_phi[wib] = hi;
+        s_pmax[wib] = xmax;
+        s_pmin[wib] = xmin;
+      }
+      __syncthreads();
+      const uint32_t g0 = wib - wr;
+      s1 = 0;
+      lo = hi = 0;
+#pragma unroll
+      for (int i = 0; i < WPR; i++) {
+        s1 += s_p1[g0 + i];
+        const unsigned long long sum = lo + s_plo[g0 + i];
+        hi += s_phi[g0 + i] + (sum < lo ? 1ull : 0ull);
+        lo = sum;
+        xmax = max(xmax, s_pmax[g0 + i]);
+        xmin = min(xmin, s_pmin[g0 + i]);
+      }
+      __syncthreads();  // (the next pass writes the slots again)
+    }
     const __int128 S2 = (__int128)(((unsigned __int128)hi << 64) | lo);
     __int128 D = ln ? ((__int128)q.n * S2 - (__int128)s1 * s1 + (__int128)q.eps) : (S2 + (__int128)q.eps);
     if (D <= 0) D = 1;
@@ -647,8 +686,8 @@ __global__ void __launch_bounds__(256, 2) ro_norm16(RoArgs q, RoArgs x) {
     const long long alpha = nn * (long long)Rm, beta = off * (long long)Rm;
 #pragma unroll
     for (int k = 0; k < NW_PER; k++) {
-      const uint32_t w = lane + 32u * k;
-      if (w >= words) continue;
+      const uint32_t w = lw + 32u * WPR * k;
+      if (w >= wl) continue;
       int16_t os[EPW];
       if (row_fast) {
 #pragma unroll
@@ -941,6 +980,7 @@ int rowops_job(const corm_rowops_desc* d, cudaStream_t st);
 
 namespace {
 constexpr int kNotFused = 1;
+constexpr uint64_t kWideRows = 148u * 8u;  // norm jobs of fewer rows: ro_norm16 with 8 warps per row
 
 // x: ADDX of int32 rows (A) and int16 rows (B) into int32 rows (C), every row
 // in the window, no SCALE; y: the RMS NORM of x's C into int16 rows; n % 8 == 0,
@@ -998,16 +1038,25 @@ int rowops_addx_norm(const corm_rowops_desc* x, const corm_rowops_desc* y, cudaS
   const RoArgs qx = args(x), qy = args(y);
   const size_t npar = ((y->op >> 13) & 1u) ? 1u : y->n, xpar = ((x->op >> 13) & 1u) ? 1u : x->n;
   const size_t smem = ((npar * 13u + 15u) & ~(size_t)15u) + xpar * 7u + 16u;
-  const unsigned grid = corm_blocks(y->rows, 8, 148u * 4u);
+  // fewer rows than 148 blocks of 8: 8 warps per row
+  const bool wide = y->rows < kWideRows;
+  const unsigned grid = corm_blocks(y->rows, wide ? 1 : 8, 148u * 4u);
   corm::ProfScope prof_("ro_addx_norm32", st);
   auto launch = [&](auto kern) {
     if (smem > 48u * 1024u) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     corm_launch_pdl(kern, dim3(grid), dim3(256), smem, st, qy, qx);
   };
   const uint32_t words = y->n / 4u;
-  if (words <= 128) launch(ro_norm16<4, 1, true>);
-  else if (words <= 256) launch(ro_norm16<8, 1, true>);
-  else launch(ro_norm16<16, 1, true>);
+  if (wide) {
+    if (words <= 256) launch(ro_norm16<1, 1, true, 8>);
+    else launch(ro_norm16<2, 1, true, 8>);
+  } else if (words <= 128) {
+    launch(ro_norm16<4, 1, true>);
+  } else if (words <= 256) {
+    launch(ro_norm16<8, 1, true>);
+  } else {
+    launch(ro_norm16<16, 1, true>);
+  }
   return corm::cuda_status("rowops addx + norm");
 }
 }  // namespace
@@ -1221,7 +1270,8 @@ int rowops_job(const corm_rowops_desc* d0, cudaStream_t st) {
   if (op == 5 && d->n % 8 == 0 && ck == 0 && (ak == 0 || (ak == 1 && !ln && d->n <= 2048))) {
     {
       corm::ProfScope prof_(ak ? "ro_norm32" : "ro_norm16", st);
-      const unsigned grid = corm_blocks(rows, 8, 148u * 4u);
+      const bool wide = rows < kWideRows;
+      const unsigned grid = corm_blocks(rows, wide ? 1 : 8, 148u * 4u);
       const size_t npar = ((d->op >> 13) & 1u) ? 1u : d->n;
       const size_t smem = npar * 13u + 16u;  // n <= 4096: under 64 KB
       auto launch = [&](auto kern) {
@@ -1230,7 +1280,15 @@ int rowops_job(const corm_rowops_desc* d0, cudaStream_t st) {
       };
       // 16-byte words per row: n / 8 (int16) or n / 4 (int32, n <= 2048), <= 32 NW_PER
       const uint32_t words = ak ? d->n / 4u : d->n / 8u;
-      if (ak == 0) {
+      if (wide) {
+        if (ak == 0) {
+          if (words <= 256) launch(ro_norm16<1, 0, false, 8>);
+          else launch(ro_norm16<2, 0, false, 8>);
+        } else {
+          if (words <= 256) launch(ro_norm16<1, 1, false, 8>);
+          else launch(ro_norm16<2, 1, false, 8>);
+        }
+      } else if (ak == 0) {
         if (words <= 128) launch(ro_norm16<4, 0>);
         else if (words <= 256) launch(ro_norm16<8, 0>);
         else launch(ro_norm16<16, 0>);

@@ -474,17 +474,33 @@ __global__ void __launch_bounds__(256) smx_cols_t(SmxArgs p) {
     }
     const uint32_t vmax = min(p.size, p.valid0 + tmax);
     __syncthreads();  // the previous tile's reads (and the table) are done
-    for (uint32_t idx = threadIdx.x; idx < ((vmax + 1u) / 2u) * PARTS; idx += 256u) {
-      const uint32_t jp = idx / PARTS, part = idx % PARTS;
-      if (q0 + 8u * part >= p.rows) continue;
-      const int16_t* src = p.a + (size_t)(2u * jp) * p.a_inc + q0 + 8u * part;
-      const int4 w0 = __ldg((const int4*)src), w1 = __ldg((const int4*)(src + p.a_inc));
-      const int16_t* v0 = (const int16_t*)&w0;
-      const int16_t* v1 = (const int16_t*)&w1;
+    // SU pairs of key rows per thread in flight (their loads first, then the
+    // transposed stores)
+    constexpr uint32_t SU = 4;
+    const uint32_t nidx = ((vmax + 1u) / 2u) * PARTS;
+    for (uint32_t base = threadIdx.x; base < nidx; base += 256u * SU) {
+      int4 w0[SU], w1[SU];
 #pragma unroll
-      for (int e = 0; e < 8; e++) {
-        const uint32_t c = 8u * part + e;
-        *(uint32_t*)(s_x + smx_tbase(c, KP) + 2u * jp) = (uint32_t)(uint16_t)v0[e] | ((uint32_t)(uint16_t)v1[e] << 16);
+      for (uint32_t u = 0; u < SU; u++) {
+        const uint32_t idx = base + 256u * u, jp = idx / PARTS, part = idx % PARTS;
+        if (idx < nidx && q0 + 8u * part < p.rows) {
+          const int16_t* src = p.a + (size_t)(2u * jp) * p.a_inc + q0 + 8u * part;
+          w0[u] = __ldg((const int4*)src);
+          w1[u] = __ldg((const int4*)(src + p.a_inc));
+        }
+      }
+#pragma unroll
+      for (uint32_t u = 0; u < SU; u++) {
+        const uint32_t idx = base + 256u * u, jp = idx / PARTS, part = idx % PARTS;
+        if (idx >= nidx || q0 + 8u * part >= p.rows) continue;
+        const int16_t* v0 = (const int16_t*)&w0[u];
+        const int16_t* v1 = (const int16_t*)&w1[u];
+#pragma unroll
+        for (int e = 0; e < 8; e++) {
+          const uint32_t c = 8u * part + e;
+          *(uint32_t*)(s_x + smx_tbase(c, KP) + 2u * jp) =
+              (uint32_t)(uint16_t)v0[e] | ((uint32_t)(uint16_t)v1[e] << 16);
+        }
       }
     }
     __syncthreads();

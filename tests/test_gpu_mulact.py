@@ -3,8 +3,9 @@ one GEMM over the gate and up weights interleaved in 16-column blocks whose
 epilogue applies the row-ops MULACT (SiLU(g << sa) u rounded at sc) equals
 the two MatMuls followed by the MULACT job — on the split-plane form (many
 rows), the int16-operand form, the weight-planes form with 64 rows (MMAs of
-M = 64) and with more, with and without the int32 wrap, with the 64-bit
-(sa <= 23) and the 128-bit SiLU paths.  Bit-exact."""
+M = 64) and with more, a K-split job (the MULACTs in the finish pass), with
+and without the int32 wrap, with the 64-bit (sa <= 23) and the 128-bit SiLU
+paths.  Bit-exact."""
 import numpy as np
 import pytest
 
@@ -29,8 +30,8 @@ def _entry(sa, sc):
 
 @pytest.mark.parametrize("case", [(2048, 256, 512, 0, 14, 22, "groups"), (300, 96, 160, 1, 10, 24, "groups"),
                                   (64, 960, 2560, 1, 1, 23, "bplanes"), (200, 128, 96, 0, 30, 35, "bplanes"),
-                                  (7, 64, 64, 0, 2, 20, "bplanes")],
-                         ids=["planes", "int16", "bplanes_m64", "bplanes_slow", "bplanes_7rows"])
+                                  (7, 64, 64, 0, 2, 20, "bplanes"), (40, 2048, 256, 1, 28, 40, "groups")],
+                         ids=["planes", "int16", "bplanes_m64", "bplanes_slow", "bplanes_7rows", "int16_split"])
 def test_mulact_pairs(ops, case):
     from cormorant_b200 import rowops_host as RH
     n, k, ffn, wrap, sa, sc, form = case

@@ -95,7 +95,8 @@ def test_param_ram_chains(ops, seed):
 
 
 @pytest.mark.parametrize("case", [(960, 64, False, False, 0), (960, 48, True, True, 5), (256, 33, False, True, 40),
-                                  (2048, 9, True, False, 2)], ids=["llama", "bcast_relu", "n256_bq40", "n2048"])
+                                  (2048, 9, True, False, 2), (960, 1300, False, False, 0)],
+                         ids=["llama", "bcast_relu", "n256_bq40", "n2048", "rows1300"])
 def test_addx_norm_pairs(ops, case):
     """An ADDX of int32 rows and int16 rows into int32 rows followed by the RMS
     NORM of its output — the pair the library runs as one pass — against the job

@@ -151,6 +151,30 @@ def test_norm32_rms(ops, n, bcast, small):
     assert np.array_equal(got, want)
 
 
+@pytest.mark.parametrize("ak,ln,n", [(0, True, 768), (0, False, 1000), (1, False, 960)])
+def test_norm_many_rows(ops, ak, ln, n):
+    """NORM over 1200 rows (600 x 2 blocks): the warp-per-row form (the tests
+    above, with a handful of rows, take the form that spreads a row over the
+    8 warps of a block)."""
+    rng = np.random.default_rng(ak + 2 * ln + n)
+    rows, blocks = 600, 2
+    eb = 4 if ak else 2
+    a_s1 = eb * n + 16
+    a_s2 = a_s1 * rows
+    c_s1, c_s2 = 2 * n, 2 * n * rows + 32
+    p = _params(rng, n, False, g=(1, 1 << 30), bq=(-(1 << 21), 1 << 21), sc=(24, 46))
+    mem, offs = _image(rng, a_s2 * blocks, 16, p, c_s2 * blocks)
+    if ak:  # residual-like values on every other row
+        vals = rng.integers(-(1 << 20), 1 << 20, a_s1 // 4).astype("<i4").view(np.uint8)
+        for r in range(0, rows * blocks, 2):
+            mem[offs["a"] + r * a_s1:offs["a"] + (r + 1) * a_s1] = vals
+    op = 5 | (ak << 4) | (spec.F_NORM_LN if ln else 0)
+    regs = dict(op=op, n=n, rows=rows, blocks=blocks, a_s1=a_s1, a_s2=a_s2, c_s1=c_s1, c_s2=c_s2,
+                eps=int(rng.integers(0, 1 << 20)), bq_sh=int(rng.integers(0, 30)))
+    got, want = _run(ops, mem, offs, regs)
+    assert np.array_equal(got, want)
+
+
 KINDS = [(ak, bk, ck) for ak in (0, 1) for bk in (0, 1) for ck in (0, 1)]
 
 
