@@ -204,10 +204,10 @@ __global__ void __launch_bounds__(256, G <= 3 ? 3 : 2) decode_attn_kernel(corm_l
   const uint32_t HD = HDT ? (uint32_t)HDT : d.HD, C = d.C;
   const uint32_t b = blockIdx.x % d.B, g = blockIdx.x / d.B;
   const uint32_t span = nk - j0;                       // keys the softmax reads
-  double* e = (double*)da_sm;                          // [G][span]
+  int32_t* q = (int32_t*)da_sm;                        // [HD][G] (16-byte aligned: HD G 4 % 32 == 0)
+  double* e = (double*)(q + HD * G);                   // [G][span]
   double* sums = e + (size_t)G * span;                 // [G]
-  int32_t* q = (int32_t*)(sums + G);                   // [HD][G]
-  int16_t* S = (int16_t*)(q + HD * G);                 // [G][span] scores, then P
+  int16_t* S = (int16_t*)(sums + G);                   // [G][span] scores, then P
   __shared__ int32_t s_max[8][8];
   __shared__ long long s_acc[1024];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -276,27 +276,39 @@ __global__ void __launch_bounds__(256, G <= 3 ? 3 : 2) decode_attn_kernel(corm_l
     for (uint32_t i = tid; i < G * HD; i += blockDim.x) out[i] = 0;
     return;
   }
-  // scores of the keys j0 .. nk - 1: a thread per key, the K row in 16-byte words
-  auto score_row = [&](const int4* kw, uint32_t jj) {
-    // the sums modulo 2^32: the rule wraps the accumulator to int32 first
-    uint32_t acc[G];
+  // scores of the keys j0 .. nk - 1: a thread per key, the K row in 16-byte
+  // words, each head's running maximum kept on the way
+  int32_t mh[G];
 #pragma unroll
-    for (int h = 0; h < G; h++) acc[h] = 0;
+  for (int h = 0; h < G; h++) mh[h] = INT32_MIN;
+  auto put_scores = [&](const uint32_t* acc, uint32_t jj) {
 #pragma unroll
-    for (int i = 0; i < NW; i++) {
-      const int16_t* kv = (const int16_t*)&kw[i];
-#pragma unroll
-      for (int e8 = 0; e8 < 8; e8++)
-#pragma unroll
-        for (int h = 0; h < G; h++) acc[h] += (uint32_t)(kv[e8] * q[(8 * i + e8) * G + h]);
+    for (int h = 0; h < G; h++) {
+      const int16_t sc = kernel_out16((long long)(int32_t)acc[h]);
+      S[h * span + jj] = sc;
+      mh[h] = max(mh[h], (int32_t)sc);
     }
-#pragma unroll
-    for (int h = 0; h < G; h++) S[h * span + jj] = kernel_out16((long long)(int32_t)acc[h]);
   };
   if (HDT) {
     for (uint32_t jj = ut; jj < span; jj += blockDim.x) {
       load_k(kA, jj);
-      score_row(kA, jj);
+      // the sums modulo 2^32: the rule wraps the accumulator to int32 first
+      uint32_t acc[G];
+#pragma unroll
+      for (int h = 0; h < G; h++) acc[h] = 0;
+#pragma unroll
+      for (int i = 0; i < NW; i++) {
+        const int16_t* kv = (const int16_t*)&kA[i];
+        int4 q4[2 * G];  // the q image of the word's 8 dimensions (8 G values)
+#pragma unroll
+        for (int t = 0; t < 2 * G; t++) q4[t] = ((const int4*)(q + 8 * i * G))[t];
+        const int32_t* qv = (const int32_t*)q4;
+#pragma unroll
+        for (int e8 = 0; e8 < 8; e8++)
+#pragma unroll
+          for (int h = 0; h < G; h++) acc[h] += (uint32_t)(kv[e8] * qv[e8 * G + h]);
+      }
+      put_scores(acc, jj);
     }
   } else {
 #pragma unroll 2
@@ -313,9 +325,14 @@ __global__ void __launch_bounds__(256, G <= 3 ? 3 : 2) decode_attn_kernel(corm_l
 #pragma unroll
           for (int h = 0; h < G; h++) acc[h] += (uint32_t)(kv[e8] * q[(d0 + e8) * G + h]);
       }
-#pragma unroll
-      for (int h = 0; h < G; h++) S[h * span + jj] = kernel_out16((long long)(int32_t)acc[h]);
+      put_scores(acc, jj);
     }
+  }
+#pragma unroll
+  for (int h = 0; h < G; h++) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mh[h] = max(mh[h], __shfl_xor_sync(0xffffffffu, mh[h], o));
+    if (lane == 0) s_max[h][warp] = mh[h];
   }
   __syncthreads();
   // P.V layout (below): a thread per 8 columns (one 16-byte V load per key)
@@ -330,35 +347,20 @@ __global__ void __launch_bounds__(256, G <= 3 ? 3 : 2) decode_attn_kernel(corm_l
     const uint32_t jj = kg + u * groups;
     vv[u] = (kg < groups && jj < span) ? *(const int4*)(V + (uint64_t)(j0 + jj) * HD + c8 * 8) : make_int4(0, 0, 0, 0);
   }
-  // per head: the max (every head in one pass), e for every head in one loop
-  // (the table lookups of all heads in flight together), the sum left to right
-  // (one thread per head), P
-  {
-    int32_t mh[G];
+  // per head: the maximum over the warps' maxima (every thread), e by the
+  // head's table (the lookups of a head in flight together), the sum left to
+  // right (one thread per head), P
 #pragma unroll
-    for (int h = 0; h < G; h++) mh[h] = INT32_MIN;
-    for (uint32_t jj = tid; jj < span; jj += blockDim.x)
-#pragma unroll
-      for (int h = 0; h < G; h++) mh[h] = max(mh[h], (int32_t)S[h * span + jj]);
-#pragma unroll
-    for (int h = 0; h < G; h++) {
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) mh[h] = max(mh[h], __shfl_xor_sync(0xffffffffu, mh[h], o));
-      if (lane == 0) s_max[h][warp] = mh[h];
-    }
+  for (int h = 0; h < G; h++) {
+    int32_t m = s_max[h][0];
+    for (int w = 1; w < (int)(blockDim.x >> 5); w++) m = max(m, s_max[h][w]);
+    mh[h] = m;
   }
-  __syncthreads();
-  if (tid < G) {
-    int32_t m = s_max[tid][0];
-    for (int w = 1; w < (int)(blockDim.x >> 5); w++) m = max(m, s_max[tid][w]);
-    s_max[tid][0] = m;
-  }
-  __syncthreads();
-#pragma unroll 4
-  for (uint32_t i = tid; i < (uint32_t)G * span; i += blockDim.x) {
-    const uint32_t h = i / span;
+#pragma unroll
+  for (int h = 0; h < G; h++) {
     const double* tab = d.tab + (uint64_t)(g * G + h) * 65536u;
-    e[i] = __ldg(tab + (s_max[h][0] - (int32_t)S[i]));
+#pragma unroll 4
+    for (uint32_t jj = ut; jj < span; jj += blockDim.x) e[h * span + jj] = __ldg(tab + (mh[h] - (int32_t)S[h * span + jj]));
   }
   __syncthreads();
   if (tid < G) {
@@ -368,10 +370,13 @@ __global__ void __launch_bounds__(256, G <= 3 ? 3 : 2) decode_attn_kernel(corm_l
     sums[tid] = sum;
   }
   __syncthreads();
-  for (uint32_t i = tid; i < G * span; i += blockDim.x) {
-    const uint32_t h = i / span;
-    const double qv = rint((e[i] / sums[h]) * d.ip[g * G + h]);
-    S[i] = (int16_t)(qv > 32767.0 ? 32767.0 : qv);  // P replaces the scores
+#pragma unroll
+  for (int h = 0; h < G; h++) {
+    const double sh = sums[h], iph = d.ip[g * G + h];
+    for (uint32_t jj = ut; jj < span; jj += blockDim.x) {
+      const double qv = rint((e[h * span + jj] / sh) * iph);
+      S[h * span + jj] = (int16_t)(qv > 32767.0 ? 32767.0 : qv);  // P replaces the scores
+    }
   }
   __syncthreads();
   // P.V: sums modulo 2^32 (the rule wraps to int32), the key groups reduced
@@ -404,19 +409,42 @@ __global__ void __launch_bounds__(256, G <= 3 ? 3 : 2) decode_attn_kernel(corm_l
         }
       }
     }
-  uint32_t* red = (uint32_t*)s_acc;  // [groups][HD]: groups * HD <= 2 blockDim.x * 4 = 2048
+  // the key groups of a warp (lanes of one column word c8: lane % c8n) by
+  // shuffles, then the 8 warps' sums through shared memory: every head at
+  // once when G HD <= 256 (8 KB), else head by head
 #pragma unroll
-  for (int h = 0; h < G; h++) {
-    if (kg < groups)
+  for (int h = 0; h < G; h++)
 #pragma unroll
-      for (int e8 = 0; e8 < 8; e8++) red[kg * HD + c8 * 8 + e8] = acc[h][e8];
+    for (int e8 = 0; e8 < 8; e8++)
+      for (uint32_t o = c8n; o < 32u; o <<= 1) acc[h][e8] += __shfl_xor_sync(0xffffffffu, acc[h][e8], o);
+  uint32_t* red = (uint32_t*)s_acc;  // [warp][columns of the pass], <= 2048 words
+  const uint32_t nwarp = blockDim.x >> 5;
+  if (G * HD <= 256u) {
+    if ((uint32_t)lane < c8n)
+#pragma unroll
+      for (int h = 0; h < G; h++)
+#pragma unroll
+        for (int e8 = 0; e8 < 8; e8++) red[warp * G * HD + h * HD + c8 * 8 + e8] = acc[h][e8];
     __syncthreads();
-    if (tid < (int)HD) {
+    for (uint32_t i = ut; i < G * HD; i += blockDim.x) {
       uint32_t t = 0;
-      for (uint32_t k2 = 0; k2 < groups; k2++) t += red[k2 * HD + tid];
-      out[h * HD + tid] = kernel_out16((long long)(int32_t)t);
+      for (uint32_t w = 0; w < nwarp; w++) t += red[w * G * HD + i];
+      out[i] = kernel_out16((long long)(int32_t)t);
     }
-    __syncthreads();
+  } else {
+#pragma unroll
+    for (int h = 0; h < G; h++) {
+      if ((uint32_t)lane < c8n)
+#pragma unroll
+        for (int e8 = 0; e8 < 8; e8++) red[warp * HD + c8 * 8 + e8] = acc[h][e8];
+      __syncthreads();
+      if (ut < HD) {
+        uint32_t t = 0;
+        for (uint32_t w = 0; w < nwarp; w++) t += red[w * HD + ut];
+        out[h * HD + ut] = kernel_out16((long long)(int32_t)t);
+      }
+      __syncthreads();
+    }
   }
 }
 

@@ -454,14 +454,28 @@ __global__ void __launch_bounds__(256, 2) ro_norm16(RoArgs q, RoArgs x) {
   if (threadIdx.x == 0) s_scmin = 63;
   __syncthreads();
   int scmin = 63;  // per thread, then one shared atomic per warp
-  for (uint32_t c = threadIdx.x; c < npar; c += blockDim.x) {
-    const int4 e = *(const int4*)(q.p + 16ull * c);
-    const uint32_t slot = bcast ? 0u : (c % EPW) * words + c / EPW;
-    scmin = min(scmin, (int)(((uint32_t)e.z >> 16) & 63u));
-    s_g[slot] = e.x;
-    const int64_t bq = (int32_t)((uint32_t)e.y << 10) >> 10;  // int22, sign-extended
-    s_bq[slot] = q.bq_sh <= 40u ? bq << q.bq_sh : 0;       // (the 128-bit path shifts itself)
-    s_sc[slot] = (uint8_t)(((uint32_t)e.z >> 16) & 63u);
+  // (WPR > 1, a block's work is one row: four entries a thread in flight,
+  // their loads, then the decodes)
+  constexpr uint32_t PB = WPR > 1 ? 4u : 1u;
+  for (uint32_t c0 = threadIdx.x; c0 < npar; c0 += PB * blockDim.x) {
+    int4 ev[PB];
+#pragma unroll
+    for (uint32_t u = 0; u < PB; u++) {
+      const uint32_t c = c0 + u * blockDim.x;
+      if (c < npar) ev[u] = *(const int4*)(q.p + 16ull * c);
+    }
+#pragma unroll
+    for (uint32_t u = 0; u < PB; u++) {
+      const uint32_t c = c0 + u * blockDim.x;
+      if (c >= npar) break;
+      const int4 e = ev[u];
+      const uint32_t slot = bcast ? 0u : (c % EPW) * words + c / EPW;
+      scmin = min(scmin, (int)(((uint32_t)e.z >> 16) & 63u));
+      s_g[slot] = e.x;
+      const int64_t bq = (int32_t)((uint32_t)e.y << 10) >> 10;  // int22, sign-extended
+      s_bq[slot] = q.bq_sh <= 40u ? bq << q.bq_sh : 0;       // (the 128-bit path shifts itself)
+      s_sc[slot] = (uint8_t)(((uint32_t)e.z >> 16) & 63u);
+    }
   }
   // PRE: the ADDX job's entries (same [e][w] slots), after this job's
   const bool xbc = PRE && ((x.op >> 13) & 1u);
@@ -475,14 +489,27 @@ __global__ void __launch_bounds__(256, 2) ro_norm16(RoArgs q, RoArgs x) {
     if (threadIdx.x == 0) s_xmax = 0;
     __syncthreads();
     int xm = 0;
-    for (uint32_t c = threadIdx.x; c < xpar; c += blockDim.x) {
-      const Param pr = ld_param(x, c);
-      const uint32_t slot = xbc ? 0u : (c % EPW) * words + c / EPW;
-      x_bq[slot] = pr.bq;
-      x_sa[slot] = (uint8_t)pr.sa;
-      x_sb[slot] = (uint8_t)pr.sb;
-      x_sc[slot] = (uint8_t)pr.sc;
-      xm = max(xm, (int)max(pr.sa + 31u, pr.sb + 15u));
+    // (x's block is 16-byte aligned: the pair's host check)
+    for (uint32_t c0 = threadIdx.x; c0 < xpar; c0 += PB * blockDim.x) {
+      int4 ev[PB];
+#pragma unroll
+      for (uint32_t u = 0; u < PB; u++) {
+        const uint32_t c = c0 + u * blockDim.x;
+        if (c < xpar) ev[u] = *(const int4*)(x.p + 16ull * c);
+      }
+#pragma unroll
+      for (uint32_t u = 0; u < PB; u++) {
+        const uint32_t c = c0 + u * blockDim.x;
+        if (c >= xpar) break;
+        const uint32_t slot = xbc ? 0u : (c % EPW) * words + c / EPW;
+        const uint32_t sa = (uint32_t)ev[u].z & 63u, sb = ((uint32_t)ev[u].z >> 8) & 63u,
+                       sc = ((uint32_t)ev[u].z >> 16) & 63u;
+        x_bq[slot] = (int32_t)((uint32_t)ev[u].y << 10) >> 10;  // int22, sign-extended
+        x_sa[slot] = (uint8_t)sa;
+        x_sb[slot] = (uint8_t)sb;
+        x_sc[slot] = (uint8_t)sc;
+        xm = max(xm, (int)max(sa + 31u, sb + 15u));
+      }
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) xm = max(xm, __shfl_xor_sync(0xffffffffu, xm, o));

@@ -2,7 +2,8 @@
 planes once; no counterpart in the reference): the MatMul job against the
 planes equals the oracle's MatMul bit for bit — few rows, a ragged row count
 and column count, a K split, the wrap flag, a batch sharing the weight, the
-fused ReLU flag, output column groups — and equals corm_matmul."""
+fused ReLU flag, output column groups, the decode step's shapes under the
+wrap rule — and equals corm_matmul."""
 import numpy as np
 import pytest
 
@@ -18,6 +19,11 @@ CASES = [  # batch, n, k, m, flags, range
     (1, 64, 2560, 960, 0, 32768),   # K split
     (3, 20, 512, 136, 0, 32768),    # one weight for every batch
     (1, 128, 128, 256, 4, 32768),   # F_ACT_RELU
+    # the decode step's shapes under the wrap rule (M = 64 MMAs), a ragged batch with ReLU
+    (1, 64, 960, 1600, 1, 32768),
+    (1, 64, 2560, 960, 1, 32768),
+    (1, 64, 960, 5120, 1, 32768),
+    (2, 7, 64, 40, 5, 32768),
 ]
 
 
@@ -43,7 +49,8 @@ def test_bplanes_vs_oracle(case):
     assert torch.equal(C, ref)
 
 
-def test_bplanes_groups_vs_oracle():
+@pytest.mark.parametrize("flags", [0, 1], ids=["exact", "wrap"])
+def test_bplanes_groups_vs_oracle(flags):
     from cormorant_b200 import ops
     n, k, widths = 64, 960, (960, 320, 320)
     m = sum(widths)
@@ -53,8 +60,8 @@ def test_bplanes_groups_vs_oracle():
     planes = ops.split_b_planes(torch.from_numpy(B.reshape(-1)).cuda(), k=k, m=m)
     outs = [torch.empty(n * w, dtype=torch.int16, device="cuda") for w in widths]
     ops.matmul_bplanes(torch.from_numpy(A.reshape(-1)).cuda(), planes, None, n=n, k=k, m=m, outs=outs,
-                       widths=list(widths))
-    want = spec.matmul_raw(A, B)
+                       widths=list(widths), flags=flags)
+    want = spec.matmul_raw(A, B, wrap=bool(flags))
     c0 = 0
     for w, o in zip(widths, outs):
         assert np.array_equal(o.cpu().numpy().reshape(n, w), want[:, c0:c0 + w])
