@@ -151,11 +151,14 @@ def test_gpu_llama_decode_vs_oracle():
 
 @pytest.mark.gpu
 @pytest.mark.parametrize("dims", [dict(hidden=64, heads=4, kv_heads=2, head_dim=16, ffn=128),
-                                  dict(hidden=256, heads=8, kv_heads=1, head_dim=32, ffn=256)],
-                         ids=["g2_hd16", "g8_hd32"])
+                                  dict(hidden=256, heads=8, kv_heads=1, head_dim=32, ffn=256),
+                                  dict(hidden=640, heads=10, kv_heads=2, head_dim=64, ffn=256)],
+                         ids=["g2_hd16", "g8_hd32", "g5_hd64"])
 def test_gpu_llama_decode_heads_vs_oracle(dims):
     """The decode attention launch at other group sizes and head widths (2
-    heads of 16, 8 heads of 32 per KV group) against the oracle's loop."""
+    heads of 16, 8 heads of 32, 5 heads of 64 per KV group: the compiled
+    64-wide form at two CTAs an SM, its P.V sums reduced head by head)
+    against the oracle's loop."""
     torch = pytest.importorskip("torch")
     if not torch.cuda.is_available():
         pytest.skip("no CUDA device")
