@@ -851,10 +851,23 @@ def bench_llama_decode(torch, dev, stream, flush, args, world, rank, pg, steps=1
     keys_avg = float(np.mean([-(-(512 + i + 1) // 16) * 16 for i in range(steps)]))
     macs = m.macs_per_token(keys_avg, prefill=False)
     rate = world * B * steps / (ms * 1e-3)
+    # HBM roofline of a step: every weight read once (int16, or its two int8
+    # planes: 2 B either way) and the K / V cache rows the attention reads (the
+    # key count of each step, 2 B per element), per rank
+    D, H, KVh, HD = m.D, m.H, m.KV, m.HD
+    w_elems = m.L * (D * (H * HD + 2 * KVh * HD) + H * HD * D + 3 * D * m.ffn) + D * m.vocab
+    kv_bytes = float(np.mean([2 * 2 * m.L * B * KVh * HD * (512 + i + 1) for i in range(steps)]))
+    step_bytes = 2.0 * w_elems + kv_bytes
+    with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as fh:
+        hbm = float(json.load(fh).get("hbm_gbs") or 6650.0)
+    gbs = world * step_bytes / (ms / steps * 1e-3) / 1e9
     out = {"batch_per_gpu": B, "steps": steps, "ms_per_decode_run": round(ms, 3),
            "ms_per_token_step": round(ms / steps, 4), "tokens_per_s": round(rate, 1),
            "GMAC/s": round(rate * macs / 1e9, 1), "mmac_per_token": round(macs / 1e6, 2),
            "graph_nodes_per_step": len(m.decode_graph.nodes),
+           "roofline": {"bound": "hbm", "alg_bytes_per_step_per_gpu": round(step_bytes),
+                        "GB/s": round(gbs, 1), "frac_of_measured_hbm": round(gbs / (world * hbm), 4),
+                        "bytes": "weights once (2 B each) + the K / V cache rows read (keys 513 .. 640)"},
            "first_ids": ids[0, :4].cpu().tolist()}
     # verification: every replay runs the same steps over the caches the prefill
     # left (a step's cache row is written before it is read), so the ids and the
