@@ -181,6 +181,19 @@ __device__ __forceinline__ uint32_t smx_e32(int32_t m, int32_t x, uint32_t cm, u
   return y >= (17ull << 12) ? 0u : e;
 }
 
+// R = floor(2^40 / S) for a row sum 1 <= S < 2^32, without a 64-bit integer
+// division (a long instruction sequence that every lane of a row's group
+// runs, a large share of a short row's work).  q = 2^40 / S rounded to
+// nearest in double lies within half an ulp (at most 2^-13) of the exact
+// quotient; rounding is monotone and every integer below 2^53 is a double, so
+// floor(q) is floor(2^40 / S) or one more, and one product test fixes it
+// (r S <= 2^40 + S < 2^64).
+__device__ __forceinline__ uint64_t smx_r40(uint32_t S) {
+  uint64_t r = (uint64_t)(1099511627776.0 / (double)S);
+  if (r * (uint64_t)S > (1ull << 40)) r--;
+  return r;
+}
+
 __device__ __forceinline__ int16_t smx_p32(uint32_t e, uint32_t R, uint64_t rnd, uint32_t sh) {
   const uint64_t q = ((uint64_t)e * R + rnd) >> sh;
   return (int16_t)(q > 32767u ? 32767u : q);
@@ -350,7 +363,7 @@ __global__ void __launch_bounds__(GROUP >= 256 ? GROUP : 256) smx_rows(SmxArgs p
       __syncthreads();  // s_max / s_sum are rewritten by the next row
     }
     if (!live) continue;
-    const uint32_t R = S > 0 ? (uint32_t)((1ull << 40) / S) : 0u;
+    const uint32_t R = S > 0 ? (uint32_t)smx_r40(S) : 0u;
     int16_t* out = p.c + (size_t)row * p.b_inc;
     const uint32_t lim = (row + 1 == p.rows) ? p.W : min(p.W, max(p.b_inc, p.size));
     const bool oa = ((uintptr_t)out & 15) == 0;
@@ -568,7 +581,7 @@ __global__ void __launch_bounds__(256) smx_cols_t(SmxArgs p) {
 #pragma unroll
     for (int o = LPQ / 2; o > 0; o >>= 1) S += __shfl_xor_sync(0xffffffffu, S, o);
     if (live) {
-      const uint32_t R = S > 0 ? (uint32_t)((1ull << 40) / S) : 0u;
+      const uint32_t R = S > 0 ? (uint32_t)smx_r40(S) : 0u;
       int16_t* out = p.c + (size_t)q * p.b_inc;
       const uint32_t lim = (q + 1 == p.rows) ? p.W : min(p.W, max(p.b_inc, p.size));
       const bool oa = ((uintptr_t)out & 15) == 0;
