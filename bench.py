@@ -206,7 +206,8 @@ def main():
     ap.add_argument("--no-models", action="store_true", help="skip the MNIST / MobileNetV2 / BERT forward passes")
     ap.add_argument("--models", help="comma list of model cases to run (default: all)")
     ap.add_argument("--detail", help="write per-problem kernel times of one profiled step to this JSON file")
-    ap.add_argument("--case", choices=["gemm", "gemm_small", "gemm_int16", "vectorop", "softmax", "softmax_col",
+    ap.add_argument("--case", choices=["gemm", "gemm_small", "gemm_int16", "vectorop", "softmax", "softmax128",
+                                       "softmax_col",
                                        "layernorm", "rmsnorm32", "dwconv", "dwconv14", "pwconv", "maxpool",
                                        "addxnorm", "mulact", "conv",
                                        "llama_prefill", "llama_decode"],
@@ -998,6 +999,11 @@ def run_case(args):
         x, p = ri(N, -2048, 2048), torch.empty(N, dtype=torch.int16, device="cuda")
         fn = lambda: ops.vectorop(x, None, p, size=1024, op=10, outer=N // 1024, a_inc=1024, b_inc=1024,  # noqa
                                   smx_cm=12102203, smx_cfg=19 | (8 << 8), smx_mask=1024)
+    elif args.case == "softmax128":  # rows of 128 (the short-row form: 16 lanes a row)
+        N = 1 << 26
+        x, p = ri(N, -2048, 2048), torch.empty(N, dtype=torch.int16, device="cuda")
+        fn = lambda: ops.vectorop(x, None, p, size=128, op=10, outer=N // 128, a_inc=128, b_inc=128,  # noqa
+                                  smx_cm=12102203, smx_cfg=19 | (8 << 8), smx_mask=128)
     elif args.case == "softmax_col":  # keys-major, 512 keys x 64K queries (a prefill head group's scores)
         N = 1 << 25
         x, p = ri(N, -2048, 2048), torch.empty(N, dtype=torch.int16, device="cuda")
