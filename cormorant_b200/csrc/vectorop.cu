@@ -199,23 +199,29 @@ __device__ __forceinline__ int16_t smx_p32(uint32_t e, uint32_t R, uint64_t rnd,
   return (int16_t)(q > 32767u ? 32767u : q);
 }
 
+// FC selects the arithmetic of e and P: 0 the 64-bit steps above, 1 (FC)
+// both in 32-bit halves as below, 2 P alone for f_p = 8 (sh = 32): e R <
+// 2^41, so P = (e R + 2^31) >> 32 is the high word of e R plus bit 31 of its
+// low word, below 2^9 (e by the 64-bit steps; with the e table, only its
+// fill).
 // The same two steps in 32-bit halves when 8 <= Cs <= 39 and 40 - f_p < 32
 // (FC): y = floor(d Cm / 2^Cs) = umulhi(d 2^16, Cm 2^8) >> (Cs - 8) for
 // d = m - x < 2^16 and Cm < 2^24 (both factors below 2^32, the high word is
 // floor(d Cm / 2^8)); P = (e R + 2^(sh-1)) >> sh by a funnel shift (e R <
 // 2^41, sh >= 9: the quotient fits 32 bits).
-template <bool FC>
+template <int FC>
 __device__ __forceinline__ uint32_t smx_e(int32_t m, int32_t x, const SmxArgs& p, const int32_t* tab) {
-  if (!FC) return smx_e32(m, x, p.cm, p.cs, tab);
+  if (FC != 1) return smx_e32(m, x, p.cm, p.cs, tab);
   const uint32_t y = __umulhi((uint32_t)(m - x) << 16, p.cm8) >> p.csm8;
   const uint32_t yc = min(y, (17u << 12) - 1u);
   const uint32_t e = (uint32_t)tab[yc & 4095u] >> (yc >> 12);
   return y >= (17u << 12) ? 0u : e;
 }
 
-template <bool FC>
+template <int FC>
 __device__ __forceinline__ int16_t smx_pq(uint32_t e, uint32_t R, uint64_t rnd, uint32_t sh) {
-  if (!FC) return smx_p32(e, R, rnd, sh);
+  if (FC == 2) return (int16_t)(__umulhi(e, R) + ((e * R) >> 31));  // sh = 32: < 2^9, no saturation
+  if (FC == 0) return smx_p32(e, R, rnd, sh);
   const uint64_t t = (uint64_t)e * R + rnd;
   const uint32_t q = __funnelshift_r((uint32_t)t, (uint32_t)(t >> 32), sh);
   return (int16_t)min(q, 32767u);
@@ -230,7 +236,7 @@ __device__ __forceinline__ int16_t smx_pq(uint32_t e, uint32_t R, uint64_t rnd, 
 // arithmetic above is the other path.
 constexpr uint32_t kSmxEMax = 8192;  // largest dm tabulated (32 KB of shared memory)
 
-template <bool FC>
+template <int FC>
 __device__ __forceinline__ void smx_fill_etab(int32_t* s_e, const SmxArgs& p, int nt) {
   for (uint32_t d = threadIdx.x; d <= p.dm; d += nt)
     s_e[d] = d < p.dm ? (int32_t)smx_e<FC>((int32_t)d, 0, p, p.tab) : 0;
@@ -238,7 +244,7 @@ __device__ __forceinline__ void smx_fill_etab(int32_t* s_e, const SmxArgs& p, in
 
 // e of the two packed int16 scores of xw (low, high) against the packed row
 // maximum m2: (m - x) mod 2^16 is m - x (0 <= m - x < 2^16), clamped to dm.
-template <bool ET, bool FC>
+template <bool ET, int FC>
 __device__ __forceinline__ void smx_e2(uint32_t m2, uint32_t xw, int32_t m, const SmxArgs& p, const int32_t* s_t,
                                        uint32_t& e0, uint32_t& e1) {
   if (ET) {
@@ -259,7 +265,7 @@ __device__ __forceinline__ void smx_e2(uint32_t m2, uint32_t xw, int32_t m, cons
 // 8-element run (a run wholly inside the valid length takes no mask), so the
 // P of a masked element is 0 with no further test.  The TAB (or the e table)
 // is built in shared memory once per CTA; CTAs then walk row groups.
-template <int GROUP, int PER, bool FC, bool ET>
+template <int GROUP, int PER, int FC, bool ET>
 __global__ void __launch_bounds__(GROUP >= 256 ? GROUP : 256) smx_rows(SmxArgs p) {
   corm_pdl_wait();
   corm_pdl_trigger();
@@ -458,7 +464,7 @@ __device__ __forceinline__ uint32_t smx_mask2(uint32_t w, uint32_t j, uint32_t v
   return j + 1 < v ? w : ((w & 0xFFFFu) | 0x80000000u);
 }
 
-template <int QT, int WPL, bool STORE_E, bool FC, bool ET>
+template <int QT, int WPL, bool STORE_E, int FC, bool ET>
 __global__ void __launch_bounds__(256) smx_cols_t(SmxArgs p) {
   constexpr uint32_t LPQ = 256u / QT;  // lanes per query: 8 (QT 32) or 32 (QT 8, long columns)
   constexpr uint32_t PARTS = QT / 8;   // 8-query groups of the staging
@@ -621,17 +627,19 @@ __global__ void __launch_bounds__(256) smx_cols_t(SmxArgs p) {
 unsigned smx_grid(uint64_t groups) { return (unsigned)(groups < 148u * 8u ? (groups ? groups : 1) : 148u * 8u); }
 
 template <int G, int P>
-void launch_rows(const SmxArgs& p, unsigned grid, unsigned threads, bool fc, cudaStream_t st) {
+void launch_rows(const SmxArgs& p, unsigned grid, unsigned threads, int fc, cudaStream_t st) {
   const bool et = p.dm <= kSmxEMax;
   const size_t smem = et ? ((size_t)p.dm + 1) * sizeof(int32_t) : 4096 * sizeof(int32_t);
-  if (et && fc)
-    corm_launch_pdl(smx_rows<G, P, true, true>, dim3(grid), dim3(threads), smem, st, p);
+  if (et && fc == 1)
+    corm_launch_pdl(smx_rows<G, P, 1, true>, dim3(grid), dim3(threads), smem, st, p);
+  else if (et && fc == 2)
+    corm_launch_pdl(smx_rows<G, P, 2, true>, dim3(grid), dim3(threads), smem, st, p);
   else if (et)
-    corm_launch_pdl(smx_rows<G, P, false, true>, dim3(grid), dim3(threads), smem, st, p);
-  else if (fc)
-    corm_launch_pdl(smx_rows<G, P, true, false>, dim3(grid), dim3(threads), smem, st, p);
+    corm_launch_pdl(smx_rows<G, P, 0, true>, dim3(grid), dim3(threads), smem, st, p);
+  else if (fc == 1)
+    corm_launch_pdl(smx_rows<G, P, 1, false>, dim3(grid), dim3(threads), smem, st, p);
   else
-    corm_launch_pdl(smx_rows<G, P, false, false>, dim3(grid), dim3(threads), smem, st, p);
+    corm_launch_pdl(smx_rows<G, P, 0, false>, dim3(grid), dim3(threads), smem, st, p);
 }
 
 // The first d = m - x (0 <= d < 2^16) with floor(d Cm / 2^Cs) >= 17 << 12, so
@@ -661,7 +669,7 @@ int launch_softmax(const corm_vectorop_desc* d, cudaStream_t st, const corm::Dev
   p.csm8 = p.cs >= 8u ? p.cs - 8u : 0u;
   p.dm = smx_dm(p.cm, p.cs);
   p.dm2 = p.dm <= 0xFFFFu ? p.dm * 0x10001u : 0xFFFFFFFFu;
-  const bool fc = p.cs >= 8u && p.cs <= 39u && 40u - p.fp < 32u;
+  const int fc = (p.cs >= 8u && p.cs <= 39u && 40u - p.fp < 32u) ? 1 : (p.fp == 8u ? 2 : 0);
   const bool col = d->op == 11;
   p.rows = col ? (d->outer & ~15u) : d->outer;
   if (p.rows == 0) return CORM_OK;
@@ -677,19 +685,20 @@ int launch_softmax(const corm_vectorop_desc* d, cudaStream_t st, const corm::Dev
     const uint32_t tiles = (p.rows + qt - 1) / qt;
     const unsigned per_sm = smem <= 56u * 1024u ? 4u : (smem <= 112u * 1024u ? 2u : 1u);
     const unsigned grid = tiles < 148u * per_sm ? tiles : 148u * per_sm;
-    auto launch = [&](auto k_fe, auto k_se, auto k_f, auto k_s) {
+    auto launch = [&](auto k_fe, auto k_he, auto k_se, auto k_f, auto k_s) {
       auto run = [&](auto kern) {
         cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         corm_launch_pdl(kern, dim3(grid), dim3(256), smem, st, p);
       };
-      if (et && fc) run(k_fe);
+      if (et && fc == 1) run(k_fe);
+      else if (et && fc == 2) run(k_he);
       else if (et) run(k_se);
-      else if (fc) run(k_f);
+      else if (fc == 1) run(k_f);
       else run(k_s);
     };
 #define CORM_SMX_COLS(Q, W, SE) \
-  launch(smx_cols_t<Q, W, SE, true, true>, smx_cols_t<Q, W, SE, false, true>, smx_cols_t<Q, W, SE, true, false>, \
-         smx_cols_t<Q, W, SE, false, false>)
+  launch(smx_cols_t<Q, W, SE, 1, true>, smx_cols_t<Q, W, SE, 2, true>, smx_cols_t<Q, W, SE, 0, true>, \
+         smx_cols_t<Q, W, SE, 1, false>, smx_cols_t<Q, W, SE, 0, false>)
     {
       corm::ProfScope prof_("smx_cols_t", st);
       if (d->size <= 64) CORM_SMX_COLS(32, 1, true);
