@@ -200,10 +200,11 @@ __device__ __forceinline__ int16_t smx_p32(uint32_t e, uint32_t R, uint64_t rnd,
 }
 
 // FC selects the arithmetic of e and P: 0 the 64-bit steps above, 1 (FC)
-// both in 32-bit halves as below, 2 P alone for f_p = 8 (sh = 32): e R <
-// 2^41, so P = (e R + 2^31) >> 32 is the high word of e R plus bit 31 of its
-// low word, below 2^9 (e by the 64-bit steps; with the e table, only its
-// fill).
+// both in 32-bit halves as below, 2 P alone for 8 <= f_p <= 15 with the e
+// table (e by the 64-bit steps in its fill): a valid row's S >= TAB[0] =
+// 2^16, so R <= 2^24 and R' = R 2^(f_p - 8) < 2^32; with sh = 40 - f_p,
+// P = (e R + 2^(sh-1)) >> sh = (e R' + 2^31) >> 32, the high word of e R'
+// plus bit 31 of its low word.
 // The same two steps in 32-bit halves when 8 <= Cs <= 39 and 40 - f_p < 32
 // (FC): y = floor(d Cm / 2^Cs) = umulhi(d 2^16, Cm 2^8) >> (Cs - 8) for
 // d = m - x < 2^16 and Cm < 2^24 (both factors below 2^32, the high word is
@@ -220,7 +221,7 @@ __device__ __forceinline__ uint32_t smx_e(int32_t m, int32_t x, const SmxArgs& p
 
 template <int FC>
 __device__ __forceinline__ int16_t smx_pq(uint32_t e, uint32_t R, uint64_t rnd, uint32_t sh) {
-  if (FC == 2) return (int16_t)(__umulhi(e, R) + ((e * R) >> 31));  // sh = 32: < 2^9, no saturation
+  if (FC == 2) return (int16_t)min(__umulhi(e, R) + ((e * R) >> 31), 32767u);  // R = R' (below)
   if (FC == 0) return smx_p32(e, R, rnd, sh);
   const uint64_t t = (uint64_t)e * R + rnd;
   const uint32_t q = __funnelshift_r((uint32_t)t, (uint32_t)(t >> 32), sh);
@@ -369,7 +370,7 @@ __global__ void __launch_bounds__(GROUP >= 256 ? GROUP : 256) smx_rows(SmxArgs p
       __syncthreads();  // s_max / s_sum are rewritten by the next row
     }
     if (!live) continue;
-    const uint32_t R = S > 0 ? (uint32_t)smx_r40(S) : 0u;
+    const uint32_t R = S > 0 ? (uint32_t)smx_r40(S) << (FC == 2 ? p.fp - 8u : 0u) : 0u;
     int16_t* out = p.c + (size_t)row * p.b_inc;
     const uint32_t lim = (row + 1 == p.rows) ? p.W : min(p.W, max(p.b_inc, p.size));
     const bool oa = ((uintptr_t)out & 15) == 0;
@@ -587,7 +588,7 @@ __global__ void __launch_bounds__(256) smx_cols_t(SmxArgs p) {
 #pragma unroll
     for (int o = LPQ / 2; o > 0; o >>= 1) S += __shfl_xor_sync(0xffffffffu, S, o);
     if (live) {
-      const uint32_t R = S > 0 ? (uint32_t)smx_r40(S) : 0u;
+      const uint32_t R = S > 0 ? (uint32_t)smx_r40(S) << (FC == 2 ? p.fp - 8u : 0u) : 0u;
       int16_t* out = p.c + (size_t)q * p.b_inc;
       const uint32_t lim = (q + 1 == p.rows) ? p.W : min(p.W, max(p.b_inc, p.size));
       const bool oa = ((uintptr_t)out & 15) == 0;
@@ -669,7 +670,8 @@ int launch_softmax(const corm_vectorop_desc* d, cudaStream_t st, const corm::Dev
   p.csm8 = p.cs >= 8u ? p.cs - 8u : 0u;
   p.dm = smx_dm(p.cm, p.cs);
   p.dm2 = p.dm <= 0xFFFFu ? p.dm * 0x10001u : 0xFFFFFFFFu;
-  const int fc = (p.cs >= 8u && p.cs <= 39u && 40u - p.fp < 32u) ? 1 : (p.fp == 8u ? 2 : 0);
+  const int fc = (p.dm <= kSmxEMax && p.fp >= 8u && p.fp <= 15u) ? 2
+                 : (p.cs >= 8u && p.cs <= 39u && 40u - p.fp < 32u) ? 1 : 0;
   const bool col = d->op == 11;
   p.rows = col ? (d->outer & ~15u) : d->outer;
   if (p.rows == 0) return CORM_OK;
